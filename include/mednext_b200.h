@@ -1,0 +1,203 @@
+/*
+ * mednext_b200.h — C ABI of the B200 (sm_100a) MedNeXt training operators.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream, launches its kernels asynchronously on that stream, and returns a
+ * mednext_status code.  Nothing here allocates device memory: scratch space is
+ * passed in by the caller (query its size with the matching *_workspace_size
+ * function).  Tensors are contiguous NCDHW, exactly as the reference package
+ * keeps them (mednext_accel/ops/adaptive.py:265 requires contiguous input).
+ *
+ * Reference interfaces replaced (paths inside the reference project
+ * nanaHa1003/mednext-accel, src/mednext_accel/):
+ *   mednext_dw_fwd        F.conv3d forward inside the custom op
+ *                         depthwise_conv3d_odd_regular, ops/_triton/depthwise.py:549-563
+ *   mednext_dw_dgrad      _depthwise_input_grad_kernel / depthwise_input_grad_regular,
+ *                         ops/_triton/depthwise.py:159-203, 486-513
+ *   mednext_dw_wgrad      _partial_dw_kernel + _finish_dw_kernel /
+ *                         depthwise_weight_grad_regular, ops/_triton/depthwise.py:13-83, 445-483
+ *                         (+ the native bias grad, ops/_triton/depthwise.py:613-633)
+ *   mednext_dw_s2_fwd     F.conv3d stride 2 in depthwise_conv3d_stride2_regular,
+ *                         ops/_triton/depthwise.py:654-666
+ *   mednext_dw_s2_dgrad   _depthwise_stride2_input_grad_kernel /
+ *                         depthwise_input_grad_stride2_regular, ops/_triton/depthwise.py:206-268, 516-546
+ *   mednext_dw_s2_wgrad   native aten.convolution_backward dW of the stride-2 op,
+ *                         ops/_triton/depthwise.py:698-713
+ *   mednext_dwT_fwd       F.conv_transpose3d in depthwise_conv_transpose3d_odd_regular,
+ *                         ops/_triton/depthwise.py:768-781
+ *   mednext_dwT_dgrad     native aten.convolution_backward dX of the transpose op,
+ *                         ops/_triton/depthwise.py:810-825
+ *   mednext_dwT_wgrad     _partial_transpose_dw_kernel + _finish_dw_kernel /
+ *                         depthwise_transpose_weight_grad_regular, ops/_triton/depthwise.py:86-156, 722-765
+ *   mednext_gn_*          nn.GroupNorm(C, C) of MedNeXtBlock, models/blocks.py:74
+ *   mednext_pw_*          AdaptivePointwise3d._gemm / F.conv3d 1x1x1, ops/adaptive.py:174-200,
+ *                         with the GroupNorm apply, exact GELU (models/blocks.py:32-44) and the
+ *                         residual add (models/blocks.py:89-90) fused into prologue/epilogue
+ */
+#ifndef MEDNEXT_B200_H
+#define MEDNEXT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; NULL means the legacy default stream. */
+typedef struct CUstream_st* mednext_stream_t;
+
+/* Element types.  Depthwise and GroupNorm kernels accept all four; the
+ * tensor-core pointwise kernels accept BFLOAT16 and FLOAT16. */
+enum mednext_dtype {
+  MEDNEXT_FLOAT32 = 0,
+  MEDNEXT_BFLOAT16 = 1,
+  MEDNEXT_FLOAT16 = 2,
+  MEDNEXT_FLOAT64 = 3
+};
+
+enum mednext_status {
+  MEDNEXT_OK = 0,
+  MEDNEXT_ERR_NULL_POINTER = 1, /* a required pointer is NULL */
+  MEDNEXT_ERR_BAD_SHAPE = 2,    /* a size is non-positive, inconsistent or too large */
+  MEDNEXT_ERR_BAD_KERNEL = 3,   /* kernel size is not one of 1, 3, 5, 7 */
+  MEDNEXT_ERR_BAD_DTYPE = 4,    /* dtype not supported by this entry point */
+  MEDNEXT_ERR_WORKSPACE = 5,    /* workspace missing or smaller than *_workspace_size */
+  MEDNEXT_ERR_ALIGNMENT = 6,    /* a pointer is not aligned to its element size */
+  MEDNEXT_ERR_CUDA = 7,         /* a CUDA launch failed (see mednext_last_cuda_error) */
+  MEDNEXT_ERR_DEVICE = 8        /* current device is not sm_100 */
+};
+
+/* Pointwise prologue applied to the activation operand while it is staged
+ * into shared memory, and epilogue applied to the accumulator tile. */
+enum mednext_pw_prologue {
+  MEDNEXT_PRO_NONE = 0,
+  MEDNEXT_PRO_GROUPNORM = 1, /* a <- (a - mean[n,k]) * rstd[n,k] * gamma[k] + beta[k] */
+  MEDNEXT_PRO_GELU = 2       /* a <- gelu(a), exact erf form */
+};
+enum mednext_pw_epilogue {
+  MEDNEXT_EPI_BIAS = 1,          /* y += bias[j] */
+  MEDNEXT_EPI_RESIDUAL = 2,      /* y += residual[n, j, v] */
+  MEDNEXT_EPI_GELU_GRAD = 4,     /* y *= gelu'(aux[n, j, v]) */
+  MEDNEXT_EPI_GN_BWD_STATS = 8   /* also emit per-tile sums of y and y*xhat(aux) for GroupNorm backward */
+};
+
+int mednext_abi_version(void);
+const char* mednext_status_string(int status);
+/* Last CUDA runtime error seen by this library on the calling thread. */
+int mednext_last_cuda_error(void);
+/* Device-side error word: kernels with bounded waits set it instead of hanging.
+ * Copies the word to *code and clears it (synchronous on the given stream). */
+int mednext_device_error(int* code, mednext_stream_t stream);
+/* Returns MEDNEXT_OK when the current device is sm_100 (B200). */
+int mednext_check_device(void);
+
+/* ---------------- depthwise Conv3d, stride 1, padding k/2 ----------------
+ * x, y: [n, c, d, h, w]; weight: [c, 1, k, k, k]; bias: [c] or NULL.
+ * If gn_stats is non-NULL the kernel also produces, for GroupNorm(c, c) on y,
+ * the per-(n, c) mean and 1/sqrt(var + eps) as gn_stats[2*(n*c+i)+{0,1}];
+ * that needs mednext_dw_fwd_workspace_size() bytes of workspace. */
+size_t mednext_dw_fwd_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                                     int k, int dtype);
+int mednext_dw_fwd(const void* x, const void* weight, const void* bias, void* y,
+                   float* gn_stats, float gn_eps, void* workspace, size_t workspace_bytes,
+                   int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
+                   mednext_stream_t stream);
+/* dx = correlation of dy with the spatially flipped weight (same shapes as fwd),
+ * plus addend (same shape, may be NULL) — the block's residual branch. */
+int mednext_dw_dgrad(const void* dy, const void* weight, const void* addend, void* dx,
+                     int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
+                     mednext_stream_t stream);
+/* dweight[c,0,kd,kh,kw] = sum over n, positions of x(shifted) * dy; dbias = sum of dy
+ * (dbias may be NULL).  Deterministic: fixed-order two-pass reduction. */
+size_t mednext_dw_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                                       int k, int dtype);
+int mednext_dw_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                     size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h,
+                     int64_t w, int k, int dtype, mednext_stream_t stream);
+
+/* ---------------- depthwise Conv3d, stride 2, padding k/2 (down block) ----
+ * (d, h, w) are the INPUT sizes; the output is ((d+1)/2, (h+1)/2, (w+1)/2). */
+int mednext_dw_s2_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n,
+                      int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
+                      mednext_stream_t stream);
+int mednext_dw_s2_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c,
+                        int64_t d, int64_t h, int64_t w, int k, int dtype,
+                        mednext_stream_t stream);
+size_t mednext_dw_s2_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                                          int k, int dtype);
+int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbias,
+                        void* workspace, size_t workspace_bytes, int64_t n, int64_t c, int64_t d,
+                        int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream);
+
+/* ------- depthwise ConvTranspose3d, stride 2, padding k/2 (up block) ------
+ * (d, h, w) are the INPUT sizes; the output is (2d-1, 2h-1, 2w-1). */
+int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n,
+                    int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
+                    mednext_stream_t stream);
+int mednext_dwT_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c,
+                      int64_t d, int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream);
+size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                                        int k, int dtype);
+int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                      size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h,
+                      int64_t w, int k, int dtype, mednext_stream_t stream);
+
+/* ---------------- GroupNorm with groups == channels ----------------------
+ * x: [n, c, spatial]; stats: float [n*c][2] = (mean, rstd).  gamma/beta: [c]
+ * in gamma_dtype (FLOAT32 parameters in the reference model). */
+size_t mednext_gn_stats_workspace_size(int64_t n, int64_t c, int64_t spatial);
+int mednext_gn_stats(const void* x, float* stats, void* workspace, size_t workspace_bytes,
+                     int64_t n, int64_t c, int64_t spatial, float eps, int dtype,
+                     mednext_stream_t stream);
+int mednext_gn_fwd(const void* x, const float* stats, const void* gamma, const void* beta,
+                   void* y, int64_t n, int64_t c, int64_t spatial, int x_dtype, int y_dtype,
+                   int gamma_dtype, mednext_stream_t stream);
+/* dx from dy (grad of the GroupNorm output) and x; dgamma/dbeta (FLOAT32, may be
+ * NULL) get the parameter grads.  Deterministic. */
+size_t mednext_gn_bwd_workspace_size(int64_t n, int64_t c, int64_t spatial);
+int mednext_gn_bwd(const void* dy, const void* x, const float* stats, const void* gamma,
+                   void* dx, float* dgamma, float* dbeta, void* workspace,
+                   size_t workspace_bytes, int64_t n, int64_t c, int64_t spatial, int dy_dtype,
+                   int x_dtype, int dx_dtype, int gamma_dtype, mednext_stream_t stream);
+
+/* ---------------- pointwise 1x1x1 convolution (tensor cores) -------------
+ * Forward / input-grad form, one GEMM per sample with the voxel axis as M:
+ *   y[s, j, v] = epi( sum_k wt[j, k] * pro(a[s, k, v]) )     j < cout, k < cin
+ * a: [n, cin, vox]; wt: [cout, cin] (K contiguous); y: [n, cout, vox].
+ * Prologue (enum mednext_pw_prologue) uses pro_stats [n*cin][2], pro_gamma,
+ * pro_beta [cin] (FLOAT32).  Epilogue flags (mednext_pw_epilogue) use bias
+ * [cout] (FLOAT32), residual [n, cout, vox] (y dtype), aux [n, cout, vox]
+ * (a dtype).  GN_BWD_STATS additionally takes aux = the GroupNorm input,
+ * epi_stats [n*cout][2] = its (mean, rstd), and writes per-(sample, channel,
+ * voxel-tile) partial sums into the workspace; mednext_gn_bwd_from_partials
+ * consumes them.  a, wt: BFLOAT16 or FLOAT16 (same type); y: a's type or FLOAT32. */
+size_t mednext_pw_fwd_workspace_size(int64_t n, int64_t cin, int64_t cout, int64_t vox,
+                                     int epilogue);
+int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const float* pro_stats,
+                   const float* pro_gamma, const float* pro_beta, int epilogue,
+                   const float* bias, const void* residual, const void* aux,
+                   const float* epi_stats, void* workspace, size_t workspace_bytes, int64_t n,
+                   int64_t cin, int64_t cout, int64_t vox, int a_dtype, int y_dtype,
+                   mednext_stream_t stream);
+/* Weight-grad form, the voxel axis is the reduction:
+ *   dw[j, k] = sum_{s, v} g[s, j, v] * pro(a[s, k, v]);  dbias[j] = sum g
+ * dw, dbias: FLOAT32 (dbias may be NULL).  Deterministic split-K. */
+size_t mednext_pw_wgrad_workspace_size(int64_t n, int64_t cin, int64_t cout, int64_t vox);
+int mednext_pw_wgrad(const void* g, const void* a, float* dw, float* dbias, int prologue,
+                     const float* pro_stats, const float* pro_gamma, const float* pro_beta,
+                     void* workspace, size_t workspace_bytes, int64_t n, int64_t cin,
+                     int64_t cout, int64_t vox, int dtype, mednext_stream_t stream);
+/* GroupNorm backward driven by the partial sums that mednext_pw_fwd wrote with
+ * MEDNEXT_EPI_GN_BWD_STATS (dz = that GEMM's output = grad of GroupNorm output). */
+int mednext_gn_bwd_from_partials(const void* dz, const void* x, const float* stats,
+                                 const void* gamma, void* dx, float* dgamma, float* dbeta,
+                                 const void* pw_workspace, int64_t n, int64_t c, int64_t vox,
+                                 int dz_dtype, int x_dtype, int dx_dtype, int gamma_dtype,
+                                 mednext_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEDNEXT_B200_H */

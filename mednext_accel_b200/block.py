@@ -1,0 +1,227 @@
+"""Fused MedNeXt block: one autograd node per block on sm_100a.
+
+Computes, for ``kind`` in {regular, down, up} (reference models/blocks.py:47-182):
+
+    t = depthwise(x)                      regular: stride 1; down: stride 2; up: transposed stride 2
+    z = GroupNorm(C, C)(t)                never materialised: applied while staging the expand GEMM
+    u = expand(z)                         tcgen05 GEMM, bias in the epilogue
+    y = project(gelu(u)) + addend         tcgen05 GEMM, GELU in the prologue, bias + residual in the epilogue
+
+Backward recomputes nothing but ``u`` when expansion checkpointing is on, and
+never materialises gelu(u), z or the GroupNorm-input gradient's intermediates:
+
+    du   = (dy Wp) * gelu'(u)             dgrad GEMM with the GELU derivative in the epilogue
+    dWp  = sum dy (x) gelu(u)             wgrad GEMM, GELU in the prologue
+    dWe  = sum du (x) z                   wgrad GEMM, GroupNorm in the prologue
+    dz   = du We                          dgrad GEMM + per-tile GroupNorm-backward sums in the epilogue
+    dt   = GroupNorm backward(dz)         one elementwise pass
+    dx   = depthwise dgrad(dt) (+ dy)     residual added in the same kernel
+    dWdw = depthwise wgrad(x, dt)         bias grad in the same pass
+
+Precision follows the reference under CUDA autocast: the depthwise conv and both
+GEMMs take bfloat16 (or float16) operands with fp32 accumulation, GroupNorm
+statistics and normalisation are fp32, outputs of each stage are rounded to the
+compute dtype where the reference stores them in that dtype.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+from torch.library import custom_op
+
+from . import _native as nat
+from . import depthwise as dwk
+from .pointwise import gn_backward_from_partials, gn_stats, pw_gemm, pw_wgrad
+
+_NS = "mednext_accel_b200"
+KIND_REGULAR, KIND_DOWN, KIND_UP = 0, 1, 2
+_CODES = {0: torch.float32, 1: torch.bfloat16, 2: torch.float16}
+
+
+def _depthwise_forward(xb: Tensor, w: Tensor, b: Tensor | None, kind: int, k: int, eps: float) -> tuple[Tensor, Tensor]:
+    if kind == KIND_REGULAR:
+        return dwk.dw_forward(xb, w, b, k, gn_eps=eps)
+    t = dwk.s2_forward(xb, w, b, k) if kind == KIND_DOWN else dwk.t_forward(xb, w, b, k)
+    return t, gn_stats(t, eps)
+
+
+def _expand(t: Tensor, stats: Tensor, gn_w: Tensor, gn_b: Tensor, e_w: Tensor, e_b: Tensor, cdt) -> Tensor:
+    rc = int(e_w.shape[0])
+    u, _ = pw_gemm(
+        t, e_w.reshape(rc, -1).to(cdt).contiguous(), rc, out_dtype=cdt, prologue=nat.PRO_GROUPNORM,
+        pro_stats=stats, pro_gamma=gn_w.float().contiguous(), pro_beta=gn_b.float().contiguous(),
+        bias=e_b.to(cdt).float(),
+    )
+    return u
+
+
+@custom_op(f"{_NS}::mednext_block", mutates_args=())
+def mednext_block(
+    x: Tensor,
+    addend: Tensor | None,
+    dw_w: Tensor,
+    dw_b: Tensor,
+    gn_w: Tensor,
+    gn_b: Tensor,
+    e_w: Tensor,
+    e_b: Tensor,
+    p_w: Tensor,
+    p_b: Tensor,
+    kind: int,
+    kernel_size: int,
+    eps: float,
+    residual_is_input: bool,
+    keep_expansion: bool,
+    compute_dtype: int,
+) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Returns (y, t, u, stats); t, u (empty when not kept) and stats are saved
+    for backward and carry no gradient."""
+    cdt = _CODES[compute_dtype]
+    xb = x.to(cdt).contiguous()
+    t, stats = _depthwise_forward(xb, dw_w.to(cdt).contiguous(), dw_b.to(cdt), kind, kernel_size, eps)
+    u = _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
+    cout = int(p_w.shape[0])
+    res = x if residual_is_input else addend
+    y, _ = pw_gemm(
+        u, p_w.reshape(cout, -1).to(cdt).contiguous(), cout,
+        out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
+        bias=p_b.to(cdt).float(), residual=res.contiguous() if res is not None else None,
+    )
+    return y, t, (u if keep_expansion else u.new_empty((0,))), stats
+
+
+@mednext_block.register_fake
+def _(x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, kind, kernel_size, eps, residual_is_input,
+      keep_expansion, compute_dtype):
+    cdt = _CODES[compute_dtype]
+    n, c = x.shape[0], x.shape[1]
+    sp = tuple(x.shape[2:])
+    if kind == KIND_DOWN:
+        sp = tuple((s + 1) // 2 for s in sp)
+    elif kind == KIND_UP:
+        sp = tuple(2 * s - 1 for s in sp)
+    res = x if residual_is_input else addend
+    y = x.new_empty((n, p_w.shape[0], *sp), dtype=res.dtype if res is not None else cdt)
+    t = x.new_empty((n, c, *sp), dtype=cdt)
+    u = x.new_empty((n, e_w.shape[0], *sp), dtype=cdt) if keep_expansion else x.new_empty((0,), dtype=cdt)
+    stats = x.new_empty((n * c, 2), dtype=torch.float32)
+    return y, t, u, stats
+
+
+@custom_op(f"{_NS}::mednext_block_backward", mutates_args=())
+def mednext_block_backward(
+    dy: Tensor,
+    x: Tensor,
+    t: Tensor,
+    u_saved: Tensor,
+    stats: Tensor,
+    dw_w: Tensor,
+    gn_w: Tensor,
+    gn_b: Tensor,
+    e_w: Tensor,
+    e_b: Tensor,
+    p_w: Tensor,
+    kind: int,
+    kernel_size: int,
+    residual_is_input: bool,
+    compute_dtype: int,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (dx, dw_w, dw_b, dgamma, dbeta, de_w, de_b, dp_w, dp_b) in the
+    parameters' dtypes."""
+    cdt = _CODES[compute_dtype]
+    dy = dy.contiguous()
+    dyb = dy.to(cdt)
+    xb = x.to(cdt).contiguous()
+    u = u_saved if u_saved.numel() > 0 else _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
+    rc, c = int(e_w.shape[0]), int(e_w.shape[1])
+    cout = int(p_w.shape[0])
+    # project dgrad with the GELU derivative in the epilogue
+    p_wt = p_w.reshape(cout, rc).to(cdt).t().contiguous()  # [rc, cout]
+    du, _ = pw_gemm(dyb, p_wt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
+    # weight grads of both GEMMs (fp32, deterministic split-K)
+    g_w = gn_w.float().contiguous()
+    g_b = gn_b.float().contiguous()
+    dpw, dpb = pw_wgrad(dyb, u, prologue=nat.PRO_GELU)
+    dew, deb = pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g_w, pro_beta=g_b)
+    # expand dgrad + GroupNorm-backward partial sums
+    e_wt = e_w.reshape(rc, c).to(cdt).t().contiguous()  # [c, rc]
+    dz, part = pw_gemm(du, e_wt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)
+    dt, dgamma, dbeta = gn_backward_from_partials(dz, t, stats, g_w, part)
+    wdw = dw_w.to(cdt).contiguous()
+    if kind == KIND_REGULAR:
+        dx = dwk.dw_dgrad(dt, wdw, kernel_size, addend=dyb if residual_is_input and dy.dtype == cdt else None)
+        dwdw, dbdw = dwk.dw_wgrad(xb, dt, kernel_size)
+    elif kind == KIND_DOWN:
+        dx = dwk.s2_dgrad(dt, wdw, tuple(int(s) for s in x.shape[2:]), kernel_size)
+        dwdw, dbdw = dwk.s2_wgrad(xb, dt, kernel_size)
+    else:
+        dx = dwk.t_dgrad(dt, wdw, kernel_size)
+        dwdw, dbdw = dwk.t_wgrad(xb, dt, kernel_size)
+    if dx.dtype != x.dtype:
+        dx = dx.to(x.dtype)
+        if residual_is_input:
+            dx = dx + dy.to(x.dtype)
+    elif residual_is_input and kind != KIND_REGULAR:
+        dx = dx + dy
+    pdt = dw_w.dtype
+    return (
+        dx,
+        dwdw.to(pdt),
+        dbdw.to(pdt),
+        dgamma.to(gn_w.dtype),
+        dbeta.to(gn_b.dtype),
+        dew.reshape(e_w.shape).to(e_w.dtype),
+        deb.to(e_b.dtype),
+        dpw.reshape(p_w.shape).to(p_w.dtype),
+        dpb.to(p_w.dtype),
+    )
+
+
+@mednext_block_backward.register_fake
+def _(dy, x, t, u_saved, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, kind, kernel_size, residual_is_input, compute_dtype):
+    return (
+        torch.empty_like(x),
+        torch.empty_like(dw_w),
+        dw_w.new_empty((dw_w.shape[0],)),
+        torch.empty_like(gn_w),
+        torch.empty_like(gn_b),
+        torch.empty_like(e_w),
+        torch.empty_like(e_b),
+        torch.empty_like(p_w),
+        p_w.new_empty((p_w.shape[0],)),
+    )
+
+
+def _setup(ctx, inputs, output):
+    (x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, kind, k, eps, residual_is_input, keep, cdt) = inputs
+    y, t, u, stats = output
+    ctx.save_for_backward(x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w)
+    ctx.mark_non_differentiable(t, u, stats)
+    ctx.kind = kind
+    ctx.k = k
+    ctx.residual_is_input = residual_is_input
+    ctx.cdt = cdt
+    ctx.has_addend = addend is not None
+    ctx.addend_dtype = addend.dtype if addend is not None else None
+
+
+def _backward(ctx, dy, _dt, _du, _dstats):
+    x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w = ctx.saved_tensors
+    dx, dww, dwb, dgw, dgb, dew, deb, dpw, dpb = mednext_block_backward(
+        dy, x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, ctx.kind, ctx.k, ctx.residual_is_input, ctx.cdt
+    )
+    d_add = None
+    if ctx.has_addend and ctx.needs_input_grad[1]:
+        d_add = dy if dy.dtype == ctx.addend_dtype else dy.to(ctx.addend_dtype)
+    return dx, d_add, dww, dwb, dgw, dgb, dew, deb, dpw, dpb, None, None, None, None, None, None
+
+
+mednext_block.register_autograd(_backward, setup_context=_setup)
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    for code, dt in _CODES.items():
+        if dt == dtype:
+            return code
+    raise ValueError(f"unsupported compute dtype {dtype}")

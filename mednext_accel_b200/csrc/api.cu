@@ -1,0 +1,403 @@
+// C ABI of libmednext_b200.so: argument validation, tile planning and the
+// calls into the per-family dispatchers.  Declarations, and the reference
+// interface each entry point replaces, are in include/mednext_b200.h.
+#include "plan.h"
+
+namespace mednext {
+namespace {
+thread_local int t_last_cuda_error = 0;
+}
+int record_launch() {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    t_last_cuda_error = (int)e;
+    return MEDNEXT_ERR_CUDA;
+  }
+  return MEDNEXT_OK;
+}
+int last_cuda_error() { return t_last_cuda_error; }
+}  // namespace mednext
+
+using namespace mednext;
+
+namespace {
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+bool aligned16(const void* p) { return aligned(p, 16); }
+bool valid_k(int k) { return k == 1 || k == 3 || k == 5 || k == 7; }
+
+// Index math inside the kernels uses 32-bit tile/plane counters and 64-bit
+// element offsets; keep every axis and the (sample, channel) count in range.
+int check_dw(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
+  if (elem_size(dtype) == 0) return MEDNEXT_ERR_BAD_DTYPE;
+  if (!valid_k(k)) return MEDNEXT_ERR_BAD_KERNEL;
+  const int64_t lim = (int64_t)1 << 30;
+  if (n <= 0 || c <= 0 || d <= 0 || h <= 0 || w <= 0) return MEDNEXT_ERR_BAD_SHAPE;
+  if (n >= lim || c >= lim || d >= lim || h >= lim || w >= lim || n * c >= lim || h * w >= lim)
+    return MEDNEXT_ERR_BAD_SHAPE;
+  return MEDNEXT_OK;
+}
+cudaStream_t as_stream(mednext_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+size_t s1_wgrad_ws(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
+  const S1Plan p = plan_s1(n, c, d, h, w, k, elem_size(dtype), true);
+  return (size_t)n * c * s1_tiles(p) * ((size_t)k * k * k + 1) * acc_size(dtype);
+}
+size_t s2_wgrad_ws(int64_t n, int64_t c, size_t svol, int k, int dtype) {
+  const S2WPlan p = plan_s2w(n, c, svol, k);
+  return (size_t)n * c * p.chunks * ((size_t)k * k * k + 1) * acc_size(dtype);
+}
+bool gn_shape_ok(int64_t n, int64_t c, int64_t spatial) {
+  return n > 0 && c > 0 && spatial > 0 && n * c < ((int64_t)1 << 30) && spatial < ((int64_t)1 << 40);
+}
+bool pw_dtype_ok(int d) { return d == MEDNEXT_BFLOAT16 || d == MEDNEXT_FLOAT16; }
+bool pw_shape_ok(int64_t n, int64_t cin, int64_t cout, int64_t vox) {
+  return n > 0 && cin > 0 && cout > 0 && vox > 0 && n < (1 << 20) && cin < (1 << 16) && cout < (1 << 16) &&
+         vox < ((int64_t)1 << 40);
+}
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+extern "C" {
+
+int mednext_abi_version(void) { return 1; }
+
+const char* mednext_status_string(int status) {
+  switch (status) {
+    case MEDNEXT_OK: return "ok";
+    case MEDNEXT_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case MEDNEXT_ERR_BAD_SHAPE: return "invalid or inconsistent shape";
+    case MEDNEXT_ERR_BAD_KERNEL: return "kernel_size must be 1, 3, 5 or 7";
+    case MEDNEXT_ERR_BAD_DTYPE: return "unsupported dtype";
+    case MEDNEXT_ERR_WORKSPACE: return "workspace missing or too small";
+    case MEDNEXT_ERR_ALIGNMENT: return "pointer not aligned to its element size";
+    case MEDNEXT_ERR_CUDA: return "CUDA launch failed";
+    case MEDNEXT_ERR_DEVICE: return "current device is not sm_100";
+    default: return "unknown status";
+  }
+}
+
+int mednext_last_cuda_error(void) { return last_cuda_error(); }
+
+int mednext_device_error(int* code, mednext_stream_t stream) {
+  if (code == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  *code = 0;
+  int st = read_clear_errors_dw(code, as_stream(stream));
+  if (st == MEDNEXT_OK) st = read_clear_errors_dw2(code, as_stream(stream));
+  if (st == MEDNEXT_OK) st = read_clear_errors_gn(code, as_stream(stream));
+  if (st == MEDNEXT_OK) st = read_clear_errors_pw(code, as_stream(stream));
+  return st;
+}
+
+int mednext_check_device(void) {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return record_launch();
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+    return record_launch();
+  return (major == 10 && minor == 0) ? MEDNEXT_OK : MEDNEXT_ERR_DEVICE;
+}
+
+// ------------------------------ depthwise stride 1 ------------------------------
+size_t mednext_dw_fwd_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
+  if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
+  const S1Plan p = plan_s1(n, c, d, h, w, k, elem_size(dtype), false);
+  return (size_t)n * c * s1_tiles(p) * sizeof(GnPartial);
+}
+
+int mednext_dw_fwd(const void* x, const void* weight, const void* bias, void* y, float* gn_stats, float gn_eps,
+                   void* workspace, size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                   int k, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (x == nullptr || weight == nullptr || y == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned16(x) || !aligned16(y) || !aligned(weight, esz) || (bias && !aligned(bias, esz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  GnPartial* part = nullptr;
+  if (gn_stats != nullptr) {
+    if (workspace == nullptr || !aligned16(workspace) ||
+        workspace_bytes < mednext_dw_fwd_workspace_size(n, c, d, h, w, k, dtype))
+      return MEDNEXT_ERR_WORKSPACE;
+    if (!aligned(gn_stats, 8)) return MEDNEXT_ERR_ALIGNMENT;
+    part = static_cast<GnPartial*>(workspace);
+  }
+  const S1Plan p = plan_s1(n, c, d, h, w, k, esz, false);
+  st = dispatch_dw_s1_conv(dtype, k, x, weight, bias, nullptr, y, part, p, 0, as_stream(stream));
+  if (st != MEDNEXT_OK || gn_stats == nullptr) return st;
+  return dispatch_gn_finalize(part, (int)s1_tiles(p), (int)(n * c), gn_eps, gn_stats, as_stream(stream));
+}
+
+int mednext_dw_dgrad(const void* dy, const void* weight, const void* addend, void* dx, int64_t n, int64_t c,
+                     int64_t d, int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (dy == nullptr || weight == nullptr || dx == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned16(dy) || !aligned16(dx) || !aligned(weight, esz) || (addend && !aligned16(addend)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  const S1Plan p = plan_s1(n, c, d, h, w, k, esz, false);
+  return dispatch_dw_s1_conv(dtype, k, dy, weight, nullptr, addend, dx, nullptr, p, 1, as_stream(stream));
+}
+
+size_t mednext_dw_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
+  if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
+  return s1_wgrad_ws(n, c, d, h, w, k, dtype);
+}
+
+int mednext_dw_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                     size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
+                     mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (x == nullptr || dy == nullptr || dweight == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned16(x) || !aligned16(dy) || !aligned(dweight, esz) || (dbias && !aligned(dbias, esz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < s1_wgrad_ws(n, c, d, h, w, k, dtype))
+    return MEDNEXT_ERR_WORKSPACE;
+  const S1Plan p = plan_s1(n, c, d, h, w, k, esz, true);
+  return dispatch_dw_s1_wgrad(dtype, k, x, dy, dweight, dbias, workspace, p, as_stream(stream));
+}
+
+// ------------------------------ depthwise stride 2 ------------------------------
+int mednext_dw_s2_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n, int64_t c, int64_t d,
+                      int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (x == nullptr || weight == nullptr || y == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(x, esz) || !aligned(y, esz) || !aligned(weight, esz) || (bias && !aligned(bias, esz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_dw_s2_gather(dtype, k, x, weight, bias, y, s2_geom_down(n, c, d, h, w), as_stream(stream));
+}
+
+int mednext_dw_s2_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c, int64_t d, int64_t h,
+                        int64_t w, int k, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (dy == nullptr || weight == nullptr || dx == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(dy, esz) || !aligned(dx, esz) || !aligned(weight, esz)) return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_dw_s2_scatter(dtype, k, dy, weight, nullptr, dx, s2_geom_down(n, c, d, h, w), as_stream(stream));
+}
+
+size_t mednext_dw_s2_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
+  if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
+  const DwS2Geom g = s2_geom_down(n, c, d, h, w);
+  return s2_wgrad_ws(n, c, (size_t)g.Ds * g.Hs * g.Ws, k, dtype);
+}
+
+int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                        size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
+                        int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (x == nullptr || dy == nullptr || dweight == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(x, esz) || !aligned(dy, esz) || !aligned(dweight, esz) || (dbias && !aligned(dbias, esz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  if (workspace == nullptr || !aligned16(workspace) ||
+      workspace_bytes < mednext_dw_s2_wgrad_workspace_size(n, c, d, h, w, k, dtype))
+    return MEDNEXT_ERR_WORKSPACE;
+  return dispatch_dw_s2_wgrad(dtype, k, x, dy, dweight, dbias, workspace, s2_geom_down(n, c, d, h, w), false,
+                              as_stream(stream));
+}
+
+// ------------------------------ depthwise transpose ------------------------------
+int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n, int64_t c, int64_t d,
+                    int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (x == nullptr || weight == nullptr || y == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(x, esz) || !aligned(y, esz) || !aligned(weight, esz) || (bias && !aligned(bias, esz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_dw_s2_scatter(dtype, k, x, weight, bias, y, s2_geom_up(n, c, d, h, w), as_stream(stream));
+}
+
+int mednext_dwT_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c, int64_t d, int64_t h,
+                      int64_t w, int k, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (dy == nullptr || weight == nullptr || dx == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(dy, esz) || !aligned(dx, esz) || !aligned(weight, esz)) return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_dw_s2_gather(dtype, k, dy, weight, nullptr, dx, s2_geom_up(n, c, d, h, w), as_stream(stream));
+}
+
+size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
+  if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
+  return s2_wgrad_ws(n, c, (size_t)d * h * w, k, dtype);
+}
+
+int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                      size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
+                      int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (x == nullptr || dy == nullptr || dweight == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(x, esz) || !aligned(dy, esz) || !aligned(dweight, esz) || (dbias && !aligned(dbias, esz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  if (workspace == nullptr || !aligned16(workspace) ||
+      workspace_bytes < mednext_dwT_wgrad_workspace_size(n, c, d, h, w, k, dtype))
+    return MEDNEXT_ERR_WORKSPACE;
+  // big grid = dy (2S-1), small grid = x (S); the bias grad sums dy (big)
+  return dispatch_dw_s2_wgrad(dtype, k, dy, x, dweight, dbias, workspace, s2_geom_up(n, c, d, h, w), true,
+                              as_stream(stream));
+}
+
+// ------------------------------ GroupNorm ------------------------------
+size_t mednext_gn_stats_workspace_size(int64_t n, int64_t c, int64_t spatial) {
+  if (!gn_shape_ok(n, c, spatial)) return 0;
+  return (size_t)n * c * gn_chunks(n * c, spatial) * sizeof(GnPartial);
+}
+
+int mednext_gn_stats(const void* x, float* stats, void* workspace, size_t workspace_bytes, int64_t n, int64_t c,
+                     int64_t spatial, float eps, int dtype, mednext_stream_t stream) {
+  if (elem_size(dtype) == 0) return MEDNEXT_ERR_BAD_DTYPE;
+  if (x == nullptr || stats == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if (!gn_shape_ok(n, c, spatial)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (!aligned(x, elem_size(dtype)) || !aligned(stats, 8)) return MEDNEXT_ERR_ALIGNMENT;
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < mednext_gn_stats_workspace_size(n, c, spatial))
+    return MEDNEXT_ERR_WORKSPACE;
+  return dispatch_gn_stats(dtype, x, static_cast<GnPartial*>(workspace), n * c, spatial, gn_chunks(n * c, spatial),
+                           eps, stats, as_stream(stream));
+}
+
+int mednext_gn_fwd(const void* x, const float* stats, const void* gamma, const void* beta, void* y, int64_t n,
+                   int64_t c, int64_t spatial, int x_dtype, int y_dtype, int gamma_dtype, mednext_stream_t stream) {
+  if (elem_size(x_dtype) == 0 || elem_size(y_dtype) == 0 || elem_size(gamma_dtype) == 0) return MEDNEXT_ERR_BAD_DTYPE;
+  if (x == nullptr || stats == nullptr || y == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if (!gn_shape_ok(n, c, spatial)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (!aligned(x, elem_size(x_dtype)) || !aligned(y, elem_size(y_dtype))) return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_gn_fwd(x_dtype, y_dtype, gamma_dtype, x, stats, gamma, beta, y, (int)c, n * c, spatial,
+                         as_stream(stream));
+}
+
+size_t mednext_gn_bwd_workspace_size(int64_t n, int64_t c, int64_t spatial) {
+  if (!gn_shape_ok(n, c, spatial)) return 0;
+  return (size_t)n * c * gn_chunks(n * c, spatial) * sizeof(GnBwdPartial);
+}
+
+int mednext_gn_bwd(const void* dy, const void* x, const float* stats, const void* gamma, void* dx, float* dgamma,
+                   float* dbeta, void* workspace, size_t workspace_bytes, int64_t n, int64_t c, int64_t spatial,
+                   int dy_dtype, int x_dtype, int dx_dtype, int gamma_dtype, mednext_stream_t stream) {
+  if (elem_size(dy_dtype) == 0 || elem_size(x_dtype) == 0 || elem_size(gamma_dtype) == 0) return MEDNEXT_ERR_BAD_DTYPE;
+  if (dx_dtype != x_dtype) return MEDNEXT_ERR_BAD_DTYPE;
+  if (dy == nullptr || x == nullptr || stats == nullptr || dx == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if (!gn_shape_ok(n, c, spatial)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < mednext_gn_bwd_workspace_size(n, c, spatial))
+    return MEDNEXT_ERR_WORKSPACE;
+  const int chunks = gn_chunks(n * c, spatial);
+  GnBwdPartial* part = static_cast<GnBwdPartial*>(workspace);
+  int st = dispatch_gn_bwd_partial(x_dtype, dy_dtype, dy, x, stats, part, n * c, spatial, chunks, as_stream(stream));
+  if (st != MEDNEXT_OK) return st;
+  return dispatch_gn_bwd_apply(x_dtype, dy_dtype, gamma_dtype, dy, x, stats, gamma, part, chunks, dx, dgamma, dbeta,
+                               (int)n, (int)c, spatial, as_stream(stream));
+}
+
+int mednext_gn_bwd_from_partials(const void* dz, const void* x, const float* stats, const void* gamma, void* dx,
+                                 float* dgamma, float* dbeta, const void* pw_workspace, int64_t n, int64_t c,
+                                 int64_t vox, int dz_dtype, int x_dtype, int dx_dtype, int gamma_dtype,
+                                 mednext_stream_t stream) {
+  if (elem_size(dz_dtype) == 0 || elem_size(x_dtype) == 0 || elem_size(gamma_dtype) == 0) return MEDNEXT_ERR_BAD_DTYPE;
+  if (dx_dtype != x_dtype) return MEDNEXT_ERR_BAD_DTYPE;
+  if (dz == nullptr || x == nullptr || stats == nullptr || dx == nullptr || pw_workspace == nullptr)
+    return MEDNEXT_ERR_NULL_POINTER;
+  if (!gn_shape_ok(n, c, vox)) return MEDNEXT_ERR_BAD_SHAPE;
+  const int mtiles = (int)((vox + kPwBM - 1) / kPwBM);
+  return dispatch_gn_bwd_apply(x_dtype, dz_dtype, gamma_dtype, dz, x, stats, gamma,
+                               static_cast<const GnBwdPartial*>(pw_workspace), mtiles, dx, dgamma, dbeta, (int)n,
+                               (int)c, vox, as_stream(stream));
+}
+
+// ------------------------------ pointwise ------------------------------
+size_t mednext_pw_fwd_workspace_size(int64_t n, int64_t cin, int64_t cout, int64_t vox, int epilogue) {
+  if (!pw_shape_ok(n, cin, cout, vox)) return 0;
+  if (!(epilogue & MEDNEXT_EPI_GN_BWD_STATS)) return 0;
+  const int64_t mtiles = (vox + kPwBM - 1) / kPwBM;
+  return (size_t)n * cout * mtiles * sizeof(GnBwdPartial);
+}
+
+int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const float* pro_stats,
+                   const float* pro_gamma, const float* pro_beta, int epilogue, const float* bias,
+                   const void* residual, const void* aux, const float* epi_stats, void* workspace,
+                   size_t workspace_bytes, int64_t n, int64_t cin, int64_t cout, int64_t vox, int a_dtype,
+                   int y_dtype, mednext_stream_t stream) {
+  if (!pw_dtype_ok(a_dtype)) return MEDNEXT_ERR_BAD_DTYPE;
+  if (y_dtype != a_dtype && y_dtype != MEDNEXT_FLOAT32) return MEDNEXT_ERR_BAD_DTYPE;
+  if (!pw_shape_ok(n, cin, cout, vox)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (prologue < MEDNEXT_PRO_NONE || prologue > MEDNEXT_PRO_GELU) return MEDNEXT_ERR_BAD_SHAPE;
+  if (epilogue & ~15) return MEDNEXT_ERR_BAD_SHAPE;
+  if (a == nullptr || wt == nullptr || y == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if (prologue == MEDNEXT_PRO_GROUPNORM && (pro_stats == nullptr || pro_gamma == nullptr || pro_beta == nullptr))
+    return MEDNEXT_ERR_NULL_POINTER;
+  if ((epilogue & MEDNEXT_EPI_BIAS) && bias == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if ((epilogue & MEDNEXT_EPI_RESIDUAL) && residual == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if ((epilogue & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) && aux == nullptr)
+    return MEDNEXT_ERR_NULL_POINTER;
+  if (epilogue & MEDNEXT_EPI_GN_BWD_STATS) {
+    if (epi_stats == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+    if (workspace == nullptr || !aligned16(workspace) ||
+        workspace_bytes < mednext_pw_fwd_workspace_size(n, cin, cout, vox, epilogue))
+      return MEDNEXT_ERR_WORKSPACE;
+  }
+  const size_t asz = elem_size(a_dtype), ysz = elem_size(y_dtype);
+  if (!aligned(a, asz) || !aligned(wt, asz) || !aligned(y, ysz) || (residual && !aligned(residual, ysz)) ||
+      (aux && !aligned(aux, asz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  PwFwdArgs args{};
+  args.a = a; args.wt = wt; args.y = y;
+  args.pro_stats = pro_stats; args.pro_gamma = pro_gamma; args.pro_beta = pro_beta;
+  args.bias = bias; args.residual = residual; args.aux = aux; args.epi_stats = epi_stats;
+  args.gn_part = static_cast<GnBwdPartial*>(workspace);
+  args.S = (int)n; args.cin = (int)cin; args.cout = (int)cout; args.vox = vox;
+  args.BN = pw_bn(cout);
+  args.mtiles = (int)((vox + kPwBM - 1) / kPwBM);
+  args.ntiles = (int)((cout + args.BN - 1) / args.BN);
+  args.epilogue = epilogue;
+  args.vec_a = (vox % 8 == 0) && aligned16(a);
+  args.vec_w = (cin % 8 == 0) && aligned16(wt);
+  if ((long long)args.S * args.ntiles * args.mtiles >= (1LL << 31)) return MEDNEXT_ERR_BAD_SHAPE;
+  return dispatch_pw_fwd(a_dtype, y_dtype, prologue, args, as_stream(stream));
+}
+
+size_t mednext_pw_wgrad_workspace_size(int64_t n, int64_t cin, int64_t cout, int64_t vox) {
+  if (!pw_shape_ok(n, cin, cout, vox)) return 0;
+  const PwWPlan p = plan_pw_wgrad(n, cin, cout, vox);
+  return align_up((size_t)p.splits * cout * cin * 4, 256) + (size_t)p.splits * cout * 4;
+}
+
+int mednext_pw_wgrad(const void* g, const void* a, float* dw, float* dbias, int prologue, const float* pro_stats,
+                     const float* pro_gamma, const float* pro_beta, void* workspace, size_t workspace_bytes,
+                     int64_t n, int64_t cin, int64_t cout, int64_t vox, int dtype, mednext_stream_t stream) {
+  if (!pw_dtype_ok(dtype)) return MEDNEXT_ERR_BAD_DTYPE;
+  if (!pw_shape_ok(n, cin, cout, vox)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (prologue < MEDNEXT_PRO_NONE || prologue > MEDNEXT_PRO_GELU) return MEDNEXT_ERR_BAD_SHAPE;
+  if (g == nullptr || a == nullptr || dw == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if (prologue == MEDNEXT_PRO_GROUPNORM && (pro_stats == nullptr || pro_gamma == nullptr || pro_beta == nullptr))
+    return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(g, esz) || !aligned(a, esz) || !aligned(dw, 4) || (dbias && !aligned(dbias, 4)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  if (workspace == nullptr || !aligned16(workspace) ||
+      workspace_bytes < mednext_pw_wgrad_workspace_size(n, cin, cout, vox))
+    return MEDNEXT_ERR_WORKSPACE;
+  const PwWPlan p = plan_pw_wgrad(n, cin, cout, vox);
+  PwWgradArgs args{};
+  args.g = g; args.a = a;
+  args.pro_stats = pro_stats; args.pro_gamma = pro_gamma; args.pro_beta = pro_beta;
+  args.part = static_cast<float*>(workspace);
+  args.part_b = reinterpret_cast<float*>(static_cast<char*>(workspace) + align_up((size_t)p.splits * cout * cin * 4, 256));
+  args.dw = dw; args.dbias = dbias;
+  args.S = (int)n; args.cin = (int)cin; args.cout = (int)cout; args.vox = vox;
+  args.BN = p.BN; args.mtiles = p.mtiles; args.ntiles = p.ntiles; args.splits = p.splits;
+  args.chunks_per_sample = p.cps; args.chunks_total = p.total; args.chunks_per_split = p.per;
+  args.vec = (vox % 8 == 0) && aligned16(g) && aligned16(a);
+  return dispatch_pw_wgrad(dtype, prologue, args, p.splits, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,297 @@
+// Shared device helpers for the sm_100a MedNeXt kernels: element traits,
+// 16-byte chunk unpacking, bounded mbarrier waits, the device error word and
+// thin inline-PTX wrappers for tcgen05 (TMEM alloc / MMA / commit / ld).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mednext_b200.h"
+
+namespace mednext {
+
+// ----------------------------------------------------------------------------
+// Element traits.  Acc is the accumulation type: fp64 inputs accumulate in
+// fp64 (the reference does the same, ops/_triton/depthwise.py:190,299), all
+// other inputs accumulate in fp32.
+// ----------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  using Acc = float;
+  static __device__ __forceinline__ float load(const float* p) { return *p; }
+  static __device__ __forceinline__ float from(float v) { return v; }
+  static __device__ __forceinline__ float to(float v) { return v; }
+};
+template <> struct Elem<double> {
+  using Acc = double;
+  static __device__ __forceinline__ double from(double v) { return v; }
+  static __device__ __forceinline__ double to(double v) { return v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+  using Acc = float;
+  static __device__ __forceinline__ float from(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 to(float v) { return __float2bfloat16_rn(v); }
+};
+template <> struct Elem<__half> {
+  using Acc = float;
+  static __device__ __forceinline__ float from(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half to(float v) { return __float2half_rn(v); }
+};
+
+template <typename T>
+__device__ __forceinline__ typename Elem<T>::Acc to_acc(T v) {
+  return Elem<T>::from(v);
+}
+template <typename T, typename A>
+__device__ __forceinline__ T from_acc(A v) {
+  return Elem<T>::to(v);
+}
+
+// Unpack one 16-byte chunk holding 16/sizeof(T) elements into Acc values.
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& q, typename Elem<T>::Acc* out);
+template <>
+__device__ __forceinline__ void unpack16<float>(const uint4& q, float* out) {
+  out[0] = __uint_as_float(q.x);
+  out[1] = __uint_as_float(q.y);
+  out[2] = __uint_as_float(q.z);
+  out[3] = __uint_as_float(q.w);
+}
+template <>
+__device__ __forceinline__ void unpack16<double>(const uint4& q, double* out) {
+  out[0] = __hiloint2double(q.y, q.x);
+  out[1] = __hiloint2double(q.w, q.z);
+}
+template <>
+__device__ __forceinline__ void unpack16<__nv_bfloat16>(const uint4& q, float* out) {
+  // bf16 -> fp32 is exact: the bf16 bits become the top half of the fp32.
+  const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(v[i] << 16);
+    out[2 * i + 1] = __uint_as_float(v[i] & 0xffff0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void unpack16<__half>(const uint4& q, float* out) {
+  const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = *reinterpret_cast<const __half2*>(&v[i]);
+    float2 f = __half22float2(h);
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
+// Pack 16/sizeof(T) Acc values into one 16-byte chunk (round to nearest even).
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const typename Elem<T>::Acc* in);
+template <>
+__device__ __forceinline__ uint4 pack16<float>(const float* in) {
+  return make_uint4(__float_as_uint(in[0]), __float_as_uint(in[1]), __float_as_uint(in[2]),
+                    __float_as_uint(in[3]));
+}
+template <>
+__device__ __forceinline__ uint4 pack16<double>(const double* in) {
+  return make_uint4(__double2loint(in[0]), __double2hiint(in[0]), __double2loint(in[1]),
+                    __double2hiint(in[1]));
+}
+template <>
+__device__ __forceinline__ uint4 pack16<__nv_bfloat16>(const float* in) {
+  uint32_t v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 b = __floats2bfloat162_rn(in[2 * i], in[2 * i + 1]);
+    v[i] = *reinterpret_cast<uint32_t*>(&b);
+  }
+  return make_uint4(v[0], v[1], v[2], v[3]);
+}
+template <>
+__device__ __forceinline__ uint4 pack16<__half>(const float* in) {
+  uint32_t v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(in[2 * i], in[2 * i + 1]);
+    v[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(v[0], v[1], v[2], v[3]);
+}
+
+// ----------------------------------------------------------------------------
+// Device error word.  Kernels never trap; a wait that exceeds its bound
+// records a code here and the kernel returns.
+// ----------------------------------------------------------------------------
+enum DeviceError : int {
+  kErrNone = 0,
+  kErrMbarTimeout = 0x100,
+  kErrTmemAlloc = 0x200,
+};
+// One word per translation unit (internal linkage); mednext_device_error()
+// reads and clears all of them.
+static __device__ int g_device_error = 0;
+
+__device__ __forceinline__ void raise_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
+
+// ----------------------------------------------------------------------------
+// mbarrier helpers (shared::cta).  Every wait is bounded.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_mbarrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bound on one wait: far above any legitimate wait in these kernels (they
+// wait microseconds for a copy or an MMA), far below anything that would
+// look like a hung GPU.
+constexpr uint64_t kMaxWaitNs = 250ull * 1000ull * 1000ull;
+
+// Returns false (and records the error) when the bound is exceeded.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i) {
+      if (mbar_try_wait(bar, parity)) return true;
+    }
+    if (global_timer_ns() - t0 > kMaxWaitNs) break;
+  }
+  raise_device_error(kErrMbarTimeout);
+  return false;
+}
+
+// ----------------------------------------------------------------------------
+// tcgen05 wrappers (PTX ISA 8.6+, sm_100a).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Make generic-proxy shared-memory writes visible to the async proxy (MMA/TMA).
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16, issued by one thread.
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on an mbarrier once all previously issued MMAs of this thread finish.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns; thread i of the warp gets lane
+// (warp%4)*32 + i.  Must be followed by tmem_ld_wait() before use.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for tcgen05.mma, SWIZZLE_128B layouts.
+//   K-major: 8-row x 128-byte atoms; sbo = byte stride between 8-row groups.
+//   MN-major: 64-element x 8-k atoms; lbo = byte stride between atoms along
+//   M/N, sbo = byte stride between atoms along K.
+// Bits: [0,14) addr>>4, [16,30) lbo>>4, [32,46) sbo>>4, [46,48) version=1,
+// [61,64) layout (2 = SWIZZLE_128B).
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// Instruction descriptor, kind::f16 with fp32 accumulation.
+//   ab_bf16: operands are bf16 (else fp16); a_mn / b_mn: operand is MN-major.
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool ab_bf16, bool a_mn,
+                                                      bool b_mn) {
+  return (1u << 4)                                     // D = f32
+         | ((ab_bf16 ? 1u : 0u) << 7)                  // A format
+         | ((ab_bf16 ? 1u : 0u) << 10)                 // B format
+         | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Exact GELU, the erf form used by F.gelu(approximate="none").
+__device__ __forceinline__ float gelu_f(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+}
+// d/dx of the exact GELU: Phi(x) + x * phi(x).
+__device__ __forceinline__ float gelu_grad_f(float x) {
+  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
+  const float pdf = 0.39894228040143267794f * expf(-0.5f * x * x);
+  return cdf + x * pdf;
+}
+
+}  // namespace mednext

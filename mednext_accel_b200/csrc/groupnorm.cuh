@@ -1,0 +1,208 @@
+// GroupNorm with groups == channels (nn.GroupNorm(C, C), models/blocks.py:74 of
+// the reference): per-(sample, channel) statistics over the spatial volume.
+//   forward : z = (x - mean) * rstd * gamma + beta,  rstd = 1/sqrt(var + eps)
+//   backward: dx = rstd * gamma * (dz - S1/V - xhat * S2/V),
+//             S1 = sum dz, S2 = sum dz * xhat;  dgamma = sum_n S2, dbeta = sum_n S1
+// Every reduction is two-pass with a fixed order, so results are bitwise
+// reproducible from run to run.
+#pragma once
+
+#include "common.cuh"
+#include "depthwise_s1.cuh"  // GnPartial, chan_merge, block_merge_stats
+
+namespace mednext {
+
+struct GnBwdPartial {
+  double s1, s2;
+};
+
+// Merge the per-tile (count, mean, M2) partials of each (n, c) in tile order.
+static __global__ void gn_finalize_kernel(const GnPartial* __restrict__ part, int tiles, int nc_total,
+                                   float eps, float* __restrict__ stats) {
+  const int nc = blockIdx.x * blockDim.x + threadIdx.x;
+  if (nc >= nc_total) return;
+  double n = 0.0, mean = 0.0, m2 = 0.0;
+  const GnPartial* p = part + (size_t)nc * tiles;
+  for (int t = 0; t < tiles; ++t) chan_merge(n, mean, m2, p[t].count, p[t].mean, p[t].m2);
+  const double var = n > 0.0 ? m2 / n : 0.0;  // biased variance, as GroupNorm uses
+  stats[2 * nc] = (float)mean;
+  stats[2 * nc + 1] = (float)(1.0 / sqrt(var + (double)eps));
+}
+
+template <typename T>
+__device__ __forceinline__ bool vec_ok(const void* p, size_t vol) {
+  constexpr int E = 16 / (int)sizeof(T);
+  return (vol % E) == 0 && ((reinterpret_cast<uintptr_t>(p) & 15) == 0);
+}
+
+// Standalone statistics: per-thread shifted sums, block Chan merge, one
+// partial per (n, c, chunk).
+template <typename T>
+__global__ void __launch_bounds__(256) gn_stats_partial_kernel(const T* __restrict__ x,
+                                                               GnPartial* __restrict__ part,
+                                                               size_t vol, int chunks) {
+  using Acc = typename Elem<T>::Acc;
+  const int j = blockIdx.x % chunks;
+  const size_t nc = blockIdx.x / chunks;
+  const size_t per = (vol + chunks - 1) / chunks;
+  const size_t beg = (size_t)j * per;
+  const size_t end = min(beg + per, vol);
+  const T* p = x + nc * vol;
+  Acc cnt = Acc(0), shift = Acc(0), s1 = Acc(0), s2 = Acc(0);
+  for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+    const Acc v = to_acc<T>(__ldg(p + i));
+    if (cnt == Acc(0)) shift = v;
+    const Acc d = v - shift;
+    s1 += d;
+    s2 = fma(d, d, s2);
+    cnt += Acc(1);
+  }
+  double n = (double)cnt, mean = 0.0, m2 = 0.0;
+  if (cnt > Acc(0)) {
+    mean = (double)shift + (double)s1 / n;
+    m2 = fmax((double)s2 - (double)s1 * (double)s1 / n, 0.0);
+  }
+  __shared__ double red[3 * 32];
+  block_merge_stats(n, mean, m2, red);
+  if (threadIdx.x == 0) {
+    GnPartial gp;
+    gp.count = n;
+    gp.mean = mean;
+    gp.m2 = m2;
+    gp.pad = 0.0;
+    part[nc * chunks + j] = gp;
+  }
+}
+
+template <typename G>
+__device__ __forceinline__ float param_f(const G* p, int c) {
+  return (float)to_acc<G>(p[c]);
+}
+
+// z = (x - mean) * rstd * gamma + beta
+template <typename TX, typename TY, typename TG>
+__global__ void __launch_bounds__(256) gn_fwd_kernel(const TX* __restrict__ x,
+                                                     const float* __restrict__ stats,
+                                                     const TG* __restrict__ gamma,
+                                                     const TG* __restrict__ beta,
+                                                     TY* __restrict__ y, int C, size_t vol,
+                                                     int chunks) {
+  const int j = blockIdx.x % chunks;
+  const size_t nc = blockIdx.x / chunks;
+  const int c = (int)(nc % C);
+  const float mean = stats[2 * nc], rstd = stats[2 * nc + 1];
+  const float a = rstd * (gamma != nullptr ? param_f(gamma, c) : 1.0f);
+  const float bsh = (beta != nullptr ? param_f(beta, c) : 0.0f) - mean * a;
+  const size_t per = (vol + chunks - 1) / chunks;
+  const size_t beg = (size_t)j * per;
+  const size_t end = min(beg + per, vol);
+  const TX* src = x + nc * vol;
+  TY* dst = y + nc * vol;
+  for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+    const float v = (float)to_acc<TX>(src[i]);
+    dst[i] = from_acc<TY>((typename Elem<TY>::Acc)fmaf(v, a, bsh));
+  }
+}
+
+// Backward pass 1: S1 = sum dz, S2 = sum dz * xhat per (n, c, chunk).
+template <typename TD, typename TX>
+__global__ void __launch_bounds__(256) gn_bwd_partial_kernel(const TD* __restrict__ dz,
+                                                             const TX* __restrict__ x,
+                                                             const float* __restrict__ stats,
+                                                             GnBwdPartial* __restrict__ part,
+                                                             size_t vol, int chunks) {
+  const int j = blockIdx.x % chunks;
+  const size_t nc = blockIdx.x / chunks;
+  const float mean = stats[2 * nc], rstd = stats[2 * nc + 1];
+  const size_t per = (vol + chunks - 1) / chunks;
+  const size_t beg = (size_t)j * per;
+  const size_t end = min(beg + per, vol);
+  const TD* g = dz + nc * vol;
+  const TX* xs = x + nc * vol;
+  float s1 = 0.f, s2 = 0.f;
+  for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+    const float d = (float)to_acc<TD>(__ldg(g + i));
+    const float xh = ((float)to_acc<TX>(__ldg(xs + i)) - mean) * rstd;
+    s1 += d;
+    s2 = fmaf(d, xh, s2);
+  }
+  __shared__ float red[2 * 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[2 * (threadIdx.x >> 5)] = s1;
+    red[2 * (threadIdx.x >> 5) + 1] = s2;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0, b = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      a += red[2 * w];
+      b += red[2 * w + 1];
+    }
+    GnBwdPartial gp;
+    gp.s1 = a;
+    gp.s2 = b;
+    part[nc * chunks + j] = gp;
+  }
+}
+
+// Backward pass 2: dx = rstd * gamma * (dz - S1/V - xhat * S2/V).
+// Each CTA first folds the partials of its (n, c) in a fixed order.
+template <typename TD, typename TX, typename TO, typename TG>
+__global__ void __launch_bounds__(256) gn_bwd_apply_kernel(
+    const TD* __restrict__ dz, const TX* __restrict__ x, const float* __restrict__ stats,
+    const TG* __restrict__ gamma, const GnBwdPartial* __restrict__ part, int part_tiles,
+    TO* __restrict__ dx, int C, size_t vol, int chunks) {
+  const int j = blockIdx.x % chunks;
+  const size_t nc = blockIdx.x / chunks;
+  const int c = (int)(nc % C);
+  __shared__ float sh[2];
+  if (threadIdx.x == 0) {
+    double a = 0.0, b = 0.0;
+    const GnBwdPartial* p = part + nc * part_tiles;
+    for (int t = 0; t < part_tiles; ++t) {
+      a += p[t].s1;
+      b += p[t].s2;
+    }
+    sh[0] = (float)(a / (double)vol);
+    sh[1] = (float)(b / (double)vol);
+  }
+  __syncthreads();
+  const float m1 = sh[0], m2 = sh[1];
+  const float mean = stats[2 * nc], rstd = stats[2 * nc + 1];
+  const float gr = rstd * (gamma != nullptr ? param_f(gamma, c) : 1.0f);
+  const size_t per = (vol + chunks - 1) / chunks;
+  const size_t beg = (size_t)j * per;
+  const size_t end = min(beg + per, vol);
+  const TD* g = dz + nc * vol;
+  const TX* xs = x + nc * vol;
+  TO* o = dx + nc * vol;
+  for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+    const float d = (float)to_acc<TD>(__ldg(g + i));
+    const float xh = ((float)to_acc<TX>(__ldg(xs + i)) - mean) * rstd;
+    o[i] = from_acc<TO>((typename Elem<TO>::Acc)(gr * (d - m1 - xh * m2)));
+  }
+}
+
+// dgamma[c] = sum_n S2[n,c], dbeta[c] = sum_n S1[n,c] (fixed order).
+static __global__ void gn_param_grad_kernel(const GnBwdPartial* __restrict__ part, int part_tiles, int N,
+                                     int C, float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  double a = 0.0, b = 0.0;
+  for (int n = 0; n < N; ++n) {
+    const GnBwdPartial* p = part + ((size_t)n * C + c) * part_tiles;
+    for (int t = 0; t < part_tiles; ++t) {
+      a += p[t].s1;
+      b += p[t].s2;
+    }
+  }
+  if (dbeta != nullptr) dbeta[c] = (float)a;
+  if (dgamma != nullptr) dgamma[c] = (float)b;
+}
+
+}  // namespace mednext

@@ -1,0 +1,98 @@
+// Template instantiation and launch of the depthwise kernels (stride 2 and
+// transpose) for every supported element type and kernel size.
+#include "plan.h"
+
+namespace mednext {
+
+namespace {
+template <typename T>
+int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, int C, int tiles, int K3,
+                 cudaStream_t s) {
+  const int total = C * (K3 + 1);
+  dw_wgrad_finish_kernel<T><<<(total + 127) / 128, 128, 0, s>>>(part, static_cast<T*>(dw), static_cast<T*>(db), N,
+                                                                C, tiles, K3);
+  return record_launch();
+}
+
+unsigned grid_1d(size_t total, int threads) {
+  const size_t blocks = (total + threads - 1) / threads;
+  return (unsigned)std::min<size_t>(std::max<size_t>(blocks, 1), (size_t)148 * 32);
+}
+
+template <typename T, int K>
+int launch_gather(const void* big, const void* w, const void* b, void* small, const DwS2Geom& g, cudaStream_t s) {
+  const size_t total = (size_t)g.N * g.C * g.Ds * g.Hs * g.Ws;
+  dw_s2_gather_kernel<T, K><<<grid_1d(total, 256), 256, 0, s>>>(
+      static_cast<const T*>(big), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(small), g);
+  return record_launch();
+}
+template <typename T, int K>
+int launch_scatter(const void* small, const void* w, const void* b, void* big, const DwS2Geom& g, cudaStream_t s) {
+  const size_t total = (size_t)g.N * g.C * g.Db * g.Hb * g.Wb;
+  dw_s2_scatter_kernel<T, K><<<grid_1d(total, 256), 256, 0, s>>>(
+      static_cast<const T*>(small), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(big), g);
+  return record_launch();
+}
+template <typename T, int K>
+int launch_s2_wgrad(const void* big, const void* small, void* dw, void* db, void* ws, const DwS2Geom& g,
+                    bool bias_from_big, cudaStream_t s) {
+  using Acc = typename Elem<T>::Acc;
+  const size_t svol = (size_t)g.Ds * g.Hs * g.Ws;
+  const S2WPlan p = plan_s2w(g.N, g.C, svol, K);
+  Acc* part = static_cast<Acc*>(ws);
+  const unsigned grid = (unsigned)((size_t)g.N * g.C * p.chunks);
+  dw_s2_wgrad_kernel<T, K><<<grid, p.threads, 0, s>>>(static_cast<const T*>(big), static_cast<const T*>(small), part,
+                                                      g, p.chunk, p.chunks, bias_from_big ? 0 : 1);
+  int st = record_launch();
+  if (st != MEDNEXT_OK) return st;
+  if (bias_from_big && db != nullptr) {
+    const size_t bvol = (size_t)g.Db * g.Hb * g.Wb;
+    chan_sum_into_partials_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(big), part, bvol, p.chunks, K * K * K);
+    st = record_launch();
+    if (st != MEDNEXT_OK) return st;
+  }
+  return finish_wgrad<T>(part, dw, db, g.N, g.C, p.chunks, K * K * K, s);
+}
+
+}  // namespace
+
+#define MEDNEXT_K_SWITCH(k, KC, ...)                         \
+  switch (k) {                                               \
+    case 1: { constexpr int KC = 1; __VA_ARGS__; } break;    \
+    case 3: { constexpr int KC = 3; __VA_ARGS__; } break;    \
+    case 5: { constexpr int KC = 5; __VA_ARGS__; } break;    \
+    case 7: { constexpr int KC = 7; __VA_ARGS__; } break;    \
+    default: return MEDNEXT_ERR_BAD_KERNEL;                  \
+  }
+#define MEDNEXT_T_SWITCH(dtype, TC, ...)                                     \
+  switch (dtype) {                                                           \
+    case MEDNEXT_FLOAT32: { using TC = float; __VA_ARGS__; } break;          \
+    case MEDNEXT_BFLOAT16: { using TC = __nv_bfloat16; __VA_ARGS__; } break; \
+    case MEDNEXT_FLOAT16: { using TC = __half; __VA_ARGS__; } break;         \
+    case MEDNEXT_FLOAT64: { using TC = double; __VA_ARGS__; } break;         \
+    default: return MEDNEXT_ERR_BAD_DTYPE;                                   \
+  }
+
+int dispatch_dw_s2_gather(int dtype, int k, const void* big, const void* w, const void* b, void* small,
+                          const DwS2Geom& g, cudaStream_t s) {
+  int st = MEDNEXT_OK;
+  MEDNEXT_T_SWITCH(dtype, T, MEDNEXT_K_SWITCH(k, KC, st = (launch_gather<T, KC>(big, w, b, small, g, s))));
+  return st;
+}
+int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, const void* b, void* big,
+                           const DwS2Geom& g, cudaStream_t s) {
+  int st = MEDNEXT_OK;
+  MEDNEXT_T_SWITCH(dtype, T, MEDNEXT_K_SWITCH(k, KC, st = (launch_scatter<T, KC>(small, w, b, big, g, s))));
+  return st;
+}
+int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,
+                         const DwS2Geom& g, bool bias_from_big, cudaStream_t s) {
+  int st = MEDNEXT_OK;
+  MEDNEXT_T_SWITCH(dtype, T,
+                   MEDNEXT_K_SWITCH(k, KC, st = (launch_s2_wgrad<T, KC>(big, small, dw, db, ws, g, bias_from_big, s))));
+  return st;
+}
+
+MEDNEXT_DEFINE_ERROR_READER(read_clear_errors_dw2)
+
+}  // namespace mednext

@@ -1,0 +1,199 @@
+// Host-side tile planning and the per-family dispatch functions that
+// launch_dw.cu, launch_gn.cu and launch_pw.cu define (one translation unit per
+// kernel family so the library builds in parallel).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "../../include/mednext_b200.h"
+#include "depthwise_s1.cuh"
+#include "depthwise_s2.cuh"
+#include "groupnorm.cuh"
+#include "pointwise.cuh"
+
+namespace mednext {
+
+constexpr int kTargetCtas = 148 * 4;  // 4 resident CTAs per SM on 148 SMs
+
+inline size_t elem_size(int dtype) {
+  switch (dtype) {
+    case MEDNEXT_FLOAT32: return 4;
+    case MEDNEXT_BFLOAT16: return 2;
+    case MEDNEXT_FLOAT16: return 2;
+    case MEDNEXT_FLOAT64: return 8;
+    default: return 0;
+  }
+}
+inline size_t acc_size(int dtype) { return dtype == MEDNEXT_FLOAT64 ? 8 : 4; }
+
+// ------------------------------ stride-1 depthwise ------------------------------
+struct S1Plan {
+  DwS1Geom g;
+  int threads;
+  size_t smem;
+  long long grid;
+};
+
+inline int nh_for(int k) { return k <= 3 ? 2 : 1; }
+
+inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, size_t esz, bool wgrad) {
+  S1Plan p{};
+  DwS1Geom& g = p.g;
+  g.N = (int)n; g.C = (int)c; g.D = (int)d; g.H = (int)h; g.W = (int)w;
+  const int NH = nh_for(k);
+  int lw = 1;
+  while (lw * kDwNW < w && lw < 16) lw *= 2;
+  g.LW = lw;
+  g.TW = kDwNW * lw;
+  const bool grouped = wgrad && k >= 5;
+  const int rows_needed = (int)((h + NH - 1) / NH);
+  int tr;
+  if (grouped) {
+    tr = std::max(1, std::min(64 / lw, rows_needed));
+    const int G = ((lw * tr + 31) / 32) * 32;
+    p.threads = G * k;
+  } else {
+    tr = std::max(1, std::min(256 / lw, rows_needed));
+    p.threads = ((lw * tr + 31) / 32) * 32;
+  }
+  g.TR = tr;
+  g.TH = tr * NH;
+  g.tilesW = (int)((w + g.TW - 1) / g.TW);
+  g.tilesH = (int)((h + g.TH - 1) / g.TH);
+  const long long base = (long long)n * c * g.tilesW * g.tilesH;
+  long long chunks = (kTargetCtas + base - 1) / base;
+  chunks = std::max(1LL, std::min(chunks, std::max(1LL, (long long)(d / 8))));
+  g.TD = (int)((d + chunks - 1) / chunks);
+  g.tilesD = (int)((d + g.TD - 1) / g.TD);
+  const int E = (int)(16 / esz);
+  g.vec = (w % E) == 0 ? 1 : 0;
+  const int P = k / 2;
+  const int off = ((P + E - 1) / E) * E;
+  const size_t rsw = (size_t)g.TW + 2 * off;
+  const size_t tile = (size_t)(g.TH + 2 * P) * rsw * esz;
+  const size_t acc = esz == 8 ? 8 : 4;
+  p.smem = wgrad ? tile : (((size_t)k * k * k * acc + 15) / 16) * 16 + tile;
+  p.grid = base * g.tilesD;
+  return p;
+}
+inline size_t s1_tiles(const S1Plan& p) { return (size_t)p.g.tilesW * p.g.tilesH * p.g.tilesD; }
+
+// ------------------------------ stride-2 depthwise ------------------------------
+constexpr int kS2Group = 64;
+struct S2WPlan {
+  int chunk, chunks, threads;
+};
+inline S2WPlan plan_s2w(int64_t n, int64_t c, size_t svol, int k) {
+  S2WPlan p{};
+  const long long nc = n * c;
+  const long long want = std::max(1LL, (long long)kTargetCtas / std::max(1LL, nc));
+  long long chunk = std::max<long long>(256, (long long)((svol + want - 1) / want));
+  chunk = std::min<long long>(chunk, (long long)svol);
+  p.chunk = (int)chunk;
+  p.chunks = (int)((svol + chunk - 1) / chunk);
+  p.threads = kS2Group * k;
+  return p;
+}
+inline DwS2Geom s2_geom_down(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w) {
+  DwS2Geom g{};
+  g.N = (int)n; g.C = (int)c;
+  g.Db = (int)d; g.Hb = (int)h; g.Wb = (int)w;
+  g.Ds = (int)((d + 1) / 2); g.Hs = (int)((h + 1) / 2); g.Ws = (int)((w + 1) / 2);
+  return g;
+}
+inline DwS2Geom s2_geom_up(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w) {
+  DwS2Geom g{};
+  g.N = (int)n; g.C = (int)c;
+  g.Ds = (int)d; g.Hs = (int)h; g.Ws = (int)w;
+  g.Db = (int)(2 * d - 1); g.Hb = (int)(2 * h - 1); g.Wb = (int)(2 * w - 1);
+  return g;
+}
+
+// ------------------------------ GroupNorm ------------------------------
+inline int gn_chunks(int64_t nc, int64_t vol) {
+  const long long want = std::max(1LL, (long long)kTargetCtas * 2 / std::max<int64_t>(1, nc));
+  const long long maxc = std::max<long long>(1, vol / 2048);
+  return (int)std::max(1LL, std::min(want, maxc));
+}
+
+// ------------------------------ pointwise ------------------------------
+inline int pw_bn(int64_t cout) {
+  if (cout >= 256) return 256;
+  return (int)(((cout + 15) / 16) * 16);
+}
+inline size_t pw_smem(int BN) { return 32768 + 2 * (size_t)BN * 128 + 1024; }
+struct PwWPlan {
+  int BN, mtiles, ntiles, splits;
+  long long cps, total, per;
+};
+inline PwWPlan plan_pw_wgrad(int64_t n, int64_t cin, int64_t cout, int64_t vox) {
+  PwWPlan p{};
+  p.BN = pw_bn(cin);
+  p.mtiles = (int)((cout + kPwBM - 1) / kPwBM);
+  p.ntiles = (int)((cin + p.BN - 1) / p.BN);
+  p.cps = (vox + kPwBK - 1) / kPwBK;
+  p.total = p.cps * n;
+  long long splits = std::max(1LL, (long long)(148 * 2) / (p.mtiles * p.ntiles));
+  splits = std::min(splits, 128LL);
+  splits = std::min(splits, p.total);
+  p.per = (p.total + splits - 1) / splits;
+  p.splits = (int)((p.total + p.per - 1) / p.per);
+  return p;
+}
+
+// ------------------------------ dispatch (defined in launch_*.cu) ----------------
+// Each returns a mednext_status and never allocates.
+int dispatch_dw_s1_conv(int dtype, int k, const void* x, const void* w, const void* b, const void* addend, void* y,
+                        GnPartial* stats, const S1Plan& p, int flip, cudaStream_t s);
+int dispatch_dw_s1_wgrad(int dtype, int k, const void* x, const void* dy, void* dw, void* db, void* ws,
+                         const S1Plan& p, cudaStream_t s);
+int dispatch_dw_s2_gather(int dtype, int k, const void* big, const void* w, const void* b, void* small,
+                          const DwS2Geom& g, cudaStream_t s);
+int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, const void* b, void* big,
+                           const DwS2Geom& g, cudaStream_t s);
+int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,
+                         const DwS2Geom& g, bool bias_from_big, cudaStream_t s);
+int dispatch_gn_finalize(const GnPartial* part, int tiles, int nc, float eps, float* stats, cudaStream_t s);
+int dispatch_gn_stats(int dtype, const void* x, GnPartial* part, int64_t nc, int64_t vol, int chunks, float eps,
+                      float* stats, cudaStream_t s);
+int dispatch_gn_fwd(int x_dtype, int y_dtype, int g_dtype, const void* x, const float* stats, const void* gamma,
+                    const void* beta, void* y, int C, int64_t nc, int64_t vol, cudaStream_t s);
+int dispatch_gn_bwd_partial(int x_dtype, int dz_dtype, const void* dz, const void* x, const float* stats,
+                            GnBwdPartial* part, int64_t nc, int64_t vol, int chunks, cudaStream_t s);
+int dispatch_gn_bwd_apply(int x_dtype, int dz_dtype, int g_dtype, const void* dz, const void* x, const float* stats,
+                          const void* gamma, const GnBwdPartial* part, int part_tiles, void* dx, float* dgamma,
+                          float* dbeta, int N, int C, int64_t vol, cudaStream_t s);
+int dispatch_pw_fwd(int a_dtype, int y_dtype, int prologue, const PwFwdArgs& a, cudaStream_t s);
+int dispatch_pw_wgrad(int dtype, int prologue, const PwWgradArgs& a, int splits, cudaStream_t s);
+
+// Read and clear the device error word of every translation unit.
+int read_clear_errors_dw(int* code, cudaStream_t s);
+int read_clear_errors_dw2(int* code, cudaStream_t s);
+int read_clear_errors_gn(int* code, cudaStream_t s);
+int read_clear_errors_pw(int* code, cudaStream_t s);
+
+// Records the CUDA error of the last launch in a thread-local slot.
+int record_launch();
+int last_cuda_error();
+
+}  // namespace mednext
+
+// Per-translation-unit reader of the device error word.
+#define MEDNEXT_DEFINE_ERROR_READER(fn)                                                                  \
+  int fn(int* code, cudaStream_t s) {                                                                     \
+    int host = 0;                                                                                         \
+    if (cudaMemcpyFromSymbolAsync(&host, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s) !=    \
+            cudaSuccess ||                                                                                \
+        cudaStreamSynchronize(s) != cudaSuccess)                                                          \
+      return record_launch();                                                                             \
+    const int zero = 0;                                                                                   \
+    if (cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) !=      \
+            cudaSuccess ||                                                                                \
+        cudaStreamSynchronize(s) != cudaSuccess)                                                          \
+      return record_launch();                                                                             \
+    if (*code == 0) *code = host;                                                                         \
+    return MEDNEXT_OK;                                                                                    \
+  }

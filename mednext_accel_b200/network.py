@@ -1,0 +1,536 @@
+"""MedNeXt v1 network with the reference package's parameter schema.
+
+The module tree (``stem``, ``encoder_stages.i.j.{depthwise,norm,expand,project}``,
+``downsamples.i.residual``, ``bottleneck``, ``upsamples``, ``decoder_stages``,
+``head.conv``, ``deep_supervision_heads.i.conv``) and every parameter shape match
+the reference (models/blocks.py:47-194, models/mednext_v1.py:36-223,
+models/config.py:11-98), so ``state_dict`` keys, checkpoints and optimizers are
+interchangeable.  What differs is execution: once
+:func:`mednext_accel_b200.adaptive.install_adaptive_operators` has run, a
+MedNeXt block executes as one fused sm_100a operator (depthwise conv with
+GroupNorm statistics, tensor-core expand with GroupNorm applied on load, GELU,
+tensor-core compress with the residual added in the epilogue) instead of six
+separate PyTorch modules.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Mapping
+from dataclasses import dataclass
+from os import PathLike
+from typing import Literal, TypeAlias
+
+import torch
+from torch import Tensor, nn
+from torch.nn import functional as F
+from torch.utils.checkpoint import checkpoint
+
+DeepSupervisionOutput = Literal["tuple", "list", "stacked"]
+OptimizationSource: TypeAlias = Literal["auto", "reference"] | str | PathLike[str] | Mapping[str, object]
+
+# Published variants (reference models/config.py:11-23).
+BLOCK_COUNTS: dict[str, tuple[int, ...]] = {
+    "small": (2,) * 9,
+    "base": (2,) * 9,
+    "medium": (3, 4, 4, 4, 4, 4, 4, 4, 3),
+    "large": (3, 4, 8, 8, 8, 8, 8, 4, 3),
+}
+EXPANSION_RATIOS: dict[str, tuple[int, ...]] = {
+    "small": (2,) * 9,
+    "base": (2, 3, 4, 4, 4, 4, 4, 3, 2),
+    "medium": (2, 3, 4, 4, 4, 4, 4, 3, 2),
+    "large": (3, 4, 8, 8, 8, 8, 8, 4, 3),
+}
+
+
+@dataclass(frozen=True, slots=True)
+class CheckpointConfig:
+    """Activation checkpointing: ``expansion`` recomputes the expanded branch of
+    each block in backward, ``block`` recomputes whole blocks; ``stages`` limits it
+    to resolution stages 0..4 (reference checkpointing.py:11-48)."""
+
+    style: Literal["expansion", "block"] = "expansion"
+    stages: tuple[int, ...] | None = None
+
+    def __post_init__(self) -> None:
+        if self.style not in ("expansion", "block"):
+            raise ValueError("style must be 'expansion' or 'block'")
+        if self.stages is None:
+            return
+        if not self.stages:
+            raise ValueError("stages must be a non-empty tuple or None")
+        if any(type(stage) is not int for stage in self.stages):
+            raise ValueError("stages must contain only integers")
+        if len(set(self.stages)) != len(self.stages):
+            raise ValueError("stages must not contain duplicates")
+        if any(stage < 0 or stage > 4 for stage in self.stages):
+            raise ValueError("stages must be between 0 and 4")
+        object.__setattr__(self, "stages", tuple(sorted(self.stages)))
+
+    def includes(self, stage: int) -> bool:
+        return self.stages is None or stage in self.stages
+
+    @property
+    def checkpoints_expansion(self) -> bool:
+        return self.style == "expansion"
+
+    @property
+    def checkpoints_blocks(self) -> bool:
+        return self.style == "block"
+
+
+@dataclass(frozen=True, slots=True)
+class MedNeXtV1Config:
+    """Serializable description of a MedNeXt v1 architecture."""
+
+    variant: str
+    spatial_dims: Literal[2, 3]
+    in_channels: int
+    out_channels: int
+    kernel_size: int
+    base_channels: int
+    block_counts: tuple[int, ...]
+    expansion_ratios: tuple[int, ...]
+    downsample_expansion_ratios: tuple[int, ...]
+    compatibility: Literal["official", "monai"]
+    residual_blocks: bool = True
+    residual_resampling: bool = True
+    deep_supervision: bool = False
+
+    def __post_init__(self) -> None:
+        if self.spatial_dims not in (2, 3):
+            raise ValueError("spatial_dims must be 2 or 3")
+        if self.in_channels <= 0 or self.out_channels <= 0:
+            raise ValueError("in_channels and out_channels must be positive")
+        if self.base_channels <= 0:
+            raise ValueError("base_channels must be positive")
+        if self.kernel_size <= 0 or self.kernel_size % 2 == 0:
+            raise ValueError("kernel_size must be a positive odd integer")
+        if len(self.block_counts) != 9 or len(self.expansion_ratios) != 9:
+            raise ValueError("MedNeXt v1 requires nine block stages")
+        if len(self.downsample_expansion_ratios) != 4:
+            raise ValueError("MedNeXt v1 requires four downsample expansion ratios")
+
+
+def get_mednext_v1_config(
+    variant: str,
+    *,
+    in_channels: int,
+    out_channels: int,
+    spatial_dims: Literal[2, 3] = 3,
+    kernel_size: int = 3,
+    base_channels: int = 32,
+    deep_supervision: bool = False,
+    compatibility: Literal["official", "monai"] = "official",
+) -> MedNeXtV1Config:
+    name = variant.lower()
+    if name not in BLOCK_COUNTS:
+        raise ValueError(
+            f"unknown MedNeXt v1 variant {variant!r}; expected one of {', '.join(BLOCK_COUNTS)}"
+        )
+    if compatibility not in ("official", "monai"):
+        raise ValueError("compatibility must be 'official' or 'monai'")
+    ratios = EXPANSION_RATIOS[name]
+    # Official checkpoints give down block i the ratio of stage i+1; MONAI uses stage i.
+    down = ratios[1:5] if compatibility == "official" else ratios[:4]
+    return MedNeXtV1Config(
+        variant=name,
+        spatial_dims=spatial_dims,
+        in_channels=in_channels,
+        out_channels=out_channels,
+        kernel_size=kernel_size,
+        base_channels=base_channels,
+        block_counts=BLOCK_COUNTS[name],
+        expansion_ratios=ratios,
+        downsample_expansion_ratios=down,
+        compatibility=compatibility,
+        deep_supervision=deep_supervision,
+    )
+
+
+def _conv(spatial_dims: int) -> type[nn.Module]:
+    if spatial_dims not in (2, 3):
+        raise ValueError("spatial_dims must be 2 or 3")
+    return nn.Conv3d if spatial_dims == 3 else nn.Conv2d
+
+
+def _conv_transpose(spatial_dims: int) -> type[nn.Module]:
+    if spatial_dims not in (2, 3):
+        raise ValueError("spatial_dims must be 2 or 3")
+    return nn.ConvTranspose3d if spatial_dims == 3 else nn.ConvTranspose2d
+
+
+class EvalModeGELU(nn.Module):
+    """Exact GELU while training; optionally the tanh form in evaluation."""
+
+    def __init__(self, approximate_eval: bool = False) -> None:
+        super().__init__()
+        self.approximate_eval = approximate_eval
+
+    def forward(self, x: Tensor) -> Tensor:
+        tanh = self.approximate_eval and not self.training
+        return F.gelu(x, approximate="tanh" if tanh else "none")
+
+    def extra_repr(self) -> str:
+        return f"approximate_eval={self.approximate_eval}"
+
+
+class MedNeXtBlock(nn.Module):
+    """depthwise conv -> GroupNorm(C, C) -> 1x1 expand -> GELU -> 1x1 project (+ x).
+
+    ``kind`` is ``"regular"`` here; the down/up subclasses change the depthwise
+    geometry.  When an sm_100a fused implementation has been installed
+    (``self._fused`` set by ``install_adaptive_operators``) and the call is a CUDA
+    training step, the whole block runs as one autograd node.
+    """
+
+    kind = "regular"
+
+    def __init__(
+        self,
+        *,
+        spatial_dims: int,
+        in_channels: int,
+        out_channels: int,
+        expansion_ratio: int,
+        kernel_size: int,
+        residual: bool = True,
+        checkpoint_expansion: bool = False,
+        approximate_gelu_eval: bool = False,
+    ) -> None:
+        super().__init__()
+        conv = _conv(spatial_dims)
+        self.use_residual = residual
+        self.checkpoint_expansion = checkpoint_expansion
+        self.depthwise = conv(
+            in_channels, in_channels, kernel_size=kernel_size, stride=1, padding=kernel_size // 2,
+            groups=in_channels,
+        )
+        self.norm = nn.GroupNorm(in_channels, in_channels)
+        self.expand = conv(in_channels, in_channels * expansion_ratio, kernel_size=1)
+        self.activation = EvalModeGELU(approximate_eval=approximate_gelu_eval)
+        self.project = conv(in_channels * expansion_ratio, out_channels, kernel_size=1)
+        self._fused = None
+
+    def _expansion(self, x: Tensor) -> Tensor:
+        return self.project(self.activation(self.expand(x)))
+
+    def _body(self, x: Tensor) -> Tensor:
+        y = self.norm(self.depthwise(x))
+        if self.checkpoint_expansion and self.training and torch.is_grad_enabled():
+            return checkpoint(self._expansion, y, use_reentrant=False)
+        return self._expansion(y)
+
+    def _fused_call(self, x: Tensor, addend: Tensor | None, residual_is_input: bool) -> Tensor | None:
+        fused = self._fused
+        if fused is None:
+            return None
+        return fused(self, x, addend, residual_is_input)
+
+    def forward(self, x: Tensor) -> Tensor:
+        out = self._fused_call(x, None, self.use_residual)
+        if out is not None:
+            return out
+        y = self._body(x)
+        return y + x if self.use_residual else y
+
+
+class MedNeXtDownBlock(MedNeXtBlock):
+    """Stride-two block; the residual branch is a strided 1x1 convolution."""
+
+    kind = "down"
+
+    def __init__(
+        self,
+        *,
+        spatial_dims: int,
+        in_channels: int,
+        out_channels: int,
+        expansion_ratio: int,
+        kernel_size: int,
+        residual: bool = True,
+        checkpoint_expansion: bool = False,
+        approximate_gelu_eval: bool = False,
+    ) -> None:
+        super().__init__(
+            spatial_dims=spatial_dims, in_channels=in_channels, out_channels=out_channels,
+            expansion_ratio=expansion_ratio, kernel_size=kernel_size, residual=False,
+            checkpoint_expansion=checkpoint_expansion, approximate_gelu_eval=approximate_gelu_eval,
+        )
+        conv = _conv(spatial_dims)
+        self.depthwise = conv(
+            in_channels, in_channels, kernel_size=kernel_size, stride=2, padding=kernel_size // 2,
+            groups=in_channels,
+        )
+        self.residual = conv(in_channels, out_channels, kernel_size=1, stride=2) if residual else None
+
+    def forward(self, x: Tensor) -> Tensor:
+        skip = self.residual(x) if self.residual is not None else None
+        out = self._fused_call(x, skip, False)
+        if out is not None:
+            return out
+        y = self._body(x)
+        return y + skip if skip is not None else y
+
+
+class MedNeXtUpBlock(MedNeXtBlock):
+    """Stride-two transposed block; output is left-padded by one voxel per axis."""
+
+    kind = "up"
+
+    def __init__(
+        self,
+        *,
+        spatial_dims: int,
+        in_channels: int,
+        out_channels: int,
+        expansion_ratio: int,
+        kernel_size: int,
+        residual: bool = True,
+        checkpoint_expansion: bool = False,
+        approximate_gelu_eval: bool = False,
+    ) -> None:
+        super().__init__(
+            spatial_dims=spatial_dims, in_channels=in_channels, out_channels=out_channels,
+            expansion_ratio=expansion_ratio, kernel_size=kernel_size, residual=False,
+            checkpoint_expansion=checkpoint_expansion, approximate_gelu_eval=approximate_gelu_eval,
+        )
+        up = _conv_transpose(spatial_dims)
+        self.depthwise = up(
+            in_channels, in_channels, kernel_size=kernel_size, stride=2, padding=kernel_size // 2,
+            groups=in_channels,
+        )
+        self.residual = up(in_channels, out_channels, kernel_size=1, stride=2) if residual else None
+        self._pad = (1, 0) * spatial_dims
+
+    def forward(self, x: Tensor) -> Tensor:
+        skip = self.residual(x) if self.residual is not None else None
+        out = self._fused_call(x, skip, False)
+        if out is None:
+            out = self._body(x)
+            if skip is not None:
+                out = out + skip
+        # pad(a) + pad(b) == pad(a + b): one pad after the fused residual add
+        return F.pad(out, self._pad)
+
+
+class OutputHead(nn.Module):
+    """1x1 transposed convolution, as in the official checkpoints."""
+
+    def __init__(self, *, spatial_dims: int, in_channels: int, out_channels: int) -> None:
+        super().__init__()
+        self.conv = _conv_transpose(spatial_dims)(in_channels, out_channels, kernel_size=1)
+
+    def forward(self, x: Tensor) -> Tensor:
+        return self.conv(x)
+
+
+class MedNeXtV1(nn.Module):
+    """MedNeXt v1 U-Net: stem, 4 encoder stages + down blocks, bottleneck,
+    4 up blocks + decoder stages, output head and optional deep-supervision heads."""
+
+    def __init__(
+        self,
+        config: MedNeXtV1Config,
+        *,
+        checkpointing: CheckpointConfig | None = None,
+        deep_supervision_output: DeepSupervisionOutput = "tuple",
+        approximate_gelu_eval: bool = False,
+    ) -> None:
+        super().__init__()
+        if deep_supervision_output not in ("tuple", "list", "stacked"):
+            raise ValueError("deep_supervision_output must be 'tuple', 'list', or 'stacked'")
+        self.config = config
+        self.checkpointing = checkpointing
+        self.deep_supervision_output = deep_supervision_output
+        self.approximate_gelu_eval = approximate_gelu_eval
+        self.optimization_source: OptimizationSource = "reference"
+        dims = config.spatial_dims
+        k = config.kernel_size
+        widths = tuple(config.base_channels * 2**stage for stage in range(5))
+
+        def ckpt_expansion(stage: int) -> bool:
+            return bool(
+                checkpointing is not None and checkpointing.checkpoints_expansion and checkpointing.includes(stage)
+            )
+
+        def blocks(stage: int, count: int, ratio: int) -> nn.Sequential:
+            return nn.Sequential(
+                *[
+                    MedNeXtBlock(
+                        spatial_dims=dims, in_channels=widths[stage], out_channels=widths[stage],
+                        expansion_ratio=ratio, kernel_size=k, residual=config.residual_blocks,
+                        checkpoint_expansion=ckpt_expansion(stage), approximate_gelu_eval=approximate_gelu_eval,
+                    )
+                    for _ in range(count)
+                ]
+            )
+
+        self.stem = _conv(dims)(config.in_channels, config.base_channels, kernel_size=1)
+        self.encoder_stages = nn.ModuleList(
+            blocks(s, config.block_counts[s], config.expansion_ratios[s]) for s in range(4)
+        )
+        self.downsamples = nn.ModuleList(
+            MedNeXtDownBlock(
+                spatial_dims=dims, in_channels=widths[s], out_channels=widths[s + 1],
+                expansion_ratio=config.downsample_expansion_ratios[s], kernel_size=k,
+                residual=config.residual_resampling, checkpoint_expansion=ckpt_expansion(s + 1),
+                approximate_gelu_eval=approximate_gelu_eval,
+            )
+            for s in range(4)
+        )
+        self.bottleneck = blocks(4, config.block_counts[4], config.expansion_ratios[4])
+        self.upsamples = nn.ModuleList()
+        self.decoder_stages = nn.ModuleList()
+        # decoder stage s (3..0) uses configuration index 8 - s
+        for s in (3, 2, 1, 0):
+            ratio = config.expansion_ratios[8 - s]
+            self.upsamples.append(
+                MedNeXtUpBlock(
+                    spatial_dims=dims, in_channels=widths[s + 1], out_channels=widths[s],
+                    expansion_ratio=ratio, kernel_size=k, residual=config.residual_resampling,
+                    checkpoint_expansion=ckpt_expansion(s), approximate_gelu_eval=approximate_gelu_eval,
+                )
+            )
+            self.decoder_stages.append(blocks(s, config.block_counts[8 - s], ratio))
+        self.head = OutputHead(spatial_dims=dims, in_channels=widths[0], out_channels=config.out_channels)
+        self.deep_supervision_heads = nn.ModuleList()
+        if config.deep_supervision:
+            self.deep_supervision_heads.extend(
+                OutputHead(spatial_dims=dims, in_channels=widths[s], out_channels=config.out_channels)
+                for s in (4, 3, 2, 1)
+            )
+
+    def _run(self, module: nn.Module, x: Tensor, stage: int) -> Tensor:
+        cfg = self.checkpointing
+        if (
+            cfg is not None and cfg.checkpoints_blocks and cfg.includes(stage) and self.training
+            and torch.is_grad_enabled()
+        ):
+            return checkpoint(module, x, use_reentrant=False)
+        return module(x)
+
+    def _stage(self, modules: nn.Sequential, x: Tensor, stage: int) -> Tensor:
+        for module in modules:
+            x = self._run(module, x, stage)
+        return x
+
+    def forward(self, x: Tensor) -> Tensor | tuple[Tensor, ...] | list[Tensor]:
+        x = self.stem(x)
+        skips: list[Tensor] = []
+        for stage in range(4):
+            x = self._stage(self.encoder_stages[stage], x, stage)
+            skips.append(x)
+            x = self._run(self.downsamples[stage], x, stage + 1)
+        x = self._stage(self.bottleneck, x, 4)
+        aux: list[Tensor] = []
+        supervise = self.training and self.config.deep_supervision
+        for i in range(4):
+            stage = 3 - i
+            if supervise:
+                aux.append(self.deep_supervision_heads[i](x))
+            x = self._run(self.upsamples[i], x, stage) + skips[stage]
+            x = self._stage(self.decoder_stages[i], x, stage)
+        primary = self.head(x)
+        if not supervise:
+            return primary
+        outputs = [primary, *reversed(aux)]
+        if self.deep_supervision_output == "tuple":
+            return tuple(outputs)
+        if self.deep_supervision_output == "list":
+            return outputs
+        size = primary.shape[2:]
+        return torch.stack(
+            [o if o.shape[2:] == size else F.interpolate(o, size=size) for o in outputs], dim=1
+        )
+
+
+def checkpoint_name(config: CheckpointConfig | None) -> str:
+    if config is None:
+        return "none"
+    if config.stages is None:
+        return "all-expansion" if config.style == "expansion" else "whole-block"
+    return f"{config.style}:{','.join(map(str, config.stages))}"
+
+
+def _factory(
+    variant: str,
+    *,
+    in_channels: int,
+    out_channels: int,
+    spatial_dims: Literal[2, 3] = 3,
+    kernel_size: int = 3,
+    base_channels: int = 32,
+    deep_supervision: bool = False,
+    checkpointing: CheckpointConfig | None = None,
+    deep_supervision_output: DeepSupervisionOutput = "tuple",
+    approximate_gelu_eval: bool = False,
+    optimization: OptimizationSource = "auto",
+) -> MedNeXtV1:
+    config = get_mednext_v1_config(
+        variant, in_channels=in_channels, out_channels=out_channels, spatial_dims=spatial_dims,
+        kernel_size=kernel_size, base_channels=base_channels, deep_supervision=deep_supervision,
+    )
+    model = MedNeXtV1(
+        config, checkpointing=checkpointing, deep_supervision_output=deep_supervision_output,
+        approximate_gelu_eval=approximate_gelu_eval,
+    )
+    return configure_optimization(model, optimization)
+
+
+def configure_optimization(model: MedNeXtV1, optimization: OptimizationSource) -> MedNeXtV1:
+    """``"reference"`` keeps plain PyTorch modules; ``"auto"`` installs the sm_100a
+    operators (reference models/mednext_v1.py:371-392)."""
+    from .adaptive import ModelOptimizationContext, install_adaptive_operators
+    from .optimization import PolicyResolver
+
+    model.optimization_source = optimization
+    if optimization == "reference":
+        return model
+    if isinstance(optimization, str) and optimization in ("torch", "conservative", "autotune"):
+        raise ValueError(f"optimization={optimization!r} was removed; use 'auto' or 'reference'")
+    if optimization != "auto":
+        raise ValueError(
+            "the sm_100a build uses a fixed dispatch table; optimization must be 'auto' or 'reference'"
+        )
+    resolver = PolicyResolver()
+    context = ModelOptimizationContext(
+        "mednext_v1", model.config.variant, checkpoint_name(model.checkpointing), model.approximate_gelu_eval
+    )
+    install_adaptive_operators(model, resolver=resolver, model_context=context)
+    model.__dict__["_optimization_resolver"] = resolver
+    model.__dict__["_optimization_model_context"] = context
+    return model
+
+
+def _make(variant: str, doc: str):
+    def factory(
+        *,
+        in_channels: int,
+        out_channels: int,
+        spatial_dims: Literal[2, 3] = 3,
+        kernel_size: int = 3,
+        base_channels: int = 32,
+        deep_supervision: bool = False,
+        checkpointing: CheckpointConfig | None = None,
+        deep_supervision_output: DeepSupervisionOutput = "tuple",
+        approximate_gelu_eval: bool = False,
+        optimization: OptimizationSource = "auto",
+    ) -> MedNeXtV1:
+        return _factory(
+            variant, in_channels=in_channels, out_channels=out_channels, spatial_dims=spatial_dims,
+            kernel_size=kernel_size, base_channels=base_channels, deep_supervision=deep_supervision,
+            checkpointing=checkpointing, deep_supervision_output=deep_supervision_output,
+            approximate_gelu_eval=approximate_gelu_eval, optimization=optimization,
+        )
+
+    factory.__name__ = f"mednext_{variant}"
+    factory.__qualname__ = factory.__name__
+    factory.__doc__ = doc
+    return factory
+
+
+mednext_small = _make("small", "Build MedNeXt Small (reference models/mednext_v1.py:395-422).")
+mednext_base = _make("base", "Build MedNeXt Base (reference models/mednext_v1.py:425-452).")
+mednext_medium = _make("medium", "Build MedNeXt Medium (reference models/mednext_v1.py:455-482).")
+mednext_large = _make("large", "Build MedNeXt Large (reference models/mednext_v1.py:485-512).")
