@@ -1,0 +1,446 @@
+"""MedNeXt-Base 128^3 bf16 training-step benchmark on B200 (1..8 GPUs, one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Workload: MedNeXt v1 Base, kernel 3, deep supervision,
+batch 1 per GPU, input 1x1x128^3 ~N(0,1), labels uniform in {0,1,2}, loss = mean of
+the five heads' cross-entropy against nearest-downsampled labels, AdamW lr 1e-4,
+random init from seed 0, bf16 autocast.  Each rank draws its own sample (seed
+1000+rank); gradients are averaged by NCCL all-reduce overlapped with backward.
+
+``--impl ours`` times the sm_100a path: the whole step (forward, backward,
+gradient all-reduce, AdamW) is captured once as a CUDA graph and replayed; K
+steps are timed with CUDA events after W warm-up steps, max over ranks.  The
+activations (128^3 voxels x 32+ channels) are far larger than the 126 MB L2, so
+no flush is needed between steps.
+
+``--impl reference`` times the reference's pure-PyTorch CPU implementation of
+the same step (the oracle's functional restatement, fp32, all host threads) on
+rank 0; other ranks exit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+from torch.nn import functional as F
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "MedNeXt-Base 128³ bf16 train-step ms at 1/2/4/8 B200; depthwise-bwd HBM GB/s"
+SPATIAL = 128
+HEAD_SIZES = (128, 64, 32, 16, 8)
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--no-graph", action="store_true", help="time eager steps instead of a CUDA graph replay")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--spatial", type=int, default=SPATIAL, help=argparse.SUPPRESS)
+    return p.parse_args(argv)
+
+
+# --------------------------------------------------------------------------- helpers
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def downsampled_targets(target: torch.Tensor) -> dict[tuple[int, ...], torch.Tensor]:
+    out = {}
+    for s in HEAD_SIZES:
+        size = (target.shape[1] * s // SPATIAL,) * 3
+        if size == tuple(target.shape[1:]):
+            out[size] = target
+        else:
+            out[size] = F.interpolate(target[:, None].float(), size=size, mode="nearest")[:, 0].long()
+    return out
+
+
+def five_head_loss(heads, targets):
+    return sum(F.cross_entropy(h, targets[tuple(h.shape[2:])]) for h in heads) / len(heads)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9], strict=True):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------- depthwise-bwd roofline
+def depthwise_backward_roofline(device: torch.device, reps: int = 10) -> dict:
+    """Time the dominant depthwise backward (C=32 at 128^3, bf16, k=3: input grad +
+    weight grad, the pair the metric names) with CUDA events on the launching
+    stream.  Algorithmic bytes = dgrad (read dy, write dx) + wgrad (read x, read dy)."""
+    from mednext_accel_b200 import depthwise as dwk
+
+    g = torch.Generator(device=device).manual_seed(7)
+    shape = (1, 32, SPATIAL, SPATIAL, SPATIAL)
+    x = torch.randn(shape, device=device, generator=g, dtype=torch.float32).to(torch.bfloat16)
+    dy = torch.randn(shape, device=device, generator=g, dtype=torch.float32).to(torch.bfloat16)
+    w = (torch.randn((32, 1, 3, 3, 3), device=device, generator=g) / 27**0.5).to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    for _ in range(3):
+        dwk.dw_dgrad(dy, w, 3)
+        dwk.dw_wgrad(x, dy, 3)
+    tg, tw = [], []
+    s = torch.cuda.current_stream()
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(s)
+        dwk.dw_dgrad(dy, w, 3)
+        e1.record(s)
+        flush.zero_()
+        e1b = torch.cuda.Event(enable_timing=True)
+        e1b.record(s)
+        dwk.dw_wgrad(x, dy, 3)
+        e2.record(s)
+        torch.cuda.synchronize()
+        tg.append(e0.elapsed_time(e1))
+        tw.append(e1b.elapsed_time(e2))
+    elem = x.numel() * x.element_size()
+    algo_bytes = 4 * elem  # dgrad: dy + dx; wgrad: x + dy
+    t_ms = statistics.median(tg) + statistics.median(tw)
+    achieved = algo_bytes / (t_ms * 1e-3) / 1e9
+    peak, kind = measured_peaks()
+    traffic = None
+    prof = ROOT / "profiles" / "depthwise_bwd_c32_128.json"
+    if prof.exists():
+        try:
+            traffic = json.loads(prof.read_text()).get("dram_bytes_per_pair")
+        except ValueError:
+            traffic = None
+    return {
+        "bound": "hbm",
+        "kernel": "depthwise dgrad + wgrad (C32 128^3 bf16 k3)",
+        "achieved": round(achieved, 1),
+        "peak": peak,
+        "peak_kind": kind,
+        "unit": "GB/s",
+        "frac": round(achieved / peak, 4),
+        "traffic": traffic,
+        "algorithmic_bytes": algo_bytes,
+        "dgrad_ms": round(statistics.median(tg), 4),
+        "wgrad_ms": round(statistics.median(tw), 4),
+    }
+
+
+# --------------------------------------------------------------------------- CPU reference
+def cpu_reference_step_ms(steps: int, spatial: int = SPATIAL, budget_s: float = 150.0) -> tuple[float, dict]:
+    """The reference's pure-PyTorch training step on the host CPU (fp32, all threads)."""
+    sys.path.insert(0, str(ROOT))
+    from oracle.reference_model import ReferenceTrainer, forward, targets_for
+
+    import mednext_accel_b200 as mx
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    model = mx.mednext_base(in_channels=1, out_channels=3, kernel_size=3, deep_supervision=True,
+                            optimization="reference")
+    trainer = ReferenceTrainer(model.state_dict(), "base", 3)
+    gen = torch.Generator().manual_seed(1000)
+    # warm-up at a quarter of the volume per axis (thread pools, allocator)
+    xs = torch.randn((1, 1, spatial // 2, spatial // 2, spatial // 2), generator=gen)
+    ts = torch.randint(0, 3, (1, spatial // 2, spatial // 2, spatial // 2), generator=gen)
+    trainer.step(xs, targets_for(ts, forward(trainer.params, xs, "base", 3)))
+    x = torch.randn((1, 1, spatial, spatial, spatial), generator=gen)
+    target = torch.randint(0, 3, (1, spatial, spatial, spatial), generator=gen)
+    with torch.no_grad():
+        tg = targets_for(target, forward(trainer.params, x, "base", 3))
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        trainer.step(x, tg)
+        times.append((time.perf_counter() - t0) * 1e3)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    ms = statistics.median(times)
+    info = {"cores": threads, "kind": "port",
+            "sample": f"{len(times)} fp32 train step(s) of the reference pure-PyTorch MedNeXt-Base "
+                      f"(oracle/reference_model.py) at {spatial}^3 B1 on {threads} host threads, median"}
+    return ms, info
+
+
+def run_reference(args) -> int:
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    ms, info = cpu_reference_step_ms(min(args.steps, 3))
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(ms, 3),
+        "unit": "ms",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "MedNeXt-Base k3 128^3 B1 train step (5-head CE, AdamW), host CPU",
+                   "global_batch": 1, "spatial": SPATIAL},
+        "cpu_baseline": {"value": round(ms, 3), "unit": "ms", **info},
+        "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- ours
+def run_ours(args) -> int:
+    world, rank, local = dist_env()
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "ours", "error": "CUDA is not available"}), flush=True)
+        return 1
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    import mednext_accel_b200 as mx
+    from mednext_accel_b200 import _native as nat
+    from mednext_accel_b200.data_parallel import GradientBucketReducer, broadcast_parameters
+
+    torch.backends.cudnn.benchmark = True
+    S = args.spatial
+    torch.manual_seed(0)
+    model = mx.mednext_base(in_channels=1, out_channels=3, kernel_size=3, deep_supervision=True).to(device).train()
+    broadcast_parameters(model)
+    reducer = GradientBucketReducer(model, bucket_cap_mb=25.0)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True, capturable=True)
+
+    gen = torch.Generator().manual_seed(1000 + rank)
+    x_host = torch.randn((1, 1, S, S, S), generator=gen).pin_memory()
+    t_host = torch.randint(0, 3, (1, S, S, S), generator=gen).pin_memory()
+    x = x_host.to(device)
+    target = t_host.to(device)
+    targets = downsampled_targets(target)
+
+    def step():
+        reducer.zero_grad()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            heads = model(x)
+            loss = five_head_loss(heads, targets)
+        loss.backward()
+        reducer.finish()
+        opt.step()
+        return loss
+
+    # warm-up on a side stream (required before graph capture)
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(3, args.warmup)):
+            loss = step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+
+    graph = None
+    mode = "eager"
+    launches_before = nat.load().mednext_kernel_launches()
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_loss = step()
+        mode = "cuda-graph"
+        per_step_launches = nat.load().mednext_kernel_launches() - launches_before
+
+        def run_step():
+            graph.replay()
+            return static_loss
+    else:
+        run_step = step
+        step()
+        per_step_launches = nat.load().mednext_kernel_launches() - launches_before
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # ---------------- timed region (device time, max over ranks)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start.record()
+        for _ in range(args.steps):
+            loss = run_step()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    elapsed = torch.tensor([start.elapsed_time(end)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+    ms = float(elapsed.item()) / args.steps
+    final_loss = float(loss.item())
+
+    # ---------------- end to end: host inputs in, loss out, through the same step
+    e2e_steps = max(1, args.e2e_steps)
+    h2d = x_host.numel() * x_host.element_size() + t_host.numel() * t_host.element_size()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0.record()
+    for _ in range(e2e_steps):
+        x.copy_(x_host, non_blocking=True)
+        target.copy_(t_host, non_blocking=True)
+        for size, t in targets.items():
+            if t is not target:
+                t.copy_(F.interpolate(target[:, None].float(), size=size, mode="nearest")[:, 0].long())
+        out = run_step()
+        _ = float(out.item())  # device -> host read of the step's loss
+    e1.record()
+    torch.cuda.synchronize()
+    e2e = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e.item()) / e2e_steps
+
+    roof = depthwise_backward_roofline(device) if rank == 0 else None
+    dev_err = nat.device_error()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_ms, info = cpu_reference_step_ms(1, spatial=S)
+        cpu = {"value": round(cpu_ms, 1), "unit": "ms", **info}
+
+    if graph is not None:
+        del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC,
+        "value": round(ms, 3),
+        "unit": "ms",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": f"MedNeXt-Base k3 {S}^3 B1/GPU train step: 5-head deep-supervision CE + AdamW (config 3)",
+            "global_batch": world,
+            "spatial": S,
+            "parallelism": f"dp{world}",
+            "step_mode": mode,
+            "l2": "inputs and activations larger than L2 (no flush)",
+        },
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4},
+        "gpu_launches": int(per_step_launches * args.steps),
+        "clocks": clocks.summary(),
+        "final_loss": round(final_loss, 5),
+        "device_error": dev_err,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -91,6 +91,8 @@ int mednext_last_cuda_error(void);
 int mednext_device_error(int* code, mednext_stream_t stream);
 /* Returns MEDNEXT_OK when the current device is sm_100 (B200). */
 int mednext_check_device(void);
+/* Number of kernels this library has launched in this process (all threads). */
+uint64_t mednext_kernel_launches(void);
 
 /* ---------------- depthwise Conv3d, stride 1, padding k/2 ----------------
  * x, y: [n, c, d, h, w]; weight: [c, 1, k, k, k]; bias: [c] or NULL.

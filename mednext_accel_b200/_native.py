@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mednext_last_cuda_error": (_INT, []),
     "mednext_device_error": (_INT, [ctypes.POINTER(_INT), _P]),
     "mednext_check_device": (_INT, []),
+    "mednext_kernel_launches": (ctypes.c_uint64, []),
     "mednext_dw_fwd_workspace_size": (_SZ, _DIMS5 + [_INT, _INT]),
     "mednext_dw_fwd": (_INT, [_P, _P, _P, _P, _P, _F, _P, _SZ] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_dgrad": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),

@@ -3,11 +3,15 @@
 // interface each entry point replaces, are in include/mednext_b200.h.
 #include "plan.h"
 
+#include <atomic>
+
 namespace mednext {
 namespace {
 thread_local int t_last_cuda_error = 0;
-}
+std::atomic<uint64_t> g_launches{0};
+}  // namespace
 int record_launch() {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     t_last_cuda_error = (int)e;
@@ -16,6 +20,7 @@ int record_launch() {
   return MEDNEXT_OK;
 }
 int last_cuda_error() { return t_last_cuda_error; }
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 }  // namespace mednext
 
 using namespace mednext;
@@ -89,6 +94,8 @@ int mednext_device_error(int* code, mednext_stream_t stream) {
   if (st == MEDNEXT_OK) st = read_clear_errors_pw(code, as_stream(stream));
   return st;
 }
+
+uint64_t mednext_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int mednext_check_device(void) {
   int dev = 0, major = 0, minor = 0;

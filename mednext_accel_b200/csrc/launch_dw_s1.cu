@@ -10,7 +10,11 @@ int launch_s1_conv(const void* x, const void* wgt, const void* bias, const void*
                    const S1Plan& p, int flip, cudaStream_t s) {
   constexpr int NH = K <= 3 ? 2 : 1;
   auto kern = dw_s1_conv_kernel<T, K, NH>;
-  if (p.smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  static size_t configured = 0;  // raise the opt-in limit once per instantiation
+  if (p.smem > 48 * 1024 && p.smem > configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    configured = p.smem;
+  }
   kern<<<(unsigned)p.grid, p.threads, p.smem, s>>>(static_cast<const T*>(x), static_cast<const T*>(wgt),
                                                    static_cast<const T*>(bias), static_cast<const T*>(addend),
                                                    static_cast<T*>(y), st, p.g, flip);
@@ -33,11 +37,19 @@ int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws,
   Acc* part = static_cast<Acc*>(ws);
   if constexpr (K <= 3) {
     auto kern = dw_s1_wgrad_kernel<T, K, NH>;
-    if (p.smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    static size_t configured = 0;  // raise the opt-in limit once per instantiation
+    if (p.smem > 48 * 1024 && p.smem > configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    configured = p.smem;
+  }
     kern<<<(unsigned)p.grid, p.threads, p.smem, s>>>(static_cast<const T*>(x), static_cast<const T*>(dy), part, p.g);
   } else {
     auto kern = dw_s1_wgrad_grouped_kernel<T, K, NH>;
-    if (p.smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    static size_t configured = 0;  // raise the opt-in limit once per instantiation
+    if (p.smem > 48 * 1024 && p.smem > configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    configured = p.smem;
+  }
     kern<<<(unsigned)p.grid, p.threads, p.smem, s>>>(static_cast<const T*>(x), static_cast<const T*>(dy), part, p.g);
   }
   const int st = record_launch();

@@ -8,7 +8,11 @@ template <typename TA, typename TY, int PRO>
 int launch_pw_fwd(const PwFwdArgs& a, cudaStream_t s) {
   auto kern = pw_fwd_kernel<TA, TY, PRO>;
   const size_t smem = pw_smem(a.BN);
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static size_t configured = 0;  // raise the opt-in limit once per instantiation
+  if (smem > configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured = smem;
+  }
   const long long grid = (long long)a.S * a.ntiles * a.mtiles;
   kern<<<(unsigned)grid, kPwThreads, smem, s>>>(a);
   return record_launch();
@@ -17,7 +21,11 @@ template <typename TA, int PRO>
 int launch_pw_wgrad(const PwWgradArgs& a, cudaStream_t s) {
   auto kern = pw_wgrad_kernel<TA, PRO>;
   const size_t smem = pw_smem(a.BN);
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  static size_t configured = 0;  // raise the opt-in limit once per instantiation
+  if (smem > configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured = smem;
+  }
   const long long grid = (long long)a.splits * a.ntiles * a.mtiles;
   kern<<<(unsigned)grid, kPwThreads, smem, s>>>(a);
   return record_launch();

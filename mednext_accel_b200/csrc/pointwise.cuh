@@ -251,6 +251,9 @@ __global__ void __launch_bounds__(kPwThreads) pw_fwd_kernel(PwFwdArgs p) {
         if (j < p.cout && vok) {
           const long long off = ((long long)s * p.cout + j) * p.vox + v;
           if (epi & MEDNEXT_EPI_BIAS) acc += p.bias[j];
+          // the convolution result is materialised in the activation dtype
+          // before any elementwise step that follows it
+          if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_RESIDUAL)) acc = to_acc<TA>(from_acc<TA>(acc));
           if (epi & MEDNEXT_EPI_GELU_GRAD) acc *= gelu_grad_f(to_acc<TA>(aux[off]));
           if (epi & MEDNEXT_EPI_RESIDUAL) acc += (float)to_acc<TY>(res[off]);
           const TY out = from_acc<TY>((typename Elem<TY>::Acc)acc);

@@ -1,0 +1,221 @@
+"""Fused MedNeXt block and full model on the GPU against the CPU oracle / the
+reference's pure-PyTorch path.  bf16 autocast bar: relative L2 <= 2e-2."""
+
+from __future__ import annotations
+
+import copy
+import zlib
+
+import numpy as np
+import pytest
+import torch
+from torch.nn import functional as F
+from torch.utils._python_dispatch import TorchDispatchMode
+
+import mednext_accel_b200 as mx
+from mednext_accel_b200 import _native as nat
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+BAR = 2e-2
+
+
+class OpSpy(TorchDispatchMode):
+    def __init__(self):
+        super().__init__()
+        self.ops = []
+
+    def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+        self.ops.append(func._schema.name)
+        return func(*args, **(kwargs or {}))
+
+
+def _seed(*key):
+    return zlib.crc32(repr(key).encode()) % 100_000
+
+
+def make_block(kind, cin, cout, ratio, k, seed, checkpoint_expansion=False):
+    torch.manual_seed(seed)
+    cls = {"regular": mx.MedNeXtBlock, "down": mx.MedNeXtDownBlock, "up": mx.MedNeXtUpBlock}[kind]
+    block = cls(spatial_dims=3, in_channels=cin, out_channels=cout, expansion_ratio=ratio, kernel_size=k,
+                checkpoint_expansion=checkpoint_expansion)
+    with torch.no_grad():
+        block.norm.weight.copy_(1.0 + 0.1 * torch.randn_like(block.norm.weight))
+        block.norm.bias.copy_(0.1 * torch.randn_like(block.norm.bias))
+    return block
+
+
+def install(module):
+    from mednext_accel_b200.adaptive import ModelOptimizationContext
+
+    mx.install_adaptive_operators(module, resolver=mx.PolicyResolver(),
+                                  model_context=ModelOptimizationContext("mednext_v1", "base", "none"))
+    return module
+
+
+def run_fused(block, x, dy):
+    block = install(copy.deepcopy(block)).cuda().train()
+    xg = x.cuda().requires_grad_()
+    with torch.autocast("cuda", dtype=torch.bfloat16), OpSpy() as spy:
+        y = block(xg)
+    grads = torch.autograd.grad(y, (xg, *block.parameters()), dy.cuda().to(y.dtype))
+    assert "mednext_accel_b200::mednext_block" in spy.ops
+    names = [n for n, _ in block.named_parameters()]
+    return y, dict(zip(["dx", *names], grads, strict=True))
+
+
+def oracle_block(block, x, dy, kind):
+    state = {k: v.detach().double().numpy() for k, v in block.state_dict().items()}
+    p = orc.BlockParams.from_state(state)
+    xn = x.double().numpy()
+    addend = None
+    if kind == "down":
+        xb = orc.round_bf16(xn)
+        addend = orc.round_bf16(orc.pointwise_fwd(xb[:, :, ::2, ::2, ::2], orc.round_bf16(state["residual.weight"]),
+                                                  orc.round_bf16(state["residual.bias"])))
+    elif kind == "up":
+        xb = orc.round_bf16(xn)
+        n, c, d, h, w = xn.shape
+        up = np.zeros((n, c, 2 * d - 1, 2 * h - 1, 2 * w - 1))
+        up[:, :, ::2, ::2, ::2] = xb
+        rw = orc.round_bf16(state["residual.weight"])
+        addend = orc.round_bf16(orc.pointwise_fwd(up, np.transpose(rw, (1, 0, 2, 3, 4)), None)
+                                + orc.round_bf16(state["residual.bias"]).reshape(1, -1, 1, 1, 1))
+    dyn = dy.double().numpy()
+    if kind == "up":
+        dyn = dyn[:, :, 1:, 1:, 1:]
+    return orc.block_reference(xn, dyn, p, kind, addend=addend, residual_is_input=(kind == "regular"))
+
+
+CASES = [
+    ("regular", 32, 32, 2, 3, (2, 32, 16, 16, 16)),
+    ("regular", 16, 16, 4, 5, (1, 16, 12, 12, 12)),
+    ("regular", 64, 64, 3, 3, (1, 64, 8, 8, 8)),
+    ("regular", 8, 8, 2, 7, (1, 8, 9, 10, 11)),
+    ("down", 16, 32, 3, 3, (1, 16, 16, 16, 16)),
+    ("up", 32, 16, 2, 3, (1, 32, 8, 8, 8)),
+]
+
+
+@pytest.mark.parametrize("kind,cin,cout,ratio,k,shape", CASES)
+def test_fused_block_matches_oracle(kind, cin, cout, ratio, k, shape):
+    seed = _seed(kind, cin, k, shape)
+    block = make_block(kind, cin, cout, ratio, k, seed)
+    gen = torch.Generator().manual_seed(seed + 1)
+    x = torch.randn(shape, generator=gen).to(torch.bfloat16)
+    ref = block.train()
+    out_shape = ref(x.float()).shape if kind != "up" else None
+    if kind == "up":
+        out_shape = (shape[0], cout, *(2 * s for s in shape[2:]))
+    dy = torch.randn(out_shape, generator=gen).to(torch.bfloat16)
+    y, grads = run_fused(block, x, dy)
+    want_y, want = oracle_block(block, x, dy, kind)
+    got_y = y.detach().double().cpu().numpy()
+    if kind == "up":
+        assert torch.count_nonzero(y[:, :, 0]) == 0
+        got_y = got_y[:, :, 1:, 1:, 1:]
+    assert orc.rel_l2(got_y, want_y) <= BAR, orc.rel_l2(got_y, want_y)
+    if kind == "regular":
+        assert orc.rel_l2(grads["dx"].double().cpu().numpy(), want["dx"]) <= BAR
+    for name in ("depthwise.weight", "depthwise.bias", "norm.weight", "norm.bias", "expand.weight", "expand.bias",
+                 "project.weight", "project.bias"):
+        got = grads[name].double().cpu().numpy()
+        err = orc.rel_l2(got, want[name])
+        assert err <= BAR, f"{name}: {err:.3e}"
+
+
+def test_checkpointed_expansion_matches_stored():
+    block = make_block("regular", 32, 32, 4, 3, 7)
+    gen = torch.Generator().manual_seed(8)
+    x = torch.randn((1, 32, 16, 16, 16), generator=gen).to(torch.bfloat16)
+    dy = torch.randn((1, 32, 16, 16, 16), generator=gen).to(torch.bfloat16)
+    y1, g1 = run_fused(block, x, dy)
+    block_ck = copy.deepcopy(block)
+    block_ck.checkpoint_expansion = True
+    y2, g2 = run_fused(block_ck, x, dy)
+    torch.testing.assert_close(y1, y2, rtol=0, atol=0)
+    for k in g1:
+        torch.testing.assert_close(g1[k], g2[k], rtol=0, atol=0)
+
+
+def test_config2_block_full_size_against_reference_path():
+    """MedNeXtBlock N=2, C=64, 64^3, R=4, k=5 under bf16
+    autocast, PyTorch default init from seed 0, input and upstream grad ~N(0,1).
+    Compared with the same block run through the reference's pure-PyTorch path
+    (native modules) in fp32 on the same GPU."""
+    torch.manual_seed(0)
+    block = mx.MedNeXtBlock(spatial_dims=3, in_channels=64, out_channels=64, expansion_ratio=4, kernel_size=5)
+    x = torch.randn(2, 64, 64, 64, 64)
+    dy = torch.randn(2, 64, 64, 64, 64)
+    ref = copy.deepcopy(block).cuda().train()
+    xr = x.cuda().requires_grad_()
+    yr = ref(xr)
+    gr = torch.autograd.grad(yr, (xr, *ref.parameters()), dy.cuda())
+    y, grads = run_fused(block, x, dy)
+    assert y.dtype == torch.float32  # residual add promotes to the fp32 input, as in the reference
+    assert orc.rel_l2(y.detach().double().cpu().numpy(), yr.detach().double().cpu().numpy()) <= BAR
+    names = ["dx", *[n for n, _ in block.named_parameters()]]
+    for name, want in zip(names, gr, strict=True):
+        err = orc.rel_l2(grads[name].double().cpu().numpy(), want.double().cpu().numpy())
+        assert err <= BAR, f"{name}: {err:.3e}"
+
+
+def _loss(heads, target):
+    if isinstance(heads, torch.Tensor):
+        heads = (heads,)
+    total = 0
+    for hd in heads:
+        t = target if hd.shape[2:] == target.shape[1:] else F.interpolate(
+            target[:, None].float(), size=hd.shape[2:], mode="nearest")[:, 0].long()
+        total = total + F.cross_entropy(hd.float(), t)
+    return total / len(heads)
+
+
+def test_small_model_step_matches_native_path():
+    torch.manual_seed(0)
+    fused = mx.mednext_small(in_channels=1, out_channels=3, base_channels=16, deep_supervision=True).cuda().train()
+    native = mx.mednext_small(in_channels=1, out_channels=3, base_channels=16, deep_supervision=True,
+                              optimization="reference").cuda().train()
+    native.load_state_dict(fused.state_dict())
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn((2, 1, 64, 64, 64), generator=gen).cuda()
+    target = torch.randint(0, 3, (2, 64, 64, 64), generator=gen).cuda()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        lf = _loss(fused(x), target)
+        ln = _loss(native(x), target)
+    lf.backward()
+    ln.backward()
+    assert abs(lf.item() - ln.item()) <= 1e-2 * abs(ln.item())
+    worst = 0.0
+    for (name, pf), (_, pn) in zip(fused.named_parameters(), native.named_parameters(), strict=True):
+        err = orc.rel_l2(pf.grad.double().cpu().numpy(), pn.grad.double().cpu().numpy())
+        worst = max(worst, err)
+        assert err <= 5e-2, f"{name}: {err:.3e}"
+
+
+def test_loss_curve_matches_native_path_over_adamw_steps():
+    """Per-step loss within 1% of the reference's pure-PyTorch path over AdamW steps."""
+    torch.manual_seed(0)
+    fused = mx.mednext_small(in_channels=1, out_channels=3, base_channels=8, deep_supervision=True).cuda().train()
+    native = mx.mednext_small(in_channels=1, out_channels=3, base_channels=8, deep_supervision=True,
+                              optimization="reference").cuda().train()
+    native.load_state_dict(fused.state_dict())
+    opt_f = torch.optim.AdamW(fused.parameters(), lr=1e-4)
+    opt_n = torch.optim.AdamW(native.parameters(), lr=1e-4)
+    gen = torch.Generator().manual_seed(2)
+    x = torch.randn((1, 1, 64, 64, 64), generator=gen).cuda()
+    target = torch.randint(0, 3, (1, 64, 64, 64), generator=gen).cuda()
+    for _ in range(50):
+        losses = []
+        for model, opt in ((fused, opt_f), (native, opt_n)):
+            opt.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = _loss(model(x), target)
+            loss.backward()
+            opt.step()
+            losses.append(loss.item())
+        assert abs(losses[0] - losses[1]) <= 1e-2 * abs(losses[1]), losses
+
+
+def test_no_device_error_recorded():
+    assert nat.device_error() == 0

@@ -1,0 +1,214 @@
+"""Depthwise Conv3d kernels on the GPU against the CPU oracle and the golden
+vectors of the reference (stride 1, stride 2 and transposed; every dtype)."""
+
+from __future__ import annotations
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+from torch.nn import functional as F
+
+from mednext_accel_b200 import _native as nat
+from mednext_accel_b200 import depthwise as dwk
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+# fp32 parity bar of the north star: max relative error <= 1e-5; 16-bit outputs
+# are compared with the oracle evaluated on the same rounded inputs.
+TOL = {
+    torch.float64: dict(max_rel=1e-12),
+    torch.float32: dict(max_rel=1e-5),
+    torch.bfloat16: dict(max_rel=1.6e-2, rel_l2=4e-3),
+    torch.float16: dict(max_rel=2e-3, rel_l2=1e-3),
+}
+
+
+def check(got: torch.Tensor, want: np.ndarray, dtype: torch.dtype, what: str, scale: float = 1.0) -> None:
+    g = got.detach().double().cpu().numpy()
+    tol = TOL[dtype]
+    mr = orc.max_rel(g, want)
+    assert mr <= tol["max_rel"] * scale, f"{what}: max_rel {mr:.3e}"
+    if "rel_l2" in tol:
+        rl = orc.rel_l2(g, want)
+        assert rl <= tol["rel_l2"] * scale, f"{what}: rel_l2 {rl:.3e}"
+
+
+def seed_of(*key) -> int:
+    return zlib.crc32(repr(key).encode()) % 100_000
+
+
+def rand(shape, dtype, seed, scale=1.0):
+    gen = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=gen, dtype=torch.float64) * scale).to(dtype)
+
+
+def host(t: torch.Tensor) -> np.ndarray:
+    return t.double().numpy()
+
+
+SHAPES = [(2, 3, 5, 6, 7), (1, 4, 8, 16, 16), (1, 2, 9, 10, 24), (2, 5, 6, 3, 33), (1, 3, 12, 12, 130)]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16, torch.float64])
+@pytest.mark.parametrize("k", [1, 3, 5, 7])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_stride1_forward_dgrad_wgrad(dtype, k, shape):
+    seed = seed_of(str(dtype), k, shape)
+    x = rand(shape, dtype, seed)
+    w = rand((shape[1], 1, k, k, k), dtype, seed + 1, scale=1 / np.sqrt(k**3))
+    b = rand((shape[1],), dtype, seed + 2)
+    dy = rand(shape, dtype, seed + 3)
+    xg, wg, bg, dyg = (t.cuda() for t in (x, w, b, dy))
+    y = dwk.dw_forward(xg, wg, bg, k)
+    dx = dwk.dw_dgrad(dyg, wg, k)
+    dw, db = dwk.dw_wgrad(xg, dyg, k)
+    torch.cuda.synchronize()
+    check(y, orc.dw_fwd(host(x), host(w), host(b), k), dtype, "y")
+    check(dx, orc.dw_dgrad(host(dy), host(w), k), dtype, "dx")
+    want_dw, want_db = orc.dw_wgrad(host(x), host(dy), k)
+    # weight grads reduce thousands of products: bf16/fp16 output rounding only
+    check(dw, want_dw, dtype, "dw", scale=2.0)
+    check(db, want_db, dtype, "db", scale=2.0)
+
+
+@pytest.mark.parametrize("k", [1, 3, 5])
+def test_stride1_against_reference_golden_fp64(golden, k):
+    g = golden("depthwise.npz")
+    t = f"s1_k{k}/"
+    cu = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    y = dwk.dw_forward(cu(g[t + "x"]), cu(g[t + "w"]), cu(g[t + "b"]), k)
+    dx = dwk.depthwise_input_grad(cu(g[t + "dy"]), cu(g[t + "w"]), block=128)
+    dw = dwk.depthwise_weight_grad(cu(g[t + "x"]), cu(g[t + "dy"]), splits=4, block=128, kernel_size=k)
+    # reference tolerances, tests/ops/test_depthwise.py:61-62
+    torch.testing.assert_close(y.cpu(), torch.from_numpy(g[t + "y"]), rtol=2e-12, atol=2e-12)
+    torch.testing.assert_close(dx.cpu(), torch.from_numpy(g[t + "dx"]), rtol=2e-12, atol=2e-12)
+    torch.testing.assert_close(dw.cpu(), torch.from_numpy(g[t + "dw"]), rtol=2e-5, atol=2e-5)
+
+
+def test_stride2_and_transpose_against_reference_golden_fp64(golden):
+    g = golden("depthwise.npz")
+    cu = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    for k in (3, 5):
+        t = f"s2_k{k}/"
+        x = g[t + "x"]
+        y = dwk.s2_forward(cu(x), cu(g[t + "w"]), cu(g[t + "b"]), k)
+        dx = dwk.depthwise_stride2_input_grad(cu(g[t + "dy"]), cu(g[t + "w"]), x.shape[2:], block=128)
+        dw, db = dwk.s2_wgrad(cu(x), cu(g[t + "dy"]), k)
+        for got, key in ((y, "y"), (dx, "dx"), (dw, "dw"), (db, "db")):
+            torch.testing.assert_close(got.cpu(), torch.from_numpy(g[t + key]), rtol=2e-12, atol=2e-12)
+        t = f"t_k{k}/"
+        y = dwk.t_forward(cu(g[t + "x"]), cu(g[t + "w"]), cu(g[t + "b"]), k)
+        dx = dwk.t_dgrad(cu(g[t + "dy"]), cu(g[t + "w"]), k)
+        dw = dwk.depthwise_transpose_weight_grad(cu(g[t + "x"]), cu(g[t + "dy"]), splits=4, block=128, kernel_size=k)
+        _, db = dwk.t_wgrad(cu(g[t + "x"]), cu(g[t + "dy"]), k)
+        for got, key in ((y, "y"), (dx, "dx"), (dw, "dw"), (db, "db")):
+            torch.testing.assert_close(got.cpu(), torch.from_numpy(g[t + key]), rtol=2e-12, atol=2e-12)
+
+
+S2_SHAPES = [(2, 3, 5, 6, 7), (1, 4, 16, 16, 16), (1, 2, 9, 12, 17)]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("k", [1, 3, 5, 7])
+@pytest.mark.parametrize("shape", S2_SHAPES)
+def test_stride2_and_transpose(dtype, k, shape):
+    seed = seed_of("s2", str(dtype), k, shape)
+    n, c = shape[:2]
+    w = rand((c, 1, k, k, k), dtype, seed + 1, scale=1 / np.sqrt(k**3))
+    b = rand((c,), dtype, seed + 2)
+    # down block: big -> small
+    x = rand(shape, dtype, seed)
+    y = dwk.s2_forward(x.cuda(), w.cuda(), b.cuda(), k)
+    dy = rand(tuple(y.shape), dtype, seed + 3)
+    dx = dwk.s2_dgrad(dy.cuda(), w.cuda(), shape[2:], k)
+    dw, db = dwk.s2_wgrad(x.cuda(), dy.cuda(), k)
+    check(y, orc.s2_fwd(host(x), host(w), host(b), k), dtype, "s2 y")
+    check(dx, orc.s2_dgrad(host(dy), host(w), shape[2:], k), dtype, "s2 dx")
+    want_dw, want_db = orc.s2_wgrad(host(x), host(dy), k)
+    check(dw, want_dw, dtype, "s2 dw", scale=2.0)
+    check(db, want_db, dtype, "s2 db", scale=2.0)
+    # up block: small -> big (2S-1)
+    xs = rand(shape, dtype, seed + 4)
+    yt = dwk.t_forward(xs.cuda(), w.cuda(), b.cuda(), k)
+    dyt = rand(tuple(yt.shape), dtype, seed + 5)
+    dxt = dwk.t_dgrad(dyt.cuda(), w.cuda(), k)
+    dwt, dbt = dwk.t_wgrad(xs.cuda(), dyt.cuda(), k)
+    check(yt, orc.t_fwd(host(xs), host(w), host(b), k), dtype, "t y")
+    check(dxt, orc.t_dgrad(host(dyt), host(w), k), dtype, "t dx")
+    want_dw, want_db = orc.t_wgrad(host(xs), host(dyt), k)
+    check(dwt, want_dw, dtype, "t dw", scale=2.0)
+    check(dbt, want_db, dtype, "t db", scale=2.0)
+
+
+def test_config1_fp32_full_size():
+    """N=1, C=32, 64^3, k=3, fp32, bias; weights ~N(0,1)/sqrt(27),
+    seed 0; y, grad_input, grad_weight against F.conv3d autograd on CPU."""
+    torch.manual_seed(0)
+    x = torch.randn(1, 32, 64, 64, 64)
+    dy = torch.randn(1, 32, 64, 64, 64)
+    w = torch.randn(32, 1, 3, 3, 3) / np.sqrt(27)
+    b = torch.randn(32)
+    xr = x.double().requires_grad_()
+    wr = w.double().requires_grad_()
+    br = b.double().requires_grad_()
+    yr = F.conv3d(xr, wr, br, padding=1, groups=32)
+    dxr, dwr, dbr = torch.autograd.grad(yr, (xr, wr, br), dy.double())
+    op = dwk.depthwise_conv3d_regular
+    xg = x.cuda().requires_grad_()
+    wg = w.cuda().requires_grad_()
+    bg = b.cuda().requires_grad_()
+    yg = op(xg, wg, bg, 3, 32, 64, 8, 512, 128, True, True)
+    dxg, dwg, dbg = torch.autograd.grad(yg, (xg, wg, bg), dy.cuda())
+    for got, want, name in ((yg, yr, "y"), (dxg, dxr, "dx"), (dwg, dwr, "dw"), (dbg, dbr, "db")):
+        mr = orc.max_rel(got.detach().double().cpu().numpy(), want.detach().numpy())
+        assert mr <= 1e-5, f"{name}: {mr:.3e}"
+
+
+def test_weight_grad_is_deterministic():
+    x = rand((2, 8, 32, 32, 32), torch.bfloat16, 5).cuda()
+    dy = rand((2, 8, 32, 32, 32), torch.bfloat16, 6).cuda()
+    a = dwk.dw_wgrad(x, dy, 3)
+    b = dwk.dw_wgrad(x, dy, 3)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    a = dwk.t_wgrad(x, rand((2, 8, 63, 63, 63), torch.bfloat16, 7).cuda(), 3)
+    assert torch.isfinite(a[0].float()).all()
+
+
+def test_dgrad_with_addend_adds_residual():
+    x = rand((1, 4, 8, 16, 16), torch.bfloat16, 8).cuda()
+    w = rand((4, 1, 3, 3, 3), torch.bfloat16, 9).cuda()
+    r = rand((1, 4, 8, 16, 16), torch.bfloat16, 10).cuda()
+    plain = dwk.dw_dgrad(x, w, 3).float()
+    fused = dwk.dw_dgrad(x, w, 3, addend=r).float()
+    torch.testing.assert_close(fused, plain + r.float(), rtol=1e-2, atol=2e-2)
+
+
+def test_gn_statistics_fused_into_forward():
+    x = rand((2, 4, 16, 16, 16), torch.bfloat16, 11).cuda()
+    w = rand((4, 1, 3, 3, 3), torch.bfloat16, 12).cuda()
+    y, stats = dwk.dw_forward(x, w, None, 3, gn_eps=1e-5)
+    yf = y.double().reshape(8, -1)
+    mean = yf.mean(1)
+    rstd = 1 / torch.sqrt(yf.var(1, unbiased=False) + 1e-5)
+    torch.testing.assert_close(stats[:, 0].double(), mean, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(stats[:, 1].double(), rstd, rtol=1e-5, atol=1e-6)
+
+
+def test_low_level_errors_match_reference():
+    x = torch.randn(1, 2, 4, 4, 4)
+    w = torch.randn(2, 1, 3, 3, 3)
+    with pytest.raises(ValueError, match="CUDA"):
+        dwk.depthwise_input_grad(x, w)
+    with pytest.raises(ValueError, match="power of two"):
+        dwk.depthwise_input_grad(x.cuda(), w.cuda(), block=100)
+    with pytest.raises(ValueError, match="odd"):
+        dwk.depthwise_weight_grad(x.cuda(), x.cuda(), kernel_size=4)
+    with pytest.raises(ValueError, match="contiguous"):
+        dwk.depthwise_input_grad(x.cuda().transpose(2, 3), w.cuda())
+
+
+def test_no_device_error_recorded():
+    assert nat.device_error() == 0

@@ -1,0 +1,158 @@
+"""tcgen05 pointwise GEMMs (forward / input-grad / weight-grad with the fused
+prologues and epilogues) against the CPU oracle on the same bf16 inputs."""
+
+from __future__ import annotations
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from mednext_accel_b200 import _native as nat
+from mednext_accel_b200.pointwise import gn_stats, pointwise_conv3d, pw_gemm, pw_wgrad
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def rand(shape, seed, dtype=torch.bfloat16, scale=1.0):
+    gen = torch.Generator().manual_seed(zlib.crc32(repr((shape, seed)).encode()) % 100_000)
+    return (torch.randn(shape, generator=gen, dtype=torch.float64) * scale).to(dtype)
+
+
+def h(t):
+    return t.double().cpu().numpy()
+
+
+def assert_close_bf16(got, want, what, rel_l2=4e-3, max_rel=2e-2):
+    g = h(got)
+    rl, mr = orc.rel_l2(g, want), orc.max_rel(g, want)
+    assert rl <= rel_l2 and mr <= max_rel, f"{what}: rel_l2 {rl:.3e} max_rel {mr:.3e}"
+
+
+GEMM_SHAPES = [
+    # (n, cin, cout, spatial)
+    (1, 32, 64, (16, 16, 16)),
+    (2, 64, 32, (8, 8, 8)),
+    (1, 1, 32, (16, 16, 16)),        # stem: K=1
+    (2, 96, 192, (5, 7, 9)),         # odd voxel count, non-multiple-of-64 K
+    (1, 128, 512, (8, 8, 8)),        # two N tiles, two K stages
+    (1, 512, 2048, (4, 4, 4)),       # 8 N tiles, 8 K stages, 64 voxels
+    (1, 2048, 512, (4, 4, 3)),       # deep K
+    (1, 64, 128, (15, 15, 15)),      # up-block volume 15^3
+]
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", GEMM_SHAPES)
+def test_forward_bias(n, cin, cout, spatial):
+    x = rand((n, cin, *spatial), 1)
+    w = rand((cout, cin), 2, scale=1 / np.sqrt(cin))
+    b = rand((cout,), 3, torch.float32)
+    y, _ = pw_gemm(x.cuda(), w.cuda(), cout, bias=b.cuda())
+    want = orc.pointwise_fwd(h(x), h(w), h(b))
+    assert_close_bf16(y, want, "y")
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", GEMM_SHAPES[:5])
+def test_forward_groupnorm_prologue_gelu_epilogue_chain(n, cin, cout, spatial):
+    """expand(GroupNorm(t)) then project(gelu(u)) + residual, as in the block."""
+    t = (rand((n, cin, *spatial), 4).double() * 3 + 1.5).to(torch.bfloat16)
+    gamma = (1 + 0.2 * rand((cin,), 5, torch.float64)).float()
+    beta = (0.2 * rand((cin,), 6, torch.float64)).float()
+    we = rand((cout, cin), 7, scale=1 / np.sqrt(cin))
+    be = rand((cout,), 8, torch.float32)
+    tg = t.cuda()
+    stats = gn_stats(tg, 1e-5)
+    u, _ = pw_gemm(tg, we.cuda(), cout, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=gamma.cuda(),
+                   pro_beta=beta.cuda(), bias=be.cuda())
+    z, mean, rstd = orc.groupnorm_fwd(h(t), h(gamma), h(beta))
+    np.testing.assert_allclose(h(stats)[:, 0], mean, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(h(stats)[:, 1], rstd, rtol=1e-4, atol=1e-5)
+    want_u = orc.pointwise_fwd(orc.round_bf16(z), h(we), h(be))
+    assert_close_bf16(u, want_u, "u")
+    wp = rand((cin, cout), 9, scale=1 / np.sqrt(cout))
+    bp = rand((cin,), 10, torch.float32)
+    res = rand((n, cin, *spatial), 11)
+    y, _ = pw_gemm(u, wp.cuda(), cin, prologue=nat.PRO_GELU, bias=bp.cuda(), residual=res.cuda())
+    want_y = orc.pointwise_fwd(orc.round_bf16(orc.gelu(h(u))), h(wp), h(bp)) + h(res)
+    assert_close_bf16(y, want_y, "y")
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", GEMM_SHAPES[:4])
+def test_dgrad_gelu_grad_epilogue(n, cin, cout, spatial):
+    dy = rand((n, cin, *spatial), 12)
+    wt = rand((cout, cin), 13, scale=1 / np.sqrt(cin))  # already transposed weight
+    u = rand((n, cout, *spatial), 14)
+    du, _ = pw_gemm(dy.cuda(), wt.cuda(), cout, aux=u.cuda(), gelu_grad=True)
+    want = orc.round_bf16(orc.pointwise_fwd(h(dy), h(wt), None)) * orc.gelu_grad(h(u))
+    assert_close_bf16(du, want, "du")
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", GEMM_SHAPES[:4])
+def test_dgrad_groupnorm_backward_partials(n, cin, cout, spatial):
+    du = rand((n, cin, *spatial), 15)
+    wt = rand((cout, cin), 16, scale=1 / np.sqrt(cin))
+    t = rand((n, cout, *spatial), 17)
+    stats = gn_stats(t.cuda(), 1e-5)
+    dz, part = pw_gemm(du.cuda(), wt.cuda(), cout, aux=t.cuda(), gn_bwd_stats=stats)
+    from mednext_accel_b200.pointwise import gn_backward_from_partials
+
+    gamma = (1 + 0.1 * rand((cout,), 18, torch.float64)).float().cuda()
+    dt, dg, db = gn_backward_from_partials(dz, t.cuda(), stats, gamma, part)
+    dzr = orc.round_bf16(orc.pointwise_fwd(h(du), h(wt), None))
+    assert_close_bf16(dz, dzr, "dz")
+    mean, rstd = h(stats)[:, 0], h(stats)[:, 1]
+    want_dt, want_dg, want_db = orc.groupnorm_bwd(h(dz), h(t), mean, rstd, h(gamma))
+    assert_close_bf16(dt, want_dt, "dt")
+    np.testing.assert_allclose(h(dg), want_dg, rtol=2e-4, atol=2e-3)
+    np.testing.assert_allclose(h(db), want_db, rtol=2e-4, atol=2e-3)
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", GEMM_SHAPES)
+@pytest.mark.parametrize("prologue", [nat.PRO_NONE, nat.PRO_GELU, nat.PRO_GROUPNORM])
+def test_wgrad(n, cin, cout, spatial, prologue):
+    g = rand((n, cout, *spatial), 19)
+    a = rand((n, cin, *spatial), 20)
+    kw = {}
+    a_eff = h(a)
+    if prologue == nat.PRO_GELU:
+        a_eff = orc.round_bf16(orc.gelu(a_eff))
+    elif prologue == nat.PRO_GROUPNORM:
+        gamma = (1 + 0.1 * rand((cin,), 21, torch.float64)).float()
+        beta = (0.1 * rand((cin,), 22, torch.float64)).float()
+        stats = gn_stats(a.cuda(), 1e-5)
+        kw = dict(pro_stats=stats, pro_gamma=gamma.cuda(), pro_beta=beta.cuda())
+        z, _, _ = orc.groupnorm_fwd(a_eff, h(gamma), h(beta))
+        a_eff = orc.round_bf16(z)
+    dw, db = pw_wgrad(g.cuda(), a.cuda(), prologue=prologue, **kw)
+    _, want_dw, want_db = orc.pointwise_bwd(h(g), a_eff, np.zeros((cout, cin)))
+    assert orc.rel_l2(h(dw), want_dw) <= 2e-3, orc.rel_l2(h(dw), want_dw)
+    assert orc.rel_l2(h(db), want_db) <= 1e-5
+
+
+def test_wgrad_is_deterministic():
+    g = rand((2, 64, 32, 32, 32), 23).cuda()
+    a = rand((2, 128, 32, 32, 32), 24).cuda()
+    a1 = pw_wgrad(g, a)
+    a2 = pw_wgrad(g, a)
+    assert torch.equal(a1[0], a2[0]) and torch.equal(a1[1], a2[1])
+
+
+def test_pointwise_op_autograd():
+    x = rand((2, 32, 8, 8, 8), 25).cuda().requires_grad_()
+    w = rand((64, 32, 1, 1, 1), 26, scale=0.2).cuda().requires_grad_()
+    b = rand((64,), 27).cuda().requires_grad_()
+    y = pointwise_conv3d(x, w, b)
+    dy = rand(tuple(y.shape), 28).cuda()
+    dx, dw, db = torch.autograd.grad(y, (x, w, b), dy)
+    want_y = orc.pointwise_fwd(h(x), h(w), h(b))
+    assert_close_bf16(y, want_y, "y")
+    wdx, wdw, wdb = orc.pointwise_bwd(h(dy), h(x), h(w))
+    assert_close_bf16(dx, wdx, "dx")
+    assert_close_bf16(dw.reshape(64, 32), wdw, "dw")
+    assert_close_bf16(db, wdb, "db")
+
+
+def test_no_device_error_recorded():
+    assert nat.device_error() == 0
