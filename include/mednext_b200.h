@@ -133,24 +133,30 @@ int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbia
                         int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream);
 
 /* ------- depthwise ConvTranspose3d, stride 2, padding k/2 (up block) ------
- * (d, h, w) are the INPUT sizes; the output is (2d-1, 2h-1, 2w-1). */
+ * (d, h, w) are the INPUT sizes; the output is (2d-1, 2h-1, 2w-1).
+ * big_pitch: elements between consecutive (n, c) volumes of the (2d-1)^3-sized
+ * tensor (y in fwd, dy in dgrad/wgrad); 0 means contiguous.  A larger pitch
+ * (e.g. the voxel count rounded up to a multiple of 8) lets the following 1x1
+ * GEMMs describe the tensor with TMA; fwd writes zeros into the pitch tail. */
 int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n,
-                    int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
+                    int64_t c, int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype,
                     mednext_stream_t stream);
 int mednext_dwT_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c,
-                      int64_t d, int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream);
+                      int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype,
+                      mednext_stream_t stream);
 size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
                                         int k, int dtype);
 int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
                       size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h,
-                      int64_t w, int k, int dtype, mednext_stream_t stream);
+                      int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream);
 
 /* ---------------- GroupNorm with groups == channels ----------------------
  * x: [n, c, spatial]; stats: float [n*c][2] = (mean, rstd).  gamma/beta: [c]
  * in gamma_dtype (FLOAT32 parameters in the reference model). */
 size_t mednext_gn_stats_workspace_size(int64_t n, int64_t c, int64_t spatial);
+/* pitch: elements between (n, c) rows (0 = spatial); only `spatial` are read. */
 int mednext_gn_stats(const void* x, float* stats, void* workspace, size_t workspace_bytes,
-                     int64_t n, int64_t c, int64_t spatial, float eps, int dtype,
+                     int64_t n, int64_t c, int64_t spatial, int64_t pitch, float eps, int dtype,
                      mednext_stream_t stream);
 int mednext_gn_fwd(const void* x, const float* stats, const void* gamma, const void* beta,
                    void* y, int64_t n, int64_t c, int64_t spatial, int x_dtype, int y_dtype,
@@ -191,12 +197,14 @@ int mednext_pw_wgrad(const void* g, const void* a, float* dw, float* dbias, int 
                      void* workspace, size_t workspace_bytes, int64_t n, int64_t cin,
                      int64_t cout, int64_t vox, int dtype, mednext_stream_t stream);
 /* GroupNorm backward driven by the partial sums that mednext_pw_fwd wrote with
- * MEDNEXT_EPI_GN_BWD_STATS (dz = that GEMM's output = grad of GroupNorm output). */
+ * MEDNEXT_EPI_GN_BWD_STATS (dz = that GEMM's output = grad of GroupNorm output).
+ * vox: valid voxels per (n, c) row; pitch: row length the GEMM ran over (its
+ * vox argument; 0 = vox).  The partials in pw_workspace are folded in place. */
 int mednext_gn_bwd_from_partials(const void* dz, const void* x, const float* stats,
                                  const void* gamma, void* dx, float* dgamma, float* dbeta,
-                                 const void* pw_workspace, int64_t n, int64_t c, int64_t vox,
-                                 int dz_dtype, int x_dtype, int dx_dtype, int gamma_dtype,
-                                 mednext_stream_t stream);
+                                 void* pw_workspace, int64_t n, int64_t c, int64_t vox,
+                                 int64_t pitch, int dz_dtype, int x_dtype, int dx_dtype,
+                                 int gamma_dtype, mednext_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -29,6 +29,7 @@ from __future__ import annotations
 import torch
 from torch import Tensor
 from torch.library import custom_op
+from torch.nn import functional as F
 
 from . import _native as nat
 from . import depthwise as dwk
@@ -37,6 +38,14 @@ from .pointwise import gn_backward_from_partials, gn_stats, pw_gemm, pw_wgrad
 _NS = "mednext_accel_b200"
 KIND_REGULAR, KIND_DOWN, KIND_UP = 0, 1, 2
 _CODES = {0: torch.float32, 1: torch.bfloat16, 2: torch.float16}
+
+
+def _pitch(spatial: tuple[int, ...]) -> tuple[int, int]:
+    """(voxels, row pitch rounded up to 8 elements = 16 bytes of bf16)."""
+    vox = 1
+    for s in spatial:
+        vox *= int(s)
+    return vox, (vox + 7) // 8 * 8
 
 
 def _depthwise_forward(xb: Tensor, w: Tensor, b: Tensor | None, kind: int, k: int, eps: float) -> tuple[Tensor, Tensor]:
@@ -76,13 +85,37 @@ def mednext_block(
     compute_dtype: int,
 ) -> tuple[Tensor, Tensor, Tensor, Tensor]:
     """Returns (y, t, u, stats); t, u (empty when not kept) and stats are saved
-    for backward and carry no gradient."""
+    for backward and carry no gradient.
+
+    For the up block (kind 2) y is the final, left-padded (2S)^3 output of the
+    reference's ``F.pad(block(x) + residual(x))`` and t, u are pitched
+    [n, c, pitch] buffers whose rows hold the (2S-1)^3 voxels followed by a zero
+    tail, so that every GEMM operand has 16-byte aligned rows for TMA."""
     cdt = _CODES[compute_dtype]
     xb = x.to(cdt).contiguous()
-    t, stats = _depthwise_forward(xb, dw_w.to(cdt).contiguous(), dw_b.to(cdt), kind, kernel_size, eps)
-    u = _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
+    wdw, bdw = dw_w.to(cdt).contiguous(), dw_b.to(cdt)
     cout = int(p_w.shape[0])
     res = x if residual_is_input else addend
+    if kind == KIND_UP:
+        big = tuple(2 * int(s) - 1 for s in x.shape[2:])
+        vox, pitch = _pitch(big)
+        t = dwk.t_forward(xb, wdw, bdw, kernel_size, pitch=pitch)
+        stats = gn_stats(t, eps, vox=vox)
+        u = _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
+        res_p = None
+        if res is not None:
+            res_p = torch.empty((x.shape[0], cout, pitch), dtype=res.dtype, device=x.device)
+            dwk.pitched_view(res_p, big).copy_(res)
+            res_p[:, :, vox:].zero_()
+        y_p, _ = pw_gemm(
+            u, p_w.reshape(cout, -1).to(cdt).contiguous(), cout,
+            out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
+            bias=p_b.to(cdt).float(), residual=res_p,
+        )
+        y = F.pad(dwk.pitched_view(y_p, big), (1, 0) * 3)
+        return y, t, (u if keep_expansion else u.new_empty((0,))), stats
+    t, stats = _depthwise_forward(xb, wdw, bdw, kind, kernel_size, eps)
+    u = _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
     y, _ = pw_gemm(
         u, p_w.reshape(cout, -1).to(cdt).contiguous(), cout,
         out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
@@ -97,14 +130,20 @@ def _(x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, kind, kernel_size, 
     cdt = _CODES[compute_dtype]
     n, c = x.shape[0], x.shape[1]
     sp = tuple(x.shape[2:])
-    if kind == KIND_DOWN:
-        sp = tuple((s + 1) // 2 for s in sp)
-    elif kind == KIND_UP:
-        sp = tuple(2 * s - 1 for s in sp)
     res = x if residual_is_input else addend
-    y = x.new_empty((n, p_w.shape[0], *sp), dtype=res.dtype if res is not None else cdt)
-    t = x.new_empty((n, c, *sp), dtype=cdt)
-    u = x.new_empty((n, e_w.shape[0], *sp), dtype=cdt) if keep_expansion else x.new_empty((0,), dtype=cdt)
+    ydt = res.dtype if res is not None else cdt
+    if kind == KIND_UP:
+        big = tuple(2 * s - 1 for s in sp)
+        _, pitch = _pitch(big)
+        y = x.new_empty((n, p_w.shape[0], *(2 * s for s in sp)), dtype=ydt)
+        t = x.new_empty((n, c, pitch), dtype=cdt)
+        u = x.new_empty((n, e_w.shape[0], pitch), dtype=cdt) if keep_expansion else x.new_empty((0,), dtype=cdt)
+    else:
+        if kind == KIND_DOWN:
+            sp = tuple((s + 1) // 2 for s in sp)
+        y = x.new_empty((n, p_w.shape[0], *sp), dtype=ydt)
+        t = x.new_empty((n, c, *sp), dtype=cdt)
+        u = x.new_empty((n, e_w.shape[0], *sp), dtype=cdt) if keep_expansion else x.new_empty((0,), dtype=cdt)
     stats = x.new_empty((n * c, 2), dtype=torch.float32)
     return y, t, u, stats
 
@@ -130,12 +169,23 @@ def mednext_block_backward(
     """Returns (dx, dw_w, dw_b, dgamma, dbeta, de_w, de_b, dp_w, dp_b) in the
     parameters' dtypes."""
     cdt = _CODES[compute_dtype]
-    dy = dy.contiguous()
-    dyb = dy.to(cdt)
-    xb = x.to(cdt).contiguous()
-    u = u_saved if u_saved.numel() > 0 else _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
     rc, c = int(e_w.shape[0]), int(e_w.shape[1])
     cout = int(p_w.shape[0])
+    vox = None
+    if kind == KIND_UP:
+        # dy is the grad of the padded (2S)^3 output; the pad voxels carry no
+        # dependence on the block, so only the (2S-1)^3 interior flows back,
+        # repacked into a pitched buffer with a zero tail
+        big = tuple(2 * int(s) - 1 for s in x.shape[2:])
+        vox, pitch = _pitch(big)
+        dyb = torch.empty((x.shape[0], cout, pitch), dtype=cdt, device=dy.device)
+        dwk.pitched_view(dyb, big).copy_(dy[:, :, 1:, 1:, 1:])
+        dyb[:, :, vox:].zero_()
+    else:
+        dy = dy.contiguous()
+        dyb = dy.to(cdt)
+    xb = x.to(cdt).contiguous()
+    u = u_saved if u_saved.numel() > 0 else _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
     # project dgrad with the GELU derivative in the epilogue
     p_wt = p_w.reshape(cout, rc).to(cdt).t().contiguous()  # [rc, cout]
     du, _ = pw_gemm(dyb, p_wt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
@@ -147,7 +197,7 @@ def mednext_block_backward(
     # expand dgrad + GroupNorm-backward partial sums
     e_wt = e_w.reshape(rc, c).to(cdt).t().contiguous()  # [c, rc]
     dz, part = pw_gemm(du, e_wt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)
-    dt, dgamma, dbeta = gn_backward_from_partials(dz, t, stats, g_w, part)
+    dt, dgamma, dbeta = gn_backward_from_partials(dz, t, stats, g_w, part, vox=vox)
     wdw = dw_w.to(cdt).contiguous()
     if kind == KIND_REGULAR:
         dx = dwk.dw_dgrad(dt, wdw, kernel_size, addend=dyb if residual_is_input and dy.dtype == cdt else None)
@@ -156,7 +206,7 @@ def mednext_block_backward(
         dx = dwk.s2_dgrad(dt, wdw, tuple(int(s) for s in x.shape[2:]), kernel_size)
         dwdw, dbdw = dwk.s2_wgrad(xb, dt, kernel_size)
     else:
-        dx = dwk.t_dgrad(dt, wdw, kernel_size)
+        dx = dwk.t_dgrad(dt, wdw, kernel_size, small=tuple(int(s) for s in x.shape[2:]))
         dwdw, dbdw = dwk.t_wgrad(xb, dt, kernel_size)
     if dx.dtype != x.dtype:
         dx = dx.to(x.dtype)
@@ -213,7 +263,8 @@ def _backward(ctx, dy, _dt, _du, _dstats):
     )
     d_add = None
     if ctx.has_addend and ctx.needs_input_grad[1]:
-        d_add = dy if dy.dtype == ctx.addend_dtype else dy.to(ctx.addend_dtype)
+        g = dy[:, :, 1:, 1:, 1:] if ctx.kind == KIND_UP else dy  # the up block's output is left-padded
+        d_add = g if g.dtype == ctx.addend_dtype else g.to(ctx.addend_dtype)
     return dx, d_add, dww, dwb, dgw, dgb, dew, deb, dpw, dpb, None, None, None, None, None, None
 
 

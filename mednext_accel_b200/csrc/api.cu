@@ -61,6 +61,7 @@ bool pw_shape_ok(int64_t n, int64_t cin, int64_t cout, int64_t vox) {
          vox < ((int64_t)1 << 40);
 }
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+bool pitch_ok(int64_t pitch, int64_t vol) { return pitch == 0 || pitch >= vol; }
 
 }  // namespace
 
@@ -214,24 +215,27 @@ int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbia
 
 // ------------------------------ depthwise transpose ------------------------------
 int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n, int64_t c, int64_t d,
-                    int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream) {
+                    int64_t h, int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
+  if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
   if (x == nullptr || weight == nullptr || y == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   if (!aligned(x, esz) || !aligned(y, esz) || !aligned(weight, esz) || (bias && !aligned(bias, esz)))
     return MEDNEXT_ERR_ALIGNMENT;
-  return dispatch_dw_s2_scatter(dtype, k, x, weight, bias, y, s2_geom_up(n, c, d, h, w), as_stream(stream));
+  return dispatch_dw_s2_scatter(dtype, k, x, weight, bias, y, s2_geom_up(n, c, d, h, w, big_pitch), as_stream(stream));
 }
 
 int mednext_dwT_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c, int64_t d, int64_t h,
-                      int64_t w, int k, int dtype, mednext_stream_t stream) {
+                      int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
+  if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
   if (dy == nullptr || weight == nullptr || dx == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   if (!aligned(dy, esz) || !aligned(dx, esz) || !aligned(weight, esz)) return MEDNEXT_ERR_ALIGNMENT;
-  return dispatch_dw_s2_gather(dtype, k, dy, weight, nullptr, dx, s2_geom_up(n, c, d, h, w), as_stream(stream));
+  return dispatch_dw_s2_gather(dtype, k, dy, weight, nullptr, dx, s2_geom_up(n, c, d, h, w, big_pitch),
+                               as_stream(stream));
 }
 
 size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
@@ -240,10 +244,11 @@ size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t
 }
 
 int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
-                      size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
-                      int dtype, mednext_stream_t stream) {
+                      size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                      int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
+  if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
   if (x == nullptr || dy == nullptr || dweight == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   if (!aligned(x, esz) || !aligned(dy, esz) || !aligned(dweight, esz) || (dbias && !aligned(dbias, esz)))
@@ -252,8 +257,8 @@ int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias,
       workspace_bytes < mednext_dwT_wgrad_workspace_size(n, c, d, h, w, k, dtype))
     return MEDNEXT_ERR_WORKSPACE;
   // big grid = dy (2S-1), small grid = x (S); the bias grad sums dy (big)
-  return dispatch_dw_s2_wgrad(dtype, k, dy, x, dweight, dbias, workspace, s2_geom_up(n, c, d, h, w), true,
-                              as_stream(stream));
+  return dispatch_dw_s2_wgrad(dtype, k, dy, x, dweight, dbias, workspace, s2_geom_up(n, c, d, h, w, big_pitch),
+                              true, as_stream(stream));
 }
 
 // ------------------------------ GroupNorm ------------------------------
@@ -263,15 +268,16 @@ size_t mednext_gn_stats_workspace_size(int64_t n, int64_t c, int64_t spatial) {
 }
 
 int mednext_gn_stats(const void* x, float* stats, void* workspace, size_t workspace_bytes, int64_t n, int64_t c,
-                     int64_t spatial, float eps, int dtype, mednext_stream_t stream) {
+                     int64_t spatial, int64_t pitch, float eps, int dtype, mednext_stream_t stream) {
   if (elem_size(dtype) == 0) return MEDNEXT_ERR_BAD_DTYPE;
   if (x == nullptr || stats == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   if (!gn_shape_ok(n, c, spatial)) return MEDNEXT_ERR_BAD_SHAPE;
   if (!aligned(x, elem_size(dtype)) || !aligned(stats, 8)) return MEDNEXT_ERR_ALIGNMENT;
   if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < mednext_gn_stats_workspace_size(n, c, spatial))
     return MEDNEXT_ERR_WORKSPACE;
-  return dispatch_gn_stats(dtype, x, static_cast<GnPartial*>(workspace), n * c, spatial, gn_chunks(n * c, spatial),
-                           eps, stats, as_stream(stream));
+  if (!pitch_ok(pitch, spatial)) return MEDNEXT_ERR_BAD_SHAPE;
+  return dispatch_gn_stats(dtype, x, static_cast<GnPartial*>(workspace), n * c, spatial, pitch > 0 ? pitch : spatial,
+                           gn_chunks(n * c, spatial), eps, stats, as_stream(stream));
 }
 
 int mednext_gn_fwd(const void* x, const float* stats, const void* gamma, const void* beta, void* y, int64_t n,
@@ -303,22 +309,25 @@ int mednext_gn_bwd(const void* dy, const void* x, const float* stats, const void
   int st = dispatch_gn_bwd_partial(x_dtype, dy_dtype, dy, x, stats, part, n * c, spatial, chunks, as_stream(stream));
   if (st != MEDNEXT_OK) return st;
   return dispatch_gn_bwd_apply(x_dtype, dy_dtype, gamma_dtype, dy, x, stats, gamma, part, chunks, dx, dgamma, dbeta,
-                               (int)n, (int)c, spatial, as_stream(stream));
+                               (int)n, (int)c, spatial, spatial, as_stream(stream));
 }
 
 int mednext_gn_bwd_from_partials(const void* dz, const void* x, const float* stats, const void* gamma, void* dx,
-                                 float* dgamma, float* dbeta, const void* pw_workspace, int64_t n, int64_t c,
-                                 int64_t vox, int dz_dtype, int x_dtype, int dx_dtype, int gamma_dtype,
-                                 mednext_stream_t stream) {
+                                 float* dgamma, float* dbeta, void* pw_workspace, int64_t n, int64_t c,
+                                 int64_t vox, int64_t pitch, int dz_dtype, int x_dtype, int dx_dtype,
+                                 int gamma_dtype, mednext_stream_t stream) {
   if (elem_size(dz_dtype) == 0 || elem_size(x_dtype) == 0 || elem_size(gamma_dtype) == 0) return MEDNEXT_ERR_BAD_DTYPE;
   if (dx_dtype != x_dtype) return MEDNEXT_ERR_BAD_DTYPE;
   if (dz == nullptr || x == nullptr || stats == nullptr || dx == nullptr || pw_workspace == nullptr)
     return MEDNEXT_ERR_NULL_POINTER;
   if (!gn_shape_ok(n, c, vox)) return MEDNEXT_ERR_BAD_SHAPE;
-  const int mtiles = (int)((vox + kPwBM - 1) / kPwBM);
+  if (!pitch_ok(pitch, vox)) return MEDNEXT_ERR_BAD_SHAPE;
+  const int64_t rows = pitch > 0 ? pitch : vox;
+  // one partial per (sample, channel, 128-voxel tile, 32-voxel quarter) of the GEMM's rows
+  const int parts = (int)((rows + kPwBM - 1) / kPwBM) * 4;
   return dispatch_gn_bwd_apply(x_dtype, dz_dtype, gamma_dtype, dz, x, stats, gamma,
-                               static_cast<const GnBwdPartial*>(pw_workspace), mtiles, dx, dgamma, dbeta, (int)n,
-                               (int)c, vox, as_stream(stream));
+                               static_cast<const GnBwdPartial*>(pw_workspace), parts, dx, dgamma, dbeta, (int)n,
+                               (int)c, vox, rows, as_stream(stream));
 }
 
 // ------------------------------ pointwise ------------------------------
@@ -326,7 +335,7 @@ size_t mednext_pw_fwd_workspace_size(int64_t n, int64_t cin, int64_t cout, int64
   if (!pw_shape_ok(n, cin, cout, vox)) return 0;
   if (!(epilogue & MEDNEXT_EPI_GN_BWD_STATS)) return 0;
   const int64_t mtiles = (vox + kPwBM - 1) / kPwBM;
-  return (size_t)n * cout * mtiles * sizeof(GnBwdPartial);
+  return (size_t)n * cout * mtiles * 4 * sizeof(GnBwdPartial);
 }
 
 int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const float* pro_stats,

@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(448) dw_s1_wgrad_grouped_kernel(
   const int w0 = tw * g.TW, h0 = th * g.TH, d0 = td * g.TD;
   const int rsw = DwTile<T>::row_elems(g.TW, P);
   const int rows = g.TH + 2 * P;
-  const int G = g.LW * g.TR;  // threads per group (a multiple of 32)
+  const int G = blockDim.x / K;  // threads per group: LW*TR rounded up to whole warps
   const int grp = threadIdx.x / G;
   const int lt = threadIdx.x - grp * G;
   const int wt = lt % g.LW;

@@ -17,6 +17,7 @@ struct DwS2Geom {
   int N, C;
   int Db, Hb, Wb;  // big grid
   int Ds, Hs, Ws;  // small grid
+  long long bp;    // elements between consecutive (n, c) volumes of the big grid (>= Db*Hb*Wb)
 };
 
 // gather: one thread per small-grid output, consecutive threads along W.
@@ -40,7 +41,7 @@ __global__ void __launch_bounds__(256) dw_s2_gather_kernel(const T* __restrict__
     const int oh = (int)(r % g.Hs);
     const int od = (int)(r / g.Hs);
     const int c = (int)(nc % g.C);
-    const T* src = big + nc * bvol;
+    const T* src = big + nc * (size_t)g.bp;
     const T* w = wgt + (size_t)c * K3;
     Acc acc = bias != nullptr ? to_acc<T>(bias[c]) : Acc(0);
 #pragma unroll
@@ -75,12 +76,17 @@ __global__ void __launch_bounds__(256) dw_s2_scatter_kernel(const T* __restrict_
   constexpr int P = K / 2;
   constexpr int K3 = K * K * K;
   const size_t bvol = (size_t)g.Db * g.Hb * g.Wb;
-  const size_t total = (size_t)g.N * g.C * bvol;
+  const size_t bp = (size_t)g.bp;
+  const size_t total = (size_t)g.N * g.C * bp;
   const size_t svol = (size_t)g.Ds * g.Hs * g.Ws;
   for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
-    const size_t nc = idx / bvol;
-    size_t r = idx - nc * bvol;
+    const size_t nc = idx / bp;
+    size_t r = idx - nc * bp;
+    if (r >= bvol) {  // padding tail of a pitched row: keep it finite
+      big[idx] = from_acc<T>(Acc(0));
+      continue;
+    }
     const int iw = (int)(r % g.Wb);
     r /= g.Wb;
     const int ih = (int)(r % g.Hb);
@@ -130,7 +136,7 @@ __global__ void __launch_bounds__(448) dw_s2_wgrad_kernel(const T* __restrict__ 
   const size_t nc = blockIdx.x / chunks;
   const size_t svol = (size_t)g.Ds * g.Hs * g.Ws;
   const size_t bvol = (size_t)g.Db * g.Hb * g.Wb;
-  const T* bsrc = big + nc * bvol;
+  const T* bsrc = big + nc * (size_t)g.bp;
   const T* ssrc = small + nc * svol;
   const size_t beg = (size_t)j * chunk;
   const size_t end = min(beg + (size_t)chunk, svol);
@@ -189,7 +195,7 @@ __global__ void __launch_bounds__(448) dw_s2_wgrad_kernel(const T* __restrict__ 
 // partials (bias grad of the up block, whose dy is the big grid).
 template <typename T>
 __global__ void __launch_bounds__(256) chan_sum_into_partials_kernel(
-    const T* __restrict__ src, typename Elem<T>::Acc* __restrict__ part, size_t vol, int chunks,
+    const T* __restrict__ src, typename Elem<T>::Acc* __restrict__ part, size_t vol, size_t pitch, int chunks,
     int K3) {
   using Acc = typename Elem<T>::Acc;
   const int j = blockIdx.x % chunks;
@@ -197,7 +203,7 @@ __global__ void __launch_bounds__(256) chan_sum_into_partials_kernel(
   const size_t per = (vol + chunks - 1) / chunks;
   const size_t beg = (size_t)j * per;
   const size_t end = min(beg + per, vol);
-  const T* p = src + nc * vol;
+  const T* p = src + nc * pitch;
   Acc s = Acc(0);
   for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) s += to_acc<T>(__ldg(p + i));
   __shared__ Acc red[8];

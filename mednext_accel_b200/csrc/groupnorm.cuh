@@ -40,14 +40,14 @@ __device__ __forceinline__ bool vec_ok(const void* p, size_t vol) {
 template <typename T>
 __global__ void __launch_bounds__(256) gn_stats_partial_kernel(const T* __restrict__ x,
                                                                GnPartial* __restrict__ part,
-                                                               size_t vol, int chunks) {
+                                                               size_t vol, size_t pitch, int chunks) {
   using Acc = typename Elem<T>::Acc;
   const int j = blockIdx.x % chunks;
   const size_t nc = blockIdx.x / chunks;
   const size_t per = (vol + chunks - 1) / chunks;
   const size_t beg = (size_t)j * per;
   const size_t end = min(beg + per, vol);
-  const T* p = x + nc * vol;
+  const T* p = x + nc * pitch;
   Acc cnt = Acc(0), shift = Acc(0), s1 = Acc(0), s2 = Acc(0);
   for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
     const Acc v = to_acc<T>(__ldg(p + i));
@@ -150,37 +150,56 @@ __global__ void __launch_bounds__(256) gn_bwd_partial_kernel(const TD* __restric
   }
 }
 
-// Backward pass 2: dx = rstd * gamma * (dz - S1/V - xhat * S2/V).
-// Each CTA first folds the partials of its (n, c) in a fixed order.
+// Fold the `tiles` partials of each (n, c) into slot 0 of its row, in place:
+// thread t sums partials t, t+256, ... in order, then a fixed-shape tree.
+static __global__ void __launch_bounds__(256) gn_fold_partials_kernel(GnBwdPartial* __restrict__ part, int tiles) {
+  const size_t nc = blockIdx.x;
+  GnBwdPartial* p = part + nc * tiles;
+  double a = 0.0, b = 0.0;
+  for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+    a += p[t].s1;
+    b += p[t].s2;
+  }
+  __shared__ double ra[256], rb[256];
+  ra[threadIdx.x] = a;
+  rb[threadIdx.x] = b;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if ((int)threadIdx.x < s) {
+      ra[threadIdx.x] += ra[threadIdx.x + s];
+      rb[threadIdx.x] += rb[threadIdx.x + s];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    GnBwdPartial gp;
+    gp.s1 = ra[0];
+    gp.s2 = rb[0];
+    p[0] = gp;
+  }
+}
+
+// Backward pass 2: dx = rstd * gamma * (dz - S1/V - xhat * S2/V), with the
+// folded sums of (n, c) at folded[nc * stride].
 template <typename TD, typename TX, typename TO, typename TG>
 __global__ void __launch_bounds__(256) gn_bwd_apply_kernel(
     const TD* __restrict__ dz, const TX* __restrict__ x, const float* __restrict__ stats,
-    const TG* __restrict__ gamma, const GnBwdPartial* __restrict__ part, int part_tiles,
-    TO* __restrict__ dx, int C, size_t vol, int chunks) {
+    const TG* __restrict__ gamma, const GnBwdPartial* __restrict__ folded, int stride,
+    TO* __restrict__ dx, int C, size_t vol, size_t pitch, int chunks) {
   const int j = blockIdx.x % chunks;
   const size_t nc = blockIdx.x / chunks;
   const int c = (int)(nc % C);
-  __shared__ float sh[2];
-  if (threadIdx.x == 0) {
-    double a = 0.0, b = 0.0;
-    const GnBwdPartial* p = part + nc * part_tiles;
-    for (int t = 0; t < part_tiles; ++t) {
-      a += p[t].s1;
-      b += p[t].s2;
-    }
-    sh[0] = (float)(a / (double)vol);
-    sh[1] = (float)(b / (double)vol);
-  }
-  __syncthreads();
-  const float m1 = sh[0], m2 = sh[1];
+  const GnBwdPartial f = folded[nc * stride];
+  const float m1 = (float)(f.s1 / (double)vol);
+  const float m2 = (float)(f.s2 / (double)vol);
   const float mean = stats[2 * nc], rstd = stats[2 * nc + 1];
   const float gr = rstd * (gamma != nullptr ? param_f(gamma, c) : 1.0f);
   const size_t per = (vol + chunks - 1) / chunks;
   const size_t beg = (size_t)j * per;
   const size_t end = min(beg + per, vol);
-  const TD* g = dz + nc * vol;
-  const TX* xs = x + nc * vol;
-  TO* o = dx + nc * vol;
+  const TD* g = dz + nc * pitch;
+  const TX* xs = x + nc * pitch;
+  TO* o = dx + nc * pitch;
   for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
     const float d = (float)to_acc<TD>(__ldg(g + i));
     const float xh = ((float)to_acc<TX>(__ldg(xs + i)) - mean) * rstd;
@@ -188,18 +207,16 @@ __global__ void __launch_bounds__(256) gn_bwd_apply_kernel(
   }
 }
 
-// dgamma[c] = sum_n S2[n,c], dbeta[c] = sum_n S1[n,c] (fixed order).
-static __global__ void gn_param_grad_kernel(const GnBwdPartial* __restrict__ part, int part_tiles, int N,
-                                     int C, float* __restrict__ dgamma, float* __restrict__ dbeta) {
+// dgamma[c] = sum_n S2[n,c], dbeta[c] = sum_n S1[n,c] from the folded sums (fixed order).
+static __global__ void gn_param_grad_kernel(const GnBwdPartial* __restrict__ folded, int stride, int N, int C,
+                                            float* __restrict__ dgamma, float* __restrict__ dbeta) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   double a = 0.0, b = 0.0;
   for (int n = 0; n < N; ++n) {
-    const GnBwdPartial* p = part + ((size_t)n * C + c) * part_tiles;
-    for (int t = 0; t < part_tiles; ++t) {
-      a += p[t].s1;
-      b += p[t].s2;
-    }
+    const GnBwdPartial f = folded[((size_t)n * C + c) * stride];
+    a += f.s1;
+    b += f.s2;
   }
   if (dbeta != nullptr) dbeta[c] = (float)a;
   if (dgamma != nullptr) dgamma[c] = (float)b;

@@ -28,7 +28,7 @@ int launch_gather(const void* big, const void* w, const void* b, void* small, co
 }
 template <typename T, int K>
 int launch_scatter(const void* small, const void* w, const void* b, void* big, const DwS2Geom& g, cudaStream_t s) {
-  const size_t total = (size_t)g.N * g.C * g.Db * g.Hb * g.Wb;
+  const size_t total = (size_t)g.N * g.C * (size_t)g.bp;
   dw_s2_scatter_kernel<T, K><<<grid_1d(total, 256), 256, 0, s>>>(
       static_cast<const T*>(small), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(big), g);
   return record_launch();
@@ -47,7 +47,8 @@ int launch_s2_wgrad(const void* big, const void* small, void* dw, void* db, void
   if (st != MEDNEXT_OK) return st;
   if (bias_from_big && db != nullptr) {
     const size_t bvol = (size_t)g.Db * g.Hb * g.Wb;
-    chan_sum_into_partials_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(big), part, bvol, p.chunks, K * K * K);
+    chan_sum_into_partials_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(big), part, bvol, (size_t)g.bp, p.chunks,
+                                                          K * K * K);
     st = record_launch();
     if (st != MEDNEXT_OK) return st;
   }

@@ -30,11 +30,13 @@ int dispatch_gn_finalize(const GnPartial* part, int tiles, int nc, float eps, fl
   return record_launch();
 }
 
-int dispatch_gn_stats(int dtype, const void* x, GnPartial* part, int64_t nc, int64_t vol, int chunks, float eps,
+int dispatch_gn_stats(int dtype, const void* x, GnPartial* part, int64_t nc, int64_t vol, int64_t pitch, int chunks,
+                      float eps,
                       float* stats, cudaStream_t s) {
   int st = MEDNEXT_OK;
   MEDNEXT_T_SWITCH(dtype, T, {
     gn_stats_partial_kernel<T><<<(unsigned)(nc * chunks), 256, 0, s>>>(static_cast<const T*>(x), part, (size_t)vol,
+                                                                         (size_t)pitch,
                                                                          chunks);
     st = record_launch();
   });
@@ -68,14 +70,20 @@ int dispatch_gn_bwd_partial(int x_dtype, int dz_dtype, const void* dz, const voi
 
 int dispatch_gn_bwd_apply(int x_dtype, int dz_dtype, int g_dtype, const void* dz, const void* x, const float* stats,
                           const void* gamma, const GnBwdPartial* part, int part_tiles, void* dx, float* dgamma,
-                          float* dbeta, int N, int C, int64_t vol, cudaStream_t s) {
+                          float* dbeta, int N, int C, int64_t vol, int64_t pitch, cudaStream_t s) {
   const int64_t nc = (int64_t)N * C;
   const int chunks = gn_chunks(nc, vol);
   int st = MEDNEXT_OK;
+  if (part_tiles > 1) {
+    // fold in place; the workspace belongs to this call sequence
+    gn_fold_partials_kernel<<<(unsigned)nc, 256, 0, s>>>(const_cast<GnBwdPartial*>(part), part_tiles);
+    st = record_launch();
+    if (st != MEDNEXT_OK) return st;
+  }
   MEDNEXT_GN_DISPATCH(x_dtype, dz_dtype, g_dtype, TX, TD, TG, {
     gn_bwd_apply_kernel<TD, TX, TX, TG><<<(unsigned)(nc * chunks), 256, 0, s>>>(
         static_cast<const TD*>(dz), static_cast<const TX*>(x), stats, static_cast<const TG*>(gamma), part, part_tiles,
-        static_cast<TX*>(dx), C, (size_t)vol, chunks);
+        static_cast<TX*>(dx), C, (size_t)vol, (size_t)pitch, chunks);
     st = record_launch();
   });
   if (st != MEDNEXT_OK) return st;

@@ -102,13 +102,17 @@ inline DwS2Geom s2_geom_down(int64_t n, int64_t c, int64_t d, int64_t h, int64_t
   g.N = (int)n; g.C = (int)c;
   g.Db = (int)d; g.Hb = (int)h; g.Wb = (int)w;
   g.Ds = (int)((d + 1) / 2); g.Hs = (int)((h + 1) / 2); g.Ws = (int)((w + 1) / 2);
+  g.bp = (long long)d * h * w;
   return g;
 }
-inline DwS2Geom s2_geom_up(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w) {
+// pitch: elements between (n, c) volumes of the (2d-1, 2h-1, 2w-1) grid; 0 = contiguous
+inline DwS2Geom s2_geom_up(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t pitch) {
   DwS2Geom g{};
   g.N = (int)n; g.C = (int)c;
   g.Ds = (int)d; g.Hs = (int)h; g.Ws = (int)w;
   g.Db = (int)(2 * d - 1); g.Hb = (int)(2 * h - 1); g.Wb = (int)(2 * w - 1);
+  const long long bvol = (long long)g.Db * g.Hb * g.Wb;
+  g.bp = pitch > 0 ? pitch : bvol;
   return g;
 }
 
@@ -136,7 +140,8 @@ inline PwWPlan plan_pw_wgrad(int64_t n, int64_t cin, int64_t cout, int64_t vox) 
   p.ntiles = (int)((cin + p.BN - 1) / p.BN);
   p.cps = (vox + kPwBK - 1) / kPwBK;
   p.total = p.cps * n;
-  long long splits = std::max(1LL, (long long)(148 * 2) / (p.mtiles * p.ntiles));
+  // one split-K unit per SM for the persistent kernel (148 SMs)
+  long long splits = std::max(1LL, (long long)148 / (p.mtiles * p.ntiles));
   splits = std::min(splits, 128LL);
   splits = std::min(splits, p.total);
   p.per = (p.total + splits - 1) / splits;
@@ -157,15 +162,15 @@ int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, c
 int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,
                          const DwS2Geom& g, bool bias_from_big, cudaStream_t s);
 int dispatch_gn_finalize(const GnPartial* part, int tiles, int nc, float eps, float* stats, cudaStream_t s);
-int dispatch_gn_stats(int dtype, const void* x, GnPartial* part, int64_t nc, int64_t vol, int chunks, float eps,
-                      float* stats, cudaStream_t s);
+int dispatch_gn_stats(int dtype, const void* x, GnPartial* part, int64_t nc, int64_t vol, int64_t pitch, int chunks,
+                      float eps, float* stats, cudaStream_t s);
 int dispatch_gn_fwd(int x_dtype, int y_dtype, int g_dtype, const void* x, const float* stats, const void* gamma,
                     const void* beta, void* y, int C, int64_t nc, int64_t vol, cudaStream_t s);
 int dispatch_gn_bwd_partial(int x_dtype, int dz_dtype, const void* dz, const void* x, const float* stats,
                             GnBwdPartial* part, int64_t nc, int64_t vol, int chunks, cudaStream_t s);
 int dispatch_gn_bwd_apply(int x_dtype, int dz_dtype, int g_dtype, const void* dz, const void* x, const float* stats,
                           const void* gamma, const GnBwdPartial* part, int part_tiles, void* dx, float* dgamma,
-                          float* dbeta, int N, int C, int64_t vol, cudaStream_t s);
+                          float* dbeta, int N, int C, int64_t vol, int64_t pitch, cudaStream_t s);
 int dispatch_pw_fwd(int a_dtype, int y_dtype, int prologue, const PwFwdArgs& a, cudaStream_t s);
 int dispatch_pw_wgrad(int dtype, int prologue, const PwWgradArgs& a, int splits, cudaStream_t s);
 

@@ -93,7 +93,6 @@ __global__ void __launch_bounds__(kPwThreads) pw_fwd_kernel(PwFwdArgs p) {
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
   __shared__ float coef[kPwBK][2];
-  __shared__ float red[4][2][32];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -280,22 +279,15 @@ __global__ void __launch_bounds__(kPwThreads) pw_fwd_kernel(PwFwdArgs p) {
         }
       }
       if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
-        // lane jj holds the warp's sums for channel c0+jj; fold the 4 warps in order
-        red[warp][0][lane] = gs1;
-        red[warp][1][lane] = gs2;
-        __syncthreads();
-        if (warp == 0) {
-          const int j = j0 + c0 + lane;
-          if (j < p.cout) {
-            const double a = (double)red[0][0][lane] + red[1][0][lane] + red[2][0][lane] + red[3][0][lane];
-            const double bb = (double)red[0][1][lane] + red[1][1][lane] + red[2][1][lane] + red[3][1][lane];
-            GnBwdPartial gp;
-            gp.s1 = a;
-            gp.s2 = bb;
-            p.gn_part[((size_t)s * p.cout + j) * p.mtiles + mt] = gp;
-          }
+        // lane jj holds the warp's sums for channel c0+jj: one partial per
+        // (channel, tile, 32-voxel quarter), folded later in a fixed order
+        const int j = j0 + c0 + lane;
+        if (j < p.cout && c0 + lane < BN) {
+          GnBwdPartial gp;
+          gp.s1 = (double)gs1;
+          gp.s2 = (double)gs2;
+          p.gn_part[(((size_t)s * p.cout + j) * p.mtiles + mt) * 4 + warp] = gp;
         }
-        __syncthreads();
       }
     }
   }

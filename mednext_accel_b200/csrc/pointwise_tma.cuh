@@ -1,0 +1,575 @@
+// Persistent, warp-specialized tcgen05 pointwise GEMMs fed by TMA.
+//
+// Forward / input-grad (voxel-M): y[s, j, v] = epi( sum_k W[j, k] * pro(a[s, k, v]) )
+//   warp 0      TMA producer: per (tile, k-stage) one 64x64 box per 64 voxels of A
+//               (MN-major, 128B swizzle) and one 64xBN box of W (K-major, 128B
+//               swizzle) into an S-stage ring; per tile the epilogue operands
+//               (aux / residual tiles, no swizzle) into an E-stage ring.
+//   warp 1      TMEM owner and MMA issuer (one lane): tcgen05.mma M=128 N=BN K=16,
+//               accumulators double-buffered in TMEM so the epilogue of tile i
+//               overlaps the MMAs of tile i+1.
+//   warps 4-7   prologue: GroupNorm apply or GELU on the staged A tile, in place,
+//               then release it to the MMA (only when a prologue is requested).
+//   warps 8-11  epilogue: tcgen05.ld of the accumulator, bias / GELU' / residual /
+//               GroupNorm-backward sums, bf16 stores.
+// Weight grad (voxel-K): same roles; the reduction runs over 64-voxel chunks of
+// a split-K range, the prologue warps also accumulate the bias grad rows.
+//
+// All waits are bounded (common.cuh); a timed-out wait raises the device error
+// word, sets the CTA abort flag and every role drains out.
+#pragma once
+
+#include <cuda.h>
+
+#include "pointwise.cuh"
+
+namespace mednext {
+
+// ------------------------------------------------------------------ TMA PTX
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+constexpr int kTmaThreads = 384;  // weight-grad kernel: producer, MMA, 4 prologue, 4 epilogue warps
+// forward kernel: warp 0 producer, warp 1 MMA, warps 4-11 prologue, warps 12-19 epilogue
+constexpr int kFwdProWarp0 = 4;
+constexpr int kFwdEpiWarp0 = 12;
+constexpr int kFwdThreads = 640;
+constexpr int kFwdProThreads = 256;
+constexpr int kFwdEpiThreads = 256;
+constexpr int kMaxStages = 8;
+constexpr int kMaxEStages = 2;
+
+struct PwTmaCfg {
+  int stages;       // A/B ring depth
+  int estages;      // aux/residual ring depth
+  int kstages;      // K stages per tile (forward) = ceil(cin / 64)
+  int total_tiles;  // forward: S * ntiles * mtiles; wgrad: work units
+  int aux_bytes;    // bytes of one aux tile (0 if unused)
+  int res_bytes;    // bytes of one residual tile (0 if unused)
+  int b_bytes;      // bytes of one W stage (BN * 128)
+};
+
+struct PwTmaSmem {
+  uint64_t full[kMaxStages];
+  uint64_t ready[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t efull[kMaxEStages];
+  uint64_t eempty[kMaxEStages];
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (*abort) return false;
+  if (!mbar_wait(bar, parity)) {
+    *abort = 1;
+    return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint32_t tmem_cols_for(int bn) {
+  return bn <= 32 ? 32u : (bn <= 64 ? 64u : (bn <= 128 ? 128u : 256u));
+}
+
+// ---------------------------------------------------------------- forward / dgrad
+template <typename TA, typename TY, int PRO>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    pw_tma_fwd_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB,
+                      const __grid_constant__ CUtensorMap mAux, const __grid_constant__ CUtensorMap mRes,
+                      const __grid_constant__ CUtensorMap mY, PwFwdArgs p, PwTmaCfg cfg) {
+  extern __shared__ uint8_t smem_dyn[];
+  __shared__ PwTmaSmem sh;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int BN = p.BN;
+  const int S = cfg.stages, E = cfg.estages, KS = cfg.kstages;
+  const bool has_aux = cfg.aux_bytes > 0, has_res = cfg.res_bytes > 0;
+
+  const uint32_t base_u32 = smem_u32(smem_dyn);
+  uint8_t* sbase = smem_dyn + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* ringA = sbase;                                 // S x 16 KB
+  uint8_t* ringB = ringA + (size_t)S * 16384;             // S x b_bytes
+  uint8_t* ringAux = ringB + (size_t)S * cfg.b_bytes;     // E x aux_bytes
+  uint8_t* ringRes = ringAux + (size_t)E * cfg.aux_bytes; // E x res_bytes
+  uint8_t* ringStg = ringRes + (size_t)E * cfg.res_bytes;  // 8 warps x 2 x 32x32 TY
+  constexpr int kStgBytes = 32 * 32 * (int)sizeof(TY);
+
+  const uint32_t ncols = tmem_cols_for(BN);
+  if (warp == 1) {
+    tmem_alloc(&sh.tmem_base, 2 * ncols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&sh.full[i], 1);
+      mbar_init(&sh.ready[i], kFwdProThreads);
+      mbar_init(&sh.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sh.tfull[i], 1);
+      mbar_init(&sh.tempty[i], kFwdEpiThreads);
+    }
+    for (int i = 0; i < E; ++i) {
+      mbar_init(&sh.efull[i], 1);
+      mbar_init(&sh.eempty[i], kFwdEpiThreads);
+    }
+    sh.abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&mA);
+    tma_prefetch_map(&mB);
+    if (has_aux) tma_prefetch_map(&mAux);
+    if (has_res) tma_prefetch_map(&mRes);
+    tma_prefetch_map(&mY);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort = &sh.abort;
+  const int ntile_local = (cfg.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+
+  auto decode = [&](int t, int& s, int& j0, long long& v0, int& mt) {
+    mt = t % p.mtiles;
+    const int rest = t / p.mtiles;
+    j0 = (rest % p.ntiles) * BN;
+    s = rest / p.ntiles;
+    v0 = (long long)mt * kPwBM;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      for (int i = 0; i < ntile_local && !*abort; ++i) {
+        int s, j0, mt;
+        long long v0;
+        decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
+        if (has_aux || has_res) {
+          const int e = i % E, re = i / E;
+          if (re > 0 && !wait_or_abort(&sh.eempty[e], (re - 1) & 1, abort)) break;
+          mbar_arrive_expect_tx(&sh.efull[e], (uint32_t)(cfg.aux_bytes + cfg.res_bytes));
+          if (has_aux) {
+            uint8_t* d = ringAux + (size_t)e * cfg.aux_bytes;
+            tma_load_3d(d, &mAux, &sh.efull[e], (int)v0, j0, s);
+            tma_load_3d(d + cfg.aux_bytes / 2, &mAux, &sh.efull[e], (int)v0 + 64, j0, s);
+          }
+          if (has_res) {
+            uint8_t* d = ringRes + (size_t)e * cfg.res_bytes;
+            tma_load_3d(d, &mRes, &sh.efull[e], (int)v0, j0, s);
+            tma_load_3d(d + cfg.res_bytes / 2, &mRes, &sh.efull[e], (int)v0 + 64, j0, s);
+          }
+        }
+        for (int kk = 0; kk < KS; ++kk) {
+          const int q = i * KS + kk;
+          const int st = q % S, r = q / S;
+          if (r > 0 && !wait_or_abort(&sh.empty[st], (r - 1) & 1, abort)) break;
+          mbar_arrive_expect_tx(&sh.full[st], (uint32_t)(16384 + cfg.b_bytes));
+          uint8_t* a = ringA + (size_t)st * 16384;
+          tma_load_3d(a, &mA, &sh.full[st], (int)v0, kk * kPwBK, s);
+          tma_load_3d(a + 8192, &mA, &sh.full[st], (int)v0 + 64, kk * kPwBK, s);
+          tma_load_2d(ringB + (size_t)st * cfg.b_bytes, &mB, &sh.full[st], kk * kPwBK, j0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(kPwBM, BN, std::is_same<TA, __nv_bfloat16>::value, true, false);
+      for (int i = 0; i < ntile_local && !*abort; ++i) {
+        const int acc = i & 1, ra = i >> 1;
+        if (ra > 0 && !wait_or_abort(&sh.tempty[acc], (ra - 1) & 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)acc * ncols;
+        for (int kk = 0; kk < KS; ++kk) {
+          const int q = i * KS + kk;
+          const int st = q % S, r = q / S;
+          uint64_t* bar = PRO != MEDNEXT_PRO_NONE ? &sh.ready[st] : &sh.full[st];
+          if (!wait_or_abort(bar, r & 1, abort)) break;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ringA + (size_t)st * 16384);
+          const uint32_t b_addr = smem_u32(ringB + (size_t)st * cfg.b_bytes);
+          const int ksteps = min(kPwBK, p.cin - kk * kPwBK + 15) / 16;
+          for (int ks = 0; ks < ksteps; ++ks) {
+            const uint64_t ad = make_sw128_desc(a_addr + ks * 2048, 8192, 1024);
+            const uint64_t bd = make_sw128_desc(b_addr + ks * 32, 16, 1024);
+            mma_f16_ss(d_tmem, ad, bd, idesc, (kk > 0 || ks > 0) ? 1u : 0u);
+          }
+          mma_commit(&sh.empty[st]);
+        }
+        mma_commit(&sh.tfull[acc]);
+      }
+    }
+  } else if (warp >= kFwdProWarp0 && warp < kFwdEpiWarp0) {
+    // ------------------------------------------------ prologue transform (in place)
+    if constexpr (PRO != MEDNEXT_PRO_NONE) {
+      const int t = tid - kFwdProWarp0 * 32;  // 0..255
+      const int mch = t & 15;                 // 16 chunks of 8 voxels (two 64-voxel boxes)
+      const int kr = t >> 4;                  // rows kr, kr+16, kr+32, kr+48 (same swizzle row)
+      for (int i = 0; i < ntile_local && !*abort; ++i) {
+        int s, j0, mt;
+        long long v0;
+        decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
+        for (int kk = 0; kk < KS; ++kk) {
+          const int q = i * KS + kk;
+          const int st = q % S, r = q / S;
+          if (!wait_or_abort(&sh.full[st], r & 1, abort)) break;
+          uint8_t* a = ringA + (size_t)st * 16384 + (mch >> 3) * 8192;
+#pragma unroll
+          for (int ii = 0; ii < 4; ++ii) {
+            const int kl = kr + 16 * ii;
+            const int k = kk * kPwBK + kl;
+            uint4* chunk = reinterpret_cast<uint4*>(a + kl * 128 + ((((mch & 7) ^ (kl & 7))) << 4));
+            float v[8];
+            unpack16<TA>(*chunk, v);
+            if constexpr (PRO == MEDNEXT_PRO_GROUPNORM) {
+              float ca = 0.f, cb = 0.f;
+              if (k < p.cin) {
+                const float mean = __ldg(p.pro_stats + 2 * (s * p.cin + k));
+                const float rstd = __ldg(p.pro_stats + 2 * (s * p.cin + k) + 1);
+                ca = rstd * __ldg(p.pro_gamma + k);
+                cb = __ldg(p.pro_beta + k) - mean * ca;
+              }
+              pw_prologue<PRO>(v, ca, cb);
+            } else {
+              pw_prologue<PRO>(v, 0.f, 0.f);
+            }
+            *chunk = pack16<TA>(v);
+          }
+          fence_async_smem();
+          mbar_arrive(&sh.ready[st]);
+        }
+      }
+    }
+  } else if (warp >= kFwdEpiWarp0) {
+    // ------------------------------------------------ epilogue
+    // 8 warps: warp%4 selects the TMEM lane quarter (32 voxels), warp/4 the
+    // column half; every 32x32 result block is staged in shared memory and
+    // written with one TMA bulk tensor store (out-of-range rows are clipped).
+    const int ew = warp - kFwdEpiWarp0;
+    const int q4 = warp & 3;
+    const int half = ew >> 2;
+    const int epi = p.epilogue;
+    uint8_t* stg0 = ringStg + (size_t)ew * 2 * kStgBytes;
+    uint32_t nstored = 0;
+    for (int i = 0; i < ntile_local && !*abort; ++i) {
+      int s, j0, mt;
+      long long v0;
+      decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
+      const int acc = i & 1, ra = i >> 1;
+      if (!wait_or_abort(&sh.tfull[acc], ra & 1, abort)) break;
+      tc_fence_after();
+      const int e = i % E, re = i / E;
+      if ((has_aux || has_res) && !wait_or_abort(&sh.efull[e], re & 1, abort)) break;
+      const int vl = q4 * 32 + lane;  // voxel within the tile
+      const uint8_t* auxt = ringAux + (size_t)e * cfg.aux_bytes + (vl >> 6) * (cfg.aux_bytes / 2);
+      const uint8_t* rest = ringRes + (size_t)e * cfg.res_bytes + (vl >> 6) * (cfg.res_bytes / 2);
+      const uint32_t d_tmem = tmem + (uint32_t)acc * ncols + ((uint32_t)(q4 * 32) << 16);
+      for (int c0 = 32 * half; c0 < BN; c0 += 64) {
+        uint32_t r[32];
+        tmem_ld32(d_tmem + (uint32_t)c0, r);
+        // per-column constants, one per lane, broadcast with shuffles
+        const int jc = j0 + c0 + lane;
+        const bool jok = jc < p.cout;
+        const float bias_l = ((epi & MEDNEXT_EPI_BIAS) && jok) ? __ldg(p.bias + jc) : 0.f;
+        float mean_l = 0.f, rstd_l = 0.f;
+        if ((epi & MEDNEXT_EPI_GN_BWD_STATS) && jok) {
+          mean_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc));
+          rstd_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc) + 1);
+        }
+        // staging buffer: wait until the store issued two blocks ago has read it
+        TY* stg = reinterpret_cast<TY*>(stg0 + (nstored & 1) * kStgBytes);
+        if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+        tmem_ld_wait();
+        float gs1 = 0.f, gs2 = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int jl = c0 + jj;
+          float a = __uint_as_float(r[jj]);
+          if (epi & MEDNEXT_EPI_BIAS) a += __shfl_sync(0xffffffffu, bias_l, jj);
+          if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_RESIDUAL)) a = to_acc<TA>(from_acc<TA>(a));
+          if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) {
+            const float ax = to_acc<TA>(reinterpret_cast<const TA*>(auxt + jl * 128)[vl & 63]);
+            if (epi & MEDNEXT_EPI_GELU_GRAD) a *= gelu_grad_f(ax);
+            if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
+              // out-of-range voxels / channels hold exact zeros (zero-filled operands)
+              const float d = (float)to_acc<TY>(from_acc<TY>((typename Elem<TY>::Acc)a));
+              const float mean = __shfl_sync(0xffffffffu, mean_l, jj);
+              const float rstd = __shfl_sync(0xffffffffu, rstd_l, jj);
+              float s1 = d, s2 = d * ((ax - mean) * rstd);
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) {
+                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+                s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+              }
+              if (lane == jj) {
+                gs1 = s1;
+                gs2 = s2;
+              }
+            }
+          }
+          if (epi & MEDNEXT_EPI_RESIDUAL) {
+            a += (float)to_acc<TY>(reinterpret_cast<const TY*>(rest + jl * 64 * sizeof(TY))[vl & 63]);
+          }
+          stg[jj * 32 + lane] = from_acc<TY>((typename Elem<TY>::Acc)a);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&mY, stg, (int)v0 + q4 * 32, j0 + c0, s);
+          bulk_commit();
+        }
+        ++nstored;
+        if ((epi & MEDNEXT_EPI_GN_BWD_STATS) && jok && c0 + lane < BN) {
+          // one partial per (channel, tile, 32-voxel quarter): no cross-warp sync
+          GnBwdPartial gp;
+          gp.s1 = (double)gs1;
+          gp.s2 = (double)gs2;
+          p.gn_part[(((size_t)s * p.cout + jc) * p.mtiles + mt) * 4 + q4] = gp;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sh.tempty[acc]);
+      if (has_aux || has_res) mbar_arrive(&sh.eempty[e]);
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 2 * ncols);
+}
+
+// ---------------------------------------------------------------- weight grad
+struct PwTmaWgradCfg {
+  int stages;
+  int b_bytes;
+  int units;  // mtiles * ntiles * splits
+};
+
+template <typename TA, int PRO>
+__global__ void __launch_bounds__(kTmaThreads, 1)
+    pw_tma_wgrad_kernel(const __grid_constant__ CUtensorMap mG, const __grid_constant__ CUtensorMap mA,
+                        PwWgradArgs p, PwTmaWgradCfg cfg) {
+  extern __shared__ uint8_t smem_dyn[];
+  __shared__ PwTmaSmem sh;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int BN = p.BN;
+  const int S = cfg.stages;
+  const uint32_t base_u32 = smem_u32(smem_dyn);
+  uint8_t* sbase = smem_dyn + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  uint8_t* ringA = sbase;                      // S x 16 KB  (g rows)
+  uint8_t* ringB = ringA + (size_t)S * 16384;  // S x b_bytes (a rows)
+
+  const uint32_t ncols = tmem_cols_for(BN);
+  if (warp == 1) {
+    tmem_alloc(&sh.tmem_base, ncols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&sh.full[i], 1);
+      mbar_init(&sh.ready[i], 128);
+      mbar_init(&sh.empty[i], 1);
+    }
+    mbar_init(&sh.tfull[0], 1);
+    mbar_init(&sh.tempty[0], 128);
+    sh.abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&mG);
+    tma_prefetch_map(&mA);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* abort = &sh.abort;
+  const int nunits = (cfg.units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+
+  auto unit_range = [&](int u, int& mt, int& nt, int& sp, long long& cb, long long& ce) {
+    mt = u % p.mtiles;
+    const int rest = u / p.mtiles;
+    nt = rest % p.ntiles;
+    sp = rest / p.ntiles;
+    cb = (long long)sp * p.chunks_per_split;
+    ce = min(cb + p.chunks_per_split, p.chunks_total);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      long long q = 0;
+      for (int i = 0; i < nunits && !*abort; ++i) {
+        int mt, nt, sp;
+        long long cb, ce;
+        unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
+        for (long long ch = cb; ch < ce; ++ch, ++q) {
+          const int st = (int)(q % S);
+          const long long r = q / S;
+          if (r > 0 && !wait_or_abort(&sh.empty[st], (uint32_t)((r - 1) & 1), abort)) break;
+          const int s = (int)(ch / p.chunks_per_sample);
+          const int v = (int)((ch - (long long)s * p.chunks_per_sample) * kPwBK);
+          mbar_arrive_expect_tx(&sh.full[st], (uint32_t)(16384 + cfg.b_bytes));
+          tma_load_3d(ringA + (size_t)st * 16384, &mG, &sh.full[st], v, mt * kPwBM, s);
+          tma_load_3d(ringB + (size_t)st * cfg.b_bytes, &mA, &sh.full[st], v, nt * BN, s);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(kPwBM, BN, std::is_same<TA, __nv_bfloat16>::value, false, false);
+      long long q = 0;
+      for (int i = 0; i < nunits && !*abort; ++i) {
+        int mt, nt, sp;
+        long long cb, ce;
+        unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
+        if (i > 0 && !wait_or_abort(&sh.tempty[0], (uint32_t)((i - 1) & 1), abort)) break;
+        tc_fence_after();
+        bool first = true;
+        for (long long ch = cb; ch < ce; ++ch, ++q) {
+          const int st = (int)(q % S);
+          const long long r = q / S;
+          if (!wait_or_abort(&sh.ready[st], (uint32_t)(r & 1), abort)) break;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ringA + (size_t)st * 16384);
+          const uint32_t b_addr = smem_u32(ringB + (size_t)st * cfg.b_bytes);
+#pragma unroll
+          for (int ks = 0; ks < kPwBK / 16; ++ks) {
+            const uint64_t ad = make_sw128_desc(a_addr + ks * 32, 16, 1024);
+            const uint64_t bd = make_sw128_desc(b_addr + ks * 32, 16, 1024);
+            mma_f16_ss(tmem, ad, bd, idesc, first ? 0u : 1u);
+            first = false;
+          }
+          mma_commit(&sh.empty[st]);
+        }
+        mma_commit(&sh.tfull[0]);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // prologue on the a rows (in place) and bias-grad row sums of the g rows
+    const int t = tid - 128;
+    long long q = 0;
+    for (int i = 0; i < nunits && !*abort; ++i) {
+      int mt, nt, sp;
+      long long cb, ce;
+      unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
+      float bsum = 0.f;  // row t of g (output channel mt*128 + t)
+      for (long long ch = cb; ch < ce; ++ch, ++q) {
+        const int st = (int)(q % S);
+        const long long r = q / S;
+        if (!wait_or_abort(&sh.full[st], (uint32_t)(r & 1), abort)) break;
+        const int s = (int)(ch / p.chunks_per_sample);
+        if (nt == 0) {
+          const uint8_t* row = ringA + (size_t)st * 16384 + (t >> 3) * 1024 + (t & 7) * 128;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float v[8];
+            unpack16<TA>(*reinterpret_cast<const uint4*>(row + c * 16), v);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) bsum += v[e];
+          }
+        }
+        if constexpr (PRO != MEDNEXT_PRO_NONE) {
+          // BN rows x 8 chunks; thread handles rows n = t/8 + 16*ii, chunk t%8
+          const int cq = t & 7;
+          for (int n = t >> 3; n < BN; n += 16) {
+            const int k = nt * BN + n;
+            uint4* chunk = reinterpret_cast<uint4*>(ringB + (size_t)st * cfg.b_bytes + sw128_kmajor_off(n, cq));
+            float v[8];
+            unpack16<TA>(*chunk, v);
+            if constexpr (PRO == MEDNEXT_PRO_GROUPNORM) {
+              float ca = 0.f, cbb = 0.f;
+              if (k < p.cin) {
+                const float mean = __ldg(p.pro_stats + 2 * (s * p.cin + k));
+                const float rstd = __ldg(p.pro_stats + 2 * (s * p.cin + k) + 1);
+                ca = rstd * __ldg(p.pro_gamma + k);
+                cbb = __ldg(p.pro_beta + k) - mean * ca;
+              }
+              pw_prologue<PRO>(v, ca, cbb);
+            } else {
+              pw_prologue<PRO>(v, 0.f, 0.f);
+            }
+            *chunk = pack16<TA>(v);
+          }
+          fence_async_smem();
+        }
+        mbar_arrive(&sh.ready[st]);
+      }
+      if (nt == 0) {
+        const int j = mt * kPwBM + t;
+        if (j < p.cout) p.part_b[(size_t)sp * p.cout + j] = bsum;
+      }
+    }
+  } else if (warp >= 8) {
+    const int q4 = warp & 3;
+    for (int i = 0; i < nunits && !*abort; ++i) {
+      int mt, nt, sp;
+      long long cb, ce;
+      unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
+      const bool any = ce > cb;
+      // the MMA warp commits tfull once per unit, with or without MMAs
+      if (!wait_or_abort(&sh.tfull[0], (uint32_t)(i & 1), abort)) break;
+      tc_fence_after();
+      const int j = mt * kPwBM + q4 * 32 + lane;
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        if (any) {
+          tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = 0u;
+        }
+        if (j < p.cout) {
+          float* dst = p.part + ((size_t)sp * p.cout + j) * p.cin;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int k = nt * BN + c0 + e;
+            if (c0 + e < BN && k < p.cin) dst[k] = __uint_as_float(r[e]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sh.tempty[0]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, ncols);
+}
+
+}  // namespace mednext

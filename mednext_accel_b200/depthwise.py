@@ -142,13 +142,18 @@ def s2_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True) 
     return dw, db
 
 
-def t_forward(x: Tensor, weight: Tensor, bias: Tensor | None, kernel_size: int) -> Tensor:
+def t_forward(x: Tensor, weight: Tensor, bias: Tensor | None, kernel_size: int, pitch: int = 0) -> Tensor:
+    """Transposed stride-2 forward.  With ``pitch`` > 0 the result is returned as an
+    [n, c, pitch] buffer whose rows hold the (2d-1)(2h-1)(2w-1) voxels followed by a
+    zero tail (see :func:`pitched_view`)."""
     nat.require_device(x)
     n, c, d, h, w = _dims(x)
-    y = torch.empty((n, c, 2 * d - 1, 2 * h - 1, 2 * w - 1), dtype=x.dtype, device=x.device)
+    big = (2 * d - 1, 2 * h - 1, 2 * w - 1)
+    shape = (n, c, pitch) if pitch else (n, c, *big)
+    y = torch.empty(shape, dtype=x.dtype, device=x.device)
     nat.check(
         nat.load().mednext_dwT_fwd(
-            x.data_ptr(), weight.data_ptr(), nat.ptr(bias), y.data_ptr(), n, c, d, h, w, kernel_size,
+            x.data_ptr(), weight.data_ptr(), nat.ptr(bias), y.data_ptr(), n, c, d, h, w, pitch, kernel_size,
             nat.dtype_code(x.dtype), nat.stream(),
         ),
         "mednext_dwT_fwd",
@@ -156,14 +161,28 @@ def t_forward(x: Tensor, weight: Tensor, bias: Tensor | None, kernel_size: int) 
     return y
 
 
-def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int) -> Tensor:
+def pitched_view(buf: Tensor, spatial: tuple[int, int, int]) -> Tensor:
+    """The [n, c, *spatial] view of the valid voxels of an [n, c, pitch] buffer."""
+    vox = spatial[0] * spatial[1] * spatial[2]
+    return buf[:, :, :vox].unflatten(2, spatial)
+
+
+def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int, small: tuple[int, int, int] | None = None) -> Tensor:
+    """Input grad of the transposed conv.  ``grad`` is [n, c, 2d-1, 2h-1, 2w-1], or a
+    pitched [n, c, pitch] buffer when ``small`` = (d, h, w) is given."""
     nat.require_device(grad)
-    n, c, od, oh, ow = _dims(grad)
-    d, h, w = (od + 1) // 2, (oh + 1) // 2, (ow + 1) // 2
+    n, c = int(grad.shape[0]), int(grad.shape[1])
+    pitch = 0
+    if small is not None:
+        d, h, w = small
+        pitch = int(grad.shape[2])
+    else:
+        _, _, od, oh, ow = _dims(grad)
+        d, h, w = (od + 1) // 2, (oh + 1) // 2, (ow + 1) // 2
     out = torch.empty((n, c, d, h, w), dtype=grad.dtype, device=grad.device)
     nat.check(
         nat.load().mednext_dwT_dgrad(
-            grad.data_ptr(), weight.data_ptr(), out.data_ptr(), n, c, d, h, w, kernel_size,
+            grad.data_ptr(), weight.data_ptr(), out.data_ptr(), n, c, d, h, w, pitch, kernel_size,
             nat.dtype_code(grad.dtype), nat.stream(),
         ),
         "mednext_dwT_dgrad",
@@ -172,9 +191,12 @@ def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int) -> Tensor:
 
 
 def t_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True) -> tuple[Tensor, Tensor | None]:
+    """Weight (and bias) grad of the transposed conv; ``grad`` may be a pitched
+    [n, c, pitch] buffer (3-D) or [n, c, 2d-1, 2h-1, 2w-1]."""
     nat.require_device(x)
     lib = nat.load()
     n, c, d, h, w = _dims(x)
+    pitch = int(grad.shape[2]) if grad.ndim == 3 else 0
     code = nat.dtype_code(x.dtype)
     dw = torch.empty((c, 1, kernel_size, kernel_size, kernel_size), dtype=x.dtype, device=x.device)
     db = torch.empty((c,), dtype=x.dtype, device=x.device) if want_bias else None
@@ -182,7 +204,7 @@ def t_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True) -
     nat.check(
         lib.mednext_dwT_wgrad(
             x.data_ptr(), grad.data_ptr(), dw.data_ptr(), nat.ptr(db), ws.data_ptr(), ws.numel(),
-            n, c, d, h, w, kernel_size, code, nat.stream(),
+            n, c, d, h, w, pitch, kernel_size, code, nat.stream(),
         ),
         "mednext_dwT_wgrad",
     )

@@ -306,11 +306,12 @@ class MedNeXtUpBlock(MedNeXtBlock):
     def forward(self, x: Tensor) -> Tensor:
         skip = self.residual(x) if self.residual is not None else None
         out = self._fused_call(x, skip, False)
-        if out is None:
-            out = self._body(x)
-            if skip is not None:
-                out = out + skip
-        # pad(a) + pad(b) == pad(a + b): one pad after the fused residual add
+        if out is not None:
+            return out  # the fused operator returns the padded output
+        out = self._body(x)
+        if skip is not None:
+            out = out + skip
+        # pad(a) + pad(b) == pad(a + b): one pad after the residual add
         return F.pad(out, self._pad)
 
 

@@ -109,16 +109,19 @@ def pw_wgrad(
     return dw, db
 
 
-def gn_stats(x: Tensor, eps: float) -> Tensor:
+def gn_stats(x: Tensor, eps: float, vox: int | None = None) -> Tensor:
+    """Per-(n, c) mean / rstd.  ``vox``: number of valid voxels when ``x`` is a pitched
+    [n, c, pitch] buffer (only the first ``vox`` of each row are statistics)."""
     nat.require_device(x)
     lib = nat.load()
     n, c = int(x.shape[0]), int(x.shape[1])
-    vox = _vox(x)
+    rows = _vox(x)
+    vox = rows if vox is None else int(vox)
     stats = torch.empty((n * c, 2), dtype=torch.float32, device=x.device)
     ws = nat.workspace(lib.mednext_gn_stats_workspace_size(n, c, vox), x.device)
     nat.check(
         lib.mednext_gn_stats(
-            x.data_ptr(), stats.data_ptr(), ws.data_ptr(), ws.numel(), n, c, vox, float(eps),
+            x.data_ptr(), stats.data_ptr(), ws.data_ptr(), ws.numel(), n, c, vox, rows, float(eps),
             nat.dtype_code(x.dtype), nat.stream(),
         ),
         "mednext_gn_stats",
@@ -165,16 +168,20 @@ def gn_backward(
 
 
 def gn_backward_from_partials(
-    dz: Tensor, x: Tensor, stats: Tensor, gamma: Tensor, partials: Tensor
+    dz: Tensor, x: Tensor, stats: Tensor, gamma: Tensor, partials: Tensor, vox: int | None = None
 ) -> tuple[Tensor, Tensor, Tensor]:
+    """GroupNorm backward from the GEMM-epilogue partials (consumed in place).
+    ``vox``: valid voxels per row when ``x``/``dz`` are pitched [n, c, pitch] buffers."""
     n, c = int(x.shape[0]), int(x.shape[1])
+    rows = _vox(x)
+    vox = rows if vox is None else int(vox)
     dx = torch.empty_like(x)
     dg = torch.empty((c,), dtype=torch.float32, device=x.device)
     db = torch.empty((c,), dtype=torch.float32, device=x.device)
     nat.check(
         nat.load().mednext_gn_bwd_from_partials(
             dz.data_ptr(), x.data_ptr(), stats.data_ptr(), gamma.data_ptr(), dx.data_ptr(), dg.data_ptr(),
-            db.data_ptr(), partials.data_ptr(), n, c, _vox(x), nat.dtype_code(dz.dtype), nat.dtype_code(x.dtype),
+            db.data_ptr(), partials.data_ptr(), n, c, vox, rows, nat.dtype_code(dz.dtype), nat.dtype_code(x.dtype),
             nat.dtype_code(x.dtype), nat.dtype_code(gamma.dtype), nat.stream(),
         ),
         "mednext_gn_bwd_from_partials",

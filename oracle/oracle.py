@@ -316,6 +316,10 @@ def block_reference(x, dy, p: BlockParams, kind: str = "regular", addend=None, r
     if residual_is_input:
         dx = dx + dy
     grads = {
+        # GroupNorm(C, C) follows the depthwise conv, so sum(dt) per channel is
+        # analytically zero and its bias grad is pure rounding noise; this is
+        # the scale to judge that noise against.
+        "depthwise.bias_scale": np.abs(dt).sum(axis=(0, 2, 3, 4)),
         "dx": dx,
         "depthwise.weight": dwdw, "depthwise.bias": dbdw,
         "norm.weight": dgamma, "norm.bias": dbeta,

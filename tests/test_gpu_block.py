@@ -117,11 +117,14 @@ def test_fused_block_matches_oracle(kind, cin, cout, ratio, k, shape):
     assert orc.rel_l2(got_y, want_y) <= BAR, orc.rel_l2(got_y, want_y)
     if kind == "regular":
         assert orc.rel_l2(grads["dx"].double().cpu().numpy(), want["dx"]) <= BAR
-    for name in ("depthwise.weight", "depthwise.bias", "norm.weight", "norm.bias", "expand.weight", "expand.bias",
+    for name in ("depthwise.weight", "norm.weight", "norm.bias", "expand.weight", "expand.bias",
                  "project.weight", "project.bias"):
         got = grads[name].double().cpu().numpy()
         err = orc.rel_l2(got, want[name])
         assert err <= BAR, f"{name}: {err:.3e}"
+    # the depthwise bias grad is sum(dt), analytically zero under GroupNorm(C, C)
+    got = grads["depthwise.bias"].double().cpu().numpy()
+    assert np.all(np.abs(got - want["depthwise.bias"]) <= BAR * want["depthwise.bias_scale"])
 
 
 def test_checkpointed_expansion_matches_stored():
@@ -156,6 +159,9 @@ def test_config2_block_full_size_against_reference_path():
     assert orc.rel_l2(y.detach().double().cpu().numpy(), yr.detach().double().cpu().numpy()) <= BAR
     names = ["dx", *[n for n, _ in block.named_parameters()]]
     for name, want in zip(names, gr, strict=True):
+        if name == "depthwise.bias":  # analytically zero under GroupNorm(C, C): rounding noise on both sides
+            assert grads[name].abs().max().item() <= 1e-2 * grads["depthwise.weight"].abs().max().item()
+            continue
         err = orc.rel_l2(grads[name].double().cpu().numpy(), want.double().cpu().numpy())
         assert err <= BAR, f"{name}: {err:.3e}"
 
@@ -188,6 +194,8 @@ def test_small_model_step_matches_native_path():
     assert abs(lf.item() - ln.item()) <= 1e-2 * abs(ln.item())
     worst = 0.0
     for (name, pf), (_, pn) in zip(fused.named_parameters(), native.named_parameters(), strict=True):
+        if name.endswith("depthwise.bias") and "residual" not in name:
+            continue  # analytically zero under GroupNorm(C, C)
         err = orc.rel_l2(pf.grad.double().cpu().numpy(), pn.grad.double().cpu().numpy())
         worst = max(worst, err)
         assert err <= 5e-2, f"{name}: {err:.3e}"

@@ -22,7 +22,7 @@ def rand(shape, seed, dtype=torch.bfloat16, scale=1.0):
 
 
 def h(t):
-    return t.double().cpu().numpy()
+    return t.detach().double().cpu().numpy()
 
 
 def assert_close_bf16(got, want, what, rel_l2=4e-3, max_rel=2e-2):

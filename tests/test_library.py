@@ -69,7 +69,7 @@ def test_argument_validation_without_gpu():
     assert lib.mednext_pw_fwd(fake, fake, fake, nat.PRO_GROUPNORM, None, None, None, 0, None, None, None, None, None, 0,
                               1, 32, 64, 4096, 1, 1, None) == nat.ERR_NULL_POINTER
     assert lib.mednext_pw_wgrad(fake, fake, fake, None, 0, None, None, None, None, 0, 1, 32, 64, 4096, 1, None) == nat.ERR_WORKSPACE
-    assert lib.mednext_gn_stats(fake, fake, None, 0, 1, 4, 512, 1e-5, 1, None) == nat.ERR_WORKSPACE
+    assert lib.mednext_gn_stats(fake, fake, None, 0, 1, 4, 512, 0, 1e-5, 1, None) == nat.ERR_WORKSPACE
     code = ctypes.c_int(0)
     assert lib.mednext_device_error(None, None) == nat.ERR_NULL_POINTER
 
@@ -86,5 +86,6 @@ def test_workspace_sizes(fn):
 def test_pointwise_workspace_sizes():
     lib = nat.load()
     assert lib.mednext_pw_fwd_workspace_size(1, 128, 32, 128**3, 0) == 0
-    assert lib.mednext_pw_fwd_workspace_size(1, 128, 32, 128**3, nat.EPI_GN_BWD_STATS) == 32 * (128**3 // 128) * 16
+    # one 16-byte partial per (channel, 128-voxel tile, 32-voxel quarter)
+    assert lib.mednext_pw_fwd_workspace_size(1, 128, 32, 128**3, nat.EPI_GN_BWD_STATS) == 32 * (128**3 // 128) * 4 * 16
     assert lib.mednext_pw_wgrad_workspace_size(1, 32, 64, 128**3) > 0
