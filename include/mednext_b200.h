@@ -65,7 +65,8 @@ enum mednext_status {
   MEDNEXT_ERR_WORKSPACE = 5,    /* workspace missing or smaller than *_workspace_size */
   MEDNEXT_ERR_ALIGNMENT = 6,    /* a pointer is not aligned to its element size */
   MEDNEXT_ERR_CUDA = 7,         /* a CUDA launch failed (see mednext_last_cuda_error) */
-  MEDNEXT_ERR_DEVICE = 8        /* current device is not sm_100 */
+  MEDNEXT_ERR_DEVICE = 8,       /* current device is not sm_100 */
+  MEDNEXT_ERR_SCRATCH_LIMIT = 9 /* shape needs more than MEDNEXT_DW_WGRAD_NOALLOC_MAX_SCRATCH */
 };
 
 /* Pointwise prologue applied to the activation operand while it is staged
@@ -117,6 +118,37 @@ size_t mednext_dw_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t 
 int mednext_dw_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
                      size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h,
                      int64_t w, int k, int dtype, mednext_stream_t stream);
+
+/* Same result as mednext_dw_wgrad, but the caller passes no workspace and the
+ * call allocates no device memory.  No reference counterpart: the reference
+ * lets torch allocate its partial-sum buffer inside the op.
+ *
+ * Who needs it: a host that cannot hand the library a workspace, e.g. a C or
+ * FFI host that takes its whole device-memory budget at start-up and has no
+ * allocator it can call per shape, or one that keeps cudaMalloc/cudaFree out
+ * of its training loop because cudaFree synchronises the whole device.
+ *
+ * The partial sums live in one array compiled into the library, one copy per
+ * device, of MEDNEXT_DW_WGRAD_NOALLOC_MAX_SCRATCH bytes (created when the
+ * library's module is loaded on that device).  A shape whose
+ * mednext_dw_wgrad_workspace_size() exceeds that returns
+ * MEDNEXT_ERR_SCRATCH_LIMIT before anything is launched; use mednext_dw_wgrad
+ * with a caller workspace for it.  16 MiB covers every MedNeXt stage up to
+ * 2 x 64 x 160^3 at k = 7 (13.4 MiB).
+ * Nothing in the array has to start at zero: each call writes every partial
+ * sum before it reads it.
+ * The first call on each device does one-time set-up with that device current
+ * (it looks up the array's device address, which loads the library's module
+ * on the device if needed); make that first call before any stream capture
+ * begins.
+ * All calls on one device share the array: two calls that can run at the same
+ * time (different streams with no ordering between them, or several host
+ * threads) race on it and produce wrong gradients.  Calls issued in order on
+ * one stream are safe. */
+#define MEDNEXT_DW_WGRAD_NOALLOC_MAX_SCRATCH ((size_t)16 << 20)
+int mednext_dw_wgrad_noalloc(const void* x, const void* dy, void* dweight, void* dbias,
+                             int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
+                             int dtype, mednext_stream_t stream);
 
 /* ---------------- depthwise Conv3d, stride 2, padding k/2 (down block) ----
  * (d, h, w) are the INPUT sizes; the output is ((d+1)/2, (h+1)/2, (w+1)/2). */

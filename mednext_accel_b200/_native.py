@@ -30,6 +30,7 @@ ERR_WORKSPACE = 5
 ERR_ALIGNMENT = 6
 ERR_CUDA = 7
 ERR_DEVICE = 8
+ERR_SCRATCH_LIMIT = 9
 
 PRO_NONE = 0
 PRO_GROUPNORM = 1
@@ -65,6 +66,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mednext_dw_dgrad": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_wgrad_workspace_size": (_SZ, _DIMS5 + [_INT, _INT]),
     "mednext_dw_wgrad": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_INT, _INT, _P]),
+    "mednext_dw_wgrad_noalloc": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_s2_fwd": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_s2_dgrad": (_INT, [_P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_s2_wgrad_workspace_size": (_SZ, _DIMS5 + [_INT, _INT]),

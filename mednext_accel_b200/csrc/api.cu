@@ -20,6 +20,7 @@ int record_launch() {
   return MEDNEXT_OK;
 }
 int last_cuda_error() { return t_last_cuda_error; }
+void note_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 }  // namespace mednext
 
@@ -80,6 +81,8 @@ const char* mednext_status_string(int status) {
     case MEDNEXT_ERR_ALIGNMENT: return "pointer not aligned to its element size";
     case MEDNEXT_ERR_CUDA: return "CUDA launch failed";
     case MEDNEXT_ERR_DEVICE: return "current device is not sm_100";
+    case MEDNEXT_ERR_SCRATCH_LIMIT:
+      return "shape needs more scratch than the built-in array of the no-allocation entry point holds";
     default: return "unknown status";
   }
 }

@@ -183,6 +183,8 @@ int read_clear_errors_pw(int* code, cudaStream_t s);
 // Records the CUDA error of the last launch in a thread-local slot.
 int record_launch();
 int last_cuda_error();
+// Records a CUDA runtime error for mednext_last_cuda_error() on this thread.
+void note_cuda_error(cudaError_t e);
 
 }  // namespace mednext
 
