@@ -96,6 +96,9 @@ int mednext_device_error(int* code, mednext_stream_t stream) {
   if (st == MEDNEXT_OK) st = read_clear_errors_dw2(code, as_stream(stream));
   if (st == MEDNEXT_OK) st = read_clear_errors_gn(code, as_stream(stream));
   if (st == MEDNEXT_OK) st = read_clear_errors_pw(code, as_stream(stream));
+  if (st == MEDNEXT_OK) st = read_clear_errors_pwf0(code, as_stream(stream));
+  if (st == MEDNEXT_OK) st = read_clear_errors_pwf1(code, as_stream(stream));
+  if (st == MEDNEXT_OK) st = read_clear_errors_pwf2(code, as_stream(stream));
   return st;
 }
 

@@ -252,6 +252,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 16 consecutive 32-bit columns, same lane mapping as tmem_ld32.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -283,15 +293,56 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool ab_bf16
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// Exact GELU, the erf form used by F.gelu(approximate="none").
-__device__ __forceinline__ float gelu_f(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f));
+// 2^x and 1/x by the PTX approximate instructions (relative error about 2^-22;
+// denormal results flush to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
-// d/dx of the exact GELU: Phi(x) + x * phi(x).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Exact (erf-form) GELU of F.gelu(approximate="none"): x * Phi(x), with
+// Phi(x) = erfc(-x / sqrt 2) / 2.  erfc(z), z >= 0, by the Chebyshev fit of
+// Numerical Recipes (Press et al., 2nd ed., sec. 6.2, "erfcc"):
+//   t = 1 / (1 + z/2),  erfc(z) = t * exp(-z^2 + P(t)),  P a degree-9 polynomial,
+// fractional error below 1.2e-7 for every z, so the negative tail keeps full
+// relative accuracy.  One exp2 and one reciprocal per element.
+__device__ __forceinline__ float gelu_f(float x) {
+  const float z = fabsf(x) * 0.70710678118654752440f;
+  const float t = rcp_approx(fmaf(0.5f, z, 1.0f));
+  float p = fmaf(t, 0.17087277f, -0.82215223f);
+  p = fmaf(t, p, 1.48851587f);
+  p = fmaf(t, p, -1.13520398f);
+  p = fmaf(t, p, 0.27886807f);
+  p = fmaf(t, p, -0.18628806f);
+  p = fmaf(t, p, 0.09678418f);
+  p = fmaf(t, p, 0.37409196f);
+  p = fmaf(t, p, 1.00002368f);
+  p = fmaf(t, p, -1.26551223f);
+  const float tail = 0.5f * t * ex2_approx(fmaf(-z, z, p) * 1.44269504088896340736f);  // Phi(-|x|)
+  return x * (x >= 0.f ? 1.0f - tail : tail);
+}
+// d/dx of the exact GELU: Phi(x) + x * phi(x).  erfc by Abramowitz & Stegun,
+// Handbook of Mathematical Functions (1964), eq. 7.1.26: for z >= 0,
+//   t = 1 / (1 + 0.3275911 z),  erfc(z) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-z^2),
+// absolute error at most 1.5e-7; exp(-z^2) = exp(-x^2 / 2) is shared with phi(x).
+// The result is within 1e-7 absolute of the exact derivative (within 3e-4
+// relative in the far negative tail, where x * phi(x) dominates).
 __device__ __forceinline__ float gelu_grad_f(float x) {
-  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752440f));
-  const float pdf = 0.39894228040143267794f * expf(-0.5f * x * x);
-  return cdf + x * pdf;
+  const float e = ex2_approx(x * x * -0.72134752044448170368f);  // exp(-x^2 / 2)
+  const float z = fabsf(x) * 0.70710678118654752440f;
+  const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
+  float p = fmaf(t, 1.061405429f, -1.453152027f);
+  p = fmaf(t, p, 1.421413741f);
+  p = fmaf(t, p, -0.284496736f);
+  p = fmaf(t, p, 0.254829592f);
+  const float tail = 0.5f * t * p * e;  // Phi(-|x|)
+  return fmaf(x, 0.39894228040143267794f * e, x >= 0.f ? 1.0f - tail : tail);
 }
 
 }  // namespace mednext

@@ -172,6 +172,10 @@ int dispatch_gn_bwd_apply(int x_dtype, int dz_dtype, int g_dtype, const void* dz
                           const void* gamma, const GnBwdPartial* part, int part_tiles, void* dx, float* dgamma,
                           float* dbeta, int N, int C, int64_t vol, int64_t pitch, cudaStream_t s);
 int dispatch_pw_fwd(int a_dtype, int y_dtype, int prologue, const PwFwdArgs& a, cudaStream_t s);
+// Per-element-type forward instantiations (pw_fwd_*.cu).
+int pw_fwd_bf16_bf16(int prologue, const PwFwdArgs& a, cudaStream_t s);
+int pw_fwd_bf16_f32(int prologue, const PwFwdArgs& a, cudaStream_t s);
+int pw_fwd_f16(int y_dtype, int prologue, const PwFwdArgs& a, cudaStream_t s);
 int dispatch_pw_wgrad(int dtype, int prologue, const PwWgradArgs& a, int splits, cudaStream_t s);
 
 // Read and clear the device error word of every translation unit.
@@ -179,6 +183,9 @@ int read_clear_errors_dw(int* code, cudaStream_t s);
 int read_clear_errors_dw2(int* code, cudaStream_t s);
 int read_clear_errors_gn(int* code, cudaStream_t s);
 int read_clear_errors_pw(int* code, cudaStream_t s);
+int read_clear_errors_pwf0(int* code, cudaStream_t s);
+int read_clear_errors_pwf1(int* code, cudaStream_t s);
+int read_clear_errors_pwf2(int* code, cudaStream_t s);
 
 // Records the CUDA error of the last launch in a thread-local slot.
 int record_launch();

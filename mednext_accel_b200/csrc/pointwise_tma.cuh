@@ -8,12 +8,16 @@
 //   warp 1      TMEM owner and MMA issuer (one lane): tcgen05.mma M=128 N=BN K=16,
 //               accumulators double-buffered in TMEM so the epilogue of tile i
 //               overlaps the MMAs of tile i+1.
-//   warps 4-7   prologue: GroupNorm apply or GELU on the staged A tile, in place,
-//               then release it to the MMA (only when a prologue is requested).
-//   warps 8-11  epilogue: tcgen05.ld of the accumulator, bias / GELU' / residual /
-//               GroupNorm-backward sums, bf16 stores.
-// Weight grad (voxel-K): same roles; the reduction runs over 64-voxel chunks of
-// a split-K range, the prologue warps also accumulate the bias grad rows.
+//   warps 4-11  prologue (only when one is requested): GroupNorm apply or GELU on
+//               the staged A tile, in place, then release it to the MMA.
+//   epilogue    warps 12-19 with a prologue, warps 4-19 without: tcgen05.ld of
+//               16-column accumulator chunks, bias / GELU' / residual / GroupNorm-
+//               backward sums, staged in shared memory and written by TMA stores.
+//               The epilogue flags are a template parameter, so the per-element
+//               loop is straight-line code.
+// Weight grad (voxel-K): producer, MMA, 4 prologue and 4 epilogue warps; the
+// reduction runs over 64-voxel chunks of a split-K range, the prologue warps also
+// accumulate the bias grad rows.
 //
 // All waits are bounded (common.cuh); a timed-out wait raises the device error
 // word, sets the CTA abort flag and every role drains out.
@@ -59,12 +63,19 @@ __device__ __forceinline__ void bulk_wait_read() {
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 constexpr int kTmaThreads = 384;  // weight-grad kernel: producer, MMA, 4 prologue, 4 epilogue warps
-// forward kernel: warp 0 producer, warp 1 MMA, warps 4-11 prologue, warps 12-19 epilogue
+// forward kernel: warp 0 producer, warp 1 MMA, warps 4-11 prologue (when requested),
+// the remaining warps up to 19 epilogue
 constexpr int kFwdProWarp0 = 4;
-constexpr int kFwdEpiWarp0 = 12;
 constexpr int kFwdThreads = 640;
 constexpr int kFwdProThreads = 256;
-constexpr int kFwdEpiThreads = 256;
+constexpr int kPwCW = 16;          // accumulator columns per epilogue chunk
+constexpr int kEpiRuntime = -1;    // EPI template value: read the flags from the arguments
+template <int PRO>
+struct FwdEpi {
+  static constexpr int warp0 = PRO == MEDNEXT_PRO_NONE ? 4 : 12;
+  static constexpr int warps = kFwdThreads / 32 - warp0;
+  static constexpr int threads = warps * 32;
+};
 constexpr int kMaxStages = 8;
 constexpr int kMaxEStages = 2;
 
@@ -103,8 +114,28 @@ __device__ __forceinline__ uint32_t tmem_cols_for(int bn) {
   return bn <= 32 ? 32u : (bn <= 64 ? 64u : (bn <= 128 ? 128u : 256u));
 }
 
+// Column sums of a 32 (lanes) x 16 (v[]) block: five butterfly exchange steps
+// that halve the columns each lane keeps, 16 shuffles in all.  On return lane L
+// holds the sum over all 32 lanes of column (L >> 1); the order of the additions
+// is fixed, so the result is deterministic.
+__device__ __forceinline__ float warp_transpose_sum16(const float (&v)[16], int lane) {
+  float w8[8], w4[4], w2[2];
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    w8[i] = (b4 ? v[i + 8] : v[i]) + __shfl_xor_sync(0xffffffffu, b4 ? v[i] : v[i + 8], 16);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w4[i] = (b3 ? w8[i + 4] : w8[i]) + __shfl_xor_sync(0xffffffffu, b3 ? w8[i] : w8[i + 4], 8);
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    w2[i] = (b2 ? w4[i + 2] : w4[i]) + __shfl_xor_sync(0xffffffffu, b2 ? w4[i] : w4[i + 2], 4);
+  const float w1 = (b1 ? w2[1] : w2[0]) + __shfl_xor_sync(0xffffffffu, b1 ? w2[0] : w2[1], 2);
+  return w1 + __shfl_xor_sync(0xffffffffu, w1, 1);
+}
+
 // ---------------------------------------------------------------- forward / dgrad
-template <typename TA, typename TY, int PRO>
+template <typename TA, typename TY, int PRO, int EPI>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     pw_tma_fwd_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB,
                       const __grid_constant__ CUtensorMap mAux, const __grid_constant__ CUtensorMap mRes,
@@ -123,8 +154,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint8_t* ringB = ringA + (size_t)S * 16384;             // S x b_bytes
   uint8_t* ringAux = ringB + (size_t)S * cfg.b_bytes;     // E x aux_bytes
   uint8_t* ringRes = ringAux + (size_t)E * cfg.aux_bytes; // E x res_bytes
-  uint8_t* ringStg = ringRes + (size_t)E * cfg.res_bytes;  // 8 warps x 2 x 32x32 TY
-  constexpr int kStgBytes = 32 * 32 * (int)sizeof(TY);
+  uint8_t* ringStg = ringRes + (size_t)E * cfg.res_bytes;  // epilogue warps x 2 x (16 x 32) TY
+  constexpr int kStgBytes = 32 * kPwCW * (int)sizeof(TY);
+  constexpr int kEpiWarp0 = FwdEpi<PRO>::warp0;
+  constexpr int kEpiThreads = FwdEpi<PRO>::threads;
 
   const uint32_t ncols = tmem_cols_for(BN);
   if (warp == 1) {
@@ -139,11 +172,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sh.tfull[i], 1);
-      mbar_init(&sh.tempty[i], kFwdEpiThreads);
+      mbar_init(&sh.tempty[i], kEpiThreads);
     }
     for (int i = 0; i < E; ++i) {
       mbar_init(&sh.efull[i], 1);
-      mbar_init(&sh.eempty[i], kFwdEpiThreads);
+      mbar_init(&sh.eempty[i], kEpiThreads);
     }
     sh.abort = 0;
     fence_mbarrier_init();
@@ -232,7 +265,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         mma_commit(&sh.tfull[acc]);
       }
     }
-  } else if (warp >= kFwdProWarp0 && warp < kFwdEpiWarp0) {
+  } else if (warp >= kFwdProWarp0 && warp < kEpiWarp0) {
     // ------------------------------------------------ prologue transform (in place)
     if constexpr (PRO != MEDNEXT_PRO_NONE) {
       const int t = tid - kFwdProWarp0 * 32;  // 0..255
@@ -273,15 +306,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
       }
     }
-  } else if (warp >= kFwdEpiWarp0) {
+  } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------ epilogue
-    // 8 warps: warp%4 selects the TMEM lane quarter (32 voxels), warp/4 the
-    // column half; every 32x32 result block is staged in shared memory and
-    // written with one TMA bulk tensor store (out-of-range rows are clipped).
-    const int ew = warp - kFwdEpiWarp0;
+    // warp%4 selects the TMEM lane quarter (32 voxels); the warps of one quarter
+    // take turns over the 16-column chunks.  Every 32x16 result block is staged
+    // in shared memory and written with one TMA bulk tensor store
+    // (out-of-range rows and columns are clipped by the store).
+    constexpr int kGroups = FwdEpi<PRO>::warps / 4;
+    const int ew = warp - kEpiWarp0;
     const int q4 = warp & 3;
-    const int half = ew >> 2;
-    const int epi = p.epilogue;
+    const int cg = ew >> 2;
+    const int epi = EPI >= 0 ? EPI : p.epilogue;
     uint8_t* stg0 = ringStg + (size_t)ew * 2 * kStgBytes;
     uint32_t nstored = 0;
     for (int i = 0; i < ntile_local && !*abort; ++i) {
@@ -294,57 +329,45 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int e = i % E, re = i / E;
       if ((has_aux || has_res) && !wait_or_abort(&sh.efull[e], re & 1, abort)) break;
       const int vl = q4 * 32 + lane;  // voxel within the tile
-      const uint8_t* auxt = ringAux + (size_t)e * cfg.aux_bytes + (vl >> 6) * (cfg.aux_bytes / 2);
-      const uint8_t* rest = ringRes + (size_t)e * cfg.res_bytes + (vl >> 6) * (cfg.res_bytes / 2);
+      const TA* auxt = reinterpret_cast<const TA*>(ringAux + (size_t)e * cfg.aux_bytes + (vl >> 6) * (cfg.aux_bytes / 2)) + (vl & 63);
+      const TY* rest = reinterpret_cast<const TY*>(ringRes + (size_t)e * cfg.res_bytes + (vl >> 6) * (cfg.res_bytes / 2)) + (vl & 63);
       const uint32_t d_tmem = tmem + (uint32_t)acc * ncols + ((uint32_t)(q4 * 32) << 16);
-      for (int c0 = 32 * half; c0 < BN; c0 += 64) {
-        uint32_t r[32];
-        tmem_ld32(d_tmem + (uint32_t)c0, r);
-        // per-column constants, one per lane, broadcast with shuffles
+      for (int c0 = kPwCW * cg; c0 < BN; c0 += kPwCW * kGroups) {
+        uint32_t r[kPwCW];
+        tmem_ld16(d_tmem + (uint32_t)c0, r);
+        // per-column constants: lane l < 16 holds column c0 + l, broadcast with shuffles
         const int jc = j0 + c0 + lane;
-        const bool jok = jc < p.cout;
+        const bool jok = lane < kPwCW && jc < p.cout;
         const float bias_l = ((epi & MEDNEXT_EPI_BIAS) && jok) ? __ldg(p.bias + jc) : 0.f;
         float mean_l = 0.f, rstd_l = 0.f;
         if ((epi & MEDNEXT_EPI_GN_BWD_STATS) && jok) {
           mean_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc));
           rstd_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc) + 1);
         }
-        // staging buffer: wait until the store issued two blocks ago has read it
+        // staging buffer: wait until the store issued two chunks ago has read it
         TY* stg = reinterpret_cast<TY*>(stg0 + (nstored & 1) * kStgBytes);
         if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
         __syncwarp();
         tmem_ld_wait();
-        float gs1 = 0.f, gs2 = 0.f;
+        float s1[kPwCW], s2[kPwCW];
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
+        for (int jj = 0; jj < kPwCW; ++jj) {
           const int jl = c0 + jj;
           float a = __uint_as_float(r[jj]);
           if (epi & MEDNEXT_EPI_BIAS) a += __shfl_sync(0xffffffffu, bias_l, jj);
           if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_RESIDUAL)) a = to_acc<TA>(from_acc<TA>(a));
-          if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) {
-            const float ax = to_acc<TA>(reinterpret_cast<const TA*>(auxt + jl * 128)[vl & 63]);
-            if (epi & MEDNEXT_EPI_GELU_GRAD) a *= gelu_grad_f(ax);
-            if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
-              // out-of-range voxels / channels hold exact zeros (zero-filled operands)
-              const float d = (float)to_acc<TY>(from_acc<TY>((typename Elem<TY>::Acc)a));
-              const float mean = __shfl_sync(0xffffffffu, mean_l, jj);
-              const float rstd = __shfl_sync(0xffffffffu, rstd_l, jj);
-              float s1 = d, s2 = d * ((ax - mean) * rstd);
-#pragma unroll
-              for (int o = 16; o > 0; o >>= 1) {
-                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-                s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-              }
-              if (lane == jj) {
-                gs1 = s1;
-                gs2 = s2;
-              }
-            }
+          float ax = 0.f;
+          if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) ax = to_acc<TA>(auxt[jl * 64]);
+          if (epi & MEDNEXT_EPI_GELU_GRAD) a *= gelu_grad_f(ax);
+          if (epi & MEDNEXT_EPI_RESIDUAL) a += (float)to_acc<TY>(rest[jl * 64]);
+          const TY o = from_acc<TY>((typename Elem<TY>::Acc)a);
+          stg[jj * 32 + lane] = o;
+          if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
+            // out-of-range voxels / channels hold exact zeros (zero-filled operands)
+            const float d = (float)to_acc<TY>(o);
+            s1[jj] = d;
+            s2[jj] = d * (ax - __shfl_sync(0xffffffffu, mean_l, jj));
           }
-          if (epi & MEDNEXT_EPI_RESIDUAL) {
-            a += (float)to_acc<TY>(reinterpret_cast<const TY*>(rest + jl * 64 * sizeof(TY))[vl & 63]);
-          }
-          stg[jj * 32 + lane] = from_acc<TY>((typename Elem<TY>::Acc)a);
         }
         fence_async_smem();
         __syncwarp();
@@ -353,12 +376,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           bulk_commit();
         }
         ++nstored;
-        if ((epi & MEDNEXT_EPI_GN_BWD_STATS) && jok && c0 + lane < BN) {
-          // one partial per (channel, tile, 32-voxel quarter): no cross-warp sync
-          GnBwdPartial gp;
-          gp.s1 = (double)gs1;
-          gp.s2 = (double)gs2;
-          p.gn_part[(((size_t)s * p.cout + jc) * p.mtiles + mt) * 4 + q4] = gp;
+        if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
+          // column sums over the 32 voxels; lanes 2c and 2c+1 end up with column c
+          const float t1 = warp_transpose_sum16(s1, lane);
+          const float t2 = warp_transpose_sum16(s2, lane);
+          const float rstd_c = __shfl_sync(0xffffffffu, rstd_l, lane >> 1);
+          const int col = j0 + c0 + (lane >> 1);
+          if ((lane & 1) == 0 && col < p.cout) {
+            // one partial per (channel, tile, 32-voxel quarter): no cross-warp sync
+            GnBwdPartial gp;
+            gp.s1 = (double)t1;
+            gp.s2 = (double)(t2 * rstd_c);
+            p.gn_part[(((size_t)s * p.cout + col) * p.mtiles + mt) * 4 + q4] = gp;
+          }
         }
       }
       tc_fence_before();

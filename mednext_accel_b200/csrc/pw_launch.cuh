@@ -1,0 +1,183 @@
+// Host helpers shared by the pointwise launch units: TMA tensor-map encoding,
+// shared-memory opt-in, and the forward-GEMM launcher templated on prologue and
+// epilogue, instantiated per element type in pw_fwd_*.cu so that the library
+// builds in parallel.
+#pragma once
+
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <type_traits>
+
+#include "plan.h"
+#include "pointwise_tma.cuh"
+
+namespace mednext {
+namespace pwl {
+
+// ------------------------------------------------------------------ TMA maps
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+template <typename T>
+inline CUtensorMapDataType tma_dtype();
+template <>
+inline CUtensorMapDataType tma_dtype<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
+template <>
+inline CUtensorMapDataType tma_dtype<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
+template <>
+inline CUtensorMapDataType tma_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+
+// [d2][d1][d0] tensor, box (b0, b1, 1)
+template <typename T>
+inline bool encode3(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
+             CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {d0 * sizeof(T), d0 * d1 * sizeof(T)};
+  const cuuint32_t box[3] = {b0, b1, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, tma_dtype<T>(), 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+template <typename T>
+inline bool encode2(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint32_t b0, uint32_t b1,
+             CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {d0 * sizeof(T)};
+  const cuuint32_t box[2] = {b0, b1};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, tma_dtype<T>(), 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+constexpr size_t kSmemBudget = 220 * 1024;
+inline int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+template <typename K>
+inline void set_smem(K kern, size_t smem, size_t& configured) {
+  if (smem > configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured = smem;
+  }
+}
+
+// ------------------------------------------------------------------ forward (TMA)
+// Returns MEDNEXT_OK when launched, -1 when the shape is not TMA-describable.
+template <typename TA, typename TY, int PRO, int EPI>
+int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
+  if (a.vox % 8 != 0 || a.cin % 8 != 0 || !a16(a.a) || !a16(a.wt)) return -1;
+  const bool has_aux = (a.epilogue & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) != 0;
+  const bool has_res = (a.epilogue & MEDNEXT_EPI_RESIDUAL) != 0;
+  if ((has_aux && !a16(a.aux)) || (has_res && !a16(a.residual))) return -1;
+  if (!a16(a.y)) return -1;
+  CUtensorMap mA, mB, mAux, mRes, mY;
+  memset(&mAux, 0, sizeof(mAux));
+  memset(&mRes, 0, sizeof(mRes));
+  if (!encode3<TY>(&mY, a.y, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 32, kPwCW,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+    return -1;
+  if (!encode3<TA>(&mA, a.a, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64, kPwBK, CU_TENSOR_MAP_SWIZZLE_128B))
+    return -1;
+  if (!encode2<TA>(&mB, a.wt, (uint64_t)a.cin, (uint64_t)a.cout, kPwBK, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return -1;
+  if (has_aux && !encode3<TA>(&mAux, a.aux, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, (uint32_t)a.BN,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
+    return -1;
+  if (has_res && !encode3<TY>(&mRes, a.residual, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, (uint32_t)a.BN,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
+    return -1;
+  PwTmaCfg cfg{};
+  cfg.kstages = (a.cin + kPwBK - 1) / kPwBK;
+  cfg.total_tiles = a.S * a.ntiles * a.mtiles;
+  cfg.b_bytes = a.BN * 128;
+  cfg.aux_bytes = has_aux ? a.BN * 64 * (int)sizeof(TA) * 2 : 0;
+  cfg.res_bytes = has_res ? a.BN * 64 * (int)sizeof(TY) * 2 : 0;
+  const size_t per_stage = 16384 + (size_t)cfg.b_bytes;
+  const size_t ebytes = (size_t)cfg.aux_bytes + cfg.res_bytes;
+  const size_t stg = (size_t)FwdEpi<PRO>::warps * 2 * 32 * kPwCW * sizeof(TY);  // epilogue staging, 2 per warp
+  const size_t budget = kSmemBudget - stg;
+  cfg.estages = (2 * ebytes + 2 * per_stage <= budget) ? 2 : 1;
+  const long long room = (long long)budget - (long long)cfg.estages * (long long)ebytes;
+  cfg.stages = (int)std::min<long long>(kMaxStages, room / (long long)per_stage);
+  if (cfg.stages < 2) return -1;
+  const size_t smem = 1024 + cfg.stages * per_stage + cfg.estages * ebytes + stg;
+  auto kern = pw_tma_fwd_kernel<TA, TY, PRO, EPI>;
+  static size_t configured = 0;
+  set_smem(kern, smem, configured);
+  const int grid = std::min(cfg.total_tiles, num_sms());
+  kern<<<grid, kFwdThreads, smem, s>>>(mA, mB, mAux, mRes, mY, a, cfg);
+  return record_launch();
+}
+
+// ------------------------------------------------------------------ forward launch
+template <typename TA, typename TY, int PRO, int EPI>
+int launch_pw_fwd(const PwFwdArgs& a, cudaStream_t s) {
+  const int st = try_pw_fwd_tma<TA, TY, PRO, EPI>(a, s);
+  if (st != -1) return st;
+  auto kern = pw_fwd_kernel<TA, TY, PRO>;
+  const size_t smem = pw_smem(a.BN);
+  static size_t configured = 0;
+  set_smem(kern, smem, configured);
+  const long long grid = (long long)a.S * a.ntiles * a.mtiles;
+  kern<<<(unsigned)grid, kPwThreads, smem, s>>>(a);
+  return record_launch();
+}
+// Compile-time epilogue for the flag sets the MedNeXt block uses; any other set
+// runs the same kernel with the flags read at run time.
+template <typename TA, typename TY, int PRO>
+int pw_fwd_epi(const PwFwdArgs& a, cudaStream_t s) {
+  constexpr int B = MEDNEXT_EPI_BIAS, R = MEDNEXT_EPI_RESIDUAL, G = MEDNEXT_EPI_GELU_GRAD,
+                N = MEDNEXT_EPI_GN_BWD_STATS;
+  const int e = a.epilogue;
+  if constexpr (std::is_same<TA, __nv_bfloat16>::value) {
+    if constexpr (PRO == MEDNEXT_PRO_NONE) {
+      if (e == 0) return launch_pw_fwd<TA, TY, PRO, 0>(a, s);
+      if (e == B) return launch_pw_fwd<TA, TY, PRO, B>(a, s);
+      if (e == G) return launch_pw_fwd<TA, TY, PRO, G>(a, s);
+      if (e == N) return launch_pw_fwd<TA, TY, PRO, N>(a, s);
+    } else if constexpr (PRO == MEDNEXT_PRO_GROUPNORM) {
+      if (e == B) return launch_pw_fwd<TA, TY, PRO, B>(a, s);
+    } else {
+      if (e == B) return launch_pw_fwd<TA, TY, PRO, B>(a, s);
+      if (e == (B | R)) return launch_pw_fwd<TA, TY, PRO, B | R>(a, s);
+    }
+  }
+  return launch_pw_fwd<TA, TY, PRO, kEpiRuntime>(a, s);
+}
+template <typename TA, typename TY>
+int pw_fwd_pro(int prologue, const PwFwdArgs& a, cudaStream_t s) {
+  switch (prologue) {
+    case MEDNEXT_PRO_NONE: return pw_fwd_epi<TA, TY, MEDNEXT_PRO_NONE>(a, s);
+    case MEDNEXT_PRO_GROUPNORM: return pw_fwd_epi<TA, TY, MEDNEXT_PRO_GROUPNORM>(a, s);
+    case MEDNEXT_PRO_GELU: return pw_fwd_epi<TA, TY, MEDNEXT_PRO_GELU>(a, s);
+    default: return MEDNEXT_ERR_BAD_SHAPE;
+  }
+}
+
+}  // namespace pwl
+}  // namespace mednext

@@ -154,5 +154,46 @@ def test_pointwise_op_autograd():
     assert_close_bf16(db, wdb, "db")
 
 
+def _all_finite_bf16(channels):
+    """Every finite bf16 value once, laid out as [1, channels, vox] (zero padded)."""
+    bits = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    vals = bits[torch.isfinite(bits.float())]
+    vox = -(-vals.numel() // channels)
+    vox = -(-vox // 64) * 64
+    flat = torch.zeros(channels * vox, dtype=torch.bfloat16)
+    flat[: vals.numel()] = vals
+    return flat.view(1, channels, vox).cuda(), vals.numel()
+
+
+def _compare_to_torch(got, want, what):
+    """Same bf16 rounding as torch's erf-form GELU except within one bf16 ulp on
+    a small fraction of elements, or within 2e-6 absolute (the far negative tail,
+    where fp32 1 + erf(x) loses its digits in the reference formula)."""
+    g, w = got.float().cpu().flatten(), want.float().cpu().flatten()
+    ulp = torch.maximum(w.abs(), torch.full_like(w, 1e-30)) * 2.0**-7
+    ok = ((g - w).abs() <= ulp) | ((g - w).abs() <= 2e-6)
+    assert bool(ok.all()), f"{what}: worst {(g - w).abs().max().item():.3e} at {w[~ok][:4].tolist()}"
+    differ = (g != w).float().mean().item()
+    assert differ <= 5e-3, f"{what}: {differ:.2e} of the elements differ in the last bf16 bit"
+
+
+def test_gelu_prologue_matches_torch_on_every_bf16_value():
+    a, count = _all_finite_bf16(16)
+    eye = torch.eye(16, dtype=torch.bfloat16, device="cuda")
+    y, _ = pw_gemm(a, eye, 16, prologue=nat.PRO_GELU)  # identity weight: y = bf16(gelu(a))
+    want = torch.nn.functional.gelu(a.float()).to(torch.bfloat16)
+    _compare_to_torch(y.flatten()[:count], want.flatten()[:count], "gelu")
+
+
+def test_gelu_grad_epilogue_matches_torch_on_every_bf16_value():
+    u, count = _all_finite_bf16(16)
+    ones = torch.ones_like(u)
+    eye = torch.eye(16, dtype=torch.bfloat16, device="cuda")
+    du, _ = pw_gemm(ones, eye, 16, aux=u, gelu_grad=True)  # 1 * gelu'(u)
+    uu = u.float().requires_grad_()
+    (want,) = torch.autograd.grad(torch.nn.functional.gelu(uu), uu, torch.ones_like(uu))
+    _compare_to_torch(du.flatten()[:count], want.to(torch.bfloat16).flatten()[:count], "gelu'")
+
+
 def test_no_device_error_recorded():
     assert nat.device_error() == 0
