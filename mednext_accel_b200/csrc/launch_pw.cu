@@ -16,13 +16,18 @@ namespace {
 template <typename TA, int PRO>
 int try_pw_wgrad_tma(const PwWgradArgs& a, cudaStream_t s) {
   if (a.vox % 8 != 0 || !a16(a.g) || !a16(a.a)) return -1;
+  PwTmaWgradCfg cfg{};
+  // a bias row fits when all a rows sit in one N tile with a row to spare
+  cfg.ones_row = (a.ntiles == 1 && a.cin < a.BN) ? a.cin : -1;
+  cfg.g_rows = std::min(a.cout, kPwBM);
+  cfg.a_rows = cfg.ones_row >= 0 ? a.cin : a.BN;
   CUtensorMap mG, mA;
-  if (!encode3<TA>(&mG, a.g, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, kPwBM, CU_TENSOR_MAP_SWIZZLE_128B))
-    return -1;
-  if (!encode3<TA>(&mA, a.a, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64, (uint32_t)a.BN,
+  if (!encode3<TA>(&mG, a.g, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, (uint32_t)cfg.g_rows,
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
-  PwTmaWgradCfg cfg{};
+  if (!encode3<TA>(&mA, a.a, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64, (uint32_t)cfg.a_rows,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return -1;
   cfg.b_bytes = a.BN * 128;
   const size_t per_stage = 16384 + (size_t)cfg.b_bytes;
   cfg.stages = (int)std::min<size_t>(kMaxStages, kSmemBudget / per_stage);
@@ -33,7 +38,7 @@ int try_pw_wgrad_tma(const PwWgradArgs& a, cudaStream_t s) {
   static size_t configured = 0;
   set_smem(kern, smem, configured);
   const int grid = std::min(cfg.units, num_sms());
-  kern<<<grid, kTmaThreads, smem, s>>>(mG, mA, a, cfg);
+  kern<<<grid, kWgThreads, smem, s>>>(mG, mA, a, cfg);
   return record_launch();
 }
 

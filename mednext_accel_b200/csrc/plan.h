@@ -135,7 +135,8 @@ struct PwWPlan {
 };
 inline PwWPlan plan_pw_wgrad(int64_t n, int64_t cin, int64_t cout, int64_t vox) {
   PwWPlan p{};
-  p.BN = pw_bn(cin);
+  // one spare row past cin when it fits: the TMA kernel puts the bias grad there
+  p.BN = cin < 256 ? pw_bn(cin + 1) : pw_bn(cin);
   p.mtiles = (int)((cout + kPwBM - 1) / kPwBM);
   p.ntiles = (int)((cin + p.BN - 1) / p.BN);
   p.cps = (vox + kPwBK - 1) / kPwBK;

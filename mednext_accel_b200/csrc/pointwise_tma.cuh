@@ -62,7 +62,6 @@ __device__ __forceinline__ void bulk_wait_read() {
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-constexpr int kTmaThreads = 384;  // weight-grad kernel: producer, MMA, 4 prologue, 4 epilogue warps
 // forward kernel: warp 0 producer, warp 1 MMA, warps 4-11 prologue (when requested),
 // the remaining warps up to 19 epilogue
 constexpr int kFwdProWarp0 = 4;
@@ -403,14 +402,31 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // ---------------------------------------------------------------- weight grad
+// 512 threads: warp 0 TMA producer, warp 1 MMA issuer, warps 4-11 prologue,
+// warps 12-15 epilogue.  D[j, k] = sum over the split's voxel chunks of
+// g[j, v] * pro(a[k, v]): A = 128 rows of g, B = BN rows of a, both K-major.
+//
+// Bias grad: when the a rows fit in one N tile with a row to spare (ones_row >=
+// 0), that row of every B stage holds 1.0, written once at start (the TMA box
+// only covers the real a rows, so loads never overwrite it), and column
+// ones_row of the accumulator is sum_v g[j, v] = dbias[j].  Otherwise the
+// prologue warps sum the g rows.
+constexpr int kWgThreads = 512;
+constexpr int kWgProWarp0 = 4;
+constexpr int kWgProThreads = 256;
+constexpr int kWgEpiWarp0 = 12;
+
 struct PwTmaWgradCfg {
   int stages;
-  int b_bytes;
-  int units;  // mtiles * ntiles * splits
+  int b_bytes;   // BN * 128: one B stage
+  int units;     // mtiles * ntiles * splits
+  int g_rows;    // rows of g per TMA box (min(128, cout))
+  int a_rows;    // rows of a per TMA box
+  int ones_row;  // B-tile row held at 1.0 for the bias grad, or -1
 };
 
 template <typename TA, int PRO>
-__global__ void __launch_bounds__(kTmaThreads, 1)
+__global__ void __launch_bounds__(kWgThreads, 1)
     pw_tma_wgrad_kernel(const __grid_constant__ CUtensorMap mG, const __grid_constant__ CUtensorMap mA,
                         PwWgradArgs p, PwTmaWgradCfg cfg) {
   extern __shared__ uint8_t smem_dyn[];
@@ -419,10 +435,30 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   const int warp = tid >> 5, lane = tid & 31;
   const int BN = p.BN;
   const int S = cfg.stages;
+  const bool ones = cfg.ones_row >= 0;
+  // the prologue warps run for a GroupNorm / GELU prologue and for bias row sums
+  const bool pro_on = PRO != MEDNEXT_PRO_NONE || !ones;
   const uint32_t base_u32 = smem_u32(smem_dyn);
   uint8_t* sbase = smem_dyn + (((base_u32 + 1023u) & ~1023u) - base_u32);
   uint8_t* ringA = sbase;                      // S x 16 KB  (g rows)
   uint8_t* ringB = ringA + (size_t)S * 16384;  // S x b_bytes (a rows)
+
+  // rows that TMA never writes stay zero; the bias row holds ones
+  {
+    const size_t ring_bytes = (size_t)S * (16384 + cfg.b_bytes);
+    for (size_t off = (size_t)tid * 16; off < ring_bytes; off += (size_t)kWgThreads * 16)
+      *reinterpret_cast<uint4*>(sbase + off) = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+    if (ones && tid < S * 8) {
+      const int st = tid >> 3, c = tid & 7;
+      float one[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) one[e] = 1.0f;
+      *reinterpret_cast<uint4*>(ringB + (size_t)st * cfg.b_bytes + sw128_kmajor_off(cfg.ones_row, c)) =
+          pack16<TA>(one);
+    }
+    fence_async_smem();
+  }
 
   const uint32_t ncols = tmem_cols_for(BN);
   if (warp == 1) {
@@ -432,7 +468,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&sh.full[i], 1);
-      mbar_init(&sh.ready[i], 128);
+      mbar_init(&sh.ready[i], kWgProThreads);
       mbar_init(&sh.empty[i], 1);
     }
     mbar_init(&sh.tfull[0], 1);
@@ -462,6 +498,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      const uint32_t tx = (uint32_t)(cfg.g_rows + cfg.a_rows) * 128u;
       long long q = 0;
       for (int i = 0; i < nunits && !*abort; ++i) {
         int mt, nt, sp;
@@ -473,7 +510,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           if (r > 0 && !wait_or_abort(&sh.empty[st], (uint32_t)((r - 1) & 1), abort)) break;
           const int s = (int)(ch / p.chunks_per_sample);
           const int v = (int)((ch - (long long)s * p.chunks_per_sample) * kPwBK);
-          mbar_arrive_expect_tx(&sh.full[st], (uint32_t)(16384 + cfg.b_bytes));
+          mbar_arrive_expect_tx(&sh.full[st], tx);
           tma_load_3d(ringA + (size_t)st * 16384, &mG, &sh.full[st], v, mt * kPwBM, s);
           tma_load_3d(ringB + (size_t)st * cfg.b_bytes, &mA, &sh.full[st], v, nt * BN, s);
         }
@@ -493,7 +530,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         for (long long ch = cb; ch < ce; ++ch, ++q) {
           const int st = (int)(q % S);
           const long long r = q / S;
-          if (!wait_or_abort(&sh.ready[st], (uint32_t)(r & 1), abort)) break;
+          if (!wait_or_abort(pro_on ? &sh.ready[st] : &sh.full[st], (uint32_t)(r & 1), abort)) break;
           tc_fence_after();
           const uint32_t a_addr = smem_u32(ringA + (size_t)st * 16384);
           const uint32_t b_addr = smem_u32(ringB + (size_t)st * cfg.b_bytes);
@@ -509,62 +546,67 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         mma_commit(&sh.tfull[0]);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
-    // prologue on the a rows (in place) and bias-grad row sums of the g rows
-    const int t = tid - 128;
-    long long q = 0;
-    for (int i = 0; i < nunits && !*abort; ++i) {
-      int mt, nt, sp;
-      long long cb, ce;
-      unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
-      float bsum = 0.f;  // row t of g (output channel mt*128 + t)
-      for (long long ch = cb; ch < ce; ++ch, ++q) {
-        const int st = (int)(q % S);
-        const long long r = q / S;
-        if (!wait_or_abort(&sh.full[st], (uint32_t)(r & 1), abort)) break;
-        const int s = (int)(ch / p.chunks_per_sample);
-        if (nt == 0) {
-          const uint8_t* row = ringA + (size_t)st * 16384 + (t >> 3) * 1024 + (t & 7) * 128;
+  } else if (warp >= kWgProWarp0 && warp < kWgEpiWarp0) {
+    if (!pro_on) {
+      // nothing to transform or sum: the MMA consumes the stages straight from TMA
+    } else {
+      // prologue on the a rows (in place) and, without a bias row, the g row sums
+      const int t = tid - kWgProWarp0 * 32;  // 0..255
+      long long q = 0;
+      for (int i = 0; i < nunits && !*abort; ++i) {
+        int mt, nt, sp;
+        long long cb, ce;
+        unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
+        const bool rowsum = !ones && nt == 0 && t < kPwBM;
+        float bsum = 0.f;  // row t of g (output channel mt*128 + t)
+        for (long long ch = cb; ch < ce; ++ch, ++q) {
+          const int st = (int)(q % S);
+          const long long r = q / S;
+          if (!wait_or_abort(&sh.full[st], (uint32_t)(r & 1), abort)) break;
+          const int s = (int)(ch / p.chunks_per_sample);
+          if (rowsum) {
+            const uint8_t* row = ringA + (size_t)st * 16384 + (t >> 3) * 1024 + (t & 7) * 128;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            float v[8];
-            unpack16<TA>(*reinterpret_cast<const uint4*>(row + c * 16), v);
+            for (int c = 0; c < 8; ++c) {
+              float v[8];
+              unpack16<TA>(*reinterpret_cast<const uint4*>(row + c * 16), v);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) bsum += v[e];
-          }
-        }
-        if constexpr (PRO != MEDNEXT_PRO_NONE) {
-          // BN rows x 8 chunks; thread handles rows n = t/8 + 16*ii, chunk t%8
-          const int cq = t & 7;
-          for (int n = t >> 3; n < BN; n += 16) {
-            const int k = nt * BN + n;
-            uint4* chunk = reinterpret_cast<uint4*>(ringB + (size_t)st * cfg.b_bytes + sw128_kmajor_off(n, cq));
-            float v[8];
-            unpack16<TA>(*chunk, v);
-            if constexpr (PRO == MEDNEXT_PRO_GROUPNORM) {
-              float ca = 0.f, cbb = 0.f;
-              if (k < p.cin) {
-                const float mean = __ldg(p.pro_stats + 2 * (s * p.cin + k));
-                const float rstd = __ldg(p.pro_stats + 2 * (s * p.cin + k) + 1);
-                ca = rstd * __ldg(p.pro_gamma + k);
-                cbb = __ldg(p.pro_beta + k) - mean * ca;
-              }
-              pw_prologue<PRO>(v, ca, cbb);
-            } else {
-              pw_prologue<PRO>(v, 0.f, 0.f);
+              for (int e = 0; e < 8; ++e) bsum += v[e];
             }
-            *chunk = pack16<TA>(v);
           }
-          fence_async_smem();
+          if constexpr (PRO != MEDNEXT_PRO_NONE) {
+            // a_rows x 8 chunks of 8 voxels; item -> (row, chunk), 4 rows per warp pass
+            for (int item = t; item < cfg.a_rows * 8; item += kWgProThreads) {
+              const int n = item >> 3, cq = item & 7;
+              const int k = nt * BN + n;
+              uint4* chunk = reinterpret_cast<uint4*>(ringB + (size_t)st * cfg.b_bytes + sw128_kmajor_off(n, cq));
+              float v[8];
+              unpack16<TA>(*chunk, v);
+              if constexpr (PRO == MEDNEXT_PRO_GROUPNORM) {
+                float ca = 0.f, cbb = 0.f;
+                if (k < p.cin) {
+                  const float mean = __ldg(p.pro_stats + 2 * (s * p.cin + k));
+                  const float rstd = __ldg(p.pro_stats + 2 * (s * p.cin + k) + 1);
+                  ca = rstd * __ldg(p.pro_gamma + k);
+                  cbb = __ldg(p.pro_beta + k) - mean * ca;
+                }
+                pw_prologue<PRO>(v, ca, cbb);
+              } else {
+                pw_prologue<PRO>(v, 0.f, 0.f);
+              }
+              *chunk = pack16<TA>(v);
+            }
+            fence_async_smem();
+          }
+          mbar_arrive(&sh.ready[st]);
         }
-        mbar_arrive(&sh.ready[st]);
-      }
-      if (nt == 0) {
-        const int j = mt * kPwBM + t;
-        if (j < p.cout) p.part_b[(size_t)sp * p.cout + j] = bsum;
+        if (rowsum) {
+          const int j = mt * kPwBM + t;
+          if (j < p.cout) p.part_b[(size_t)sp * p.cout + j] = bsum;
+        }
       }
     }
-  } else if (warp >= 8) {
+  } else if (warp >= kWgEpiWarp0) {
     const int q4 = warp & 3;
     for (int i = 0; i < nunits && !*abort; ++i) {
       int mt, nt, sp;
@@ -575,6 +617,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       if (!wait_or_abort(&sh.tfull[0], (uint32_t)(i & 1), abort)) break;
       tc_fence_after();
       const int j = mt * kPwBM + q4 * 32 + lane;
+      float bval = 0.f;
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         if (any) {
@@ -590,9 +633,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
           for (int e = 0; e < 32; ++e) {
             const int k = nt * BN + c0 + e;
             if (c0 + e < BN && k < p.cin) dst[k] = __uint_as_float(r[e]);
+            if (c0 + e == cfg.ones_row) bval = __uint_as_float(r[e]);
           }
         }
       }
+      if (ones && j < p.cout) p.part_b[(size_t)sp * p.cout + j] = bval;
       tc_fence_before();
       mbar_arrive(&sh.tempty[0]);
     }
