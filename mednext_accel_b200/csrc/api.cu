@@ -49,8 +49,8 @@ size_t s1_wgrad_ws(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
   const S1Plan p = plan_s1(n, c, d, h, w, k, elem_size(dtype), true);
   return (size_t)n * c * s1_tiles(p) * ((size_t)k * k * k + 1) * acc_size(dtype);
 }
-size_t s2_wgrad_ws(int64_t n, int64_t c, size_t svol, int k, int dtype) {
-  const S2WPlan p = plan_s2w(n, c, svol, k);
+size_t s2_wgrad_ws(int64_t n, int64_t c, int64_t ds, int k, int dtype) {
+  const S2WPlan p = plan_s2w(n, c, ds, k);
   return (size_t)n * c * p.chunks * ((size_t)k * k * k + 1) * acc_size(dtype);
 }
 bool gn_shape_ok(int64_t n, int64_t c, int64_t spatial) {
@@ -200,7 +200,7 @@ int mednext_dw_s2_dgrad(const void* dy, const void* weight, void* dx, int64_t n,
 size_t mednext_dw_s2_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
   if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
   const DwS2Geom g = s2_geom_down(n, c, d, h, w);
-  return s2_wgrad_ws(n, c, (size_t)g.Ds * g.Hs * g.Ws, k, dtype);
+  return s2_wgrad_ws(n, c, g.Ds, k, dtype);
 }
 
 int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
@@ -246,7 +246,7 @@ int mednext_dwT_dgrad(const void* dy, const void* weight, void* dx, int64_t n, i
 
 size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
   if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
-  return s2_wgrad_ws(n, c, (size_t)d * h * w, k, dtype);
+  return s2_wgrad_ws(n, c, d, k, dtype);
 }
 
 int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,

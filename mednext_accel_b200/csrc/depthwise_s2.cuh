@@ -20,105 +20,193 @@ struct DwS2Geom {
   long long bp;    // elements between consecutive (n, c) volumes of the big grid (>= Db*Hb*Wb)
 };
 
-// gather: one thread per small-grid output, consecutive threads along W.
+// Work decomposition of the three kernels: a CTA owns one (sample, channel) and
+// one plane (gather, scatter) or a run of small-grid planes (wgrad); its warps
+// take the rows of the plane in turn and the lanes run along W.  Index math is
+// 32-bit per row, the per-channel weights are loaded once per CTA.
+constexpr int kS2Warps = 8;
+
 template <typename T, int K>
-__global__ void __launch_bounds__(256) dw_s2_gather_kernel(const T* __restrict__ big,
-                                                           const T* __restrict__ wgt,
-                                                           const T* __restrict__ bias,
-                                                           T* __restrict__ small, DwS2Geom g) {
+struct S2Weights {
+  using Acc = typename Elem<T>::Acc;
+  static constexpr int K3 = K * K * K;
+  static constexpr bool kReg = K <= 3;  // registers for k <= 3, shared memory above
+  Acc r[kReg ? K3 : 1];
+  const Acc* s;
+  __device__ __forceinline__ void load(const T* __restrict__ w, Acc* sm) {
+    if constexpr (kReg) {
+#pragma unroll
+      for (int t = 0; t < K3; ++t) r[t] = to_acc<T>(__ldg(w + t));
+    } else {
+      for (int t = threadIdx.x; t < K3; t += blockDim.x) sm[t] = to_acc<T>(w[t]);
+      __syncthreads();
+      s = sm;
+    }
+  }
+  __device__ __forceinline__ Acc operator[](int t) const {
+    if constexpr (kReg) return r[t];
+    else return s[t];
+  }
+};
+
+// Clamped, unconditional load: out-of-range positions read a valid element and
+// are multiplied by zero, so every load of an output's stencil can be in flight
+// at once (range checks as branches would serialise the loads per tap row).
+template <typename T>
+__device__ __forceinline__ typename Elem<T>::Acc s2_ld(const T* __restrict__ p, int i, int n) {
+  using Acc = typename Elem<T>::Acc;
+  const int c = min(max(i, 0), n - 1);
+  const Acc v = to_acc<T>(__ldg(p + c));
+  return (i >= 0 && i < n) ? v : Acc(0);
+}
+
+// gather: CTA = (n, c, md) small-grid plane; one output per lane.
+template <typename T, int K>
+__global__ void __launch_bounds__(kS2Warps * 32) dw_s2_gather_kernel(const T* __restrict__ big,
+                                                                     const T* __restrict__ wgt,
+                                                                     const T* __restrict__ bias,
+                                                                     T* __restrict__ small, DwS2Geom g) {
   using Acc = typename Elem<T>::Acc;
   constexpr int P = K / 2;
   constexpr int K3 = K * K * K;
-  const size_t svol = (size_t)g.Ds * g.Hs * g.Ws;
-  const size_t total = (size_t)g.N * g.C * svol;
-  const size_t bvol = (size_t)g.Db * g.Hb * g.Wb;
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (size_t)gridDim.x * blockDim.x) {
-    const size_t nc = idx / svol;
-    size_t r = idx - nc * svol;
-    const int ow = (int)(r % g.Ws);
-    r /= g.Ws;
-    const int oh = (int)(r % g.Hs);
-    const int od = (int)(r / g.Hs);
-    const int c = (int)(nc % g.C);
-    const T* src = big + nc * (size_t)g.bp;
-    const T* w = wgt + (size_t)c * K3;
-    Acc acc = bias != nullptr ? to_acc<T>(bias[c]) : Acc(0);
+  __shared__ Acc wsm[S2Weights<T, K>::kReg ? 1 : K3];
+  const int md = (int)(blockIdx.x % (unsigned)g.Ds);
+  const int nc = (int)(blockIdx.x / (unsigned)g.Ds);
+  const int c = nc % g.C;
+  S2Weights<T, K> w;
+  w.load(wgt + (size_t)c * K3, wsm);
+  const Acc b0 = bias != nullptr ? to_acc<T>(bias[c]) : Acc(0);
+  const T* bsrc = big + (size_t)nc * (size_t)g.bp;
+  T* dst = small + ((size_t)nc * g.Ds + md) * ((size_t)g.Hs * g.Ws);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int mh = warp; mh < g.Hs; mh += kS2Warps) {
+    for (int mw = lane; mw < g.Ws; mw += 32) {
+      Acc acc = b0;
 #pragma unroll
-    for (int kd = 0; kd < K; ++kd) {
-      const int id = 2 * od - P + kd;
-      if (id < 0 || id >= g.Db) continue;
+      for (int kd = 0; kd < K; ++kd) {
+        const int id = 2 * md - P + kd;
+        const bool dok = id >= 0 && id < g.Db;
+        const int idc = min(max(id, 0), g.Db - 1);
 #pragma unroll
-      for (int kh = 0; kh < K; ++kh) {
-        const int ih = 2 * oh - P + kh;
-        if (ih < 0 || ih >= g.Hb) continue;
-        const T* row = src + ((size_t)id * g.Hb + ih) * g.Wb;
+        for (int kh = 0; kh < K; ++kh) {
+          const int ih = 2 * mh - P + kh;
+          const bool ok = dok && ih >= 0 && ih < g.Hb;
+          const int ihc = min(max(ih, 0), g.Hb - 1);
+          const T* row = bsrc + ((size_t)idc * g.Hb + ihc) * g.Wb;
 #pragma unroll
-        for (int kw = 0; kw < K; ++kw) {
-          const int iw = 2 * ow - P + kw;
-          if (iw < 0 || iw >= g.Wb) continue;
-          acc = fma(to_acc<T>(__ldg(row + iw)), to_acc<T>(__ldg(w + (kd * K + kh) * K + kw)), acc);
+          for (int kw = 0; kw < K; ++kw) {
+            const Acc v = s2_ld<T>(row, 2 * mw - P + kw, g.Wb);
+            acc = fma(ok ? v : Acc(0), w[(kd * K + kh) * K + kw], acc);
+          }
         }
       }
+      dst[(size_t)mh * g.Ws + mw] = from_acc<T>(acc);
     }
-    small[idx] = from_acc<T>(acc);
   }
 }
 
-// scatter: one thread per big-grid output.  Per axis only taps with
-// t = (i + P) mod 2 (mod 2) contribute, i.e. ceil(K/2) or floor(K/2) taps.
+// Parity blocks of the scatter.  Along an axis, big index i = 2q + e (e = 0, 1)
+// receives small[m] through tap t = i + P - 2m; over both parities m runs over
+// q + lo .. q + lo + R - 1, so a thread that owns the 2x2x2 outputs of block q
+// reads R^3 small values and uses every tap once (K^3 FMAs for 8 outputs), with
+// the tap of each (parity, window offset) pair known at compile time.
+template <int K>
+struct S2Block {
+  static constexpr int P = K / 2;
+  static constexpr int lo = -(P / 2);
+  static constexpr int R = (1 + P) / 2 - lo + 1;
+  // tap joining parity e to window offset a, or -1
+  static constexpr int tap(int e, int a) { return (e + P - 2 * (lo + a) >= 0 && e + P - 2 * (lo + a) < K) ? e + P - 2 * (lo + a) : -1; }
+};
+
+// scatter: CTA = (n, c, qd) pair of big-grid planes 2qd, 2qd+1; warps take block
+// rows, lanes run along W; each thread writes a 2x2x2 output block.
 template <typename T, int K>
-__global__ void __launch_bounds__(256) dw_s2_scatter_kernel(const T* __restrict__ small,
-                                                            const T* __restrict__ wgt,
-                                                            const T* __restrict__ bias,
-                                                            T* __restrict__ big, DwS2Geom g) {
+__global__ void __launch_bounds__(kS2Warps * 32) dw_s2_scatter_kernel(const T* __restrict__ small,
+                                                                      const T* __restrict__ wgt,
+                                                                      const T* __restrict__ bias,
+                                                                      T* __restrict__ big, DwS2Geom g) {
   using Acc = typename Elem<T>::Acc;
-  constexpr int P = K / 2;
+  using B = S2Block<K>;
+  constexpr int R = B::R;
   constexpr int K3 = K * K * K;
-  const size_t bvol = (size_t)g.Db * g.Hb * g.Wb;
-  const size_t bp = (size_t)g.bp;
-  const size_t total = (size_t)g.N * g.C * bp;
-  const size_t svol = (size_t)g.Ds * g.Hs * g.Ws;
-  for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (size_t)gridDim.x * blockDim.x) {
-    const size_t nc = idx / bp;
-    size_t r = idx - nc * bp;
-    if (r >= bvol) {  // padding tail of a pitched row: keep it finite
-      big[idx] = from_acc<T>(Acc(0));
-      continue;
-    }
-    const int iw = (int)(r % g.Wb);
-    r /= g.Wb;
-    const int ih = (int)(r % g.Hb);
-    const int id = (int)(r / g.Hb);
-    const int c = (int)(nc % g.C);
-    const T* src = small + nc * svol;
-    const T* w = wgt + (size_t)c * K3;
-    Acc acc = bias != nullptr ? to_acc<T>(bias[c]) : Acc(0);
-    // first contributing tap per axis has the parity of (i + P)
-    const int td0 = (id + P) & 1, th0 = (ih + P) & 1, tw0 = (iw + P) & 1;
-    for (int kd = td0; kd < K; kd += 2) {
-      const int md = (id + P - kd) >> 1;
-      if (md < 0 || md >= g.Ds) continue;
-      for (int kh = th0; kh < K; kh += 2) {
-        const int mh = (ih + P - kh) >> 1;
-        if (mh < 0 || mh >= g.Hs) continue;
-        const T* row = src + ((size_t)md * g.Hs + mh) * g.Ws;
-        for (int kw = tw0; kw < K; kw += 2) {
-          const int mw = (iw + P - kw) >> 1;
-          if (mw < 0 || mw >= g.Ws) continue;
-          acc = fma(to_acc<T>(__ldg(row + mw)), to_acc<T>(__ldg(w + (kd * K + kh) * K + kw)), acc);
+  __shared__ Acc wsm[S2Weights<T, K>::kReg ? 1 : K3];
+  const int QD = (g.Db + 1) >> 1, QH = (g.Hb + 1) >> 1, QW = (g.Wb + 1) >> 1;
+  const int qd = (int)(blockIdx.x % (unsigned)QD);
+  const int nc = (int)(blockIdx.x / (unsigned)QD);
+  const int c = nc % g.C;
+  S2Weights<T, K> w;
+  w.load(wgt + (size_t)c * K3, wsm);
+  const Acc b0 = bias != nullptr ? to_acc<T>(bias[c]) : Acc(0);
+  const T* src = small + (size_t)nc * ((size_t)g.Ds * g.Hs * g.Ws);
+  T* bvol = big + (size_t)nc * (size_t)g.bp;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int qh = warp; qh < QH; qh += kS2Warps) {
+    for (int qw = lane; qw < QW; qw += 32) {
+      Acc sv[R][R][R];
+#pragma unroll
+      for (int ad = 0; ad < R; ++ad) {
+        const int md = qd + B::lo + ad;
+        const bool dok = md >= 0 && md < g.Ds;
+        const int mdc = min(max(md, 0), g.Ds - 1);
+#pragma unroll
+        for (int ah = 0; ah < R; ++ah) {
+          const int mh = qh + B::lo + ah;
+          const bool ok = dok && mh >= 0 && mh < g.Hs;
+          const int mhc = min(max(mh, 0), g.Hs - 1);
+          const T* row = src + ((size_t)mdc * g.Hs + mhc) * g.Ws;
+#pragma unroll
+          for (int aw = 0; aw < R; ++aw) {
+            const Acc v = s2_ld<T>(row, qw + B::lo + aw, g.Ws);
+            sv[ad][ah][aw] = ok ? v : Acc(0);
+          }
+        }
+      }
+#pragma unroll
+      for (int ed = 0; ed < 2; ++ed) {
+        const int id = 2 * qd + ed;
+#pragma unroll
+        for (int eh = 0; eh < 2; ++eh) {
+          const int ih = 2 * qh + eh;
+          T* row = bvol + ((size_t)id * g.Hb + ih) * g.Wb;
+#pragma unroll
+          for (int ew = 0; ew < 2; ++ew) {
+            Acc acc = b0;
+#pragma unroll
+            for (int ad = 0; ad < R; ++ad) {
+              const int td = B::tap(ed, ad);
+              if (td < 0) continue;
+#pragma unroll
+              for (int ah = 0; ah < R; ++ah) {
+                const int th = B::tap(eh, ah);
+                if (th < 0) continue;
+#pragma unroll
+                for (int aw = 0; aw < R; ++aw) {
+                  const int tw = B::tap(ew, aw);
+                  if (tw < 0) continue;
+                  acc = fma(sv[ad][ah][aw], w[(td * K + th) * K + tw], acc);
+                }
+              }
+            }
+            const int iw = 2 * qw + ew;
+            if (id < g.Db && ih < g.Hb && iw < g.Wb) row[iw] = from_acc<T>(acc);
+          }
         }
       }
     }
-    big[idx] = from_acc<T>(acc);
+  }
+  // padding tail of a pitched (n, c) row: keep it finite
+  const size_t bvol_elems = (size_t)g.Db * g.Hb * g.Wb;
+  if (qd == QD - 1) {
+    for (size_t e = bvol_elems + threadIdx.x; e < (size_t)g.bp; e += blockDim.x) bvol[e] = from_acc<T>(Acc(0));
   }
 }
 
-// wgrad: the CTA's threads form K groups (group g owns the K*K taps with
-// kd = g).  A CTA covers `chunk` consecutive small-grid positions of one
-// (sample, channel); with `small_bias` it also sums the small grid (the down
-// block's bias grad).  Partials: part[(nc*chunks + j)*(K^3+1) + tap].
+// wgrad: the CTA's threads form K groups (group g owns the K*K taps with kd = g,
+// and its warps take the small-grid rows in turn).  A CTA covers `chunk`
+// consecutive small-grid planes of one (sample, channel); with `small_bias` it
+// also sums the small grid (the down block's bias grad).
+// Partials: part[(nc*chunks + j)*(K^3+1) + tap].
 template <typename T, int K>
 __global__ void __launch_bounds__(448) dw_s2_wgrad_kernel(const T* __restrict__ big,
                                                           const T* __restrict__ small,
@@ -129,47 +217,46 @@ __global__ void __launch_bounds__(448) dw_s2_wgrad_kernel(const T* __restrict__ 
   constexpr int P = K / 2;
   constexpr int K2 = K * K;
   constexpr int K3 = K2 * K;
-  const int G = blockDim.x / K;
+  const int G = blockDim.x / K;  // threads per group, a multiple of 32
   const int grp = threadIdx.x / G;
   const int lt = threadIdx.x - grp * G;
-  const int j = blockIdx.x % chunks;
-  const size_t nc = blockIdx.x / chunks;
-  const size_t svol = (size_t)g.Ds * g.Hs * g.Ws;
-  const size_t bvol = (size_t)g.Db * g.Hb * g.Wb;
-  const T* bsrc = big + nc * (size_t)g.bp;
-  const T* ssrc = small + nc * svol;
-  const size_t beg = (size_t)j * chunk;
-  const size_t end = min(beg + (size_t)chunk, svol);
+  const int gwarp = lt >> 5, gwarps = G >> 5;
+  const int lane = threadIdx.x & 31;
+  const int j = (int)(blockIdx.x % (unsigned)chunks);
+  const int nc = (int)(blockIdx.x / (unsigned)chunks);
+  const size_t splane = (size_t)g.Hs * g.Ws;
+  const T* bsrc = big + (size_t)nc * (size_t)g.bp;
+  const T* ssrc = small + (size_t)nc * g.Ds * splane;
+  const int md0 = j * chunk;
+  const int md1 = min(md0 + chunk, g.Ds);
   Acc acc[K2 + 1];
 #pragma unroll
   for (int t = 0; t <= K2; ++t) acc[t] = Acc(0);
   const int kd = grp;
-  for (size_t m = beg + lt; m < end; m += G) {
-    size_t r = m;
-    const int mw = (int)(r % g.Ws);
-    r /= g.Ws;
-    const int mh = (int)(r % g.Hs);
-    const int md = (int)(r / g.Hs);
-    const Acc sv = to_acc<T>(__ldg(ssrc + m));
-    acc[K2] += sv;
+  for (int md = md0; md < md1; ++md) {
     const int id = 2 * md - P + kd;
-    if (id < 0 || id >= g.Db) continue;
+    const bool dok = id >= 0 && id < g.Db;
+    const int idc = min(max(id, 0), g.Db - 1);
+    for (int mh = gwarp; mh < g.Hs; mh += gwarps) {
+      const T* srow = ssrc + (size_t)md * splane + (size_t)mh * g.Ws;
+      for (int mw = lane; mw < g.Ws; mw += 32) {
+        const Acc sv = to_acc<T>(__ldg(srow + mw));
+        acc[K2] += sv;
+        const Acc svd = dok ? sv : Acc(0);
 #pragma unroll
-    for (int kh = 0; kh < K; ++kh) {
-      const int ih = 2 * mh - P + kh;
-      if (ih < 0 || ih >= g.Hb) continue;
-      const T* row = bsrc + ((size_t)id * g.Hb + ih) * g.Wb;
+        for (int kh = 0; kh < K; ++kh) {
+          const int ih = 2 * mh - P + kh;
+          const Acc svh = (ih >= 0 && ih < g.Hb) ? svd : Acc(0);
+          const T* row = bsrc + ((size_t)idc * g.Hb + min(max(ih, 0), g.Hb - 1)) * g.Wb;
 #pragma unroll
-      for (int kw = 0; kw < K; ++kw) {
-        const int iw = 2 * mw - P + kw;
-        if (iw < 0 || iw >= g.Wb) continue;
-        acc[kh * K + kw] = fma(to_acc<T>(__ldg(row + iw)), sv, acc[kh * K + kw]);
+          for (int kw = 0; kw < K; ++kw)
+            acc[kh * K + kw] = fma(s2_ld<T>(row, 2 * mw - P + kw, g.Wb), svh, acc[kh * K + kw]);
+        }
       }
     }
   }
   // reduce within each group (G is a multiple of 32)
   __shared__ Acc red[14 * (K2 + 1)];
-  const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
 #pragma unroll
   for (int t = 0; t <= K2; ++t) {
@@ -179,13 +266,12 @@ __global__ void __launch_bounds__(448) dw_s2_wgrad_kernel(const T* __restrict__ 
     if (lane == 0) red[warp * (K2 + 1) + t] = s;
   }
   __syncthreads();
-  const int wpg = G >> 5;
   Acc* dst = part + ((size_t)nc * chunks + j) * (K3 + 1);
   for (int e = threadIdx.x; e < K * (K2 + 1); e += blockDim.x) {
     const int gg = e / (K2 + 1);
     const int t = e - gg * (K2 + 1);
     Acc s = Acc(0);
-    for (int w = 0; w < wpg; ++w) s += red[(gg * wpg + w) * (K2 + 1) + t];
+    for (int w = 0; w < gwarps; ++w) s += red[(gg * gwarps + w) * (K2 + 1) + t];
     if (t < K2) dst[gg * K2 + t] = s;
     else if (gg == 0) dst[K3] = small_bias ? s : Acc(0);
   }

@@ -14,22 +14,22 @@ int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, i
   return record_launch();
 }
 
-unsigned grid_1d(size_t total, int threads) {
-  const size_t blocks = (total + threads - 1) / threads;
-  return (unsigned)std::min<size_t>(std::max<size_t>(blocks, 1), (size_t)148 * 32);
-}
+// One CTA per (sample, channel, plane): the grid must fit gridDim.x.
+bool grid_ok(long long ctas) { return ctas > 0 && ctas < (1LL << 31); }
 
 template <typename T, int K>
 int launch_gather(const void* big, const void* w, const void* b, void* small, const DwS2Geom& g, cudaStream_t s) {
-  const size_t total = (size_t)g.N * g.C * g.Ds * g.Hs * g.Ws;
-  dw_s2_gather_kernel<T, K><<<grid_1d(total, 256), 256, 0, s>>>(
+  const long long ctas = (long long)g.N * g.C * g.Ds;
+  if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
+  dw_s2_gather_kernel<T, K><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(
       static_cast<const T*>(big), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(small), g);
   return record_launch();
 }
 template <typename T, int K>
 int launch_scatter(const void* small, const void* w, const void* b, void* big, const DwS2Geom& g, cudaStream_t s) {
-  const size_t total = (size_t)g.N * g.C * (size_t)g.bp;
-  dw_s2_scatter_kernel<T, K><<<grid_1d(total, 256), 256, 0, s>>>(
+  const long long ctas = (long long)g.N * g.C * ((g.Db + 1) / 2);
+  if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
+  dw_s2_scatter_kernel<T, K><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(
       static_cast<const T*>(small), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(big), g);
   return record_launch();
 }
@@ -37,10 +37,11 @@ template <typename T, int K>
 int launch_s2_wgrad(const void* big, const void* small, void* dw, void* db, void* ws, const DwS2Geom& g,
                     bool bias_from_big, cudaStream_t s) {
   using Acc = typename Elem<T>::Acc;
-  const size_t svol = (size_t)g.Ds * g.Hs * g.Ws;
-  const S2WPlan p = plan_s2w(g.N, g.C, svol, K);
+  const S2WPlan p = plan_s2w(g.N, g.C, g.Ds, K);
   Acc* part = static_cast<Acc*>(ws);
-  const unsigned grid = (unsigned)((size_t)g.N * g.C * p.chunks);
+  const long long ctas = (long long)g.N * g.C * p.chunks;
+  if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
+  const unsigned grid = (unsigned)ctas;
   dw_s2_wgrad_kernel<T, K><<<grid, p.threads, 0, s>>>(static_cast<const T*>(big), static_cast<const T*>(small), part,
                                                       g, p.chunk, p.chunks, bias_from_big ? 0 : 1);
   int st = record_launch();

@@ -86,14 +86,14 @@ constexpr int kS2Group = 64;
 struct S2WPlan {
   int chunk, chunks, threads;
 };
-inline S2WPlan plan_s2w(int64_t n, int64_t c, size_t svol, int k) {
+// Chunks of whole small-grid planes, about kTargetCtas CTAs in all.
+inline S2WPlan plan_s2w(int64_t n, int64_t c, int64_t ds, int k) {
   S2WPlan p{};
   const long long nc = n * c;
   const long long want = std::max(1LL, (long long)kTargetCtas / std::max(1LL, nc));
-  long long chunk = std::max<long long>(256, (long long)((svol + want - 1) / want));
-  chunk = std::min<long long>(chunk, (long long)svol);
+  const long long chunk = std::max(1LL, (ds + want - 1) / want);
   p.chunk = (int)chunk;
-  p.chunks = (int)((svol + chunk - 1) / chunk);
+  p.chunks = (int)((ds + chunk - 1) / chunk);
   p.threads = kS2Group * k;
   return p;
 }
