@@ -52,6 +52,10 @@ def parse_args(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--spatial", type=int, default=SPATIAL, help=argparse.SUPPRESS)
+    p.add_argument("--profile-step", action="store_true",
+                   help="after warm-up run one eager step between cudaProfilerStart/Stop and exit "
+                        "(for ncu --profile-from-start off: the launch list of one whole step, "
+                        "backward-thread kernels included)")
     return p.parse_args(argv)
 
 
@@ -319,6 +323,18 @@ def run_ours(args) -> int:
             loss = step()
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
+
+    if args.profile_step:
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        if world > 1:
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"profile_step": True, "device_error": nat.device_error()}), flush=True)
+        return 0
 
     graph = None
     mode = "eager"

@@ -278,20 +278,37 @@ __global__ void __launch_bounds__(448) dw_s2_wgrad_kernel(const T* __restrict__ 
 }
 
 // Per-(sample, channel, chunk) sums of a tensor into slot K^3 of the wgrad
-// partials (bias grad of the up block, whose dy is the big grid).
+// partials (bias grad of the up block, whose dy is the big grid).  Rows start
+// every `pitch` elements; with a 16-byte aligned base and pitch the chunks are
+// read as 16-byte vectors.
 template <typename T>
 __global__ void __launch_bounds__(256) chan_sum_into_partials_kernel(
     const T* __restrict__ src, typename Elem<T>::Acc* __restrict__ part, size_t vol, size_t pitch, int chunks,
     int K3) {
   using Acc = typename Elem<T>::Acc;
-  const int j = blockIdx.x % chunks;
-  const size_t nc = blockIdx.x / chunks;
-  const size_t per = (vol + chunks - 1) / chunks;
-  const size_t beg = (size_t)j * per;
-  const size_t end = min(beg + per, vol);
+  constexpr int E = 16 / (int)sizeof(T);
+  const int j = (int)(blockIdx.x % (unsigned)chunks);
+  const size_t nc = blockIdx.x / (unsigned)chunks;
   const T* p = src + nc * pitch;
+  const bool vec = (reinterpret_cast<uintptr_t>(src) % 16 == 0) && (pitch % E == 0);
+  // chunk bounds on whole 16-byte vectors
+  const size_t per = ((vol + chunks - 1) / chunks + E - 1) / E * E;
+  const size_t beg = min((size_t)j * per, vol);
+  const size_t end = min(beg + per, vol);
   Acc s = Acc(0);
-  for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) s += to_acc<T>(__ldg(p + i));
+  if (vec) {
+    const size_t nv = (end - beg) / E;
+    const uint4* pv = reinterpret_cast<const uint4*>(p + beg);
+    for (size_t i = threadIdx.x; i < nv; i += blockDim.x) {
+      Acc v[E];
+      unpack16<T>(__ldg(pv + i), v);
+#pragma unroll
+      for (int e = 0; e < E; ++e) s += v[e];
+    }
+    for (size_t i = beg + nv * E + threadIdx.x; i < end; i += blockDim.x) s += to_acc<T>(__ldg(p + i));
+  } else {
+    for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) s += to_acc<T>(__ldg(p + i));
+  }
   __shared__ Acc red[8];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);

@@ -86,15 +86,15 @@ constexpr int kS2Group = 64;
 struct S2WPlan {
   int chunk, chunks, threads;
 };
-// Chunks of whole small-grid planes, about kTargetCtas CTAs in all.
+// One CTA per (sample, channel, small-grid plane): many short CTAs keep enough
+// loads in flight; K thread groups (one per kd), 128 threads each for k <= 3.
 inline S2WPlan plan_s2w(int64_t n, int64_t c, int64_t ds, int k) {
+  (void)n;
+  (void)c;
   S2WPlan p{};
-  const long long nc = n * c;
-  const long long want = std::max(1LL, (long long)kTargetCtas / std::max(1LL, nc));
-  const long long chunk = std::max(1LL, (ds + want - 1) / want);
-  p.chunk = (int)chunk;
-  p.chunks = (int)((ds + chunk - 1) / chunk);
-  p.threads = kS2Group * k;
+  p.chunk = 1;
+  p.chunks = (int)ds;
+  p.threads = (k <= 3 ? 2 * kS2Group : kS2Group) * k;
   return p;
 }
 inline DwS2Geom s2_geom_down(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w) {

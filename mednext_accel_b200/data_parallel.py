@@ -30,10 +30,11 @@ import torch.distributed as dist
 from torch import nn
 
 
-@dataclass
+@dataclass(eq=False)
 class _Bucket:
     params: list[nn.Parameter]
     buffer: torch.Tensor
+    index: int = 0
     pending: int = 0
     launched: bool = False
     works: list = field(default_factory=list)
@@ -58,10 +59,13 @@ class GradientBucketReducer:
             self.buckets.append(self._make(current))
         self.owner = {}
         for i, b in enumerate(self.buckets):
+            b.index = i
             for p in b.params:
                 self.owner[p] = i
         device = params[0].device
         self.stream = stream or (torch.cuda.Stream(device=device) if device.type == "cuda" else None)
+        # NCCL averages in the collective; gloo (CPU tests) has no AVG, so sum and scale
+        self.native_avg = (not dist.is_initialized()) or dist.get_backend(group) == "nccl"
         self.handles = [p.register_post_accumulate_grad_hook(self._hook) for p in params]
         self.order: list[int] = []
 
@@ -95,15 +99,22 @@ class GradientBucketReducer:
         if b.launched:
             return
         b.launched = True
-        self.order.append(self.buckets.index(b))
+        self.order.append(b.index)
         if self.world == 1:
             return
         if self.stream is None:
-            dist.all_reduce(b.buffer, op=dist.ReduceOp.AVG, group=self.group)
+            self._all_reduce_mean(b.buffer)
             return
         self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
-            dist.all_reduce(b.buffer, op=dist.ReduceOp.AVG, group=self.group)
+            self._all_reduce_mean(b.buffer)
+
+    def _all_reduce_mean(self, buf: torch.Tensor) -> None:
+        if self.native_avg:
+            dist.all_reduce(buf, op=dist.ReduceOp.AVG, group=self.group)
+        else:
+            dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group)
+            buf.div_(self.world)
 
     def finish(self) -> None:
         """Launch buckets whose parameters got no gradient and join the comm stream."""

@@ -1,0 +1,116 @@
+"""Per-operator timings of the sm_100a kernels at MedNeXt-Base level-0 shapes.
+
+    python -m mednext_accel_b200.microbench [CASE-SUBSTRING ...] [--reps N] [--warmup W] [--json]
+
+Each case is one library call (one or a few kernel launches) on inputs that are
+larger than the 126 MB L2.  The case is run W times untimed, then timed over N
+back-to-back repetitions with CUDA events on the current stream.  The reported GB/s
+divides the algorithmic bytes (every input element read once, every output element
+written once) by that time.  The same command under ``ncu -k <kernel>`` gives the
+per-kernel counters summarised in ``profiles/``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+import torch
+
+from . import _native as nat
+from . import depthwise as dwk
+from .pointwise import gn_stats, pw_gemm, pw_wgrad
+
+V = 128**3  # level-0 voxels
+C, RC = 32, 64  # level-0 channels and expanded channels (ratio 2)
+
+
+def _cases(dev: torch.device) -> dict[str, tuple]:
+    torch.manual_seed(0)
+    bf = torch.bfloat16
+
+    def r(*shape):
+        return torch.randn(*shape, device=dev).to(bf)
+
+    t, u, dy, du, x = r(1, C, V), r(1, RC, V), r(1, C, V), r(1, RC, V), r(1, C, V)
+    we, wp = r(RC, C) * 0.2, r(C, RC) * 0.2
+    b1, b2 = torch.randn(RC, device=dev), torch.randn(C, device=dev)
+    g, bb = torch.ones(C, device=dev), torch.zeros(C, device=dev)
+    stats = gn_stats(t, 1e-5)
+    wp_t, we_t = wp.t().contiguous(), we.t().contiguous()
+    vol = (1, C, 128, 128, 128)
+    x5, dy5 = x.view(vol), dy.view(vol)
+    w3 = (torch.randn(C, 1, 3, 3, 3, device=dev) * 0.2).to(bf)
+    w3b = (torch.randn(2 * C, 1, 3, 3, 3, device=dev) * 0.2).to(bf)
+    ys2 = r(1, C, 64, 64, 64)
+    xs, ybig = r(1, 2 * C, 64, 64, 64), r(1, 2 * C, 127, 127, 127)
+    up_bytes = 2 * C * 2 * (64**3 + 127**3)
+    return {
+        "pw expand fwd (GroupNorm prologue, bias)": (
+            lambda: pw_gemm(t, we, RC, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g, pro_beta=bb, bias=b1),
+            (C + RC) * 2 * V),
+        "pw project fwd (GELU prologue, bias, residual)": (
+            lambda: pw_gemm(u, wp, C, prologue=nat.PRO_GELU, bias=b2, residual=x), (RC + C + C) * 2 * V),
+        "pw project dgrad (GELU' epilogue)": (
+            lambda: pw_gemm(dy, wp_t, RC, aux=u, gelu_grad=True), (C + RC + RC) * 2 * V),
+        "pw expand dgrad (GroupNorm-backward sums)": (
+            lambda: pw_gemm(du, we_t, C, aux=t, gn_bwd_stats=stats), (RC + C + C) * 2 * V),
+        "pw project wgrad (GELU prologue)": (lambda: pw_wgrad(dy, u, prologue=nat.PRO_GELU), (C + RC) * 2 * V),
+        "pw expand wgrad (GroupNorm prologue)": (
+            lambda: pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g, pro_beta=bb),
+            (C + RC) * 2 * V),
+        "dw fwd C32 k3": (lambda: dwk.dw_forward(x5, w3, None, 3), 2 * C * 2 * V),
+        "dw dgrad C32 k3": (lambda: dwk.dw_dgrad(dy5, w3, 3), 2 * C * 2 * V),
+        "dw wgrad C32 k3": (lambda: dwk.dw_wgrad(x5, dy5, 3), 2 * C * 2 * V),
+        "s2 fwd C32 k3": (lambda: dwk.s2_forward(x5, w3, None, 3), C * 2 * V * 9 // 8),
+        "s2 dgrad C32 k3": (lambda: dwk.s2_dgrad(ys2, w3, (128, 128, 128), 3), C * 2 * V * 9 // 8),
+        "s2 wgrad C32 k3": (lambda: dwk.s2_wgrad(x5, ys2, 3), C * 2 * V * 9 // 8),
+        "dwT fwd C64 64^3->127^3 k3": (lambda: dwk.t_forward(xs, w3b, None, 3), up_bytes),
+        "dwT dgrad C64 k3": (lambda: dwk.t_dgrad(ybig, w3b, 3), up_bytes),
+        "dwT wgrad C64 k3": (lambda: dwk.t_wgrad(xs, ybig, 3), up_bytes),
+    }
+
+
+def run(patterns: list[str], reps: int = 10, warmup: int = 3) -> dict[str, dict]:
+    dev = torch.device("cuda", torch.cuda.current_device())
+    results = {}
+    for name, (fn, nbytes) in _cases(dev).items():
+        if patterns and not any(p in name for p in patterns):
+            continue
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        results[name] = {"us": round(ms * 1e3, 1), "GB/s": round(nbytes / ms / 1e6, 1), "bytes": nbytes}
+    return results
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("cases", nargs="*", help="substrings of case names (default: all)")
+    ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--json", action="store_true")
+    args = ap.parse_args(argv)
+    res = run(args.cases, args.reps, args.warmup)
+    if args.json:
+        print(json.dumps(res))
+    else:
+        for name, r in res.items():
+            print(f"{name:48s} {r['us']:9.1f} us {r['GB/s']:9.1f} GB/s")
+    err = nat.device_error()
+    if err:
+        print(f"device error word {err:#x}", file=sys.stderr)
+        return 1
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
