@@ -76,7 +76,8 @@ struct FwdEpi {
   static constexpr int threads = warps * 32;
 };
 constexpr int kMaxStages = 8;
-constexpr int kMaxEStages = 2;
+constexpr int kMaxEStages = 4;
+constexpr int kMaxAcc = 4;  // TMEM accumulator buffers between the MMA and the epilogue
 
 struct PwTmaCfg {
   int stages;       // A/B ring depth
@@ -86,14 +87,16 @@ struct PwTmaCfg {
   int aux_bytes;    // bytes of one aux tile (0 if unused)
   int res_bytes;    // bytes of one residual tile (0 if unused)
   int b_bytes;      // bytes of one W stage (BN * 128)
+  int nacc;         // TMEM accumulator buffers (1, 2 or 4)
+  int a_rows;       // channel rows per A box: min(64, roundup16(cin)); the MMA reads no further
 };
 
 struct PwTmaSmem {
   uint64_t full[kMaxStages];
   uint64_t ready[kMaxStages];
   uint64_t empty[kMaxStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[kMaxAcc];
+  uint64_t tempty[kMaxAcc];
   uint64_t efull[kMaxEStages];
   uint64_t eempty[kMaxEStages];
   uint32_t tmem_base;
@@ -109,7 +112,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   return true;
 }
 
-__device__ __forceinline__ uint32_t tmem_cols_for(int bn) {
+__host__ __device__ __forceinline__ uint32_t tmem_cols_for(int bn) {
   return bn <= 32 ? 32u : (bn <= 64 ? 64u : (bn <= 128 ? 128u : 256u));
 }
 
@@ -160,7 +163,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const uint32_t ncols = tmem_cols_for(BN);
   if (warp == 1) {
-    tmem_alloc(&sh.tmem_base, 2 * ncols);
+    tmem_alloc(&sh.tmem_base, (uint32_t)cfg.nacc * ncols);
     tmem_relinquish();
   }
   if (tid == 0) {
@@ -169,7 +172,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&sh.ready[i], kFwdProThreads);
       mbar_init(&sh.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < cfg.nacc; ++i) {
       mbar_init(&sh.tfull[i], 1);
       mbar_init(&sh.tempty[i], kEpiThreads);
     }
@@ -202,14 +205,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     v0 = (long long)mt * kPwBM;
   };
 
-  if (warp == 0) {
-    // ------------------------------------------------ TMA producer
-    if (lane == 0) {
+  if (warp == 2) {
+    // ------------------------------------------------ TMA producer of the epilogue operands
+    if (lane == 0 && (has_aux || has_res)) {
       for (int i = 0; i < ntile_local && !*abort; ++i) {
         int s, j0, mt;
         long long v0;
         decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
-        if (has_aux || has_res) {
+        {
           const int e = i % E, re = i / E;
           if (re > 0 && !wait_or_abort(&sh.eempty[e], (re - 1) & 1, abort)) break;
           mbar_arrive_expect_tx(&sh.efull[e], (uint32_t)(cfg.aux_bytes + cfg.res_bytes));
@@ -224,11 +227,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tma_load_3d(d + cfg.res_bytes / 2, &mRes, &sh.efull[e], (int)v0 + 64, j0, s);
           }
         }
+      }
+    }
+  } else if (warp == 0) {
+    // ------------------------------------------------ TMA producer of the A / W stages
+    if (lane == 0) {
+      for (int i = 0; i < ntile_local && !*abort; ++i) {
+        int s, j0, mt;
+        long long v0;
+        decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
         for (int kk = 0; kk < KS; ++kk) {
           const int q = i * KS + kk;
           const int st = q % S, r = q / S;
           if (r > 0 && !wait_or_abort(&sh.empty[st], (r - 1) & 1, abort)) break;
-          mbar_arrive_expect_tx(&sh.full[st], (uint32_t)(16384 + cfg.b_bytes));
+          mbar_arrive_expect_tx(&sh.full[st], (uint32_t)(2 * 128 * cfg.a_rows + cfg.b_bytes));
           uint8_t* a = ringA + (size_t)st * 16384;
           tma_load_3d(a, &mA, &sh.full[st], (int)v0, kk * kPwBK, s);
           tma_load_3d(a + 8192, &mA, &sh.full[st], (int)v0 + 64, kk * kPwBK, s);
@@ -241,7 +253,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(kPwBM, BN, std::is_same<TA, __nv_bfloat16>::value, true, false);
       for (int i = 0; i < ntile_local && !*abort; ++i) {
-        const int acc = i & 1, ra = i >> 1;
+        const int acc = i % cfg.nacc, ra = i / cfg.nacc;
         if (ra > 0 && !wait_or_abort(&sh.tempty[acc], (ra - 1) & 1, abort)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + (uint32_t)acc * ncols;
@@ -282,6 +294,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
           for (int ii = 0; ii < 4; ++ii) {
             const int kl = kr + 16 * ii;
+            if (kl >= cfg.a_rows) break;  // rows the TMA box does not cover are never read
             const int k = kk * kPwBK + kl;
             uint4* chunk = reinterpret_cast<uint4*>(a + kl * 128 + ((((mch & 7) ^ (kl & 7))) << 4));
             float v[8];
@@ -322,7 +335,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       int s, j0, mt;
       long long v0;
       decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
-      const int acc = i & 1, ra = i >> 1;
+      const int acc = i % cfg.nacc, ra = i / cfg.nacc;
       if (!wait_or_abort(&sh.tfull[acc], ra & 1, abort)) break;
       tc_fence_after();
       const int e = i % E, re = i / E;
@@ -398,7 +411,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, 2 * ncols);
+  if (warp == 1) tmem_dealloc(tmem, (uint32_t)cfg.nacc * ncols);
 }
 
 // ---------------------------------------------------------------- weight grad

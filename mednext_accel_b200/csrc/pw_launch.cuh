@@ -101,7 +101,9 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   if (!encode3<TY>(&mY, a.y, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 32, kPwCW,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
     return -1;
-  if (!encode3<TA>(&mA, a.a, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64, kPwBK, CU_TENSOR_MAP_SWIZZLE_128B))
+  const int a_rows = std::min(kPwBK, (a.cin + 15) / 16 * 16);
+  if (!encode3<TA>(&mA, a.a, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64, (uint32_t)a_rows,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
   if (!encode2<TA>(&mB, a.wt, (uint64_t)a.cin, (uint64_t)a.cout, kPwBK, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
@@ -112,6 +114,7 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
                               CU_TENSOR_MAP_SWIZZLE_NONE))
     return -1;
   PwTmaCfg cfg{};
+  cfg.a_rows = a_rows;
   cfg.kstages = (a.cin + kPwBK - 1) / kPwBK;
   cfg.total_tiles = a.S * a.ntiles * a.mtiles;
   cfg.b_bytes = a.BN * 128;
@@ -121,7 +124,15 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   const size_t ebytes = (size_t)cfg.aux_bytes + cfg.res_bytes;
   const size_t stg = (size_t)FwdEpi<PRO>::warps * 2 * 32 * kPwCW * sizeof(TY);  // epilogue staging, 2 per warp
   const size_t budget = kSmemBudget - stg;
-  cfg.estages = (2 * ebytes + 2 * per_stage <= budget) ? 2 : 1;
+  // up to 4 epilogue-operand stages while keeping at least 4 A/W stages
+  cfg.estages = 1;
+  if (ebytes > 0)
+    for (int e = kMaxEStages; e >= 1; --e)
+      if (e * ebytes + 4 * per_stage <= budget || e == 1) {
+        cfg.estages = e;
+        break;
+      }
+  cfg.nacc = (int)std::min<uint32_t>(kMaxAcc, 512u / tmem_cols_for(a.BN));
   const long long room = (long long)budget - (long long)cfg.estages * (long long)ebytes;
   cfg.stages = (int)std::min<long long>(kMaxStages, room / (long long)per_stage);
   if (cfg.stages < 2) return -1;
