@@ -224,7 +224,8 @@ __global__ void __launch_bounds__(kPwThreads) pw_fwd_kernel(PwFwdArgs p) {
   // wait for the last commit (all earlier MMAs complete before it)
   {
     const int last = nstage - 1;
-    if (!abort_sh && !mbar_wait(&mma_bar[last & 1], (last >> 1) & 1)) abort_sh = 1;
+    // always, also after an abort: no MMA may still read shared memory or write TMEM at exit
+    if (!mbar_wait(&mma_bar[last & 1], (last >> 1) & 1)) abort_sh = 1;
   }
   tc_fence_after();
   __syncthreads();
@@ -443,7 +444,8 @@ __global__ void __launch_bounds__(kPwThreads) pw_wgrad_kernel(PwWgradArgs p) {
   const bool any = st > 0;
   if (any) {
     const int last = st - 1;
-    if (!abort_sh && !mbar_wait(&mma_bar[last & 1], (last >> 1) & 1)) abort_sh = 1;
+    // always, also after an abort: no MMA may still read shared memory or write TMEM at exit
+    if (!mbar_wait(&mma_bar[last & 1], (last >> 1) & 1)) abort_sh = 1;
   }
   tc_fence_after();
   __syncthreads();

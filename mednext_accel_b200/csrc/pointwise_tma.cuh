@@ -87,7 +87,8 @@ struct PwTmaCfg {
   int aux_bytes;    // bytes of one aux tile (0 if unused)
   int res_bytes;    // bytes of one residual tile (0 if unused)
   int b_bytes;      // bytes of one W stage (BN * 128)
-  int nacc;         // TMEM accumulator buffers (1, 2 or 4)
+  int nacc;         // TMEM accumulator buffers (2 or 4)
+  int tgroups;      // epilogue warp groups on alternate tiles (1 or 2)
   int a_rows;       // channel rows per A box: min(64, roundup16(cin)); the MMA reads no further
 };
 
@@ -99,9 +100,25 @@ struct PwTmaSmem {
   uint64_t tempty[kMaxAcc];
   uint64_t efull[kMaxEStages];
   uint64_t eempty[kMaxEStages];
+  uint64_t drain;  // final tcgen05.commit: every MMA of the CTA has completed
   uint32_t tmem_base;
   int abort;
 };
+
+// Exit discipline: nothing asynchronous may still target the CTA's shared
+// memory or TMEM when it exits.  On the normal path every fill and every MMA has
+// been waited for by its consumer.  After an abort (a bounded wait gave up), the
+// roles meet at a CTA barrier, then each producer waits, bounded, for the last
+// fill of each ring slot it issued and the MMA issuer commits to `drain` and
+// waits for it, before TMEM is freed.
+__device__ __forceinline__ void drain_ring(uint64_t* full, int slots, long long issued) {
+  for (long long q = issued > slots ? issued - slots : 0; q < issued; ++q)
+    mbar_wait(&full[q % slots], (uint32_t)((q / slots) & 1));
+}
+__device__ __forceinline__ void drain_mma(uint64_t* drain) {
+  mma_commit(drain);
+  mbar_wait(drain, 0);
+}
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (*abort) return false;
@@ -174,12 +191,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     for (int i = 0; i < cfg.nacc; ++i) {
       mbar_init(&sh.tfull[i], 1);
-      mbar_init(&sh.tempty[i], kEpiThreads);
+      mbar_init(&sh.tempty[i], kEpiThreads / cfg.tgroups);
     }
     for (int i = 0; i < E; ++i) {
       mbar_init(&sh.efull[i], 1);
-      mbar_init(&sh.eempty[i], kEpiThreads);
+      mbar_init(&sh.eempty[i], kEpiThreads / cfg.tgroups);
     }
+    mbar_init(&sh.drain, 1);
     sh.abort = 0;
     fence_mbarrier_init();
   }
@@ -196,6 +214,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t tmem = sh.tmem_base;
   volatile int* abort = &sh.abort;
   const int ntile_local = (cfg.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  long long a_issued = 0, aux_issued = 0;  // TMA fills issued by the two producers
 
   auto decode = [&](int t, int& s, int& j0, long long& v0, int& mt) {
     mt = t % p.mtiles;
@@ -208,6 +227,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (warp == 2) {
     // ------------------------------------------------ TMA producer of the epilogue operands
     if (lane == 0 && (has_aux || has_res)) {
+      long long issued = 0;
       for (int i = 0; i < ntile_local && !*abort; ++i) {
         int s, j0, mt;
         long long v0;
@@ -226,12 +246,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             tma_load_3d(d, &mRes, &sh.efull[e], (int)v0, j0, s);
             tma_load_3d(d + cfg.res_bytes / 2, &mRes, &sh.efull[e], (int)v0 + 64, j0, s);
           }
+          ++issued;
         }
       }
+      aux_issued = issued;
     }
   } else if (warp == 0) {
     // ------------------------------------------------ TMA producer of the A / W stages
     if (lane == 0) {
+      long long issued = 0;
       for (int i = 0; i < ntile_local && !*abort; ++i) {
         int s, j0, mt;
         long long v0;
@@ -245,8 +268,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           tma_load_3d(a, &mA, &sh.full[st], (int)v0, kk * kPwBK, s);
           tma_load_3d(a + 8192, &mA, &sh.full[st], (int)v0 + 64, kk * kPwBK, s);
           tma_load_2d(ringB + (size_t)st * cfg.b_bytes, &mB, &sh.full[st], kk * kPwBK, j0);
+          ++issued;
         }
       }
+      a_issued = issued;
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
@@ -320,18 +345,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------ epilogue
-    // warp%4 selects the TMEM lane quarter (32 voxels); the warps of one quarter
-    // take turns over the 16-column chunks.  Every 32x16 result block is staged
-    // in shared memory and written with one TMA bulk tensor store
-    // (out-of-range rows and columns are clipped by the store).
-    constexpr int kGroups = FwdEpi<PRO>::warps / 4;
+    // Two groups of epilogue warps take alternate tiles, so the latency chain of
+    // one tile (TMEM load, staging, store issue) overlaps the next.  Within a
+    // group, warp%4 selects the TMEM lane quarter (32 voxels) and the warps of
+    // one quarter take turns over the 16-column chunks.  Every 32x16 result
+    // block is staged in shared memory and written with one TMA bulk tensor
+    // store (out-of-range rows and columns are clipped by the store).
+    const int tgs = cfg.tgroups;
+    const int kGroups = FwdEpi<PRO>::warps / 4 / tgs;
     const int ew = warp - kEpiWarp0;
     const int q4 = warp & 3;
-    const int cg = ew >> 2;
+    const int tg = (ew >> 2) % tgs;
+    const int cg = (ew >> 2) / tgs;
     const int epi = EPI >= 0 ? EPI : p.epilogue;
     uint8_t* stg0 = ringStg + (size_t)ew * 2 * kStgBytes;
     uint32_t nstored = 0;
-    for (int i = 0; i < ntile_local && !*abort; ++i) {
+    for (int i = tg; i < ntile_local && !*abort; i += tgs) {
       int s, j0, mt;
       long long v0;
       decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
@@ -408,6 +437,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (has_aux || has_res) mbar_arrive(&sh.eempty[e]);
     }
     if (lane == 0) bulk_wait_all();
+  }
+  __syncthreads();
+  if (*abort && lane == 0) {
+    if (warp == 0) drain_ring(sh.full, S, a_issued);
+    if (warp == 2) drain_ring(sh.efull, E, aux_issued);
+    if (warp == 1) drain_mma(&sh.drain);
   }
   tc_fence_before();
   __syncthreads();
@@ -486,6 +521,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
     }
     mbar_init(&sh.tfull[0], 1);
     mbar_init(&sh.tempty[0], 128);
+    mbar_init(&sh.drain, 1);
     sh.abort = 0;
     fence_mbarrier_init();
   }
@@ -499,6 +535,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
   const uint32_t tmem = sh.tmem_base;
   volatile int* abort = &sh.abort;
   const int nunits = (cfg.units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  long long g_issued = 0;  // TMA fills issued by the producer
 
   auto unit_range = [&](int u, int& mt, int& nt, int& sp, long long& cb, long long& ce) {
     mt = u % p.mtiles;
@@ -512,7 +549,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t tx = (uint32_t)(cfg.g_rows + cfg.a_rows) * 128u;
-      long long q = 0;
+      long long q = 0;  // fills issued
       for (int i = 0; i < nunits && !*abort; ++i) {
         int mt, nt, sp;
         long long cb, ce;
@@ -528,6 +565,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
           tma_load_3d(ringB + (size_t)st * cfg.b_bytes, &mA, &sh.full[st], v, nt * BN, s);
         }
       }
+      g_issued = q;
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -654,6 +692,11 @@ __global__ void __launch_bounds__(kWgThreads, 1)
       tc_fence_before();
       mbar_arrive(&sh.tempty[0]);
     }
+  }
+  __syncthreads();
+  if (*abort && lane == 0) {
+    if (warp == 0) drain_ring(sh.full, S, g_issued);
+    if (warp == 1) drain_mma(&sh.drain);
   }
   tc_fence_before();
   __syncthreads();

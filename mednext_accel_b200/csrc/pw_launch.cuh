@@ -124,14 +124,16 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   const size_t ebytes = (size_t)cfg.aux_bytes + cfg.res_bytes;
   const size_t stg = (size_t)FwdEpi<PRO>::warps * 2 * 32 * kPwCW * sizeof(TY);  // epilogue staging, 2 per warp
   const size_t budget = kSmemBudget - stg;
-  // up to 4 epilogue-operand stages while keeping at least 4 A/W stages
+  // Epilogue-operand ring: 4 or 2 stages while keeping at least 4 A/W stages,
+  // else 1.  Two epilogue warp groups take alternate tiles only when every ring
+  // slot then belongs to one group (an even ring, or none): a slot shared by two
+  // groups would let one of them wait on a phase parity two fills ahead.
   cfg.estages = 1;
-  if (ebytes > 0)
-    for (int e = kMaxEStages; e >= 1; --e)
-      if (e * ebytes + 4 * per_stage <= budget || e == 1) {
-        cfg.estages = e;
-        break;
-      }
+  if (ebytes > 0) {
+    if (4 * ebytes + 4 * per_stage <= budget) cfg.estages = 4;
+    else if (2 * ebytes + 4 * per_stage <= budget) cfg.estages = 2;
+  }
+  cfg.tgroups = (ebytes == 0 || cfg.estages % 2 == 0) ? 2 : 1;
   cfg.nacc = (int)std::min<uint32_t>(kMaxAcc, 512u / tmem_cols_for(a.BN));
   const long long room = (long long)budget - (long long)cfg.estages * (long long)ebytes;
   cfg.stages = (int)std::min<long long>(kMaxStages, room / (long long)per_stage);

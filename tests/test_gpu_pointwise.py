@@ -154,6 +154,38 @@ def test_pointwise_op_autograd():
     assert_close_bf16(db, wdb, "db")
 
 
+@pytest.mark.parametrize("cin,cout", [(64, 256), (256, 64), (32, 64)])
+def test_epilogue_rings_wrap_many_times_per_cta(cin, cout):
+    """2 x 64^3 voxels: every persistent CTA handles dozens of tiles, so the TMEM
+    accumulators and the epilogue-operand ring (1, 2 or 4 slots, one or two
+    epilogue groups depending on the tile width) wrap many times."""
+    n, vox = 2, 64**3
+    a = rand((n, cin, vox), 41)
+    w = rand((cout, cin), 42, scale=cin**-0.5)
+    u = rand((n, cout, vox), 43)
+    t = rand((n, cout, vox), 44)
+    stats = gn_stats(t.cuda(), 1e-5)
+    ag, wg, ug, tg = a.cuda(), w.cuda(), u.cuda(), t.cuda()
+    acc = torch.einsum("jk,skv->sjv", wg.float(), ag.float())
+    # GELU' epilogue: round the GEMM to bf16, then multiply by GELU'(u) (fp32)
+    du, _ = pw_gemm(ag, wg, cout, aux=ug, gelu_grad=True)
+    uu = ug.float().requires_grad_()
+    (gp,) = torch.autograd.grad(torch.nn.functional.gelu(uu), uu, torch.ones_like(uu))
+    want = (acc.to(torch.bfloat16).float() * gp).to(torch.bfloat16)
+    assert orc.rel_l2(h(du), h(want)) <= 4e-3
+    # GroupNorm-backward partial sums against torch on the same dz
+    from mednext_accel_b200.pointwise import gn_backward_from_partials
+
+    dz, part = pw_gemm(ag, wg, cout, aux=tg, gn_bwd_stats=stats)
+    assert orc.rel_l2(h(dz), h(acc.to(torch.bfloat16))) <= 2e-3
+    _, dg, db = gn_backward_from_partials(dz, tg, stats, torch.ones(cout, device="cuda"), part)
+    xhat = (tg.float() - stats[:, 0].view(n, cout, 1)) * stats[:, 1].view(n, cout, 1)
+    for got, terms in ((db, dz.float()), (dg, dz.float() * xhat)):
+        want, scale = terms.sum(dim=(0, 2)), terms.abs().sum(dim=(0, 2))
+        assert bool(((got - want).abs() <= 1e-5 * scale + 1e-3).all())
+    assert nat.device_error() == 0
+
+
 def _all_finite_bf16(channels):
     """Every finite bf16 value once, laid out as [1, channels, vox] (zero padded)."""
     bits = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
