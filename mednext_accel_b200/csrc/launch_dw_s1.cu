@@ -1,13 +1,62 @@
 // Template instantiation and launch of the depthwise kernels (stride 1) for every supported element type and kernel size.
+#include <type_traits>
+
+#include "depthwise_s1_tma.cuh"
 #include "plan.h"
+#include "tma_host.h"
 
 namespace mednext {
 
 namespace {
 
+// The TMA plane-ring kernels need rows of whole 16-byte chunks (W * sizeof(T) a
+// multiple of 16), a 16-byte aligned base and a plane tile within the 256-element
+// TMA box; fp64 and other shapes use the kernels of depthwise_s1.cuh.
+template <typename T, int K>
+bool s1_tma_ok(const void* base, const S1Plan& p) {
+  if constexpr (std::is_same<T, double>::value) {
+    return false;
+  } else {
+    const DwS1Geom& g = p.g;
+    const int P = K / 2;
+    return ((size_t)g.W * sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(base) & 15) == 0 &&
+           p.threads <= kDwMaxComputeWarps * 32 && DwTile<T>::row_elems(g.TW, P) <= 256 && g.TH + 2 * P <= 256;
+  }
+}
+
+template <typename T, int K>
+int try_s1_conv_tma(const void* x, const void* wgt, const void* bias, const void* addend, void* y, GnPartial* st,
+                    const S1Plan& p, int flip, cudaStream_t s) {
+  if constexpr (std::is_same<T, double>::value) {
+    return -1;
+  } else {
+    if (!s1_tma_ok<T, K>(x, p)) return -1;
+    constexpr int NH = K <= 3 ? 2 : 1;
+    using L = DwTmaLayout<T>;
+    const DwS1Geom& g = p.g;
+    CUtensorMap m;
+    if (!tma::encode4<T>(&m, x, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.D, (uint64_t)g.N * g.C,
+                         (uint32_t)DwTile<T>::row_elems(g.TW, K / 2), (uint32_t)(g.TH + 2 * (K / 2))))
+      return -1;
+    const size_t smem = 128 + L::weights(K, sizeof(typename Elem<T>::Acc)) + kDwSlots * L::slot(g, K, false);
+    auto kern = dw_s1_conv_tma_kernel<T, K, NH>;
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      configured = smem;
+    }
+    kern<<<(unsigned)p.grid, p.threads + 32, smem, s>>>(m, static_cast<const T*>(wgt), static_cast<const T*>(bias),
+                                                          static_cast<const T*>(addend), static_cast<T*>(y), st, p.g,
+                                                          flip);
+    return record_launch();
+  }
+}
+
 template <typename T, int K>
 int launch_s1_conv(const void* x, const void* wgt, const void* bias, const void* addend, void* y, GnPartial* st,
                    const S1Plan& p, int flip, cudaStream_t s) {
+  const int tst = try_s1_conv_tma<T, K>(x, wgt, bias, addend, y, st, p, flip, s);
+  if (tst != -1) return tst;
   constexpr int NH = K <= 3 ? 2 : 1;
   auto kern = dw_s1_conv_kernel<T, K, NH>;
   static size_t configured = 0;  // raise the opt-in limit once per instantiation
@@ -31,10 +80,41 @@ int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, i
 }
 
 template <typename T, int K>
+int try_s1_wgrad_tma(const void* x, const void* dy, typename Elem<T>::Acc* part, const S1Plan& p, cudaStream_t s) {
+  if constexpr (std::is_same<T, double>::value || K > 3) {
+    return -1;
+  } else {
+    if (!s1_tma_ok<T, K>(x, p) || (reinterpret_cast<uintptr_t>(dy) & 15) != 0) return -1;
+    constexpr int NH = K <= 3 ? 2 : 1;
+    using L = DwTmaLayout<T>;
+    const DwS1Geom& g = p.g;
+    CUtensorMap mx, mdy;
+    const uint64_t nc = (uint64_t)g.N * g.C;
+    if (!tma::encode4<T>(&mx, x, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.D, nc,
+                         (uint32_t)DwTile<T>::row_elems(g.TW, K / 2), (uint32_t)(g.TH + 2 * (K / 2))))
+      return -1;
+    if (!tma::encode4<T>(&mdy, dy, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.D, nc, (uint32_t)g.TW, (uint32_t)g.TH))
+      return -1;
+    const size_t smem = 128 + kDwSlots * L::slot(g, K, true);
+    auto kern = dw_s1_wgrad_tma_kernel<T, K, NH>;
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      configured = smem;
+    }
+    kern<<<(unsigned)p.grid, p.threads + 32, smem, s>>>(mx, mdy, part, p.g);
+    return record_launch();
+  }
+}
+
+template <typename T, int K>
 int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws, const S1Plan& p, cudaStream_t s) {
   using Acc = typename Elem<T>::Acc;
   constexpr int NH = K <= 3 ? 2 : 1;
   Acc* part = static_cast<Acc*>(ws);
+  const int tst = try_s1_wgrad_tma<T, K>(x, dy, part, p, s);
+  if (tst == MEDNEXT_OK) return finish_wgrad<T>(part, dw, db, p.g.N, p.g.C, (int)s1_tiles(p), K * K * K, s);
+  if (tst != -1) return tst;
   if constexpr (K <= 3) {
     auto kern = dw_s1_wgrad_kernel<T, K, NH>;
     static size_t configured = 0;  // raise the opt-in limit once per instantiation

@@ -29,39 +29,6 @@
 
 namespace mednext {
 
-// ------------------------------------------------------------------ TMA PTX
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
-                                            int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
-      : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Wait until at most N committed bulk groups still read shared memory.
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
 // forward kernel: warp 0 producer, warp 1 MMA, warps 4-11 prologue (when requested),
 // the remaining warps up to 19 epilogue
 constexpr int kFwdProWarp0 = 4;
@@ -360,15 +327,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int epi = EPI >= 0 ? EPI : p.epilogue;
     uint8_t* stg0 = ringStg + (size_t)ew * 2 * kStgBytes;
     uint32_t nstored = 0;
-    for (int i = tg; i < ntile_local && !*abort; i += tgs) {
+    for (int i = tg; i < ntile_local; i += tgs) {
       int s, j0, mt;
       long long v0;
       decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
       const int acc = i % cfg.nacc, ra = i / cfg.nacc;
-      if (!wait_or_abort(&sh.tfull[acc], ra & 1, abort)) break;
+      // warp-uniform waits: the warp issues tcgen05.ld and shuffles as a whole
+      if (!__all_sync(0xffffffffu, wait_or_abort(&sh.tfull[acc], ra & 1, abort))) break;
       tc_fence_after();
       const int e = i % E, re = i / E;
-      if ((has_aux || has_res) && !wait_or_abort(&sh.efull[e], re & 1, abort)) break;
+      if ((has_aux || has_res) && !__all_sync(0xffffffffu, wait_or_abort(&sh.efull[e], re & 1, abort))) break;
       const int vl = q4 * 32 + lane;  // voxel within the tile
       const TA* auxt = reinterpret_cast<const TA*>(ringAux + (size_t)e * cfg.aux_bytes + (vl >> 6) * (cfg.aux_bytes / 2)) + (vl & 63);
       const TY* rest = reinterpret_cast<const TY*>(ringRes + (size_t)e * cfg.res_bytes + (vl >> 6) * (cfg.res_bytes / 2)) + (vl & 63);
@@ -659,13 +627,13 @@ __global__ void __launch_bounds__(kWgThreads, 1)
     }
   } else if (warp >= kWgEpiWarp0) {
     const int q4 = warp & 3;
-    for (int i = 0; i < nunits && !*abort; ++i) {
+    for (int i = 0; i < nunits; ++i) {
       int mt, nt, sp;
       long long cb, ce;
       unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
       const bool any = ce > cb;
       // the MMA warp commits tfull once per unit, with or without MMAs
-      if (!wait_or_abort(&sh.tfull[0], (uint32_t)(i & 1), abort)) break;
+      if (!__all_sync(0xffffffffu, wait_or_abort(&sh.tfull[0], (uint32_t)(i & 1), abort))) break;  // warp-uniform
       tc_fence_after();
       const int j = mt * kPwBM + q4 * 32 + lane;
       float bval = 0.f;

@@ -11,59 +11,12 @@
 
 #include "plan.h"
 #include "pointwise_tma.cuh"
+#include "tma_host.h"
 
 namespace mednext {
 namespace pwl {
 
-// ------------------------------------------------------------------ TMA maps
-inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-template <typename T>
-inline CUtensorMapDataType tma_dtype();
-template <>
-inline CUtensorMapDataType tma_dtype<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
-template <>
-inline CUtensorMapDataType tma_dtype<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
-template <>
-inline CUtensorMapDataType tma_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
-
-// [d2][d1][d0] tensor, box (b0, b1, 1)
-template <typename T>
-inline bool encode3(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
-             CUtensorMapSwizzle sw) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[3] = {d0, d1, d2};
-  const cuuint64_t strides[2] = {d0 * sizeof(T), d0 * d1 * sizeof(T)};
-  const cuuint32_t box[3] = {b0, b1, 1};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return fn(m, tma_dtype<T>(), 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-template <typename T>
-inline bool encode2(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint32_t b0, uint32_t b1,
-             CUtensorMapSwizzle sw) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[2] = {d0, d1};
-  const cuuint64_t strides[1] = {d0 * sizeof(T)};
-  const cuuint32_t box[2] = {b0, b1};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(m, tma_dtype<T>(), 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
+using namespace tma;
 
 inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 constexpr size_t kSmemBudget = 220 * 1024;
