@@ -238,6 +238,27 @@ int mednext_gn_bwd_from_partials(const void* dz, const void* x, const float* sta
                                  int64_t pitch, int dz_dtype, int x_dtype, int dx_dtype,
                                  int gamma_dtype, mednext_stream_t stream);
 
+/* ---------------- parameter casts of the fused block ----------------
+ * No reference counterpart: under autocast the reference casts each fp32
+ * parameter separately at every use.  One launch casts a table of fp32 tensors;
+ * entry i reads src (rows x cols, fp32, 4-byte aligned) and writes dst:
+ *   out_dtype BFLOAT16 / FLOAT16: the value rounded to that type;
+ *   out_dtype FLOAT32: the value rounded to via_dtype (FLOAT32 = unchanged) and
+ *     stored as fp32, e.g. a bias that autocast rounds before an fp32 epilogue;
+ *   transpose != 0: dst is the cols x rows transpose.
+ * At most MEDNEXT_CAST_MAX_ENTRIES entries of fewer than 2^31 elements each. */
+#define MEDNEXT_CAST_MAX_ENTRIES 16
+typedef struct {
+  const float* src;
+  void* dst;
+  int64_t rows;
+  int64_t cols;
+  int out_dtype;
+  int via_dtype;
+  int transpose;
+} mednext_cast_entry;
+int mednext_cast_params(const mednext_cast_entry* entries, int count, mednext_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

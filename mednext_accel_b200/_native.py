@@ -93,11 +93,23 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _INT,
         [_P, _P, _P, _P, _INT, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _P],
     ),
+    "mednext_cast_params": (_INT, [_P, _INT, _P]),
     "mednext_gn_bwd_from_partials": (
         _INT,
         [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _INT, _INT, _INT, _INT, _P],
     ),
 }
+
+
+
+class CastEntry(ctypes.Structure):
+    """``mednext_cast_entry`` of the header."""
+
+    _fields_ = [("src", _P), ("dst", _P), ("rows", _I64), ("cols", _I64), ("out_dtype", _INT),
+                ("via_dtype", _INT), ("transpose", _INT)]
+
+
+CAST_MAX_ENTRIES = 16
 
 _lib: ctypes.CDLL | None = None
 _device_checked: set[int] = set()

@@ -22,6 +22,8 @@ as a single operator (:mod:`mednext_accel_b200.block`).
 
 from __future__ import annotations
 
+import dataclasses
+
 from dataclasses import dataclass
 
 import torch
@@ -152,14 +154,18 @@ class AdaptivePointwise3d(_AdaptiveConv3d):
 
     _mednext_accel_backend_kind = "pointwise_gemm"
 
-    def __init__(self, conv: nn.Conv3d, resolver: PolicyResolver, model_context: ModelOptimizationContext,
-                 *, role: str | None = None) -> None:
+    def __init__(self, conv: nn.Conv3d | nn.ConvTranspose3d, resolver: PolicyResolver,
+                 model_context: ModelOptimizationContext, *, role: str | None = None) -> None:
         super().__init__()
         self.weight = conv.weight
         self.bias = conv.bias
         for name in ("in_channels", "out_channels", "kernel_size", "stride", "padding", "dilation", "groups"):
             setattr(self, name, getattr(conv, name))
+        # a 1x1x1 transposed convolution is the pointwise contraction with weight [cin, cout]
+        self.transposed = isinstance(conv, nn.ConvTranspose3d)
         self.descriptor = conv_descriptor(conv, role=role)
+        if self.transposed:
+            self.descriptor = dataclasses.replace(self.descriptor, family="pointwise_conv3d", direction="regular")
         self.resolver = resolver
         self.model_context = model_context
         self.train(conv.training)
@@ -181,7 +187,10 @@ class AdaptivePointwise3d(_AdaptiveConv3d):
 
             cdt = getattr(torch, context.dtype)
             bias = self.bias.to(cdt) if self.bias is not None else None
-            return pointwise_conv3d(x.to(cdt), self.weight.to(cdt), bias)
+            weight = self.weight.transpose(0, 1) if self.transposed else self.weight
+            return pointwise_conv3d(x.to(cdt), weight.to(cdt), bias)
+        if self.transposed:
+            return F.conv_transpose3d(x, self.weight, self.bias)
         return F.conv3d(x, self.weight, self.bias)
 
 
@@ -242,8 +251,12 @@ class AdaptiveDepthwise3d(_AdaptiveConv3d):
 
 
 def _pointwise_eligible(module: nn.Module) -> bool:
+    """1x1x1, stride-1 Conv3d, or ConvTranspose3d (the output heads), which is the
+    same contraction with the weight's first two axes swapped."""
+    if type(module) is nn.ConvTranspose3d and module.output_padding != (0, 0, 0):
+        return False
     return (
-        type(module) is nn.Conv3d
+        type(module) in (nn.Conv3d, nn.ConvTranspose3d)
         and module.kernel_size == (1, 1, 1)
         and module.stride == (1, 1, 1)
         and module.padding == (0, 0, 0)

@@ -40,6 +40,69 @@ KIND_REGULAR, KIND_DOWN, KIND_UP = 0, 1, 2
 _CODES = {0: torch.float32, 1: torch.bfloat16, 2: torch.float16}
 
 
+class _Params:
+    """Compute-dtype copies of one block's parameters: depthwise weight and bias,
+    expand / project GEMM weights ([out, in]) and their biases rounded to the
+    compute dtype but kept fp32 for the epilogue, plus, for the backward, the
+    transposed GEMM weights of the input-grad GEMMs."""
+
+    __slots__ = ("wdw", "bdw", "ew", "eb", "pw", "pb", "ewt", "pwt")
+
+
+def _block_params(dw_w: Tensor, dw_b: Tensor | None, e_w: Tensor, e_b: Tensor, p_w: Tensor, p_b: Tensor | None,
+                  cdt, *, transposed: bool) -> _Params:
+    """All casts of a block in one ``mednext_cast_params`` launch (fp32 parameters),
+    else per-tensor casts.  Every GEMM weight starts on a 128-byte boundary, as the
+    TMA paths require.  ``dw_b`` / ``p_b`` may be None (the backward needs neither)."""
+    rc, c = int(e_w.shape[0]), int(e_w.shape[1])
+    cout = int(p_w.shape[0])
+    out = _Params()
+    params = [t for t in (dw_w, dw_b, e_w, e_b, p_w, p_b) if t is not None]
+    if not all(t.dtype == torch.float32 and t.is_contiguous() for t in params) or cdt == torch.float32:
+        out.wdw = dw_w.to(cdt).contiguous()
+        out.bdw = dw_b.to(cdt) if dw_b is not None else None
+        out.ew, out.eb = e_w.reshape(rc, c).to(cdt).contiguous(), e_b.to(cdt).float()
+        out.pw = p_w.reshape(cout, rc).to(cdt).contiguous()
+        out.pb = p_b.to(cdt).float() if p_b is not None else None
+        out.ewt = out.ew.t().contiguous() if transposed else None
+        out.pwt = out.pw.t().contiguous() if transposed else None
+        return out
+    code = nat.dtype_code(cdt)
+    f32 = nat.dtype_code(torch.float32)
+    # (name, src, rows, cols, transpose) in the compute dtype; offsets on 64-element boundaries
+    half = [("wdw", dw_w, c, dw_w[0].numel(), 0), ("ew", e_w, rc, c, 0), ("pw", p_w, cout, rc, 0)]
+    if dw_b is not None:
+        half.append(("bdw", dw_b, 1, c, 0))
+    if transposed:
+        half += [("ewt", e_w, rc, c, 1), ("pwt", p_w, cout, rc, 1)]
+    offs, total = [], 0
+    for _, _, r, k, _ in half:
+        offs.append(total)
+        total += (r * k + 63) // 64 * 64
+    buf = torch.empty(total, dtype=cdt, device=dw_w.device)
+    fbuf = torch.empty(rc + cout, dtype=torch.float32, device=dw_w.device)
+    out.bdw = out.pb = None
+    entries = []
+    for (name, src, r, k, tr), off in zip(half, offs, strict=True):
+        view = buf[off : off + r * k]
+        setattr(out, name, view)
+        entries.append(nat.CastEntry(src.data_ptr(), view.data_ptr(), r, k, code, f32, tr))
+    out.eb = fbuf[:rc]
+    entries.append(nat.CastEntry(e_b.data_ptr(), out.eb.data_ptr(), 1, rc, f32, code, 0))
+    if p_b is not None:
+        out.pb = fbuf[rc:]
+        entries.append(nat.CastEntry(p_b.data_ptr(), out.pb.data_ptr(), 1, cout, f32, code, 0))
+    table = (nat.CastEntry * len(entries))(*entries)
+    nat.check(nat.load().mednext_cast_params(table, len(entries), nat.stream()), "mednext_cast_params")
+    out.wdw = out.wdw.view(dw_w.shape)
+    out.ew, out.pw = out.ew.view(rc, c), out.pw.view(cout, rc)
+    if transposed:
+        out.ewt, out.pwt = out.ewt.view(c, rc), out.pwt.view(rc, cout)
+    else:
+        out.ewt = out.pwt = None
+    return out
+
+
 def _pitch(spatial: tuple[int, ...]) -> tuple[int, int]:
     """(voxels, row pitch rounded up to 8 elements = 16 bytes of bf16)."""
     vox = 1
@@ -55,12 +118,11 @@ def _depthwise_forward(xb: Tensor, w: Tensor, b: Tensor | None, kind: int, k: in
     return t, gn_stats(t, eps)
 
 
-def _expand(t: Tensor, stats: Tensor, gn_w: Tensor, gn_b: Tensor, e_w: Tensor, e_b: Tensor, cdt) -> Tensor:
-    rc = int(e_w.shape[0])
+def _expand(t: Tensor, stats: Tensor, gn_w: Tensor, gn_b: Tensor, prm: _Params, cdt) -> Tensor:
+    rc = int(prm.ew.shape[0])
     u, _ = pw_gemm(
-        t, e_w.reshape(rc, -1).to(cdt).contiguous(), rc, out_dtype=cdt, prologue=nat.PRO_GROUPNORM,
-        pro_stats=stats, pro_gamma=gn_w.float().contiguous(), pro_beta=gn_b.float().contiguous(),
-        bias=e_b.to(cdt).float(),
+        t, prm.ew, rc, out_dtype=cdt, prologue=nat.PRO_GROUPNORM, pro_stats=stats,
+        pro_gamma=gn_w.float().contiguous(), pro_beta=gn_b.float().contiguous(), bias=prm.eb,
     )
     return u
 
@@ -93,7 +155,8 @@ def mednext_block(
     tail, so that every GEMM operand has 16-byte aligned rows for TMA."""
     cdt = _CODES[compute_dtype]
     xb = x.to(cdt).contiguous()
-    wdw, bdw = dw_w.to(cdt).contiguous(), dw_b.to(cdt)
+    prm = _block_params(dw_w, dw_b, e_w, e_b, p_w, p_b, cdt, transposed=False)
+    wdw, bdw = prm.wdw, prm.bdw
     cout = int(p_w.shape[0])
     res = x if residual_is_input else addend
     if kind == KIND_UP:
@@ -101,25 +164,23 @@ def mednext_block(
         vox, pitch = _pitch(big)
         t = dwk.t_forward(xb, wdw, bdw, kernel_size, pitch=pitch)
         stats = gn_stats(t, eps, vox=vox)
-        u = _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
+        u = _expand(t, stats, gn_w, gn_b, prm, cdt)
         res_p = None
         if res is not None:
             res_p = torch.empty((x.shape[0], cout, pitch), dtype=res.dtype, device=x.device)
             dwk.pitched_view(res_p, big).copy_(res)
             res_p[:, :, vox:].zero_()
         y_p, _ = pw_gemm(
-            u, p_w.reshape(cout, -1).to(cdt).contiguous(), cout,
-            out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
-            bias=p_b.to(cdt).float(), residual=res_p,
+            u, prm.pw, cout, out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
+            bias=prm.pb, residual=res_p,
         )
         y = F.pad(dwk.pitched_view(y_p, big), (1, 0) * 3)
         return y, t, (u if keep_expansion else u.new_empty((0,))), stats
     t, stats = _depthwise_forward(xb, wdw, bdw, kind, kernel_size, eps)
-    u = _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
+    u = _expand(t, stats, gn_w, gn_b, prm, cdt)
     y, _ = pw_gemm(
-        u, p_w.reshape(cout, -1).to(cdt).contiguous(), cout,
-        out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
-        bias=p_b.to(cdt).float(), residual=res.contiguous() if res is not None else None,
+        u, prm.pw, cout, out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
+        bias=prm.pb, residual=res.contiguous() if res is not None else None,
     )
     return y, t, (u if keep_expansion else u.new_empty((0,))), stats
 
@@ -185,20 +246,19 @@ def mednext_block_backward(
         dy = dy.contiguous()
         dyb = dy.to(cdt)
     xb = x.to(cdt).contiguous()
-    u = u_saved if u_saved.numel() > 0 else _expand(t, stats, gn_w, gn_b, e_w, e_b, cdt)
+    prm = _block_params(dw_w, None, e_w, e_b, p_w, None, cdt, transposed=True)
+    u = u_saved if u_saved.numel() > 0 else _expand(t, stats, gn_w, gn_b, prm, cdt)
     # project dgrad with the GELU derivative in the epilogue
-    p_wt = p_w.reshape(cout, rc).to(cdt).t().contiguous()  # [rc, cout]
-    du, _ = pw_gemm(dyb, p_wt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
+    du, _ = pw_gemm(dyb, prm.pwt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
     # weight grads of both GEMMs (fp32, deterministic split-K)
     g_w = gn_w.float().contiguous()
     g_b = gn_b.float().contiguous()
     dpw, dpb = pw_wgrad(dyb, u, prologue=nat.PRO_GELU)
     dew, deb = pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g_w, pro_beta=g_b)
     # expand dgrad + GroupNorm-backward partial sums
-    e_wt = e_w.reshape(rc, c).to(cdt).t().contiguous()  # [c, rc]
-    dz, part = pw_gemm(du, e_wt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)
+    dz, part = pw_gemm(du, prm.ewt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)
     dt, dgamma, dbeta = gn_backward_from_partials(dz, t, stats, g_w, part, vox=vox)
-    wdw = dw_w.to(cdt).contiguous()
+    wdw = prm.wdw
     if kind == KIND_REGULAR:
         dx = dwk.dw_dgrad(dt, wdw, kernel_size, addend=dyb if residual_is_input and dy.dtype == cdt else None)
         dwdw, dbdw = dwk.dw_wgrad(xb, dt, kernel_size)
@@ -248,6 +308,9 @@ def _setup(ctx, inputs, output):
     y, t, u, stats = output
     ctx.save_for_backward(x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w)
     ctx.mark_non_differentiable(t, u, stats)
+    # t, u and stats never receive a gradient: without this, autograd would allocate
+    # and zero-fill tensors of their (expanded, full-resolution) shapes every step
+    ctx.set_materialize_grads(False)
     ctx.kind = kind
     ctx.k = k
     ctx.residual_is_input = residual_is_input

@@ -337,11 +337,19 @@ int mednext_gn_bwd_from_partials(const void* dz, const void* x, const float* sta
 }
 
 // ------------------------------ pointwise ------------------------------
-size_t mednext_pw_fwd_workspace_size(int64_t n, int64_t cin, int64_t cout, int64_t vox, int epilogue) {
-  if (!pw_shape_ok(n, cin, cout, vox)) return 0;
+// GroupNorm-backward partials (with MEDNEXT_EPI_GN_BWD_STATS), then, when cin is
+// not a multiple of 8, W padded to 8-element rows for the TMA kernels.
+size_t pw_fwd_gn_bytes(int64_t n, int64_t cout, int64_t vox, int epilogue) {
   if (!(epilogue & MEDNEXT_EPI_GN_BWD_STATS)) return 0;
   const int64_t mtiles = (vox + kPwBM - 1) / kPwBM;
-  return (size_t)n * cout * mtiles * 4 * sizeof(GnBwdPartial);
+  return align_up((size_t)n * cout * mtiles * 4 * sizeof(GnBwdPartial), 256);
+}
+size_t pw_fwd_wpad_bytes(int64_t cin, int64_t cout) {
+  return cin % 8 == 0 ? 0 : (size_t)cout * ((cin + 7) / 8 * 8) * 2;
+}
+size_t mednext_pw_fwd_workspace_size(int64_t n, int64_t cin, int64_t cout, int64_t vox, int epilogue) {
+  if (!pw_shape_ok(n, cin, cout, vox)) return 0;
+  return pw_fwd_gn_bytes(n, cout, vox, epilogue) + pw_fwd_wpad_bytes(cin, cout);
 }
 
 int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const float* pro_stats,
@@ -361,12 +369,10 @@ int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const f
   if ((epilogue & MEDNEXT_EPI_RESIDUAL) && residual == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   if ((epilogue & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) && aux == nullptr)
     return MEDNEXT_ERR_NULL_POINTER;
-  if (epilogue & MEDNEXT_EPI_GN_BWD_STATS) {
-    if (epi_stats == nullptr) return MEDNEXT_ERR_NULL_POINTER;
-    if (workspace == nullptr || !aligned16(workspace) ||
-        workspace_bytes < mednext_pw_fwd_workspace_size(n, cin, cout, vox, epilogue))
-      return MEDNEXT_ERR_WORKSPACE;
-  }
+  if ((epilogue & MEDNEXT_EPI_GN_BWD_STATS) && epi_stats == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t ws_need = mednext_pw_fwd_workspace_size(n, cin, cout, vox, epilogue);
+  if (ws_need > 0 && (workspace == nullptr || !aligned16(workspace) || workspace_bytes < ws_need))
+    return MEDNEXT_ERR_WORKSPACE;
   const size_t asz = elem_size(a_dtype), ysz = elem_size(y_dtype);
   if (!aligned(a, asz) || !aligned(wt, asz) || !aligned(y, ysz) || (residual && !aligned(residual, ysz)) ||
       (aux && !aligned(aux, asz)))
@@ -383,6 +389,8 @@ int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const f
   args.epilogue = epilogue;
   args.vec_a = (vox % 8 == 0) && aligned16(a);
   args.vec_w = (cin % 8 == 0) && aligned16(wt);
+  args.wpad = pw_fwd_wpad_bytes(cin, cout) > 0 ? static_cast<char*>(workspace) + pw_fwd_gn_bytes(n, cout, vox, epilogue)
+                                              : nullptr;
   if ((long long)args.S * args.ntiles * args.mtiles >= (1LL << 31)) return MEDNEXT_ERR_BAD_SHAPE;
   return dispatch_pw_fwd(a_dtype, y_dtype, prologue, args, as_stream(stream));
 }

@@ -43,7 +43,17 @@ struct PwFwdArgs {
   int epilogue;
   int vec_a;  // vox % 8 == 0 and aligned
   int vec_w;  // cin % 8 == 0 and aligned
+  void* wpad;  // workspace for W with rows padded to a multiple of 8 (cin % 8 != 0), or null
 };
+
+// W [cout][cin] -> [cout][cin8] with zero columns: TMA needs 16-byte row strides.
+template <typename T>
+static __global__ void pw_pad_weight_kernel(const T* __restrict__ w, T* __restrict__ out, int cout, int cin, int cin8) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)cout * cin8) return;
+  const int j = (int)(i / cin8), k = (int)(i - (long long)j * cin8);
+  out[i] = k < cin ? w[(size_t)j * cin + k] : from_acc<T>(0.0f);
+}
 
 __device__ __forceinline__ uint32_t sw128_kmajor_off(int row, int chunk) {
   // 8-row x 128-byte atoms stacked along rows; 16-byte chunk index XOR row%8.

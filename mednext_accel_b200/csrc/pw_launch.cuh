@@ -43,7 +43,20 @@ inline void set_smem(K kern, size_t smem, size_t& configured) {
 // Returns MEDNEXT_OK when launched, -1 when the shape is not TMA-describable.
 template <typename TA, typename TY, int PRO, int EPI>
 int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
-  if (a.vox % 8 != 0 || a.cin % 8 != 0 || !a16(a.a) || !a16(a.wt)) return -1;
+  if (a.vox % 8 != 0 || !a16(a.a) || !a16(a.wt)) return -1;
+  // W rows must be whole 16-byte chunks for its tensor map: pad them in the workspace
+  const void* wt = a.wt;
+  int wk = a.cin;
+  if (a.cin % 8 != 0) {
+    if (a.wpad == nullptr || !a16(a.wpad)) return -1;
+    wk = (a.cin + 7) / 8 * 8;
+    const long long total = (long long)a.cout * wk;
+    pw_pad_weight_kernel<TA><<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+        static_cast<const TA*>(a.wt), static_cast<TA*>(a.wpad), a.cout, a.cin, wk);
+    const int st = record_launch();
+    if (st != MEDNEXT_OK) return st;
+    wt = a.wpad;
+  }
   const bool has_aux = (a.epilogue & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) != 0;
   const bool has_res = (a.epilogue & MEDNEXT_EPI_RESIDUAL) != 0;
   if ((has_aux && !a16(a.aux)) || (has_res && !a16(a.residual))) return -1;
@@ -58,7 +71,7 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   if (!encode3<TA>(&mA, a.a, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64, (uint32_t)a_rows,
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
-  if (!encode2<TA>(&mB, a.wt, (uint64_t)a.cin, (uint64_t)a.cout, kPwBK, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!encode2<TA>(&mB, wt, (uint64_t)wk, (uint64_t)a.cout, kPwBK, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
   if (has_aux && !encode3<TA>(&mAux, a.aux, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, (uint32_t)a.BN,
                               CU_TENSOR_MAP_SWIZZLE_NONE))

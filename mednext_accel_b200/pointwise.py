@@ -63,10 +63,10 @@ def pw_gemm(
         epi |= nat.EPI_RESIDUAL
     if gelu_grad:
         epi |= nat.EPI_GELU_GRAD
-    ws = None
     if gn_bwd_stats is not None:
         epi |= nat.EPI_GN_BWD_STATS
-        ws = nat.workspace(lib.mednext_pw_fwd_workspace_size(n, cin, cout, vox, epi), a.device)
+    ws_bytes = lib.mednext_pw_fwd_workspace_size(n, cin, cout, vox, epi)
+    ws = nat.workspace(ws_bytes, a.device) if ws_bytes > 0 else None
     nat.check(
         lib.mednext_pw_fwd(
             a.data_ptr(), wt.data_ptr(), y.data_ptr(), prologue, nat.ptr(pro_stats), nat.ptr(pro_gamma),
