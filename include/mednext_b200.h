@@ -155,8 +155,11 @@ int mednext_dw_wgrad_noalloc(const void* x, const void* dy, void* dweight, void*
 int mednext_dw_s2_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n,
                       int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
                       mednext_stream_t stream);
-int mednext_dw_s2_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c,
-                        int64_t d, int64_t h, int64_t w, int k, int dtype,
+/* addend_even: NULL, or a tensor of dy's shape added to dx at the all-even
+ * positions 2m: the input grad of the down block's 1x1, stride-2 residual
+ * convolution (models/blocks.py:128-136), which samples the input there. */
+int mednext_dw_s2_dgrad(const void* dy, const void* weight, const void* addend_even, void* dx,
+                        int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
                         mednext_stream_t stream);
 size_t mednext_dw_s2_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
                                           int k, int dtype);
@@ -173,9 +176,19 @@ int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbia
 int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n,
                     int64_t c, int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype,
                     mednext_stream_t stream);
-int mednext_dwT_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c,
-                      int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype,
-                      mednext_stream_t stream);
+/* addend: NULL, or a tensor of dx's shape added to dx: the input grad of the up
+ * block's 1x1, stride-2 transposed residual convolution (models/blocks.py:173-182). */
+int mednext_dwT_dgrad(const void* dy, const void* weight, const void* addend, void* dx, int64_t n,
+                      int64_t c, int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k,
+                      int dtype, mednext_stream_t stream);
+/* Stride-2 expansion onto the up block's (2d-1, 2h-1, 2w-1) grid (pitch as above):
+ * big[2m] = small[m] at the all-even positions, bias[c] (fp32, NULL = 0) at all
+ * others, zeros in the pitch tail.  With small = W x + bias from the pointwise
+ * GEMM this is the output of the up block's ConvTranspose3d(1x1x1, stride 2)
+ * residual branch (models/blocks.py:173-182). */
+int mednext_upsample2_fill(const void* small, const float* bias, void* big, int64_t n, int64_t c,
+                           int64_t d, int64_t h, int64_t w, int64_t big_pitch, int dtype,
+                           mednext_stream_t stream);
 size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
                                         int k, int dtype);
 int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,

@@ -316,7 +316,7 @@ class FusedBlockRunner:
         decision = self.decision(block, x)
         if decision.implementation == "reference":
             return None
-        from .block import dtype_code, mednext_block
+        from .block import KIND_REGULAR, dtype_code, mednext_block
 
         cdt = compute_dtype(x)
         if cdt not in _AUTOCAST_COMPUTE:
@@ -324,10 +324,15 @@ class FusedBlockRunner:
         if not x.is_contiguous():
             x = x.contiguous()
         keep = not (block.checkpoint_expansion or decision.parameters.get("recompute_expansion", False))
+        # the down / up blocks' strided 1x1 residual convolution runs inside the operator
+        res = getattr(block, "residual", None) if self.kind != KIND_REGULAR and addend is None else None
+        res_w = res.weight if res is not None else None
+        res_b = res.bias if res is not None else None
         y, _, _, _ = mednext_block(
             x, addend, block.depthwise.weight, block.depthwise.bias, block.norm.weight, block.norm.bias,
-            block.expand.weight, block.expand.bias, block.project.weight, block.project.bias, self.kind,
-            int(block.depthwise.kernel_size[0]), float(block.norm.eps), bool(residual_is_input), keep, dtype_code(cdt),
+            block.expand.weight, block.expand.bias, block.project.weight, block.project.bias, res_w, res_b,
+            self.kind, int(block.depthwise.kernel_size[0]), float(block.norm.eps), bool(residual_is_input), keep,
+            dtype_code(cdt),
         )
         return y
 

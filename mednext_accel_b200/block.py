@@ -46,19 +46,28 @@ class _Params:
     compute dtype but kept fp32 for the epilogue, plus, for the backward, the
     transposed GEMM weights of the input-grad GEMMs."""
 
-    __slots__ = ("wdw", "bdw", "ew", "eb", "pw", "pb", "ewt", "pwt")
+    __slots__ = ("wdw", "bdw", "ew", "eb", "pw", "pb", "ewt", "pwt", "rw", "rb")
 
 
 def _block_params(dw_w: Tensor, dw_b: Tensor | None, e_w: Tensor, e_b: Tensor, p_w: Tensor, p_b: Tensor | None,
-                  cdt, *, transposed: bool) -> _Params:
+                  cdt, *, transposed: bool, res: tuple[Tensor, bool] | None = None,
+                  res_b: Tensor | None = None) -> _Params:
     """All casts of a block in one ``mednext_cast_params`` launch (fp32 parameters),
     else per-tensor casts.  Every GEMM weight starts on a 128-byte boundary, as the
-    TMA paths require.  ``dw_b`` / ``p_b`` may be None (the backward needs neither)."""
+    TMA paths require.  ``dw_b`` / ``p_b`` may be None (the backward needs neither).
+    ``res`` = (residual conv weight, transpose): its [rows, cols] matrix is cast to
+    ``rw`` as is or transposed; ``res_b`` becomes ``rb`` (rounded, fp32)."""
     rc, c = int(e_w.shape[0]), int(e_w.shape[1])
     cout = int(p_w.shape[0])
     out = _Params()
-    params = [t for t in (dw_w, dw_b, e_w, e_b, p_w, p_b) if t is not None]
+    out.rw = out.rb = None
+    params = [t for t in (dw_w, dw_b, e_w, e_b, p_w, p_b, res_b, res[0] if res else None) if t is not None]
     if not all(t.dtype == torch.float32 and t.is_contiguous() for t in params) or cdt == torch.float32:
+        if res is not None:
+            r2 = res[0].reshape(res[0].shape[0], res[0].shape[1])
+            out.rw = (r2.t() if res[1] else r2).to(cdt).contiguous()
+        if res_b is not None:
+            out.rb = res_b.to(cdt).float()
         out.wdw = dw_w.to(cdt).contiguous()
         out.bdw = dw_b.to(cdt) if dw_b is not None else None
         out.ew, out.eb = e_w.reshape(rc, c).to(cdt).contiguous(), e_b.to(cdt).float()
@@ -71,6 +80,8 @@ def _block_params(dw_w: Tensor, dw_b: Tensor | None, e_w: Tensor, e_b: Tensor, p
     f32 = nat.dtype_code(torch.float32)
     # (name, src, rows, cols, transpose) in the compute dtype; offsets on 64-element boundaries
     half = [("wdw", dw_w, c, dw_w[0].numel(), 0), ("ew", e_w, rc, c, 0), ("pw", p_w, cout, rc, 0)]
+    if res is not None:
+        half.append(("rw", res[0], int(res[0].shape[0]), int(res[0].shape[1]), int(res[1])))
     if dw_b is not None:
         half.append(("bdw", dw_b, 1, c, 0))
     if transposed:
@@ -80,7 +91,8 @@ def _block_params(dw_w: Tensor, dw_b: Tensor | None, e_w: Tensor, e_b: Tensor, p
         offs.append(total)
         total += (r * k + 63) // 64 * 64
     buf = torch.empty(total, dtype=cdt, device=dw_w.device)
-    fbuf = torch.empty(rc + cout, dtype=torch.float32, device=dw_w.device)
+    nrb = int(res_b.numel()) if res_b is not None else 0
+    fbuf = torch.empty(rc + cout + nrb, dtype=torch.float32, device=dw_w.device)
     out.bdw = out.pb = None
     entries = []
     for (name, src, r, k, tr), off in zip(half, offs, strict=True):
@@ -90,17 +102,28 @@ def _block_params(dw_w: Tensor, dw_b: Tensor | None, e_w: Tensor, e_b: Tensor, p
     out.eb = fbuf[:rc]
     entries.append(nat.CastEntry(e_b.data_ptr(), out.eb.data_ptr(), 1, rc, f32, code, 0))
     if p_b is not None:
-        out.pb = fbuf[rc:]
+        out.pb = fbuf[rc : rc + cout]
         entries.append(nat.CastEntry(p_b.data_ptr(), out.pb.data_ptr(), 1, cout, f32, code, 0))
+    if res_b is not None:
+        out.rb = fbuf[rc + cout :]
+        entries.append(nat.CastEntry(res_b.data_ptr(), out.rb.data_ptr(), 1, nrb, f32, code, 0))
     table = (nat.CastEntry * len(entries))(*entries)
     nat.check(nat.load().mednext_cast_params(table, len(entries), nat.stream()), "mednext_cast_params")
     out.wdw = out.wdw.view(dw_w.shape)
     out.ew, out.pw = out.ew.view(rc, c), out.pw.view(cout, rc)
+    if res is not None:
+        r0, r1 = int(res[0].shape[0]), int(res[0].shape[1])
+        out.rw = out.rw.view((r1, r0) if res[1] else (r0, r1))
     if transposed:
         out.ewt, out.pwt = out.ewt.view(c, rc), out.pwt.view(rc, cout)
     else:
         out.ewt = out.pwt = None
     return out
+
+
+def _even(x: Tensor) -> Tensor:
+    """x at the all-even positions, contiguous: the input of a 1x1x1 stride-2 conv."""
+    return x[:, :, ::2, ::2, ::2].contiguous()
 
 
 def _pitch(spatial: tuple[int, ...]) -> tuple[int, int]:
@@ -139,6 +162,8 @@ def mednext_block(
     e_b: Tensor,
     p_w: Tensor,
     p_b: Tensor,
+    res_w: Tensor | None,
+    res_b: Tensor | None,
     kind: int,
     kernel_size: int,
     eps: float,
@@ -152,10 +177,18 @@ def mednext_block(
     For the up block (kind 2) y is the final, left-padded (2S)^3 output of the
     reference's ``F.pad(block(x) + residual(x))`` and t, u are pitched
     [n, c, pitch] buffers whose rows hold the (2S-1)^3 voxels followed by a zero
-    tail, so that every GEMM operand has 16-byte aligned rows for TMA."""
+    tail, so that every GEMM operand has 16-byte aligned rows for TMA.
+
+    ``res_w`` / ``res_b`` (down and up blocks, instead of ``addend``): the 1x1x1
+    stride-2 residual convolution (models/blocks.py:128-136, 173-182) computed here
+    on the pointwise GEMM: the down block's reads x at the even positions, the up
+    block's product on the small grid is expanded onto the big grid with the bias
+    at the odd positions."""
     cdt = _CODES[compute_dtype]
     xb = x.to(cdt).contiguous()
-    prm = _block_params(dw_w, dw_b, e_w, e_b, p_w, p_b, cdt, transposed=False)
+    # the down block's residual weight is [cout, cin]; the transposed up block's is [cin, cout]
+    rmode = (res_w, kind == KIND_UP) if res_w is not None else None
+    prm = _block_params(dw_w, dw_b, e_w, e_b, p_w, p_b, cdt, transposed=False, res=rmode, res_b=res_b)
     wdw, bdw = prm.wdw, prm.bdw
     cout = int(p_w.shape[0])
     res = x if residual_is_input else addend
@@ -166,7 +199,11 @@ def mednext_block(
         stats = gn_stats(t, eps, vox=vox)
         u = _expand(t, stats, gn_w, gn_b, prm, cdt)
         res_p = None
-        if res is not None:
+        if res_w is not None:
+            rs, _ = pw_gemm(xb, prm.rw, cout, out_dtype=cdt, bias=prm.rb)
+            res_p = dwk.upsample2_fill(rs, prm.rb, pitch)
+            res = res_p
+        elif res is not None:
             res_p = torch.empty((x.shape[0], cout, pitch), dtype=res.dtype, device=x.device)
             dwk.pitched_view(res_p, big).copy_(res)
             res_p[:, :, vox:].zero_()
@@ -177,6 +214,8 @@ def mednext_block(
         y = F.pad(dwk.pitched_view(y_p, big), (1, 0) * 3)
         return y, t, (u if keep_expansion else u.new_empty((0,))), stats
     t, stats = _depthwise_forward(xb, wdw, bdw, kind, kernel_size, eps)
+    if res_w is not None and kind == KIND_DOWN:
+        res, _ = pw_gemm(_even(xb), prm.rw, cout, out_dtype=cdt, bias=prm.rb)
     u = _expand(t, stats, gn_w, gn_b, prm, cdt)
     y, _ = pw_gemm(
         u, prm.pw, cout, out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
@@ -186,13 +225,13 @@ def mednext_block(
 
 
 @mednext_block.register_fake
-def _(x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, kind, kernel_size, eps, residual_is_input,
+def _(x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, res_w, res_b, kind, kernel_size, eps, residual_is_input,
       keep_expansion, compute_dtype):
     cdt = _CODES[compute_dtype]
     n, c = x.shape[0], x.shape[1]
     sp = tuple(x.shape[2:])
     res = x if residual_is_input else addend
-    ydt = res.dtype if res is not None else cdt
+    ydt = res.dtype if res is not None and res_w is None else cdt
     if kind == KIND_UP:
         big = tuple(2 * s - 1 for s in sp)
         _, pitch = _pitch(big)
@@ -222,13 +261,14 @@ def mednext_block_backward(
     e_w: Tensor,
     e_b: Tensor,
     p_w: Tensor,
+    res_w: Tensor | None,
     kind: int,
     kernel_size: int,
     residual_is_input: bool,
     compute_dtype: int,
-) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
-    """Returns (dx, dw_w, dw_b, dgamma, dbeta, de_w, de_b, dp_w, dp_b) in the
-    parameters' dtypes."""
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (dx, dw_w, dw_b, dgamma, dbeta, de_w, de_b, dp_w, dp_b, dres_w, dres_b)
+    in the parameters' dtypes (the last two empty without ``res_w``)."""
     cdt = _CODES[compute_dtype]
     rc, c = int(e_w.shape[0]), int(e_w.shape[1])
     cout = int(p_w.shape[0])
@@ -246,7 +286,9 @@ def mednext_block_backward(
         dy = dy.contiguous()
         dyb = dy.to(cdt)
     xb = x.to(cdt).contiguous()
-    prm = _block_params(dw_w, None, e_w, e_b, p_w, None, cdt, transposed=True)
+    # input grad of the residual GEMM: the down block needs W^T [cin, cout], the up block W [cin, cout]
+    rmode = (res_w, kind == KIND_DOWN) if res_w is not None else None
+    prm = _block_params(dw_w, None, e_w, e_b, p_w, None, cdt, transposed=True, res=rmode)
     u = u_saved if u_saved.numel() > 0 else _expand(t, stats, gn_w, gn_b, prm, cdt)
     # project dgrad with the GELU derivative in the epilogue
     du, _ = pw_gemm(dyb, prm.pwt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
@@ -259,14 +301,30 @@ def mednext_block_backward(
     dz, part = pw_gemm(du, prm.ewt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)
     dt, dgamma, dbeta = gn_backward_from_partials(dz, t, stats, g_w, part, vox=vox)
     wdw = prm.wdw
+    drw = drb = dxr = None
+    if res_w is not None:
+        cin = int(x.shape[1])
+        if kind == KIND_DOWN:
+            # residual out[m] = W x[2m] + b: its grad is dy on the small grid
+            drw, drb = pw_wgrad(dyb, _even(xb))
+            dxr, _ = pw_gemm(dyb, prm.rw, cin, out_dtype=cdt)  # added at the even positions of dx
+        else:
+            # residual out[2m] = W^T x[m] + b, out[odd] = b: the weight and input grads see dy at
+            # the even interior positions (odd in the left-padded output); the bias grad is the
+            # sum of dy over the whole interior, which the project GEMM's bias grad already is
+            dye = dy[:, :, 1::2, 1::2, 1::2].to(cdt).contiguous()
+            drw_t, _ = pw_wgrad(dye, xb, want_bias=False)  # [cout, cin]
+            drw = drw_t.t()
+            drb = dpb.clone()
+            dxr, _ = pw_gemm(dye, prm.rw, cin, out_dtype=cdt)
     if kind == KIND_REGULAR:
         dx = dwk.dw_dgrad(dt, wdw, kernel_size, addend=dyb if residual_is_input and dy.dtype == cdt else None)
         dwdw, dbdw = dwk.dw_wgrad(xb, dt, kernel_size)
     elif kind == KIND_DOWN:
-        dx = dwk.s2_dgrad(dt, wdw, tuple(int(s) for s in x.shape[2:]), kernel_size)
+        dx = dwk.s2_dgrad(dt, wdw, tuple(int(s) for s in x.shape[2:]), kernel_size, addend_even=dxr)
         dwdw, dbdw = dwk.s2_wgrad(xb, dt, kernel_size)
     else:
-        dx = dwk.t_dgrad(dt, wdw, kernel_size, small=tuple(int(s) for s in x.shape[2:]))
+        dx = dwk.t_dgrad(dt, wdw, kernel_size, small=tuple(int(s) for s in x.shape[2:]), addend=dxr)
         dwdw, dbdw = dwk.t_wgrad(xb, dt, kernel_size)
     if dx.dtype != x.dtype:
         dx = dx.to(x.dtype)
@@ -285,11 +343,15 @@ def mednext_block_backward(
         deb.to(e_b.dtype),
         dpw.reshape(p_w.shape).to(p_w.dtype),
         dpb.to(p_w.dtype),
+        drw.reshape(res_w.shape).to(res_w.dtype) if drw is not None else dpw.new_empty((0,)),
+        drb.to(res_w.dtype) if drb is not None else dpw.new_empty((0,)),
     )
 
 
 @mednext_block_backward.register_fake
-def _(dy, x, t, u_saved, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, kind, kernel_size, residual_is_input, compute_dtype):
+def _(dy, x, t, u_saved, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w, kind, kernel_size, residual_is_input,
+      compute_dtype):
+    nres = 0 if res_w is None else res_w.shape[1] if kind == KIND_UP else res_w.shape[0]
     return (
         torch.empty_like(x),
         torch.empty_like(dw_w),
@@ -300,13 +362,16 @@ def _(dy, x, t, u_saved, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, kind, kernel_si
         torch.empty_like(e_b),
         torch.empty_like(p_w),
         p_w.new_empty((p_w.shape[0],)),
+        torch.empty_like(res_w) if res_w is not None else p_w.new_empty((0,)),
+        p_w.new_empty((nres,)),
     )
 
 
 def _setup(ctx, inputs, output):
-    (x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, kind, k, eps, residual_is_input, keep, cdt) = inputs
+    (x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, res_w, res_b, kind, k, eps, residual_is_input, keep,
+     cdt) = inputs
     y, t, u, stats = output
-    ctx.save_for_backward(x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w)
+    ctx.save_for_backward(x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w)
     ctx.mark_non_differentiable(t, u, stats)
     # t, u and stats never receive a gradient: without this, autograd would allocate
     # and zero-fill tensors of their (expanded, full-resolution) shapes every step
@@ -320,15 +385,19 @@ def _setup(ctx, inputs, output):
 
 
 def _backward(ctx, dy, _dt, _du, _dstats):
-    x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w = ctx.saved_tensors
-    dx, dww, dwb, dgw, dgb, dew, deb, dpw, dpb = mednext_block_backward(
-        dy, x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, ctx.kind, ctx.k, ctx.residual_is_input, ctx.cdt
+    if dy is None:  # the block output does not reach the loss
+        return (None,) * 18
+    x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w = ctx.saved_tensors
+    dx, dww, dwb, dgw, dgb, dew, deb, dpw, dpb, drw, drb = mednext_block_backward(
+        dy, x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w, ctx.kind, ctx.k, ctx.residual_is_input, ctx.cdt
     )
+    if res_w is None:
+        drw = drb = None
     d_add = None
     if ctx.has_addend and ctx.needs_input_grad[1]:
         g = dy[:, :, 1:, 1:, 1:] if ctx.kind == KIND_UP else dy  # the up block's output is left-padded
         d_add = g if g.dtype == ctx.addend_dtype else g.to(ctx.addend_dtype)
-    return dx, d_add, dww, dwb, dgw, dgb, dew, deb, dpw, dpb, None, None, None, None, None, None
+    return dx, d_add, dww, dwb, dgw, dgb, dew, deb, dpw, dpb, drw, drb, None, None, None, None, None, None
 
 
 mednext_block.register_autograd(_backward, setup_context=_setup)

@@ -184,17 +184,20 @@ int mednext_dw_s2_fwd(const void* x, const void* weight, const void* bias, void*
   const size_t esz = elem_size(dtype);
   if (!aligned(x, esz) || !aligned(y, esz) || !aligned(weight, esz) || (bias && !aligned(bias, esz)))
     return MEDNEXT_ERR_ALIGNMENT;
-  return dispatch_dw_s2_gather(dtype, k, x, weight, bias, y, s2_geom_down(n, c, d, h, w), as_stream(stream));
+  return dispatch_dw_s2_gather(dtype, k, x, weight, bias, nullptr, y, s2_geom_down(n, c, d, h, w),
+                               as_stream(stream));
 }
 
-int mednext_dw_s2_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c, int64_t d, int64_t h,
-                        int64_t w, int k, int dtype, mednext_stream_t stream) {
+int mednext_dw_s2_dgrad(const void* dy, const void* weight, const void* addend_even, void* dx, int64_t n, int64_t c,
+                        int64_t d, int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
   if (dy == nullptr || weight == nullptr || dx == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
-  if (!aligned(dy, esz) || !aligned(dx, esz) || !aligned(weight, esz)) return MEDNEXT_ERR_ALIGNMENT;
-  return dispatch_dw_s2_scatter(dtype, k, dy, weight, nullptr, dx, s2_geom_down(n, c, d, h, w), as_stream(stream));
+  if (!aligned(dy, esz) || !aligned(dx, esz) || !aligned(weight, esz) || (addend_even && !aligned(addend_even, esz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_dw_s2_scatter(dtype, k, dy, weight, nullptr, addend_even, dx, s2_geom_down(n, c, d, h, w),
+                                as_stream(stream));
 }
 
 size_t mednext_dw_s2_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
@@ -229,19 +232,32 @@ int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y
   const size_t esz = elem_size(dtype);
   if (!aligned(x, esz) || !aligned(y, esz) || !aligned(weight, esz) || (bias && !aligned(bias, esz)))
     return MEDNEXT_ERR_ALIGNMENT;
-  return dispatch_dw_s2_scatter(dtype, k, x, weight, bias, y, s2_geom_up(n, c, d, h, w, big_pitch), as_stream(stream));
+  return dispatch_dw_s2_scatter(dtype, k, x, weight, bias, nullptr, y, s2_geom_up(n, c, d, h, w, big_pitch),
+                                as_stream(stream));
 }
 
-int mednext_dwT_dgrad(const void* dy, const void* weight, void* dx, int64_t n, int64_t c, int64_t d, int64_t h,
-                      int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
+int mednext_dwT_dgrad(const void* dy, const void* weight, const void* addend, void* dx, int64_t n, int64_t c,
+                      int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
   if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
   if (dy == nullptr || weight == nullptr || dx == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
-  if (!aligned(dy, esz) || !aligned(dx, esz) || !aligned(weight, esz)) return MEDNEXT_ERR_ALIGNMENT;
-  return dispatch_dw_s2_gather(dtype, k, dy, weight, nullptr, dx, s2_geom_up(n, c, d, h, w, big_pitch),
+  if (!aligned(dy, esz) || !aligned(dx, esz) || !aligned(weight, esz) || (addend && !aligned(addend, esz)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_dw_s2_gather(dtype, k, dy, weight, nullptr, addend, dx, s2_geom_up(n, c, d, h, w, big_pitch),
                                as_stream(stream));
+}
+
+int mednext_upsample2_fill(const void* small, const float* bias, void* big, int64_t n, int64_t c, int64_t d,
+                           int64_t h, int64_t w, int64_t big_pitch, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, 1, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
+  if (small == nullptr || big == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(small, esz) || !aligned(big, esz) || (bias && !aligned(bias, 4))) return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_upsample2_fill(dtype, small, bias, big, s2_geom_up(n, c, d, h, w, big_pitch), as_stream(stream));
 }
 
 size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {

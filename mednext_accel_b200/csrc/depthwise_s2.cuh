@@ -65,6 +65,7 @@ template <typename T, int K>
 __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_gather_kernel(const T* __restrict__ big,
                                                                      const T* __restrict__ wgt,
                                                                      const T* __restrict__ bias,
+                                                                     const T* __restrict__ addend,
                                                                      T* __restrict__ small, DwS2Geom g) {
   using Acc = typename Elem<T>::Acc;
   constexpr int P = K / 2;
@@ -100,6 +101,8 @@ __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_gather_kernel(const T* __
           }
         }
       }
+      if (addend != nullptr)
+        acc += to_acc<T>(addend[(((size_t)nc * g.Ds + md) * g.Hs + mh) * g.Ws + mw]);
       dst[(size_t)mh * g.Ws + mw] = from_acc<T>(acc);
     }
   }
@@ -120,11 +123,13 @@ struct S2Block {
 };
 
 // scatter: CTA = (n, c, qd) pair of big-grid planes 2qd, 2qd+1; warps take block
-// rows, lanes run along W; each thread writes a 2x2x2 output block.
+// rows, lanes run along W; each thread writes a 2x2x2 output block.  add_even
+// (small-grid shaped, may be null) is added at the all-even output 2q.
 template <typename T, int K>
 __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_scatter_kernel(const T* __restrict__ small,
                                                                       const T* __restrict__ wgt,
                                                                       const T* __restrict__ bias,
+                                                                      const T* __restrict__ add_even,
                                                                       T* __restrict__ big, DwS2Geom g) {
   using Acc = typename Elem<T>::Acc;
   using B = S2Block<K>;
@@ -189,6 +194,8 @@ __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_scatter_kernel(const T* _
               }
             }
             const int iw = 2 * qw + ew;
+            if (add_even != nullptr && ed == 0 && eh == 0 && ew == 0)
+              acc += to_acc<T>(add_even[(((size_t)nc * g.Ds + qd) * g.Hs + qh) * g.Ws + qw]);
             if (id < g.Db && ih < g.Hb && iw < g.Wb) row[iw] = from_acc<T>(acc);
           }
         }
@@ -199,6 +206,34 @@ __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_scatter_kernel(const T* _
   const size_t bvol_elems = (size_t)g.Db * g.Hb * g.Wb;
   if (qd == QD - 1) {
     for (size_t e = bvol_elems + threadIdx.x; e < (size_t)g.bp; e += blockDim.x) bvol[e] = from_acc<T>(Acc(0));
+  }
+}
+
+// Stride-2 expansion of a small grid onto the big grid of the up block:
+// big[2m] = small[m] at the all-even positions, bias[c] (0 without bias) at the
+// others, zeros in the pitch tail.  This is the layout of a ConvTranspose3d with a
+// 1x1x1 kernel and stride 2 once its per-voxel product (small, bias included) is
+// done.  CTA = (n, c, id) big-grid plane; warps take rows, lanes run along W.
+template <typename T>
+__global__ void __launch_bounds__(kS2Warps * 32) upsample2_fill_kernel(const T* __restrict__ small,
+                                                                       const float* __restrict__ bias,
+                                                                       T* __restrict__ big, DwS2Geom g) {
+  const int id = (int)(blockIdx.x % (unsigned)g.Db);
+  const int nc = (int)(blockIdx.x / (unsigned)g.Db);
+  const T fill = from_acc<T>(bias != nullptr ? bias[nc % g.C] : 0.0f);
+  const T* src = small + ((size_t)nc * g.Ds + (id >> 1)) * ((size_t)g.Hs * g.Ws);
+  T* bvol = big + (size_t)nc * (size_t)g.bp;
+  T* dst = bvol + (size_t)id * g.Hb * g.Wb;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int ih = warp; ih < g.Hb; ih += kS2Warps) {
+    const bool even_row = ((id | ih) & 1) == 0;
+    const T* srow = src + (size_t)(ih >> 1) * g.Ws;
+    for (int iw = lane; iw < g.Wb; iw += 32)
+      dst[(size_t)ih * g.Wb + iw] = (even_row && (iw & 1) == 0) ? srow[iw >> 1] : fill;
+  }
+  const size_t bvol_elems = (size_t)g.Db * g.Hb * g.Wb;
+  if (id == g.Db - 1) {
+    for (size_t e = bvol_elems + threadIdx.x; e < (size_t)g.bp; e += blockDim.x) bvol[e] = from_acc<T>(0.0f);
   }
 }
 

@@ -18,19 +18,31 @@ int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, i
 bool grid_ok(long long ctas) { return ctas > 0 && ctas < (1LL << 31); }
 
 template <typename T, int K>
-int launch_gather(const void* big, const void* w, const void* b, void* small, const DwS2Geom& g, cudaStream_t s) {
+int launch_gather(const void* big, const void* w, const void* b, const void* addend, void* small, const DwS2Geom& g,
+                  cudaStream_t s) {
   const long long ctas = (long long)g.N * g.C * g.Ds;
   if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
   dw_s2_gather_kernel<T, K><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(
-      static_cast<const T*>(big), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(small), g);
+      static_cast<const T*>(big), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<const T*>(addend),
+      static_cast<T*>(small), g);
   return record_launch();
 }
 template <typename T, int K>
-int launch_scatter(const void* small, const void* w, const void* b, void* big, const DwS2Geom& g, cudaStream_t s) {
+int launch_scatter(const void* small, const void* w, const void* b, const void* add_even, void* big,
+                   const DwS2Geom& g, cudaStream_t s) {
   const long long ctas = (long long)g.N * g.C * ((g.Db + 1) / 2);
   if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
   dw_s2_scatter_kernel<T, K><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(
-      static_cast<const T*>(small), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<T*>(big), g);
+      static_cast<const T*>(small), static_cast<const T*>(w), static_cast<const T*>(b),
+      static_cast<const T*>(add_even), static_cast<T*>(big), g);
+  return record_launch();
+}
+template <typename T>
+int launch_upsample2_fill(const void* small, const float* bias, void* big, const DwS2Geom& g, cudaStream_t s) {
+  const long long ctas = (long long)g.N * g.C * g.Db;
+  if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
+  upsample2_fill_kernel<T><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(static_cast<const T*>(small), bias,
+                                                                    static_cast<T*>(big), g);
   return record_launch();
 }
 template <typename T, int K>
@@ -75,16 +87,23 @@ int launch_s2_wgrad(const void* big, const void* small, void* dw, void* db, void
     default: return MEDNEXT_ERR_BAD_DTYPE;                                   \
   }
 
-int dispatch_dw_s2_gather(int dtype, int k, const void* big, const void* w, const void* b, void* small,
-                          const DwS2Geom& g, cudaStream_t s) {
+int dispatch_dw_s2_gather(int dtype, int k, const void* big, const void* w, const void* b, const void* addend,
+                          void* small, const DwS2Geom& g, cudaStream_t s) {
   int st = MEDNEXT_OK;
-  MEDNEXT_T_SWITCH(dtype, T, MEDNEXT_K_SWITCH(k, KC, st = (launch_gather<T, KC>(big, w, b, small, g, s))));
+  MEDNEXT_T_SWITCH(dtype, T, MEDNEXT_K_SWITCH(k, KC, st = (launch_gather<T, KC>(big, w, b, addend, small, g, s))));
   return st;
 }
-int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, const void* b, void* big,
-                           const DwS2Geom& g, cudaStream_t s) {
+int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, const void* b, const void* add_even,
+                           void* big, const DwS2Geom& g, cudaStream_t s) {
   int st = MEDNEXT_OK;
-  MEDNEXT_T_SWITCH(dtype, T, MEDNEXT_K_SWITCH(k, KC, st = (launch_scatter<T, KC>(small, w, b, big, g, s))));
+  MEDNEXT_T_SWITCH(dtype, T,
+                   MEDNEXT_K_SWITCH(k, KC, st = (launch_scatter<T, KC>(small, w, b, add_even, big, g, s))));
+  return st;
+}
+int dispatch_upsample2_fill(int dtype, const void* small, const float* bias, void* big, const DwS2Geom& g,
+                            cudaStream_t s) {
+  int st = MEDNEXT_OK;
+  MEDNEXT_T_SWITCH(dtype, T, st = (launch_upsample2_fill<T>(small, bias, big, g, s)));
   return st;
 }
 int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,

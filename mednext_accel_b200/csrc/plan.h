@@ -156,9 +156,13 @@ int dispatch_dw_s1_conv(int dtype, int k, const void* x, const void* w, const vo
                         GnPartial* stats, const S1Plan& p, int flip, cudaStream_t s);
 int dispatch_dw_s1_wgrad(int dtype, int k, const void* x, const void* dy, void* dw, void* db, void* ws,
                          const S1Plan& p, cudaStream_t s);
-int dispatch_dw_s2_gather(int dtype, int k, const void* big, const void* w, const void* b, void* small,
+int dispatch_upsample2_fill(int dtype, const void* small, const float* bias, void* big, const DwS2Geom& g,
+                            cudaStream_t s);
+int dispatch_dw_s2_gather(int dtype, int k, const void* big, const void* w, const void* b, const void* addend,
+                          void* small,
                           const DwS2Geom& g, cudaStream_t s);
-int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, const void* b, void* big,
+int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, const void* b,
+                           const void* add_even, void* big,
                            const DwS2Geom& g, cudaStream_t s);
 int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,
                          const DwS2Geom& g, bool bias_from_big, cudaStream_t s);

@@ -109,14 +109,20 @@ def s2_forward(x: Tensor, weight: Tensor, bias: Tensor | None, kernel_size: int)
     return y
 
 
-def s2_dgrad(grad: Tensor, weight: Tensor, input_size: tuple[int, int, int], kernel_size: int) -> Tensor:
+def s2_dgrad(grad: Tensor, weight: Tensor, input_size: tuple[int, int, int], kernel_size: int,
+             addend_even: Tensor | None = None) -> Tensor:
+    """Input grad of the stride-2 depthwise conv; ``addend_even`` (grad's shape) is
+    added at the all-even input positions (the strided 1x1 residual's input grad)."""
     nat.require_device(grad)
     n, c = int(grad.shape[0]), int(grad.shape[1])
     d, h, w = (int(v) for v in input_size)
+    if addend_even is not None:
+        _check_addend(addend_even, grad.shape, grad.dtype, "addend_even")
+        addend_even = addend_even.contiguous()
     out = torch.empty((n, c, d, h, w), dtype=grad.dtype, device=grad.device)
     nat.check(
         nat.load().mednext_dw_s2_dgrad(
-            grad.data_ptr(), weight.data_ptr(), out.data_ptr(), n, c, d, h, w, kernel_size,
+            grad.data_ptr(), weight.data_ptr(), nat.ptr(addend_even), out.data_ptr(), n, c, d, h, w, kernel_size,
             nat.dtype_code(grad.dtype), nat.stream(),
         ),
         "mednext_dw_s2_dgrad",
@@ -167,9 +173,11 @@ def pitched_view(buf: Tensor, spatial: tuple[int, int, int]) -> Tensor:
     return buf[:, :, :vox].unflatten(2, spatial)
 
 
-def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int, small: tuple[int, int, int] | None = None) -> Tensor:
+def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int, small: tuple[int, int, int] | None = None,
+            addend: Tensor | None = None) -> Tensor:
     """Input grad of the transposed conv.  ``grad`` is [n, c, 2d-1, 2h-1, 2w-1], or a
-    pitched [n, c, pitch] buffer when ``small`` = (d, h, w) is given."""
+    pitched [n, c, pitch] buffer when ``small`` = (d, h, w) is given.  ``addend``
+    (the output's shape) is added to the result."""
     nat.require_device(grad)
     n, c = int(grad.shape[0]), int(grad.shape[1])
     pitch = 0
@@ -180,9 +188,12 @@ def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int, small: tuple[int, in
         _, _, od, oh, ow = _dims(grad)
         d, h, w = (od + 1) // 2, (oh + 1) // 2, (ow + 1) // 2
     out = torch.empty((n, c, d, h, w), dtype=grad.dtype, device=grad.device)
+    if addend is not None:
+        _check_addend(addend, out.shape, out.dtype, "addend")
+        addend = addend.contiguous()
     nat.check(
         nat.load().mednext_dwT_dgrad(
-            grad.data_ptr(), weight.data_ptr(), out.data_ptr(), n, c, d, h, w, pitch, kernel_size,
+            grad.data_ptr(), weight.data_ptr(), nat.ptr(addend), out.data_ptr(), n, c, d, h, w, pitch, kernel_size,
             nat.dtype_code(grad.dtype), nat.stream(),
         ),
         "mednext_dwT_dgrad",
@@ -212,6 +223,31 @@ def t_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True) -
 
 
 # --------------------------------------------------------------------------- low-level API
+def _check_addend(t: Tensor, shape, dtype, name: str) -> None:
+    if not t.is_cuda or tuple(t.shape) != tuple(shape) or t.dtype != dtype:
+        raise ValueError(f"{name} must be a CUDA tensor of shape {tuple(shape)} and dtype {dtype}")
+
+
+def upsample2_fill(small: Tensor, bias: Tensor | None, pitch: int) -> Tensor:
+    """[n, c, pitch] buffer holding the (2d-1, 2h-1, 2w-1) grid with small[m] at the
+    all-even positions 2m, bias[c] elsewhere and a zero pitch tail: the output of a
+    1x1x1, stride-2 ConvTranspose3d whose per-voxel product (bias included) is
+    ``small`` [n, c, d, h, w]."""
+    nat.require_device(small)
+    n, c, d, h, w = _dims(small)
+    small = small.contiguous()
+    big = torch.empty((n, c, int(pitch)), dtype=small.dtype, device=small.device)
+    b = bias.float().contiguous() if bias is not None else None
+    nat.check(
+        nat.load().mednext_upsample2_fill(
+            small.data_ptr(), nat.ptr(b), big.data_ptr(), n, c, d, h, w, int(pitch), nat.dtype_code(small.dtype),
+            nat.stream(),
+        ),
+        "mednext_upsample2_fill",
+    )
+    return big
+
+
 def _check_pair(a: Tensor, b: Tensor, names: str) -> None:
     if not (a.is_cuda and b.is_cuda):
         raise ValueError("CUDA tensors are required")

@@ -265,10 +265,11 @@ class MedNeXtDownBlock(MedNeXtBlock):
         self.residual = conv(in_channels, out_channels, kernel_size=1, stride=2) if residual else None
 
     def forward(self, x: Tensor) -> Tensor:
-        skip = self.residual(x) if self.residual is not None else None
-        out = self._fused_call(x, skip, False)
+        # the fused operator computes the strided residual convolution itself
+        out = self._fused_call(x, None, False)
         if out is not None:
             return out
+        skip = self.residual(x) if self.residual is not None else None
         y = self._body(x)
         return y + skip if skip is not None else y
 
@@ -304,10 +305,12 @@ class MedNeXtUpBlock(MedNeXtBlock):
         self._pad = (1, 0) * spatial_dims
 
     def forward(self, x: Tensor) -> Tensor:
-        skip = self.residual(x) if self.residual is not None else None
-        out = self._fused_call(x, skip, False)
+        # the fused operator computes the strided residual convolution itself and
+        # returns the padded output
+        out = self._fused_call(x, None, False)
         if out is not None:
-            return out  # the fused operator returns the padded output
+            return out
+        skip = self.residual(x) if self.residual is not None else None
         out = self._body(x)
         if skip is not None:
             out = out + skip

@@ -125,6 +125,22 @@ def test_fused_block_matches_oracle(kind, cin, cout, ratio, k, shape):
     # the depthwise bias grad is sum(dt), analytically zero under GroupNorm(C, C)
     got = grads["depthwise.bias"].double().cpu().numpy()
     assert np.all(np.abs(got - want["depthwise.bias"]) <= BAR * want["depthwise.bias_scale"])
+    if kind in ("down", "up"):
+        # the strided 1x1 residual convolution runs inside the fused operator
+        xb = orc.round_bf16(x.double().numpy())
+        dyn = dy.double().numpy()
+        if kind == "down":
+            # out[m] = W x[2m] + b: dW = sum dy (x) x_even, db = sum dy
+            _, want_rw, want_rb = orc.pointwise_bwd(dyn, np.ascontiguousarray(xb[:, :, ::2, ::2, ::2]),
+                                                    block.residual.weight.detach().double().numpy()[:, :, 0, 0, 0])
+        else:
+            # out[2m] = W^T x[m] + b on the (2S-1)^3 interior of the left-padded output
+            inner = dyn[:, :, 1:, 1:, 1:]
+            want_rw = np.einsum("ncdhw,nkdhw->ck", xb, inner[:, :, ::2, ::2, ::2])
+            want_rb = inner.sum(axis=(0, 2, 3, 4))
+        got_rw = grads["residual.weight"].double().cpu().numpy().reshape(want_rw.shape)
+        assert orc.rel_l2(got_rw, want_rw) <= BAR, orc.rel_l2(got_rw, want_rw)
+        assert orc.rel_l2(grads["residual.bias"].double().cpu().numpy(), want_rb) <= BAR
 
 
 def test_checkpointed_expansion_matches_stored():
