@@ -389,4 +389,45 @@ __device__ __forceinline__ float gelu_grad_f(float x) {
   return fmaf(x, 0.39894228040143267794f * e, x >= 0.f ? 1.0f - tail : tail);
 }
 
+// The same two functions on pairs with the packed fp32 instructions (FFMA2 /
+// FMUL2 / FADD2): every lane rounds exactly as the scalar fmaf / mul / add, so
+// the results are bit-identical to gelu_f / gelu_grad_f with half the FMA-pipe
+// instructions.
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 abs2(float2 x) { return make_float2(fabsf(x.x), fabsf(x.y)); }
+__device__ __forceinline__ float2 gelu2(float2 x) {
+  const float2 z = __fmul2_rn(abs2(x), f2(0.70710678118654752440f));
+  const float2 den = __ffma2_rn(f2(0.5f), z, f2(1.0f));
+  const float2 t = make_float2(rcp_approx(den.x), rcp_approx(den.y));
+  float2 p = __ffma2_rn(t, f2(0.17087277f), f2(-0.82215223f));
+  p = __ffma2_rn(t, p, f2(1.48851587f));
+  p = __ffma2_rn(t, p, f2(-1.13520398f));
+  p = __ffma2_rn(t, p, f2(0.27886807f));
+  p = __ffma2_rn(t, p, f2(-0.18628806f));
+  p = __ffma2_rn(t, p, f2(0.09678418f));
+  p = __ffma2_rn(t, p, f2(0.37409196f));
+  p = __ffma2_rn(t, p, f2(1.00002368f));
+  p = __ffma2_rn(t, p, f2(-1.26551223f));
+  const float2 arg = __fmul2_rn(__ffma2_rn(make_float2(-z.x, -z.y), z, p), f2(1.44269504088896340736f));
+  const float2 e = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));
+  const float2 tail = __fmul2_rn(__fmul2_rn(f2(0.5f), t), e);
+  const float2 one_m = __fadd2_rn(f2(1.0f), make_float2(-tail.x, -tail.y));
+  return __fmul2_rn(x, make_float2(x.x >= 0.f ? one_m.x : tail.x, x.y >= 0.f ? one_m.y : tail.y));
+}
+__device__ __forceinline__ float2 gelu_grad2(float2 x) {
+  const float2 xx = __fmul2_rn(__fmul2_rn(x, x), f2(-0.72134752044448170368f));
+  const float2 e = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+  const float2 z = __fmul2_rn(abs2(x), f2(0.70710678118654752440f));
+  const float2 den = __ffma2_rn(f2(0.3275911f), z, f2(1.0f));
+  const float2 t = make_float2(rcp_approx(den.x), rcp_approx(den.y));
+  float2 p = __ffma2_rn(t, f2(1.061405429f), f2(-1.453152027f));
+  p = __ffma2_rn(t, p, f2(1.421413741f));
+  p = __ffma2_rn(t, p, f2(-0.284496736f));
+  p = __ffma2_rn(t, p, f2(0.254829592f));
+  const float2 tail = __fmul2_rn(__fmul2_rn(__fmul2_rn(f2(0.5f), t), p), e);
+  const float2 one_m = __fadd2_rn(f2(1.0f), make_float2(-tail.x, -tail.y));
+  const float2 cdf = make_float2(x.x >= 0.f ? one_m.x : tail.x, x.y >= 0.f ? one_m.y : tail.y);
+  return __ffma2_rn(x, __fmul2_rn(f2(0.39894228040143267794f), e), cdf);
+}
+
 }  // namespace mednext

@@ -63,7 +63,7 @@ int mednext_cast_params(const mednext_cast_entry* entries, int count, mednext_st
     t.e[i] = e;
     most = std::max(most, e.rows * e.cols);
   }
-  const unsigned bx = (unsigned)std::min<int64_t>((most + 255) / 256, 64);
+  const unsigned bx = (unsigned)std::min<int64_t>((most + 255) / 256, 1024);
   cast_params_kernel<<<dim3(bx, (unsigned)count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(t);
   return record_launch();
 }

@@ -80,7 +80,11 @@ __device__ __forceinline__ void pw_prologue(float* v, float ca, float cb) {
     for (int i = 0; i < 8; ++i) v[i] = fmaf(v[i], ca, cb);
   } else if constexpr (PRO == MEDNEXT_PRO_GELU) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = gelu_f(v[i]);
+    for (int i = 0; i < 8; i += 2) {
+      const float2 g = gelu2(make_float2(v[i], v[i + 1]));
+      v[i] = g.x;
+      v[i + 1] = g.y;
+    }
   }
 }
 

@@ -359,6 +359,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         __syncwarp();
         tmem_ld_wait();
         float s1[kPwCW], s2[kPwCW];
+        float gg[kPwCW];  // GELU'(aux) of the chunk's columns, in pairs
+        if (epi & MEDNEXT_EPI_GELU_GRAD) {
+#pragma unroll
+          for (int jj = 0; jj < kPwCW; jj += 2) {
+            const float2 g = gelu_grad2(
+                make_float2(to_acc<TA>(auxt[(c0 + jj) * 64]), to_acc<TA>(auxt[(c0 + jj + 1) * 64])));
+            gg[jj] = g.x;
+            gg[jj + 1] = g.y;
+          }
+        }
 #pragma unroll
         for (int jj = 0; jj < kPwCW; ++jj) {
           const int jl = c0 + jj;
@@ -366,8 +376,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (epi & MEDNEXT_EPI_BIAS) a += __shfl_sync(0xffffffffu, bias_l, jj);
           if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_RESIDUAL)) a = to_acc<TA>(from_acc<TA>(a));
           float ax = 0.f;
-          if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) ax = to_acc<TA>(auxt[jl * 64]);
-          if (epi & MEDNEXT_EPI_GELU_GRAD) a *= gelu_grad_f(ax);
+          if (epi & MEDNEXT_EPI_GN_BWD_STATS) ax = to_acc<TA>(auxt[jl * 64]);
+          if (epi & MEDNEXT_EPI_GELU_GRAD) a *= gg[jj];
           if (epi & MEDNEXT_EPI_RESIDUAL) a += (float)to_acc<TY>(rest[jl * 64]);
           const TY o = from_acc<TY>((typename Elem<TY>::Acc)a);
           stg[jj * 32 + lane] = o;

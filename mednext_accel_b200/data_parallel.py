@@ -4,17 +4,20 @@ The reference has no distributed code; MedNeXt training shards naturally over
 the batch, so the only exchange per step is the average of the parameter
 gradients.  Design (one process per GPU, ``torch.distributed`` with NCCL):
 
-* parameters are packed, in reverse registration order (roughly the order their
-  gradients become final during backward), into flat fp32 buckets of about
-  ``bucket_cap_mb``; every ``param.grad`` is a view into its bucket, so no copy
-  is needed before or after the collective;
-* a post-accumulate-grad hook counts the parameters of each bucket; when a
-  bucket is complete its all-reduce (``ReduceOp.AVG``) is issued on a dedicated
-  communication stream that first waits for the compute stream, so the
-  transfer of early buckets (the wide pointwise weights of the decoder) runs
-  under the remaining backward;
+* parameters are grouped, in reverse registration order (roughly the order
+  their gradients become final during backward), into flat fp32 buckets of
+  about ``bucket_cap_mb``;
+* :meth:`GradientBucketReducer.zero_grad` sets every ``param.grad`` to None, so
+  autograd stores each gradient as produced (no per-parameter accumulation
+  kernel); a post-accumulate-grad hook counts the parameters of each bucket, and
+  when a bucket is complete one multi-tensor copy gathers its gradients into the
+  flat buffer, whose all-reduce (``ReduceOp.AVG``) is issued on a dedicated
+  communication stream that first waits for the compute stream, so early
+  buckets (the wide pointwise weights of the decoder) travel under the remaining
+  backward; each ``param.grad`` then becomes a view of the reduced buffer;
 * :meth:`GradientBucketReducer.finish` makes the compute stream wait for the
   communication stream before the optimizer step.
+* With a single process the reducer does nothing beyond ``zero_grad``.
 
 Every rank issues the same collectives in the same order (buckets complete in a
 deterministic order because backward is deterministic), which is required for
@@ -66,25 +69,31 @@ class GradientBucketReducer:
         self.stream = stream or (torch.cuda.Stream(device=device) if device.type == "cuda" else None)
         # NCCL averages in the collective; gloo (CPU tests) has no AVG, so sum and scale
         self.native_avg = (not dist.is_initialized()) or dist.get_backend(group) == "nccl"
-        self.handles = [p.register_post_accumulate_grad_hook(self._hook) for p in params]
+        # one process: nothing to reduce, gradients stay where autograd puts them
+        self.handles = [p.register_post_accumulate_grad_hook(self._hook) for p in params] if self.world > 1 else []
         self.order: list[int] = []
 
     @staticmethod
     def _make(params: list[nn.Parameter]) -> _Bucket:
-        total = sum(p.numel() for p in params)
-        buf = torch.zeros(total, dtype=torch.float32, device=params[0].device)
-        offset = 0
         for p in params:
             if p.dtype != torch.float32:
                 raise ValueError("gradient buckets hold fp32 parameters")
-            p.grad = buf[offset : offset + p.numel()].view_as(p)
-            offset += p.numel()
+        total = sum(p.numel() for p in params)
+        buf = torch.zeros(total, dtype=torch.float32, device=params[0].device)
         return _Bucket(params, buf, pending=len(params))
 
+    def _views(self, b: _Bucket) -> list[torch.Tensor]:
+        out, offset = [], 0
+        for p in b.params:
+            out.append(b.buffer[offset : offset + p.numel()].view_as(p))
+            offset += p.numel()
+        return out
+
     def zero_grad(self) -> None:
-        """Zero the buckets in place (grads stay views into them)."""
+        """Drop the gradients: autograd stores the next ones without accumulation."""
         for b in self.buckets:
-            b.buffer.zero_()
+            for p in b.params:
+                p.grad = None
             b.pending = len(b.params)
             b.launched = False
         self.order.clear()
@@ -102,12 +111,21 @@ class GradientBucketReducer:
         self.order.append(b.index)
         if self.world == 1:
             return
+        views = self._views(b)
+        have = [(v, p.grad) for v, p in zip(views, b.params, strict=True) if p.grad is not None]
+        for v, p in zip(views, b.params, strict=True):
+            if p.grad is None:
+                v.zero_()  # no gradient this step (unused parameter)
+        if have:
+            torch._foreach_copy_([v for v, _ in have], [g for _, g in have])
         if self.stream is None:
             self._all_reduce_mean(b.buffer)
-            return
-        self.stream.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(self.stream):
-            self._all_reduce_mean(b.buffer)
+        else:
+            self.stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self.stream):
+                self._all_reduce_mean(b.buffer)
+        for v, p in zip(views, b.params, strict=True):
+            p.grad = v
 
     def _all_reduce_mean(self, buf: torch.Tensor) -> None:
         if self.native_avg:
