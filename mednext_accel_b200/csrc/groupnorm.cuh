@@ -7,6 +7,8 @@
 // reproducible from run to run.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "depthwise_s1.cuh"  // GnPartial, chan_merge, block_merge_stats
 
@@ -44,18 +46,32 @@ __global__ void __launch_bounds__(256) gn_stats_partial_kernel(const T* __restri
   using Acc = typename Elem<T>::Acc;
   const int j = blockIdx.x % chunks;
   const size_t nc = blockIdx.x / chunks;
-  const size_t per = (vol + chunks - 1) / chunks;
-  const size_t beg = (size_t)j * per;
+  // chunks start on 8-element boundaries (16-byte vectors); trailing chunks may be empty
+  const size_t per = ((vol + chunks - 1) / chunks + 7) / 8 * 8;
+  const size_t beg = min((size_t)j * per, vol);
   const size_t end = min(beg + per, vol);
   const T* p = x + nc * pitch;
   Acc cnt = Acc(0), shift = Acc(0), s1 = Acc(0), s2 = Acc(0);
-  for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
-    const Acc v = to_acc<T>(__ldg(p + i));
+  auto add = [&](Acc v) {
     if (cnt == Acc(0)) shift = v;
     const Acc d = v - shift;
     s1 += d;
     s2 = fma(d, d, s2);
     cnt += Acc(1);
+  };
+  constexpr int E = 16 / (int)sizeof(T);
+  if (vec_ok<T>(x, pitch) && beg % E == 0) {
+    // whole 16-byte chunks, then the (at most E-1) trailing elements
+    const size_t vend = beg + (end - beg) / E * E;
+    for (size_t i = beg + (size_t)threadIdx.x * E; i < vend; i += (size_t)blockDim.x * E) {
+      Acc v[E];
+      unpack16<T>(__ldg(reinterpret_cast<const uint4*>(p + i)), v);
+#pragma unroll
+      for (int e = 0; e < E; ++e) add(v[e]);
+    }
+    for (size_t i = vend + threadIdx.x; i < end; i += blockDim.x) add(to_acc<T>(__ldg(p + i)));
+  } else {
+    for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) add(to_acc<T>(__ldg(p + i)));
   }
   double n = (double)cnt, mean = 0.0, m2 = 0.0;
   if (cnt > Acc(0)) {
@@ -150,13 +166,20 @@ __global__ void __launch_bounds__(256) gn_bwd_partial_kernel(const TD* __restric
   }
 }
 
-// Fold the `tiles` partials of each (n, c) into slot 0 of its row, in place:
-// thread t sums partials t, t+256, ... in order, then a fixed-shape tree.
+// Fold the `tiles` partials of each (n, c) into slot 0 of its row, in place, in
+// two passes with a fixed order: pass 1 has one CTA per span of kGnFoldSpan
+// partials and writes the span's sum into the span's first slot; pass 2
+// (gn_fold_spans_kernel) adds those slots into slot 0.  Within a CTA, thread t
+// sums partials t, t+256, ... in order, then a fixed-shape tree.
+constexpr int kGnFoldSpan = 4096;
 static __global__ void __launch_bounds__(256) gn_fold_partials_kernel(GnBwdPartial* __restrict__ part, int tiles) {
-  const size_t nc = blockIdx.x;
-  GnBwdPartial* p = part + nc * tiles;
+  const int spans = (tiles + kGnFoldSpan - 1) / kGnFoldSpan;
+  const size_t nc = blockIdx.x / spans;
+  const int sp = (int)(blockIdx.x % spans);
+  GnBwdPartial* p = part + nc * tiles + (size_t)sp * kGnFoldSpan;
+  const int count = min(kGnFoldSpan, tiles - sp * kGnFoldSpan);
   double a = 0.0, b = 0.0;
-  for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+  for (int t = threadIdx.x; t < count; t += blockDim.x) {
     a += p[t].s1;
     b += p[t].s2;
   }
@@ -178,6 +201,18 @@ static __global__ void __launch_bounds__(256) gn_fold_partials_kernel(GnBwdParti
     p[0] = gp;
   }
 }
+static __global__ void gn_fold_spans_kernel(GnBwdPartial* __restrict__ part, int tiles, int nc_total) {
+  const int nc = blockIdx.x * blockDim.x + threadIdx.x;
+  if (nc >= nc_total) return;
+  GnBwdPartial* p = part + (size_t)nc * tiles;
+  double a = p[0].s1, b = p[0].s2;
+  for (int s = kGnFoldSpan; s < tiles; s += kGnFoldSpan) {
+    a += p[s].s1;
+    b += p[s].s2;
+  }
+  p[0].s1 = a;
+  p[0].s2 = b;
+}
 
 // Backward pass 2: dx = rstd * gamma * (dz - S1/V - xhat * S2/V), with the
 // folded sums of (n, c) at folded[nc * stride].
@@ -194,13 +229,30 @@ __global__ void __launch_bounds__(256) gn_bwd_apply_kernel(
   const float m2 = (float)(f.s2 / (double)vol);
   const float mean = stats[2 * nc], rstd = stats[2 * nc + 1];
   const float gr = rstd * (gamma != nullptr ? param_f(gamma, c) : 1.0f);
-  const size_t per = (vol + chunks - 1) / chunks;
-  const size_t beg = (size_t)j * per;
+  // chunks start on 8-element boundaries (16-byte vectors); trailing chunks may be empty
+  const size_t per = ((vol + chunks - 1) / chunks + 7) / 8 * 8;
+  const size_t beg = min((size_t)j * per, vol);
   const size_t end = min(beg + per, vol);
   const TD* g = dz + nc * pitch;
   const TX* xs = x + nc * pitch;
   TO* o = dx + nc * pitch;
-  for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) {
+  size_t i0 = beg;
+  if constexpr (std::is_same<TD, TX>::value && std::is_same<TX, TO>::value && sizeof(TX) == 2) {
+    constexpr int E = 8;
+    if (vec_ok<TX>(dz, pitch) && vec_ok<TX>(x, pitch) && vec_ok<TX>(dx, pitch) && beg % E == 0) {
+      const size_t vend = beg + (end - beg) / E * E;
+      for (size_t i = beg + (size_t)threadIdx.x * E; i < vend; i += (size_t)blockDim.x * E) {
+        float d[E], xv[E], r[E];
+        unpack16<TD>(__ldg(reinterpret_cast<const uint4*>(g + i)), d);
+        unpack16<TX>(__ldg(reinterpret_cast<const uint4*>(xs + i)), xv);
+#pragma unroll
+        for (int e = 0; e < E; ++e) r[e] = gr * (d[e] - m1 - (xv[e] - mean) * rstd * m2);
+        *reinterpret_cast<uint4*>(o + i) = pack16<TO>(r);
+      }
+      i0 = vend;
+    }
+  }
+  for (size_t i = i0 + threadIdx.x; i < end; i += blockDim.x) {
     const float d = (float)to_acc<TD>(__ldg(g + i));
     const float xh = ((float)to_acc<TX>(__ldg(xs + i)) - mean) * rstd;
     o[i] = from_acc<TO>((typename Elem<TO>::Acc)(gr * (d - m1 - xh * m2)));

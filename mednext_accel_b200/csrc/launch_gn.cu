@@ -76,9 +76,16 @@ int dispatch_gn_bwd_apply(int x_dtype, int dz_dtype, int g_dtype, const void* dz
   int st = MEDNEXT_OK;
   if (part_tiles > 1) {
     // fold in place; the workspace belongs to this call sequence
-    gn_fold_partials_kernel<<<(unsigned)nc, 256, 0, s>>>(const_cast<GnBwdPartial*>(part), part_tiles);
+    const int spans = (part_tiles + kGnFoldSpan - 1) / kGnFoldSpan;
+    gn_fold_partials_kernel<<<(unsigned)(nc * spans), 256, 0, s>>>(const_cast<GnBwdPartial*>(part), part_tiles);
     st = record_launch();
     if (st != MEDNEXT_OK) return st;
+    if (spans > 1) {
+      gn_fold_spans_kernel<<<(unsigned)((nc + 127) / 128), 128, 0, s>>>(const_cast<GnBwdPartial*>(part), part_tiles,
+                                                                         (int)nc);
+      st = record_launch();
+      if (st != MEDNEXT_OK) return st;
+    }
   }
   MEDNEXT_GN_DISPATCH(x_dtype, dz_dtype, g_dtype, TX, TD, TG, {
     gn_bwd_apply_kernel<TD, TX, TX, TG><<<(unsigned)(nc * chunks), 256, 0, s>>>(

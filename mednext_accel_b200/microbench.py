@@ -20,7 +20,7 @@ import torch
 
 from . import _native as nat
 from . import depthwise as dwk
-from .pointwise import gn_stats, pw_gemm, pw_wgrad
+from .pointwise import gn_backward_from_partials, gn_stats, pw_gemm, pw_wgrad
 
 V = 128**3  # level-0 voxels
 C, RC = 32, 64  # level-0 channels and expanded channels (ratio 2)
@@ -38,6 +38,7 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
     b1, b2 = torch.randn(RC, device=dev), torch.randn(C, device=dev)
     g, bb = torch.ones(C, device=dev), torch.zeros(C, device=dev)
     stats = gn_stats(t, 1e-5)
+    dz, part = pw_gemm(du, (r(C, RC) * 0.2), C, aux=t, gn_bwd_stats=stats)
     wp_t, we_t = wp.t().contiguous(), we.t().contiguous()
     vol = (1, C, 128, 128, 128)
     x5, dy5 = x.view(vol), dy.view(vol)
@@ -69,6 +70,8 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
         "dwT fwd C64 64^3->127^3 k3": (lambda: dwk.t_forward(xs, w3b, None, 3), up_bytes),
         "dwT dgrad C64 k3": (lambda: dwk.t_dgrad(ybig, w3b, 3), up_bytes),
         "dwT wgrad C64 k3": (lambda: dwk.t_wgrad(xs, ybig, 3), up_bytes),
+        "gn stats C32": (lambda: gn_stats(t, 1e-5), C * 2 * V),
+        "gn bwd C32 (fold + apply)": (lambda: gn_backward_from_partials(dz, t, stats, g, part), 3 * C * 2 * V),
     }
 
 
