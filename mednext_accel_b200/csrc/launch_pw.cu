@@ -29,7 +29,12 @@ int try_pw_wgrad_tma(const PwWgradArgs& a, cudaStream_t s) {
                    CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
   cfg.b_bytes = a.BN * 128;
-  const size_t per_stage = 16384 + (size_t)cfg.b_bytes;
+  // two 64-voxel chunks per ring stage when four such stages fit: the hand-off
+  // between the TMA producer and its consumers costs about the same per stage
+  // whatever the stage holds, so larger stages stream faster
+  const size_t per_chunk = 16384 + (size_t)cfg.b_bytes;
+  cfg.nch = 4 * 2 * per_chunk <= kSmemBudget ? 2 : 1;
+  const size_t per_stage = cfg.nch * per_chunk;
   cfg.stages = (int)std::min<size_t>(kMaxStages, kSmemBudget / per_stage);
   if (cfg.stages < 2) return -1;
   cfg.units = a.mtiles * a.ntiles * a.splits;

@@ -143,7 +143,6 @@ inline PwWPlan plan_pw_wgrad(int64_t n, int64_t cin, int64_t cout, int64_t vox) 
   p.total = p.cps * n;
   // one split-K unit per SM for the persistent kernel (148 SMs)
   long long splits = std::max(1LL, (long long)148 / (p.mtiles * p.ntiles));
-  splits = std::min(splits, 128LL);
   splits = std::min(splits, p.total);
   p.per = (p.total + splits - 1) / splits;
   p.splits = (int)((p.total + p.per - 1) / p.per);

@@ -57,6 +57,7 @@ struct PwTmaCfg {
   int nacc;         // TMEM accumulator buffers (2 or 4)
   int tgroups;      // epilogue warp groups on alternate tiles (1 or 2)
   int a_rows;       // channel rows per A box: min(64, roundup16(cin)); the MMA reads no further
+  int w_res;        // 1: the whole W operand (kstages boxes) is loaded once and stays in shared memory
 };
 
 struct PwTmaSmem {
@@ -68,6 +69,7 @@ struct PwTmaSmem {
   uint64_t efull[kMaxEStages];
   uint64_t eempty[kMaxEStages];
   uint64_t drain;  // final tcgen05.commit: every MMA of the CTA has completed
+  uint64_t wfull;  // resident W operand landed
   uint32_t tmem_base;
   int abort;
 };
@@ -136,9 +138,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   const uint32_t base_u32 = smem_u32(smem_dyn);
   uint8_t* sbase = smem_dyn + (((base_u32 + 1023u) & ~1023u) - base_u32);
+  // W: one box per ring stage, or (w_res) all KS boxes resident for the whole kernel
+  const bool w_res = cfg.w_res != 0;
   uint8_t* ringA = sbase;                                 // S x 16 KB
-  uint8_t* ringB = ringA + (size_t)S * 16384;             // S x b_bytes
-  uint8_t* ringAux = ringB + (size_t)S * cfg.b_bytes;     // E x aux_bytes
+  uint8_t* ringB = ringA + (size_t)S * 16384;             // (w_res ? KS : S) x b_bytes
+  uint8_t* ringAux = ringB + (size_t)(w_res ? KS : S) * cfg.b_bytes;  // E x aux_bytes
   uint8_t* ringRes = ringAux + (size_t)E * cfg.aux_bytes; // E x res_bytes
   uint8_t* ringStg = ringRes + (size_t)E * cfg.res_bytes;  // epilogue warps x 2 x (16 x 32) TY
   constexpr int kStgBytes = 32 * kPwCW * (int)sizeof(TY);
@@ -165,6 +169,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&sh.eempty[i], kEpiThreads / cfg.tgroups);
     }
     mbar_init(&sh.drain, 1);
+    mbar_init(&sh.wfull, 1);
     sh.abort = 0;
     fence_mbarrier_init();
   }
@@ -182,6 +187,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   volatile int* abort = &sh.abort;
   const int ntile_local = (cfg.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
   long long a_issued = 0, aux_issued = 0;  // TMA fills issued by the two producers
+  bool w_issued = false;
 
   auto decode = [&](int t, int& s, int& j0, long long& v0, int& mt) {
     mt = t % p.mtiles;
@@ -221,6 +227,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (warp == 0) {
     // ------------------------------------------------ TMA producer of the A / W stages
     if (lane == 0) {
+      if (w_res && ntile_local > 0) {
+        // a single N tile (j0 = 0): every tile of the CTA multiplies by the same W
+        mbar_arrive_expect_tx(&sh.wfull, (uint32_t)(KS * cfg.b_bytes));
+        for (int kk = 0; kk < KS; ++kk)
+          tma_load_2d(ringB + (size_t)kk * cfg.b_bytes, &mB, &sh.wfull, kk * kPwBK, 0);
+        w_issued = true;
+      }
+      const uint32_t stage_tx = (uint32_t)(2 * 128 * cfg.a_rows + (w_res ? 0 : cfg.b_bytes));
       long long issued = 0;
       for (int i = 0; i < ntile_local && !*abort; ++i) {
         int s, j0, mt;
@@ -230,11 +244,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int q = i * KS + kk;
           const int st = q % S, r = q / S;
           if (r > 0 && !wait_or_abort(&sh.empty[st], (r - 1) & 1, abort)) break;
-          mbar_arrive_expect_tx(&sh.full[st], (uint32_t)(2 * 128 * cfg.a_rows + cfg.b_bytes));
+          mbar_arrive_expect_tx(&sh.full[st], stage_tx);
           uint8_t* a = ringA + (size_t)st * 16384;
           tma_load_3d(a, &mA, &sh.full[st], (int)v0, kk * kPwBK, s);
           tma_load_3d(a + 8192, &mA, &sh.full[st], (int)v0 + 64, kk * kPwBK, s);
-          tma_load_2d(ringB + (size_t)st * cfg.b_bytes, &mB, &sh.full[st], kk * kPwBK, j0);
+          if (!w_res) tma_load_2d(ringB + (size_t)st * cfg.b_bytes, &mB, &sh.full[st], kk * kPwBK, j0);
           ++issued;
         }
       }
@@ -244,6 +258,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(kPwBM, BN, std::is_same<TA, __nv_bfloat16>::value, true, false);
+      if (w_res && ntile_local > 0) wait_or_abort(&sh.wfull, 0, abort);
       for (int i = 0; i < ntile_local && !*abort; ++i) {
         const int acc = i % cfg.nacc, ra = i / cfg.nacc;
         if (ra > 0 && !wait_or_abort(&sh.tempty[acc], (ra - 1) & 1, abort)) break;
@@ -256,7 +271,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (!wait_or_abort(bar, r & 1, abort)) break;
           tc_fence_after();
           const uint32_t a_addr = smem_u32(ringA + (size_t)st * 16384);
-          const uint32_t b_addr = smem_u32(ringB + (size_t)st * cfg.b_bytes);
+          const uint32_t b_addr = smem_u32(ringB + (size_t)(w_res ? kk : st) * cfg.b_bytes);
           const int ksteps = min(kPwBK, p.cin - kk * kPwBK + 15) / 16;
           for (int ks = 0; ks < ksteps; ++ks) {
             const uint64_t ad = make_sw128_desc(a_addr + ks * 2048, 8192, 1024);
@@ -418,7 +433,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
   __syncthreads();
   if (*abort && lane == 0) {
-    if (warp == 0) drain_ring(sh.full, S, a_issued);
+    if (warp == 0) {
+      drain_ring(sh.full, S, a_issued);
+      if (w_issued) mbar_wait(&sh.wfull, 0);
+    }
     if (warp == 2) drain_ring(sh.efull, E, aux_issued);
     if (warp == 1) drain_mma(&sh.drain);
   }
@@ -444,7 +462,8 @@ constexpr int kWgEpiWarp0 = 12;
 
 struct PwTmaWgradCfg {
   int stages;
-  int b_bytes;   // BN * 128: one B stage
+  int nch;       // 64-voxel chunks per ring stage (one TMA barrier phase covers all of them)
+  int b_bytes;   // BN * 128: one B slot
   int units;     // mtiles * ntiles * splits
   int g_rows;    // rows of g per TMA box (min(128, cout))
   int a_rows;    // rows of a per TMA box
@@ -466,21 +485,26 @@ __global__ void __launch_bounds__(kWgThreads, 1)
   const bool pro_on = PRO != MEDNEXT_PRO_NONE || !ones;
   const uint32_t base_u32 = smem_u32(smem_dyn);
   uint8_t* sbase = smem_dyn + (((base_u32 + 1023u) & ~1023u) - base_u32);
-  uint8_t* ringA = sbase;                      // S x 16 KB  (g rows)
-  uint8_t* ringB = ringA + (size_t)S * 16384;  // S x b_bytes (a rows)
+  // stage st holds chunk slots st*nch .. st*nch+nch-1: a stage of several chunks
+  // amortises the per-phase cost of the TMA barrier hand-off
+  const int NCH = cfg.nch;
+  const int SL = S * NCH;                       // chunk slots
+  uint8_t* ringA = sbase;                       // SL x 16 KB  (g rows)
+  uint8_t* ringB = ringA + (size_t)SL * 16384;  // SL x b_bytes (a rows)
+  const uint32_t chunk_tx = (uint32_t)(cfg.g_rows + cfg.a_rows) * 128u;
 
   // rows that TMA never writes stay zero; the bias row holds ones
   {
-    const size_t ring_bytes = (size_t)S * (16384 + cfg.b_bytes);
+    const size_t ring_bytes = (size_t)SL * (16384 + cfg.b_bytes);
     for (size_t off = (size_t)tid * 16; off < ring_bytes; off += (size_t)kWgThreads * 16)
       *reinterpret_cast<uint4*>(sbase + off) = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
-    if (ones && tid < S * 8) {
-      const int st = tid >> 3, c = tid & 7;
+    for (int t = tid; ones && t < SL * 8; t += kWgThreads) {
+      const int sl = t >> 3, c = t & 7;
       float one[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) one[e] = 1.0f;
-      *reinterpret_cast<uint4*>(ringB + (size_t)st * cfg.b_bytes + sw128_kmajor_off(cfg.ones_row, c)) =
+      *reinterpret_cast<uint4*>(ringB + (size_t)sl * cfg.b_bytes + sw128_kmajor_off(cfg.ones_row, c)) =
           pack16<TA>(one);
     }
     fence_async_smem();
@@ -526,21 +550,25 @@ __global__ void __launch_bounds__(kWgThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t tx = (uint32_t)(cfg.g_rows + cfg.a_rows) * 128u;
-      long long q = 0;  // fills issued
+      long long q = 0;  // stages filled
       for (int i = 0; i < nunits && !*abort; ++i) {
         int mt, nt, sp;
         long long cb, ce;
         unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
-        for (long long ch = cb; ch < ce; ++ch, ++q) {
+        for (long long ch0 = cb; ch0 < ce; ch0 += NCH, ++q) {
           const int st = (int)(q % S);
           const long long r = q / S;
           if (r > 0 && !wait_or_abort(&sh.empty[st], (uint32_t)((r - 1) & 1), abort)) break;
-          const int s = (int)(ch / p.chunks_per_sample);
-          const int v = (int)((ch - (long long)s * p.chunks_per_sample) * kPwBK);
-          mbar_arrive_expect_tx(&sh.full[st], tx);
-          tma_load_3d(ringA + (size_t)st * 16384, &mG, &sh.full[st], v, mt * kPwBM, s);
-          tma_load_3d(ringB + (size_t)st * cfg.b_bytes, &mA, &sh.full[st], v, nt * BN, s);
+          const int n = (int)min((long long)NCH, ce - ch0);
+          mbar_arrive_expect_tx(&sh.full[st], chunk_tx * (uint32_t)n);
+          for (int c = 0; c < n; ++c) {
+            const long long ch = ch0 + c;
+            const int s = (int)(ch / p.chunks_per_sample);
+            const int v = (int)((ch - (long long)s * p.chunks_per_sample) * kPwBK);
+            const int sl = st * NCH + c;
+            tma_load_3d(ringA + (size_t)sl * 16384, &mG, &sh.full[st], v, mt * kPwBM, s);
+            tma_load_3d(ringB + (size_t)sl * cfg.b_bytes, &mA, &sh.full[st], v, nt * BN, s);
+          }
         }
       }
       g_issued = q;
@@ -556,19 +584,23 @@ __global__ void __launch_bounds__(kWgThreads, 1)
         if (i > 0 && !wait_or_abort(&sh.tempty[0], (uint32_t)((i - 1) & 1), abort)) break;
         tc_fence_after();
         bool first = true;
-        for (long long ch = cb; ch < ce; ++ch, ++q) {
+        for (long long ch0 = cb; ch0 < ce; ch0 += NCH, ++q) {
           const int st = (int)(q % S);
           const long long r = q / S;
           if (!wait_or_abort(pro_on ? &sh.ready[st] : &sh.full[st], (uint32_t)(r & 1), abort)) break;
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(ringA + (size_t)st * 16384);
-          const uint32_t b_addr = smem_u32(ringB + (size_t)st * cfg.b_bytes);
+          const int n = (int)min((long long)NCH, ce - ch0);
+          for (int c = 0; c < n; ++c) {
+            const int sl = st * NCH + c;
+            const uint32_t a_addr = smem_u32(ringA + (size_t)sl * 16384);
+            const uint32_t b_addr = smem_u32(ringB + (size_t)sl * cfg.b_bytes);
 #pragma unroll
-          for (int ks = 0; ks < kPwBK / 16; ++ks) {
-            const uint64_t ad = make_sw128_desc(a_addr + ks * 32, 16, 1024);
-            const uint64_t bd = make_sw128_desc(b_addr + ks * 32, 16, 1024);
-            mma_f16_ss(tmem, ad, bd, idesc, first ? 0u : 1u);
-            first = false;
+            for (int ks = 0; ks < kPwBK / 16; ++ks) {
+              const uint64_t ad = make_sw128_desc(a_addr + ks * 32, 16, 1024);
+              const uint64_t bd = make_sw128_desc(b_addr + ks * 32, 16, 1024);
+              mma_f16_ss(tmem, ad, bd, idesc, first ? 0u : 1u);
+              first = false;
+            }
           }
           mma_commit(&sh.empty[st]);
         }
@@ -588,45 +620,49 @@ __global__ void __launch_bounds__(kWgThreads, 1)
         unit_range((int)blockIdx.x + i * (int)gridDim.x, mt, nt, sp, cb, ce);
         const bool rowsum = !ones && nt == 0 && t < kPwBM;
         float bsum = 0.f;  // row t of g (output channel mt*128 + t)
-        for (long long ch = cb; ch < ce; ++ch, ++q) {
+        for (long long ch0 = cb; ch0 < ce; ch0 += NCH, ++q) {
           const int st = (int)(q % S);
           const long long r = q / S;
           if (!wait_or_abort(&sh.full[st], (uint32_t)(r & 1), abort)) break;
-          const int s = (int)(ch / p.chunks_per_sample);
-          if (rowsum) {
-            const uint8_t* row = ringA + (size_t)st * 16384 + (t >> 3) * 1024 + (t & 7) * 128;
+          const int nc = (int)min((long long)NCH, ce - ch0);
+          for (int c = 0; c < nc; ++c) {
+            const int sl = st * NCH + c;
+            const int s = (int)((ch0 + c) / p.chunks_per_sample);
+            if (rowsum) {
+              const uint8_t* row = ringA + (size_t)sl * 16384 + (t >> 3) * 1024 + (t & 7) * 128;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              float v[8];
-              unpack16<TA>(*reinterpret_cast<const uint4*>(row + c * 16), v);
+              for (int c16 = 0; c16 < 8; ++c16) {
+                float v[8];
+                unpack16<TA>(*reinterpret_cast<const uint4*>(row + c16 * 16), v);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) bsum += v[e];
-            }
-          }
-          if constexpr (PRO != MEDNEXT_PRO_NONE) {
-            // a_rows x 8 chunks of 8 voxels; item -> (row, chunk), 4 rows per warp pass
-            for (int item = t; item < cfg.a_rows * 8; item += kWgProThreads) {
-              const int n = item >> 3, cq = item & 7;
-              const int k = nt * BN + n;
-              uint4* chunk = reinterpret_cast<uint4*>(ringB + (size_t)st * cfg.b_bytes + sw128_kmajor_off(n, cq));
-              float v[8];
-              unpack16<TA>(*chunk, v);
-              if constexpr (PRO == MEDNEXT_PRO_GROUPNORM) {
-                float ca = 0.f, cbb = 0.f;
-                if (k < p.cin) {
-                  const float mean = __ldg(p.pro_stats + 2 * (s * p.cin + k));
-                  const float rstd = __ldg(p.pro_stats + 2 * (s * p.cin + k) + 1);
-                  ca = rstd * __ldg(p.pro_gamma + k);
-                  cbb = __ldg(p.pro_beta + k) - mean * ca;
-                }
-                pw_prologue<PRO>(v, ca, cbb);
-              } else {
-                pw_prologue<PRO>(v, 0.f, 0.f);
+                for (int e = 0; e < 8; ++e) bsum += v[e];
               }
-              *chunk = pack16<TA>(v);
             }
-            fence_async_smem();
+            if constexpr (PRO != MEDNEXT_PRO_NONE) {
+              // a_rows x 8 chunks of 8 voxels; item -> (row, chunk), 4 rows per warp pass
+              for (int item = t; item < cfg.a_rows * 8; item += kWgProThreads) {
+                const int n = item >> 3, cq = item & 7;
+                const int k = nt * BN + n;
+                uint4* chunk = reinterpret_cast<uint4*>(ringB + (size_t)sl * cfg.b_bytes + sw128_kmajor_off(n, cq));
+                float v[8];
+                unpack16<TA>(*chunk, v);
+                if constexpr (PRO == MEDNEXT_PRO_GROUPNORM) {
+                  float ca = 0.f, cbb = 0.f;
+                  if (k < p.cin) {
+                    const float mean = __ldg(p.pro_stats + 2 * (s * p.cin + k));
+                    const float rstd = __ldg(p.pro_stats + 2 * (s * p.cin + k) + 1);
+                    ca = rstd * __ldg(p.pro_gamma + k);
+                    cbb = __ldg(p.pro_beta + k) - mean * ca;
+                  }
+                  pw_prologue<PRO>(v, ca, cbb);
+                } else {
+                  pw_prologue<PRO>(v, 0.f, 0.f);
+                }
+                *chunk = pack16<TA>(v);
+              }
+            }
           }
+          if constexpr (PRO != MEDNEXT_PRO_NONE) fence_async_smem();
           mbar_arrive(&sh.ready[st]);
         }
         if (rowsum) {

@@ -20,6 +20,7 @@ using namespace tma;
 
 inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 constexpr size_t kSmemBudget = 220 * 1024;
+constexpr size_t kWResidentBytes = 64 * 1024;  // largest W operand kept resident in the forward kernel
 inline int num_sms() {
   static int sms = 0;
   if (sms == 0) {
@@ -84,12 +85,15 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   cfg.kstages = (a.cin + kPwBK - 1) / kPwBK;
   cfg.total_tiles = a.S * a.ntiles * a.mtiles;
   cfg.b_bytes = a.BN * 128;
+  // one N tile and a small W: load it once per CTA instead of once per ring stage
+  cfg.w_res = (a.ntiles == 1 && (size_t)cfg.kstages * cfg.b_bytes <= kWResidentBytes) ? 1 : 0;
+  const size_t w_bytes = cfg.w_res ? (size_t)cfg.kstages * cfg.b_bytes : 0;
   cfg.aux_bytes = has_aux ? a.BN * 64 * (int)sizeof(TA) * 2 : 0;
   cfg.res_bytes = has_res ? a.BN * 64 * (int)sizeof(TY) * 2 : 0;
-  const size_t per_stage = 16384 + (size_t)cfg.b_bytes;
+  const size_t per_stage = 16384 + (cfg.w_res ? 0 : (size_t)cfg.b_bytes);
   const size_t ebytes = (size_t)cfg.aux_bytes + cfg.res_bytes;
   const size_t stg = (size_t)FwdEpi<PRO>::warps * 2 * 32 * kPwCW * sizeof(TY);  // epilogue staging, 2 per warp
-  const size_t budget = kSmemBudget - stg;
+  const size_t budget = kSmemBudget - stg - w_bytes;
   // Epilogue-operand ring: 4 or 2 stages while keeping at least 4 A/W stages,
   // else 1.  Two epilogue warp groups take alternate tiles only when every ring
   // slot then belongs to one group (an even ring, or none): a slot shared by two
@@ -104,7 +108,7 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   const long long room = (long long)budget - (long long)cfg.estages * (long long)ebytes;
   cfg.stages = (int)std::min<long long>(kMaxStages, room / (long long)per_stage);
   if (cfg.stages < 2) return -1;
-  const size_t smem = 1024 + cfg.stages * per_stage + cfg.estages * ebytes + stg;
+  const size_t smem = 1024 + cfg.stages * per_stage + w_bytes + cfg.estages * ebytes + stg;
   auto kern = pw_tma_fwd_kernel<TA, TY, PRO, EPI>;
   static size_t configured = 0;
   set_smem(kern, smem, configured);
