@@ -233,6 +233,19 @@ int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const f
                    const float* epi_stats, void* workspace, size_t workspace_bytes, int64_t n,
                    int64_t cin, int64_t cout, int64_t vox, int a_dtype, int y_dtype,
                    mednext_stream_t stream);
+/* mednext_pw_fwd that also writes pro_out [n, cin, vox] (a's dtype) = pro(a), the
+ * GEMM's transformed input, when prologue != NONE (pro_out NULL: same as
+ * mednext_pw_fwd).  The compress GEMM of models/blocks.py:79-80
+ * (project(activation(expand(x)))) keeps activation(expand(x)) this way, the
+ * tensor PyTorch's autograd saves for project's weight grad.
+ * pro_out must not alias a or y. */
+int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue,
+                           const float* pro_stats, const float* pro_gamma,
+                           const float* pro_beta, int epilogue, const float* bias,
+                           const void* residual, const void* aux, const float* epi_stats,
+                           void* pro_out, void* workspace, size_t workspace_bytes, int64_t n,
+                           int64_t cin, int64_t cout, int64_t vox, int a_dtype, int y_dtype,
+                           mednext_stream_t stream);
 /* Weight-grad form, the voxel axis is the reduction:
  *   dw[j, k] = sum_{s, v} g[s, j, v] * pro(a[s, k, v]);  dbias[j] = sum g
  * dw, dbias: FLOAT32 (dbias may be NULL).  Deterministic split-K. */

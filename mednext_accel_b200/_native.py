@@ -89,6 +89,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _INT,
         [_P, _P, _P, _INT, _P, _P, _P, _INT, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _INT, _P],
     ),
+    "mednext_pw_fwd_pro_out": (
+        _INT,
+        [_P, _P, _P, _INT, _P, _P, _P, _INT, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _INT, _P],
+    ),
     "mednext_pw_wgrad_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "mednext_pw_wgrad": (
         _INT,

@@ -373,6 +373,16 @@ int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const f
                    const void* residual, const void* aux, const float* epi_stats, void* workspace,
                    size_t workspace_bytes, int64_t n, int64_t cin, int64_t cout, int64_t vox, int a_dtype,
                    int y_dtype, mednext_stream_t stream) {
+  return mednext_pw_fwd_pro_out(a, wt, y, prologue, pro_stats, pro_gamma, pro_beta, epilogue, bias, residual, aux,
+                                epi_stats, nullptr, workspace, workspace_bytes, n, cin, cout, vox, a_dtype, y_dtype,
+                                stream);
+}
+
+int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue, const float* pro_stats,
+                           const float* pro_gamma, const float* pro_beta, int epilogue, const float* bias,
+                           const void* residual, const void* aux, const float* epi_stats, void* pro_out,
+                           void* workspace, size_t workspace_bytes, int64_t n, int64_t cin, int64_t cout,
+                           int64_t vox, int a_dtype, int y_dtype, mednext_stream_t stream) {
   if (!pw_dtype_ok(a_dtype)) return MEDNEXT_ERR_BAD_DTYPE;
   if (y_dtype != a_dtype && y_dtype != MEDNEXT_FLOAT32) return MEDNEXT_ERR_BAD_DTYPE;
   if (!pw_shape_ok(n, cin, cout, vox)) return MEDNEXT_ERR_BAD_SHAPE;
@@ -391,12 +401,14 @@ int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const f
     return MEDNEXT_ERR_WORKSPACE;
   const size_t asz = elem_size(a_dtype), ysz = elem_size(y_dtype);
   if (!aligned(a, asz) || !aligned(wt, asz) || !aligned(y, ysz) || (residual && !aligned(residual, ysz)) ||
-      (aux && !aligned(aux, asz)))
+      (aux && !aligned(aux, asz)) || (pro_out && !aligned(pro_out, asz)))
     return MEDNEXT_ERR_ALIGNMENT;
+  if (prologue == MEDNEXT_PRO_NONE) pro_out = nullptr;  // nothing transformed: nothing to write
   PwFwdArgs args{};
   args.a = a; args.wt = wt; args.y = y;
   args.pro_stats = pro_stats; args.pro_gamma = pro_gamma; args.pro_beta = pro_beta;
   args.bias = bias; args.residual = residual; args.aux = aux; args.epi_stats = epi_stats;
+  args.pro_out = pro_out;
   args.gn_part = static_cast<GnBwdPartial*>(workspace);
   args.S = (int)n; args.cin = (int)cin; args.cout = (int)cout; args.vox = vox;
   args.BN = pw_bn(cout);

@@ -44,6 +44,7 @@ struct PwFwdArgs {
   int vec_a;  // vox % 8 == 0 and aligned
   int vec_w;  // cin % 8 == 0 and aligned
   void* wpad;  // workspace for W with rows padded to a multiple of 8 (cin % 8 != 0), or null
+  void* pro_out;  // [S, cin, vox] in a's dtype: pro(a) as the GEMM consumed it, or null
 };
 
 // W [cout][cin] -> [cout][cin8] with zero columns: TMA needs 16-byte row strides.
@@ -85,6 +86,28 @@ __device__ __forceinline__ void pw_prologue(float* v, float ca, float cb) {
       v[i] = g.x;
       v[i + 1] = g.y;
     }
+  }
+}
+
+// out = pro(a) elementwise over [S, cin, vox], with the same arithmetic as the
+// GEMM prologue: the prologue output of the first-generation kernel.
+template <typename TA, int PRO>
+static __global__ void pw_prologue_out_kernel(const TA* __restrict__ a, TA* __restrict__ out,
+                                              const float* __restrict__ stats, const float* __restrict__ gamma,
+                                              const float* __restrict__ beta, int cin, long long vox,
+                                              long long total) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float v = to_acc<TA>(a[i]);
+    if constexpr (PRO == MEDNEXT_PRO_GROUPNORM) {
+      const long long row = i / vox;  // s * cin + k
+      const int k = (int)(row % cin);
+      const float ca = stats[2 * row + 1] * gamma[k];
+      v = fmaf(v, ca, beta[k] - stats[2 * row] * ca);
+    } else {
+      v = gelu_f(v);
+    }
+    out[i] = from_acc<TA>(v);
   }
 }
 

@@ -8,6 +8,8 @@
 //   warp 1      TMEM owner and MMA issuer (one lane): tcgen05.mma M=128 N=BN K=16,
 //               accumulators double-buffered in TMEM so the epilogue of tile i
 //               overlaps the MMAs of tile i+1.
+//   warp 3      (prologue output requested) TMA-stores each transformed A stage to
+//               pro_out and releases the stage once the store has read it.
 //   warps 4-11  prologue (only when one is requested): GroupNorm apply or GELU on
 //               the staged A tile, in place, then release it to the MMA.
 //   epilogue    warps 12-19 with a prologue, warps 4-19 without: tcgen05.ld of
@@ -43,6 +45,11 @@ struct FwdEpi {
   static constexpr int threads = warps * 32;
 };
 constexpr int kMaxStages = 8;
+// Prologue-output stores kept in flight by warp 3 (< ring stages, checked on the host).
+#ifndef MEDNEXT_PRO_STORE_LAG
+#define MEDNEXT_PRO_STORE_LAG 2
+#endif
+constexpr int kProStoreLag = MEDNEXT_PRO_STORE_LAG;
 constexpr int kMaxEStages = 4;
 constexpr int kMaxAcc = 4;  // TMEM accumulator buffers between the MMA and the epilogue
 
@@ -58,6 +65,7 @@ struct PwTmaCfg {
   int tgroups;      // epilogue warp groups on alternate tiles (1 or 2)
   int a_rows;       // channel rows per A box: min(64, roundup16(cin)); the MMA reads no further
   int w_res;        // 1: the whole W operand (kstages boxes) is loaded once and stays in shared memory
+  int pro_store;    // 1: warp 3 writes every transformed A stage to pro_out (tensor map mP)
 };
 
 struct PwTmaSmem {
@@ -127,7 +135,8 @@ template <typename TA, typename TY, int PRO, int EPI>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     pw_tma_fwd_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB,
                       const __grid_constant__ CUtensorMap mAux, const __grid_constant__ CUtensorMap mRes,
-                      const __grid_constant__ CUtensorMap mY, PwFwdArgs p, PwTmaCfg cfg) {
+                      const __grid_constant__ CUtensorMap mY, const __grid_constant__ CUtensorMap mP, PwFwdArgs p,
+                      PwTmaCfg cfg) {
   extern __shared__ uint8_t smem_dyn[];
   __shared__ PwTmaSmem sh;
   const int tid = threadIdx.x;
@@ -158,7 +167,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int i = 0; i < S; ++i) {
       mbar_init(&sh.full[i], 1);
       mbar_init(&sh.ready[i], kFwdProThreads);
-      mbar_init(&sh.empty[i], 1);
+      // a stage is free again after its MMAs and, with a prologue output, its store
+      mbar_init(&sh.empty[i], cfg.pro_store ? 2 : 1);
     }
     for (int i = 0; i < cfg.nacc; ++i) {
       mbar_init(&sh.tfull[i], 1);
@@ -179,6 +189,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (has_aux) tma_prefetch_map(&mAux);
     if (has_res) tma_prefetch_map(&mRes);
     tma_prefetch_map(&mY);
+    if (cfg.pro_store) tma_prefetch_map(&mP);
   }
   tc_fence_before();
   __syncthreads();
@@ -281,6 +292,33 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           mma_commit(&sh.empty[st]);
         }
         mma_commit(&sh.tfull[acc]);
+      }
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------ prologue output store
+    if constexpr (PRO != MEDNEXT_PRO_NONE) {
+      if (cfg.pro_store && lane == 0) {
+        long long q = 0;  // stages stored
+        for (int i = 0; i < ntile_local && !*abort; ++i) {
+          int s, j0, mt;
+          long long v0;
+          decode((int)blockIdx.x + i * (int)gridDim.x, s, j0, v0, mt);
+          for (int kk = 0; kk < KS; ++kk) {
+            const int st = (int)(q % S), r = (int)(q / S);
+            if (!wait_or_abort(&sh.ready[st], r & 1, abort)) break;
+            uint8_t* a = ringA + (size_t)st * 16384;
+            tma_store_3d(&mP, a, (int)v0, kk * kPwBK, s);
+            tma_store_3d(&mP, a + 8192, (int)v0 + 64, kk * kPwBK, s);
+            bulk_commit();
+            // kProStoreLag stores in flight; a stage is released once its store has read it
+            bulk_wait_read<kProStoreLag>();
+            if (q >= kProStoreLag) mbar_arrive(&sh.empty[(q - kProStoreLag) % S]);
+            ++q;
+          }
+        }
+        bulk_wait_read<0>();
+        for (long long k = q > kProStoreLag ? q - kProStoreLag : 0; k < q; ++k) mbar_arrive(&sh.empty[k % S]);
+        bulk_wait_all();
       }
     }
   } else if (warp >= kFwdProWarp0 && warp < kEpiWarp0) {

@@ -60,17 +60,23 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   }
   const bool has_aux = (a.epilogue & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) != 0;
   const bool has_res = (a.epilogue & MEDNEXT_EPI_RESIDUAL) != 0;
+  const bool pro_store = PRO != MEDNEXT_PRO_NONE && a.pro_out != nullptr;
   if ((has_aux && !a16(a.aux)) || (has_res && !a16(a.residual))) return -1;
-  if (!a16(a.y)) return -1;
-  CUtensorMap mA, mB, mAux, mRes, mY;
+  if (!a16(a.y) || (pro_store && !a16(a.pro_out))) return -1;
+  CUtensorMap mA, mB, mAux, mRes, mY, mP;
   memset(&mAux, 0, sizeof(mAux));
   memset(&mRes, 0, sizeof(mRes));
+  memset(&mP, 0, sizeof(mP));
   if (!encode3<TY>(&mY, a.y, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 32, kPwCW,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
     return -1;
   const int a_rows = std::min(kPwBK, (a.cin + 15) / 16 * 16);
   if (!encode3<TA>(&mA, a.a, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64, (uint32_t)a_rows,
                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return -1;
+  // the prologue output leaves through the A stage's own (swizzled) layout
+  if (pro_store && !encode3<TA>(&mP, a.pro_out, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64,
+                                (uint32_t)a_rows, CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
   if (!encode2<TA>(&mB, wt, (uint64_t)wk, (uint64_t)a.cout, kPwBK, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
@@ -82,6 +88,7 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
     return -1;
   PwTmaCfg cfg{};
   cfg.a_rows = a_rows;
+  cfg.pro_store = pro_store ? 1 : 0;
   cfg.kstages = (a.cin + kPwBK - 1) / kPwBK;
   cfg.total_tiles = a.S * a.ntiles * a.mtiles;
   cfg.b_bytes = a.BN * 128;
@@ -107,13 +114,13 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   cfg.nacc = (int)std::min<uint32_t>(kMaxAcc, 512u / tmem_cols_for(a.BN));
   const long long room = (long long)budget - (long long)cfg.estages * (long long)ebytes;
   cfg.stages = (int)std::min<long long>(kMaxStages, room / (long long)per_stage);
-  if (cfg.stages < 2) return -1;
+  if (cfg.stages < 2 || (pro_store && cfg.stages <= kProStoreLag)) return -1;
   const size_t smem = 1024 + cfg.stages * per_stage + w_bytes + cfg.estages * ebytes + stg;
   auto kern = pw_tma_fwd_kernel<TA, TY, PRO, EPI>;
   static size_t configured = 0;
   set_smem(kern, smem, configured);
   const int grid = std::min(cfg.total_tiles, num_sms());
-  kern<<<grid, kFwdThreads, smem, s>>>(mA, mB, mAux, mRes, mY, a, cfg);
+  kern<<<grid, kFwdThreads, smem, s>>>(mA, mB, mAux, mRes, mY, mP, a, cfg);
   return record_launch();
 }
 
@@ -128,6 +135,13 @@ int launch_pw_fwd(const PwFwdArgs& a, cudaStream_t s) {
   set_smem(kern, smem, configured);
   const long long grid = (long long)a.S * a.ntiles * a.mtiles;
   kern<<<(unsigned)grid, kPwThreads, smem, s>>>(a);
+  int rc = record_launch();
+  if (rc != MEDNEXT_OK || PRO == MEDNEXT_PRO_NONE || a.pro_out == nullptr) return rc;
+  // the first-generation kernel keeps its transformed tiles private: write pro(a) separately
+  const long long total = (long long)a.S * a.cin * a.vox;
+  const unsigned blocks = (unsigned)std::min<long long>((total + 255) / 256, 148LL * 32);
+  pw_prologue_out_kernel<TA, PRO><<<blocks, 256, 0, s>>>(static_cast<const TA*>(a.a), static_cast<TA*>(a.pro_out),
+                                                         a.pro_stats, a.pro_gamma, a.pro_beta, a.cin, a.vox, total);
   return record_launch();
 }
 // Compile-time epilogue for the flag sets the MedNeXt block uses; any other set

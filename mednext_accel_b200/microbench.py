@@ -40,6 +40,7 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
     stats = gn_stats(t, 1e-5)
     dz, part = pw_gemm(du, (r(C, RC) * 0.2), C, aux=t, gn_bwd_stats=stats)
     wp_t, we_t = wp.t().contiguous(), we.t().contiguous()
+    gout = torch.empty_like(u)
     vol = (1, C, 128, 128, 128)
     x5, dy5 = x.view(vol), dy.view(vol)
     w3 = (torch.randn(C, 1, 3, 3, 3, device=dev) * 0.2).to(bf)
@@ -53,11 +54,15 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
             (C + RC) * 2 * V),
         "pw project fwd (GELU prologue, bias, residual)": (
             lambda: pw_gemm(u, wp, C, prologue=nat.PRO_GELU, bias=b2, residual=x), (RC + C + C) * 2 * V),
+        "pw project fwd + GELU output": (
+            lambda: pw_gemm(u, wp, C, prologue=nat.PRO_GELU, bias=b2, residual=x, pro_out=gout),
+            (RC + C + C + RC) * 2 * V),
         "pw project dgrad (GELU' epilogue)": (
             lambda: pw_gemm(dy, wp_t, RC, aux=u, gelu_grad=True), (C + RC + RC) * 2 * V),
         "pw expand dgrad (GroupNorm-backward sums)": (
             lambda: pw_gemm(du, we_t, C, aux=t, gn_bwd_stats=stats), (RC + C + C) * 2 * V),
         "pw project wgrad (GELU prologue)": (lambda: pw_wgrad(dy, u, prologue=nat.PRO_GELU), (C + RC) * 2 * V),
+        "pw project wgrad (saved GELU output)": (lambda: pw_wgrad(dy, gout), (C + RC) * 2 * V),
         "pw expand wgrad (GroupNorm prologue)": (
             lambda: pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g, pro_beta=bb),
             (C + RC) * 2 * V),

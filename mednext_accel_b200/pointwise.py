@@ -45,10 +45,12 @@ def pw_gemm(
     gelu_grad: bool = False,
     gn_bwd_stats: Tensor | None = None,
     out: Tensor | None = None,
+    pro_out: Tensor | None = None,
 ) -> tuple[Tensor, Tensor | None]:
     """y[s, j, v] = epi(sum_k wt[j, k] * pro(a[s, k, v])) on the tensor cores.
 
     ``a``: [S, cin, *spatial]; ``wt``: [cout, cin] contiguous in a's dtype.
+    ``pro_out`` (shape and dtype of ``a``): receives pro(a) as the GEMM consumed it.
     Returns (y, gn_partial_workspace or None)."""
     nat.require_device(a)
     lib = nat.load()
@@ -67,14 +69,16 @@ def pw_gemm(
         epi |= nat.EPI_GN_BWD_STATS
     ws_bytes = lib.mednext_pw_fwd_workspace_size(n, cin, cout, vox, epi)
     ws = nat.workspace(ws_bytes, a.device) if ws_bytes > 0 else None
+    if pro_out is not None and (pro_out.shape != a.shape or pro_out.dtype != a.dtype or not pro_out.is_contiguous()):
+        raise ValueError("pro_out must be a contiguous tensor of a's shape and dtype")
     nat.check(
-        lib.mednext_pw_fwd(
+        lib.mednext_pw_fwd_pro_out(
             a.data_ptr(), wt.data_ptr(), y.data_ptr(), prologue, nat.ptr(pro_stats), nat.ptr(pro_gamma),
             nat.ptr(pro_beta), epi, nat.ptr(bias), nat.ptr(residual), nat.ptr(aux), nat.ptr(gn_bwd_stats),
-            nat.ptr(ws), 0 if ws is None else ws.numel(), n, cin, cout, vox,
+            nat.ptr(pro_out), nat.ptr(ws), 0 if ws is None else ws.numel(), n, cin, cout, vox,
             nat.dtype_code(a.dtype), nat.dtype_code(y.dtype), nat.stream(),
         ),
-        "mednext_pw_fwd",
+        "mednext_pw_fwd_pro_out",
     )
     return y, ws
 

@@ -227,5 +227,53 @@ def test_gelu_grad_epilogue_matches_torch_on_every_bf16_value():
     _compare_to_torch(du.flatten()[:count], want.to(torch.bfloat16).flatten()[:count], "gelu'")
 
 
+PRO_OUT_SHAPES = [
+    (1, 32, 64, (16, 16, 16)),
+    (2, 64, 32, (8, 8, 8)),
+    (2, 96, 192, (5, 7, 9)),     # odd voxel count: first-generation kernel + separate prologue output
+    (1, 128, 512, (8, 8, 8)),    # two K stages per tile
+    (1, 64, 32, (64, 64, 64)),   # 2048 tiles: every ring stage is stored and released many times
+]
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", PRO_OUT_SHAPES)
+@pytest.mark.parametrize("prologue", [nat.PRO_GELU, nat.PRO_GROUPNORM])
+def test_prologue_output(n, cin, cout, spatial, prologue):
+    """pro_out holds pro(a) exactly as the GEMM consumed it; y is unchanged by asking for it."""
+    a = (rand((n, cin, *spatial), 21).double() * 2 + 0.5).to(torch.bfloat16).cuda()
+    w = rand((cout, cin), 22, scale=1 / np.sqrt(cin)).cuda()
+    b = rand((cout,), 23, torch.float32).cuda()
+    kw = {}
+    if prologue == nat.PRO_GROUPNORM:
+        gamma = (1 + 0.2 * rand((cin,), 24, torch.float64)).float().cuda()
+        beta = (0.2 * rand((cin,), 25, torch.float64)).float().cuda()
+        kw = dict(pro_stats=gn_stats(a, 1e-5), pro_gamma=gamma, pro_beta=beta)
+    y0, _ = pw_gemm(a, w, cout, prologue=prologue, bias=b, **kw)
+    g = torch.full_like(a, float("nan"))
+    y1, _ = pw_gemm(a, w, cout, prologue=prologue, bias=b, pro_out=g, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1)
+    if prologue == nat.PRO_GELU:
+        want = orc.round_bf16(orc.gelu(h(a)))
+    else:
+        z, _, _ = orc.groupnorm_fwd(h(a), h(kw["pro_gamma"]), h(kw["pro_beta"]))
+        want = orc.round_bf16(z)
+    assert not torch.isnan(g).any()
+    assert_close_bf16(g, want, "pro_out", rel_l2=2e-3, max_rel=1e-2)
+    # the same prologue through the identity GEMM is bit-identical to pro_out
+    if cin <= 256:
+        eye = torch.eye(cin, dtype=torch.bfloat16, device="cuda")
+        yi, _ = pw_gemm(a, eye, cin, prologue=prologue, **kw)
+        assert torch.equal(yi, g)
+
+
+def test_gelu_prologue_output_on_every_bf16_value():
+    a, count = _all_finite_bf16(16)
+    eye = torch.eye(16, dtype=torch.bfloat16, device="cuda")
+    g = torch.empty_like(a)
+    y, _ = pw_gemm(a, eye, 16, prologue=nat.PRO_GELU, pro_out=g)
+    assert torch.equal(y, g)
+
+
 def test_no_device_error_recorded():
     assert nat.device_error() == 0
