@@ -530,20 +530,32 @@ __global__ void __launch_bounds__(kPwThreads) pw_wgrad_kernel(PwWgradArgs p) {
 }
 
 // dw[j,k] = sum_split part[split][j][k];  dbias[j] = sum_split part_b[split][j]
-static __global__ void pw_wgrad_reduce_kernel(const float* __restrict__ part, const float* __restrict__ part_b,
-                                       float* __restrict__ dw, float* __restrict__ dbias, int splits,
-                                       int cout, int cin) {
-  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+// A block reduces 32 consecutive outputs (dw then dbias, one index space) with
+// kPwRedGroups split groups: group g adds splits g, g + G, g + 2G, ... in order,
+// then the group sums are added in group order.  The order is fixed, so the
+// result is deterministic; each warp reads 128 contiguous bytes of one split.
+constexpr int kPwRedGroups = 8;
+static __global__ void __launch_bounds__(32 * kPwRedGroups)
+    pw_wgrad_reduce_kernel(const float* __restrict__ part, const float* __restrict__ part_b, float* __restrict__ dw,
+                           float* __restrict__ dbias, int splits, int cout, int cin) {
+  __shared__ float acc[kPwRedGroups][32];
+  const int o = threadIdx.x & 31, g = threadIdx.x >> 5;
   const long long nw = (long long)cout * cin;
+  const long long idx = (long long)blockIdx.x * 32 + o;
+  float sum = 0.f;
   if (idx < nw) {
-    float s = 0.f;
-    for (int i = 0; i < splits; ++i) s += part[(size_t)i * nw + idx];
-    dw[idx] = s;
+    for (int i = g; i < splits; i += kPwRedGroups) sum += part[(size_t)i * nw + idx];
   } else if (idx < nw + cout) {
-    const int j = (int)(idx - nw);
-    float s = 0.f;
-    for (int i = 0; i < splits; ++i) s += part_b[(size_t)i * cout + j];
-    if (dbias != nullptr) dbias[j] = s;
+    for (int i = g; i < splits; i += kPwRedGroups) sum += part_b[(size_t)i * cout + (idx - nw)];
+  }
+  acc[g][o] = sum;
+  __syncthreads();
+  if (g == 0) {
+    float t = acc[0][o];
+#pragma unroll
+    for (int k = 1; k < kPwRedGroups; ++k) t += acc[k][o];
+    if (idx < nw) dw[idx] = t;
+    else if (idx < nw + cout && dbias != nullptr) dbias[idx - nw] = t;
   }
 }
 
