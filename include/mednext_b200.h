@@ -186,6 +186,18 @@ int mednext_dwT_dgrad(const void* dy, const void* weight, const void* addend, vo
  * others, zeros in the pitch tail.  With small = W x + bias from the pointwise
  * GEMM this is the output of the up block's ConvTranspose3d(1x1x1, stride 2)
  * residual branch (models/blocks.py:173-182). */
+/* out [n, c, d+1, h+1, w+1] = F.pad(v, (1, 0, 1, 0, 1, 0)) + addend, one rounding;
+ * v is the pitched [n, c, pitch] grid of (d, h, w) voxels, addend (out's shape,
+ * may be NULL) in the same dtype.  Replaces the up block's output pad and the
+ * decoder's skip add: models/blocks.py:177-181, models/mednext_v1.py:205. */
+int mednext_pad_front_add(const void* v, const void* addend, void* out, int64_t n, int64_t c,
+                          int64_t d, int64_t h, int64_t w, int64_t pitch, int dtype,
+                          mednext_stream_t stream);
+/* The inverse: v [n, c, pitch] = the (z, y, x >= 1) interior of padded
+ * [n, c, d+1, h+1, w+1], zero tail.  The grad of the up block's padded output,
+ * repacked for its GEMMs (the backward of models/blocks.py:178). */
+int mednext_unpad_front(const void* padded, void* v, int64_t n, int64_t c, int64_t d, int64_t h,
+                        int64_t w, int64_t pitch, int dtype, mednext_stream_t stream);
 int mednext_upsample2_fill(const void* small, const float* bias, void* big, int64_t n, int64_t c,
                            int64_t d, int64_t h, int64_t w, int64_t big_pitch, int dtype,
                            mednext_stream_t stream);

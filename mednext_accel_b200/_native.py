@@ -74,6 +74,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mednext_dwT_fwd": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_dwT_dgrad": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_upsample2_fill": (_INT, [_P, _P, _P] + _DIMS5 + [_I64, _INT, _P]),
+    "mednext_pad_front_add": (_INT, [_P, _P, _P] + _DIMS5 + [_I64, _INT, _P]),
+    "mednext_unpad_front": (_INT, [_P, _P] + _DIMS5 + [_I64, _INT, _P]),
     "mednext_dwT_wgrad_workspace_size": (_SZ, _DIMS5 + [_INT, _INT]),
     "mednext_dwT_wgrad": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_gn_stats_workspace_size": (_SZ, [_I64, _I64, _I64]),

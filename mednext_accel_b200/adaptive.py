@@ -316,7 +316,7 @@ class FusedBlockRunner:
         decision = self.decision(block, x)
         if decision.implementation == "reference":
             return None
-        from .block import KIND_REGULAR, dtype_code, mednext_block
+        from .block import KIND_REGULAR, KIND_UP, dtype_code, mednext_block
 
         cdt = compute_dtype(x)
         if cdt not in _AUTOCAST_COMPUTE:
@@ -325,7 +325,9 @@ class FusedBlockRunner:
             x = x.contiguous()
         keep = not (block.checkpoint_expansion or decision.parameters.get("recompute_expansion", False))
         # the down / up blocks' strided 1x1 residual convolution runs inside the operator
-        res = getattr(block, "residual", None) if self.kind != KIND_REGULAR and addend is None else None
+        # (the up block's addend is added after its pad, so its residual conv stays fused)
+        fuse_res = self.kind != KIND_REGULAR and (addend is None or self.kind == KIND_UP)
+        res = getattr(block, "residual", None) if fuse_res else None
         res_w = res.weight if res is not None else None
         res_b = res.bias if res is not None else None
         y, _, _, _ = mednext_block(

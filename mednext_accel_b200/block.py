@@ -177,7 +177,9 @@ def mednext_block(
     For the up block (kind 2) y is the final, left-padded (2S)^3 output of the
     reference's ``F.pad(block(x) + residual(x))`` and t, u are pitched
     [n, c, pitch] buffers whose rows hold the (2S-1)^3 voxels followed by a zero
-    tail, so that every GEMM operand has 16-byte aligned rows for TMA.
+    tail, so that every GEMM operand has 16-byte aligned rows for TMA.  Its
+    ``addend`` (the decoder's skip, models/mednext_v1.py:205) has the padded
+    shape and is added after the pad, in the same pass.
 
     ``res_w`` / ``res_b`` (down and up blocks, instead of ``addend``): the 1x1x1
     stride-2 residual convolution (models/blocks.py:128-136, 173-182) computed here
@@ -202,16 +204,11 @@ def mednext_block(
         if res_w is not None:
             rs, _ = pw_gemm(xb, prm.rw, cout, out_dtype=cdt, bias=prm.rb)
             res_p = dwk.upsample2_fill(rs, prm.rb, pitch)
-            res = res_p
-        elif res is not None:
-            res_p = torch.empty((x.shape[0], cout, pitch), dtype=res.dtype, device=x.device)
-            dwk.pitched_view(res_p, big).copy_(res)
-            res_p[:, :, vox:].zero_()
-        y_p, _ = pw_gemm(
-            u, prm.pw, cout, out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
-            bias=prm.pb, residual=res_p,
-        )
-        y = F.pad(dwk.pitched_view(y_p, big), (1, 0) * 3)
+        y_p, _ = pw_gemm(u, prm.pw, cout, out_dtype=cdt, prologue=nat.PRO_GELU, bias=prm.pb, residual=res_p)
+        if addend is not None and addend.dtype != cdt:
+            y = F.pad(dwk.pitched_view(y_p, big), (1, 0) * 3) + addend
+        else:
+            y = dwk.pad_front_add(y_p, big, addend)
         return y, t, (u if keep_expansion else u.new_empty((0,))), stats
     t, stats = _depthwise_forward(xb, wdw, bdw, kind, kernel_size, eps)
     if res_w is not None and kind == KIND_DOWN:
@@ -233,6 +230,7 @@ def _(x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, res_w, res_b, kind,
     res = x if residual_is_input else addend
     ydt = res.dtype if res is not None and res_w is None else cdt
     if kind == KIND_UP:
+        ydt = torch.promote_types(cdt, addend.dtype) if addend is not None else cdt
         big = tuple(2 * s - 1 for s in sp)
         _, pitch = _pitch(big)
         y = x.new_empty((n, p_w.shape[0], *(2 * s for s in sp)), dtype=ydt)
@@ -279,9 +277,7 @@ def mednext_block_backward(
         # repacked into a pitched buffer with a zero tail
         big = tuple(2 * int(s) - 1 for s in x.shape[2:])
         vox, pitch = _pitch(big)
-        dyb = torch.empty((x.shape[0], cout, pitch), dtype=cdt, device=dy.device)
-        dwk.pitched_view(dyb, big).copy_(dy[:, :, 1:, 1:, 1:])
-        dyb[:, :, vox:].zero_()
+        dyb = dwk.unpad_front(dy.to(cdt), pitch)
     else:
         dy = dy.contiguous()
         dyb = dy.to(cdt)
@@ -395,8 +391,8 @@ def _backward(ctx, dy, _dt, _du, _dstats):
         drw = drb = None
     d_add = None
     if ctx.has_addend and ctx.needs_input_grad[1]:
-        g = dy[:, :, 1:, 1:, 1:] if ctx.kind == KIND_UP else dy  # the up block's output is left-padded
-        d_add = g if g.dtype == ctx.addend_dtype else g.to(ctx.addend_dtype)
+        # the up block's addend is added after the pad: its grad is all of dy
+        d_add = dy if dy.dtype == ctx.addend_dtype else dy.to(ctx.addend_dtype)
     return dx, d_add, dww, dwb, dgw, dgb, dew, deb, dpw, dpb, drw, drb, None, None, None, None, None, None
 
 

@@ -260,6 +260,36 @@ int mednext_upsample2_fill(const void* small, const float* bias, void* big, int6
   return dispatch_upsample2_fill(dtype, small, bias, big, s2_geom_up(n, c, d, h, w, big_pitch), as_stream(stream));
 }
 
+static DwS2Geom pad_geom(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t pitch) {
+  DwS2Geom g{};
+  g.N = (int)n; g.C = (int)c;
+  g.Db = (int)d; g.Hb = (int)h; g.Wb = (int)w;
+  g.bp = pitch;
+  return g;
+}
+
+int mednext_pad_front_add(const void* v, const void* addend, void* out, int64_t n, int64_t c, int64_t d, int64_t h,
+                          int64_t w, int64_t pitch, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d + 1, h + 1, w + 1, 1, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (d < 1 || h < 1 || w < 1 || !pitch_ok(pitch, d * h * w)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (v == nullptr || out == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(v, esz) || !aligned(out, esz) || (addend && !aligned(addend, esz))) return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_pad_front(dtype, v, addend, out, pad_geom(n, c, d, h, w, pitch), false, as_stream(stream));
+}
+
+int mednext_unpad_front(const void* padded, void* v, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                        int64_t pitch, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d + 1, h + 1, w + 1, 1, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (d < 1 || h < 1 || w < 1 || !pitch_ok(pitch, d * h * w)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (padded == nullptr || v == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(padded, esz) || !aligned(v, esz)) return MEDNEXT_ERR_ALIGNMENT;
+  return dispatch_pad_front(dtype, padded, nullptr, v, pad_geom(n, c, d, h, w, pitch), true, as_stream(stream));
+}
+
 size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
   if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
   return s2_wgrad_ws(n, c, d, k, dtype);

@@ -237,6 +237,86 @@ __global__ void __launch_bounds__(kS2Warps * 32) upsample2_fill_kernel(const T* 
   }
 }
 
+// F.pad(v, (1, 0, 1, 0, 1, 0)) of the pitched grid v (Db, Hb, Wb), plus an
+// optional addend of the padded shape (Db+1, Hb+1, Wb+1), in one pass:
+//   out[nc, z, y, x] = (z, y, x > 0 ? v[nc, z-1, y-1, x-1] : 0) + addend[nc, z, y, x]
+// with the sum rounded once, as torch's add of the two tensors does.  The up
+// block's output (models/blocks.py:177-181) and the decoder's skip add
+// (models/mednext_v1.py:205).  CTA = (n, c, output plane); warps take rows,
+// lanes run along W.
+template <typename T>
+__global__ void __launch_bounds__(kS2Warps * 32) pad_front_add_kernel(const T* __restrict__ v,
+                                                                      const T* __restrict__ addend,
+                                                                      T* __restrict__ out, DwS2Geom g) {
+  using Acc = typename Elem<T>::Acc;
+  constexpr int E = 16 / (int)sizeof(T);  // elements per 16-byte chunk
+  const int Dp = g.Db + 1, Hp = g.Hb + 1, Wp = g.Wb + 1;
+  const int z = (int)(blockIdx.x % (unsigned)Dp);
+  const int nc = (int)(blockIdx.x / (unsigned)Dp);
+  const size_t plane = ((size_t)nc * Dp + z) * ((size_t)Hp * Wp);
+  T* dst = out + plane;
+  const T* add = addend != nullptr ? addend + plane : nullptr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // padded rows of whole 16-byte chunks: one chunk of the output (and addend) per
+  // lane step; the source row is shifted by one element, so it is read per element
+  const bool vec = sizeof(T) <= 4 && Wp % E == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                   (add == nullptr || (reinterpret_cast<uintptr_t>(addend) & 15) == 0);
+  if (vec) {
+    // the plane's 16-byte output chunks are spread over all the CTA's threads
+    const int cpr = Wp / E;  // chunks per row
+    for (int q = threadIdx.x; q < Hp * cpr; q += blockDim.x) {
+      const int y = q / cpr, x0 = (q - y * cpr) * E;
+      Acc a[E];
+      if (add != nullptr) {
+        unpack16<T>(*reinterpret_cast<const uint4*>(add + (size_t)y * Wp + x0), a);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) a[e] = Acc(0);
+      }
+      if (z > 0 && y > 0) {
+        const T* srow = v + (size_t)nc * (size_t)g.bp + ((size_t)(z - 1) * g.Hb + (y - 1)) * g.Wb;
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+          if (x0 + e > 0) a[e] += to_acc<T>(srow[x0 + e - 1]);
+      }
+      *reinterpret_cast<uint4*>(dst + (size_t)y * Wp + x0) = pack16<T>(a);
+    }
+    return;
+  }
+  for (int y = warp; y < Hp; y += kS2Warps) {
+    const bool row_in = z > 0 && y > 0;
+    const T* srow = row_in ? v + (size_t)nc * (size_t)g.bp + ((size_t)(z - 1) * g.Hb + (y - 1)) * g.Wb : nullptr;
+    for (int x = lane; x < Wp; x += 32) {
+      Acc a = (row_in && x > 0) ? to_acc<T>(srow[x - 1]) : Acc(0);
+      if (add != nullptr) a += to_acc<T>(add[(size_t)y * Wp + x]);
+      dst[(size_t)y * Wp + x] = from_acc<T>(a);
+    }
+  }
+}
+
+// The inverse: the interior (z, y, x >= 1) of a left-padded (Db+1, Hb+1, Wb+1)
+// volume into the pitched grid, with a zero pitch tail.  The up block's output
+// grad, repacked for its GEMMs.  CTA = (n, c, interior plane).
+template <typename T>
+__global__ void __launch_bounds__(kS2Warps * 32) unpad_front_kernel(const T* __restrict__ padded,
+                                                                    T* __restrict__ v, DwS2Geom g) {
+  const int Hp = g.Hb + 1, Wp = g.Wb + 1;
+  const int z = (int)(blockIdx.x % (unsigned)g.Db);
+  const int nc = (int)(blockIdx.x / (unsigned)g.Db);
+  // padded row y+1 of plane z+1; output element x is its element x+1
+  const T* src = padded + ((size_t)nc * (g.Db + 1) + (z + 1)) * ((size_t)Hp * Wp) + Wp;
+  T* vol = v + (size_t)nc * (size_t)g.bp;
+  T* dst = vol + (size_t)z * g.Hb * g.Wb;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // lanes on consecutive elements: both the (shifted) reads and the writes coalesce
+  for (int y = warp; y < g.Hb; y += kS2Warps)
+    for (int x = lane; x < g.Wb; x += 32) dst[(size_t)y * g.Wb + x] = src[(size_t)y * Wp + x + 1];
+  if (z == g.Db - 1) {
+    const size_t vox = (size_t)g.Db * g.Hb * g.Wb;
+    for (size_t e = vox + threadIdx.x; e < (size_t)g.bp; e += blockDim.x) vol[e] = from_acc<T>(0.0f);
+  }
+}
+
 // wgrad: the CTA's threads form K groups (group g owns the K*K taps with kd = g,
 // and its warps take the small-grid rows in turn).  A CTA covers `chunk`
 // consecutive small-grid planes of one (sample, channel); with `small_bias` it

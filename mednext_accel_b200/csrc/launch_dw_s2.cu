@@ -45,6 +45,18 @@ int launch_upsample2_fill(const void* small, const float* bias, void* big, const
                                                                     static_cast<T*>(big), g);
   return record_launch();
 }
+template <typename T>
+int launch_pad_front(const void* v, const void* addend, void* out, const DwS2Geom& g, bool unpad, cudaStream_t s) {
+  const long long ctas = (long long)g.N * g.C * (unpad ? g.Db : g.Db + 1);
+  if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (unpad)
+    unpad_front_kernel<T><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(static_cast<const T*>(v), static_cast<T*>(out), g);
+  else
+    pad_front_add_kernel<T><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(static_cast<const T*>(v),
+                                                                      static_cast<const T*>(addend),
+                                                                      static_cast<T*>(out), g);
+  return record_launch();
+}
 template <typename T, int K>
 int launch_s2_wgrad(const void* big, const void* small, void* dw, void* db, void* ws, const DwS2Geom& g,
                     bool bias_from_big, cudaStream_t s) {
@@ -104,6 +116,12 @@ int dispatch_upsample2_fill(int dtype, const void* small, const float* bias, voi
                             cudaStream_t s) {
   int st = MEDNEXT_OK;
   MEDNEXT_T_SWITCH(dtype, T, st = (launch_upsample2_fill<T>(small, bias, big, g, s)));
+  return st;
+}
+int dispatch_pad_front(int dtype, const void* v, const void* addend, void* out, const DwS2Geom& g, bool unpad,
+                       cudaStream_t s) {
+  int st = MEDNEXT_OK;
+  MEDNEXT_T_SWITCH(dtype, T, st = (launch_pad_front<T>(v, addend, out, g, unpad, s)));
   return st;
 }
 int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,

@@ -84,8 +84,10 @@ int dispatch_pw_wgrad(int dtype, int prologue, const PwWgradArgs& a, int splits,
   if (dtype == MEDNEXT_FLOAT16) st = pw_wgrad_pro<__half>(prologue, a, s);
   if (st != MEDNEXT_OK) return st;
   const long long total = (long long)a.cout * a.cin + a.cout;
-  pw_wgrad_reduce_kernel<<<(unsigned)((total + 31) / 32), 32 * kPwRedGroups, 0, s>>>(a.part, a.part_b, a.dw, a.dbias,
-                                                                                      splits, a.cout, a.cin);
+  const int groups = splits >= 32 ? 8 : 1;
+  const int per = kPwRedThreads / groups;
+  pw_wgrad_reduce_kernel<<<(unsigned)((total + per - 1) / per), kPwRedThreads, 0, s>>>(a.part, a.part_b, a.dw, a.dbias,
+                                                                                      splits, a.cout, a.cin, groups);
   return record_launch();
 }
 

@@ -157,6 +157,8 @@ int dispatch_dw_s1_wgrad(int dtype, int k, const void* x, const void* dy, void* 
                          const S1Plan& p, cudaStream_t s);
 int dispatch_upsample2_fill(int dtype, const void* small, const float* bias, void* big, const DwS2Geom& g,
                             cudaStream_t s);
+int dispatch_pad_front(int dtype, const void* v, const void* addend, void* out, const DwS2Geom& g, bool unpad,
+                       cudaStream_t s);
 int dispatch_dw_s2_gather(int dtype, int k, const void* big, const void* w, const void* b, const void* addend,
                           void* small,
                           const DwS2Geom& g, cudaStream_t s);

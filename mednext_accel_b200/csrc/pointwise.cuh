@@ -530,33 +530,50 @@ __global__ void __launch_bounds__(kPwThreads) pw_wgrad_kernel(PwWgradArgs p) {
 }
 
 // dw[j,k] = sum_split part[split][j][k];  dbias[j] = sum_split part_b[split][j]
-// A block reduces 32 consecutive outputs (dw then dbias, one index space) with
-// kPwRedGroups split groups: group g adds splits g, g + G, g + 2G, ... in order,
-// then the group sums are added in group order.  The order is fixed, so the
-// result is deterministic; each warp reads 128 contiguous bytes of one split.
-constexpr int kPwRedGroups = 8;
-static __global__ void __launch_bounds__(32 * kPwRedGroups)
+// A block of kPwRedThreads reduces kPwRedThreads / groups consecutive outputs (dw
+// then dbias, one index space) with `groups` split groups: group g adds splits
+// g, g + groups, ... in order (loads issued four at a time), then the group sums
+// are added in group order.  The order is fixed, so the result is deterministic.
+// Many splits and few outputs (level 0) take 8 groups; few splits one.
+constexpr int kPwRedThreads = 256;
+static __global__ void __launch_bounds__(kPwRedThreads)
     pw_wgrad_reduce_kernel(const float* __restrict__ part, const float* __restrict__ part_b, float* __restrict__ dw,
-                           float* __restrict__ dbias, int splits, int cout, int cin) {
-  __shared__ float acc[kPwRedGroups][32];
-  const int o = threadIdx.x & 31, g = threadIdx.x >> 5;
+                           float* __restrict__ dbias, int splits, int cout, int cin, int groups) {
+  __shared__ float acc[kPwRedThreads];
+  const int per = kPwRedThreads / groups;  // outputs per block
+  const int o = threadIdx.x % per, g = threadIdx.x / per;
   const long long nw = (long long)cout * cin;
-  const long long idx = (long long)blockIdx.x * 32 + o;
-  float sum = 0.f;
+  const long long idx = (long long)blockIdx.x * per + o;
+  const float* src = nullptr;
+  size_t stride = 0;
   if (idx < nw) {
-    for (int i = g; i < splits; i += kPwRedGroups) sum += part[(size_t)i * nw + idx];
+    src = part + idx;
+    stride = (size_t)nw;
   } else if (idx < nw + cout) {
-    for (int i = g; i < splits; i += kPwRedGroups) sum += part_b[(size_t)i * cout + (idx - nw)];
+    src = part_b + (idx - nw);
+    stride = (size_t)cout;
   }
-  acc[g][o] = sum;
-  __syncthreads();
-  if (g == 0) {
-    float t = acc[0][o];
-#pragma unroll
-    for (int k = 1; k < kPwRedGroups; ++k) t += acc[k][o];
-    if (idx < nw) dw[idx] = t;
-    else if (idx < nw + cout && dbias != nullptr) dbias[idx - nw] = t;
+  float sum = 0.f;
+  if (src != nullptr) {
+    int i = g;
+    for (; i + 3 * groups < splits; i += 4 * groups) {
+      const float a0 = src[(size_t)i * stride], a1 = src[(size_t)(i + groups) * stride];
+      const float a2 = src[(size_t)(i + 2 * groups) * stride], a3 = src[(size_t)(i + 3 * groups) * stride];
+      sum += a0;
+      sum += a1;
+      sum += a2;
+      sum += a3;
+    }
+    for (; i < splits; i += groups) sum += src[(size_t)i * stride];
   }
+  if (groups > 1) {
+    acc[threadIdx.x] = sum;
+    __syncthreads();
+    if (g != 0) return;
+    for (int k = 1; k < groups; ++k) sum += acc[k * per + o];
+  }
+  if (idx < nw) dw[idx] = sum;
+  else if (idx < nw + cout && dbias != nullptr) dbias[idx - nw] = sum;
 }
 
 }  // namespace mednext

@@ -228,6 +228,44 @@ def _check_addend(t: Tensor, shape, dtype, name: str) -> None:
         raise ValueError(f"{name} must be a CUDA tensor of shape {tuple(shape)} and dtype {dtype}")
 
 
+def pad_front_add(v: Tensor, spatial: tuple[int, int, int], addend: Tensor | None = None) -> Tensor:
+    """``F.pad(pitched_view(v, spatial), (1, 0) * 3) + addend`` in one pass: ``v`` is a
+    pitched [n, c, pitch] buffer of the (d, h, w) grid, ``addend`` (optional) has the
+    padded shape [n, c, d+1, h+1, w+1] and v's dtype."""
+    nat.require_device(v)
+    n, c = int(v.shape[0]), int(v.shape[1])
+    d, h, w = (int(s) for s in spatial)
+    out = torch.empty((n, c, d + 1, h + 1, w + 1), dtype=v.dtype, device=v.device)
+    if addend is not None:
+        if addend.shape != out.shape or addend.dtype != v.dtype:
+            raise ValueError("addend must have the padded shape and v's dtype")
+        addend = addend.contiguous()
+    nat.check(
+        nat.load().mednext_pad_front_add(
+            v.data_ptr(), nat.ptr(addend), out.data_ptr(), n, c, d, h, w, int(v.shape[2]),
+            nat.dtype_code(v.dtype), nat.stream(),
+        ),
+        "mednext_pad_front_add",
+    )
+    return out
+
+
+def unpad_front(padded: Tensor, pitch: int) -> Tensor:
+    """The pitched [n, c, pitch] buffer of ``padded[:, :, 1:, 1:, 1:]`` with a zero tail."""
+    nat.require_device(padded)
+    n, c = int(padded.shape[0]), int(padded.shape[1])
+    d, h, w = (int(s) - 1 for s in padded.shape[2:])
+    padded = padded.contiguous()
+    v = torch.empty((n, c, int(pitch)), dtype=padded.dtype, device=padded.device)
+    nat.check(
+        nat.load().mednext_unpad_front(
+            padded.data_ptr(), v.data_ptr(), n, c, d, h, w, int(pitch), nat.dtype_code(padded.dtype), nat.stream(),
+        ),
+        "mednext_unpad_front",
+    )
+    return v
+
+
 def upsample2_fill(small: Tensor, bias: Tensor | None, pitch: int) -> Tensor:
     """[n, c, pitch] buffer holding the (2d-1, 2h-1, 2w-1) grid with small[m] at the
     all-even positions 2m, bias[c] elsewhere and a zero pitch tail: the output of a

@@ -304,10 +304,13 @@ class MedNeXtUpBlock(MedNeXtBlock):
         self.residual = up(in_channels, out_channels, kernel_size=1, stride=2) if residual else None
         self._pad = (1, 0) * spatial_dims
 
-    def forward(self, x: Tensor) -> Tensor:
+    def forward(self, x: Tensor, addend: Tensor | None = None) -> Tensor:
+        """``addend`` (optional, the padded output's shape): added to the output, as
+        the decoder adds its encoder skip (models/mednext_v1.py:205); the fused
+        operator does it in the pass that writes the padded output."""
         # the fused operator computes the strided residual convolution itself and
         # returns the padded output
-        out = self._fused_call(x, None, False)
+        out = self._fused_call(x, addend, False)
         if out is not None:
             return out
         skip = self.residual(x) if self.residual is not None else None
@@ -315,7 +318,8 @@ class MedNeXtUpBlock(MedNeXtBlock):
         if skip is not None:
             out = out + skip
         # pad(a) + pad(b) == pad(a + b): one pad after the residual add
-        return F.pad(out, self._pad)
+        out = F.pad(out, self._pad)
+        return out + addend if addend is not None else out
 
 
 class OutputHead(nn.Module):
@@ -405,14 +409,16 @@ class MedNeXtV1(nn.Module):
                 for s in (4, 3, 2, 1)
             )
 
-    def _run(self, module: nn.Module, x: Tensor, stage: int) -> Tensor:
+    def _run(self, module: nn.Module, x: Tensor, stage: int, addend: Tensor | None = None) -> Tensor:
+        """module(x), or module(x, addend) for an up block given the decoder skip."""
+        args = (x,) if addend is None else (x, addend)
         cfg = self.checkpointing
         if (
             cfg is not None and cfg.checkpoints_blocks and cfg.includes(stage) and self.training
             and torch.is_grad_enabled()
         ):
-            return checkpoint(module, x, use_reentrant=False)
-        return module(x)
+            return checkpoint(module, *args, use_reentrant=False)
+        return module(*args)
 
     def _stage(self, modules: nn.Sequential, x: Tensor, stage: int) -> Tensor:
         for module in modules:
@@ -433,7 +439,7 @@ class MedNeXtV1(nn.Module):
             stage = 3 - i
             if supervise:
                 aux.append(self.deep_supervision_heads[i](x))
-            x = self._run(self.upsamples[i], x, stage) + skips[stage]
+            x = self._run(self.upsamples[i], x, stage, skips[stage])
             x = self._stage(self.decoder_stages[i], x, stage)
         primary = self.head(x)
         if not supervise:

@@ -243,5 +243,50 @@ def test_loss_curve_matches_native_path_over_adamw_steps():
         assert abs(losses[0] - losses[1]) <= 1e-2 * abs(losses[1]), losses
 
 
+@pytest.mark.parametrize("spatial", [(7, 9, 11), (15, 15, 15), (127, 127, 127)])
+@pytest.mark.parametrize("with_addend", [False, True])
+def test_pad_front_and_unpad_match_torch(spatial, with_addend):
+    from mednext_accel_b200 import depthwise as dwk
+
+    n, c = 2, 3
+    vox = spatial[0] * spatial[1] * spatial[2]
+    pitch = (vox + 7) // 8 * 8
+    gen = torch.Generator().manual_seed(_seed("pad", spatial))
+    v = torch.randn((n, c, pitch), generator=gen).to(torch.bfloat16).cuda()
+    padded_shape = (n, c, *(s + 1 for s in spatial))
+    addend = torch.randn(padded_shape, generator=gen).to(torch.bfloat16).cuda() if with_addend else None
+    got = dwk.pad_front_add(v, spatial, addend)
+    want = F.pad(dwk.pitched_view(v, spatial), (1, 0) * 3)
+    if addend is not None:
+        want = want + addend
+    assert torch.equal(got, want)
+    back = dwk.unpad_front(got if addend is None else want, pitch)
+    want_back = torch.zeros_like(v)
+    dwk.pitched_view(want_back, spatial).copy_((want)[:, :, 1:, 1:, 1:])
+    assert torch.equal(back, want_back)
+
+
+def test_up_block_skip_addend_is_fused_exactly():
+    """block(x, addend=skip) == block(x) + skip, and the skip's grad is dy."""
+    block = make_block("up", 32, 16, 2, 3, 7)
+    gen = torch.Generator().manual_seed(8)
+    x = torch.randn((1, 32, 8, 8, 8), generator=gen).to(torch.bfloat16)
+    skip = torch.randn((1, 16, 16, 16, 16), generator=gen).to(torch.bfloat16).cuda()
+    dy = torch.randn((1, 16, 16, 16, 16), generator=gen).to(torch.bfloat16).cuda()
+    blk = install(copy.deepcopy(block)).cuda().train()
+    xg = x.cuda().requires_grad_()
+    sg = skip.clone().requires_grad_()
+    with torch.autocast("cuda", dtype=torch.bfloat16), OpSpy() as spy:
+        y1 = blk(xg, sg)
+        y0 = blk(xg)
+    assert spy.ops.count("mednext_accel_b200::mednext_block") == 2
+    assert torch.equal(y1, y0 + skip)
+    g1 = torch.autograd.grad(y1, (xg, sg, *blk.parameters()), dy)
+    g0 = torch.autograd.grad(y0, (xg, *blk.parameters()), dy)
+    assert torch.equal(g1[1], dy)
+    for a, b in zip((g1[0], *g1[2:]), g0, strict=True):
+        assert torch.equal(a, b)
+
+
 def test_no_device_error_recorded():
     assert nat.device_error() == 0
