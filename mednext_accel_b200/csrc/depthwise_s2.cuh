@@ -60,8 +60,10 @@ __device__ __forceinline__ typename Elem<T>::Acc s2_ld(const T* __restrict__ p, 
   return (i >= 0 && i < n) ? v : Acc(0);
 }
 
-// gather: CTA = (n, c, md) small-grid plane; one output per lane.
-template <typename T, int K>
+// gather: CTA = (n, c, md) small-grid plane; one output per lane.  ADD: the
+// addend operand is present (a template flag, so the plain gather keeps its own
+// register allocation).
+template <typename T, int K, bool ADD>
 __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_gather_kernel(const T* __restrict__ big,
                                                                      const T* __restrict__ wgt,
                                                                      const T* __restrict__ bias,
@@ -101,8 +103,7 @@ __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_gather_kernel(const T* __
           }
         }
       }
-      if (addend != nullptr)
-        acc += to_acc<T>(addend[(((size_t)nc * g.Ds + md) * g.Hs + mh) * g.Ws + mw]);
+      if constexpr (ADD) acc += to_acc<T>(addend[(((size_t)nc * g.Ds + md) * g.Hs + mh) * g.Ws + mw]);
       dst[(size_t)mh * g.Ws + mw] = from_acc<T>(acc);
     }
   }
@@ -123,9 +124,9 @@ struct S2Block {
 };
 
 // scatter: CTA = (n, c, qd) pair of big-grid planes 2qd, 2qd+1; warps take block
-// rows, lanes run along W; each thread writes a 2x2x2 output block.  add_even
-// (small-grid shaped, may be null) is added at the all-even output 2q.
-template <typename T, int K>
+// rows, lanes run along W; each thread writes a 2x2x2 output block.  ADD:
+// add_even (small-grid shaped) is added at the all-even output 2q.
+template <typename T, int K, bool ADD>
 __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_scatter_kernel(const T* __restrict__ small,
                                                                       const T* __restrict__ wgt,
                                                                       const T* __restrict__ bias,
@@ -194,8 +195,10 @@ __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_scatter_kernel(const T* _
               }
             }
             const int iw = 2 * qw + ew;
-            if (add_even != nullptr && ed == 0 && eh == 0 && ew == 0)
-              acc += to_acc<T>(add_even[(((size_t)nc * g.Ds + qd) * g.Hs + qh) * g.Ws + qw]);
+            if constexpr (ADD) {
+              if (ed == 0 && eh == 0 && ew == 0)
+                acc += to_acc<T>(add_even[(((size_t)nc * g.Ds + qd) * g.Hs + qh) * g.Ws + qw]);
+            }
             if (id < g.Db && ih < g.Hb && iw < g.Wb) row[iw] = from_acc<T>(acc);
           }
         }

@@ -22,9 +22,10 @@ int launch_gather(const void* big, const void* w, const void* b, const void* add
                   cudaStream_t s) {
   const long long ctas = (long long)g.N * g.C * g.Ds;
   if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
-  dw_s2_gather_kernel<T, K><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(
-      static_cast<const T*>(big), static_cast<const T*>(w), static_cast<const T*>(b), static_cast<const T*>(addend),
-      static_cast<T*>(small), g);
+  auto kern = addend != nullptr ? dw_s2_gather_kernel<T, K, true> : dw_s2_gather_kernel<T, K, false>;
+  kern<<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(static_cast<const T*>(big), static_cast<const T*>(w),
+                                                static_cast<const T*>(b), static_cast<const T*>(addend),
+                                                static_cast<T*>(small), g);
   return record_launch();
 }
 template <typename T, int K>
@@ -32,9 +33,10 @@ int launch_scatter(const void* small, const void* w, const void* b, const void* 
                    const DwS2Geom& g, cudaStream_t s) {
   const long long ctas = (long long)g.N * g.C * ((g.Db + 1) / 2);
   if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
-  dw_s2_scatter_kernel<T, K><<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(
-      static_cast<const T*>(small), static_cast<const T*>(w), static_cast<const T*>(b),
-      static_cast<const T*>(add_even), static_cast<T*>(big), g);
+  auto kern = add_even != nullptr ? dw_s2_scatter_kernel<T, K, true> : dw_s2_scatter_kernel<T, K, false>;
+  kern<<<(unsigned)ctas, kS2Warps * 32, 0, s>>>(static_cast<const T*>(small), static_cast<const T*>(w),
+                                                static_cast<const T*>(b), static_cast<const T*>(add_even),
+                                                static_cast<T*>(big), g);
   return record_launch();
 }
 template <typename T>
