@@ -66,7 +66,8 @@ enum mednext_status {
   MEDNEXT_ERR_ALIGNMENT = 6,    /* a pointer is not aligned to its element size */
   MEDNEXT_ERR_CUDA = 7,         /* a CUDA launch failed (see mednext_last_cuda_error) */
   MEDNEXT_ERR_DEVICE = 8,       /* current device is not sm_100 */
-  MEDNEXT_ERR_SCRATCH_LIMIT = 9 /* shape needs more than MEDNEXT_DW_WGRAD_NOALLOC_MAX_SCRATCH */
+  MEDNEXT_ERR_SCRATCH_LIMIT = 9, /* shape needs more than MEDNEXT_DW_WGRAD_NOALLOC_MAX_SCRATCH */
+  MEDNEXT_ERR_UNSUPPORTED = 10   /* a fused entry point does not cover this shape: run the parts */
 };
 
 /* Pointwise prologue applied to the activation operand while it is staged
@@ -258,6 +259,20 @@ int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue,
                            void* pro_out, void* workspace, size_t workspace_bytes, int64_t n,
                            int64_t cin, int64_t cout, int64_t vox, int a_dtype, int y_dtype,
                            mednext_stream_t stream);
+/* Backward of the compress GEMM through the GELU, fused (models/blocks.py:80,
+ * project(activation(u))), in one kernel plus a split reduction:
+ *   du[s, h, v]  = (sum_c wpt[h, c] * dy[s, c, v]) * GELU'(u[s, h, v])
+ *   dw[c, h]     = sum_{s, v} dy[s, c, v] * GELU(u[s, h, v]);  dbias[c] = sum dy
+ * dy: [n, c, vox]; wpt: [h, c] (the compress weight transposed); u, du: [n, h, vox];
+ * dw, dbias: FLOAT32.  GELU(u) is computed in the same pass as GELU'(u) and never
+ * stored.  BFLOAT16 only.  workspace_size returns 0 for shapes the fused kernel
+ * does not cover (c > 64, h > 127, ...); the call then returns
+ * MEDNEXT_ERR_UNSUPPORTED and the caller runs mednext_pw_fwd + mednext_pw_wgrad.
+ * Deterministic. */
+size_t mednext_pw_gelu_bwd_workspace_size(int64_t n, int64_t c, int64_t h, int64_t vox, int dtype);
+int mednext_pw_gelu_bwd(const void* dy, const void* wpt, const void* u, void* du, float* dw, float* dbias,
+                        void* workspace, size_t workspace_bytes, int64_t n, int64_t c, int64_t h,
+                        int64_t vox, int dtype, mednext_stream_t stream);
 /* Weight-grad form, the voxel axis is the reduction:
  *   dw[j, k] = sum_{s, v} g[s, j, v] * pro(a[s, k, v]);  dbias[j] = sum g
  * dw, dbias: FLOAT32 (dbias may be NULL).  Deterministic split-K. */

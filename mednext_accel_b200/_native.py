@@ -31,6 +31,7 @@ ERR_ALIGNMENT = 6
 ERR_CUDA = 7
 ERR_DEVICE = 8
 ERR_SCRATCH_LIMIT = 9
+ERR_UNSUPPORTED = 10
 
 PRO_NONE = 0
 PRO_GROUPNORM = 1
@@ -95,6 +96,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _INT,
         [_P, _P, _P, _INT, _P, _P, _P, _INT, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _INT, _P],
     ),
+    "mednext_pw_gelu_bwd_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _INT]),
+    "mednext_pw_gelu_bwd": (_INT, [_P, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _P]),
     "mednext_pw_wgrad_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "mednext_pw_wgrad": (
         _INT,

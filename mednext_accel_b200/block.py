@@ -33,7 +33,7 @@ from torch.nn import functional as F
 
 from . import _native as nat
 from . import depthwise as dwk
-from .pointwise import gn_backward_from_partials, gn_stats, pw_gemm, pw_wgrad
+from .pointwise import gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_wgrad
 
 _NS = "mednext_accel_b200"
 KIND_REGULAR, KIND_DOWN, KIND_UP = 0, 1, 2
@@ -286,12 +286,17 @@ def mednext_block_backward(
     rmode = (res_w, kind == KIND_DOWN) if res_w is not None else None
     prm = _block_params(dw_w, None, e_w, e_b, p_w, None, cdt, transposed=True, res=rmode)
     u = u_saved if u_saved.numel() > 0 else _expand(t, stats, gn_w, gn_b, prm, cdt)
-    # project dgrad with the GELU derivative in the epilogue
-    du, _ = pw_gemm(dyb, prm.pwt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
-    # weight grads of both GEMMs (fp32, deterministic split-K)
+    # project dgrad with the GELU derivative in the epilogue and, where the fused
+    # kernel covers the shape, the project weight grad from the same pass
+    fused = pw_gelu_bwd(dyb, prm.pwt, u)
+    if fused is not None:
+        du, dpw, dpb = fused
+    else:
+        du, _ = pw_gemm(dyb, prm.pwt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
+        dpw, dpb = pw_wgrad(dyb, u, prologue=nat.PRO_GELU)
+    # expand weight grad (fp32, deterministic split-K)
     g_w = gn_w.float().contiguous()
     g_b = gn_b.float().contiguous()
-    dpw, dpb = pw_wgrad(dyb, u, prologue=nat.PRO_GELU)
     dew, deb = pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g_w, pro_beta=g_b)
     # expand dgrad + GroupNorm-backward partial sums
     dz, part = pw_gemm(du, prm.ewt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)

@@ -453,6 +453,48 @@ int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue,
   return dispatch_pw_fwd(a_dtype, y_dtype, prologue, args, as_stream(stream));
 }
 
+static bool pw_gelu_bwd_covered(int64_t n, int64_t c, int64_t h, int64_t vox, int dtype) {
+  return dtype == MEDNEXT_BFLOAT16 && pw_shape_ok(n, c, h, vox) && c % 16 == 0 && c <= kPwBK && h + 1 <= kPwBM &&
+         vox % 8 == 0;
+}
+
+size_t mednext_pw_gelu_bwd_workspace_size(int64_t n, int64_t c, int64_t h, int64_t vox, int dtype) {
+  if (!pw_gelu_bwd_covered(n, c, h, vox, dtype)) return 0;
+  const long long tiles = n * ((vox + kPwBM - 1) / kPwBM);
+  const size_t splits = (size_t)pw_fused_grid(tiles);
+  return align_up(splits * c * h * 4, 256) + splits * c * 4;
+}
+
+int mednext_pw_gelu_bwd(const void* dy, const void* wpt, const void* u, void* du, float* dw, float* dbias,
+                        void* workspace, size_t workspace_bytes, int64_t n, int64_t c, int64_t h, int64_t vox,
+                        int dtype, mednext_stream_t stream) {
+  if (!pw_dtype_ok(dtype)) return MEDNEXT_ERR_BAD_DTYPE;
+  if (!pw_shape_ok(n, c, h, vox)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (dy == nullptr || wpt == nullptr || u == nullptr || du == nullptr || dw == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if (!pw_gelu_bwd_covered(n, c, h, vox, dtype)) return MEDNEXT_ERR_UNSUPPORTED;
+  const size_t ws_need = mednext_pw_gelu_bwd_workspace_size(n, c, h, vox, dtype);
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < ws_need) return MEDNEXT_ERR_WORKSPACE;
+  if (!aligned16(dy) || !aligned16(wpt) || !aligned16(u) || !aligned16(du) || !aligned(dw, 4) ||
+      (dbias && !aligned(dbias, 4)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  PwFwdArgs args{};
+  args.a = dy; args.wt = wpt; args.y = du; args.aux = u;
+  args.S = (int)n; args.cin = (int)c; args.cout = (int)h; args.vox = vox;
+  args.BN = pw_bn(h);
+  args.mtiles = (int)((vox + kPwBM - 1) / kPwBM);
+  args.ntiles = (int)((h + args.BN - 1) / args.BN);
+  args.epilogue = MEDNEXT_EPI_GELU_GRAD;
+  args.vec_a = 1; args.vec_w = (c % 8 == 0) ? 1 : 0;
+  const int splits = pw_fused_grid((long long)args.S * args.mtiles);
+  args.w_part = static_cast<float*>(workspace);
+  args.w_part_b = reinterpret_cast<float*>(static_cast<char*>(workspace) + align_up((size_t)splits * c * h * 4, 256));
+  const int st = pw_gelu_bwd_bf16(args, as_stream(stream));
+  if (st == -1) return MEDNEXT_ERR_UNSUPPORTED;
+  if (st != MEDNEXT_OK) return st;
+  // dw[c][h] = sum over the CTAs' partials (cout = c rows, cin = h columns), dbias[c]
+  return dispatch_pw_wgrad_reduce(args.w_part, args.w_part_b, dw, dbias, splits, (int)c, (int)h, as_stream(stream));
+}
+
 size_t mednext_pw_wgrad_workspace_size(int64_t n, int64_t cin, int64_t cout, int64_t vox) {
   if (!pw_shape_ok(n, cin, cout, vox)) return 0;
   const PwWPlan p = plan_pw_wgrad(n, cin, cout, vox);

@@ -83,11 +83,16 @@ int dispatch_pw_wgrad(int dtype, int prologue, const PwWgradArgs& a, int splits,
   if (dtype == MEDNEXT_BFLOAT16) st = pw_wgrad_pro<__nv_bfloat16>(prologue, a, s);
   if (dtype == MEDNEXT_FLOAT16) st = pw_wgrad_pro<__half>(prologue, a, s);
   if (st != MEDNEXT_OK) return st;
-  const long long total = (long long)a.cout * a.cin + a.cout;
+  return dispatch_pw_wgrad_reduce(a.part, a.part_b, a.dw, a.dbias, splits, a.cout, a.cin, s);
+}
+
+int dispatch_pw_wgrad_reduce(const float* part, const float* part_b, float* dw, float* dbias, int splits, int cout,
+                             int cin, cudaStream_t s) {
+  const long long total = (long long)cout * cin + cout;
   const int groups = splits >= 32 ? 8 : 1;
   const int per = kPwRedThreads / groups;
-  pw_wgrad_reduce_kernel<<<(unsigned)((total + per - 1) / per), kPwRedThreads, 0, s>>>(a.part, a.part_b, a.dw, a.dbias,
-                                                                                      splits, a.cout, a.cin, groups);
+  pw_wgrad_reduce_kernel<<<(unsigned)((total + per - 1) / per), kPwRedThreads, 0, s>>>(part, part_b, dw, dbias,
+                                                                                      splits, cout, cin, groups);
   return record_launch();
 }
 

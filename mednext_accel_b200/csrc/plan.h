@@ -180,6 +180,10 @@ int dispatch_gn_bwd_apply(int x_dtype, int dz_dtype, int g_dtype, const void* dz
 int dispatch_pw_fwd(int a_dtype, int y_dtype, int prologue, const PwFwdArgs& a, cudaStream_t s);
 // Per-element-type forward instantiations (pw_fwd_*.cu).
 int pw_fwd_bf16_bf16(int prologue, const PwFwdArgs& a, cudaStream_t s);
+int pw_gelu_bwd_bf16(const PwFwdArgs& a, cudaStream_t s);
+int pw_fused_grid(long long total_tiles);  // CTAs (= weight-grad splits) of pw_gelu_bwd_bf16
+int dispatch_pw_wgrad_reduce(const float* part, const float* part_b, float* dw, float* dbias, int splits, int cout,
+                             int cin, cudaStream_t s);
 int pw_fwd_bf16_f32(int prologue, const PwFwdArgs& a, cudaStream_t s);
 int pw_fwd_f16(int y_dtype, int prologue, const PwFwdArgs& a, cudaStream_t s);
 int dispatch_pw_wgrad(int dtype, int prologue, const PwWgradArgs& a, int splits, cudaStream_t s);

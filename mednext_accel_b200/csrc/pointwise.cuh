@@ -45,6 +45,8 @@ struct PwFwdArgs {
   int vec_w;  // cin % 8 == 0 and aligned
   void* wpad;  // workspace for W with rows padded to a multiple of 8 (cin % 8 != 0), or null
   void* pro_out;  // [S, cin, vox] in a's dtype: pro(a) as the GEMM consumed it, or null
+  float* w_part;    // fused compress weight grad: [splits][cin][cout] partials (splits = grid)
+  float* w_part_b;  // [splits][cin] bias-grad partials
 };
 
 // W [cout][cin] -> [cout][cin8] with zero columns: TMA needs 16-byte row strides.

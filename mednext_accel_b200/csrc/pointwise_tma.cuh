@@ -38,6 +38,15 @@ constexpr int kFwdThreads = 640;
 constexpr int kFwdProThreads = 256;
 constexpr int kPwCW = 16;          // accumulator columns per epilogue chunk
 constexpr int kEpiRuntime = -1;    // EPI template value: read the flags from the arguments
+// EPI bit (internal, with GELU_GRAD): the compress input-grad GEMM also computes the
+// compress weight grad.  The epilogue writes GELU(u) into a K-major shared-memory
+// tile g (rows = the GEMM's output channels h, plus a row of ones), and the MMA
+// warp accumulates D^T[h, c] += g[h, v] * dy[c, v] over the CTA's tiles with the
+// dy tile still in the A ring, so neither GELU(u) nor a second read of dy and u
+// reaches HBM.  Row h = H of D^T is sum_v dy[c, v], the bias grad.
+constexpr int kEpiFusedWgrad = 16;
+constexpr int kFwLag = 2;          // the weight-grad MMAs of tile i run after the input-grad MMAs of tile i+2
+constexpr int kFwGBytes = 32768;   // one g tile: two 64-voxel K-major boxes of 128 rows
 template <int PRO>
 struct FwdEpi {
   static constexpr int warp0 = PRO == MEDNEXT_PRO_NONE ? 4 : 12;
@@ -65,6 +74,7 @@ struct PwTmaCfg {
   int tgroups;      // epilogue warp groups on alternate tiles (1 or 2)
   int a_rows;       // channel rows per A box: min(64, roundup16(cin)); the MMA reads no further
   int w_res;        // 1: the whole W operand (kstages boxes) is loaded once and stays in shared memory
+  int tmem_cols;    // TMEM columns allocated (a power of two >= nacc x accumulator columns)
   int pro_store;    // 1: warp 3 writes every transformed A stage to pro_out (tensor map mP)
 };
 
@@ -78,6 +88,9 @@ struct PwTmaSmem {
   uint64_t eempty[kMaxEStages];
   uint64_t drain;  // final tcgen05.commit: every MMA of the CTA has completed
   uint64_t wfull;  // resident W operand landed
+  uint64_t gready[2];  // fused weight grad: g tile of epilogue group b written
+  uint64_t gempty[2];  // fused weight grad: its MMAs have read g tile b (and the dy stage)
+  uint64_t wdone;      // fused weight grad: every MMA into the weight-grad accumulator done
   uint32_t tmem_base;
   int abort;
 };
@@ -157,11 +170,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   constexpr int kStgBytes = 32 * kPwCW * (int)sizeof(TY);
   constexpr int kEpiWarp0 = FwdEpi<PRO>::warp0;
   constexpr int kEpiThreads = FwdEpi<PRO>::threads;
+  constexpr bool FW = EPI >= 0 && (EPI & kEpiFusedWgrad) != 0;
+  // fused weight grad: two g tiles (one per epilogue group) after the staging buffers
+  uint8_t* gbuf = ringStg + (size_t)FwdEpi<PRO>::warps * 2 * kStgBytes;
+  gbuf += ((1024u - (smem_u32(gbuf) & 1023u)) & 1023u);
 
   const uint32_t ncols = tmem_cols_for(BN);
   if (warp == 1) {
-    tmem_alloc(&sh.tmem_base, (uint32_t)cfg.nacc * ncols);
+    tmem_alloc(&sh.tmem_base, (uint32_t)cfg.tmem_cols);
     tmem_relinquish();
+  }
+  if constexpr (FW) {
+    // rows past the H channels stay zero, row H holds ones (the bias grad)
+    for (int off = tid * 16; off < 2 * kFwGBytes; off += kFwdThreads * 16)
+      *reinterpret_cast<uint4*>(gbuf + off) = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+    if (tid < 2 * 2 * 8) {
+      const int b = tid >> 4, box = (tid >> 3) & 1, c = tid & 7;
+      float one[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) one[k] = 1.0f;
+      *reinterpret_cast<uint4*>(gbuf + b * kFwGBytes + box * 16384 + sw128_kmajor_off(p.cout, c)) = pack16<TA>(one);
+    }
+    fence_async_smem();
   }
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
@@ -180,6 +211,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     mbar_init(&sh.drain, 1);
     mbar_init(&sh.wfull, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.gready[b], kEpiThreads / 2);
+      mbar_init(&sh.gempty[b], 1);
+    }
+    mbar_init(&sh.wdone, 1);
     sh.abort = 0;
     fence_mbarrier_init();
   }
@@ -269,7 +305,35 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(kPwBM, BN, std::is_same<TA, __nv_bfloat16>::value, true, false);
+      // fused weight grad: D^T[h, c] (M = 128 rows of g, N = cin columns of dy), both K-major
+      const uint32_t widesc = make_idesc_f16(kPwBM, p.cin, std::is_same<TA, __nv_bfloat16>::value, false, false);
+      const uint32_t wacc = tmem + (uint32_t)cfg.nacc * ncols;
+      bool wfirst = true;
+      // the weight-grad MMAs of tile w (KS == 1): g tile w & 1 times the dy stage of tile w,
+      // then release both
+      auto wgrad_tile = [&](int w) -> bool {
+        const int gb = w & 1;
+        if (!wait_or_abort(&sh.gready[gb], (uint32_t)((w >> 1) & 1), abort)) return false;
+        tc_fence_after();
+        const int st = w % S;
+        const uint32_t g_addr = smem_u32(gbuf + gb * kFwGBytes);
+        const uint32_t d_addr = smem_u32(ringA + (size_t)st * 16384);
+#pragma unroll
+        for (int box = 0; box < 2; ++box) {
+#pragma unroll
+          for (int ks = 0; ks < kPwBK / 16; ++ks) {
+            const uint64_t ad = make_sw128_desc(g_addr + box * 16384 + ks * 32, 16, 1024);
+            const uint64_t bd = make_sw128_desc(d_addr + box * 8192 + ks * 32, 16, 1024);
+            mma_f16_ss(wacc, ad, bd, widesc, wfirst ? 0u : 1u);
+            wfirst = false;
+          }
+        }
+        mma_commit(&sh.gempty[gb]);
+        mma_commit(&sh.empty[st]);
+        return true;
+      };
       if (w_res && ntile_local > 0) wait_or_abort(&sh.wfull, 0, abort);
+      bool ok = true;
       for (int i = 0; i < ntile_local && !*abort; ++i) {
         const int acc = i % cfg.nacc, ra = i / cfg.nacc;
         if (ra > 0 && !wait_or_abort(&sh.tempty[acc], (ra - 1) & 1, abort)) break;
@@ -289,9 +353,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             const uint64_t bd = make_sw128_desc(b_addr + ks * 32, 16, 1024);
             mma_f16_ss(d_tmem, ad, bd, idesc, (kk > 0 || ks > 0) ? 1u : 0u);
           }
-          mma_commit(&sh.empty[st]);
+          // fused weight grad: the stage is released after its weight-grad MMAs
+          if constexpr (!FW) mma_commit(&sh.empty[st]);
         }
         mma_commit(&sh.tfull[acc]);
+        if constexpr (FW) {
+          if (i >= kFwLag && !wgrad_tile(i - kFwLag)) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      if constexpr (FW) {
+        for (int w = max(0, ntile_local - kFwLag); ok && !*abort && w < ntile_local; ++w) ok = wgrad_tile(w);
+        if (ok && !*abort) mma_commit(&sh.wdone);
       }
     }
   } else if (warp == 3) {
@@ -394,6 +469,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const TA* auxt = reinterpret_cast<const TA*>(ringAux + (size_t)e * cfg.aux_bytes + (vl >> 6) * (cfg.aux_bytes / 2)) + (vl & 63);
       const TY* rest = reinterpret_cast<const TY*>(ringRes + (size_t)e * cfg.res_bytes + (vl >> 6) * (cfg.res_bytes / 2)) + (vl & 63);
       const uint32_t d_tmem = tmem + (uint32_t)acc * ncols + ((uint32_t)(q4 * 32) << 16);
+      // fused weight grad: this group's g tile (voxel vl's column of box vl / 64), free
+      // again once the weight-grad MMAs of the group's previous tile have read it
+      uint8_t* gcol = gbuf + tg * kFwGBytes + (vl >> 6) * 16384 + (vl & 7) * 2;
+      const int gchunk = (vl & 63) >> 3;
+      if constexpr (FW) {
+        if (i >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&sh.gempty[tg], (uint32_t)(((i >> 1) - 1) & 1), abort)))
+          break;
+      }
       for (int c0 = kPwCW * cg; c0 < BN; c0 += kPwCW * kGroups) {
         uint32_t r[kPwCW];
         tmem_ld16(d_tmem + (uint32_t)c0, r);
@@ -413,7 +496,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tmem_ld_wait();
         float s1[kPwCW], s2[kPwCW];
         float gg[kPwCW];  // GELU'(aux) of the chunk's columns, in pairs
-        if (epi & MEDNEXT_EPI_GELU_GRAD) {
+        if constexpr (FW) {
+          // GELU(aux) as well, from the same Phi: into the g tile (channels past cout keep their zeros / ones)
+#pragma unroll
+          for (int jj = 0; jj < kPwCW; jj += 2) {
+            float2 gv;
+            const float2 g = gelu_grad2_and_gelu(
+                make_float2(to_acc<TA>(auxt[(c0 + jj) * 64]), to_acc<TA>(auxt[(c0 + jj + 1) * 64])), gv);
+            gg[jj] = g.x;
+            gg[jj + 1] = g.y;
+            if (c0 + jj < p.cout)
+              *reinterpret_cast<TA*>(gcol + sw128_kmajor_off(c0 + jj, gchunk)) = from_acc<TA>(gv.x);
+            if (c0 + jj + 1 < p.cout)
+              *reinterpret_cast<TA*>(gcol + sw128_kmajor_off(c0 + jj + 1, gchunk)) = from_acc<TA>(gv.y);
+          }
+        } else if (epi & MEDNEXT_EPI_GELU_GRAD) {
 #pragma unroll
           for (int jj = 0; jj < kPwCW; jj += 2) {
             const float2 g = gelu_grad2(
@@ -466,6 +563,31 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_before();
       mbar_arrive(&sh.tempty[acc]);
       if (has_aux || has_res) mbar_arrive(&sh.eempty[e]);
+      if constexpr (FW) {
+        // the group's g tile is complete: hand it to the MMA warp (async proxy)
+        fence_async_smem();
+        mbar_arrive(&sh.gready[tg]);
+      }
+    }
+    if constexpr (FW) {
+      // the CTA's weight-grad partial: D^T[h, c] from TMEM lane h, one split per CTA
+      if (tg == 0 && cg == 0 && __all_sync(0xffffffffu, wait_or_abort(&sh.wdone, 0u, abort))) {
+        tc_fence_after();
+        const int h = q4 * 32 + lane;
+        const uint32_t wt = tmem + (uint32_t)cfg.nacc * ncols + ((uint32_t)(q4 * 32) << 16);
+        for (int c0 = 0; c0 < p.cin; c0 += kPwCW) {
+          uint32_t r[kPwCW];
+          tmem_ld16(wt + (uint32_t)c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < kPwCW; ++jj) {
+            const int c = c0 + jj;
+            if (c >= p.cin) break;
+            if (h < p.cout) p.w_part[((size_t)blockIdx.x * p.cin + c) * p.cout + h] = __uint_as_float(r[jj]);
+            else if (h == p.cout) p.w_part_b[(size_t)blockIdx.x * p.cin + c] = __uint_as_float(r[jj]);
+          }
+        }
+      }
     }
     if (lane == 0) bulk_wait_all();
   }
@@ -480,7 +602,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, (uint32_t)cfg.nacc * ncols);
+  if (warp == 1) tmem_dealloc(tmem, (uint32_t)cfg.tmem_cols);
 }
 
 // ---------------------------------------------------------------- weight grad

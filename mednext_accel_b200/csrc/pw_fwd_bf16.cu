@@ -8,6 +8,14 @@ using namespace pwl;
 int pw_fwd_bf16_bf16(int prologue, const PwFwdArgs& a, cudaStream_t s) {
   return pw_fwd_pro<__nv_bfloat16, __nv_bfloat16>(prologue, a, s);
 }
+
+// Compress input grad with the compress weight grad fused in (kEpiFusedWgrad):
+// MEDNEXT_OK when launched, -1 when the shape or the shared-memory plan does not
+// allow it (the caller then runs the two GEMMs separately).
+int pw_gelu_bwd_bf16(const PwFwdArgs& a, cudaStream_t s) {
+  return try_pw_fwd_tma<__nv_bfloat16, __nv_bfloat16, MEDNEXT_PRO_NONE, MEDNEXT_EPI_GELU_GRAD | kEpiFusedWgrad>(a, s);
+}
+int pw_fused_grid(long long total_tiles) { return (int)std::min<long long>(total_tiles, num_sms()); }
 MEDNEXT_DEFINE_ERROR_READER(read_clear_errors_pwf0)
 
 }  // namespace mednext

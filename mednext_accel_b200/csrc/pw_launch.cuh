@@ -86,6 +86,12 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   if (has_res && !encode3<TY>(&mRes, a.residual, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, (uint32_t)a.BN,
                               CU_TENSOR_MAP_SWIZZLE_NONE))
     return -1;
+  // fused compress weight grad (kEpiFusedWgrad): one K stage and one N tile, H + 1
+  // rows of g within the 128-row MMA, the dy channels a legal MMA N
+  constexpr bool FW = EPI >= 0 && (EPI & kEpiFusedWgrad) != 0;
+  if (FW && (a.cin > kPwBK || a.ntiles != 1 || a.cout + 1 > kPwBM || a.cin % 16 != 0 || a.cin > 256 ||
+             a.w_part == nullptr || a.w_part_b == nullptr))
+    return -1;
   PwTmaCfg cfg{};
   cfg.a_rows = a_rows;
   cfg.pro_store = pro_store ? 1 : 0;
@@ -100,22 +106,35 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   const size_t per_stage = 16384 + (cfg.w_res ? 0 : (size_t)cfg.b_bytes);
   const size_t ebytes = (size_t)cfg.aux_bytes + cfg.res_bytes;
   const size_t stg = (size_t)FwdEpi<PRO>::warps * 2 * 32 * kPwCW * sizeof(TY);  // epilogue staging, 2 per warp
-  const size_t budget = kSmemBudget - stg - w_bytes;
+  const size_t g_bytes = FW ? 1024 + 2 * (size_t)kFwGBytes : 0;                // two g tiles, 1 KB aligned
+  const size_t budget = kSmemBudget - stg - w_bytes - g_bytes;
   // Epilogue-operand ring: 4 or 2 stages while keeping at least 4 A/W stages,
   // else 1.  Two epilogue warp groups take alternate tiles only when every ring
   // slot then belongs to one group (an even ring, or none): a slot shared by two
   // groups would let one of them wait on a phase parity two fills ahead.
   cfg.estages = 1;
   if (ebytes > 0) {
-    if (4 * ebytes + 4 * per_stage <= budget) cfg.estages = 4;
-    else if (2 * ebytes + 4 * per_stage <= budget) cfg.estages = 2;
+    // (the fused weight grad needs the two groups, so it settles for kFwLag + 1 A/W stages)
+    const size_t min_a = FW ? kFwLag + 1 : 4;
+    if (4 * ebytes + min_a * per_stage <= budget) cfg.estages = 4;
+    else if (2 * ebytes + min_a * per_stage <= budget) cfg.estages = 2;
   }
   cfg.tgroups = (ebytes == 0 || cfg.estages % 2 == 0) ? 2 : 1;
-  cfg.nacc = (int)std::min<uint32_t>(kMaxAcc, 512u / tmem_cols_for(a.BN));
+  // the fused weight grad gives each of the two epilogue groups its own g tile
+  if (FW && cfg.tgroups != 2) return -1;
+  const uint32_t wcols = FW ? tmem_cols_for(a.cin) : 0u;
+  cfg.nacc = (int)std::min<uint32_t>(kMaxAcc, (512u - wcols) / tmem_cols_for(a.BN));
+  if (cfg.nacc < 1) return -1;
+  {
+    uint32_t cols = (uint32_t)cfg.nacc * tmem_cols_for(a.BN) + wcols, pow2 = 32;
+    while (pow2 < cols) pow2 <<= 1;
+    cfg.tmem_cols = (int)pow2;
+  }
   const long long room = (long long)budget - (long long)cfg.estages * (long long)ebytes;
   cfg.stages = (int)std::min<long long>(kMaxStages, room / (long long)per_stage);
-  if (cfg.stages < 2 || (pro_store && cfg.stages <= kProStoreLag)) return -1;
-  const size_t smem = 1024 + cfg.stages * per_stage + w_bytes + cfg.estages * ebytes + stg;
+  // a stage of the fused weight grad is held until kFwLag tiles later
+  if (cfg.stages < 2 || (pro_store && cfg.stages <= kProStoreLag) || (FW && cfg.stages <= kFwLag)) return -1;
+  const size_t smem = 1024 + cfg.stages * per_stage + w_bytes + cfg.estages * ebytes + stg + g_bytes;
   auto kern = pw_tma_fwd_kernel<TA, TY, PRO, EPI>;
   static size_t configured = 0;
   set_smem(kern, smem, configured);

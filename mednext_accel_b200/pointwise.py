@@ -113,6 +113,35 @@ def pw_wgrad(
     return dw, db
 
 
+def pw_gelu_bwd(dy: Tensor, wpt: Tensor, u: Tensor) -> tuple[Tensor, Tensor, Tensor] | None:
+    """Backward of y = W @ GELU(u) in one fused kernel: (du, dW, dbias) with
+    du = (W^T dy) * GELU'(u), dW = sum_v dy GELU(u)^T (fp32), dbias = sum_v dy (fp32).
+    ``dy``: [S, c, *spatial]; ``wpt`` = W^T: [h, c]; ``u``: [S, h, *spatial].  Returns
+    None when the fused kernel does not cover the shape (the caller runs pw_gemm and
+    pw_wgrad instead)."""
+    nat.require_device(dy)
+    lib = nat.load()
+    n, c = int(dy.shape[0]), int(dy.shape[1])
+    h = int(u.shape[1])
+    vox = _vox(dy)
+    code = nat.dtype_code(dy.dtype)
+    ws_bytes = lib.mednext_pw_gelu_bwd_workspace_size(n, c, h, vox, code)
+    if ws_bytes == 0:
+        return None
+    ws = nat.workspace(ws_bytes, dy.device)
+    du = torch.empty_like(u)
+    dw = torch.empty((c, h), dtype=torch.float32, device=dy.device)
+    db = torch.empty((c,), dtype=torch.float32, device=dy.device)
+    st = lib.mednext_pw_gelu_bwd(
+        dy.data_ptr(), wpt.data_ptr(), u.data_ptr(), du.data_ptr(), dw.data_ptr(), db.data_ptr(), ws.data_ptr(),
+        ws.numel(), n, c, h, vox, code, nat.stream(),
+    )
+    if st == nat.ERR_UNSUPPORTED:
+        return None
+    nat.check(st, "mednext_pw_gelu_bwd")
+    return du, dw, db
+
+
 def gn_stats(x: Tensor, eps: float, vox: int | None = None) -> Tensor:
     """Per-(n, c) mean / rstd.  ``vox``: number of valid voxels when ``x`` is a pitched
     [n, c, pitch] buffer (only the first ``vox`` of each row are statistics)."""

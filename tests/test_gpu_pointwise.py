@@ -275,5 +275,51 @@ def test_gelu_prologue_output_on_every_bf16_value():
     assert torch.equal(y, g)
 
 
+GELU_BWD_SHAPES = [
+    # (n, c = dy channels, h = GEMM output channels, spatial)
+    (1, 32, 64, (16, 16, 16)),
+    (2, 64, 64, (8, 8, 8)),
+    (1, 32, 112, (16, 16, 16)),
+    (2, 32, 64, (9, 10, 16)),     # voxel count not a multiple of the 128-voxel tile
+    (1, 32, 64, (64, 64, 64)),    # 2048 tiles: g tiles and ring stages reused many times
+    (1, 16, 48, (3, 4, 8)),       # a single tile
+]
+
+
+@pytest.mark.parametrize("n,c,hc,spatial", GELU_BWD_SHAPES)
+def test_fused_gelu_backward_matches_separate_kernels(n, c, hc, spatial):
+    from mednext_accel_b200.pointwise import pw_gelu_bwd
+
+    dy = rand((n, c, *spatial), 31).cuda()
+    u = (rand((n, hc, *spatial), 32).double() * 1.5).to(torch.bfloat16).cuda()
+    w = rand((c, hc), 33, scale=1 / np.sqrt(hc)).cuda()   # project weight [c, h]
+    wpt = w.t().contiguous()
+    out = pw_gelu_bwd(dy, wpt, u)
+    assert out is not None
+    du, dw, db = out
+    du_ref, _ = pw_gemm(dy, wpt, hc, aux=u, gelu_grad=True)
+    dw_ref, db_ref = pw_wgrad(dy, u, prologue=nat.PRO_GELU)
+    torch.cuda.synchronize()
+    assert torch.equal(du, du_ref)  # same input-grad arithmetic
+    assert orc.rel_l2(h(dw), h(dw_ref)) <= 2e-3
+    assert orc.rel_l2(h(db), h(db_ref)) <= 1e-5
+    # and against the oracle: dW = dy . GELU(u)^T on the same bf16 inputs
+    g = orc.round_bf16(orc.gelu(h(u)))
+    want_dw = np.einsum("ncv,nhv->ch", h(dy).reshape(n, c, -1), g.reshape(n, hc, -1))
+    assert orc.rel_l2(h(dw), want_dw) <= 4e-3
+    assert orc.rel_l2(h(db), h(dy).reshape(n, c, -1).sum(axis=(0, 2))) <= 1e-5
+
+
+def test_fused_gelu_backward_declines_uncovered_shapes():
+    from mednext_accel_b200.pointwise import pw_gelu_bwd
+
+    dy = rand((1, 32, 8, 8, 8), 34).cuda()
+    for hh, cc in ((128, 32), (64, 96)):
+        d = rand((1, cc, 8, 8, 8), 35).cuda()
+        u = rand((1, hh, 8, 8, 8), 36).cuda()
+        assert pw_gelu_bwd(d, torch.zeros((hh, cc), dtype=torch.bfloat16, device="cuda"), u) is None
+    assert dy is not None
+
+
 def test_no_device_error_recorded():
     assert nat.device_error() == 0
