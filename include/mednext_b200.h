@@ -273,6 +273,22 @@ size_t mednext_pw_gelu_bwd_workspace_size(int64_t n, int64_t c, int64_t h, int64
 int mednext_pw_gelu_bwd(const void* dy, const void* wpt, const void* u, void* du, float* dw, float* dbias,
                         void* workspace, size_t workspace_bytes, int64_t n, int64_t c, int64_t h,
                         int64_t vox, int dtype, mednext_stream_t stream);
+/* Backward of the expand GEMM after its GroupNorm, fused (models/blocks.py:79-84,
+ * expand(norm(t))): one kernel computes
+ *   dz[s, c, v] = sum_h wt[c, h] * du[s, h, v]   (wt = expand weight transposed, [c, h])
+ * with the GroupNorm-backward partial sums of mednext_pw_fwd's
+ * MEDNEXT_EPI_GN_BWD_STATS (aux = t, epi_stats = stats) at the start of the
+ * workspace, for mednext_gn_bwd_from_partials, and
+ *   dw[h, c] = sum_{s, v} du[s, h, v] * GroupNorm(t)[s, c, v];  dbias[h] = sum du
+ * with GroupNorm(t) = t * rstd * gamma + (beta - mean * rstd * gamma) (gamma, beta
+ * FLOAT32 [c]) computed in the same pass and never stored.  BFLOAT16 only.
+ * workspace_size returns 0 when not covered (h > 64, c > 127, ...); the call then
+ * returns MEDNEXT_ERR_UNSUPPORTED.  Deterministic. */
+size_t mednext_pw_gn_bwd_fused_workspace_size(int64_t n, int64_t h, int64_t c, int64_t vox, int dtype);
+int mednext_pw_gn_bwd_fused(const void* du, const void* wt, const void* t, const float* stats,
+                            const float* gamma, const float* beta, void* dz, float* dw, float* dbias,
+                            void* workspace, size_t workspace_bytes, int64_t n, int64_t h, int64_t c,
+                            int64_t vox, int dtype, mednext_stream_t stream);
 /* Weight-grad form, the voxel axis is the reduction:
  *   dw[j, k] = sum_{s, v} g[s, j, v] * pro(a[s, k, v]);  dbias[j] = sum g
  * dw, dbias: FLOAT32 (dbias may be NULL).  Deterministic split-K. */

@@ -33,7 +33,7 @@ from torch.nn import functional as F
 
 from . import _native as nat
 from . import depthwise as dwk
-from .pointwise import gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_wgrad
+from .pointwise import gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_gn_bwd_fused, pw_wgrad
 
 _NS = "mednext_accel_b200"
 KIND_REGULAR, KIND_DOWN, KIND_UP = 0, 1, 2
@@ -294,12 +294,16 @@ def mednext_block_backward(
     else:
         du, _ = pw_gemm(dyb, prm.pwt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
         dpw, dpb = pw_wgrad(dyb, u, prologue=nat.PRO_GELU)
-    # expand weight grad (fp32, deterministic split-K)
+    # GroupNorm affine parameters in fp32 for the kernels
     g_w = gn_w.float().contiguous()
     g_b = gn_b.float().contiguous()
-    dew, deb = pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g_w, pro_beta=g_b)
-    # expand dgrad + GroupNorm-backward partial sums
-    dz, part = pw_gemm(du, prm.ewt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)
+    # expand dgrad + GroupNorm-backward partial sums (+ the expand weight grad, fused where covered)
+    fused = pw_gn_bwd_fused(du, prm.ewt, t, stats, g_w, g_b)
+    if fused is not None:
+        dz, part, dew, deb = fused
+    else:
+        dew, deb = pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g_w, pro_beta=g_b)
+        dz, part = pw_gemm(du, prm.ewt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)
     dt, dgamma, dbeta = gn_backward_from_partials(dz, t, stats, g_w, part, vox=vox)
     wdw = prm.wdw
     drw = drb = dxr = None

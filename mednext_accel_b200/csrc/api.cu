@@ -495,6 +495,55 @@ int mednext_pw_gelu_bwd(const void* dy, const void* wpt, const void* u, void* du
   return dispatch_pw_wgrad_reduce(args.w_part, args.w_part_b, dw, dbias, splits, (int)c, (int)h, as_stream(stream));
 }
 
+// h = channels of du (the GEMM's K), c = channels of dz and t (its output)
+static bool pw_gn_bwd_covered(int64_t n, int64_t h, int64_t c, int64_t vox, int dtype) {
+  return dtype == MEDNEXT_BFLOAT16 && pw_shape_ok(n, h, c, vox) && h % 16 == 0 && h <= kPwBK && c + 1 <= kPwBM &&
+         vox % 8 == 0;
+}
+
+size_t mednext_pw_gn_bwd_fused_workspace_size(int64_t n, int64_t h, int64_t c, int64_t vox, int dtype) {
+  if (!pw_gn_bwd_covered(n, h, c, vox, dtype)) return 0;
+  const long long tiles = n * ((vox + kPwBM - 1) / kPwBM);
+  const size_t splits = (size_t)pw_fused_grid(tiles);
+  return pw_fwd_gn_bytes(n, c, vox, MEDNEXT_EPI_GN_BWD_STATS) + align_up(splits * h * c * 4, 256) + splits * h * 4;
+}
+
+int mednext_pw_gn_bwd_fused(const void* du, const void* wt, const void* t, const float* stats, const float* gamma,
+                            const float* beta, void* dz, float* dw, float* dbias, void* workspace,
+                            size_t workspace_bytes, int64_t n, int64_t h, int64_t c, int64_t vox, int dtype,
+                            mednext_stream_t stream) {
+  if (!pw_dtype_ok(dtype)) return MEDNEXT_ERR_BAD_DTYPE;
+  if (!pw_shape_ok(n, h, c, vox)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (du == nullptr || wt == nullptr || t == nullptr || stats == nullptr || gamma == nullptr || beta == nullptr ||
+      dz == nullptr || dw == nullptr)
+    return MEDNEXT_ERR_NULL_POINTER;
+  if (!pw_gn_bwd_covered(n, h, c, vox, dtype)) return MEDNEXT_ERR_UNSUPPORTED;
+  const size_t ws_need = mednext_pw_gn_bwd_fused_workspace_size(n, h, c, vox, dtype);
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < ws_need) return MEDNEXT_ERR_WORKSPACE;
+  if (!aligned16(du) || !aligned16(wt) || !aligned16(t) || !aligned16(dz) || !aligned(dw, 4) || !aligned(stats, 4) ||
+      !aligned(gamma, 4) || !aligned(beta, 4) || (dbias && !aligned(dbias, 4)))
+    return MEDNEXT_ERR_ALIGNMENT;
+  PwFwdArgs args{};
+  args.a = du; args.wt = wt; args.y = dz; args.aux = t; args.epi_stats = stats;
+  args.pro_gamma = gamma; args.pro_beta = beta;  // the fused GroupNorm(t) coefficients
+  args.gn_part = static_cast<GnBwdPartial*>(workspace);
+  args.S = (int)n; args.cin = (int)h; args.cout = (int)c; args.vox = vox;
+  args.BN = pw_bn(c);
+  args.mtiles = (int)((vox + kPwBM - 1) / kPwBM);
+  args.ntiles = (int)((c + args.BN - 1) / args.BN);
+  args.epilogue = MEDNEXT_EPI_GN_BWD_STATS;
+  args.vec_a = 1; args.vec_w = (h % 8 == 0) ? 1 : 0;
+  const int splits = pw_fused_grid((long long)args.S * args.mtiles);
+  char* wbase = static_cast<char*>(workspace) + pw_fwd_gn_bytes(n, c, vox, MEDNEXT_EPI_GN_BWD_STATS);
+  args.w_part = reinterpret_cast<float*>(wbase);
+  args.w_part_b = reinterpret_cast<float*>(wbase + align_up((size_t)splits * h * c * 4, 256));
+  const int st = pw_gn_bwd_bf16(args, as_stream(stream));
+  if (st == -1) return MEDNEXT_ERR_UNSUPPORTED;
+  if (st != MEDNEXT_OK) return st;
+  // dw[h][c] = sum over the CTAs' partials (h rows, c columns), dbias[h]
+  return dispatch_pw_wgrad_reduce(args.w_part, args.w_part_b, dw, dbias, splits, (int)h, (int)c, as_stream(stream));
+}
+
 size_t mednext_pw_wgrad_workspace_size(int64_t n, int64_t cin, int64_t cout, int64_t vox) {
   if (!pw_shape_ok(n, cin, cout, vox)) return 0;
   const PwWPlan p = plan_pw_wgrad(n, cin, cout, vox);

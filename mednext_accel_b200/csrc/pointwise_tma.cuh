@@ -38,12 +38,14 @@ constexpr int kFwdThreads = 640;
 constexpr int kFwdProThreads = 256;
 constexpr int kPwCW = 16;          // accumulator columns per epilogue chunk
 constexpr int kEpiRuntime = -1;    // EPI template value: read the flags from the arguments
-// EPI bit (internal, with GELU_GRAD): the compress input-grad GEMM also computes the
-// compress weight grad.  The epilogue writes GELU(u) into a K-major shared-memory
-// tile g (rows = the GEMM's output channels h, plus a row of ones), and the MMA
-// warp accumulates D^T[h, c] += g[h, v] * dy[c, v] over the CTA's tiles with the
-// dy tile still in the A ring, so neither GELU(u) nor a second read of dy and u
-// reaches HBM.  Row h = H of D^T is sum_v dy[c, v], the bias grad.
+// EPI bit (internal, with GELU_GRAD or GN_BWD_STATS): the input-grad GEMM also
+// computes the weight grad of the GEMM it differentiates.  The epilogue writes
+// g = GELU(aux) (compress GEMM) or GroupNorm(aux) (expand GEMM) into a K-major
+// shared-memory tile (rows = this GEMM's output channels, plus a row of ones),
+// and the MMA warp accumulates D^T[row, k] += g[row, v] * a[k, v] over the CTA's
+// tiles with the A tile (the incoming grad) still in the ring, so neither g nor a
+// second read of the grad and aux reaches HBM.  The ones row of D^T is
+// sum_v a[k, v], the bias grad.
 constexpr int kEpiFusedWgrad = 16;
 constexpr int kFwLag = 2;          // the weight-grad MMAs of tile i run after the input-grad MMAs of tile i+2
 constexpr int kFwGBytes = 32768;   // one g tile: two 64-voxel K-major boxes of 128 rows
@@ -75,6 +77,7 @@ struct PwTmaCfg {
   int a_rows;       // channel rows per A box: min(64, roundup16(cin)); the MMA reads no further
   int w_res;        // 1: the whole W operand (kstages boxes) is loaded once and stays in shared memory
   int tmem_cols;    // TMEM columns allocated (a power of two >= nacc x accumulator columns)
+  int a_slot;       // bytes of one A stage: two boxes of a_rows x 128 B
   int pro_store;    // 1: warp 3 writes every transformed A stage to pro_out (tensor map mP)
 };
 
@@ -162,8 +165,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint8_t* sbase = smem_dyn + (((base_u32 + 1023u) & ~1023u) - base_u32);
   // W: one box per ring stage, or (w_res) all KS boxes resident for the whole kernel
   const bool w_res = cfg.w_res != 0;
-  uint8_t* ringA = sbase;                                 // S x 16 KB
-  uint8_t* ringB = ringA + (size_t)S * 16384;             // (w_res ? KS : S) x b_bytes
+  uint8_t* ringA = sbase;                                 // S x a_slot
+  // an A stage is two 64-voxel boxes of a_rows channel rows, a_slot = 256 * a_rows bytes
+  const int AS = cfg.a_slot, AH = cfg.a_slot / 2;
+  uint8_t* ringB = ringA + (size_t)S * AS;                // (w_res ? KS : S) x b_bytes
   uint8_t* ringAux = ringB + (size_t)(w_res ? KS : S) * cfg.b_bytes;  // E x aux_bytes
   uint8_t* ringRes = ringAux + (size_t)E * cfg.aux_bytes; // E x res_bytes
   uint8_t* ringStg = ringRes + (size_t)E * cfg.res_bytes;  // epilogue warps x 2 x (16 x 32) TY
@@ -171,6 +176,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   constexpr int kEpiWarp0 = FwdEpi<PRO>::warp0;
   constexpr int kEpiThreads = FwdEpi<PRO>::threads;
   constexpr bool FW = EPI >= 0 && (EPI & kEpiFusedWgrad) != 0;
+  constexpr bool FW_GELU = FW && (EPI & MEDNEXT_EPI_GELU_GRAD) != 0;      // g = GELU(aux)
+  constexpr bool FW_GN = FW && (EPI & MEDNEXT_EPI_GN_BWD_STATS) != 0;     // g = GroupNorm(aux)
+  static_assert(!(FW_GELU && FW_GN), "one fused weight-grad operand");
   // fused weight grad: two g tiles (one per epilogue group) after the staging buffers
   uint8_t* gbuf = ringStg + (size_t)FwdEpi<PRO>::warps * 2 * kStgBytes;
   gbuf += ((1024u - (smem_u32(gbuf) & 1023u)) & 1023u);
@@ -292,9 +300,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int st = q % S, r = q / S;
           if (r > 0 && !wait_or_abort(&sh.empty[st], (r - 1) & 1, abort)) break;
           mbar_arrive_expect_tx(&sh.full[st], stage_tx);
-          uint8_t* a = ringA + (size_t)st * 16384;
+          uint8_t* a = ringA + (size_t)st * AS;
           tma_load_3d(a, &mA, &sh.full[st], (int)v0, kk * kPwBK, s);
-          tma_load_3d(a + 8192, &mA, &sh.full[st], (int)v0 + 64, kk * kPwBK, s);
+          tma_load_3d(a + AH, &mA, &sh.full[st], (int)v0 + 64, kk * kPwBK, s);
           if (!w_res) tma_load_2d(ringB + (size_t)st * cfg.b_bytes, &mB, &sh.full[st], kk * kPwBK, j0);
           ++issued;
         }
@@ -317,13 +325,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
         const int st = w % S;
         const uint32_t g_addr = smem_u32(gbuf + gb * kFwGBytes);
-        const uint32_t d_addr = smem_u32(ringA + (size_t)st * 16384);
+        const uint32_t d_addr = smem_u32(ringA + (size_t)st * AS);
 #pragma unroll
         for (int box = 0; box < 2; ++box) {
 #pragma unroll
           for (int ks = 0; ks < kPwBK / 16; ++ks) {
             const uint64_t ad = make_sw128_desc(g_addr + box * 16384 + ks * 32, 16, 1024);
-            const uint64_t bd = make_sw128_desc(d_addr + box * 8192 + ks * 32, 16, 1024);
+            const uint64_t bd = make_sw128_desc(d_addr + box * AH + ks * 32, 16, 1024);
             mma_f16_ss(wacc, ad, bd, widesc, wfirst ? 0u : 1u);
             wfirst = false;
           }
@@ -345,11 +353,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           uint64_t* bar = PRO != MEDNEXT_PRO_NONE ? &sh.ready[st] : &sh.full[st];
           if (!wait_or_abort(bar, r & 1, abort)) break;
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(ringA + (size_t)st * 16384);
+          const uint32_t a_addr = smem_u32(ringA + (size_t)st * AS);
           const uint32_t b_addr = smem_u32(ringB + (size_t)(w_res ? kk : st) * cfg.b_bytes);
           const int ksteps = min(kPwBK, p.cin - kk * kPwBK + 15) / 16;
           for (int ks = 0; ks < ksteps; ++ks) {
-            const uint64_t ad = make_sw128_desc(a_addr + ks * 2048, 8192, 1024);
+            const uint64_t ad = make_sw128_desc(a_addr + ks * 2048, (uint32_t)AH, 1024);
             const uint64_t bd = make_sw128_desc(b_addr + ks * 32, 16, 1024);
             mma_f16_ss(d_tmem, ad, bd, idesc, (kk > 0 || ks > 0) ? 1u : 0u);
           }
@@ -381,9 +389,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           for (int kk = 0; kk < KS; ++kk) {
             const int st = (int)(q % S), r = (int)(q / S);
             if (!wait_or_abort(&sh.ready[st], r & 1, abort)) break;
-            uint8_t* a = ringA + (size_t)st * 16384;
+            uint8_t* a = ringA + (size_t)st * AS;
             tma_store_3d(&mP, a, (int)v0, kk * kPwBK, s);
-            tma_store_3d(&mP, a + 8192, (int)v0 + 64, kk * kPwBK, s);
+            tma_store_3d(&mP, a + AH, (int)v0 + 64, kk * kPwBK, s);
             bulk_commit();
             // kProStoreLag stores in flight; a stage is released once its store has read it
             bulk_wait_read<kProStoreLag>();
@@ -410,7 +418,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int q = i * KS + kk;
           const int st = q % S, r = q / S;
           if (!wait_or_abort(&sh.full[st], r & 1, abort)) break;
-          uint8_t* a = ringA + (size_t)st * 16384 + (mch >> 3) * 8192;
+          uint8_t* a = ringA + (size_t)st * AS + (mch >> 3) * AH;
 #pragma unroll
           for (int ii = 0; ii < 4; ++ii) {
             const int kl = kr + 16 * ii;
@@ -471,8 +479,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t d_tmem = tmem + (uint32_t)acc * ncols + ((uint32_t)(q4 * 32) << 16);
       // fused weight grad: this group's g tile (voxel vl's column of box vl / 64), free
       // again once the weight-grad MMAs of the group's previous tile have read it
-      uint8_t* gcol = gbuf + tg * kFwGBytes + (vl >> 6) * 16384 + (vl & 7) * 2;
-      const int gchunk = (vl & 63) >> 3;
+      // g-tile addresses of this lane's voxel in rows 8q + k (k < 8): the K-major
+      // 128-byte swizzle XORs the 16-byte chunk index with k
+      uint32_t gx[8];
+      if constexpr (FW) {
+        const uint32_t gcol = smem_u32(gbuf + tg * kFwGBytes + (vl >> 6) * 16384 + (vl & 7) * 2);
+        const int gchunk = (vl & 63) >> 3;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gx[k] = gcol + (uint32_t)(k * 128 + ((gchunk ^ k) << 4));
+      }
       if constexpr (FW) {
         if (i >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&sh.gempty[tg], (uint32_t)(((i >> 1) - 1) & 1), abort)))
           break;
@@ -489,6 +504,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           mean_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc));
           rstd_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc) + 1);
         }
+        // fused weight grad after a GroupNorm: g = GroupNorm(aux) = aux * ca + cb, with the
+        // same coefficients (and rounding) as the weight-grad kernel's GroupNorm prologue
+        float ca_l = 0.f, cb_l = 0.f;
+        if constexpr (FW_GN) {
+          if (jok) {
+            ca_l = rstd_l * __ldg(p.pro_gamma + jc);
+            cb_l = __ldg(p.pro_beta + jc) - mean_l * ca_l;
+          }
+        }
         // staging buffer: wait until the store issued two chunks ago has read it
         TY* stg = reinterpret_cast<TY*>(stg0 + (nstored & 1) * kStgBytes);
         if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
@@ -496,7 +520,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tmem_ld_wait();
         float s1[kPwCW], s2[kPwCW];
         float gg[kPwCW];  // GELU'(aux) of the chunk's columns, in pairs
-        if constexpr (FW) {
+        // g row c0 + jj of this lane's voxel (rows past cout keep their zeros / ones)
+        const bool gfull = c0 + kPwCW <= p.cout;
+        auto gstore = [&](int jj, float v) {
+          if (gfull || c0 + jj < p.cout) {
+            const TA b = from_acc<TA>(v);
+            st_shared_b16(gx[jj & 7] + (uint32_t)(((c0 >> 3) + (jj >> 3)) * 1024), *reinterpret_cast<const uint16_t*>(&b));
+          }
+        };
+        if constexpr (FW_GELU) {
           // GELU(aux) as well, from the same Phi: into the g tile (channels past cout keep their zeros / ones)
 #pragma unroll
           for (int jj = 0; jj < kPwCW; jj += 2) {
@@ -505,10 +537,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 make_float2(to_acc<TA>(auxt[(c0 + jj) * 64]), to_acc<TA>(auxt[(c0 + jj + 1) * 64])), gv);
             gg[jj] = g.x;
             gg[jj + 1] = g.y;
-            if (c0 + jj < p.cout)
-              *reinterpret_cast<TA*>(gcol + sw128_kmajor_off(c0 + jj, gchunk)) = from_acc<TA>(gv.x);
-            if (c0 + jj + 1 < p.cout)
-              *reinterpret_cast<TA*>(gcol + sw128_kmajor_off(c0 + jj + 1, gchunk)) = from_acc<TA>(gv.y);
+            gstore(jj, gv.x);
+            gstore(jj + 1, gv.y);
           }
         } else if (epi & MEDNEXT_EPI_GELU_GRAD) {
 #pragma unroll
@@ -527,6 +557,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_RESIDUAL)) a = to_acc<TA>(from_acc<TA>(a));
           float ax = 0.f;
           if (epi & MEDNEXT_EPI_GN_BWD_STATS) ax = to_acc<TA>(auxt[jl * 64]);
+          if constexpr (FW_GN)
+            gstore(jj, fmaf(ax, __shfl_sync(0xffffffffu, ca_l, jj), __shfl_sync(0xffffffffu, cb_l, jj)));
           if (epi & MEDNEXT_EPI_GELU_GRAD) a *= gg[jj];
           if (epi & MEDNEXT_EPI_RESIDUAL) a += (float)to_acc<TY>(rest[jl * 64]);
           const TY o = from_acc<TY>((typename Elem<TY>::Acc)a);

@@ -15,6 +15,11 @@ int pw_fwd_bf16_bf16(int prologue, const PwFwdArgs& a, cudaStream_t s) {
 int pw_gelu_bwd_bf16(const PwFwdArgs& a, cudaStream_t s) {
   return try_pw_fwd_tma<__nv_bfloat16, __nv_bfloat16, MEDNEXT_PRO_NONE, MEDNEXT_EPI_GELU_GRAD | kEpiFusedWgrad>(a, s);
 }
+// Expand input grad with the GroupNorm-backward sums and the expand weight grad fused in.
+int pw_gn_bwd_bf16(const PwFwdArgs& a, cudaStream_t s) {
+  return try_pw_fwd_tma<__nv_bfloat16, __nv_bfloat16, MEDNEXT_PRO_NONE, MEDNEXT_EPI_GN_BWD_STATS | kEpiFusedWgrad>(a,
+                                                                                                             s);
+}
 int pw_fused_grid(long long total_tiles) { return (int)std::min<long long>(total_tiles, num_sms()); }
 MEDNEXT_DEFINE_ERROR_READER(read_clear_errors_pwf0)
 

@@ -103,7 +103,8 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   const size_t w_bytes = cfg.w_res ? (size_t)cfg.kstages * cfg.b_bytes : 0;
   cfg.aux_bytes = has_aux ? a.BN * 64 * (int)sizeof(TA) * 2 : 0;
   cfg.res_bytes = has_res ? a.BN * 64 * (int)sizeof(TY) * 2 : 0;
-  const size_t per_stage = 16384 + (cfg.w_res ? 0 : (size_t)cfg.b_bytes);
+  cfg.a_slot = 2 * 128 * a_rows;  // a multiple of 4 KB: the boxes stay 1 KB aligned for the swizzle
+  const size_t per_stage = (size_t)cfg.a_slot + (cfg.w_res ? 0 : (size_t)cfg.b_bytes);
   const size_t ebytes = (size_t)cfg.aux_bytes + cfg.res_bytes;
   const size_t stg = (size_t)FwdEpi<PRO>::warps * 2 * 32 * kPwCW * sizeof(TY);  // epilogue staging, 2 per warp
   const size_t g_bytes = FW ? 1024 + 2 * (size_t)kFwGBytes : 0;                // two g tiles, 1 KB aligned

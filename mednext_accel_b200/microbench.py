@@ -20,7 +20,7 @@ import torch
 
 from . import _native as nat
 from . import depthwise as dwk
-from .pointwise import gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_wgrad
+from .pointwise import gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_gn_bwd_fused, pw_wgrad
 
 V = 128**3  # level-0 voxels
 C, RC = 32, 64  # level-0 channels and expanded channels (ratio 2)
@@ -62,6 +62,8 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
         "pw project bwd fused (dgrad + wgrad)": (lambda: pw_gelu_bwd(dy, wp_t, u), (C + RC + RC) * 2 * V),
         "pw expand dgrad (GroupNorm-backward sums)": (
             lambda: pw_gemm(du, we_t, C, aux=t, gn_bwd_stats=stats), (RC + C + C) * 2 * V),
+        "pw expand bwd fused (dgrad + GroupNorm sums + wgrad)": (
+            lambda: pw_gn_bwd_fused(du, we_t, t, stats, g, bb), (RC + C + C) * 2 * V),
         "pw project wgrad (GELU prologue)": (lambda: pw_wgrad(dy, u, prologue=nat.PRO_GELU), (C + RC) * 2 * V),
         "pw project wgrad (saved GELU output)": (lambda: pw_wgrad(dy, gout), (C + RC) * 2 * V),
         "pw expand wgrad (GroupNorm prologue)": (

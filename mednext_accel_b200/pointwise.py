@@ -142,6 +142,37 @@ def pw_gelu_bwd(dy: Tensor, wpt: Tensor, u: Tensor) -> tuple[Tensor, Tensor, Ten
     return du, dw, db
 
 
+def pw_gn_bwd_fused(
+    du: Tensor, wt: Tensor, t: Tensor, stats: Tensor, gamma: Tensor, beta: Tensor
+) -> tuple[Tensor, Tensor, Tensor, Tensor] | None:
+    """Backward of u = W @ GroupNorm(t) in one fused kernel: (dz, partials, dW, dbias)
+    with dz = W^T du (its GroupNorm-backward partial sums in ``partials``, for
+    gn_backward_from_partials), dW = sum_v du GroupNorm(t)^T (fp32) and dbias = sum_v du.
+    ``du``: [S, h, *spatial]; ``wt`` = W^T: [c, h]; ``t``: [S, c, *spatial]; ``gamma``,
+    ``beta``: fp32 [c].  None when the fused kernel does not cover the shape."""
+    nat.require_device(du)
+    lib = nat.load()
+    n, h = int(du.shape[0]), int(du.shape[1])
+    c = int(t.shape[1])
+    vox = _vox(du)
+    code = nat.dtype_code(du.dtype)
+    ws_bytes = lib.mednext_pw_gn_bwd_fused_workspace_size(n, h, c, vox, code)
+    if ws_bytes == 0:
+        return None
+    ws = nat.workspace(ws_bytes, du.device)
+    dz = torch.empty_like(t)
+    dw = torch.empty((h, c), dtype=torch.float32, device=du.device)
+    db = torch.empty((h,), dtype=torch.float32, device=du.device)
+    st = lib.mednext_pw_gn_bwd_fused(
+        du.data_ptr(), wt.data_ptr(), t.data_ptr(), stats.data_ptr(), gamma.data_ptr(), beta.data_ptr(),
+        dz.data_ptr(), dw.data_ptr(), db.data_ptr(), ws.data_ptr(), ws.numel(), n, h, c, vox, code, nat.stream(),
+    )
+    if st == nat.ERR_UNSUPPORTED:
+        return None
+    nat.check(st, "mednext_pw_gn_bwd_fused")
+    return dz, ws, dw, db
+
+
 def gn_stats(x: Tensor, eps: float, vox: int | None = None) -> Tensor:
     """Per-(n, c) mean / rstd.  ``vox``: number of valid voxels when ``x`` is a pitched
     [n, c, pitch] buffer (only the first ``vox`` of each row are statistics)."""

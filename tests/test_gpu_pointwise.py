@@ -310,6 +310,41 @@ def test_fused_gelu_backward_matches_separate_kernels(n, c, hc, spatial):
     assert orc.rel_l2(h(db), h(dy).reshape(n, c, -1).sum(axis=(0, 2))) <= 1e-5
 
 
+GN_BWD_SHAPES = [
+    # (n, h = du channels, c = dz / t channels, spatial)
+    (1, 64, 32, (16, 16, 16)),
+    (2, 64, 64, (8, 8, 8)),
+    (2, 48, 112, (9, 10, 16)),
+    (1, 64, 32, (64, 64, 64)),
+]
+
+
+@pytest.mark.parametrize("n,hc,c,spatial", GN_BWD_SHAPES)
+def test_fused_groupnorm_backward_matches_separate_kernels(n, hc, c, spatial):
+    from mednext_accel_b200.pointwise import gn_backward_from_partials, pw_gn_bwd_fused
+
+    du = rand((n, hc, *spatial), 51).cuda()
+    t = (rand((n, c, *spatial), 52).double() * 2 + 0.5).to(torch.bfloat16).cuda()
+    w = rand((hc, c), 53, scale=1 / np.sqrt(c)).cuda()   # expand weight [h, c]
+    wt = w.t().contiguous()
+    gamma = (1 + 0.2 * rand((c,), 54, torch.float64)).float().cuda()
+    beta = (0.2 * rand((c,), 55, torch.float64)).float().cuda()
+    stats = gn_stats(t, 1e-5)
+    out = pw_gn_bwd_fused(du, wt, t, stats, gamma, beta)
+    assert out is not None
+    dz, part, dw, db = out
+    dz_ref, part_ref = pw_gemm(du, wt, c, aux=t, gn_bwd_stats=stats)
+    dw_ref, db_ref = pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=gamma, pro_beta=beta)
+    torch.cuda.synchronize()
+    assert torch.equal(dz, dz_ref)  # same input-grad arithmetic
+    got = gn_backward_from_partials(dz, t, stats, gamma, part)
+    want = gn_backward_from_partials(dz_ref, t, stats, gamma, part_ref)
+    for a, b in zip(got, want, strict=True):
+        assert torch.equal(a, b)  # the same GroupNorm-backward partial sums
+    assert orc.rel_l2(h(dw), h(dw_ref)) <= 1e-5  # same GroupNorm(t) values, another summation order
+    assert orc.rel_l2(h(db), h(db_ref)) <= 1e-5
+
+
 def test_fused_gelu_backward_declines_uncovered_shapes():
     from mednext_accel_b200.pointwise import pw_gelu_bwd
 
