@@ -83,6 +83,7 @@ const char* mednext_status_string(int status) {
     case MEDNEXT_ERR_DEVICE: return "current device is not sm_100";
     case MEDNEXT_ERR_SCRATCH_LIMIT:
       return "shape needs more scratch than the built-in array of the no-allocation entry point holds";
+    case MEDNEXT_ERR_UNSUPPORTED: return "the fused entry point does not cover this shape; run its parts";
     default: return "unknown status";
   }
 }
