@@ -288,5 +288,30 @@ def test_up_block_skip_addend_is_fused_exactly():
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("c,rc,cout", [(32, 64, 32), (17, 51, 33), (512, 2048, 512)])
+def test_parameter_casts_are_exact(c, rc, cout):
+    """One mednext_cast_params launch gives exactly torch's casts, plain and transposed."""
+    from mednext_accel_b200.block import _block_params
+
+    gen = torch.Generator().manual_seed(_seed("cast", c, rc))
+    dw_w = torch.randn((c, 1, 3, 3, 3), generator=gen).cuda()
+    dw_b = torch.randn((c,), generator=gen).cuda()
+    e_w = torch.randn((rc, c, 1, 1, 1), generator=gen).cuda()
+    e_b = torch.randn((rc,), generator=gen).cuda()
+    p_w = torch.randn((cout, rc, 1, 1, 1), generator=gen).cuda()
+    p_b = torch.randn((cout,), generator=gen).cuda()
+    bf = torch.bfloat16
+    prm = _block_params(dw_w, dw_b, e_w, e_b, p_w, p_b, bf, transposed=True)
+    torch.cuda.synchronize()
+    assert torch.equal(prm.wdw, dw_w.to(bf))
+    assert torch.equal(prm.bdw.reshape(-1), dw_b.to(bf))
+    assert torch.equal(prm.ew, e_w.reshape(rc, c).to(bf))
+    assert torch.equal(prm.pw, p_w.reshape(cout, rc).to(bf))
+    assert torch.equal(prm.ewt, e_w.reshape(rc, c).t().contiguous().to(bf))
+    assert torch.equal(prm.pwt, p_w.reshape(cout, rc).t().contiguous().to(bf))
+    assert torch.equal(prm.eb, e_b.to(bf).float())
+    assert torch.equal(prm.pb, p_b.to(bf).float())
+
+
 def test_no_device_error_recorded():
     assert nat.device_error() == 0
