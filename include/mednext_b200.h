@@ -259,6 +259,19 @@ int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue,
                            void* pro_out, void* workspace, size_t workspace_bytes, int64_t n,
                            int64_t cin, int64_t cout, int64_t vox, int a_dtype, int y_dtype,
                            mednext_stream_t stream);
+/* The block's expansion, fused (models/blocks.py:79-84 with the residual add of
+ * 89-90): with z = GroupNorm(t) (stats [n*c][2], gamma, beta FLOAT32 [c]),
+ *   u[s, h, v] = sum_k we[h, k] * z[s, k, v] + be[h]               (written: saved for backward)
+ *   y[s, j, v] = sum_h wp[j, h] * GELU(u)[s, h, v] + bp[j] (+ residual[s, j, v])
+ * in one kernel: GELU(u) stays in shared memory as the second GEMM's operand and u
+ * is not read back.  t: [n, c, vox]; we: [h, c]; wp: [c2, h]; be [h], bp [c2] FLOAT32;
+ * u: [n, h, vox]; y, residual (may be NULL): [n, c2, vox].  BFLOAT16 only; covers
+ * c <= 64, h <= 128 (multiples of 8 and 16), c2 <= 256, vox % 8 == 0, and returns
+ * MEDNEXT_ERR_UNSUPPORTED otherwise (the caller then runs two mednext_pw_fwd). */
+int mednext_pw_mlp_fwd(const void* t, const float* stats, const float* gamma, const float* beta,
+                       const void* we, const float* be, const void* wp, const float* bp,
+                       const void* residual, void* u, void* y, int64_t n, int64_t c, int64_t h,
+                       int64_t c2, int64_t vox, int dtype, mednext_stream_t stream);
 /* Backward of the compress GEMM through the GELU, fused (models/blocks.py:80,
  * project(activation(u))), in one kernel plus a split reduction:
  *   du[s, h, v]  = (sum_c wpt[h, c] * dy[s, c, v]) * GELU'(u[s, h, v])

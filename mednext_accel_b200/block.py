@@ -141,6 +141,17 @@ def _depthwise_forward(xb: Tensor, w: Tensor, b: Tensor | None, kind: int, k: in
     return t, gn_stats(t, eps)
 
 
+def _expansion(t: Tensor, stats: Tensor, gn_w: Tensor, gn_b: Tensor, prm: _Params, cdt, cout: int,
+               res: Tensor | None) -> tuple[Tensor, Tensor]:
+    """(u, y): u = expand(GroupNorm(t)), y = project(GELU(u)) (+ res), as two GEMMs.
+    (The one-kernel form, ``pointwise.pw_mlp_fwd``, gives the same bits but measured
+    slower at level 0: its two epilogue groups wait on the GELU pass between the GEMMs.)"""
+    u = _expand(t, stats, gn_w, gn_b, prm, cdt)
+    y, _ = pw_gemm(u, prm.pw, cout, out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
+                   bias=prm.pb, residual=res.contiguous() if res is not None else None)
+    return u, y
+
+
 def _expand(t: Tensor, stats: Tensor, gn_w: Tensor, gn_b: Tensor, prm: _Params, cdt) -> Tensor:
     rc = int(prm.ew.shape[0])
     u, _ = pw_gemm(
@@ -199,12 +210,11 @@ def mednext_block(
         vox, pitch = _pitch(big)
         t = dwk.t_forward(xb, wdw, bdw, kernel_size, pitch=pitch)
         stats = gn_stats(t, eps, vox=vox)
-        u = _expand(t, stats, gn_w, gn_b, prm, cdt)
         res_p = None
         if res_w is not None:
             rs, _ = pw_gemm(xb, prm.rw, cout, out_dtype=cdt, bias=prm.rb)
             res_p = dwk.upsample2_fill(rs, prm.rb, pitch)
-        y_p, _ = pw_gemm(u, prm.pw, cout, out_dtype=cdt, prologue=nat.PRO_GELU, bias=prm.pb, residual=res_p)
+        u, y_p = _expansion(t, stats, gn_w, gn_b, prm, cdt, cout, res_p)
         if addend is not None and addend.dtype != cdt:
             y = F.pad(dwk.pitched_view(y_p, big), (1, 0) * 3) + addend
         else:
@@ -213,11 +223,7 @@ def mednext_block(
     t, stats = _depthwise_forward(xb, wdw, bdw, kind, kernel_size, eps)
     if res_w is not None and kind == KIND_DOWN:
         res, _ = pw_gemm(_even(xb), prm.rw, cout, out_dtype=cdt, bias=prm.rb)
-    u = _expand(t, stats, gn_w, gn_b, prm, cdt)
-    y, _ = pw_gemm(
-        u, prm.pw, cout, out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
-        bias=prm.pb, residual=res.contiguous() if res is not None else None,
-    )
+    u, y = _expansion(t, stats, gn_w, gn_b, prm, cdt, cout, res)
     return y, t, (u if keep_expansion else u.new_empty((0,))), stats
 
 

@@ -496,6 +496,36 @@ int mednext_pw_gelu_bwd(const void* dy, const void* wpt, const void* u, void* du
   return dispatch_pw_wgrad_reduce(args.w_part, args.w_part_b, dw, dbias, splits, (int)c, (int)h, as_stream(stream));
 }
 
+int mednext_pw_mlp_fwd(const void* t, const float* stats, const float* gamma, const float* beta, const void* we,
+                       const float* be, const void* wp, const float* bp, const void* residual, void* u, void* y,
+                       int64_t n, int64_t c, int64_t h, int64_t c2, int64_t vox, int dtype, mednext_stream_t stream) {
+  if (!pw_dtype_ok(dtype)) return MEDNEXT_ERR_BAD_DTYPE;
+  if (!pw_shape_ok(n, c, h, vox) || !pw_shape_ok(n, h, c2, vox)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (t == nullptr || stats == nullptr || gamma == nullptr || beta == nullptr || we == nullptr || be == nullptr ||
+      wp == nullptr || bp == nullptr || u == nullptr || y == nullptr)
+    return MEDNEXT_ERR_NULL_POINTER;
+  if (dtype != MEDNEXT_BFLOAT16 || c % 8 != 0 || c > kPwBK || h % 16 != 0 || h > kPwBM || c2 % 8 != 0 || c2 > 256 ||
+      vox % 8 != 0)
+    return MEDNEXT_ERR_UNSUPPORTED;
+  if (!aligned16(t) || !aligned16(we) || !aligned16(wp) || !aligned16(u) || !aligned16(y) ||
+      (residual && !aligned16(residual)) || !aligned(stats, 4) || !aligned(gamma, 4) || !aligned(beta, 4) ||
+      !aligned(be, 4) || !aligned(bp, 4))
+    return MEDNEXT_ERR_ALIGNMENT;
+  PwFwdArgs args{};
+  args.a = t; args.wt = we; args.y = u;
+  args.pro_stats = stats; args.pro_gamma = gamma; args.pro_beta = beta;
+  args.bias = be; args.residual = residual;
+  args.S = (int)n; args.cin = (int)c; args.cout = (int)h; args.vox = vox;
+  args.BN = pw_bn(h);
+  args.mtiles = (int)((vox + kPwBM - 1) / kPwBM);
+  args.ntiles = (int)((h + args.BN - 1) / args.BN);
+  args.epilogue = MEDNEXT_EPI_BIAS;
+  args.vec_a = 1; args.vec_w = 1;
+  args.w2 = wp; args.bias2 = bp; args.y2 = y; args.cout2 = (int)c2;
+  const int st = pw_mlp_fwd_bf16(args, as_stream(stream));
+  return st == -1 ? MEDNEXT_ERR_UNSUPPORTED : st;
+}
+
 // h = channels of du (the GEMM's K), c = channels of dz and t (its output)
 static bool pw_gn_bwd_covered(int64_t n, int64_t h, int64_t c, int64_t vox, int dtype) {
   return dtype == MEDNEXT_BFLOAT16 && pw_shape_ok(n, h, c, vox) && h % 16 == 0 && h <= kPwBK && c + 1 <= kPwBM &&

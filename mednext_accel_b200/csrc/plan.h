@@ -182,6 +182,7 @@ int dispatch_pw_fwd(int a_dtype, int y_dtype, int prologue, const PwFwdArgs& a, 
 int pw_fwd_bf16_bf16(int prologue, const PwFwdArgs& a, cudaStream_t s);
 int pw_gelu_bwd_bf16(const PwFwdArgs& a, cudaStream_t s);
 int pw_gn_bwd_bf16(const PwFwdArgs& a, cudaStream_t s);
+int pw_mlp_fwd_bf16(const PwFwdArgs& a, cudaStream_t s);
 int pw_fused_grid(long long total_tiles);  // CTAs (= weight-grad splits) of pw_gelu_bwd_bf16
 int dispatch_pw_wgrad_reduce(const float* part, const float* part_b, float* dw, float* dbias, int splits, int cout,
                              int cin, cudaStream_t s);

@@ -47,6 +47,11 @@ struct PwFwdArgs {
   void* pro_out;  // [S, cin, vox] in a's dtype: pro(a) as the GEMM consumed it, or null
   float* w_part;    // fused compress weight grad: [splits][cin][cout] partials (splits = grid)
   float* w_part_b;  // [splits][cin] bias-grad partials
+  // fused expansion (second GEMM): y2 = w2 @ GELU(y) + bias2 (+ residual, [S, cout2, vox])
+  const void* w2;       // [cout2, cout] (K = cout contiguous)
+  const float* bias2;   // [cout2]
+  void* y2;             // [S, cout2, vox]
+  int cout2;
 };
 
 // W [cout][cin] -> [cout][cin8] with zero columns: TMA needs 16-byte row strides.

@@ -48,6 +48,14 @@ constexpr int kEpiRuntime = -1;    // EPI template value: read the flags from th
 // sum_v a[k, v], the bias grad.
 constexpr int kEpiFusedWgrad = 16;
 constexpr int kFwLag = 2;          // the weight-grad MMAs of tile i run after the input-grad MMAs of tile i+2
+// EPI bit (internal, with PRO = GroupNorm and BIAS): the block's whole expansion,
+// y = Wp @ GELU(We @ GroupNorm(t) + be) + bp (+ residual), in one kernel.  The
+// first GEMM's epilogue writes u (saved for the backward) and GELU(u) into a
+// shared-memory g tile, whose bytes are the MN-major A operand of the second GEMM
+// (M = voxels, K = H); its resident weight Wp is the second B operand and its
+// accumulators the second TMEM region.  The same epilogue group then adds bp and
+// the residual and stores y.  u is never read back from HBM.
+constexpr int kEpiMlp = 32;
 constexpr int kFwGBytes = 32768;   // one g tile: two 64-voxel K-major boxes of 128 rows
 template <int PRO>
 struct FwdEpi {
@@ -78,6 +86,11 @@ struct PwTmaCfg {
   int w_res;        // 1: the whole W operand (kstages boxes) is loaded once and stays in shared memory
   int tmem_cols;    // TMEM columns allocated (a power of two >= nacc x accumulator columns)
   int a_slot;       // bytes of one A stage: two boxes of a_rows x 128 B
+  int ks2;          // MLP: K boxes of the resident second weight (ceil(H / 64)), else 0
+  int b2_bytes;     // MLP: one box of the second weight, BN2 x 128 B
+  int bn2;          // MLP: second GEMM's N (output channels rounded to 16)
+  int d2_col;       // MLP: TMEM column of the second GEMM's two accumulators
+  int d2_stride;    // MLP: TMEM columns between them (a power of two >= bn2)
   int pro_store;    // 1: warp 3 writes every transformed A stage to pro_out (tensor map mP)
 };
 
@@ -94,6 +107,8 @@ struct PwTmaSmem {
   uint64_t gready[2];  // fused weight grad: g tile of epilogue group b written
   uint64_t gempty[2];  // fused weight grad: its MMAs have read g tile b (and the dy stage)
   uint64_t wdone;      // fused weight grad: every MMA into the weight-grad accumulator done
+  uint64_t d2full[2];  // MLP: second-GEMM accumulator of epilogue group b complete
+  uint64_t uready[2];  // MLP: u written into g tile b (the prologue warps then apply GELU in place)
   uint32_t tmem_base;
   int abort;
 };
@@ -151,7 +166,8 @@ template <typename TA, typename TY, int PRO, int EPI>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     pw_tma_fwd_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB,
                       const __grid_constant__ CUtensorMap mAux, const __grid_constant__ CUtensorMap mRes,
-                      const __grid_constant__ CUtensorMap mY, const __grid_constant__ CUtensorMap mP, PwFwdArgs p,
+                      const __grid_constant__ CUtensorMap mY, const __grid_constant__ CUtensorMap mP,
+                      const __grid_constant__ CUtensorMap mB2, const __grid_constant__ CUtensorMap mY2, PwFwdArgs p,
                       PwTmaCfg cfg) {
   extern __shared__ uint8_t smem_dyn[];
   __shared__ PwTmaSmem sh;
@@ -169,7 +185,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   // an A stage is two 64-voxel boxes of a_rows channel rows, a_slot = 256 * a_rows bytes
   const int AS = cfg.a_slot, AH = cfg.a_slot / 2;
   uint8_t* ringB = ringA + (size_t)S * AS;                // (w_res ? KS : S) x b_bytes
-  uint8_t* ringAux = ringB + (size_t)(w_res ? KS : S) * cfg.b_bytes;  // E x aux_bytes
+  uint8_t* ringB2 = ringB + (size_t)(w_res ? KS : S) * cfg.b_bytes;    // MLP: ks2 x b2_bytes (resident Wp)
+  uint8_t* ringAux = ringB2 + (size_t)cfg.ks2 * cfg.b2_bytes;          // E x aux_bytes
   uint8_t* ringRes = ringAux + (size_t)E * cfg.aux_bytes; // E x res_bytes
   uint8_t* ringStg = ringRes + (size_t)E * cfg.res_bytes;  // epilogue warps x 2 x (16 x 32) TY
   constexpr int kStgBytes = 32 * kPwCW * (int)sizeof(TY);
@@ -179,6 +196,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   constexpr bool FW_GELU = FW && (EPI & MEDNEXT_EPI_GELU_GRAD) != 0;      // g = GELU(aux)
   constexpr bool FW_GN = FW && (EPI & MEDNEXT_EPI_GN_BWD_STATS) != 0;     // g = GroupNorm(aux)
   static_assert(!(FW_GELU && FW_GN), "one fused weight-grad operand");
+  constexpr bool MLP = EPI >= 0 && (EPI & kEpiMlp) != 0;
+  static_assert(!(MLP && FW), "one fused second GEMM");
   // fused weight grad: two g tiles (one per epilogue group) after the staging buffers
   uint8_t* gbuf = ringStg + (size_t)FwdEpi<PRO>::warps * 2 * kStgBytes;
   gbuf += ((1024u - (smem_u32(gbuf) & 1023u)) & 1023u);
@@ -220,10 +239,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     mbar_init(&sh.drain, 1);
     mbar_init(&sh.wfull, 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&sh.gready[b], kEpiThreads / 2);
+      // the fused expansion's g tile is finished (GELU applied) by the prologue warps
+      mbar_init(&sh.gready[b], MLP ? kFwdProThreads : kEpiThreads / 2);
       mbar_init(&sh.gempty[b], 1);
+      mbar_init(&sh.uready[b], kEpiThreads / 2);
     }
     mbar_init(&sh.wdone, 1);
+    for (int b = 0; b < 2; ++b) mbar_init(&sh.d2full[b], 1);
     sh.abort = 0;
     fence_mbarrier_init();
   }
@@ -234,6 +256,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (has_res) tma_prefetch_map(&mRes);
     tma_prefetch_map(&mY);
     if (cfg.pro_store) tma_prefetch_map(&mP);
+    if (cfg.ks2 > 0) {
+      tma_prefetch_map(&mB2);
+      tma_prefetch_map(&mY2);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -284,9 +310,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (lane == 0) {
       if (w_res && ntile_local > 0) {
         // a single N tile (j0 = 0): every tile of the CTA multiplies by the same W
-        mbar_arrive_expect_tx(&sh.wfull, (uint32_t)(KS * cfg.b_bytes));
+        mbar_arrive_expect_tx(&sh.wfull, (uint32_t)(KS * cfg.b_bytes + cfg.ks2 * cfg.b2_bytes));
         for (int kk = 0; kk < KS; ++kk)
           tma_load_2d(ringB + (size_t)kk * cfg.b_bytes, &mB, &sh.wfull, kk * kPwBK, 0);
+        // MLP: the second GEMM's weight, resident too
+        for (int k2 = 0; k2 < cfg.ks2; ++k2)
+          tma_load_2d(ringB2 + (size_t)k2 * cfg.b2_bytes, &mB2, &sh.wfull, k2 * kPwBK, 0);
         w_issued = true;
       }
       const uint32_t stage_tx = (uint32_t)(2 * 128 * cfg.a_rows + (w_res ? 0 : cfg.b_bytes));
@@ -317,6 +346,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t widesc = make_idesc_f16(kPwBM, p.cin, std::is_same<TA, __nv_bfloat16>::value, false, false);
       const uint32_t wacc = tmem + (uint32_t)cfg.nacc * ncols;
       bool wfirst = true;
+      // MLP: the second GEMM of tile w, y2[v, j] = sum_h g[h, v] * Wp[j, h]: A = the g tile of
+      // epilogue group w & 1 (MN-major, the two 64-voxel boxes 16 KB apart), B = resident Wp
+      const uint32_t idesc2 = make_idesc_f16(kPwBM, cfg.bn2, std::is_same<TA, __nv_bfloat16>::value, true, false);
+      auto gemm2_tile = [&](int w) -> bool {
+        const int gb = w & 1;
+        if (!wait_or_abort(&sh.gready[gb], (uint32_t)((w >> 1) & 1), abort)) return false;
+        tc_fence_after();
+        const uint32_t g_addr = smem_u32(gbuf + gb * kFwGBytes);
+        const uint32_t b2_addr = smem_u32(ringB2);
+        const uint32_t d2 = tmem + (uint32_t)cfg.d2_col + (uint32_t)(gb * cfg.d2_stride);
+        const int ksteps = p.cout / 16;  // K = H, a multiple of 16
+        for (int ks = 0; ks < ksteps; ++ks) {
+          const uint64_t ad = make_sw128_desc(g_addr + ks * 2048, 16384, 1024);
+          const uint64_t bd = make_sw128_desc(b2_addr + (ks >> 2) * cfg.b2_bytes + (ks & 3) * 32, 16, 1024);
+          mma_f16_ss(d2, ad, bd, idesc2, ks > 0 ? 1u : 0u);
+        }
+        mma_commit(&sh.gempty[gb]);
+        mma_commit(&sh.d2full[gb]);
+        return true;
+      };
       // the weight-grad MMAs of tile w (KS == 1): g tile w & 1 times the dy stage of tile w,
       // then release both
       auto wgrad_tile = [&](int w) -> bool {
@@ -371,10 +420,19 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             break;
           }
         }
+        if constexpr (MLP) {
+          if (i >= kFwLag && !gemm2_tile(i - kFwLag)) {
+            ok = false;
+            break;
+          }
+        }
       }
       if constexpr (FW) {
         for (int w = max(0, ntile_local - kFwLag); ok && !*abort && w < ntile_local; ++w) ok = wgrad_tile(w);
         if (ok && !*abort) mma_commit(&sh.wdone);
+      }
+      if constexpr (MLP) {
+        for (int w = max(0, ntile_local - kFwLag); ok && !*abort && w < ntile_local; ++w) ok = gemm2_tile(w);
       }
     }
   } else if (warp == 3) {
@@ -410,6 +468,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const int t = tid - kFwdProWarp0 * 32;  // 0..255
       const int mch = t & 15;                 // 16 chunks of 8 voxels (two 64-voxel boxes)
       const int kr = t >> 4;                  // rows kr, kr+16, kr+32, kr+48 (same swizzle row)
+      // MLP: GELU in place over the u that epilogue group w & 1 wrote into its g tile (two
+      // 64-voxel boxes of H rows, 16-byte chunks; elementwise, so the swizzle is irrelevant)
+      auto gelu_tile = [&](int w) -> bool {
+        const int gb = w & 1;
+        if (!wait_or_abort(&sh.uready[gb], (uint32_t)((w >> 1) & 1), abort)) return false;
+        uint8_t* gt = gbuf + gb * kFwGBytes;
+        const int per_box = p.cout * 8;
+        for (int item = t; item < 2 * per_box; item += kFwdProThreads) {
+          const int box = item / per_box, rem = item - box * per_box;
+          uint4* chunk = reinterpret_cast<uint4*>(gt + box * 16384 + rem * 16);
+          float v[8];
+          unpack16<TA>(*chunk, v);
+          pw_prologue<MEDNEXT_PRO_GELU>(v, 0.f, 0.f);
+          *chunk = pack16<TA>(v);
+        }
+        fence_async_smem();
+        mbar_arrive(&sh.gready[gb]);
+        return true;
+      };
       for (int i = 0; i < ntile_local && !*abort; ++i) {
         int s, j0, mt;
         long long v0;
@@ -444,6 +521,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           fence_async_smem();
           mbar_arrive(&sh.ready[st]);
         }
+        if constexpr (MLP) {
+          if (i >= kFwLag && !gelu_tile(i - kFwLag)) break;
+        }
+      }
+      if constexpr (MLP) {
+        for (int w = max(0, ntile_local - kFwLag); !*abort && w < ntile_local; ++w)
+          if (!gelu_tile(w)) break;
       }
     }
   } else if (warp >= kEpiWarp0) {
@@ -482,13 +566,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // g-tile addresses of this lane's voxel in rows 8q + k (k < 8): the K-major
       // 128-byte swizzle XORs the 16-byte chunk index with k
       uint32_t gx[8];
-      if constexpr (FW) {
+      if constexpr (FW || MLP) {
         const uint32_t gcol = smem_u32(gbuf + tg * kFwGBytes + (vl >> 6) * 16384 + (vl & 7) * 2);
         const int gchunk = (vl & 63) >> 3;
 #pragma unroll
         for (int k = 0; k < 8; ++k) gx[k] = gcol + (uint32_t)(k * 128 + ((gchunk ^ k) << 4));
       }
-      if constexpr (FW) {
+      if constexpr (FW || MLP) {
         if (i >= 2 && !__all_sync(0xffffffffu, wait_or_abort(&sh.gempty[tg], (uint32_t)(((i >> 1) - 1) & 1), abort)))
           break;
       }
@@ -563,6 +647,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (epi & MEDNEXT_EPI_RESIDUAL) a += (float)to_acc<TY>(rest[jl * 64]);
           const TY o = from_acc<TY>((typename Elem<TY>::Acc)a);
           stg[jj * 32 + lane] = o;
+          if constexpr (MLP) gstore(jj, (float)to_acc<TY>(o));  // u as stored; GELU follows in place
           if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
             // out-of-range voxels / channels hold exact zeros (zero-filled operands)
             const float d = (float)to_acc<TY>(o);
@@ -594,12 +679,42 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&sh.tempty[acc]);
-      if (has_aux || has_res) mbar_arrive(&sh.eempty[e]);
       if constexpr (FW) {
         // the group's g tile is complete: hand it to the MMA warp (async proxy)
         fence_async_smem();
         mbar_arrive(&sh.gready[tg]);
       }
+      if constexpr (MLP) mbar_arrive(&sh.uready[tg]);  // u in the g tile: the prologue warps take over
+      if constexpr (MLP) {
+        // second GEMM of this tile: y2 = D2 + bias2 (+ residual), as the compress GEMM's epilogue
+        if (!__all_sync(0xffffffffu, wait_or_abort(&sh.d2full[tg], (uint32_t)((i >> 1) & 1), abort))) break;
+        tc_fence_after();
+        const uint32_t d2_tmem = tmem + (uint32_t)cfg.d2_col + (uint32_t)(tg * cfg.d2_stride) + ((uint32_t)(q4 * 32) << 16);
+        for (int c0 = kPwCW * cg; c0 < cfg.bn2; c0 += kPwCW * kGroups) {
+          uint32_t r[kPwCW];
+          tmem_ld16(d2_tmem + (uint32_t)c0, r);
+          const int jc = c0 + lane;
+          const float bias_l = (lane < kPwCW && jc < p.cout2) ? __ldg(p.bias2 + jc) : 0.f;
+          TY* stg = reinterpret_cast<TY*>(stg0 + (nstored & 1) * kStgBytes);
+          if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < kPwCW; ++jj) {
+            float a = __uint_as_float(r[jj]) + __shfl_sync(0xffffffffu, bias_l, jj);
+            if (has_res) a = to_acc<TA>(from_acc<TA>(a)) + (float)to_acc<TY>(rest[(c0 + jj) * 64]);
+            stg[jj * 32 + lane] = from_acc<TY>((typename Elem<TY>::Acc)a);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&mY2, stg, (int)v0 + q4 * 32, c0, s);
+            bulk_commit();
+          }
+          ++nstored;
+        }
+      }
+      if (has_aux || has_res) mbar_arrive(&sh.eempty[e]);
     }
     if constexpr (FW) {
       // the CTA's weight-grad partial: D^T[h, c] from TMEM lane h, one split per CTA

@@ -20,6 +20,11 @@ int pw_gn_bwd_bf16(const PwFwdArgs& a, cudaStream_t s) {
   return try_pw_fwd_tma<__nv_bfloat16, __nv_bfloat16, MEDNEXT_PRO_NONE, MEDNEXT_EPI_GN_BWD_STATS | kEpiFusedWgrad>(a,
                                                                                                              s);
 }
+// The block's whole expansion (GroupNorm prologue, expand GEMM + bias, GELU, compress
+// GEMM + bias + residual) in one kernel.
+int pw_mlp_fwd_bf16(const PwFwdArgs& a, cudaStream_t s) {
+  return try_pw_fwd_tma<__nv_bfloat16, __nv_bfloat16, MEDNEXT_PRO_GROUPNORM, MEDNEXT_EPI_BIAS | kEpiMlp>(a, s);
+}
 int pw_fused_grid(long long total_tiles) { return (int)std::min<long long>(total_tiles, num_sms()); }
 MEDNEXT_DEFINE_ERROR_READER(read_clear_errors_pwf0)
 

@@ -58,15 +58,25 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
     if (st != MEDNEXT_OK) return st;
     wt = a.wpad;
   }
+  constexpr bool MLP = EPI >= 0 && (EPI & kEpiMlp) != 0;
   const bool has_aux = (a.epilogue & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_GN_BWD_STATS)) != 0;
-  const bool has_res = (a.epilogue & MEDNEXT_EPI_RESIDUAL) != 0;
+  // (the fused expansion's residual belongs to its second GEMM)
+  const bool has_res = MLP ? a.residual != nullptr : (a.epilogue & MEDNEXT_EPI_RESIDUAL) != 0;
   const bool pro_store = PRO != MEDNEXT_PRO_NONE && a.pro_out != nullptr;
   if ((has_aux && !a16(a.aux)) || (has_res && !a16(a.residual))) return -1;
   if (!a16(a.y) || (pro_store && !a16(a.pro_out))) return -1;
-  CUtensorMap mA, mB, mAux, mRes, mY, mP;
+  CUtensorMap mA, mB, mAux, mRes, mY, mP, mB2, mY2;
   memset(&mAux, 0, sizeof(mAux));
   memset(&mRes, 0, sizeof(mRes));
   memset(&mP, 0, sizeof(mP));
+  memset(&mB2, 0, sizeof(mB2));
+  memset(&mY2, 0, sizeof(mY2));
+  // fused expansion: one K stage and one N tile in the first GEMM, H <= 128 rows of the g
+  // tile, the second GEMM's N a legal MMA N
+  const int bn2 = MLP ? (a.cout2 + 15) / 16 * 16 : 0;
+  if (MLP && (a.cin > kPwBK || a.ntiles != 1 || a.cout % 16 != 0 || a.cout > kPwBM || bn2 < 16 || bn2 > 256 ||
+              a.w2 == nullptr || a.y2 == nullptr || a.bias2 == nullptr || !a16(a.w2) || !a16(a.y2)))
+    return -1;
   if (!encode3<TY>(&mY, a.y, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 32, kPwCW,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
     return -1;
@@ -83,9 +93,17 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   if (has_aux && !encode3<TA>(&mAux, a.aux, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, (uint32_t)a.BN,
                               CU_TENSOR_MAP_SWIZZLE_NONE))
     return -1;
-  if (has_res && !encode3<TY>(&mRes, a.residual, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, (uint32_t)a.BN,
-                              CU_TENSOR_MAP_SWIZZLE_NONE))
+  const int res_rows = MLP ? a.cout2 : a.cout, res_bn = MLP ? bn2 : a.BN;
+  if (has_res && !encode3<TY>(&mRes, a.residual, (uint64_t)a.vox, (uint64_t)res_rows, (uint64_t)a.S, 64,
+                              (uint32_t)res_bn, CU_TENSOR_MAP_SWIZZLE_NONE))
     return -1;
+  if (MLP) {
+    if (!encode2<TA>(&mB2, a.w2, (uint64_t)a.cout, (uint64_t)a.cout2, kPwBK, (uint32_t)bn2, CU_TENSOR_MAP_SWIZZLE_128B))
+      return -1;
+    if (!encode3<TY>(&mY2, a.y2, (uint64_t)a.vox, (uint64_t)a.cout2, (uint64_t)a.S, 32, kPwCW,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+      return -1;
+  }
   // fused compress weight grad (kEpiFusedWgrad): one K stage and one N tile, H + 1
   // rows of g within the 128-row MMA, the dy channels a legal MMA N
   constexpr bool FW = EPI >= 0 && (EPI & kEpiFusedWgrad) != 0;
@@ -102,31 +120,40 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   cfg.w_res = (a.ntiles == 1 && (size_t)cfg.kstages * cfg.b_bytes <= kWResidentBytes) ? 1 : 0;
   const size_t w_bytes = cfg.w_res ? (size_t)cfg.kstages * cfg.b_bytes : 0;
   cfg.aux_bytes = has_aux ? a.BN * 64 * (int)sizeof(TA) * 2 : 0;
-  cfg.res_bytes = has_res ? a.BN * 64 * (int)sizeof(TY) * 2 : 0;
+  cfg.res_bytes = has_res ? res_bn * 64 * (int)sizeof(TY) * 2 : 0;
+  if (MLP && !cfg.w_res) return -1;
+  cfg.ks2 = MLP ? (a.cout + kPwBK - 1) / kPwBK : 0;
+  cfg.b2_bytes = MLP ? bn2 * 128 : 0;
+  cfg.bn2 = bn2;
+  const size_t w2_bytes = (size_t)cfg.ks2 * cfg.b2_bytes;
   cfg.a_slot = 2 * 128 * a_rows;  // a multiple of 4 KB: the boxes stay 1 KB aligned for the swizzle
   const size_t per_stage = (size_t)cfg.a_slot + (cfg.w_res ? 0 : (size_t)cfg.b_bytes);
   const size_t ebytes = (size_t)cfg.aux_bytes + cfg.res_bytes;
   const size_t stg = (size_t)FwdEpi<PRO>::warps * 2 * 32 * kPwCW * sizeof(TY);  // epilogue staging, 2 per warp
-  const size_t g_bytes = FW ? 1024 + 2 * (size_t)kFwGBytes : 0;                // two g tiles, 1 KB aligned
-  const size_t budget = kSmemBudget - stg - w_bytes - g_bytes;
+  const size_t g_bytes = (FW || MLP) ? 1024 + 2 * (size_t)kFwGBytes : 0;       // two g tiles, 1 KB aligned
+  const size_t budget = kSmemBudget - stg - w_bytes - g_bytes - w2_bytes;
   // Epilogue-operand ring: 4 or 2 stages while keeping at least 4 A/W stages,
   // else 1.  Two epilogue warp groups take alternate tiles only when every ring
   // slot then belongs to one group (an even ring, or none): a slot shared by two
   // groups would let one of them wait on a phase parity two fills ahead.
   cfg.estages = 1;
   if (ebytes > 0) {
-    // (the fused weight grad needs the two groups, so it settles for kFwLag + 1 A/W stages)
-    const size_t min_a = FW ? kFwLag + 1 : 4;
+    // (the fused weight grad and the fused expansion need the two groups, so they settle
+    // for kFwLag + 1 A/W stages)
+    const size_t min_a = (FW || MLP) ? kFwLag + 1 : 4;
     if (4 * ebytes + min_a * per_stage <= budget) cfg.estages = 4;
     else if (2 * ebytes + min_a * per_stage <= budget) cfg.estages = 2;
   }
   cfg.tgroups = (ebytes == 0 || cfg.estages % 2 == 0) ? 2 : 1;
   // the fused weight grad gives each of the two epilogue groups its own g tile
-  if (FW && cfg.tgroups != 2) return -1;
-  const uint32_t wcols = FW ? tmem_cols_for(a.cin) : 0u;
+  if ((FW || MLP) && cfg.tgroups != 2) return -1;
+  // extra TMEM: the fused weight grad's accumulator, or the fused expansion's two second-GEMM ones
+  cfg.d2_stride = MLP ? (int)tmem_cols_for(bn2) : 0;
+  const uint32_t wcols = FW ? tmem_cols_for(a.cin) : (MLP ? 2u * (uint32_t)cfg.d2_stride : 0u);
   cfg.nacc = (int)std::min<uint32_t>(kMaxAcc, (512u - wcols) / tmem_cols_for(a.BN));
   if (cfg.nacc < 1) return -1;
   {
+    cfg.d2_col = cfg.nacc * (int)tmem_cols_for(a.BN);
     uint32_t cols = (uint32_t)cfg.nacc * tmem_cols_for(a.BN) + wcols, pow2 = 32;
     while (pow2 < cols) pow2 <<= 1;
     cfg.tmem_cols = (int)pow2;
@@ -134,13 +161,13 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   const long long room = (long long)budget - (long long)cfg.estages * (long long)ebytes;
   cfg.stages = (int)std::min<long long>(kMaxStages, room / (long long)per_stage);
   // a stage of the fused weight grad is held until kFwLag tiles later
-  if (cfg.stages < 2 || (pro_store && cfg.stages <= kProStoreLag) || (FW && cfg.stages <= kFwLag)) return -1;
-  const size_t smem = 1024 + cfg.stages * per_stage + w_bytes + cfg.estages * ebytes + stg + g_bytes;
+  if (cfg.stages < 2 || (pro_store && cfg.stages <= kProStoreLag) || ((FW || MLP) && cfg.stages <= kFwLag)) return -1;
+  const size_t smem = 1024 + cfg.stages * per_stage + w_bytes + w2_bytes + cfg.estages * ebytes + stg + g_bytes;
   auto kern = pw_tma_fwd_kernel<TA, TY, PRO, EPI>;
   static size_t configured = 0;
   set_smem(kern, smem, configured);
   const int grid = std::min(cfg.total_tiles, num_sms());
-  kern<<<grid, kFwdThreads, smem, s>>>(mA, mB, mAux, mRes, mY, mP, a, cfg);
+  kern<<<grid, kFwdThreads, smem, s>>>(mA, mB, mAux, mRes, mY, mP, mB2, mY2, a, cfg);
   return record_launch();
 }
 

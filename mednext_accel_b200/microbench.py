@@ -20,7 +20,9 @@ import torch
 
 from . import _native as nat
 from . import depthwise as dwk
-from .pointwise import gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_gn_bwd_fused, pw_wgrad
+from .pointwise import (
+    gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_gn_bwd_fused, pw_mlp_fwd, pw_wgrad,
+)
 
 V = 128**3  # level-0 voxels
 C, RC = 32, 64  # level-0 channels and expanded channels (ratio 2)
@@ -54,6 +56,8 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
             (C + RC) * 2 * V),
         "pw project fwd (GELU prologue, bias, residual)": (
             lambda: pw_gemm(u, wp, C, prologue=nat.PRO_GELU, bias=b2, residual=x), (RC + C + C) * 2 * V),
+        "pw expansion fwd fused (expand + GELU + project)": (
+            lambda: pw_mlp_fwd(t, stats, g, bb, we, b1, wp, b2, x), (C + RC + C + C) * 2 * V),
         "pw project fwd + GELU output": (
             lambda: pw_gemm(u, wp, C, prologue=nat.PRO_GELU, bias=b2, residual=x, pro_out=gout),
             (RC + C + C + RC) * 2 * V),

@@ -142,6 +142,33 @@ def pw_gelu_bwd(dy: Tensor, wpt: Tensor, u: Tensor) -> tuple[Tensor, Tensor, Ten
     return du, dw, db
 
 
+def pw_mlp_fwd(
+    t: Tensor, stats: Tensor, gamma: Tensor, beta: Tensor, we: Tensor, be: Tensor, wp: Tensor, bp: Tensor,
+    residual: Tensor | None = None,
+) -> tuple[Tensor, Tensor] | None:
+    """The block's expansion in one kernel: (u, y) with u = we @ GroupNorm(t) + be and
+    y = wp @ GELU(u) + bp (+ residual).  ``t``: [S, c, *spatial]; ``we``: [h, c];
+    ``wp``: [c2, h] (t's dtype); ``be``, ``bp``, ``gamma``, ``beta``: fp32.  None when
+    the fused kernel does not cover the shape."""
+    nat.require_device(t)
+    n, c = int(t.shape[0]), int(t.shape[1])
+    h, c2 = int(we.shape[0]), int(wp.shape[0])
+    vox = _vox(t)
+    u = torch.empty((n, h, *t.shape[2:]), dtype=t.dtype, device=t.device)
+    y = torch.empty((n, c2, *t.shape[2:]), dtype=t.dtype, device=t.device)
+    if residual is not None and (residual.dtype != t.dtype or tuple(residual.shape) != tuple(y.shape)):
+        return None
+    st = nat.load().mednext_pw_mlp_fwd(
+        t.data_ptr(), stats.data_ptr(), gamma.data_ptr(), beta.data_ptr(), we.data_ptr(), be.data_ptr(),
+        wp.data_ptr(), bp.data_ptr(), nat.ptr(residual), u.data_ptr(), y.data_ptr(), n, c, h, c2, vox,
+        nat.dtype_code(t.dtype), nat.stream(),
+    )
+    if st == nat.ERR_UNSUPPORTED:
+        return None
+    nat.check(st, "mednext_pw_mlp_fwd")
+    return u, y
+
+
 def pw_gn_bwd_fused(
     du: Tensor, wt: Tensor, t: Tensor, stats: Tensor, gamma: Tensor, beta: Tensor
 ) -> tuple[Tensor, Tensor, Tensor, Tensor] | None:

@@ -345,6 +345,41 @@ def test_fused_groupnorm_backward_matches_separate_kernels(n, hc, c, spatial):
     assert orc.rel_l2(h(db), h(db_ref)) <= 1e-5
 
 
+MLP_SHAPES = [
+    # (n, c, h, c2, spatial, residual)
+    (1, 32, 64, 32, (16, 16, 16), True),
+    (2, 32, 64, 64, (8, 8, 8), False),
+    (1, 64, 128, 32, (15, 15, 16), True),   # the up block's level-0 shapes
+    (2, 16, 48, 16, (9, 10, 16), True),     # voxel count not a multiple of 128
+    (1, 32, 64, 32, (64, 64, 64), True),    # 2048 tiles: rings and g tiles wrap many times
+]
+
+
+@pytest.mark.parametrize("n,c,hc,c2,spatial,with_res", MLP_SHAPES)
+def test_fused_expansion_matches_separate_kernels(n, c, hc, c2, spatial, with_res):
+    """u and y bit for bit against the two separate GEMMs (same roundings, same MMAs)."""
+    from mednext_accel_b200.pointwise import pw_mlp_fwd
+
+    t = (rand((n, c, *spatial), 61).double() * 2 + 0.5).to(torch.bfloat16).cuda()
+    gamma = (1 + 0.2 * rand((c,), 62, torch.float64)).float().cuda()
+    beta = (0.2 * rand((c,), 63, torch.float64)).float().cuda()
+    we = rand((hc, c), 64, scale=1 / np.sqrt(c)).cuda()
+    be = rand((hc,), 65, torch.float32).cuda()
+    wp = rand((c2, hc), 66, scale=1 / np.sqrt(hc)).cuda()
+    bp = rand((c2,), 67, torch.float32).cuda()
+    res = rand((n, c2, *spatial), 68).cuda() if with_res else None
+    stats = gn_stats(t, 1e-5)
+    out = pw_mlp_fwd(t, stats, gamma, beta, we, be, wp, bp, res)
+    assert out is not None
+    u, y = out
+    u_ref, _ = pw_gemm(t, we, hc, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=gamma, pro_beta=beta,
+                       bias=be)
+    y_ref, _ = pw_gemm(u_ref, wp, c2, prologue=nat.PRO_GELU, bias=bp, residual=res)
+    torch.cuda.synchronize()
+    assert torch.equal(u, u_ref)
+    assert torch.equal(y, y_ref)
+
+
 def test_fused_gelu_backward_declines_uncovered_shapes():
     from mednext_accel_b200.pointwise import pw_gelu_bwd
 
