@@ -227,6 +227,24 @@ int mednext_gn_bwd(const void* dy, const void* x, const float* stats, const void
                    size_t workspace_bytes, int64_t n, int64_t c, int64_t spatial, int dy_dtype,
                    int x_dtype, int dx_dtype, int gamma_dtype, mednext_stream_t stream);
 
+/* ---------------- deep-supervision loss -------------------------------------
+ * Mean cross-entropy over the class axis, F.cross_entropy(logits, target,
+ * ignore_index=ignore_index) for the training step's heads
+ * (benchmarks/implementations.py:133-190): logits [n, k, v] (FLOAT32, BFLOAT16 or
+ * FLOAT16, computed in fp32), target INT64 [n, v].  fwd writes out[0] = mean loss,
+ * out[1] = number of counted targets (FLOAT32, device); bwd writes grad (the
+ * logits' shape and dtype) = (softmax - onehot) * grad_loss[0] / out[1], with
+ * grad_loss a device FLOAT32 scalar.  A target outside [0, k) that is not
+ * ignore_index is skipped and raises the device error word (0x300).
+ * Deterministic. */
+size_t mednext_ce_workspace_size(int64_t n, int64_t k, int64_t v);
+int mednext_ce_fwd(const void* logits, const int64_t* target, float* out, void* workspace,
+                   size_t workspace_bytes, int64_t n, int64_t k, int64_t v, int64_t ignore_index,
+                   int dtype, mednext_stream_t stream);
+int mednext_ce_bwd(const void* logits, const int64_t* target, const float* fwd_out,
+                   const float* grad_loss, void* grad, int64_t n, int64_t k, int64_t v,
+                   int64_t ignore_index, int dtype, mednext_stream_t stream);
+
 /* ---------------- pointwise 1x1x1 convolution (tensor cores) -------------
  * Forward / input-grad form, one GEMM per sample with the voxel axis as M:
  *   y[s, j, v] = epi( sum_k wt[j, k] * pro(a[s, k, v]) )     j < cout, k < cin

@@ -14,6 +14,7 @@ from .adaptive import (
     ModelOptimizationContext,
     install_adaptive_operators,
 )
+from .loss import cross_entropy
 from .network import (
     CheckpointConfig,
     MedNeXtBlock,
@@ -59,6 +60,7 @@ __all__ = [
     "OutputHead",
     "PolicyDecision",
     "PolicyResolver",
+    "cross_entropy",
     "default_implementation_registry",
     "get_mednext_v1_config",
     "install_adaptive_operators",

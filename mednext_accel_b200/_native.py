@@ -98,6 +98,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "mednext_pw_gelu_bwd_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _INT]),
     "mednext_pw_gelu_bwd": (_INT, [_P, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _P]),
+    "mednext_ce_workspace_size": (_SZ, [_I64, _I64, _I64]),
+    "mednext_ce_fwd": (_INT, [_P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _P]),
+    "mednext_ce_bwd": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _INT, _P]),
     "mednext_pw_mlp_fwd": (
         _INT, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _INT, _P],
     ),

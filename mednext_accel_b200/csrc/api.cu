@@ -100,6 +100,7 @@ int mednext_device_error(int* code, mednext_stream_t stream) {
   if (st == MEDNEXT_OK) st = read_clear_errors_pwf0(code, as_stream(stream));
   if (st == MEDNEXT_OK) st = read_clear_errors_pwf1(code, as_stream(stream));
   if (st == MEDNEXT_OK) st = read_clear_errors_pwf2(code, as_stream(stream));
+  if (st == MEDNEXT_OK) st = read_clear_errors_loss(code, as_stream(stream));
   return st;
 }
 

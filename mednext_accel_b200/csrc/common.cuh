@@ -129,6 +129,7 @@ enum DeviceError : int {
   kErrNone = 0,
   kErrMbarTimeout = 0x100,
   kErrTmemAlloc = 0x200,
+  kErrBadTarget = 0x300,  // a class index outside [0, K) that is not ignore_index
 };
 // One word per translation unit (internal linkage); mednext_device_error()
 // reads and clears all of them.

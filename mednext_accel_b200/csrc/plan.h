@@ -198,6 +198,7 @@ int read_clear_errors_pw(int* code, cudaStream_t s);
 int read_clear_errors_pwf0(int* code, cudaStream_t s);
 int read_clear_errors_pwf1(int* code, cudaStream_t s);
 int read_clear_errors_pwf2(int* code, cudaStream_t s);
+int read_clear_errors_loss(int* code, cudaStream_t s);
 
 // Records the CUDA error of the last launch in a thread-local slot.
 int record_launch();
