@@ -267,6 +267,342 @@ __global__ void __launch_bounds__(kDwMaxComputeWarps * 32 + 32, 1)
 }
 
 // ----------------------------------------------------------------------------
+// Forward (flip = 0) and input grad (flip = 1) for k = 3 on 16-bit types with
+// the packed fp32 FMA of sm_100 (fma.rn.f32x2).  Same CTA tile and plane ring
+// as dw_s1_conv_tma_kernel; each thread owns one output row of kDwPkCols = 16
+// columns and holds its accumulators as column pairs (i, i + 8), so one packed
+// FMA applies a tap to two outputs and the FMA instruction count halves.  Every
+// output sums its taps in (kd, kh, kw) order from zero and adds the bias last,
+// the order of dw_s1_conv_tma_kernel, so the two kernels give the same bits.
+// Pairs are 64-bit values end to end (window, weights, accumulators), so the
+// bf16 -> fp32 conversions write straight into the pair halves.  STATS
+// (GroupNorm partial statistics of the stored output) and ADD (an addend
+// tensor) are compile-time switches.
+//
+// No producer warp: thread 0 issues the first kDwSlots plane loads, and the
+// warp that releases a slot last (a counter per slot) issues the slot's next
+// load, so no thread polls for free slots.  Every warp computes; two CTAs of
+// 8 warps fit an SM at up to 128 registers.
+//
+// Shared-memory reads are free of bank conflicts: the plane tile's rows are
+// pitched to an odd number of 16-byte units (kDwPkPad extra columns in the TMA
+// box), a quarter warp covers 4 threads x 2 rows, so the 8 lanes of every
+// 16-byte load hit 8 different bank groups, and the two halo columns of a
+// thread come from its neighbours by shuffle (tile edges from one broadcast
+// load per row).
+// ----------------------------------------------------------------------------
+constexpr int kDwPkCols = 16;
+constexpr int kDwPkPad = 8;
+constexpr int kDwPkThreads = 256;  // 8 warps: 32 rows of a 128-wide tile
+
+template <typename T>
+struct DwPkLayout {
+  static __host__ __device__ int pitch(int TW) { return DwTile<T>::row_elems(TW, 1) + kDwPkPad; }
+  static __host__ __device__ size_t x_tile(const DwS1Geom& g) { return (size_t)(g.TH + 2) * pitch(g.TW) * sizeof(T); }
+  static __host__ __device__ size_t slot(const DwS1Geom& g) { return DwTmaLayout<T>::align128(x_tile(g)); }
+  static __host__ __device__ size_t weights() { return DwTmaLayout<T>::align128(27 * sizeof(uint64_t)); }
+  static __host__ size_t smem(const DwS1Geom& g) { return 128 + weights() + kDwSlots * slot(g); }
+};
+
+struct DwPkRing {
+  uint64_t full[kDwSlots];
+  int released[kDwSlots];  // warp releases of the slot so far (nwarps per plane)
+  int issued;              // plane loads issued so far
+  int abort;
+};
+
+// fp32 bit patterns of the low / high 16-bit element of a packed word
+template <typename T>
+__device__ __forceinline__ uint32_t lo_bits(uint32_t w);
+template <typename T>
+__device__ __forceinline__ uint32_t hi_bits(uint32_t w);
+template <>
+__device__ __forceinline__ uint32_t lo_bits<__nv_bfloat16>(uint32_t w) {
+  return w << 16;
+}
+template <>
+__device__ __forceinline__ uint32_t hi_bits<__nv_bfloat16>(uint32_t w) {
+  return w & 0xffff0000u;
+}
+template <>
+__device__ __forceinline__ uint32_t lo_bits<__half>(uint32_t w) {
+  return __float_as_uint(__half2float(__ushort_as_half((unsigned short)(w & 0xffffu))));
+}
+template <>
+__device__ __forceinline__ uint32_t hi_bits<__half>(uint32_t w) {
+  return __float_as_uint(__half2float(__ushort_as_half((unsigned short)(w >> 16))));
+}
+
+__device__ __forceinline__ uint64_t pk_pair(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+__device__ __forceinline__ void pk_split(uint64_t v, float& lo, float& hi) {
+  uint32_t a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+  lo = __uint_as_float(a);
+  hi = __uint_as_float(b);
+}
+// d = a * b + c on both fp32 halves, round to nearest even
+__device__ __forceinline__ uint64_t pk_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// lane of the thread that owns (column group wt, tile row r) in its warp
+__device__ __forceinline__ int dw_pk_lane(int wt, int r, int lw2) {
+  return lw2 == 8 ? ((wt & 3) | ((wt & 4) << 1) | ((r & 1) << 2) | ((r & 2) << 3)) : ((r * lw2 + wt) & 31);
+}
+
+// p[m] = (x[m-1], x[m+7]) for the 18 inputs x[-1..16] around the thread's 16
+// output columns.  rowp is the shared-memory row, col the thread's first column
+// in it; x[-1] and x[16] come from the neighbouring lanes src_l / src_r, or from
+// the row's halo columns at the tile edges.  Every lane of the warp takes part.
+template <typename T>
+__device__ __forceinline__ void dw_pk_window(const T* __restrict__ rowp, int col, int tw, bool left_edge,
+                                             bool right_edge, int src_l, int src_r, uint64_t (&p)[10]) {
+  constexpr int OFF = DwTile<T>::off(1);
+  const uint4 c0 = *reinterpret_cast<const uint4*>(rowp + col);
+  const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + col + 8);
+  const uint32_t from_l = __shfl_sync(0xffffffffu, c1.w, src_l);  // (x[14], x[15]) of the left neighbour
+  const uint32_t from_r = __shfl_sync(0xffffffffu, c0.x, src_r);  // (x[0], x[1]) of the right neighbour
+  const unsigned short* row16 = reinterpret_cast<const unsigned short*>(rowp);
+  const uint32_t el = row16[OFF - 1], er = row16[OFF + tw];
+  const uint32_t xl = left_edge ? el : (from_l >> 16);
+  const uint32_t xr = right_edge ? er : (from_r & 0xffffu);
+  const uint32_t a[4] = {c0.x, c0.y, c0.z, c0.w};  // x[0..7]
+  const uint32_t b[4] = {c1.x, c1.y, c1.z, c1.w};  // x[8..15]
+  p[0] = pk_pair(lo_bits<T>(xl), hi_bits<T>(a[3]));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    p[2 * q + 1] = pk_pair(lo_bits<T>(a[q]), lo_bits<T>(b[q]));  // (x[2q], x[2q+8])
+    p[2 * q + 2] = pk_pair(hi_bits<T>(a[q]), hi_bits<T>(b[q]));  // (x[2q+1], x[2q+9])
+  }
+  p[9] = pk_pair(lo_bits<T>(b[0]), lo_bits<T>(xr));
+}
+
+template <typename T, bool STATS, bool ADD>
+__global__ void __launch_bounds__(kDwPkThreads, 2)
+    dw_s1_conv_pk_kernel(const __grid_constant__ CUtensorMap mX, const T* __restrict__ wgt,
+                         const T* __restrict__ bias, const T* __restrict__ addend, T* __restrict__ y,
+                         GnPartial* __restrict__ stats, DwS1Geom g, int flip) {
+  constexpr int K = 3;
+  constexpr int K3 = 27;
+  using L = DwPkLayout<T>;
+  constexpr int OFF = DwTile<T>::off(1);
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ DwPkRing ring;
+  unsigned char* base = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  uint64_t* sw = reinterpret_cast<uint64_t*>(base);
+  const size_t slot_bytes = L::slot(g);
+  unsigned char* slots = base + L::weights();
+  const int nwarps = (int)blockDim.x >> 5;
+
+  int b = blockIdx.x;
+  const int tw = b % g.tilesW;
+  b /= g.tilesW;
+  const int th = b % g.tilesH;
+  b /= g.tilesH;
+  const int td = b % g.tilesD;
+  const int nc = b / g.tilesD;
+  const int c = nc % g.C;
+  const int w0 = tw * g.TW, h0 = th * g.TH, d0 = td * g.TD;
+  const int rsp = L::pitch(g.TW);
+  const int dcount = min(g.TD, g.D - d0);
+  const int nsteps = dcount + K - 1;
+  const uint32_t tile_bytes = (uint32_t)L::x_tile(g);
+
+  for (int t = threadIdx.x; t < K3; t += blockDim.x) {
+    const uint32_t wv = __float_as_uint(to_acc<T>(wgt[(size_t)c * K3 + (flip ? K3 - 1 - t : t)]));
+    sw[t] = pk_pair(wv, wv);
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDwSlots; ++i) {
+      mbar_init(&ring.full[i], 1);
+      ring.released[i] = 0;
+    }
+    ring.abort = 0;
+    fence_mbarrier_init();
+    tma_prefetch_map(&mX);
+    const int first = min(nsteps, kDwSlots);
+    for (int q = 0; q < first; ++q) {
+      mbar_arrive_expect_tx(&ring.full[q], tile_bytes);
+      tma_load_4d(slots + (size_t)q * slot_bytes, &mX, &ring.full[q], w0 - OFF, h0 - 1, d0 - 1 + q, nc);
+    }
+    ring.issued = first;
+  }
+  __syncthreads();
+  volatile int* abort = &ring.abort;
+
+  // shifted running sums for GroupNorm statistics, column pairs
+  float st_n = 0.f, st_shift = 0.f;
+  float2 st_s1 = make_float2(0.f, 0.f), st_s2 = make_float2(0.f, 0.f);
+
+  const int lane = threadIdx.x & 31;
+  const int lw2 = g.LW >> 1;
+  int wt, row;
+  if (lw2 == 8) {
+    wt = (lane & 3) | ((lane >> 1) & 4);
+    row = ((threadIdx.x >> 5) << 2) | ((lane >> 2) & 1) | ((lane >> 3) & 2);
+  } else {
+    wt = threadIdx.x % lw2;
+    row = threadIdx.x / lw2;
+  }
+  const bool active = row < g.TH;
+  const int oh = h0 + row;
+  const int ow0 = w0 + kDwPkCols * wt;
+  // W is a multiple of 8 on this path: each half of the 16 columns is in or out as a whole
+  const bool store_row = active && oh < g.H && ow0 < g.W;
+  const bool hi_ok = ow0 + 8 < g.W;
+  const int src_l = dw_pk_lane(wt > 0 ? wt - 1 : wt, row, lw2);
+  const int src_r = dw_pk_lane(wt < lw2 - 1 ? wt + 1 : wt, row, lw2);
+  const bool left_edge = wt == 0, right_edge = wt == lw2 - 1;
+  const float bv = bias != nullptr ? to_acc<T>(bias[c]) : 0.f;
+  // output row of this thread in plane 0 of its (n, c) volume; planes are plane_elems apart
+  const size_t plane_elems = (size_t)g.H * g.W;
+  const size_t out0 = (size_t)nc * g.D * plane_elems + (size_t)oh * g.W + ow0;
+  // rows of lanes past the tile read row 0 (every lane joins the shuffles) and store nothing
+  const int rbase = (active ? row : 0) * rsp;
+  const int col = OFF + kDwPkCols * wt;
+  uint64_t acc[K][8];
+#pragma unroll
+  for (int a = 0; a < K; ++a)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[a][i] = 0ull;
+
+  bool stop = false;  // warp-uniform: every lane leaves the loop at the same step
+  for (int sb = 0; sb < nsteps && !stop; sb += K) {
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const int s = sb + j;
+      if (s < nsteps) {
+        const int slot = s % kDwSlots;
+        const bool ok = !*abort && mbar_wait(&ring.full[slot], (uint32_t)((s / kDwSlots) & 1));
+        if (!__all_sync(0xffffffffu, ok)) {
+          *abort = 1;
+          stop = true;
+          break;
+        }
+        const T* sp = reinterpret_cast<const T*>(slots + (size_t)slot * slot_bytes) + rbase;
+        // output plane s starts here: its slot is j
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[j][i] = 0ull;
+#pragma unroll
+        for (int kh = 0; kh < K; ++kh) {
+          uint64_t p[10];
+          dw_pk_window<T>(sp + kh * rsp, col, g.TW, left_edge, right_edge, src_l, src_r, p);
+#pragma unroll
+          for (int kd = 0; kd < K; ++kd) {
+            const int slotk = (j - kd + K) % K;
+#pragma unroll
+            for (int kw = 0; kw < K; ++kw) {
+              const uint64_t wv = sw[(kd * K + kh) * K + kw];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[slotk][i] = pk_fma(p[i + kw], wv, acc[slotk][i]);
+            }
+          }
+        }
+        // release the slot; the warp that releases it last loads the slot's next plane
+        __syncwarp();
+        if (lane == 0) {
+          int prev;
+          asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;"
+                       : "=r"(prev)
+                       : "r"(smem_u32(&ring.released[slot]))
+                       : "memory");
+          // the count only grows: the slot's (s / kDwSlots)-th plane is released by nwarps arrivals
+          if (prev == (s / kDwSlots + 1) * nwarps - 1) {
+            const int q = s + kDwSlots;
+            if (q < nsteps) {
+              fence_async_smem();
+              mbar_arrive_expect_tx(&ring.full[slot], tile_bytes);
+              tma_load_4d(slots + (size_t)slot * slot_bytes, &mX, &ring.full[slot], w0 - OFF, h0 - 1, d0 - 1 + q,
+                          nc);
+              atomicAdd(&ring.issued, 1);
+            }
+          }
+        }
+        // output plane s-(K-1) is complete; its slot is (j+1) % K
+        const int o = s - (K - 1);
+        if (store_row && o >= 0) {
+          const int oslot = (j + 1) % K;
+          const size_t off = out0 + (size_t)(d0 + o) * plane_elems;
+          float lo[8], hi[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            pk_split(acc[oslot][i], lo[i], hi[i]);
+            lo[i] += bv;
+            hi[i] += bv;
+          }
+          if constexpr (ADD) {
+            float al[8], ah[8];
+            const uint4* ap = reinterpret_cast<const uint4*>(addend + off);
+            unpack16<T>(__ldg(ap), al);
+            unpack16<T>(hi_ok ? __ldg(ap + 1) : make_uint4(0, 0, 0, 0), ah);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              lo[i] += al[i];
+              hi[i] += ah[i];
+            }
+          }
+          const uint4 qlo = pack16<T>(lo), qhi = pack16<T>(hi);
+          uint4* dst = reinterpret_cast<uint4*>(y + off);
+          dst[0] = qlo;
+          if (hi_ok) dst[1] = qhi;
+          if constexpr (STATS) {
+            // statistics of the stored values
+            float rl[8], rh[8];
+            unpack16<T>(qlo, rl);
+            unpack16<T>(qhi, rh);
+            if (st_n == 0.f) st_shift = rl[0];
+            const float2 sh = make_float2(-st_shift, -st_shift);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float2 dv = __fadd2_rn(make_float2(rl[i], hi_ok ? rh[i] : st_shift), sh);
+              st_s1 = __fadd2_rn(st_s1, dv);
+              st_s2 = __ffma2_rn(dv, dv, st_s2);
+            }
+            st_n += hi_ok ? 16.f : 8.f;
+          }
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  // after an abort, wait (bounded) for the loads still in flight before the CTA exits
+  if (*abort && threadIdx.x == 0) {
+    const int issued = ring.issued;
+    for (int q = issued > kDwSlots ? issued - kDwSlots : 0; q < issued; ++q)
+      mbar_wait(&ring.full[q % kDwSlots], (uint32_t)((q / kDwSlots) & 1));
+  }
+  if constexpr (STATS) {
+    __shared__ double red[3 * 32];
+    double n = (double)st_n, mean = 0.0, m2 = 0.0;
+    if (st_n > 0.f) {
+      const double s1 = (double)st_s1.x + (double)st_s1.y, s2 = (double)st_s2.x + (double)st_s2.y;
+      mean = (double)st_shift + s1 / n;
+      m2 = fmax(s2 - s1 * s1 / n, 0.0);
+    }
+    __syncthreads();
+    block_merge_stats(n, mean, m2, red);
+    if (threadIdx.x == 0) {
+      const int tiles = g.tilesW * g.tilesH * g.tilesD;
+      const int tile = (td * g.tilesH + th) * g.tilesW + tw;
+      GnPartial gp;
+      gp.count = n;
+      gp.mean = mean;
+      gp.m2 = m2;
+      gp.pad = 0.0;
+      stats[(size_t)nc * tiles + tile] = gp;
+    }
+  }
+  if (*abort && threadIdx.x == 0) raise_device_error(kErrMbarTimeout);
+}
+
+// ----------------------------------------------------------------------------
 // Weight grad, every tap in one thread (k = 1, 3).  The ring slot carries the
 // x plane tile and, after it, the dy plane tile of the same step.
 // ----------------------------------------------------------------------------

@@ -52,9 +52,51 @@ int try_s1_conv_tma(const void* x, const void* wgt, const void* bias, const void
   }
 }
 
+template <typename T, bool STATS, bool ADD>
+int launch_s1_conv_pk(const CUtensorMap& m, const void* wgt, const void* bias, const void* addend, void* y,
+                      GnPartial* st, const S1Plan& p, int flip, cudaStream_t s) {
+  const size_t smem = DwPkLayout<T>::smem(p.g);
+  auto kern = dw_s1_conv_pk_kernel<T, STATS, ADD>;
+  static size_t configured = 0;  // raise the opt-in limit once per instantiation
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured = smem;
+  }
+  kern<<<(unsigned)p.grid, p.threads, smem, s>>>(m, static_cast<const T*>(wgt), static_cast<const T*>(bias),
+                                                   static_cast<const T*>(addend), static_cast<T*>(y), st, p.g, flip);
+  return record_launch();
+}
+
+// k = 3 on 16-bit types with packed fp32 FMAs: one output row of 16 columns per
+// thread, so the tile width must be a whole number of 16-column groups.
+template <typename T, int K>
+int try_s1_conv_pk(const void* x, const void* wgt, const void* bias, const void* addend, void* y, GnPartial* st,
+                   const S1Plan& p, int flip, cudaStream_t s) {
+  if constexpr (K != 3 || !(std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value)) {
+    return -1;
+  } else {
+    const DwS1Geom& g = p.g;
+    if (!s1_tma_ok<T, K>(x, p) || g.LW < 2 || p.threads > kDwPkThreads) return -1;
+    using L = DwPkLayout<T>;
+    CUtensorMap m;
+    if (L::pitch(g.TW) > 256 ||
+        !tma::encode4<T>(&m, x, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.D, (uint64_t)g.N * g.C,
+                         (uint32_t)L::pitch(g.TW), (uint32_t)(g.TH + 2)))
+      return -1;
+    if (st != nullptr) {
+      return addend != nullptr ? launch_s1_conv_pk<T, true, true>(m, wgt, bias, addend, y, st, p, flip, s)
+                               : launch_s1_conv_pk<T, true, false>(m, wgt, bias, addend, y, st, p, flip, s);
+    }
+    return addend != nullptr ? launch_s1_conv_pk<T, false, true>(m, wgt, bias, addend, y, st, p, flip, s)
+                             : launch_s1_conv_pk<T, false, false>(m, wgt, bias, addend, y, st, p, flip, s);
+  }
+}
+
 template <typename T, int K>
 int launch_s1_conv(const void* x, const void* wgt, const void* bias, const void* addend, void* y, GnPartial* st,
                    const S1Plan& p, int flip, cudaStream_t s) {
+  const int pst = try_s1_conv_pk<T, K>(x, wgt, bias, addend, y, st, p, flip, s);
+  if (pst != -1) return pst;
   const int tst = try_s1_conv_tma<T, K>(x, wgt, bias, addend, y, st, p, flip, s);
   if (tst != -1) return tst;
   constexpr int NH = K <= 3 ? 2 : 1;

@@ -64,8 +64,30 @@ inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int
   g.tilesW = (int)((w + g.TW - 1) / g.TW);
   g.tilesH = (int)((h + g.TH - 1) / g.TH);
   const long long base = (long long)n * c * g.tilesW * g.tilesH;
-  long long chunks = (kTargetCtas + base - 1) / base;
-  chunks = std::max(1LL, std::min(chunks, std::max(1LL, (long long)(d / 8))));
+  const long long max_chunks = std::max(1LL, (long long)(d / 8));
+  long long chunks;
+  if (!wgrad) {
+    // Depth chunks that minimise (rounds of resident CTAs) x (planes each CTA
+    // streams, k - 1 of them halo).  Residency: the packed k = 3 kernel on
+    // 16-bit types holds 16 warps per SM, the other kernels about 12.
+    const int warps = (p.threads + 31) / 32;
+    const bool packed = k == 3 && esz == 2 && lw >= 2;
+    const long long per_sm = std::max(1, (packed ? 16 : 12) / (warps + (packed ? 0 : 1)));
+    const long long slots = 148 * per_sm;
+    long long best_cost = -1;
+    chunks = 1;
+    for (long long cand = 1; cand <= max_chunks; ++cand) {
+      const long long td = (d + cand - 1) / cand;
+      const long long ctas = base * ((d + td - 1) / td);
+      const long long cost = ((ctas + slots - 1) / slots) * (td + k - 1);
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        chunks = cand;
+      }
+    }
+  } else {
+    chunks = std::max(1LL, std::min((kTargetCtas + base - 1) / base, max_chunks));
+  }
   g.TD = (int)((d + chunks - 1) / chunks);
   g.tilesD = (int)((d + g.TD - 1) / g.TD);
   const int E = (int)(16 / esz);

@@ -46,6 +46,7 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
     vol = (1, C, 128, 128, 128)
     x5, dy5 = x.view(vol), dy.view(vol)
     w3 = (torch.randn(C, 1, 3, 3, 3, device=dev) * 0.2).to(bf)
+    b3 = torch.randn(C, device=dev).to(bf)
     w3b = (torch.randn(2 * C, 1, 3, 3, 3, device=dev) * 0.2).to(bf)
     ys2 = r(1, C, 64, 64, 64)
     xs, ybig = r(1, 2 * C, 64, 64, 64), r(1, 2 * C, 127, 127, 127)
@@ -74,6 +75,8 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
             lambda: pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g, pro_beta=bb),
             (C + RC) * 2 * V),
         "dw fwd C32 k3": (lambda: dwk.dw_forward(x5, w3, None, 3), 2 * C * 2 * V),
+        "dw fwd + GN stats C32 k3": (lambda: dwk.dw_forward(x5, w3, b3, 3, gn_eps=1e-5), 2 * C * 2 * V),
+        "dw dgrad + addend C32 k3": (lambda: dwk.dw_dgrad(dy5, w3, 3, addend=x5), 3 * C * 2 * V),
         "dw dgrad C32 k3": (lambda: dwk.dw_dgrad(dy5, w3, 3), 2 * C * 2 * V),
         "dw wgrad C32 k3": (lambda: dwk.dw_wgrad(x5, dy5, 3), 2 * C * 2 * V),
         "s2 fwd C32 k3": (lambda: dwk.s2_forward(x5, w3, None, 3), C * 2 * V * 9 // 8),

@@ -177,6 +177,36 @@ def test_weight_grad_is_deterministic():
     assert torch.isfinite(a[0].float()).all()
 
 
+PACKED_SHAPES = [
+    (1, 3, 6, 40, 256),      # 8 column groups per row (permuted lanes), two W tiles, ragged H tile
+    (2, 2, 5, 9, 64),        # 4 column groups per row
+    (1, 2, 11, 70, 128),     # three H tiles, the last one ragged
+    (1, 2, 7, 8, 16),        # one column group per row
+    (1, 32, 128, 128, 128),  # the benchmark's level-0 shape
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", PACKED_SHAPES)
+def test_packed_k3_kernel_is_bit_exact_with_fp32_kernel(dtype, shape):
+    """k = 3 on 16-bit tensors runs the packed-FMA kernel, which sums each output in
+    the fp32 kernel's order: its outputs are the fp32 kernel's outputs on the same
+    inputs, rounded once (forward with bias, input grad with addend)."""
+    seed = seed_of("packed", str(dtype), shape)
+    x = rand(shape, dtype, seed).cuda()
+    w = rand((shape[1], 1, 3, 3, 3), dtype, seed + 1, scale=0.2).cuda()
+    b = rand((shape[1],), dtype, seed + 2).cuda()
+    a = rand(shape, dtype, seed + 3).cuda()
+    y, stats = dwk.dw_forward(x, w, b, 3, gn_eps=1e-5)
+    assert torch.equal(y, dwk.dw_forward(x.float(), w.float(), b.float(), 3).to(dtype))
+    dx = dwk.dw_dgrad(x, w, 3, addend=a)
+    assert torch.equal(dx, dwk.dw_dgrad(x.float(), w.float(), 3, addend=a.float()).to(dtype))
+    yf = y.double().reshape(shape[0] * shape[1], -1)
+    torch.testing.assert_close(stats[:, 0].double(), yf.mean(1), rtol=1e-5, atol=1e-6)
+    rstd = 1 / torch.sqrt(yf.var(1, unbiased=False) + 1e-5)
+    torch.testing.assert_close(stats[:, 1].double(), rstd, rtol=1e-5, atol=1e-6)
+
+
 def test_dgrad_with_addend_adds_residual():
     x = rand((1, 4, 8, 16, 16), torch.bfloat16, 8).cuda()
     w = rand((4, 1, 3, 3, 3), torch.bfloat16, 9).cuda()
