@@ -14,6 +14,8 @@
 // after an abort the producer waits for the fills it issued before the CTA exits.
 #pragma once
 
+#include <type_traits>
+
 #include "depthwise_s1.cuh"
 
 namespace mednext {
@@ -351,6 +353,13 @@ __device__ __forceinline__ uint64_t pk_fma(uint64_t a, uint64_t b, uint64_t c) {
   return d;
 }
 
+// a + b on both fp32 halves, round to nearest even
+__device__ __forceinline__ uint64_t pk_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // lane of the thread that owns (column group wt, tile row r) in its warp
 __device__ __forceinline__ int dw_pk_lane(int wt, int r, int lw2) {
   return lw2 == 8 ? ((wt & 3) | ((wt & 4) << 1) | ((r & 1) << 2) | ((r & 2) << 3)) : ((r * lw2 + wt) & 31);
@@ -459,7 +468,7 @@ __global__ void __launch_bounds__(kDwPkThreads, 2)
   const int src_l = dw_pk_lane(wt > 0 ? wt - 1 : wt, row, lw2);
   const int src_r = dw_pk_lane(wt < lw2 - 1 ? wt + 1 : wt, row, lw2);
   const bool left_edge = wt == 0, right_edge = wt == lw2 - 1;
-  const float bv = bias != nullptr ? to_acc<T>(bias[c]) : 0.f;
+  const uint32_t bvb = __float_as_uint(bias != nullptr ? to_acc<T>(bias[c]) : 0.f);
   // output row of this thread in plane 0 of its (n, c) volume; planes are plane_elems apart
   const size_t plane_elems = (size_t)g.H * g.W;
   const size_t out0 = (size_t)nc * g.D * plane_elems + (size_t)oh * g.W + ow0;
@@ -472,104 +481,106 @@ __global__ void __launch_bounds__(kDwPkThreads, 2)
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[a][i] = 0ull;
 
-  bool stop = false;  // warp-uniform: every lane leaves the loop at the same step
-  for (int sb = 0; sb < nsteps && !stop; sb += K) {
+  // one ring step: plane s of the input enters, output plane s - (K - 1) leaves;
+  // j = s % K names the accumulator slot at compile time.  False after an abort.
+  auto step = [&](auto jc, const int s) -> bool {
+    constexpr int j = decltype(jc)::value;
+    const int slot = s % kDwSlots;
+    const bool ok = !*abort && mbar_wait(&ring.full[slot], (uint32_t)((s / kDwSlots) & 1));
+    if (!__all_sync(0xffffffffu, ok)) {
+      *abort = 1;
+      return false;
+    }
+    const T* sp = reinterpret_cast<const T*>(slots + (size_t)slot * slot_bytes) + rbase;
+    // output plane s starts here: its slot is j
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      const int s = sb + j;
-      if (s < nsteps) {
-        const int slot = s % kDwSlots;
-        const bool ok = !*abort && mbar_wait(&ring.full[slot], (uint32_t)((s / kDwSlots) & 1));
-        if (!__all_sync(0xffffffffu, ok)) {
-          *abort = 1;
-          stop = true;
-          break;
-        }
-        const T* sp = reinterpret_cast<const T*>(slots + (size_t)slot * slot_bytes) + rbase;
-        // output plane s starts here: its slot is j
+    for (int i = 0; i < 8; ++i) acc[j][i] = 0ull;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[j][i] = 0ull;
+    for (int kh = 0; kh < K; ++kh) {
+      uint64_t p[10];
+      dw_pk_window<T>(sp + kh * rsp, col, g.TW, left_edge, right_edge, src_l, src_r, p);
 #pragma unroll
-        for (int kh = 0; kh < K; ++kh) {
-          uint64_t p[10];
-          dw_pk_window<T>(sp + kh * rsp, col, g.TW, left_edge, right_edge, src_l, src_r, p);
+      for (int kd = 0; kd < K; ++kd) {
+        const int slotk = (j - kd + K) % K;
 #pragma unroll
-          for (int kd = 0; kd < K; ++kd) {
-            const int slotk = (j - kd + K) % K;
+        for (int kw = 0; kw < K; ++kw) {
+          const uint64_t wv = sw[(kd * K + kh) * K + kw];
 #pragma unroll
-            for (int kw = 0; kw < K; ++kw) {
-              const uint64_t wv = sw[(kd * K + kh) * K + kw];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) acc[slotk][i] = pk_fma(p[i + kw], wv, acc[slotk][i]);
-            }
-          }
-        }
-        // release the slot; the warp that releases it last loads the slot's next plane
-        __syncwarp();
-        if (lane == 0) {
-          int prev;
-          asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;"
-                       : "=r"(prev)
-                       : "r"(smem_u32(&ring.released[slot]))
-                       : "memory");
-          // the count only grows: the slot's (s / kDwSlots)-th plane is released by nwarps arrivals
-          if (prev == (s / kDwSlots + 1) * nwarps - 1) {
-            const int q = s + kDwSlots;
-            if (q < nsteps) {
-              fence_async_smem();
-              mbar_arrive_expect_tx(&ring.full[slot], tile_bytes);
-              tma_load_4d(slots + (size_t)slot * slot_bytes, &mX, &ring.full[slot], w0 - OFF, h0 - 1, d0 - 1 + q,
-                          nc);
-              atomicAdd(&ring.issued, 1);
-            }
-          }
-        }
-        // output plane s-(K-1) is complete; its slot is (j+1) % K
-        const int o = s - (K - 1);
-        if (store_row && o >= 0) {
-          const int oslot = (j + 1) % K;
-          const size_t off = out0 + (size_t)(d0 + o) * plane_elems;
-          float lo[8], hi[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            pk_split(acc[oslot][i], lo[i], hi[i]);
-            lo[i] += bv;
-            hi[i] += bv;
-          }
-          if constexpr (ADD) {
-            float al[8], ah[8];
-            const uint4* ap = reinterpret_cast<const uint4*>(addend + off);
-            unpack16<T>(__ldg(ap), al);
-            unpack16<T>(hi_ok ? __ldg(ap + 1) : make_uint4(0, 0, 0, 0), ah);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              lo[i] += al[i];
-              hi[i] += ah[i];
-            }
-          }
-          const uint4 qlo = pack16<T>(lo), qhi = pack16<T>(hi);
-          uint4* dst = reinterpret_cast<uint4*>(y + off);
-          dst[0] = qlo;
-          if (hi_ok) dst[1] = qhi;
-          if constexpr (STATS) {
-            // statistics of the stored values
-            float rl[8], rh[8];
-            unpack16<T>(qlo, rl);
-            unpack16<T>(qhi, rh);
-            if (st_n == 0.f) st_shift = rl[0];
-            const float2 sh = make_float2(-st_shift, -st_shift);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float2 dv = __fadd2_rn(make_float2(rl[i], hi_ok ? rh[i] : st_shift), sh);
-              st_s1 = __fadd2_rn(st_s1, dv);
-              st_s2 = __ffma2_rn(dv, dv, st_s2);
-            }
-            st_n += hi_ok ? 16.f : 8.f;
-          }
+          for (int i = 0; i < 8; ++i) acc[slotk][i] = pk_fma(p[i + kw], wv, acc[slotk][i]);
         }
       }
     }
-  }
+    // release the slot; the warp that releases it last loads the slot's next plane
+    __syncwarp();
+    if (lane == 0) {
+      int prev;
+      asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;"
+                   : "=r"(prev)
+                   : "r"(smem_u32(&ring.released[slot]))
+                   : "memory");
+      // the count only grows: the slot's (s / kDwSlots)-th plane is released by nwarps arrivals
+      if (prev == (s / kDwSlots + 1) * nwarps - 1) {
+        const int q = s + kDwSlots;
+        if (q < nsteps) {
+          fence_async_smem();
+          mbar_arrive_expect_tx(&ring.full[slot], tile_bytes);
+          tma_load_4d(slots + (size_t)slot * slot_bytes, &mX, &ring.full[slot], w0 - OFF, h0 - 1, d0 - 1 + q,
+                      nc);
+          atomicAdd(&ring.issued, 1);
+        }
+      }
+    }
+    // output plane s-(K-1) is complete; its slot is (j+1) % K
+    const int o = s - (K - 1);
+    if (store_row && o >= 0) {
+      const int oslot = (j + 1) % K;
+      const size_t off = out0 + (size_t)(d0 + o) * plane_elems;
+      const uint64_t bv2 = pk_pair(bvb, bvb);
+      float lo[8], hi[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pk_split(pk_add(acc[oslot][i], bv2), lo[i], hi[i]);
+      if constexpr (ADD) {
+        float al[8], ah[8];
+        const uint4* ap = reinterpret_cast<const uint4*>(addend + off);
+        unpack16<T>(__ldg(ap), al);
+        unpack16<T>(hi_ok ? __ldg(ap + 1) : make_uint4(0, 0, 0, 0), ah);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          lo[i] += al[i];
+          hi[i] += ah[i];
+        }
+      }
+      const uint4 qlo = pack16<T>(lo), qhi = pack16<T>(hi);
+      uint4* dst = reinterpret_cast<uint4*>(y + off);
+      dst[0] = qlo;
+      if (hi_ok) dst[1] = qhi;
+      if constexpr (STATS) {
+        // statistics of the stored values
+        float rl[8], rh[8];
+        unpack16<T>(qlo, rl);
+        unpack16<T>(qhi, rh);
+        if (st_n == 0.f) st_shift = rl[0];
+        const float2 sh = make_float2(-st_shift, -st_shift);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 dv = __fadd2_rn(make_float2(rl[i], hi_ok ? rh[i] : st_shift), sh);
+          st_s1 = __fadd2_rn(st_s1, dv);
+          st_s2 = __ffma2_rn(dv, dv, st_s2);
+        }
+        st_n += hi_ok ? 16.f : 8.f;
+      }
+    }
+    return true;
+  };
+  using J0 = std::integral_constant<int, 0>;
+  using J1 = std::integral_constant<int, 1>;
+  using J2 = std::integral_constant<int, 2>;
+  // whole rounds of K steps, then the remainder; every lane of a warp leaves together
+  int sb = 0;
+  bool ok = true;
+  for (; ok && sb + K <= nsteps; sb += K) ok = step(J0{}, sb) && step(J1{}, sb + 1) && step(J2{}, sb + 2);
+  if (ok && sb < nsteps) ok = step(J0{}, sb);
+  if (ok && sb + 1 < nsteps) step(J1{}, sb + 1);
 
   __syncthreads();
   // after an abort, wait (bounded) for the loads still in flight before the CTA exits
