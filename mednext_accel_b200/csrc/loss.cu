@@ -52,16 +52,30 @@ __global__ void __launch_bounds__(kCeThreads) ce_partial_kernel(const T* __restr
   }
 }
 
-// out[0] = sum(loss) / count (NaN when nothing is counted, as torch), out[1] = count
-__global__ void ce_finish_kernel(const double* __restrict__ part, int blocks, float* __restrict__ out) {
-  if (threadIdx.x != 0) return;
+// out[0] = sum(loss) / count (NaN when nothing is counted, as torch), out[1] = count.
+// One block: strided per-thread sums, then a tree, both in a fixed order.
+__global__ void __launch_bounds__(kCeThreads) ce_finish_kernel(const double* __restrict__ part, int blocks,
+                                                               float* __restrict__ out) {
+  __shared__ double sl[kCeThreads], sc[kCeThreads];
   double l = 0.0, c = 0.0;
-  for (int b = 0; b < blocks; ++b) {
+  for (int b = threadIdx.x; b < blocks; b += kCeThreads) {
     l += part[2 * b];
     c += part[2 * b + 1];
   }
-  out[0] = (float)(l / c);
-  out[1] = (float)c;
+  sl[threadIdx.x] = l;
+  sc[threadIdx.x] = c;
+  __syncthreads();
+  for (int o = kCeThreads / 2; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) {
+      sl[threadIdx.x] += sl[threadIdx.x + o];
+      sc[threadIdx.x] += sc[threadIdx.x + o];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    out[0] = (float)(sl[0] / sc[0]);
+    out[1] = (float)sc[0];
+  }
 }
 
 template <typename T>
@@ -106,7 +120,7 @@ int launch_ce_fwd(const void* logits, const int64_t* target, double* part, float
                                                      ignore_index);
   int st = record_launch();
   if (st != MEDNEXT_OK) return st;
-  ce_finish_kernel<<<1, 32, 0, s>>>(part, blocks, out);
+  ce_finish_kernel<<<1, kCeThreads, 0, s>>>(part, blocks, out);
   return record_launch();
 }
 
