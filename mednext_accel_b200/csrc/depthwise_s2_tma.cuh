@@ -1,0 +1,245 @@
+// Stride-2 depthwise gather (the down block's forward, k = 3, 16-bit types)
+// with the input planes streamed by TMA and packed fp32 FMAs (sm_100a).
+//
+//   small[m] = bias + sum_t big[2m - 1 + t] * w[t]    (t over the 3x3x3 taps)
+//
+// A CTA owns one (sample, channel) tile of TWo x THo outputs and a chunk of
+// output planes.  The halo'd input plane tiles (2*THo + 1 rows, 2*TWo + 16
+// columns starting at the 16-byte boundary 2*ow0 - 8) stream through the same
+// kDwSlots ring as the stride-1 packed kernel, with no producer warp: thread 0
+// issues the first loads and the warp that releases a slot last issues the
+// slot's next load.  Out-of-range rows, columns and planes arrive as zeros,
+// which is the convolution's zero padding.
+//
+// Each thread owns 8 outputs of one row and accumulates the pairs (i, i+4) with
+// fma.rn.f32x2; the window pairs (x[m-1], x[m+7]) are the stride-1 packed
+// kernel's.  Input plane s of a chunk feeds output plane s/2 with tap kd = 0
+// (even s, which also finishes output s/2 - 1 with kd = 2) or output (s-1)/2
+// with kd = 1 (odd s), so every output sums bias first, then its taps in
+// (kd, kh, kw) order: the order of dw_s2_gather_kernel, whose results this
+// kernel reproduces bit for bit.
+#pragma once
+
+#include <type_traits>
+
+#include "depthwise_s1_tma.cuh"
+#include "depthwise_s2.cuh"
+
+namespace mednext {
+
+constexpr int kS2PkThreads = 256;
+
+struct DwS2PkGeom {
+  DwS2Geom g;
+  int TWo, THo, TDo;  // output tile (columns, rows, planes)
+  int tilesW, tilesH, tilesD;
+  int lw;             // threads along W (8 outputs each)
+};
+
+template <typename T>
+struct DwS2PkLayout {
+  static __host__ __device__ int pitch(int TWo) { return 2 * TWo + 16; }
+  static __host__ __device__ int rows(int THo) { return 2 * THo + 1; }
+  static __host__ __device__ size_t x_tile(const DwS2PkGeom& p) { return (size_t)rows(p.THo) * pitch(p.TWo) * sizeof(T); }
+  static __host__ __device__ size_t slot(const DwS2PkGeom& p) { return DwTmaLayout<T>::align128(x_tile(p)); }
+  static __host__ size_t smem(const DwS2PkGeom& p) { return 128 + kDwSlots * slot(p); }
+};
+
+// p[m] = (x[m-1], x[m+7]), m = 0..8, for the 17 inputs x[-1..15] of the thread's
+// 8 outputs; rowp[col] is x[0].  x[-1] comes from the left neighbour's last
+// input (lane src_l), or from the row's halo column at the tile edge.
+template <typename T>
+__device__ __forceinline__ void dw_s2pk_window(const T* __restrict__ rowp, int col, bool left_edge, int src_l,
+                                               uint64_t (&p)[9]) {
+  const uint4 c0 = *reinterpret_cast<const uint4*>(rowp + col);      // x[0..7]
+  const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + col + 8);  // x[8..15]
+  const uint32_t from_l = __shfl_sync(0xffffffffu, c1.w, src_l);     // (x[14], x[15]) of the left neighbour
+  const uint32_t el = reinterpret_cast<const unsigned short*>(rowp)[col - 1];
+  const uint32_t xl = left_edge ? el : (from_l >> 16);
+  const uint32_t a[4] = {c0.x, c0.y, c0.z, c0.w};
+  const uint32_t b[4] = {c1.x, c1.y, c1.z, c1.w};
+  p[0] = pk_pair(lo_bits<T>(xl), hi_bits<T>(a[3]));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    p[2 * q + 1] = pk_pair(lo_bits<T>(a[q]), lo_bits<T>(b[q]));  // (x[2q], x[2q+8])
+    p[2 * q + 2] = pk_pair(hi_bits<T>(a[q]), hi_bits<T>(b[q]));  // (x[2q+1], x[2q+9])
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kS2PkThreads, 2)
+    dw_s2_gather_pk_kernel(const __grid_constant__ CUtensorMap mX, const T* __restrict__ wgt,
+                           const T* __restrict__ bias, T* __restrict__ small, DwS2PkGeom pg) {
+  constexpr int K = 3;
+  constexpr int K3 = 27;
+  using L = DwS2PkLayout<T>;
+  const DwS2Geom& g = pg.g;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ DwPkRing ring;
+  unsigned char* slots = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  const size_t slot_bytes = L::slot(pg);
+  const uint32_t tile_bytes = (uint32_t)L::x_tile(pg);
+  const int rsp = L::pitch(pg.TWo);
+  const int nwarps = (int)blockDim.x >> 5;
+
+  int bx = blockIdx.x;
+  const int tw = bx % pg.tilesW;
+  bx /= pg.tilesW;
+  const int th = bx % pg.tilesH;
+  bx /= pg.tilesH;
+  const int td = bx % pg.tilesD;
+  const int nc = bx / pg.tilesD;
+  const int c = nc % g.C;
+  const int ow0 = tw * pg.TWo, oh0 = th * pg.THo, md0 = td * pg.TDo;
+  const int dcount = min(pg.TDo, g.Ds - md0);
+  const int nsteps = 2 * dcount + 1;
+
+  auto issue = [&](int q) {
+    const int slot = q % kDwSlots;
+    mbar_arrive_expect_tx(&ring.full[slot], tile_bytes);
+    tma_load_4d(slots + (size_t)slot * slot_bytes, &mX, &ring.full[slot], 2 * ow0 - 8, 2 * oh0 - 1, 2 * md0 - 1 + q,
+                nc);
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDwSlots; ++i) {
+      mbar_init(&ring.full[i], 1);
+      ring.released[i] = 0;
+    }
+    ring.abort = 0;
+    fence_mbarrier_init();
+    tma_prefetch_map(&mX);
+    const int first = min(nsteps, kDwSlots);
+    for (int q = 0; q < first; ++q) issue(q);
+    ring.issued = first;
+  }
+  __syncthreads();
+  volatile int* abort = &ring.abort;
+
+  const int lane = threadIdx.x & 31;
+  const int lw = pg.lw;
+  const int wt = threadIdx.x % lw;
+  const int r = threadIdx.x / lw;
+  const bool active = r < pg.THo;
+  const int oh = oh0 + r;
+  const int ow = ow0 + 8 * wt;
+  // Ws is a multiple of 8 on this path: a thread's 8 outputs are in or out as a whole
+  const bool store_row = active && oh < g.Hs && ow < g.Ws;
+  // a row of lw <= 8 threads lies within one warp: the left neighbour is lane - 1
+  const int src_l = wt > 0 ? lane - 1 : lane;
+  const bool left_edge = wt == 0;
+  // lanes past the tile read row 0 (every lane joins the shuffles) and store nothing
+  const int xbase = (active ? 2 * r : 0) * rsp;
+  const int col = 8 + 16 * wt;
+  uint64_t wp[K3];
+#pragma unroll
+  for (int t = 0; t < K3; ++t) {
+    const uint32_t wv = __float_as_uint(to_acc<T>(__ldg(wgt + (size_t)c * K3 + t)));
+    wp[t] = pk_pair(wv, wv);
+  }
+  const uint32_t bvb = __float_as_uint(bias != nullptr ? to_acc<T>(bias[c]) : 0.f);
+  const uint64_t bv2 = pk_pair(bvb, bvb);
+  const size_t plane = (size_t)g.Hs * g.Ws;
+  T* out0 = small + ((size_t)nc * g.Ds) * plane + (size_t)oh * g.Ws + ow;
+
+  uint64_t acc[2][4];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[a][i] = 0ull;
+
+  // step s (phase F = s % 4): input plane 2*md0 - 1 + s.  Even s = 2u finishes
+  // output u - 1 (tap kd = 2, slot (u-1) % 2) and starts output u (bias, then
+  // kd = 0, slot u % 2); odd s = 2u + 1 adds kd = 1 to output u.
+  auto step = [&](auto fc, const int s) -> bool {
+    constexpr int F = decltype(fc)::value;
+    constexpr bool even = (F % 2) == 0;
+    constexpr int cur = (F / 2) % 2;   // slot of output u = s / 2
+    constexpr int prev = 1 - cur;      // slot of output u - 1
+    const int slot = s % kDwSlots;
+    const bool ok = !*abort && mbar_wait(&ring.full[slot], (uint32_t)((s / kDwSlots) & 1));
+    if (!__all_sync(0xffffffffu, ok)) {
+      *abort = 1;
+      return false;
+    }
+    const int u = s >> 1;
+    const bool finish = even && u >= 1;
+    const bool start = even && u < dcount;
+    if (start) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[cur][i] = bv2;
+    }
+    const T* xp = reinterpret_cast<const T*>(slots + (size_t)slot * slot_bytes) + xbase;
+#pragma unroll
+    for (int kh = 0; kh < K; ++kh) {
+      uint64_t p[9];
+      dw_s2pk_window<T>(xp + kh * rsp, col, left_edge, src_l, p);
+#pragma unroll
+      for (int kw = 0; kw < K; ++kw) {
+        if constexpr (even) {
+          if (finish) {
+            const uint64_t w2 = wp[(2 * K + kh) * K + kw];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[prev][i] = pk_fma(p[2 * i + kw], w2, acc[prev][i]);
+          }
+          if (start) {
+            const uint64_t w0 = wp[(0 * K + kh) * K + kw];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[cur][i] = pk_fma(p[2 * i + kw], w0, acc[cur][i]);
+          }
+        } else {
+          const uint64_t w1 = wp[(1 * K + kh) * K + kw];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[cur][i] = pk_fma(p[2 * i + kw], w1, acc[cur][i]);
+        }
+      }
+    }
+    // release the slot; the warp that releases it last loads the slot's next plane
+    __syncwarp();
+    if (lane == 0) {
+      int prv;
+      asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;"
+                   : "=r"(prv)
+                   : "r"(smem_u32(&ring.released[slot]))
+                   : "memory");
+      // the count only grows: the slot's (s / kDwSlots)-th plane is released by nwarps arrivals
+      if (prv == (s / kDwSlots + 1) * nwarps - 1) {
+        const int q = s + kDwSlots;
+        if (q < nsteps) {
+          fence_async_smem();
+          issue(q);
+          atomicAdd(&ring.issued, 1);
+        }
+      }
+    }
+    if (finish && store_row) {
+      float lo[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pk_split(acc[prev][i], lo[i], lo[i + 4]);
+      *reinterpret_cast<uint4*>(out0 + (size_t)(md0 + u - 1) * plane) = pack16<T>(lo);
+    }
+    return true;
+  };
+  using F0 = std::integral_constant<int, 0>;
+  using F1 = std::integral_constant<int, 1>;
+  using F2 = std::integral_constant<int, 2>;
+  using F3 = std::integral_constant<int, 3>;
+  // whole rounds of 4 steps, then the remainder; every lane of a warp leaves together
+  int sb = 0;
+  bool ok = true;
+  for (; ok && sb + 4 <= nsteps; sb += 4)
+    ok = step(F0{}, sb) && step(F1{}, sb + 1) && step(F2{}, sb + 2) && step(F3{}, sb + 3);
+  if (ok && sb < nsteps) ok = step(F0{}, sb);
+  if (ok && sb + 1 < nsteps) ok = step(F1{}, sb + 1);
+  if (ok && sb + 2 < nsteps) step(F2{}, sb + 2);
+
+  __syncthreads();
+  // after an abort, wait (bounded) for the loads still in flight before the CTA exits
+  if (*abort && threadIdx.x == 0) {
+    const int issued = ring.issued;
+    for (int q = issued > kDwSlots ? issued - kDwSlots : 0; q < issued; ++q)
+      mbar_wait(&ring.full[q % kDwSlots], (uint32_t)((q / kDwSlots) & 1));
+    raise_device_error(kErrMbarTimeout);
+  }
+}
+
+}  // namespace mednext

@@ -1,6 +1,10 @@
 // Template instantiation and launch of the depthwise kernels (stride 2 and
 // transpose) for every supported element type and kernel size.
+#include <type_traits>
+
+#include "depthwise_s2_tma.cuh"
 #include "plan.h"
+#include "tma_host.h"
 
 namespace mednext {
 
@@ -17,9 +21,68 @@ int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, i
 // One CTA per (sample, channel, plane): the grid must fit gridDim.x.
 bool grid_ok(long long ctas) { return ctas > 0 && ctas < (1LL << 31); }
 
+// Down-block forward (k = 3, 16-bit types, no addend) on the TMA plane ring with
+// packed FMAs: needs 16-byte rows on both grids (W multiple of 8, big W = 2 x
+// small W), contiguous (n, c) volumes and 16-byte aligned bases.
+template <typename T, int K>
+int try_gather_pk(const void* big, const void* w, const void* b, const void* addend, void* small, const DwS2Geom& g,
+                  cudaStream_t s) {
+  if constexpr (K != 3 || !(std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value)) {
+    return -1;
+  } else {
+    if (addend != nullptr || g.Wb != 2 * g.Ws || g.Wb % 8 != 0 || g.Ws % 8 != 0 ||
+        g.bp != (long long)g.Db * g.Hb * g.Wb || (reinterpret_cast<uintptr_t>(big) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(small) & 15) != 0)
+      return -1;
+    DwS2PkGeom pg{};
+    pg.g = g;
+    pg.TWo = std::min(64, g.Ws);
+    pg.lw = pg.TWo / 8;
+    pg.THo = std::min(std::min(kS2PkThreads / pg.lw, g.Hs), 127);
+    pg.tilesW = (g.Ws + pg.TWo - 1) / pg.TWo;
+    pg.tilesH = (g.Hs + pg.THo - 1) / pg.THo;
+    const long long base = (long long)g.N * g.C * pg.tilesW * pg.tilesH;
+    using L = DwS2PkLayout<T>;
+    // output-plane chunks minimising (rounds of resident CTAs) x (input planes per CTA)
+    const size_t smem_one = L::smem(pg);
+    const long long per_sm = std::max<long long>(1, std::min<long long>(2, (long long)(200 * 1024 / smem_one)));
+    const long long slots = 148 * per_sm;
+    long long best_cost = -1, chunks = 1;
+    for (long long cand = 1; cand <= std::max(1, g.Ds / 2); ++cand) {
+      const long long td = (g.Ds + cand - 1) / cand;
+      const long long ctas = base * ((g.Ds + td - 1) / td);
+      const long long cost = ((ctas + slots - 1) / slots) * (2 * td + 1);
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        chunks = cand;
+      }
+    }
+    pg.TDo = (int)((g.Ds + chunks - 1) / chunks);
+    pg.tilesD = (g.Ds + pg.TDo - 1) / pg.TDo;
+    const long long ctas = base * pg.tilesD;
+    if (!grid_ok(ctas)) return -1;
+    CUtensorMap m;
+    if (!tma::encode4<T>(&m, big, (uint64_t)g.Wb, (uint64_t)g.Hb, (uint64_t)g.Db, (uint64_t)g.N * g.C,
+                         (uint32_t)L::pitch(pg.TWo), (uint32_t)L::rows(pg.THo)))
+      return -1;
+    const int threads = (pg.lw * pg.THo + 31) / 32 * 32;
+    auto kern = dw_s2_gather_pk_kernel<T>;
+    static size_t configured = 0;
+    if (smem_one > 48 * 1024 && smem_one > configured) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_one);
+      configured = smem_one;
+    }
+    kern<<<(unsigned)ctas, threads, smem_one, s>>>(m, static_cast<const T*>(w), static_cast<const T*>(b),
+                                                   static_cast<T*>(small), pg);
+    return record_launch();
+  }
+}
+
 template <typename T, int K>
 int launch_gather(const void* big, const void* w, const void* b, const void* addend, void* small, const DwS2Geom& g,
                   cudaStream_t s) {
+  const int pst = try_gather_pk<T, K>(big, w, b, addend, small, g, s);
+  if (pst != -1) return pst;
   const long long ctas = (long long)g.N * g.C * g.Ds;
   if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
   auto kern = addend != nullptr ? dw_s2_gather_kernel<T, K, true> : dw_s2_gather_kernel<T, K, false>;

@@ -207,6 +207,30 @@ def test_packed_k3_kernel_is_bit_exact_with_fp32_kernel(dtype, shape):
     torch.testing.assert_close(stats[:, 1].double(), rstd, rtol=1e-5, atol=1e-6)
 
 
+DOWN_SHAPES = [
+    (1, 32, 128, 128, 128),  # the benchmark's first down block
+    (2, 3, 16, 20, 32),      # ragged last row tile of the small grid
+    (1, 2, 9, 6, 16),        # odd depth: the last input plane is padding
+    (1, 4, 8, 40, 256),      # two 64-wide tiles along W
+    (1, 2, 4, 4, 16),        # a single output plane pair
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", DOWN_SHAPES)
+def test_stride2_forward_tma_kernel_is_bit_exact_with_fp32_kernel(dtype, shape):
+    """The down block's forward (k = 3, 16-bit) runs on the TMA plane ring with
+    packed FMAs and sums bias, then taps in (kd, kh, kw) order, as the fp32 gather
+    does: its outputs are the fp32 kernel's outputs on the same inputs, rounded once."""
+    seed = seed_of("down", str(dtype), shape)
+    x = rand(shape, dtype, seed).cuda()
+    w = rand((shape[1], 1, 3, 3, 3), dtype, seed + 1, scale=0.2).cuda()
+    b = rand((shape[1],), dtype, seed + 2).cuda()
+    y = dwk.s2_forward(x, w, b, 3)
+    assert torch.equal(y, dwk.s2_forward(x.float(), w.float(), b.float(), 3).to(dtype))
+    assert nat.device_error() == 0
+
+
 def test_dgrad_with_addend_adds_residual():
     x = rand((1, 4, 8, 16, 16), torch.bfloat16, 8).cuda()
     w = rand((4, 1, 3, 3, 3), torch.bfloat16, 9).cuda()
