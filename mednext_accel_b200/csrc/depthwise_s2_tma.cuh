@@ -242,4 +242,218 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
   }
 }
 
+// ----------------------------------------------------------------------------
+// Stride-2 weight grad of the down block (k = 3, 16-bit types):
+//   dw[t] = sum_m big[2m - 1 + t] * small[m],  dbias = sum_m small[m]
+// Same tile, ring and input windows as dw_s2_gather_pk_kernel; a slot also holds
+// the small-grid (dy) plane tile of output plane s/2 at even steps.  The thread's
+// dy row (8 values as pairs (i, i+4)) stays in registers for the three steps that
+// use it (kd = 0 at step 2u, kd = 1 at 2u + 1, kd = 2 at 2u + 2).  The 27 tap
+// sums and the bias sum are per-thread pairs folded at the end in a fixed order;
+// one partial per (sample, channel, tile), summed by dw_wgrad_finish_kernel.
+// ----------------------------------------------------------------------------
+template <typename T>
+struct DwS2PkWLayout {
+  static __host__ __device__ size_t dy_offset(const DwS2PkGeom& p) {
+    return DwTmaLayout<T>::align128(DwS2PkLayout<T>::x_tile(p));
+  }
+  static __host__ __device__ size_t dy_tile(const DwS2PkGeom& p) { return (size_t)p.THo * p.TWo * sizeof(T); }
+  static __host__ __device__ size_t slot(const DwS2PkGeom& p) { return DwTmaLayout<T>::align128(dy_offset(p) + dy_tile(p)); }
+  static __host__ size_t smem(const DwS2PkGeom& p) { return 128 + kDwSlots * slot(p); }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kS2PkThreads, 2)
+    dw_s2_wgrad_pk_kernel(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mDY,
+                          float* __restrict__ part, DwS2PkGeom pg) {
+  constexpr int K = 3;
+  constexpr int K3 = 27;
+  using L = DwS2PkLayout<T>;
+  using LW = DwS2PkWLayout<T>;
+  const DwS2Geom& g = pg.g;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ DwPkRing ring;
+  __shared__ float red[(kS2PkThreads / 32) * (K3 + 1)];
+  unsigned char* slots = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  const size_t slot_bytes = LW::slot(pg);
+  const size_t dy_off = LW::dy_offset(pg);
+  const uint32_t x_bytes = (uint32_t)L::x_tile(pg);
+  const uint32_t dy_bytes = (uint32_t)LW::dy_tile(pg);
+  const int rsp = L::pitch(pg.TWo);
+  const int nwarps = (int)blockDim.x >> 5;
+
+  int bx = blockIdx.x;
+  const int tw = bx % pg.tilesW;
+  bx /= pg.tilesW;
+  const int th = bx % pg.tilesH;
+  bx /= pg.tilesH;
+  const int td = bx % pg.tilesD;
+  const int nc = bx / pg.tilesD;
+  const int ow0 = tw * pg.TWo, oh0 = th * pg.THo, md0 = td * pg.TDo;
+  const int dcount = min(pg.TDo, g.Ds - md0);
+  const int nsteps = 2 * dcount + 1;
+
+  // step q: the big plane 2*md0 - 1 + q and, at even q below 2*dcount, the small plane md0 + q/2
+  auto issue = [&](int q) {
+    const int slot = q % kDwSlots;
+    unsigned char* dst = slots + (size_t)slot * slot_bytes;
+    const bool with_dy = (q % 2) == 0 && q / 2 < dcount;
+    mbar_arrive_expect_tx(&ring.full[slot], x_bytes + (with_dy ? dy_bytes : 0u));
+    tma_load_4d(dst, &mX, &ring.full[slot], 2 * ow0 - 8, 2 * oh0 - 1, 2 * md0 - 1 + q, nc);
+    if (with_dy) tma_load_4d(dst + dy_off, &mDY, &ring.full[slot], ow0, oh0, md0 + q / 2, nc);
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDwSlots; ++i) {
+      mbar_init(&ring.full[i], 1);
+      ring.released[i] = 0;
+    }
+    ring.abort = 0;
+    fence_mbarrier_init();
+    tma_prefetch_map(&mX);
+    tma_prefetch_map(&mDY);
+    const int first = min(nsteps, kDwSlots);
+    for (int q = 0; q < first; ++q) issue(q);
+    ring.issued = first;
+  }
+  __syncthreads();
+  volatile int* abort = &ring.abort;
+
+  const int lane = threadIdx.x & 31;
+  const int lw = pg.lw;
+  const int wt = threadIdx.x % lw;
+  const int r = threadIdx.x / lw;
+  const bool active = r < pg.THo;
+  const int src_l = wt > 0 ? lane - 1 : lane;
+  const bool left_edge = wt == 0;
+  // lanes past the tile read row 0 (every lane joins the shuffles) with a zero dy
+  const int xbase = (active ? 2 * r : 0) * rsp;
+  const int col = 8 + 16 * wt;
+  const int dybase = (active ? r : 0) * pg.TWo + 8 * wt;
+
+  uint64_t acc[K3];
+  uint64_t accb = 0ull;
+  uint64_t dyp[2][4];
+#pragma unroll
+  for (int t = 0; t < K3; ++t) acc[t] = 0ull;
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dyp[a][i] = 0ull;
+
+  // step s (phase F = s % 4), u = s / 2: even s loads dy plane u into slot u % 2 and
+  // adds kd = 0 (dy u) and kd = 2 (dy u - 1); odd s adds kd = 1 (dy u).
+  auto step = [&](auto fc, const int s) -> bool {
+    constexpr int F = decltype(fc)::value;
+    constexpr bool even = (F % 2) == 0;
+    constexpr int cur = (F / 2) % 2;
+    constexpr int prev = 1 - cur;
+    const int slot = s % kDwSlots;
+    const bool ok = !*abort && mbar_wait(&ring.full[slot], (uint32_t)((s / kDwSlots) & 1));
+    if (!__all_sync(0xffffffffu, ok)) {
+      *abort = 1;
+      return false;
+    }
+    const int u = s >> 1;
+    const unsigned char* sb = slots + (size_t)slot * slot_bytes;
+    if constexpr (even) {
+      if (active && u < dcount) {
+        const uint4 d = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(sb + dy_off) + dybase);
+        dyp[cur][0] = pk_pair(lo_bits<T>(d.x), lo_bits<T>(d.z));
+        dyp[cur][1] = pk_pair(hi_bits<T>(d.x), hi_bits<T>(d.z));
+        dyp[cur][2] = pk_pair(lo_bits<T>(d.y), lo_bits<T>(d.w));
+        dyp[cur][3] = pk_pair(hi_bits<T>(d.y), hi_bits<T>(d.w));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dyp[cur][i] = 0ull;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) accb = pk_add(accb, dyp[cur][i]);
+    }
+    const T* xp = reinterpret_cast<const T*>(sb) + xbase;
+#pragma unroll
+    for (int kh = 0; kh < K; ++kh) {
+      uint64_t p[9];
+      dw_s2pk_window<T>(xp + kh * rsp, col, left_edge, src_l, p);
+#pragma unroll
+      for (int kw = 0; kw < K; ++kw) {
+        if constexpr (even) {
+          uint64_t a0 = acc[(0 * K + kh) * K + kw], a2 = acc[(2 * K + kh) * K + kw];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            a0 = pk_fma(p[2 * i + kw], dyp[cur][i], a0);
+            a2 = pk_fma(p[2 * i + kw], dyp[prev][i], a2);
+          }
+          acc[(0 * K + kh) * K + kw] = a0;
+          acc[(2 * K + kh) * K + kw] = a2;
+        } else {
+          uint64_t a1 = acc[(1 * K + kh) * K + kw];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a1 = pk_fma(p[2 * i + kw], dyp[cur][i], a1);
+          acc[(1 * K + kh) * K + kw] = a1;
+        }
+      }
+    }
+    // release the slot; the warp that releases it last loads the slot's next planes
+    __syncwarp();
+    if (lane == 0) {
+      int prv;
+      asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;"
+                   : "=r"(prv)
+                   : "r"(smem_u32(&ring.released[slot]))
+                   : "memory");
+      // the count only grows: the slot's (s / kDwSlots)-th planes are released by nwarps arrivals
+      if (prv == (s / kDwSlots + 1) * nwarps - 1) {
+        const int q = s + kDwSlots;
+        if (q < nsteps) {
+          fence_async_smem();
+          issue(q);
+          atomicAdd(&ring.issued, 1);
+        }
+      }
+    }
+    return true;
+  };
+  using F0 = std::integral_constant<int, 0>;
+  using F1 = std::integral_constant<int, 1>;
+  using F2 = std::integral_constant<int, 2>;
+  using F3 = std::integral_constant<int, 3>;
+  int sb = 0;
+  bool ok = true;
+  for (; ok && sb + 4 <= nsteps; sb += 4)
+    ok = step(F0{}, sb) && step(F1{}, sb + 1) && step(F2{}, sb + 2) && step(F3{}, sb + 3);
+  if (ok && sb < nsteps) ok = step(F0{}, sb);
+  if (ok && sb + 1 < nsteps) ok = step(F1{}, sb + 1);
+  if (ok && sb + 2 < nsteps) step(F2{}, sb + 2);
+
+  __syncthreads();
+  // after an abort, wait (bounded) for the loads still in flight before the CTA exits
+  if (*abort && threadIdx.x == 0) {
+    const int issued = ring.issued;
+    for (int q = issued > kDwSlots ? issued - kDwSlots : 0; q < issued; ++q)
+      mbar_wait(&ring.full[q % kDwSlots], (uint32_t)((q / kDwSlots) & 1));
+    raise_device_error(kErrMbarTimeout);
+  }
+  float sums[K3 + 1];
+#pragma unroll
+  for (int t = 0; t < K3; ++t) {
+    float lo, hi;
+    pk_split(acc[t], lo, hi);
+    sums[t] = lo + hi;
+  }
+  {
+    float lo, hi;
+    pk_split(accb, lo, hi);
+    sums[K3] = lo + hi;
+  }
+  block_sum_to_smem<float, K3 + 1>(sums, red);
+  __syncthreads();
+  const int tiles = pg.tilesW * pg.tilesH * pg.tilesD;
+  const int tile = (td * pg.tilesH + th) * pg.tilesW + tw;
+  for (int t = threadIdx.x; t <= K3; t += blockDim.x) {
+    float v = 0.f;
+    for (int w = 0; w < nwarps; ++w) v += red[w * (K3 + 1) + t];
+    part[((size_t)nc * tiles + tile) * (K3 + 1) + t] = v;
+  }
+}
+
 }  // namespace mednext

@@ -21,60 +21,110 @@ int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, i
 // One CTA per (sample, channel, plane): the grid must fit gridDim.x.
 bool grid_ok(long long ctas) { return ctas > 0 && ctas < (1LL << 31); }
 
-// Down-block forward (k = 3, 16-bit types, no addend) on the TMA plane ring with
-// packed FMAs: needs 16-byte rows on both grids (W multiple of 8, big W = 2 x
-// small W), contiguous (n, c) volumes and 16-byte aligned bases.
+// Tiles of the TMA stride-2 kernels (down block, k = 3, 16-bit types): 16-byte
+// rows on both grids (W a multiple of 8, big W = 2 x small W), contiguous (n, c)
+// volumes.  Output planes are chunked to minimise (rounds of resident CTAs) x
+// (input planes per CTA), with at most max_tiles tiles per (n, c).
+bool s2pk_geom_ok(const DwS2Geom& g, const void* big, const void* small) {
+  return g.Wb == 2 * g.Ws && g.Wb % 8 == 0 && g.Ws % 8 == 0 && g.bp == (long long)g.Db * g.Hb * g.Wb &&
+         (reinterpret_cast<uintptr_t>(big) & 15) == 0 && (reinterpret_cast<uintptr_t>(small) & 15) == 0;
+}
+DwS2PkGeom s2pk_plan(const DwS2Geom& g, size_t (*smem_of)(const DwS2PkGeom&), long long max_tiles) {
+  DwS2PkGeom pg{};
+  pg.g = g;
+  pg.TWo = std::min(64, g.Ws);
+  pg.lw = pg.TWo / 8;
+  pg.THo = std::min(std::min(kS2PkThreads / pg.lw, g.Hs), 127);
+  pg.tilesW = (g.Ws + pg.TWo - 1) / pg.TWo;
+  pg.tilesH = (g.Hs + pg.THo - 1) / pg.THo;
+  const long long per_nc = (long long)pg.tilesW * pg.tilesH;
+  const long long base = (long long)g.N * g.C * per_nc;
+  pg.TDo = g.Ds;
+  const size_t smem_one = smem_of(pg);
+  const long long slots = 148 * std::max<long long>(1, std::min<long long>(2, (long long)(200 * 1024 / smem_one)));
+  long long best_cost = -1;
+  for (long long cand = 1; cand <= std::max(1, g.Ds / 2); ++cand) {
+    const long long td = (g.Ds + cand - 1) / cand;
+    const long long tiles_d = (g.Ds + td - 1) / td;
+    if (per_nc * tiles_d > max_tiles) break;
+    const long long cost = ((base * tiles_d + slots - 1) / slots) * (2 * td + 1);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      pg.TDo = (int)td;
+    }
+  }
+  pg.tilesD = (g.Ds + pg.TDo - 1) / pg.TDo;
+  return pg;
+}
+template <typename T>
+size_t s2pk_gather_smem(const DwS2PkGeom& p) { return DwS2PkLayout<T>::smem(p); }
+template <typename T>
+size_t s2pk_wgrad_smem(const DwS2PkGeom& p) { return DwS2PkWLayout<T>::smem(p); }
+
 template <typename T, int K>
 int try_gather_pk(const void* big, const void* w, const void* b, const void* addend, void* small, const DwS2Geom& g,
                   cudaStream_t s) {
   if constexpr (K != 3 || !(std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value)) {
     return -1;
   } else {
-    if (addend != nullptr || g.Wb != 2 * g.Ws || g.Wb % 8 != 0 || g.Ws % 8 != 0 ||
-        g.bp != (long long)g.Db * g.Hb * g.Wb || (reinterpret_cast<uintptr_t>(big) & 15) != 0 ||
-        (reinterpret_cast<uintptr_t>(small) & 15) != 0)
-      return -1;
-    DwS2PkGeom pg{};
-    pg.g = g;
-    pg.TWo = std::min(64, g.Ws);
-    pg.lw = pg.TWo / 8;
-    pg.THo = std::min(std::min(kS2PkThreads / pg.lw, g.Hs), 127);
-    pg.tilesW = (g.Ws + pg.TWo - 1) / pg.TWo;
-    pg.tilesH = (g.Hs + pg.THo - 1) / pg.THo;
-    const long long base = (long long)g.N * g.C * pg.tilesW * pg.tilesH;
+    if (addend != nullptr || !s2pk_geom_ok(g, big, small)) return -1;
     using L = DwS2PkLayout<T>;
-    // output-plane chunks minimising (rounds of resident CTAs) x (input planes per CTA)
-    const size_t smem_one = L::smem(pg);
-    const long long per_sm = std::max<long long>(1, std::min<long long>(2, (long long)(200 * 1024 / smem_one)));
-    const long long slots = 148 * per_sm;
-    long long best_cost = -1, chunks = 1;
-    for (long long cand = 1; cand <= std::max(1, g.Ds / 2); ++cand) {
-      const long long td = (g.Ds + cand - 1) / cand;
-      const long long ctas = base * ((g.Ds + td - 1) / td);
-      const long long cost = ((ctas + slots - 1) / slots) * (2 * td + 1);
-      if (best_cost < 0 || cost < best_cost) {
-        best_cost = cost;
-        chunks = cand;
-      }
-    }
-    pg.TDo = (int)((g.Ds + chunks - 1) / chunks);
-    pg.tilesD = (g.Ds + pg.TDo - 1) / pg.TDo;
-    const long long ctas = base * pg.tilesD;
+    const DwS2PkGeom pg = s2pk_plan(g, s2pk_gather_smem<T>, 1LL << 30);
+    const long long ctas = (long long)g.N * g.C * pg.tilesW * pg.tilesH * pg.tilesD;
     if (!grid_ok(ctas)) return -1;
     CUtensorMap m;
     if (!tma::encode4<T>(&m, big, (uint64_t)g.Wb, (uint64_t)g.Hb, (uint64_t)g.Db, (uint64_t)g.N * g.C,
                          (uint32_t)L::pitch(pg.TWo), (uint32_t)L::rows(pg.THo)))
       return -1;
+    const size_t smem = L::smem(pg);
     const int threads = (pg.lw * pg.THo + 31) / 32 * 32;
     auto kern = dw_s2_gather_pk_kernel<T>;
     static size_t configured = 0;
-    if (smem_one > 48 * 1024 && smem_one > configured) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_one);
-      configured = smem_one;
+    if (smem > 48 * 1024 && smem > configured) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      configured = smem;
     }
-    kern<<<(unsigned)ctas, threads, smem_one, s>>>(m, static_cast<const T*>(w), static_cast<const T*>(b),
-                                                   static_cast<T*>(small), pg);
+    kern<<<(unsigned)ctas, threads, smem, s>>>(m, static_cast<const T*>(w), static_cast<const T*>(b),
+                                               static_cast<T*>(small), pg);
     return record_launch();
+  }
+}
+
+// Down-block weight grad on the same ring: partials per (n, c, tile), at most the
+// Ds per (n, c) that the workspace holds, summed by dw_wgrad_finish_kernel.
+template <typename T, int K>
+int try_s2_wgrad_pk(const void* big, const void* small, void* dw, void* db, float* part, const DwS2Geom& g,
+                    bool bias_from_big, cudaStream_t s) {
+  if constexpr (K != 3 || !(std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value)) {
+    return -1;
+  } else {
+    if (bias_from_big || !s2pk_geom_ok(g, big, small)) return -1;
+    using L = DwS2PkLayout<T>;
+    const DwS2PkGeom pg = s2pk_plan(g, s2pk_wgrad_smem<T>, plan_s2w(g.N, g.C, g.Ds, K).chunks);
+    const int tiles = pg.tilesW * pg.tilesH * pg.tilesD;
+    if (tiles > plan_s2w(g.N, g.C, g.Ds, K).chunks) return -1;
+    const long long ctas = (long long)g.N * g.C * tiles;
+    if (!grid_ok(ctas)) return -1;
+    CUtensorMap mx, mdy;
+    const uint64_t nc = (uint64_t)g.N * g.C;
+    if (!tma::encode4<T>(&mx, big, (uint64_t)g.Wb, (uint64_t)g.Hb, (uint64_t)g.Db, nc, (uint32_t)L::pitch(pg.TWo),
+                         (uint32_t)L::rows(pg.THo)))
+      return -1;
+    if (!tma::encode4<T>(&mdy, small, (uint64_t)g.Ws, (uint64_t)g.Hs, (uint64_t)g.Ds, nc, (uint32_t)pg.TWo,
+                         (uint32_t)pg.THo))
+      return -1;
+    const size_t smem = DwS2PkWLayout<T>::smem(pg);
+    const int threads = (pg.lw * pg.THo + 31) / 32 * 32;
+    auto kern = dw_s2_wgrad_pk_kernel<T>;
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && smem > configured) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      configured = smem;
+    }
+    kern<<<(unsigned)ctas, threads, smem, s>>>(mx, mdy, part, pg);
+    const int st = record_launch();
+    if (st != MEDNEXT_OK) return st;
+    return finish_wgrad<T>(part, dw, db, g.N, g.C, tiles, K * K * K, s);
   }
 }
 
@@ -128,6 +178,10 @@ int launch_s2_wgrad(const void* big, const void* small, void* dw, void* db, void
   using Acc = typename Elem<T>::Acc;
   const S2WPlan p = plan_s2w(g.N, g.C, g.Ds, K);
   Acc* part = static_cast<Acc*>(ws);
+  if constexpr (std::is_same<Acc, float>::value) {
+    const int pst = try_s2_wgrad_pk<T, K>(big, small, dw, db, part, g, bias_from_big, s);
+    if (pst != -1) return pst;
+  }
   const long long ctas = (long long)g.N * g.C * p.chunks;
   if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
   const unsigned grid = (unsigned)ctas;

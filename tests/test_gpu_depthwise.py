@@ -231,6 +231,26 @@ def test_stride2_forward_tma_kernel_is_bit_exact_with_fp32_kernel(dtype, shape):
     assert nat.device_error() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", DOWN_SHAPES)
+def test_stride2_weight_grad_tma_kernel_matches_fp32_kernel(dtype, shape):
+    """The down block's weight grad (k = 3, 16-bit) runs on the TMA plane ring with
+    packed FMAs; it sums in its own fixed order, so it matches the fp32 kernel on
+    the same inputs to the output's rounding (one 16-bit ulp), and repeats exactly."""
+    seed = seed_of("down-wgrad", str(dtype), shape)
+    x = rand(shape, dtype, seed).cuda()
+    small = (shape[0], shape[1], *((s + 1) // 2 for s in shape[2:]))
+    dy = rand(small, dtype, seed + 1).cuda()
+    dw, db = dwk.s2_wgrad(x, dy, 3)
+    dw32, db32 = dwk.s2_wgrad(x.float(), dy.float(), 3)
+    for got, want in ((dw, dw32), (db, db32)):
+        scale = want.abs().max().item()
+        torch.testing.assert_close(got.float(), want, rtol=2.0**-7, atol=1e-4 * scale)
+    dw2, db2 = dwk.s2_wgrad(x, dy, 3)
+    assert torch.equal(dw, dw2) and torch.equal(db, db2)
+    assert nat.device_error() == 0
+
+
 def test_dgrad_with_addend_adds_residual():
     x = rand((1, 4, 8, 16, 16), torch.bfloat16, 8).cuda()
     w = rand((4, 1, 3, 3, 3), torch.bfloat16, 9).cuda()
