@@ -456,4 +456,257 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
   }
 }
 
+// ----------------------------------------------------------------------------
+// Stride-2 scatter of the down block's input grad (k = 3, 16-bit types):
+//   big[2q + e] = bias + sum over a of small[q + a] * w[tap(e, a)]   (per axis;
+//   e = 0: a = 0, tap 1; e = 1: a = 0, tap 2, then a = 1, tap 0)
+// plus add_even at the all-even positions.  A CTA owns a tile of TWs x THs
+// small-grid positions (2*TWs x 2*THs big outputs per plane) and a chunk of big
+// plane pairs; the small plane tiles (THs + 1 rows, TWs + 8 columns) stream
+// through the TMA ring.  Small plane q finishes big plane 2q (tap kd = 1), gives
+// big plane 2q + 1 its first half (kd = 2) and big plane 2q - 1 its second half
+// (kd = 0).  Each thread owns 8 small positions of one row, i.e. 16 big columns
+// of 2 big rows, with pairs (i, i+4) of small positions; every output sums bias
+// first, then its taps in (a_d, a_h, a_w) order and the addend last: the order
+// of dw_s2_scatter_kernel, whose results this kernel reproduces bit for bit.
+// ----------------------------------------------------------------------------
+struct DwS2ScGeom {
+  DwS2Geom g;
+  int TWs, THs, TDq;  // small-grid tile (columns, rows) and big plane pairs per CTA
+  int tilesW, tilesH, tilesD;
+  int lw;             // threads along W (8 small columns each)
+};
+
+template <typename T>
+struct DwS2ScLayout {
+  static __host__ __device__ int pitch(int TWs) { return TWs + 8; }
+  static __host__ __device__ int rows(int THs) { return THs + 1; }
+  static __host__ __device__ size_t tile(const DwS2ScGeom& p) { return (size_t)rows(p.THs) * pitch(p.TWs) * sizeof(T); }
+  static __host__ __device__ size_t slot(const DwS2ScGeom& p) { return DwTmaLayout<T>::align128(tile(p)); }
+  static __host__ size_t smem(const DwS2ScGeom& p) { return 128 + kDwSlots * slot(p); }
+};
+
+// q[m] = (s[m], s[m+4]), m = 0..4, for the 9 small values s[0..8] of one row
+// starting at the thread's first column; s[8] comes from the right neighbour
+// (lane src_r), or from the tile's last column at the tile edge.
+template <typename T>
+__device__ __forceinline__ void dw_s2sc_window(const T* __restrict__ rowp, int col, int tws, bool right_edge,
+                                               int src_r, uint64_t (&q)[5]) {
+  const uint4 c = *reinterpret_cast<const uint4*>(rowp + col);     // s[0..7]
+  const uint32_t from_r = __shfl_sync(0xffffffffu, c.x, src_r);    // (s[0], s[1]) of the right neighbour
+  const uint32_t er = reinterpret_cast<const unsigned short*>(rowp)[tws];
+  const uint32_t s8 = right_edge ? er : (from_r & 0xffffu);
+  q[0] = pk_pair(lo_bits<T>(c.x), lo_bits<T>(c.z));
+  q[1] = pk_pair(hi_bits<T>(c.x), hi_bits<T>(c.z));
+  q[2] = pk_pair(lo_bits<T>(c.y), lo_bits<T>(c.w));
+  q[3] = pk_pair(hi_bits<T>(c.y), hi_bits<T>(c.w));
+  q[4] = pk_pair(lo_bits<T>(c.z), lo_bits<T>(s8));
+}
+
+// big-grid parity e and small offset a along one axis -> tap, or -1 (k = 3)
+__host__ __device__ constexpr int s2sc_tap(int e, int a) { return e == 0 ? (a == 0 ? 1 : -1) : (a == 0 ? 2 : 0); }
+
+template <typename T, bool ADD>
+__global__ void __launch_bounds__(kS2PkThreads, 2)
+    dw_s2_scatter_pk_kernel(const __grid_constant__ CUtensorMap mS, const T* __restrict__ wgt,
+                            const T* __restrict__ bias, const T* __restrict__ add_even, T* __restrict__ big,
+                            DwS2ScGeom pg) {
+  constexpr int K = 3;
+  constexpr int K3 = 27;
+  using L = DwS2ScLayout<T>;
+  const DwS2Geom& g = pg.g;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ DwPkRing ring;
+  unsigned char* slots = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  const size_t slot_bytes = L::slot(pg);
+  const uint32_t tile_bytes = (uint32_t)L::tile(pg);
+  const int rsp = L::pitch(pg.TWs);
+  const int nwarps = (int)blockDim.x >> 5;
+
+  int bx = blockIdx.x;
+  const int tw = bx % pg.tilesW;
+  bx /= pg.tilesW;
+  const int th = bx % pg.tilesH;
+  bx /= pg.tilesH;
+  const int td = bx % pg.tilesD;
+  const int nc = bx / pg.tilesD;
+  const int c = nc % g.C;
+  const int qw0 = tw * pg.TWs, qh0 = th * pg.THs, qd0 = td * pg.TDq;
+  const int QD = (g.Db + 1) >> 1;
+  const int dcount = min(pg.TDq, QD - qd0);
+  const int nsteps = dcount + 1;
+
+  auto issue = [&](int q) {
+    const int slot = q % kDwSlots;
+    mbar_arrive_expect_tx(&ring.full[slot], tile_bytes);
+    tma_load_4d(slots + (size_t)slot * slot_bytes, &mS, &ring.full[slot], qw0, qh0, qd0 + q, nc);
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDwSlots; ++i) {
+      mbar_init(&ring.full[i], 1);
+      ring.released[i] = 0;
+    }
+    ring.abort = 0;
+    fence_mbarrier_init();
+    tma_prefetch_map(&mS);
+    const int first = min(nsteps, kDwSlots);
+    for (int q = 0; q < first; ++q) issue(q);
+    ring.issued = first;
+  }
+  __syncthreads();
+  volatile int* abort = &ring.abort;
+
+  const int lane = threadIdx.x & 31;
+  const int lw = pg.lw;
+  const int wt = threadIdx.x % lw;
+  const int r = threadIdx.x / lw;
+  const bool active = r < pg.THs;
+  const int qh = qh0 + r;
+  const int qw = qw0 + 8 * wt;
+  // Ws is a multiple of 8 and Wb = 2 Ws on this path: a thread's 16 big columns are in or out together
+  const bool cols_ok = active && qw < g.Ws;
+  const bool row0_ok = cols_ok && 2 * qh < g.Hb, row1_ok = cols_ok && 2 * qh + 1 < g.Hb;
+  // a row of lw <= 8 threads lies within one warp: the right neighbour is lane + 1
+  const int src_r = wt < lw - 1 ? lane + 1 : lane;
+  const bool right_edge = wt == lw - 1;
+  // lanes past the tile read row 0 (every lane joins the shuffles) and store nothing
+  const int sbase = (active ? r : 0) * rsp;
+  const int col = 8 * wt;
+  uint64_t wp[K3];
+#pragma unroll
+  for (int t = 0; t < K3; ++t) {
+    const uint32_t wv = __float_as_uint(to_acc<T>(__ldg(wgt + (size_t)c * K3 + t)));
+    wp[t] = pk_pair(wv, wv);
+  }
+  const uint32_t bvb = __float_as_uint(bias != nullptr ? to_acc<T>(bias[c]) : 0.f);
+  const uint64_t bv2 = pk_pair(bvb, bvb);
+  const size_t bplane = (size_t)g.Hb * g.Wb;
+  T* out0 = big + (size_t)nc * (size_t)g.bp + (size_t)(2 * qh) * g.Wb + 2 * qw;
+  const T* add0 = ADD ? add_even + (size_t)nc * g.Ds * ((size_t)g.Hs * g.Ws) + (size_t)qh * g.Ws + qw : nullptr;
+
+  // the odd big plane 2q + 1 between its two halves: [eh][ew][pair]
+  uint64_t odd[2][2][4];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int b2 = 0; b2 < 2; ++b2)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) odd[a][b2][i] = 0ull;
+
+  // acc[ew][i] += taps of plane tap td (and small offset a_d) for big row parity eh
+  auto add_taps = [&](const int td, const int eh, uint64_t (&acc)[2][4], const uint64_t (&q0)[5],
+                      const uint64_t (&q1)[5]) {
+#pragma unroll
+    for (int ah = 0; ah < 2; ++ah) {
+      const int th2 = s2sc_tap(eh, ah);
+      if (th2 < 0) continue;
+#pragma unroll
+      for (int ew = 0; ew < 2; ++ew) {
+#pragma unroll
+        for (int aw = 0; aw < 2; ++aw) {
+          const int tw2 = s2sc_tap(ew, aw);
+          if (tw2 < 0) continue;
+          const uint64_t wv = wp[(td * K + th2) * K + tw2];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[ew][i] = pk_fma(ah == 0 ? q0[i + aw] : q1[i + aw], wv, acc[ew][i]);
+        }
+      }
+    }
+  };
+  // 16 big columns of one row: column 2i + ew is pair (i % 4) of acc[ew], low half for i < 4
+  auto store_row = [&](T* dst, const uint64_t (&acc)[2][4]) {
+    float lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      pk_split(acc[0][i], lo[2 * i], hi[2 * i]);
+      pk_split(acc[1][i], lo[2 * i + 1], hi[2 * i + 1]);
+    }
+    reinterpret_cast<uint4*>(dst)[0] = pack16<T>(lo);
+    reinterpret_cast<uint4*>(dst)[1] = pack16<T>(hi);
+  };
+
+  auto step = [&](const int s) -> bool {
+    const int slot = s % kDwSlots;
+    const bool ok = !*abort && mbar_wait(&ring.full[slot], (uint32_t)((s / kDwSlots) & 1));
+    if (!__all_sync(0xffffffffu, ok)) {
+      *abort = 1;
+      return false;
+    }
+    const T* sp = reinterpret_cast<const T*>(slots + (size_t)slot * slot_bytes) + sbase;
+    uint64_t q0[5], q1[5];
+    dw_s2sc_window<T>(sp, col, pg.TWs, right_edge, src_r, q0);
+    dw_s2sc_window<T>(sp + rsp, col, pg.TWs, right_edge, src_r, q1);
+    const int qd = qd0 + s;  // small plane of this step
+    // big plane 2qd - 1: its second half (a_d = 1, tap 0), then store
+    if (s >= 1 && 2 * qd - 1 < g.Db) {
+#pragma unroll
+      for (int eh = 0; eh < 2; ++eh) {
+        add_taps(0, eh, odd[eh], q0, q1);
+        if (eh == 0 ? row0_ok : row1_ok) store_row(out0 + (size_t)(2 * qd - 1) * bplane + (size_t)eh * g.Wb, odd[eh]);
+      }
+    }
+    if (s < dcount) {
+      // big plane 2qd (a_d = 0, tap 1): complete here
+#pragma unroll
+      for (int eh = 0; eh < 2; ++eh) {
+        uint64_t acc[2][4];
+#pragma unroll
+        for (int ew = 0; ew < 2; ++ew)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[ew][i] = bv2;
+        add_taps(1, eh, acc, q0, q1);
+        if constexpr (ADD) {
+          if (eh == 0 && cols_ok && qh < g.Hs) {
+            float al[8];
+            unpack16<T>(__ldg(reinterpret_cast<const uint4*>(add0 + (size_t)qd * ((size_t)g.Hs * g.Ws))), al);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[0][i] = pk_add(acc[0][i], pk_pair(__float_as_uint(al[i]), __float_as_uint(al[i + 4])));
+          }
+        }
+        if (2 * qd < g.Db && (eh == 0 ? row0_ok : row1_ok))
+          store_row(out0 + (size_t)(2 * qd) * bplane + (size_t)eh * g.Wb, acc);
+      }
+      // big plane 2qd + 1: bias and its first half (a_d = 0, tap 2)
+#pragma unroll
+      for (int eh = 0; eh < 2; ++eh) {
+#pragma unroll
+        for (int ew = 0; ew < 2; ++ew)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) odd[eh][ew][i] = bv2;
+        add_taps(2, eh, odd[eh], q0, q1);
+      }
+    }
+    // release the slot; the warp that releases it last loads the slot's next plane
+    __syncwarp();
+    if (lane == 0) {
+      int prv;
+      asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], 1;"
+                   : "=r"(prv)
+                   : "r"(smem_u32(&ring.released[slot]))
+                   : "memory");
+      // the count only grows: the slot's (s / kDwSlots)-th plane is released by nwarps arrivals
+      if (prv == (s / kDwSlots + 1) * nwarps - 1) {
+        const int q = s + kDwSlots;
+        if (q < nsteps) {
+          fence_async_smem();
+          issue(q);
+          atomicAdd(&ring.issued, 1);
+        }
+      }
+    }
+    return true;
+  };
+  for (int s = 0; s < nsteps; ++s)
+    if (!step(s)) break;
+
+  __syncthreads();
+  // after an abort, wait (bounded) for the loads still in flight before the CTA exits
+  if (*abort && threadIdx.x == 0) {
+    const int issued = ring.issued;
+    for (int q = issued > kDwSlots ? issued - kDwSlots : 0; q < issued; ++q)
+      mbar_wait(&ring.full[q % kDwSlots], (uint32_t)((q / kDwSlots) & 1));
+    raise_device_error(kErrMbarTimeout);
+  }
+}
+
 }  // namespace mednext

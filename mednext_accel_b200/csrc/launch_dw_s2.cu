@@ -141,9 +141,59 @@ int launch_gather(const void* big, const void* w, const void* b, const void* add
                                                 static_cast<T*>(small), g);
   return record_launch();
 }
+// Down-block input grad (k = 3, 16-bit types) on the TMA ring: the same grid
+// conditions as the gather, plus a 16-byte aligned add_even.
+template <typename T, int K>
+int try_scatter_pk(const void* small, const void* w, const void* b, const void* add_even, void* big,
+                   const DwS2Geom& g, cudaStream_t s) {
+  if constexpr (K != 3 || !(std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value)) {
+    return -1;
+  } else {
+    if (!s2pk_geom_ok(g, big, small) || (reinterpret_cast<uintptr_t>(add_even) & 15) != 0) return -1;
+    using L = DwS2ScLayout<T>;
+    DwS2ScGeom pg{};
+    pg.g = g;
+    pg.TWs = std::min(64, g.Ws);
+    pg.lw = pg.TWs / 8;
+    pg.THs = std::min(std::min(kS2PkThreads / pg.lw, g.Hs), 255);
+    pg.tilesW = (g.Ws + pg.TWs - 1) / pg.TWs;
+    pg.tilesH = (g.Hs + pg.THs - 1) / pg.THs;
+    const int QD = (g.Db + 1) / 2;
+    const long long base = (long long)g.N * g.C * pg.tilesW * pg.tilesH;
+    const long long slots = 148 * 2;
+    long long best_cost = -1;
+    pg.TDq = QD;
+    for (long long cand = 1; cand <= std::max(1, QD / 2); ++cand) {
+      const long long td = (QD + cand - 1) / cand;
+      const long long tiles_d = (QD + td - 1) / td;
+      const long long cost = ((base * tiles_d + slots - 1) / slots) * (td + 1);
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        pg.TDq = (int)td;
+      }
+    }
+    pg.tilesD = (QD + pg.TDq - 1) / pg.TDq;
+    const long long ctas = base * pg.tilesD;
+    if (!grid_ok(ctas)) return -1;
+    CUtensorMap m;
+    if (!tma::encode4<T>(&m, small, (uint64_t)g.Ws, (uint64_t)g.Hs, (uint64_t)g.Ds, (uint64_t)g.N * g.C,
+                         (uint32_t)L::pitch(pg.TWs), (uint32_t)L::rows(pg.THs)))
+      return -1;
+    const size_t smem = L::smem(pg);
+    const int threads = (pg.lw * pg.THs + 31) / 32 * 32;
+    auto kern = add_even != nullptr ? dw_s2_scatter_pk_kernel<T, true> : dw_s2_scatter_pk_kernel<T, false>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<(unsigned)ctas, threads, smem, s>>>(m, static_cast<const T*>(w), static_cast<const T*>(b),
+                                               static_cast<const T*>(add_even), static_cast<T*>(big), pg);
+    return record_launch();
+  }
+}
+
 template <typename T, int K>
 int launch_scatter(const void* small, const void* w, const void* b, const void* add_even, void* big,
                    const DwS2Geom& g, cudaStream_t s) {
+  const int pst = try_scatter_pk<T, K>(small, w, b, add_even, big, g, s);
+  if (pst != -1) return pst;
   const long long ctas = (long long)g.N * g.C * ((g.Db + 1) / 2);
   if (!grid_ok(ctas)) return MEDNEXT_ERR_BAD_SHAPE;
   auto kern = add_even != nullptr ? dw_s2_scatter_kernel<T, K, true> : dw_s2_scatter_kernel<T, K, false>;

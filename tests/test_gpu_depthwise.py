@@ -251,6 +251,26 @@ def test_stride2_weight_grad_tma_kernel_matches_fp32_kernel(dtype, shape):
     assert nat.device_error() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", DOWN_SHAPES)
+def test_stride2_input_grad_tma_kernel_is_bit_exact_with_fp32_kernel(dtype, shape):
+    """The down block's input grad (k = 3, 16-bit) scatters small-grid planes from the
+    TMA ring with packed FMAs, summing bias, taps in (a_d, a_h, a_w) order and the
+    even-position addend last, as the fp32 scatter does: equal after one rounding."""
+    seed = seed_of("down-dgrad", str(dtype), shape)
+    small = (shape[0], shape[1], *((s + 1) // 2 for s in shape[2:]))
+    dy = rand(small, dtype, seed).cuda()
+    w = rand((shape[1], 1, 3, 3, 3), dtype, seed + 1, scale=0.2).cuda()
+    a = rand(small, dtype, seed + 2).cuda()
+    spatial = tuple(shape[2:])
+    for addend in (None, a):
+        dx = dwk.s2_dgrad(dy, w, spatial, 3, addend_even=addend)
+        want = dwk.s2_dgrad(dy.float(), w.float(), spatial, 3,
+                            addend_even=None if addend is None else addend.float())
+        assert torch.equal(dx, want.to(dtype))
+    assert nat.device_error() == 0
+
+
 def test_dgrad_with_addend_adds_residual():
     x = rand((1, 4, 8, 16, 16), torch.bfloat16, 8).cuda()
     w = rand((4, 1, 3, 3, 3), torch.bfloat16, 9).cuda()
