@@ -119,6 +119,13 @@ size_t mednext_dw_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t 
 int mednext_dw_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
                      size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h,
                      int64_t w, int k, int dtype, mednext_stream_t stream);
+/* The same weight grad with dweight / dbias written as fp32 (dtype bf16, fp16 or fp32):
+ * the values mednext_dw_wgrad writes in dtype, widened, i.e. what casting its output to
+ * fp32 gives (an autocast gradient reaching an fp32 parameter), without the cast. */
+int mednext_dw_wgrad_f32out(const void* x, const void* dy, void* dweight, void* dbias,
+                            void* workspace, size_t workspace_bytes, int64_t n, int64_t c,
+                            int64_t d, int64_t h, int64_t w, int k, int dtype,
+                            mednext_stream_t stream);
 
 /* Same result as mednext_dw_wgrad, but the caller passes no workspace and the
  * call allocates no device memory.  No reference counterpart: the reference
@@ -167,6 +174,11 @@ size_t mednext_dw_s2_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64
 int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbias,
                         void* workspace, size_t workspace_bytes, int64_t n, int64_t c, int64_t d,
                         int64_t h, int64_t w, int k, int dtype, mednext_stream_t stream);
+/* mednext_dw_s2_wgrad with fp32 dweight / dbias (see mednext_dw_wgrad_f32out). */
+int mednext_dw_s2_wgrad_f32out(const void* x, const void* dy, void* dweight, void* dbias,
+                               void* workspace, size_t workspace_bytes, int64_t n, int64_t c,
+                               int64_t d, int64_t h, int64_t w, int k, int dtype,
+                               mednext_stream_t stream);
 
 /* ------- depthwise ConvTranspose3d, stride 2, padding k/2 (up block) ------
  * (d, h, w) are the INPUT sizes; the output is (2d-1, 2h-1, 2w-1).
@@ -207,6 +219,11 @@ size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t
 int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
                       size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h,
                       int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream);
+/* mednext_dwT_wgrad with fp32 dweight / dbias (see mednext_dw_wgrad_f32out). */
+int mednext_dwT_wgrad_f32out(const void* x, const void* dy, void* dweight, void* dbias,
+                             void* workspace, size_t workspace_bytes, int64_t n, int64_t c,
+                             int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype,
+                             mednext_stream_t stream);
 
 /* ---------------- GroupNorm with groups == channels ----------------------
  * x: [n, c, spatial]; stats: float [n*c][2] = (mean, rstd).  gamma/beta: [c]

@@ -67,11 +67,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mednext_dw_dgrad": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_wgrad_workspace_size": (_SZ, _DIMS5 + [_INT, _INT]),
     "mednext_dw_wgrad": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_INT, _INT, _P]),
+    "mednext_dw_wgrad_f32out": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_wgrad_noalloc": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_s2_fwd": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_s2_dgrad": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_s2_wgrad_workspace_size": (_SZ, _DIMS5 + [_INT, _INT]),
     "mednext_dw_s2_wgrad": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_INT, _INT, _P]),
+    "mednext_dw_s2_wgrad_f32out": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dwT_fwd": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_dwT_dgrad": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_upsample2_fill": (_INT, [_P, _P, _P] + _DIMS5 + [_I64, _INT, _P]),
@@ -79,6 +81,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mednext_unpad_front": (_INT, [_P, _P] + _DIMS5 + [_I64, _INT, _P]),
     "mednext_dwT_wgrad_workspace_size": (_SZ, _DIMS5 + [_INT, _INT]),
     "mednext_dwT_wgrad": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_I64, _INT, _INT, _P]),
+    "mednext_dwT_wgrad_f32out": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_gn_stats_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "mednext_gn_stats": (_INT, [_P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _F, _INT, _P]),
     "mednext_gn_fwd": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _INT, _INT, _INT, _P]),

@@ -328,15 +328,18 @@ def mednext_block_backward(
             drw = drw_t.t()
             drb = dpb.clone()
             dxr, _ = pw_gemm(dye, prm.rw, cin, out_dtype=cdt)
+    # the depthwise weight grad straight in the parameter's dtype where the kernels offer it
+    # (fp32 parameters, 16-bit compute: the same values as a cast of the compute-dtype grad)
+    wdt = dw_w.dtype if dw_w.dtype in (xb.dtype, torch.float32) else None
     if kind == KIND_REGULAR:
         dx = dwk.dw_dgrad(dt, wdw, kernel_size, addend=dyb if residual_is_input and dy.dtype == cdt else None)
-        dwdw, dbdw = dwk.dw_wgrad(xb, dt, kernel_size)
+        dwdw, dbdw = dwk.dw_wgrad(xb, dt, kernel_size, out_dtype=wdt)
     elif kind == KIND_DOWN:
         dx = dwk.s2_dgrad(dt, wdw, tuple(int(s) for s in x.shape[2:]), kernel_size, addend_even=dxr)
-        dwdw, dbdw = dwk.s2_wgrad(xb, dt, kernel_size)
+        dwdw, dbdw = dwk.s2_wgrad(xb, dt, kernel_size, out_dtype=wdt)
     else:
         dx = dwk.t_dgrad(dt, wdw, kernel_size, small=tuple(int(s) for s in x.shape[2:]), addend=dxr)
-        dwdw, dbdw = dwk.t_wgrad(xb, dt, kernel_size)
+        dwdw, dbdw = dwk.t_wgrad(xb, dt, kernel_size, out_dtype=wdt)
     if dx.dtype != x.dtype:
         dx = dx.to(x.dtype)
         if residual_is_input:

@@ -162,19 +162,38 @@ size_t mednext_dw_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t 
   return s1_wgrad_ws(n, c, d, h, w, k, dtype);
 }
 
-int mednext_dw_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
-                     size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
-                     mednext_stream_t stream) {
+namespace {
+// out_f32: dweight / dbias are fp32 (16-bit dtypes: the dtype-rounded sums, widened)
+bool f32_out_ok(int dtype) { return dtype == MEDNEXT_BFLOAT16 || dtype == MEDNEXT_FLOAT16 || dtype == MEDNEXT_FLOAT32; }
+
+int dw_wgrad_impl(const void* x, const void* dy, void* dweight, void* dbias, void* workspace, size_t workspace_bytes,
+                  int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype, bool out_f32,
+                  mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
+  if (out_f32 && !f32_out_ok(dtype)) return MEDNEXT_ERR_BAD_DTYPE;
   if (x == nullptr || dy == nullptr || dweight == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
-  if (!aligned16(x) || !aligned16(dy) || !aligned(dweight, esz) || (dbias && !aligned(dbias, esz)))
+  const size_t osz = out_f32 ? 4 : esz;
+  if (!aligned16(x) || !aligned16(dy) || !aligned(dweight, osz) || (dbias && !aligned(dbias, osz)))
     return MEDNEXT_ERR_ALIGNMENT;
   if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < s1_wgrad_ws(n, c, d, h, w, k, dtype))
     return MEDNEXT_ERR_WORKSPACE;
   const S1Plan p = plan_s1(n, c, d, h, w, k, esz, true);
-  return dispatch_dw_s1_wgrad(dtype, k, x, dy, dweight, dbias, workspace, p, as_stream(stream));
+  return dispatch_dw_s1_wgrad(dtype, k, x, dy, dweight, dbias, workspace, p, out_f32, as_stream(stream));
+}
+}  // namespace
+
+int mednext_dw_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                     size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
+                     mednext_stream_t stream) {
+  return dw_wgrad_impl(x, dy, dweight, dbias, workspace, workspace_bytes, n, c, d, h, w, k, dtype, false, stream);
+}
+
+int mednext_dw_wgrad_f32out(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                            size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
+                            int dtype, mednext_stream_t stream) {
+  return dw_wgrad_impl(x, dy, dweight, dbias, workspace, workspace_bytes, n, c, d, h, w, k, dtype, true, stream);
 }
 
 // ------------------------------ depthwise stride 2 ------------------------------
@@ -208,20 +227,36 @@ size_t mednext_dw_s2_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64
   return s2_wgrad_ws(n, c, g.Ds, k, dtype);
 }
 
-int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
-                        size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
-                        int dtype, mednext_stream_t stream) {
+namespace {
+int dw_s2_wgrad_impl(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                     size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype,
+                     bool out_f32, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
+  if (out_f32 && !f32_out_ok(dtype)) return MEDNEXT_ERR_BAD_DTYPE;
   if (x == nullptr || dy == nullptr || dweight == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
-  if (!aligned(x, esz) || !aligned(dy, esz) || !aligned(dweight, esz) || (dbias && !aligned(dbias, esz)))
+  const size_t osz = out_f32 ? 4 : esz;
+  if (!aligned(x, esz) || !aligned(dy, esz) || !aligned(dweight, osz) || (dbias && !aligned(dbias, osz)))
     return MEDNEXT_ERR_ALIGNMENT;
   if (workspace == nullptr || !aligned16(workspace) ||
       workspace_bytes < mednext_dw_s2_wgrad_workspace_size(n, c, d, h, w, k, dtype))
     return MEDNEXT_ERR_WORKSPACE;
   return dispatch_dw_s2_wgrad(dtype, k, x, dy, dweight, dbias, workspace, s2_geom_down(n, c, d, h, w), false,
-                              as_stream(stream));
+                              out_f32, as_stream(stream));
+}
+}  // namespace
+
+int mednext_dw_s2_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                        size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
+                        int dtype, mednext_stream_t stream) {
+  return dw_s2_wgrad_impl(x, dy, dweight, dbias, workspace, workspace_bytes, n, c, d, h, w, k, dtype, false, stream);
+}
+
+int mednext_dw_s2_wgrad_f32out(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                               size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k,
+                               int dtype, mednext_stream_t stream) {
+  return dw_s2_wgrad_impl(x, dy, dweight, dbias, workspace, workspace_bytes, n, c, d, h, w, k, dtype, true, stream);
 }
 
 // ------------------------------ depthwise transpose ------------------------------
@@ -297,22 +332,40 @@ size_t mednext_dwT_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t
   return s2_wgrad_ws(n, c, d, k, dtype);
 }
 
-int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
-                      size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
-                      int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
+namespace {
+int dwT_wgrad_impl(const void* x, const void* dy, void* dweight, void* dbias, void* workspace, size_t workspace_bytes,
+                   int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype,
+                   bool out_f32, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
+  if (out_f32 && !f32_out_ok(dtype)) return MEDNEXT_ERR_BAD_DTYPE;
   if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
   if (x == nullptr || dy == nullptr || dweight == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
-  if (!aligned(x, esz) || !aligned(dy, esz) || !aligned(dweight, esz) || (dbias && !aligned(dbias, esz)))
+  const size_t osz = out_f32 ? 4 : esz;
+  if (!aligned(x, esz) || !aligned(dy, esz) || !aligned(dweight, osz) || (dbias && !aligned(dbias, osz)))
     return MEDNEXT_ERR_ALIGNMENT;
   if (workspace == nullptr || !aligned16(workspace) ||
       workspace_bytes < mednext_dwT_wgrad_workspace_size(n, c, d, h, w, k, dtype))
     return MEDNEXT_ERR_WORKSPACE;
   // big grid = dy (2S-1), small grid = x (S); the bias grad sums dy (big)
   return dispatch_dw_s2_wgrad(dtype, k, dy, x, dweight, dbias, workspace, s2_geom_up(n, c, d, h, w, big_pitch),
-                              true, as_stream(stream));
+                              true, out_f32, as_stream(stream));
+}
+}  // namespace
+
+int mednext_dwT_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                      size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                      int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
+  return dwT_wgrad_impl(x, dy, dweight, dbias, workspace, workspace_bytes, n, c, d, h, w, big_pitch, k, dtype, false,
+                        stream);
+}
+
+int mednext_dwT_wgrad_f32out(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,
+                             size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                             int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
+  return dwT_wgrad_impl(x, dy, dweight, dbias, workspace, workspace_bytes, n, c, d, h, w, big_pitch, k, dtype, true,
+                        stream);
 }
 
 // ------------------------------ GroupNorm ------------------------------

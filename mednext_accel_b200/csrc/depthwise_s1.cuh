@@ -14,6 +14,8 @@
 // 191-202 issues k^3 masked loads per output).
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace mednext {
@@ -587,9 +589,9 @@ __global__ void __launch_bounds__(448) dw_s1_wgrad_grouped_kernel(
 
 // Deterministic second pass: dw[c,t] = sum over (n, tile) of the partials, in
 // a fixed order; dbias[c] from tap index K^3.
-template <typename T>
+template <typename T, typename O = T>
 __global__ void dw_wgrad_finish_kernel(const typename Elem<T>::Acc* __restrict__ part,
-                                       T* __restrict__ dw, T* __restrict__ db, int N, int C,
+                                       O* __restrict__ dw, O* __restrict__ db, int N, int C,
                                        int tiles, int K3) {
   using Acc = typename Elem<T>::Acc;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -601,8 +603,16 @@ __global__ void dw_wgrad_finish_kernel(const typename Elem<T>::Acc* __restrict__
     const Acc* p = part + ((size_t)(n * C + c) * tiles) * (K3 + 1) + t;
     for (int i = 0; i < tiles; ++i) s += p[(size_t)i * (K3 + 1)];
   }
-  if (t < K3) dw[(size_t)c * K3 + t] = from_acc<T>(s);
-  else if (db != nullptr) db[c] = from_acc<T>(s);
+  // O = float for 16-bit T: the T-rounded value, widened (what a T gradient cast to fp32 holds)
+  const T v = from_acc<T>(s);
+  O o;
+  if constexpr (std::is_same<O, T>::value) {
+    o = v;
+  } else {
+    o = static_cast<O>(to_acc<T>(v));
+  }
+  if (t < K3) dw[(size_t)c * K3 + t] = o;
+  else if (db != nullptr) db[c] = o;
 }
 
 }  // namespace mednext

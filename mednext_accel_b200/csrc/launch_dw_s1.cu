@@ -112,10 +112,20 @@ int launch_s1_conv(const void* x, const void* wgt, const void* bias, const void*
   return record_launch();
 }
 
+// f32: write dW and dbias as fp32 (16-bit types only; the T-rounded values)
 template <typename T>
-int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, int C, int tiles, int K3,
+int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, int C, int tiles, int K3, bool f32,
                  cudaStream_t s) {
   const int total = C * (K3 + 1);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value) {
+    if (f32) {
+      dw_wgrad_finish_kernel<T, float><<<(total + 127) / 128, 128, 0, s>>>(
+          part, static_cast<float*>(dw), static_cast<float*>(db), N, C, tiles, K3);
+      return record_launch();
+    }
+  } else {
+    if (f32 && !std::is_same<T, float>::value) return MEDNEXT_ERR_BAD_DTYPE;
+  }
   dw_wgrad_finish_kernel<T><<<(total + 127) / 128, 128, 0, s>>>(part, static_cast<T*>(dw), static_cast<T*>(db), N,
                                                                 C, tiles, K3);
   return record_launch();
@@ -150,12 +160,13 @@ int try_s1_wgrad_tma(const void* x, const void* dy, typename Elem<T>::Acc* part,
 }
 
 template <typename T, int K>
-int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws, const S1Plan& p, cudaStream_t s) {
+int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws, const S1Plan& p, bool f32,
+                    cudaStream_t s) {
   using Acc = typename Elem<T>::Acc;
   constexpr int NH = K <= 3 ? 2 : 1;
   Acc* part = static_cast<Acc*>(ws);
   const int tst = try_s1_wgrad_tma<T, K>(x, dy, part, p, s);
-  if (tst == MEDNEXT_OK) return finish_wgrad<T>(part, dw, db, p.g.N, p.g.C, (int)s1_tiles(p), K * K * K, s);
+  if (tst == MEDNEXT_OK) return finish_wgrad<T>(part, dw, db, p.g.N, p.g.C, (int)s1_tiles(p), K * K * K, f32, s);
   if (tst != -1) return tst;
   if constexpr (K <= 3) {
     auto kern = dw_s1_wgrad_kernel<T, K, NH>;
@@ -176,7 +187,7 @@ int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws,
   }
   const int st = record_launch();
   if (st != MEDNEXT_OK) return st;
-  return finish_wgrad<T>(part, dw, db, p.g.N, p.g.C, (int)s1_tiles(p), K * K * K, s);
+  return finish_wgrad<T>(part, dw, db, p.g.N, p.g.C, (int)s1_tiles(p), K * K * K, f32, s);
 }
 
 }  // namespace
@@ -205,9 +216,9 @@ int dispatch_dw_s1_conv(int dtype, int k, const void* x, const void* w, const vo
   return st;
 }
 int dispatch_dw_s1_wgrad(int dtype, int k, const void* x, const void* dy, void* dw, void* db, void* ws,
-                         const S1Plan& p, cudaStream_t s) {
+                         const S1Plan& p, bool out_f32, cudaStream_t s) {
   int st = MEDNEXT_OK;
-  MEDNEXT_T_SWITCH(dtype, T, MEDNEXT_K_SWITCH(k, KC, st = (launch_s1_wgrad<T, KC>(x, dy, dw, db, ws, p, s))));
+  MEDNEXT_T_SWITCH(dtype, T, MEDNEXT_K_SWITCH(k, KC, st = (launch_s1_wgrad<T, KC>(x, dy, dw, db, ws, p, out_f32, s))));
   return st;
 }
 MEDNEXT_DEFINE_ERROR_READER(read_clear_errors_dw)

@@ -9,10 +9,20 @@
 namespace mednext {
 
 namespace {
+// f32: write dW and dbias as fp32 (16-bit types only; the T-rounded values)
 template <typename T>
-int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, int C, int tiles, int K3,
+int finish_wgrad(const typename Elem<T>::Acc* part, void* dw, void* db, int N, int C, int tiles, int K3, bool f32,
                  cudaStream_t s) {
   const int total = C * (K3 + 1);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value) {
+    if (f32) {
+      dw_wgrad_finish_kernel<T, float><<<(total + 127) / 128, 128, 0, s>>>(
+          part, static_cast<float*>(dw), static_cast<float*>(db), N, C, tiles, K3);
+      return record_launch();
+    }
+  } else {
+    if (f32 && !std::is_same<T, float>::value) return MEDNEXT_ERR_BAD_DTYPE;
+  }
   dw_wgrad_finish_kernel<T><<<(total + 127) / 128, 128, 0, s>>>(part, static_cast<T*>(dw), static_cast<T*>(db), N,
                                                                 C, tiles, K3);
   return record_launch();
@@ -94,7 +104,7 @@ int try_gather_pk(const void* big, const void* w, const void* b, const void* add
 // Ds per (n, c) that the workspace holds, summed by dw_wgrad_finish_kernel.
 template <typename T, int K>
 int try_s2_wgrad_pk(const void* big, const void* small, void* dw, void* db, float* part, const DwS2Geom& g,
-                    bool bias_from_big, cudaStream_t s) {
+                    bool bias_from_big, bool f32, cudaStream_t s) {
   if constexpr (K != 3 || !(std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value)) {
     return -1;
   } else {
@@ -124,7 +134,7 @@ int try_s2_wgrad_pk(const void* big, const void* small, void* dw, void* db, floa
     kern<<<(unsigned)ctas, threads, smem, s>>>(mx, mdy, part, pg);
     const int st = record_launch();
     if (st != MEDNEXT_OK) return st;
-    return finish_wgrad<T>(part, dw, db, g.N, g.C, tiles, K * K * K, s);
+    return finish_wgrad<T>(part, dw, db, g.N, g.C, tiles, K * K * K, f32, s);
   }
 }
 
@@ -224,12 +234,12 @@ int launch_pad_front(const void* v, const void* addend, void* out, const DwS2Geo
 }
 template <typename T, int K>
 int launch_s2_wgrad(const void* big, const void* small, void* dw, void* db, void* ws, const DwS2Geom& g,
-                    bool bias_from_big, cudaStream_t s) {
+                    bool bias_from_big, bool f32, cudaStream_t s) {
   using Acc = typename Elem<T>::Acc;
   const S2WPlan p = plan_s2w(g.N, g.C, g.Ds, K);
   Acc* part = static_cast<Acc*>(ws);
   if constexpr (std::is_same<Acc, float>::value) {
-    const int pst = try_s2_wgrad_pk<T, K>(big, small, dw, db, part, g, bias_from_big, s);
+    const int pst = try_s2_wgrad_pk<T, K>(big, small, dw, db, part, g, bias_from_big, f32, s);
     if (pst != -1) return pst;
   }
   const long long ctas = (long long)g.N * g.C * p.chunks;
@@ -246,7 +256,7 @@ int launch_s2_wgrad(const void* big, const void* small, void* dw, void* db, void
     st = record_launch();
     if (st != MEDNEXT_OK) return st;
   }
-  return finish_wgrad<T>(part, dw, db, g.N, g.C, p.chunks, K * K * K, s);
+  return finish_wgrad<T>(part, dw, db, g.N, g.C, p.chunks, K * K * K, f32, s);
 }
 
 }  // namespace
@@ -294,10 +304,11 @@ int dispatch_pad_front(int dtype, const void* v, const void* addend, void* out, 
   return st;
 }
 int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,
-                         const DwS2Geom& g, bool bias_from_big, cudaStream_t s) {
+                         const DwS2Geom& g, bool bias_from_big, bool out_f32, cudaStream_t s) {
   int st = MEDNEXT_OK;
   MEDNEXT_T_SWITCH(dtype, T,
-                   MEDNEXT_K_SWITCH(k, KC, st = (launch_s2_wgrad<T, KC>(big, small, dw, db, ws, g, bias_from_big, s))));
+                   MEDNEXT_K_SWITCH(k, KC, st = (launch_s2_wgrad<T, KC>(big, small, dw, db, ws, g, bias_from_big,
+                                                                        out_f32, s))));
   return st;
 }
 

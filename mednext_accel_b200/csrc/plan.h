@@ -176,7 +176,7 @@ inline PwWPlan plan_pw_wgrad(int64_t n, int64_t cin, int64_t cout, int64_t vox) 
 int dispatch_dw_s1_conv(int dtype, int k, const void* x, const void* w, const void* b, const void* addend, void* y,
                         GnPartial* stats, const S1Plan& p, int flip, cudaStream_t s);
 int dispatch_dw_s1_wgrad(int dtype, int k, const void* x, const void* dy, void* dw, void* db, void* ws,
-                         const S1Plan& p, cudaStream_t s);
+                         const S1Plan& p, bool out_f32, cudaStream_t s);
 int dispatch_upsample2_fill(int dtype, const void* small, const float* bias, void* big, const DwS2Geom& g,
                             cudaStream_t s);
 int dispatch_pad_front(int dtype, const void* v, const void* addend, void* out, const DwS2Geom& g, bool unpad,
@@ -188,7 +188,7 @@ int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, c
                            const void* add_even, void* big,
                            const DwS2Geom& g, cudaStream_t s);
 int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,
-                         const DwS2Geom& g, bool bias_from_big, cudaStream_t s);
+                         const DwS2Geom& g, bool bias_from_big, bool out_f32, cudaStream_t s);
 int dispatch_gn_finalize(const GnPartial* part, int tiles, int nc, float eps, float* stats, cudaStream_t s);
 int dispatch_gn_stats(int dtype, const void* x, GnPartial* part, int64_t nc, int64_t vol, int64_t pitch, int chunks,
                       float eps, float* stats, cudaStream_t s);

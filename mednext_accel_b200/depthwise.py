@@ -77,20 +77,33 @@ def dw_dgrad(grad: Tensor, weight: Tensor, kernel_size: int, addend: Tensor | No
     return out
 
 
-def dw_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True) -> tuple[Tensor, Tensor | None]:
+def _wgrad_outputs(x: Tensor, kernel_size: int, want_bias: bool, out_dtype: torch.dtype | None):
+    """dW / dbias buffers and the entry-point suffix: ``out_dtype=torch.float32`` asks for
+    fp32 results (x's dtype rounding, widened) from the ``_f32out`` entry points."""
+    c = int(x.shape[1])
+    odt = x.dtype if out_dtype is None else out_dtype
+    if odt not in (x.dtype, torch.float32):
+        raise ValueError(f"weight grads come in {x.dtype} or float32, not {odt}")
+    suffix = "_f32out" if odt != x.dtype else ""
+    dw = torch.empty((c, 1, kernel_size, kernel_size, kernel_size), dtype=odt, device=x.device)
+    db = torch.empty((c,), dtype=odt, device=x.device) if want_bias else None
+    return dw, db, suffix
+
+
+def dw_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True,
+             out_dtype: torch.dtype | None = None) -> tuple[Tensor, Tensor | None]:
     nat.require_device(x)
     lib = nat.load()
     n, c, d, h, w = _dims(x)
     code = nat.dtype_code(x.dtype)
-    dw = torch.empty((c, 1, kernel_size, kernel_size, kernel_size), dtype=x.dtype, device=x.device)
-    db = torch.empty((c,), dtype=x.dtype, device=x.device) if want_bias else None
+    dw, db, suffix = _wgrad_outputs(x, kernel_size, want_bias, out_dtype)
     ws = nat.workspace(lib.mednext_dw_wgrad_workspace_size(n, c, d, h, w, kernel_size, code), x.device)
     nat.check(
-        lib.mednext_dw_wgrad(
+        getattr(lib, "mednext_dw_wgrad" + suffix)(
             x.data_ptr(), grad.data_ptr(), dw.data_ptr(), nat.ptr(db), ws.data_ptr(), ws.numel(),
             n, c, d, h, w, kernel_size, code, nat.stream(),
         ),
-        "mednext_dw_wgrad",
+        "mednext_dw_wgrad" + suffix,
     )
     return dw, db
 
@@ -130,20 +143,20 @@ def s2_dgrad(grad: Tensor, weight: Tensor, input_size: tuple[int, int, int], ker
     return out
 
 
-def s2_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True) -> tuple[Tensor, Tensor | None]:
+def s2_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True,
+             out_dtype: torch.dtype | None = None) -> tuple[Tensor, Tensor | None]:
     nat.require_device(x)
     lib = nat.load()
     n, c, d, h, w = _dims(x)
     code = nat.dtype_code(x.dtype)
-    dw = torch.empty((c, 1, kernel_size, kernel_size, kernel_size), dtype=x.dtype, device=x.device)
-    db = torch.empty((c,), dtype=x.dtype, device=x.device) if want_bias else None
+    dw, db, suffix = _wgrad_outputs(x, kernel_size, want_bias, out_dtype)
     ws = nat.workspace(lib.mednext_dw_s2_wgrad_workspace_size(n, c, d, h, w, kernel_size, code), x.device)
     nat.check(
-        lib.mednext_dw_s2_wgrad(
+        getattr(lib, "mednext_dw_s2_wgrad" + suffix)(
             x.data_ptr(), grad.data_ptr(), dw.data_ptr(), nat.ptr(db), ws.data_ptr(), ws.numel(),
             n, c, d, h, w, kernel_size, code, nat.stream(),
         ),
-        "mednext_dw_s2_wgrad",
+        "mednext_dw_s2_wgrad" + suffix,
     )
     return dw, db
 
@@ -201,7 +214,8 @@ def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int, small: tuple[int, in
     return out
 
 
-def t_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True) -> tuple[Tensor, Tensor | None]:
+def t_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True,
+            out_dtype: torch.dtype | None = None) -> tuple[Tensor, Tensor | None]:
     """Weight (and bias) grad of the transposed conv; ``grad`` may be a pitched
     [n, c, pitch] buffer (3-D) or [n, c, 2d-1, 2h-1, 2w-1]."""
     nat.require_device(x)
@@ -209,15 +223,14 @@ def t_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True) -
     n, c, d, h, w = _dims(x)
     pitch = int(grad.shape[2]) if grad.ndim == 3 else 0
     code = nat.dtype_code(x.dtype)
-    dw = torch.empty((c, 1, kernel_size, kernel_size, kernel_size), dtype=x.dtype, device=x.device)
-    db = torch.empty((c,), dtype=x.dtype, device=x.device) if want_bias else None
+    dw, db, suffix = _wgrad_outputs(x, kernel_size, want_bias, out_dtype)
     ws = nat.workspace(lib.mednext_dwT_wgrad_workspace_size(n, c, d, h, w, kernel_size, code), x.device)
     nat.check(
-        lib.mednext_dwT_wgrad(
+        getattr(lib, "mednext_dwT_wgrad" + suffix)(
             x.data_ptr(), grad.data_ptr(), dw.data_ptr(), nat.ptr(db), ws.data_ptr(), ws.numel(),
             n, c, d, h, w, pitch, kernel_size, code, nat.stream(),
         ),
-        "mednext_dwT_wgrad",
+        "mednext_dwT_wgrad" + suffix,
     )
     return dw, db
 

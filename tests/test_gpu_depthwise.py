@@ -271,6 +271,33 @@ def test_stride2_input_grad_tma_kernel_is_bit_exact_with_fp32_kernel(dtype, shap
     assert nat.device_error() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_weight_grads_with_fp32_output_equal_the_cast_of_the_16bit_ones(dtype):
+    """The _f32out weight-grad entry points write what casting the 16-bit result to fp32
+    gives (stride 1, stride 2 on aligned and unaligned grids, transposed)."""
+    gen_seed = seed_of("f32out", str(dtype))
+    for shape in ((1, 4, 8, 16, 16), (2, 3, 5, 6, 7), (1, 32, 32, 32, 32)):
+        x = rand(shape, dtype, gen_seed).cuda()
+        dy = rand(shape, dtype, gen_seed + 1).cuda()
+        small = (shape[0], shape[1], *((s + 1) // 2 for s in shape[2:]))
+        dys = rand(small, dtype, gen_seed + 2).cuda()
+        big_t = (shape[0], shape[1], *(2 * s - 1 for s in small[2:]))
+        dyt = rand(big_t, dtype, gen_seed + 3).cuda()
+        xs = rand(small, dtype, gen_seed + 4).cuda()
+        cases = (
+            (dwk.dw_wgrad, (x, dy, 3)),
+            (dwk.s2_wgrad, (x, dys, 3)),
+            (dwk.t_wgrad, (xs, dyt, 3)),
+        )
+        for fn, args in cases:
+            dw16, db16 = fn(*args)
+            dw32, db32 = fn(*args, out_dtype=torch.float32)
+            assert dw32.dtype == torch.float32 and db32.dtype == torch.float32
+            assert torch.equal(dw32, dw16.float()), fn.__name__
+            assert torch.equal(db32, db16.float()), fn.__name__
+    assert nat.device_error() == 0
+
+
 def test_dgrad_with_addend_adds_residual():
     x = rand((1, 4, 8, 16, 16), torch.bfloat16, 8).cuda()
     w = rand((4, 1, 3, 3, 3), torch.bfloat16, 9).cuda()
