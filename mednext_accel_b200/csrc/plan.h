@@ -39,7 +39,9 @@ struct S1Plan {
 
 inline int nh_for(int k) { return k <= 3 ? 2 : 1; }
 
-inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, size_t esz, bool wgrad) {
+// stats: the forward also writes GroupNorm partial statistics (one per CTA tile)
+inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, size_t esz, bool wgrad,
+                      bool stats = false) {
   S1Plan p{};
   DwS1Geom& g = p.g;
   g.N = (int)n; g.C = (int)c; g.D = (int)d; g.H = (int)h; g.W = (int)w;
@@ -56,7 +58,11 @@ inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int
     const int G = ((lw * tr + 31) / 32) * 32;
     p.threads = G * k;
   } else {
-    tr = std::max(1, std::min(256 / lw, rows_needed));
+    // the packed k = 3 forward / input grad on 16-bit types runs 4-warp tiles (4 CTAs per
+    // SM): smaller units of work balance the SMs better than 8-warp tiles.  With
+    // statistics the larger tiles stay ahead (4x the partials to merge otherwise).
+    const bool packed = !wgrad && !stats && k == 3 && esz == 2 && lw >= 2;
+    tr = std::max(1, std::min((packed ? 128 : 256) / lw, rows_needed));
     p.threads = ((lw * tr + 31) / 32) * 32;
   }
   g.TR = tr;
@@ -67,20 +73,24 @@ inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int
   const long long max_chunks = std::max(1LL, (long long)(d / 8));
   long long chunks;
   if (!wgrad) {
-    // Depth chunks that minimise (rounds of resident CTAs) x (planes each CTA
-    // streams, k - 1 of them halo).  Residency: the packed k = 3 kernel on
-    // 16-bit types holds 16 warps per SM, the other kernels about 12.
+    // Depth chunks that minimise the busiest SM's time: (CTAs it runs) x (planes each
+    // streams, k - 1 of them halo, plus about 4 planes' worth of start-up: barriers,
+    // the first load's latency, the statistics epilogue) / (its throughput).  An SM
+    // runs at full rate with 16 resident warps and proportionally slower with fewer.
+    // Residency: the packed k = 3 kernel on 16-bit types holds 16 warps per SM, the
+    // other kernels about 12.
     const int warps = (p.threads + 31) / 32;
     const bool packed = k == 3 && esz == 2 && lw >= 2;
     const long long per_sm = std::max(1, (packed ? 16 : 12) / (warps + (packed ? 0 : 1)));
-    const long long slots = 148 * per_sm;
-    long long best_cost = -1;
+    double best_cost = -1.0;
     chunks = 1;
     for (long long cand = 1; cand <= max_chunks; ++cand) {
       const long long td = (d + cand - 1) / cand;
       const long long ctas = base * ((d + td - 1) / td);
-      const long long cost = ((ctas + slots - 1) / slots) * (td + k - 1);
-      if (best_cost < 0 || cost < best_cost) {
+      const long long on_sm = (ctas + 147) / 148;
+      const double rate = std::min(1.0, (double)(std::min(on_sm, per_sm) * warps) / 16.0);
+      const double cost = (double)on_sm * (double)(td + k - 1 + 4) / rate;
+      if (best_cost < 0.0 || cost < best_cost) {
         best_cost = cost;
         chunks = cand;
       }
