@@ -72,16 +72,17 @@ inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int
   const long long base = (long long)n * c * g.tilesW * g.tilesH;
   const long long max_chunks = std::max(1LL, (long long)(d / 8));
   long long chunks;
-  if (!wgrad) {
+  if (!grouped) {
     // Depth chunks that minimise the busiest SM's time: (CTAs it runs) x (planes each
     // streams, k - 1 of them halo, plus about 4 planes' worth of start-up: barriers,
     // the first load's latency, the statistics epilogue) / (its throughput).  An SM
     // runs at full rate with 16 resident warps and proportionally slower with fewer.
     // Residency: the packed k = 3 kernel on 16-bit types holds 16 warps per SM, the
     // other kernels about 12.
-    const int warps = (p.threads + 31) / 32;
-    const bool packed = k == 3 && esz == 2 && lw >= 2;
-    const long long per_sm = std::max(1, (packed ? 16 : 12) / (warps + (packed ? 0 : 1)));
+    // The weight-grad kernel (k <= 3) holds about 20 warps per SM (2 CTAs of 8 + 1).
+    const bool packed = !wgrad && k == 3 && esz == 2 && lw >= 2;
+    const int warps = (p.threads + 31) / 32 + (packed ? 0 : 1);
+    const long long per_sm = std::max(1, (wgrad ? 20 : packed ? 16 : 12) / warps);
     double best_cost = -1.0;
     chunks = 1;
     for (long long cand = 1; cand <= max_chunks; ++cand) {
