@@ -118,7 +118,7 @@ int mednext_check_device(void) {
 // ------------------------------ depthwise stride 1 ------------------------------
 size_t mednext_dw_fwd_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
   if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
-  const S1Plan p = plan_s1(n, c, d, h, w, k, elem_size(dtype), false, true);
+  const S1Plan p = plan_s1(n, c, d, h, w, k, elem_size(dtype), false);
   return (size_t)n * c * s1_tiles(p) * sizeof(GnPartial);
 }
 
@@ -139,7 +139,7 @@ int mednext_dw_fwd(const void* x, const void* weight, const void* bias, void* y,
     if (!aligned(gn_stats, 8)) return MEDNEXT_ERR_ALIGNMENT;
     part = static_cast<GnPartial*>(workspace);
   }
-  const S1Plan p = plan_s1(n, c, d, h, w, k, esz, false, gn_stats != nullptr);
+  const S1Plan p = plan_s1(n, c, d, h, w, k, esz, false);
   st = dispatch_dw_s1_conv(dtype, k, x, weight, bias, nullptr, y, part, p, 0, as_stream(stream));
   if (st != MEDNEXT_OK || gn_stats == nullptr) return st;
   return dispatch_gn_finalize(part, (int)s1_tiles(p), (int)(n * c), gn_eps, gn_stats, as_stream(stream));

@@ -19,13 +19,24 @@ struct GnBwdPartial {
 };
 
 // Merge the per-tile (count, mean, M2) partials of each (n, c) in tile order.
+// One warp per (n, c): lane l merges partials l, l + 32, ... in order, then a
+// butterfly over the lanes; lane 0 writes.  The order is fixed (deterministic).
 static __global__ void gn_finalize_kernel(const GnPartial* __restrict__ part, int tiles, int nc_total,
                                    float eps, float* __restrict__ stats) {
-  const int nc = blockIdx.x * blockDim.x + threadIdx.x;
-  if (nc >= nc_total) return;
+  const int nc = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (nc >= nc_total) return;  // warp-uniform
   double n = 0.0, mean = 0.0, m2 = 0.0;
   const GnPartial* p = part + (size_t)nc * tiles;
-  for (int t = 0; t < tiles; ++t) chan_merge(n, mean, m2, p[t].count, p[t].mean, p[t].m2);
+  for (int t = lane; t < tiles; t += 32) chan_merge(n, mean, m2, p[t].count, p[t].mean, p[t].m2);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double nb = __shfl_xor_sync(0xffffffffu, n, o);
+    const double mb = __shfl_xor_sync(0xffffffffu, mean, o);
+    const double qb = __shfl_xor_sync(0xffffffffu, m2, o);
+    chan_merge(n, mean, m2, nb, mb, qb);
+  }
+  if (lane != 0) return;
   const double var = n > 0.0 ? m2 / n : 0.0;  // biased variance, as GroupNorm uses
   stats[2 * nc] = (float)mean;
   stats[2 * nc + 1] = (float)(1.0 / sqrt(var + (double)eps));

@@ -26,7 +26,7 @@ namespace mednext {
   })
 
 int dispatch_gn_finalize(const GnPartial* part, int tiles, int nc, float eps, float* stats, cudaStream_t s) {
-  gn_finalize_kernel<<<(nc + 127) / 128, 128, 0, s>>>(part, tiles, nc, eps, stats);
+  gn_finalize_kernel<<<(unsigned)(((long long)nc * 32 + 127) / 128), 128, 0, s>>>(part, tiles, nc, eps, stats);
   return record_launch();
 }
 

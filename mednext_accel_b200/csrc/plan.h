@@ -39,9 +39,7 @@ struct S1Plan {
 
 inline int nh_for(int k) { return k <= 3 ? 2 : 1; }
 
-// stats: the forward also writes GroupNorm partial statistics (one per CTA tile)
-inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, size_t esz, bool wgrad,
-                      bool stats = false) {
+inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, size_t esz, bool wgrad) {
   S1Plan p{};
   DwS1Geom& g = p.g;
   g.N = (int)n; g.C = (int)c; g.D = (int)d; g.H = (int)h; g.W = (int)w;
@@ -59,9 +57,8 @@ inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int
     p.threads = G * k;
   } else {
     // the packed k = 3 forward / input grad on 16-bit types runs 4-warp tiles (4 CTAs per
-    // SM): smaller units of work balance the SMs better than 8-warp tiles.  With
-    // statistics the larger tiles stay ahead (4x the partials to merge otherwise).
-    const bool packed = !wgrad && !stats && k == 3 && esz == 2 && lw >= 2;
+    // SM): smaller units of work balance the SMs better than 8-warp tiles
+    const bool packed = !wgrad && k == 3 && esz == 2 && lw >= 2;
     tr = std::max(1, std::min((packed ? 128 : 256) / lw, rows_needed));
     p.threads = ((lw * tr + 31) / 32) * 32;
   }
