@@ -1,12 +1,13 @@
 """MedNeXt-Base 128^3 bf16 training-step benchmark on B200 (1..8 GPUs, one process per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-gpu]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Workload: MedNeXt v1 Base, kernel 3, deep supervision,
-batch 1 per GPU, input 1x1x128^3 ~N(0,1), labels uniform in {0,1,2}, loss = mean of
-the five heads' cross-entropy against nearest-downsampled labels, AdamW lr 1e-4,
-random init from seed 0, bf16 autocast.  Each rank draws its own sample (seed
+Workload: MedNeXt v1 Base, kernel 3, deep supervision, batch 1 per GPU, input
+1x1x128^3 ~N(0,1), labels uniform in {0,1,2}, loss = mean of the five heads'
+cross-entropy against nearest-downsampled labels, AdamW lr 1e-4, random init
+from seed 0, bf16 autocast (the reference's own training benchmark,
+benchmarks/implementations.py:137-190).  Each rank draws its own sample (seed
 1000+rank); gradients are averaged by NCCL all-reduce overlapped with backward.
 
 ``--impl ours`` times the sm_100a path: the whole step (forward, backward,
@@ -17,7 +18,15 @@ no flush is needed between steps.
 
 ``--impl reference`` times the reference's pure-PyTorch CPU implementation of
 the same step (the oracle's functional restatement, fp32, all host threads) on
-rank 0; other ranks exit.
+rank 0; other ranks exit.  A CPU step takes seconds, so at most
+``--ref-max-steps`` full-size steps are timed after one full-size warm-up step,
+and the line reports the number actually timed.
+
+``--impl reference-gpu`` (opt-in, one GPU) times the unmodified reference
+package from ``baseline/_ref`` on the GPU: ``mednext_base(...,
+optimization="auto")`` compiled with ``torch.compile(mode="default",
+fullgraph=True)`` and ``cudnn.benchmark``, median of per-step CUDA events, as the
+reference's benchmarks/implementations.py:137-190 does.
 """
 
 from __future__ import annotations
@@ -47,9 +56,15 @@ def parse_args(argv=None):
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--impl", choices=("ours", "reference", "reference-gpu"), default="ours")
     p.add_argument("--no-graph", action="store_true", help="time eager steps instead of a CUDA graph replay")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--ref-max-steps", type=int, default=3,
+                   help="CPU reference: at most this many full-size steps are timed (median reported)")
+    p.add_argument("--ref-optimization", default="auto",
+                   help="reference-gpu: the reference factory's optimization argument (auto or reference)")
+    p.add_argument("--ref-eager", action="store_true", help="reference-gpu: skip torch.compile")
+    p.add_argument("--bucket-mb", type=float, default=6.0, help="gradient all-reduce bucket size (fp32 MB)")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--spatial", type=int, default=SPATIAL, help=argparse.SUPPRESS)
     p.add_argument("--profile-step", action="store_true",
@@ -212,9 +227,83 @@ def depthwise_backward_roofline(device: torch.device, reps: int = 10) -> dict:
     }
 
 
+def compress_forward_roofline(device: torch.device, reps: int = 10) -> dict:
+    """Time the step's dominant tensor-core GEMM instance: level 0's compress
+    forward (1x1x1 conv 64 -> 32 at 128^3, bf16: GELU applied to the A tile as it
+    is loaded, bias and residual added in the epilogue), with CUDA events on the
+    launching stream and L2 flushed before each launch.
+
+    Algorithmic bytes = read u (64 ch) + read residual (32 ch) + write y (32 ch),
+    2 B each, per voxel; FLOPs = 2 * 64 * 32 per voxel.  K = 64 and N = 32 make
+    it HBM-bound (36 FLOP/B against a ridge of about 250), so the fraction is
+    taken against the measured HBM copy bandwidth; the tensor-pipe fraction is
+    reported beside it."""
+    from mednext_accel_b200 import _native as nat
+    from mednext_accel_b200.pointwise import pw_gemm
+
+    g = torch.Generator(device=device).manual_seed(11)
+    vox = SPATIAL ** 3
+    cin, cout = 64, 32
+    bf = torch.bfloat16
+    u = torch.randn((1, cin, SPATIAL, SPATIAL, SPATIAL), device=device, generator=g).to(bf)
+    res = torch.randn((1, cout, SPATIAL, SPATIAL, SPATIAL), device=device, generator=g).to(bf)
+    w = (torch.randn((cout, cin), device=device, generator=g) / cin**0.5).to(bf)
+    b = torch.randn((cout,), device=device, generator=g).to(bf).float()
+    y = torch.empty_like(res)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    for _ in range(3):
+        pw_gemm(u, w, cout, out_dtype=bf, prologue=nat.PRO_GELU, bias=b, residual=res, out=y)
+    s = torch.cuda.current_stream()
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        pw_gemm(u, w, cout, out_dtype=bf, prologue=nat.PRO_GELU, bias=b, residual=res, out=y)
+        e1.record(s)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    t_ms = statistics.median(times)
+    algo_bytes = vox * 2 * (cin + 2 * cout)
+    flops = 2 * cin * cout * vox
+    achieved = algo_bytes / (t_ms * 1e-3) / 1e9
+    peak, kind = measured_peaks()
+    tflops_peak = None
+    try:
+        tflops_peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        tflops_peak = 1590.0
+    traffic = None
+    prof = ROOT / "profiles" / "pw_compress_fwd_c32_128.json"
+    if prof.exists():
+        try:
+            traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+        except ValueError:
+            traffic = None
+    return {
+        "bound": "hbm",
+        "kernel": "pw_tma_fwd_kernel compress forward 64->32 at 128^3 bf16 (GELU prologue, bias+residual epilogue)",
+        "achieved": round(achieved, 1),
+        "peak": peak,
+        "peak_kind": kind,
+        "unit": "GB/s",
+        "frac": round(achieved / peak, 4),
+        "traffic": traffic,
+        "algorithmic_bytes": algo_bytes,
+        "ms": round(t_ms, 4),
+        "tflops": round(flops / (t_ms * 1e-3) / 1e12, 2),
+        "tensor_frac_of_bf16_peak": round(flops / (t_ms * 1e-3) / 1e12 / tflops_peak, 5),
+    }
+
+
 # --------------------------------------------------------------------------- CPU reference
-def cpu_reference_step_ms(steps: int, spatial: int = SPATIAL, budget_s: float = 150.0) -> tuple[float, dict]:
-    """The reference's pure-PyTorch training step on the host CPU (fp32, all threads)."""
+def cpu_reference_step_ms(steps: int, spatial: int = SPATIAL, warmup: int = 1,
+                          budget_s: float = 120.0) -> tuple[float, dict, int]:
+    """The reference's pure-PyTorch training step on the host CPU (fp32, all threads).
+
+    ``warmup`` full-size steps (thread pools, allocator, first-touch pages), then
+    up to ``steps`` timed full-size steps, stopping early once ``budget_s`` of
+    timed work has run.  Returns (median ms, description, steps timed)."""
     sys.path.insert(0, str(ROOT))
     from oracle.reference_model import ReferenceTrainer, forward, targets_for
 
@@ -227,14 +316,12 @@ def cpu_reference_step_ms(steps: int, spatial: int = SPATIAL, budget_s: float = 
                             optimization="reference")
     trainer = ReferenceTrainer(model.state_dict(), "base", 3)
     gen = torch.Generator().manual_seed(1000)
-    # warm-up at a quarter of the volume per axis (thread pools, allocator)
-    xs = torch.randn((1, 1, spatial // 2, spatial // 2, spatial // 2), generator=gen)
-    ts = torch.randint(0, 3, (1, spatial // 2, spatial // 2, spatial // 2), generator=gen)
-    trainer.step(xs, targets_for(ts, forward(trainer.params, xs, "base", 3)))
     x = torch.randn((1, 1, spatial, spatial, spatial), generator=gen)
     target = torch.randint(0, 3, (1, spatial, spatial, spatial), generator=gen)
     with torch.no_grad():
         tg = targets_for(target, forward(trainer.params, x, "base", 3))
+    for _ in range(max(1, warmup)):
+        trainer.step(x, tg)
     times = []
     t_start = time.perf_counter()
     for _ in range(max(1, steps)):
@@ -245,24 +332,26 @@ def cpu_reference_step_ms(steps: int, spatial: int = SPATIAL, budget_s: float = 
             break
     ms = statistics.median(times)
     info = {"cores": threads, "kind": "port",
-            "sample": f"{len(times)} fp32 train step(s) of the reference pure-PyTorch MedNeXt-Base "
-                      f"(oracle/reference_model.py) at {spatial}^3 B1 on {threads} host threads, median"}
-    return ms, info
+            "sample": f"median of {len(times)} fp32 train step(s) after {max(1, warmup)} full-size warm-up "
+                      f"step(s): the reference's pure-PyTorch MedNeXt-Base (oracle/reference_model.py) "
+                      f"at {spatial}^3 B1 on {threads} host threads"}
+    return ms, info, len(times)
 
 
 def run_reference(args) -> int:
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
-    ms, info = cpu_reference_step_ms(min(args.steps, 3))
+    ms, info, timed = cpu_reference_step_ms(min(args.steps, args.ref_max_steps), warmup=1)
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": round(ms, 3),
         "unit": "ms",
         "n_gpus": args.gpus,
-        "steps": args.steps,
-        "warmup": args.warmup,
+        "steps": timed,
+        "steps_requested": args.steps,
+        "warmup": 1,
         "ms_per_step": round(ms, 3),
         "higher_is_better": False,
         "scaling": "weak",
@@ -270,9 +359,102 @@ def run_reference(args) -> int:
         "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": "MedNeXt-Base k3 128^3 B1 train step (5-head CE, AdamW), host CPU",
-                   "global_batch": 1, "spatial": SPATIAL},
+                   "global_batch": 1, "spatial": SPATIAL,
+                   "timing": "median of the timed steps (a CPU step takes seconds; see cpu_baseline.sample)"},
         "cpu_baseline": {"value": round(ms, 3), "unit": "ms", **info},
         "e2e": {"value": round(ms, 3), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- reference on the GPU
+def run_reference_gpu(args) -> int:
+    """The unmodified reference package on one B200: the GPU bar of the comparison.
+
+    Mirrors the reference's benchmarks/implementations.py:137-190: the stock
+    factory (``optimization="auto"`` by default), ``torch.compile(mode="default",
+    fullgraph=True)``, ``cudnn.benchmark``, a resident synthetic sample, the
+    five-head mean cross-entropy under bf16 autocast and AdamW; per-step CUDA
+    events after the warm-up, median reported."""
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "mednext_accel").is_dir():
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "baseline/_ref/mednext_accel is absent"}),
+              flush=True)
+        return 0
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "CUDA is not available"}), flush=True)
+        return 0
+    sys.path.insert(0, str(ref_root))
+    import mednext_accel as ref
+
+    torch.cuda.set_device(local)
+    torch.backends.cudnn.benchmark = True
+    torch.manual_seed(0)
+    model = ref.mednext_base(in_channels=1, out_channels=3, kernel_size=3, deep_supervision=True,
+                             optimization=args.ref_optimization).cuda().train()
+    compiled = not args.ref_eager
+    if compiled:
+        model = torch.compile(model, mode="default", fullgraph=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4)
+    gen = torch.Generator().manual_seed(1000)
+    x = torch.randn((1, 1, SPATIAL, SPATIAL, SPATIAL), generator=gen).cuda()
+    target = torch.randint(0, 3, (1, SPATIAL, SPATIAL, SPATIAL), generator=gen).cuda()
+    targets = downsampled_targets(target)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            heads = model(x)
+            if isinstance(heads, torch.Tensor):
+                heads = (heads,)
+            loss = sum(F.cross_entropy(h, targets[tuple(h.shape[2:])]) for h in heads) / len(heads)
+        loss.backward()
+        opt.step()
+        return loss
+
+    t0 = time.perf_counter()
+    for _ in range(max(3, args.warmup)):
+        loss = step()
+    torch.cuda.synchronize()
+    warm_s = time.perf_counter() - t0
+    events = []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            loss = step()
+            e1.record()
+            events.append((e0, e1))
+        torch.cuda.synchronize()
+    times = [a.elapsed_time(b) for a, b in events]
+    ms = statistics.median(times)
+    line = {
+        "impl": "reference-gpu",
+        "metric": METRIC,
+        "value": round(ms, 3),
+        "unit": "ms",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms, 3),
+        "mean_ms": round(statistics.fmean(times), 3),
+        "higher_is_better": False,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "MedNeXt-Base k3 128^3 B1 train step (5-head CE, AdamW), reference package on GPU",
+                   "optimization": args.ref_optimization, "compiled": compiled,
+                   "compile": "torch.compile(mode='default', fullgraph=True)" if compiled else None,
+                   "cudnn_benchmark": True, "timing": "median of per-step CUDA events"},
+        "warmup_wall_s": round(warm_s, 1),
+        "peak_allocated_mib": round(torch.cuda.max_memory_allocated() / 2**20),
+        "final_loss": round(float(loss.item()), 5),
+        "clocks": clocks.summary(),
+        "device": torch.cuda.get_device_name(),
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -299,7 +481,7 @@ def run_ours(args) -> int:
     torch.manual_seed(0)
     model = mx.mednext_base(in_channels=1, out_channels=3, kernel_size=3, deep_supervision=True).to(device).train()
     broadcast_parameters(model)
-    reducer = GradientBucketReducer(model, bucket_cap_mb=25.0)
+    reducer = GradientBucketReducer(model, bucket_cap_mb=args.bucket_mb)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True, capturable=True)
 
     gen = torch.Generator().manual_seed(1000 + rank)
@@ -319,12 +501,16 @@ def run_ours(args) -> int:
         opt.step()
         return loss
 
-    # warm-up on a side stream (required before graph capture)
+    # Warm-up on the stream the graph is captured on (required before capture).
+    # Autograd's AccumulateGrad nodes remember the stream of their first use, so
+    # warming up on any other stream leaves them on that stream during capture;
+    # dropping the last warm-up loss frees its graph before the capture begins.
     side = torch.cuda.Stream(device=device)
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
         for _ in range(max(3, args.warmup)):
             loss = step()
+        del loss
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
 
@@ -345,7 +531,7 @@ def run_ours(args) -> int:
     launches_before = nat.load().mednext_kernel_launches()
     if not args.no_graph:
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        with torch.cuda.graph(graph, stream=side):
             static_loss = step()
         mode = "cuda-graph"
         per_step_launches = nat.load().mednext_kernel_launches() - launches_before
@@ -408,12 +594,13 @@ def run_ours(args) -> int:
     e2e_ms = float(e2e.item()) / e2e_steps
 
     roof = depthwise_backward_roofline(device) if rank == 0 else None
+    roof_gemm = compress_forward_roofline(device) if rank == 0 else None
     dev_err = nat.device_error()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_ms, info = cpu_reference_step_ms(1, spatial=S)
-        cpu = {"value": round(cpu_ms, 1), "unit": "ms", **info}
+        cpu_ms, info, timed = cpu_reference_step_ms(3, spatial=S, warmup=1)
+        cpu = {"value": round(cpu_ms, 1), "unit": "ms", "steps": timed, **info}
 
     if graph is not None:
         del graph
@@ -444,6 +631,7 @@ def run_ours(args) -> int:
             "l2": "inputs and activations larger than L2 (no flush)",
         },
         "roofline": roof,
+        "roofline_gemm": roof_gemm,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4},
         "gpu_launches": int(per_step_launches * args.steps),
@@ -459,6 +647,8 @@ def main(argv=None) -> int:
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
+    if args.impl == "reference-gpu":
+        return run_reference_gpu(args)
     return run_ours(args)
 
 

@@ -148,7 +148,10 @@ int mednext_dw_wgrad_f32out(const void* x, const void* dy, void* dweight, void* 
  * The first call on each device does one-time set-up with that device current
  * (it looks up the array's device address, which loads the library's module
  * on the device if needed); make that first call before any stream capture
- * begins.
+ * begins.  The looked-up address is kept for the life of the process: after
+ * cudaDeviceReset(), or any other teardown of the device's primary context,
+ * the array may move, so a process that resets a device must not call this
+ * entry point on that device again.
  * All calls on one device share the array: two calls that can run at the same
  * time (different streams with no ordering between them, or several host
  * threads) race on it and produce wrong gradients.  Calls issued in order on

@@ -37,14 +37,19 @@ _AUTOCAST_COMPUTE = (torch.bfloat16, torch.float16)
 
 @dataclass(frozen=True, slots=True)
 class ModelOptimizationContext:
+    """Model-level facts every operator of one model shares (family, variant,
+    checkpointing label, approximation opt-in)."""
+
     family: str
     variant: str
     checkpointing: str
     allow_approximate: bool = False
 
 
-def _dtype_name(dtype: torch.dtype | str) -> str:
-    return str(dtype).removeprefix("torch.")
+def _phase(training: bool, export: bool) -> str:
+    if export:
+        return "export"
+    return "training" if training else "inference"
 
 
 def execution_context_for_shape(
@@ -59,20 +64,14 @@ def execution_context_for_shape(
     training: bool = True,
     export: bool = False,
 ) -> ExecutionContext:
-    return ExecutionContext(
-        phase="export" if export else ("training" if training else "inference"),
-        device_type=device_type,
-        sm=sm,
-        total_vram_bytes=total_vram_bytes,
-        dtype=_dtype_name(dtype),
-        batch_size=batch_size,
-        spatial_shape=spatial_shape,
-        model_family=model_context.family,
-        variant=model_context.variant,
-        checkpointing=model_context.checkpointing,
-        export=export,
-        allow_approximate=model_context.allow_approximate,
-    )
+    """Combine the model's context with the facts of one call into the
+    ExecutionContext the resolver reads.  ``dtype`` may be a torch dtype or its
+    name ("bfloat16")."""
+    dtype_name = dtype if isinstance(dtype, str) else str(dtype).split(".")[-1]
+    model = model_context
+    return ExecutionContext(_phase(training, export), device_type, sm, total_vram_bytes, dtype_name, batch_size,
+                            spatial_shape, model.family, model.variant, model.checkpointing, export,
+                            model.allow_approximate)
 
 
 _DEVICE_FACTS: dict[int, tuple[tuple[int, int], int]] = {}

@@ -4,6 +4,9 @@
 #include "plan.h"
 
 #include <atomic>
+#include <map>
+#include <mutex>
+#include <utility>
 
 namespace mednext {
 namespace {
@@ -21,6 +24,27 @@ int record_launch() {
 }
 int last_cuda_error() { return t_last_cuda_error; }
 void note_cuda_error(cudaError_t e) { t_last_cuda_error = (int)e; }
+
+int ensure_smem_fn(const void* fn, size_t smem) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    note_cuda_error(e);
+    return MEDNEXT_ERR_CUDA;
+  }
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> granted;  // largest size granted per (kernel, device)
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& have = granted[{fn, dev}];
+  if (smem <= have) return MEDNEXT_OK;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) {
+    note_cuda_error(e);
+    return MEDNEXT_ERR_CUDA;
+  }
+  have = smem;
+  return MEDNEXT_OK;
+}
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 }  // namespace mednext
 

@@ -23,7 +23,7 @@ struct GnBwdPartial {
 // butterfly over the lanes; lane 0 writes.  The order is fixed (deterministic).
 static __global__ void gn_finalize_kernel(const GnPartial* __restrict__ part, int tiles, int nc_total,
                                    float eps, float* __restrict__ stats) {
-  const int nc = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const long long nc = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // 64-bit: no wrap at 2^27 warps
   const int lane = threadIdx.x & 31;
   if (nc >= nc_total) return;  // warp-uniform
   double n = 0.0, mean = 0.0, m2 = 0.0;

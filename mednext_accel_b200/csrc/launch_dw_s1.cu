@@ -40,11 +40,7 @@ int try_s1_conv_tma(const void* x, const void* wgt, const void* bias, const void
       return -1;
     const size_t smem = 128 + L::weights(K, sizeof(typename Elem<T>::Acc)) + kDwSlots * L::slot(g, K, false);
     auto kern = dw_s1_conv_tma_kernel<T, K, NH>;
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      configured = smem;
-    }
+    if (const int rc = ensure_smem(kern, smem)) return rc;
     kern<<<(unsigned)p.grid, p.threads + 32, smem, s>>>(m, static_cast<const T*>(wgt), static_cast<const T*>(bias),
                                                           static_cast<const T*>(addend), static_cast<T*>(y), st, p.g,
                                                           flip);
@@ -57,11 +53,7 @@ int launch_s1_conv_pk(const CUtensorMap& m, const void* wgt, const void* bias, c
                       GnPartial* st, const S1Plan& p, int flip, cudaStream_t s) {
   const size_t smem = DwPkLayout<T>::smem(p.g);
   auto kern = dw_s1_conv_pk_kernel<T, STATS, ADD>;
-  static size_t configured = 0;  // raise the opt-in limit once per instantiation
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    configured = smem;
-  }
+  if (const int rc = ensure_smem(kern, smem)) return rc;
   kern<<<(unsigned)p.grid, p.threads, smem, s>>>(m, static_cast<const T*>(wgt), static_cast<const T*>(bias),
                                                    static_cast<const T*>(addend), static_cast<T*>(y), st, p.g, flip);
   return record_launch();
@@ -101,11 +93,7 @@ int launch_s1_conv(const void* x, const void* wgt, const void* bias, const void*
   if (tst != -1) return tst;
   constexpr int NH = K <= 3 ? 2 : 1;
   auto kern = dw_s1_conv_kernel<T, K, NH>;
-  static size_t configured = 0;  // raise the opt-in limit once per instantiation
-  if (p.smem > 48 * 1024 && p.smem > configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-    configured = p.smem;
-  }
+  if (const int rc = ensure_smem(kern, p.smem)) return rc;
   kern<<<(unsigned)p.grid, p.threads, p.smem, s>>>(static_cast<const T*>(x), static_cast<const T*>(wgt),
                                                    static_cast<const T*>(bias), static_cast<const T*>(addend),
                                                    static_cast<T*>(y), st, p.g, flip);
@@ -149,11 +137,7 @@ int try_s1_wgrad_tma(const void* x, const void* dy, typename Elem<T>::Acc* part,
       return -1;
     const size_t smem = 128 + kDwSlots * L::slot(g, K, true);
     auto kern = dw_s1_wgrad_tma_kernel<T, K, NH>;
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      configured = smem;
-    }
+    if (const int rc = ensure_smem(kern, smem)) return rc;
     kern<<<(unsigned)p.grid, p.threads + 32, smem, s>>>(mx, mdy, part, p.g);
     return record_launch();
   }
@@ -170,19 +154,11 @@ int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws,
   if (tst != -1) return tst;
   if constexpr (K <= 3) {
     auto kern = dw_s1_wgrad_kernel<T, K, NH>;
-    static size_t configured = 0;  // raise the opt-in limit once per instantiation
-    if (p.smem > 48 * 1024 && p.smem > configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-    configured = p.smem;
-  }
+    if (const int rc = ensure_smem(kern, p.smem)) return rc;
     kern<<<(unsigned)p.grid, p.threads, p.smem, s>>>(static_cast<const T*>(x), static_cast<const T*>(dy), part, p.g);
   } else {
     auto kern = dw_s1_wgrad_grouped_kernel<T, K, NH>;
-    static size_t configured = 0;  // raise the opt-in limit once per instantiation
-    if (p.smem > 48 * 1024 && p.smem > configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-    configured = p.smem;
-  }
+    if (const int rc = ensure_smem(kern, p.smem)) return rc;
     kern<<<(unsigned)p.grid, p.threads, p.smem, s>>>(static_cast<const T*>(x), static_cast<const T*>(dy), part, p.g);
   }
   const int st = record_launch();

@@ -89,11 +89,7 @@ int try_gather_pk(const void* big, const void* w, const void* b, const void* add
     const size_t smem = L::smem(pg);
     const int threads = (pg.lw * pg.THo + 31) / 32 * 32;
     auto kern = dw_s2_gather_pk_kernel<T>;
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      configured = smem;
-    }
+    if (const int rc = ensure_smem(kern, smem)) return rc;
     kern<<<(unsigned)ctas, threads, smem, s>>>(m, static_cast<const T*>(w), static_cast<const T*>(b),
                                                static_cast<T*>(small), pg);
     return record_launch();
@@ -126,11 +122,7 @@ int try_s2_wgrad_pk(const void* big, const void* small, void* dw, void* db, floa
     const size_t smem = DwS2PkWLayout<T>::smem(pg);
     const int threads = (pg.lw * pg.THo + 31) / 32 * 32;
     auto kern = dw_s2_wgrad_pk_kernel<T>;
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && smem > configured) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      configured = smem;
-    }
+    if (const int rc = ensure_smem(kern, smem)) return rc;
     kern<<<(unsigned)ctas, threads, smem, s>>>(mx, mdy, part, pg);
     const int st = record_launch();
     if (st != MEDNEXT_OK) return st;
@@ -192,7 +184,7 @@ int try_scatter_pk(const void* small, const void* w, const void* b, const void* 
     const size_t smem = L::smem(pg);
     const int threads = (pg.lw * pg.THs + 31) / 32 * 32;
     auto kern = add_even != nullptr ? dw_s2_scatter_pk_kernel<T, true> : dw_s2_scatter_pk_kernel<T, false>;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (const int rc = ensure_smem(kern, smem)) return rc;
     kern<<<(unsigned)ctas, threads, smem, s>>>(m, static_cast<const T*>(w), static_cast<const T*>(b),
                                                static_cast<const T*>(add_even), static_cast<T*>(big), pg);
     return record_launch();

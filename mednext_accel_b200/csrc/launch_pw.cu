@@ -40,8 +40,7 @@ int try_pw_wgrad_tma(const PwWgradArgs& a, cudaStream_t s) {
   cfg.units = a.mtiles * a.ntiles * a.splits;
   const size_t smem = 1024 + cfg.stages * per_stage;
   auto kern = pw_tma_wgrad_kernel<TA, PRO>;
-  static size_t configured = 0;
-  set_smem(kern, smem, configured);
+  if (const int rc = ensure_smem(kern, smem)) return rc;
   const int grid = std::min(cfg.units, num_sms());
   kern<<<grid, kWgThreads, smem, s>>>(mG, mA, a, cfg);
   return record_launch();
@@ -54,8 +53,7 @@ int launch_pw_wgrad(const PwWgradArgs& a, cudaStream_t s) {
   if (st != -1) return st;
   auto kern = pw_wgrad_kernel<TA, PRO>;
   const size_t smem = pw_smem(a.BN);
-  static size_t configured = 0;
-  set_smem(kern, smem, configured);
+  if (const int rc = ensure_smem(kern, smem)) return rc;
   const long long grid = (long long)a.splits * a.ntiles * a.mtiles;
   kern<<<(unsigned)grid, kPwThreads, smem, s>>>(a);
   return record_launch();

@@ -236,6 +236,15 @@ int last_cuda_error();
 // Records a CUDA runtime error for mednext_last_cuda_error() on this thread.
 void note_cuda_error(cudaError_t e);
 
+// Dynamic shared memory above 48 KB needs an opt-in per kernel and per device.
+// Grants the opt-in for `smem` bytes on the current device (once per kernel,
+// device and size; thread-safe).  Returns MEDNEXT_OK or MEDNEXT_ERR_CUDA.
+int ensure_smem_fn(const void* fn, size_t smem);
+template <typename K>
+inline int ensure_smem(K* kern, size_t smem) {
+  return smem <= 48 * 1024 ? 0 : ensure_smem_fn(reinterpret_cast<const void*>(kern), smem);
+}
+
 }  // namespace mednext
 
 // Per-translation-unit reader of the device error word.

@@ -21,23 +21,14 @@ using namespace tma;
 inline bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 constexpr size_t kSmemBudget = 220 * 1024;
 constexpr size_t kWResidentBytes = 64 * 1024;  // largest W operand kept resident in the forward kernel
+// SM count of the current device (queried per call: a process may drive
+// several devices, and the runtime caches the attribute).
 inline int num_sms() {
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0)
+    return 148;
   return sms;
-}
-
-template <typename K>
-inline void set_smem(K kern, size_t smem, size_t& configured) {
-  if (smem > configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    configured = smem;
-  }
 }
 
 // ------------------------------------------------------------------ forward (TMA)
@@ -164,8 +155,7 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   if (cfg.stages < 2 || (pro_store && cfg.stages <= kProStoreLag) || ((FW || MLP) && cfg.stages <= kFwLag)) return -1;
   const size_t smem = 1024 + cfg.stages * per_stage + w_bytes + w2_bytes + cfg.estages * ebytes + stg + g_bytes;
   auto kern = pw_tma_fwd_kernel<TA, TY, PRO, EPI>;
-  static size_t configured = 0;
-  set_smem(kern, smem, configured);
+  if (const int rc = ensure_smem(kern, smem)) return rc;
   const int grid = std::min(cfg.total_tiles, num_sms());
   kern<<<grid, kFwdThreads, smem, s>>>(mA, mB, mAux, mRes, mY, mP, mB2, mY2, a, cfg);
   return record_launch();
@@ -178,8 +168,7 @@ int launch_pw_fwd(const PwFwdArgs& a, cudaStream_t s) {
   if (st != -1) return st;
   auto kern = pw_fwd_kernel<TA, TY, PRO>;
   const size_t smem = pw_smem(a.BN);
-  static size_t configured = 0;
-  set_smem(kern, smem, configured);
+  if (const int rc = ensure_smem(kern, smem)) return rc;
   const long long grid = (long long)a.S * a.ntiles * a.mtiles;
   kern<<<(unsigned)grid, kPwThreads, smem, s>>>(a);
   int rc = record_launch();

@@ -43,32 +43,41 @@ EXPANSION_RATIOS: dict[str, tuple[int, ...]] = {
 }
 
 
+def _canonical_stages(stages: object) -> tuple[int, ...]:
+    """Sorted tuple of distinct resolution-stage indices in 0..4; ValueError otherwise."""
+    values = tuple(stages)  # type: ignore[arg-type]
+    if len(values) == 0:
+        raise ValueError("stages: give at least one stage, or None for every stage")
+    if not all(type(v) is int for v in values):
+        raise ValueError(f"stages: expected integers, got {values!r}")
+    if len(set(values)) < len(values):
+        raise ValueError(f"stages: duplicates are not allowed, got {values!r}")
+    if not all(0 <= v <= 4 for v in values):
+        raise ValueError(f"stages: every stage must be between 0 and 4 (the five resolutions), got {values!r}")
+    return tuple(sorted(values))
+
+
 @dataclass(frozen=True, slots=True)
 class CheckpointConfig:
-    """Activation checkpointing: ``expansion`` recomputes the expanded branch of
-    each block in backward, ``block`` recomputes whole blocks; ``stages`` limits it
-    to resolution stages 0..4 (reference checkpointing.py:11-48)."""
+    """Activation checkpointing for MedNeXt.
+
+    ``style="expansion"`` recomputes each block's expanded branch (expand, GELU,
+    compress) in backward; ``style="block"`` recomputes whole blocks.  ``stages``
+    names the resolution stages 0..4 it applies to (None: all of them).  Same
+    public fields and meaning as the reference's checkpointing.py:11-48."""
 
     style: Literal["expansion", "block"] = "expansion"
     stages: tuple[int, ...] | None = None
 
     def __post_init__(self) -> None:
-        if self.style not in ("expansion", "block"):
-            raise ValueError("style must be 'expansion' or 'block'")
-        if self.stages is None:
-            return
-        if not self.stages:
-            raise ValueError("stages must be a non-empty tuple or None")
-        if any(type(stage) is not int for stage in self.stages):
-            raise ValueError("stages must contain only integers")
-        if len(set(self.stages)) != len(self.stages):
-            raise ValueError("stages must not contain duplicates")
-        if any(stage < 0 or stage > 4 for stage in self.stages):
-            raise ValueError("stages must be between 0 and 4")
-        object.__setattr__(self, "stages", tuple(sorted(self.stages)))
+        if self.style not in _CHECKPOINT_STYLES:
+            raise ValueError(f"style: unknown checkpointing style {self.style!r} "
+                             f"(expected {' or '.join(_CHECKPOINT_STYLES)})")
+        if self.stages is not None:
+            object.__setattr__(self, "stages", _canonical_stages(self.stages))
 
     def includes(self, stage: int) -> bool:
-        return self.stages is None or stage in self.stages
+        return True if self.stages is None else stage in self.stages
 
     @property
     def checkpoints_expansion(self) -> bool:
@@ -79,9 +88,13 @@ class CheckpointConfig:
         return self.style == "block"
 
 
+_CHECKPOINT_STYLES = ("expansion", "block")
+
+
 @dataclass(frozen=True, slots=True)
 class MedNeXtV1Config:
-    """Serializable description of a MedNeXt v1 architecture."""
+    """Architecture of one MedNeXt v1 network (the reference's models/config.py
+    fields, so configs serialise the same way)."""
 
     variant: str
     spatial_dims: Literal[2, 3]
@@ -98,18 +111,19 @@ class MedNeXtV1Config:
     deep_supervision: bool = False
 
     def __post_init__(self) -> None:
-        if self.spatial_dims not in (2, 3):
-            raise ValueError("spatial_dims must be 2 or 3")
-        if self.in_channels <= 0 or self.out_channels <= 0:
-            raise ValueError("in_channels and out_channels must be positive")
-        if self.base_channels <= 0:
-            raise ValueError("base_channels must be positive")
-        if self.kernel_size <= 0 or self.kernel_size % 2 == 0:
-            raise ValueError("kernel_size must be a positive odd integer")
-        if len(self.block_counts) != 9 or len(self.expansion_ratios) != 9:
-            raise ValueError("MedNeXt v1 requires nine block stages")
-        if len(self.downsample_expansion_ratios) != 4:
-            raise ValueError("MedNeXt v1 requires four downsample expansion ratios")
+        rules = (
+            (self.spatial_dims in (2, 3), "spatial_dims must be 2 or 3"),
+            (min(self.in_channels, self.out_channels) > 0, "in_channels and out_channels must be positive"),
+            (self.base_channels > 0, "base_channels must be positive"),
+            (self.kernel_size > 0 and self.kernel_size % 2 == 1, "kernel_size must be a positive odd integer"),
+            (len(self.block_counts) == 9, "block_counts needs one entry per stage (nine stages)"),
+            (len(self.expansion_ratios) == 9, "expansion_ratios needs one entry per stage (nine stages)"),
+            (len(self.downsample_expansion_ratios) == 4,
+             "downsample_expansion_ratios needs one entry per down block (four)"),
+        )
+        for ok, message in rules:
+            if not ok:
+                raise ValueError(message)
 
 
 def get_mednext_v1_config(
@@ -123,27 +137,23 @@ def get_mednext_v1_config(
     deep_supervision: bool = False,
     compatibility: Literal["official", "monai"] = "official",
 ) -> MedNeXtV1Config:
-    name = variant.lower()
-    if name not in BLOCK_COUNTS:
-        raise ValueError(
-            f"unknown MedNeXt v1 variant {variant!r}; expected one of {', '.join(BLOCK_COUNTS)}"
-        )
-    if compatibility not in ("official", "monai"):
-        raise ValueError("compatibility must be 'official' or 'monai'")
-    ratios = EXPANSION_RATIOS[name]
-    # Official checkpoints give down block i the ratio of stage i+1; MONAI uses stage i.
-    down = ratios[1:5] if compatibility == "official" else ratios[:4]
+    """The published variant ``small`` / ``base`` / ``medium`` / ``large``."""
+    key = variant.lower()
+    counts = BLOCK_COUNTS.get(key)
+    if counts is None:
+        raise ValueError(f"unknown MedNeXt v1 variant {variant!r}; known variants: {', '.join(BLOCK_COUNTS)}")
+    ratios = EXPANSION_RATIOS[key]
+    # Which stage's ratio a down block uses is where the two published
+    # implementations differ: the official code takes the ratio of the stage it
+    # leads into (i + 1), MONAI the ratio of the stage it leaves (i).
+    offsets = {"official": 1, "monai": 0}
+    if compatibility not in offsets:
+        raise ValueError(f"compatibility must be one of {', '.join(offsets)}, got {compatibility!r}")
+    first = offsets[compatibility]
     return MedNeXtV1Config(
-        variant=name,
-        spatial_dims=spatial_dims,
-        in_channels=in_channels,
-        out_channels=out_channels,
-        kernel_size=kernel_size,
-        base_channels=base_channels,
-        block_counts=BLOCK_COUNTS[name],
-        expansion_ratios=ratios,
-        downsample_expansion_ratios=down,
-        compatibility=compatibility,
+        variant=key, spatial_dims=spatial_dims, in_channels=in_channels, out_channels=out_channels,
+        kernel_size=kernel_size, base_channels=base_channels, block_counts=counts, expansion_ratios=ratios,
+        downsample_expansion_ratios=tuple(ratios[first:first + 4]), compatibility=compatibility,
         deep_supervision=deep_supervision,
     )
 

@@ -21,10 +21,10 @@ from __future__ import annotations
 
 import warnings
 from collections.abc import Callable, Mapping, Sequence
-from dataclasses import asdict, dataclass, field
+from dataclasses import dataclass, field, fields
 from math import prod
 from types import MappingProxyType
-from typing import Literal
+from typing import Literal, NamedTuple
 
 ExecutionPhase = Literal["training", "inference", "export"]
 SemanticEquivalence = Literal["exact", "numerical", "approximate"]
@@ -32,19 +32,35 @@ Confidence = Literal["guard", "fixed-table", "measured-exact-context"]
 SM100 = (10, 0)
 
 
-def _spatial_tuple(value: tuple[int, ...], name: str, *, positive: bool = True) -> tuple[int, ...]:
-    result = tuple(value)
-    if len(result) not in (2, 3) or any(not isinstance(item, int) for item in result):
-        raise ValueError(f"{name} must contain two or three integers")
-    lower = 1 if positive else 0
-    if any(item < lower for item in result):
-        raise ValueError(f"{name} values must be >= {lower}")
-    return result
+# --------------------------------------------------------------------------- descriptors
+_CONV_GEOMETRY = ("kernel_size", "stride", "padding", "dilation", "groups")
+_PHASES = ("training", "inference", "export")
+_EQUIVALENCES = ("exact", "numerical", "approximate")
+
+
+def _extents(value: object, field_name: str, least: int) -> tuple[int, ...]:
+    """Normalise a 2-D or 3-D extent (kernel, stride, padding, ...) to a tuple.
+
+    Raises ValueError naming ``field_name`` when the value is not two or three
+    plain integers or when an entry is below ``least``."""
+    try:
+        dims = tuple(value)  # type: ignore[arg-type]
+    except TypeError:
+        dims = ()
+    if len(dims) not in (2, 3) or not all(type(v) is int for v in dims):
+        raise ValueError(f"{field_name}: expected two or three integers, got {value!r}")
+    if min(dims) < least:
+        raise ValueError(f"{field_name}: every entry must be at least {least}, got {value!r}")
+    return dims
 
 
 @dataclass(frozen=True, slots=True)
 class OperatorDescriptor:
-    """Shape-independent identity of one optimizable operator."""
+    """What an optimizable operator is, independent of the input's size.
+
+    Convolutions carry their full geometry (all five geometry fields, or none for
+    operators such as normalisations).  ``expansion_ratio`` is set on MedNeXt
+    block descriptors, whose table rows are keyed on it."""
 
     family: str
     direction: str
@@ -59,39 +75,57 @@ class OperatorDescriptor:
     expansion_ratio: int | None = None
 
     def __post_init__(self) -> None:
-        if not self.family or not self.direction:
-            raise ValueError("family and direction must be non-empty")
-        for name in ("in_channels", "out_channels"):
-            if getattr(self, name) <= 0:
-                raise ValueError(f"{name} must be positive")
-        geometry = ("kernel_size", "stride", "padding", "dilation", "groups")
-        present = tuple(getattr(self, name) is not None for name in geometry)
-        if any(present) and not all(present):
-            raise ValueError("convolution geometry fields must be supplied together")
-        if not any(present):
+        if not (self.family and self.direction):
+            raise ValueError("an operator needs a non-empty family and direction")
+        if self.in_channels <= 0 or self.out_channels <= 0:
+            bad = "in_channels" if self.in_channels <= 0 else "out_channels"
+            raise ValueError(f"{bad} must be positive")
+        given = [getattr(self, f) is not None for f in _CONV_GEOMETRY]
+        if not any(given):
             return
-        if self.groups is None or self.groups <= 0:
+        if not all(given):
+            missing = [f for f, g in zip(_CONV_GEOMETRY, given, strict=True) if not g]
+            raise ValueError(f"convolution geometry is incomplete: missing {', '.join(missing)}")
+        if self.groups <= 0:  # type: ignore[operator]
             raise ValueError("groups must be positive")
-        object.__setattr__(self, "kernel_size", _spatial_tuple(self.kernel_size, "kernel_size"))
-        object.__setattr__(self, "stride", _spatial_tuple(self.stride, "stride"))
-        object.__setattr__(self, "padding", _spatial_tuple(self.padding, "padding", positive=False))
-        object.__setattr__(self, "dilation", _spatial_tuple(self.dilation, "dilation"))
+        for name, least in (("kernel_size", 1), ("stride", 1), ("padding", 0), ("dilation", 1)):
+            object.__setattr__(self, name, _extents(getattr(self, name), name, least))
+
+    @classmethod
+    def normalization(cls, *, family: str, channels: int, role: str | None = None) -> OperatorDescriptor:
+        """A shape-preserving per-channel operator (GroupNorm, GRN)."""
+        return cls(family=family, direction="regular", in_channels=channels, out_channels=channels, role=role)
+
+    @classmethod
+    def convolution(cls, *, family: str, direction: str, in_channels: int, out_channels: int,
+                    kernel_size: tuple[int, ...], stride: tuple[int, ...], padding: tuple[int, ...],
+                    dilation: tuple[int, ...], groups: int, role: str | None = None) -> OperatorDescriptor:
+        return cls(family=family, direction=direction, in_channels=in_channels, out_channels=out_channels,
+                   kernel_size=kernel_size, stride=stride, padding=padding, dilation=dilation, groups=groups,
+                   role=role)
+
+    @property
+    def is_convolution(self) -> bool:
+        return self.kernel_size is not None
 
     @property
     def signature(self) -> tuple[object, ...]:
         return (self.family, self.direction, self.in_channels, self.out_channels, self.kernel_size, self.stride)
 
     def to_primitive(self) -> dict[str, object]:
-        value = asdict(self)
-        for name in ("kernel_size", "stride", "padding", "dilation"):
-            if value[name] is not None:
-                value[name] = list(value[name])
-        return {name: item for name, item in value.items() if item is not None}
+        out: dict[str, object] = {}
+        for f in fields(self):
+            v = getattr(self, f.name)
+            if isinstance(v, tuple):
+                v = list(v)
+            if v is not None or self.is_convolution and f.name in _CONV_GEOMETRY + ("role",):
+                out[f.name] = v
+        return out
 
 
 @dataclass(frozen=True, slots=True)
 class ExecutionContext:
-    """Runtime facts used for implementation resolution."""
+    """The run-time facts a decision depends on: phase, device, dtype, shapes."""
 
     phase: ExecutionPhase
     device_type: str
@@ -107,17 +141,17 @@ class ExecutionContext:
     allow_approximate: bool = False
 
     def __post_init__(self) -> None:
-        if self.phase not in ("training", "inference", "export"):
-            raise ValueError(f"unknown phase {self.phase!r}")
-        if self.batch_size <= 0:
-            raise ValueError("batch_size must be positive")
+        if self.phase not in _PHASES:
+            raise ValueError(f"unknown phase {self.phase!r} (expected one of {', '.join(_PHASES)})")
+        if self.batch_size < 1:
+            raise ValueError(f"batch_size must be positive, got {self.batch_size}")
         if self.total_vram_bytes < 0:
-            raise ValueError("total_vram_bytes must be nonnegative")
-        object.__setattr__(self, "spatial_shape", _spatial_tuple(self.spatial_shape, "spatial_shape"))
+            raise ValueError("total_vram_bytes cannot be negative")
+        object.__setattr__(self, "spatial_shape", _extents(self.spatial_shape, "spatial_shape", 1))
         if self.sm is not None:
             sm = tuple(self.sm)
-            if len(sm) != 2 or any(item < 0 for item in sm):
-                raise ValueError("sm must contain two nonnegative integers")
+            if len(sm) != 2 or min(sm) < 0:
+                raise ValueError(f"sm must be a (major, minor) pair of non-negative integers, got {self.sm!r}")
             object.__setattr__(self, "sm", sm)
 
     @property
@@ -126,13 +160,13 @@ class ExecutionContext:
 
     @property
     def total_vram_gib(self) -> float:
-        return self.total_vram_bytes / 2**30
+        return self.total_vram_bytes / float(1 << 30)
 
     def to_primitive(self) -> dict[str, object]:
-        value = asdict(self)
-        value["spatial_shape"] = list(self.spatial_shape)
-        value["sm"] = None if self.sm is None else list(self.sm)
-        return value
+        out = {f.name: getattr(self, f.name) for f in fields(self)}
+        out["spatial_shape"] = list(self.spatial_shape)
+        out["sm"] = list(self.sm) if self.sm is not None else None
+        return out
 
 
 EligibilityGuard = Callable[[OperatorDescriptor, ExecutionContext, str], "str | None"]
@@ -140,6 +174,8 @@ EligibilityGuard = Callable[[OperatorDescriptor, ExecutionContext, str], "str | 
 
 @dataclass(frozen=True, slots=True)
 class ImplementationSpec:
+    """Static facts about one implementation id: what it covers and how exact it is."""
+
     identifier: str
     version: int
     families: tuple[str, ...]
@@ -148,60 +184,63 @@ class ImplementationSpec:
     export_safe: bool
 
     def __post_init__(self) -> None:
+        if not self.identifier:
+            raise ValueError("an implementation needs an identifier")
+        if self.version < 1:
+            raise ValueError(f"implementation {self.identifier!r}: version must be at least 1")
         object.__setattr__(self, "families", tuple(self.families))
         object.__setattr__(self, "phases", tuple(self.phases))
-        if not self.identifier or self.version <= 0:
-            raise ValueError("implementation identifier and version must be valid")
-        if not self.families or not self.phases:
-            raise ValueError("implementation families and phases must not be empty")
-        if self.equivalence not in ("exact", "numerical", "approximate"):
-            raise ValueError(f"unknown equivalence {self.equivalence!r}")
+        if not (self.families and self.phases):
+            raise ValueError(f"implementation {self.identifier!r} lists no families or no phases")
+        if self.equivalence not in _EQUIVALENCES:
+            raise ValueError(f"implementation {self.identifier!r}: unknown equivalence {self.equivalence!r}")
 
     def is_allowed(self, *, allow_approximate: bool, export: bool = False) -> bool:
-        return (self.equivalence != "approximate" or allow_approximate) and (not export or self.export_safe)
+        if export and not self.export_safe:
+            return False
+        return allow_approximate or self.equivalence != "approximate"
+
+
+class _Registration(NamedTuple):
+    spec: ImplementationSpec
+    eligibility: EligibilityGuard | None
+    execution_guards: tuple[str, ...]
 
 
 class ImplementationRegistry:
-    """Backend-independent registry keyed by stable public identifiers."""
+    """Implementation ids -> (spec, eligibility guard, execution guards)."""
 
     def __init__(self) -> None:
-        self._specs: dict[str, ImplementationSpec] = {}
-        self._eligibility: dict[str, EligibilityGuard | None] = {}
-        self._execution_guards: dict[str, tuple[str, ...]] = {}
+        self._entries: dict[str, _Registration] = {}
 
-    def register(
-        self,
-        spec: ImplementationSpec,
-        *,
-        eligibility: EligibilityGuard | None = None,
-        execution_guards: tuple[str, ...] = (),
-    ) -> None:
-        if spec.identifier in self._specs:
-            raise ValueError(f"implementation {spec.identifier!r} is already registered")
-        self._specs[spec.identifier] = spec
-        self._eligibility[spec.identifier] = eligibility
-        self._execution_guards[spec.identifier] = tuple(execution_guards)
+    def register(self, spec: ImplementationSpec, *, eligibility: EligibilityGuard | None = None,
+                 execution_guards: tuple[str, ...] = ()) -> None:
+        if spec.identifier in self._entries:
+            raise ValueError(f"duplicate implementation id {spec.identifier!r}")
+        self._entries[spec.identifier] = _Registration(spec, eligibility, tuple(execution_guards))
+
+    def _entry(self, identifier: str) -> _Registration:
+        entry = self._entries.get(identifier)
+        if entry is None:
+            raise ValueError(f"no implementation is registered as {identifier!r}")
+        return entry
 
     def resolve_metadata(self, identifier: str) -> ImplementationSpec:
-        try:
-            return self._specs[identifier]
-        except KeyError as error:
-            raise ValueError(f"unknown implementation {identifier!r}") from error
+        return self._entry(identifier).spec
 
-    def guard(self, identifier: str, descriptor: OperatorDescriptor, context: ExecutionContext, phase: str) -> str | None:
-        self.resolve_metadata(identifier)
-        guard = self._eligibility[identifier]
-        return None if guard is None else guard(descriptor, context, phase)
+    def guard(self, identifier: str, descriptor: OperatorDescriptor, context: ExecutionContext,
+              phase: str) -> str | None:
+        check = self._entry(identifier).eligibility
+        return check(descriptor, context, phase) if check is not None else None
 
     def execution_guards(self, identifier: str) -> tuple[str, ...]:
-        self.resolve_metadata(identifier)
-        return self._execution_guards[identifier]
+        return self._entry(identifier).execution_guards
 
     def __contains__(self, identifier: object) -> bool:
-        return identifier in self._specs
+        return identifier in self._entries
 
     def __iter__(self):
-        return iter(self._specs.values())
+        return (entry.spec for entry in self._entries.values())
 
 
 # --------------------------------------------------------------------------- eligibility

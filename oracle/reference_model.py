@@ -82,7 +82,9 @@ def targets_for(target: torch.Tensor, heads: list[torch.Tensor]) -> list[torch.T
 
 
 def loss_fn(heads: list[torch.Tensor], targets: list[torch.Tensor]) -> torch.Tensor:
-    return sum(F.cross_entropy(h.float(), t) for h, t in zip(heads, targets, strict=True)) / len(heads)
+    # fp64 heads stay fp64 (golden-vector checks); anything narrower is taken to fp32
+    return sum(F.cross_entropy(h if h.dtype == torch.float64 else h.float(), t)
+               for h, t in zip(heads, targets, strict=True)) / len(heads)
 
 
 class ReferenceTrainer:

@@ -158,7 +158,7 @@ def test_checkpointed_expansion_matches_stored():
 
 
 def test_config2_block_full_size_against_reference_path():
-    """MedNeXtBlock N=2, C=64, 64^3, R=4, k=5 under bf16
+    """The standalone-block workload: MedNeXtBlock N=2, C=64, 64^3, R=4, k=5 under bf16
     autocast, PyTorch default init from seed 0, input and upstream grad ~N(0,1).
     Compared with the same block run through the reference's pure-PyTorch path
     (native modules) in fp32 on the same GPU."""

@@ -144,7 +144,7 @@ def test_stride2_and_transpose(dtype, k, shape):
 
 
 def test_config1_fp32_full_size():
-    """N=1, C=32, 64^3, k=3, fp32, bias; weights ~N(0,1)/sqrt(27),
+    """The single depthwise-conv workload: N=1, C=32, 64^3, k=3, fp32, bias; weights ~N(0,1)/sqrt(27),
     seed 0; y, grad_input, grad_weight against F.conv3d autograd on CPU."""
     torch.manual_seed(0)
     x = torch.randn(1, 32, 64, 64, 64)

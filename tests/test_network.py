@@ -156,3 +156,75 @@ def test_checkpoint_config_validation():
     assert mx.CheckpointConfig(stages=(1, 0)).stages == (0, 1)
     with pytest.raises(ValueError):
         mx.mednext_base(in_channels=1, out_channels=3, optimization="autotune")
+
+
+# ---- public configuration API (the reference's tests/test_public_api.py:8-53 and
+# tests/optimization/test_descriptors.py, test_implementations.py pin these)
+def test_v1_config_downsample_ratios_follow_compatibility():
+    from mednext_accel_b200.network import get_mednext_v1_config
+
+    official = get_mednext_v1_config("base", in_channels=1, out_channels=3)
+    assert official.block_counts == (2,) * 9
+    assert official.expansion_ratios == (2, 3, 4, 4, 4, 4, 4, 3, 2)
+    assert official.downsample_expansion_ratios == (3, 4, 4, 4)
+    monai = get_mednext_v1_config("base", in_channels=1, out_channels=3, compatibility="monai")
+    assert monai.downsample_expansion_ratios == (2, 3, 4, 4)
+    with pytest.raises(ValueError, match="variant"):
+        get_mednext_v1_config("huge", in_channels=1, out_channels=3)
+
+
+@pytest.mark.parametrize("stages, message", [((0, 0), "duplicates"), ((-1,), "between 0 and 4"),
+                                             ((5,), "between 0 and 4"), ((1.0,), "integers")])
+def test_checkpoint_stages_are_validated(stages, message):
+    with pytest.raises(ValueError, match=message):
+        mx.CheckpointConfig(stages=stages)
+
+
+def test_checkpoint_config_canonicalises_and_reports_style():
+    cfg = mx.CheckpointConfig(style="block", stages=(2, 0, 1))
+    assert cfg.stages == (0, 1, 2) and cfg.checkpoints_blocks and not cfg.checkpoints_expansion
+    assert cfg.includes(1) and not cfg.includes(3)
+    assert mx.CheckpointConfig().includes(4)
+    with pytest.raises(ValueError, match="style"):
+        mx.CheckpointConfig(style="whole")
+
+
+def test_descriptor_validation_and_primitive_form():
+    from mednext_accel_b200.optimization import ExecutionContext, OperatorDescriptor
+
+    with pytest.raises(ValueError, match="kernel_size"):
+        OperatorDescriptor.convolution(family="depthwise_conv3d", direction="regular", in_channels=4,
+                                       out_channels=4, kernel_size=(0, 0, 0), stride=(1, 1, 1),
+                                       padding=(1, 1, 1), dilation=(1, 1, 1), groups=4)
+    with pytest.raises(ValueError, match="geometry"):
+        OperatorDescriptor("depthwise_conv3d", "regular", 4, 4, kernel_size=(3, 3, 3))
+    norm = OperatorDescriptor.normalization(family="global_response_norm3d", channels=96,
+                                            role="encoder_stages.0.0.grn")
+    assert norm.to_primitive() == {"family": "global_response_norm3d", "direction": "regular",
+                                   "in_channels": 96, "out_channels": 96, "role": "encoder_stages.0.0.grn"}
+    conv = OperatorDescriptor.convolution(family="depthwise_conv3d", direction="regular", in_channels=4,
+                                          out_channels=4, kernel_size=[3, 3, 3], stride=(1, 1, 1),
+                                          padding=(1, 1, 1), dilation=(1, 1, 1), groups=4)
+    assert conv.kernel_size == (3, 3, 3)
+    assert conv.to_primitive()["kernel_size"] == [3, 3, 3] and conv.to_primitive()["role"] is None
+    with pytest.raises(ValueError, match="batch_size"):
+        ExecutionContext("training", "cpu", None, 0, "float32", 0, (8, 8, 8), "mednext_v1", "base", "none")
+    ctx = ExecutionContext("training", "cuda", (10, 0), 32 << 30, "bfloat16", 3, (128, 128, 128),
+                           "mednext_v1", "base", "all-expansion")
+    assert ctx.spatial_volume == 128**3 and ctx.total_vram_gib == 32
+
+
+def test_registry_rejects_duplicates_and_names_unknown_ids():
+    from mednext_accel_b200.optimization import (ImplementationRegistry, ImplementationSpec,
+                                                  default_implementation_registry)
+
+    reg = ImplementationRegistry()
+    spec = ImplementationSpec("reference", 1, ("pointwise_conv3d",), ("training",), "exact", True)
+    reg.register(spec)
+    with pytest.raises(ValueError, match="reference"):
+        reg.register(spec)
+    with pytest.raises(ValueError, match="missing_backend"):
+        reg.resolve_metadata("missing_backend")
+    approx = ImplementationSpec("gelu_tanh", 1, ("gelu",), ("inference",), "approximate", True)
+    assert not approx.is_allowed(allow_approximate=False) and approx.is_allowed(allow_approximate=True)
+    assert default_implementation_registry().resolve_metadata("triton_split_dw").identifier == "triton_split_dw"
