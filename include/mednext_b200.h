@@ -33,6 +33,8 @@
  *   mednext_pw_*          AdaptivePointwise3d._gemm / F.conv3d 1x1x1, ops/adaptive.py:174-200,
  *                         with the GroupNorm apply, exact GELU (models/blocks.py:32-44) and the
  *                         residual add (models/blocks.py:89-90) fused into prologue/epilogue
+ *   mednext_grn_*         the v2 Global Response Norm fused op mednext_accel::grn_forward /
+ *                         grn_backward, ops/_triton/grn.py:235-402 (formula ops/grn.py:16-29)
  */
 #ifndef MEDNEXT_B200_H
 #define MEDNEXT_B200_H
@@ -67,7 +69,8 @@ enum mednext_status {
   MEDNEXT_ERR_CUDA = 7,         /* a CUDA launch failed (see mednext_last_cuda_error) */
   MEDNEXT_ERR_DEVICE = 8,       /* current device is not sm_100 */
   MEDNEXT_ERR_SCRATCH_LIMIT = 9, /* shape needs more than MEDNEXT_DW_WGRAD_NOALLOC_MAX_SCRATCH */
-  MEDNEXT_ERR_UNSUPPORTED = 10   /* a fused entry point does not cover this shape: run the parts */
+  MEDNEXT_ERR_UNSUPPORTED = 10,  /* a fused entry point does not cover this shape: run the parts */
+  MEDNEXT_ERR_BAD_VALUE = 11     /* a scalar argument is out of range (e.g. eps not finite and > 0) */
 };
 
 /* Pointwise prologue applied to the activation operand while it is staged
@@ -378,6 +381,30 @@ typedef struct {
   int transpose;
 } mednext_cast_entry;
 int mednext_cast_params(const mednext_cast_entry* entries, int count, mednext_stream_t stream);
+
+/* ---------------- MedNeXt v2 Global Response Norm -------------------------
+ * x [n, c, spatial] contiguous (NCDHW with spatial = D*H*W), dtype float32,
+ * bfloat16 or float16; gamma, beta: [c] float32 (the (1, C, 1, 1, 1) parameters).
+ *   norm[n,c] = ||x[n,c,:]||_2,  denom[n] = sum_c norm[n,c] + eps,
+ *   y = x + gamma[c] * x * (norm[n,c] / denom[n]) + beta[c]   (fp32 math, one rounding)
+ * norm ([n*c] float32) and denom ([n] float32) are outputs of the forward and
+ * inputs of the backward.  Reductions run in a fixed order: deterministic.
+ * Replaces the fused op mednext_accel::grn_forward / grn_backward
+ * (ops/_triton/grn.py:235-290, 300-377), whose formula is ops/grn.py:16-29.
+ * The workspace (float32 partial sums) is shared by the forward and backward:
+ * mednext_grn_workspace_size() bytes, 4-byte aligned; 0 means invalid sizes. */
+size_t mednext_grn_workspace_size(int64_t n, int64_t c, int64_t spatial, int dtype);
+int mednext_grn_fwd(const void* x, const float* gamma, const float* beta, void* y, float* norm,
+                    float* denom, void* workspace, size_t workspace_bytes, int64_t n, int64_t c,
+                    int64_t spatial, float eps, int dtype, mednext_stream_t stream);
+/* dx = dy (1 + gamma r) + (norm > 0 ? x / norm : 0) dnorm, with
+ * dnorm[n,c] = (gamma[c] qx[n,c] - sum_j gamma[j] qx[n,j] r[n,j]) / denom[n],
+ * qx = sum_v dy x, r = norm / denom; dgamma[c] = sum_n qx r, dbeta[c] = sum_n sum_v dy
+ * ([c] float32 each, overwritten). */
+int mednext_grn_bwd(const void* dy, const void* x, const float* gamma, const float* norm,
+                    const float* denom, void* dx, float* dgamma, float* dbeta, void* workspace,
+                    size_t workspace_bytes, int64_t n, int64_t c, int64_t spatial, int dtype,
+                    mednext_stream_t stream);
 
 #ifdef __cplusplus
 }

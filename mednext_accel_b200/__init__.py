@@ -14,6 +14,13 @@ from .adaptive import (
     ModelOptimizationContext,
     install_adaptive_operators,
 )
+from .grn import (
+    AdaptiveGlobalResponseNorm3d,
+    GlobalResponseNorm3d,
+    fused_global_response_norm3d,
+    global_response_norm3d_reference,
+    install_adaptive_grn,
+)
 from .loss import cross_entropy
 from .network import (
     CheckpointConfig,
@@ -44,6 +51,11 @@ __version__ = "0.1.0"
 
 __all__ = [
     "AdaptiveDepthwise3d",
+    "AdaptiveGlobalResponseNorm3d",
+    "GlobalResponseNorm3d",
+    "fused_global_response_norm3d",
+    "global_response_norm3d_reference",
+    "install_adaptive_grn",
     "AdaptivePointwise3d",
     "CheckpointConfig",
     "ExecutionContext",

@@ -23,7 +23,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build_obj"
 LIB = PKG / "lib" / "libmednext_b200.so"
 UNITS = ("api.cu", "launch_dw_s1.cu", "launch_dw_s2.cu", "launch_gn.cu", "launch_pw.cu", "pw_fwd_bf16.cu", "pw_fwd_bf16_f32.cu",
-         "pw_fwd_f16.cu", "noalloc_dw_wgrad.cu", "params.cu", "loss.cu")
+         "pw_fwd_f16.cu", "noalloc_dw_wgrad.cu", "params.cu", "loss.cu", "grn.cu")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 

@@ -32,6 +32,7 @@ ERR_CUDA = 7
 ERR_DEVICE = 8
 ERR_SCRATCH_LIMIT = 9
 ERR_UNSUPPORTED = 10
+ERR_BAD_VALUE = 11
 
 PRO_NONE = 0
 PRO_GROUPNORM = 1
@@ -117,6 +118,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _P, _P, _INT, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _P],
     ),
     "mednext_cast_params": (_INT, [_P, _INT, _P]),
+    "mednext_grn_workspace_size": (_SZ, [_I64, _I64, _I64, _INT]),
+    "mednext_grn_fwd": (_INT, [_P, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _F, _INT, _P]),
+    "mednext_grn_bwd": (_INT, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _INT, _P]),
     "mednext_gn_bwd_from_partials": (
         _INT,
         [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _INT, _INT, _INT, _INT, _P],

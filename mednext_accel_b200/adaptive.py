@@ -345,7 +345,9 @@ def install_adaptive_operators(
     model_context: ModelOptimizationContext,
     _prefix: str = "",
 ) -> int:
-    """Install wrappers in place while retaining every Parameter object."""
+    """Install wrappers in place while retaining every Parameter object
+    (depthwise and pointwise convolutions, MedNeXt blocks, GRN layers)."""
+    from .grn import AdaptiveGlobalResponseNorm3d, GlobalResponseNorm3d
     from .network import MedNeXtBlock
 
     count = 0
@@ -358,6 +360,9 @@ def install_adaptive_operators(
             count += 1
         elif _depthwise_eligible(child):
             setattr(model, name, AdaptiveDepthwise3d(child, resolver, model_context, role=role))
+            count += 1
+        elif type(child) is GlobalResponseNorm3d:
+            setattr(model, name, AdaptiveGlobalResponseNorm3d(child, resolver, model_context, role))
             count += 1
         else:
             count += install_adaptive_operators(child, resolver=resolver, model_context=model_context, _prefix=role)

@@ -108,6 +108,7 @@ const char* mednext_status_string(int status) {
     case MEDNEXT_ERR_SCRATCH_LIMIT:
       return "shape needs more scratch than the built-in array of the no-allocation entry point holds";
     case MEDNEXT_ERR_UNSUPPORTED: return "the fused entry point does not cover this shape; run its parts";
+    case MEDNEXT_ERR_BAD_VALUE: return "a scalar argument is out of range";
     default: return "unknown status";
   }
 }

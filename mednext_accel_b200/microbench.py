@@ -90,10 +90,33 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
     }
 
 
+def _grn_cases(dev: torch.device) -> dict[str, tuple]:
+    """GRN at the v2 Wide stage-0 expansion: [2, 192, 160^3] bf16 (3.1 GB per tensor).
+    Algorithmic bytes: forward x + y, backward dy + x + dx.  The kernels take two
+    passes over x (its per-channel norms are needed before any output), so the
+    forward moves 1.5x and the backward 5/3x the algorithmic bytes."""
+    from .grn import grn_backward, grn_forward
+
+    shape = (2, 192, 160, 160, 160)
+    x = torch.randn(shape, device=dev, dtype=torch.bfloat16)
+    dy = torch.randn(shape, device=dev, dtype=torch.bfloat16)
+    gamma = torch.randn((1, 192, 1, 1, 1), device=dev)
+    beta = torch.randn((1, 192, 1, 1, 1), device=dev)
+    _, norm, den = grn_forward(x, gamma, beta, 1e-6)
+    nbytes = x.numel() * 2
+    return {
+        "grn fwd 2x192x160^3": (lambda: grn_forward(x, gamma, beta, 1e-6), 2 * nbytes),
+        "grn bwd 2x192x160^3": (lambda: grn_backward(dy, x, gamma, norm, den), 3 * nbytes),
+    }
+
+
 def run(patterns: list[str], reps: int = 10, warmup: int = 3) -> dict[str, dict]:
     dev = torch.device("cuda", torch.cuda.current_device())
     results = {}
-    for name, (fn, nbytes) in _cases(dev).items():
+    cases = _cases(dev)
+    if not patterns or any("grn" in p for p in patterns):
+        cases.update(_grn_cases(dev))
+    for name, (fn, nbytes) in cases.items():
         if patterns and not any(p in name for p in patterns):
             continue
         for _ in range(warmup):

@@ -312,6 +312,16 @@ def _block_eligibility(descriptor: OperatorDescriptor, context: ExecutionContext
     return None
 
 
+def _grn_eligibility(descriptor: OperatorDescriptor, context: ExecutionContext, phase: str) -> str | None:
+    if context.phase != "training" or phase != "training":
+        return "implementation requires training"
+    if context.device_type != "cuda":
+        return "implementation requires CUDA"
+    if context.dtype not in ("float16", "bfloat16", "float32"):
+        return "implementation does not support this dtype"
+    return None
+
+
 DEPTHWISE_PHASES = ("forward", "backward_input", "backward_weight", "backward_bias")
 
 
@@ -344,6 +354,10 @@ def default_implementation_registry() -> ImplementationRegistry:
          _depthwise_eligibility("transpose"), conv_guards),
         ("triton_downsample_dx", ("depthwise_conv3d",), ("backward_input",), "numerical", False,
          _depthwise_eligibility("downsample"), conv_guards),
+        ("sm100_grn", ("global_response_norm3d",), ("training",), "numerical", False, _grn_eligibility,
+         ("grad_enabled", "rank_5", "contiguous")),
+        ("triton_fused_grn", ("global_response_norm3d",), ("training",), "numerical", False, _grn_eligibility,
+         ("grad_enabled", "rank_5", "contiguous")),
         ("gelu_tanh", ("gelu",), ("inference",), "approximate", True, None, ()),
     )
     for identifier, families, phases, equivalence, export_safe, eligibility, guards in definitions:
@@ -363,6 +377,7 @@ LEGACY_ALIASES: Mapping[str, str] = MappingProxyType(
         "triton_split_dw": "sm100_depthwise",
         "triton_transpose_split_dw": "sm100_depthwise_transpose",
         "triton_downsample_dx": "sm100_depthwise_downsample",
+        "triton_fused_grn": "sm100_grn",
     }
 )
 
@@ -424,6 +439,7 @@ SM100_TABLE: tuple[TableRow, ...] = (
     TableRow("depthwise-downsample", "depthwise_conv3d", "downsample", "sm100_depthwise_downsample"),
     TableRow("depthwise-transpose", "depthwise_conv_transpose3d", "transpose", "sm100_depthwise_transpose"),
     TableRow("pointwise", "pointwise_conv3d", "regular", "sm100_pointwise"),
+    TableRow("grn", "global_response_norm3d", "regular", "sm100_grn"),
 )
 
 

@@ -12,6 +12,8 @@
  *   GroupNorm(C, C) ..................... models/blocks.py:74 (torch.nn.GroupNorm, biased variance)
  *   exact GELU .......................... models/blocks.py:32-41 (F.gelu approximate="none")
  *   1x1x1 convolution ................... ops/adaptive.py:174-188 (per-sample W @ X + b)
+ *   Global Response Norm (v2) ........... ops/grn.py:16-29 (forward formula),
+ *                                         ops/_triton/grn.py:150-232 (backward: channel coupling)
  * All tensors are contiguous NCDHW double arrays; sums are plain sequential
  * loops in fp64.
  */
@@ -295,6 +297,69 @@ void oracle_pointwise_bwd(const double* dy, const double* x, const double* wt, d
       for (i64 n = 0; n < N; ++n)
         for (i64 v = 0; v < vol; ++v) s += dy[(n * Cout + j) * vol + v];
       db[j] = s;
+    }
+  }
+}
+
+/* MedNeXt v2 GRN forward, ops/grn.py:16-29:
+ *   norm[n,c] = ||x[n,c,:]||_2,  den[n] = sum_c norm[n,c] + eps,
+ *   y = x + gamma[c] * x * (norm[n,c] / den[n]) + beta[c].
+ * norm and den are also returned (the saved statistics of the backward). */
+void oracle_grn_fwd(const double* x, const double* gamma, const double* beta, double* y, double* norm, double* den,
+                    i64 N, i64 C, i64 V, double eps) {
+  for (i64 n = 0; n < N; ++n) {
+    double total = 0.0;
+    for (i64 c = 0; c < C; ++c) {
+      const double* row = x + (n * C + c) * V;
+      double ss = 0.0;
+      for (i64 v = 0; v < V; ++v) ss += row[v] * row[v];
+      norm[n * C + c] = sqrt(ss);
+      total += norm[n * C + c];
+    }
+    den[n] = total + eps;
+    for (i64 c = 0; c < C; ++c) {
+      const double r = norm[n * C + c] / den[n];
+      const double* row = x + (n * C + c) * V;
+      double* out = y + (n * C + c) * V;
+      for (i64 v = 0; v < V; ++v) out[v] = row[v] + gamma[c] * row[v] * r + beta[c];
+    }
+  }
+}
+
+/* GRN backward (the derivative of oracle_grn_fwd; the reference's split form is
+ * ops/_triton/grn.py:150-232):
+ *   qx[c] = sum_v dy x,  q[c] = sum_v dy,  h[c] = gamma[c] qx[c],
+ *   dnorm[c] = (h[c] - sum_j h[j] norm[j] / den) / den,
+ *   dx = dy (1 + gamma[c] norm[c] / den) + (norm[c] > 0 ? x / norm[c] : 0) dnorm[c],
+ *   dgamma[c] = sum_n qx[n,c] norm[n,c] / den[n],  dbeta[c] = sum_n q[n,c]. */
+void oracle_grn_bwd(const double* dy, const double* x, const double* gamma, const double* norm, const double* den,
+                    double* dx, double* dgamma, double* dbeta, i64 N, i64 C, i64 V) {
+  for (i64 c = 0; c < C; ++c) dgamma[c] = dbeta[c] = 0.0;
+  for (i64 n = 0; n < N; ++n) {
+    double coupled = 0.0;
+    for (i64 c = 0; c < C; ++c) {
+      const double* xr = x + (n * C + c) * V;
+      const double* gr = dy + (n * C + c) * V;
+      double qx = 0.0, q = 0.0;
+      for (i64 v = 0; v < V; ++v) {
+        qx += gr[v] * xr[v];
+        q += gr[v];
+      }
+      const double r = norm[n * C + c] / den[n];
+      coupled += gamma[c] * qx * r;
+      dgamma[c] += qx * r;
+      dbeta[c] += q;
+    }
+    for (i64 c = 0; c < C; ++c) {
+      const double* xr = x + (n * C + c) * V;
+      const double* gr = dy + (n * C + c) * V;
+      double qx = 0.0;
+      for (i64 v = 0; v < V; ++v) qx += gr[v] * xr[v];
+      const double g = norm[n * C + c];
+      const double dnorm = (gamma[c] * qx - coupled) / den[n];
+      const double scale = 1.0 + gamma[c] * (g / den[n]);
+      double* out = dx + (n * C + c) * V;
+      for (i64 v = 0; v < V; ++v) out[v] = gr[v] * scale + (g > 0.0 ? xr[v] / g : 0.0) * dnorm;
     }
   }
 }

@@ -6,7 +6,8 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
 
 Layers:
 * ``mednext_oracle.c``: fp64 loop restatement of depthwise conv (stride 1,
-  stride 2, transpose), GroupNorm, exact GELU and 1x1 convolution, each citing
+  stride 2, transpose), GroupNorm, exact GELU, 1x1 convolution and the v2
+  Global Response Norm, each citing
   the reference file:line it follows; compiled with gcc into ``_build/``.
 * :func:`block_reference`: the reference ``MedNeXtBlock`` forward and backward
   (models/blocks.py:82-91) composed from those primitives, with the roundings
@@ -66,6 +67,8 @@ def lib() -> ctypes.CDLL:
             "oracle_gelu_grad": [_D, _D, _I],
             "oracle_pointwise_fwd": [_D, _D, _D, _D, _I, _I, _I, _I],
             "oracle_pointwise_bwd": [_D, _D, _D, _D, _D, _D, _I, _I, _I, _I],
+            "oracle_grn_fwd": [_D, _D, _D, _D, _D, _D, _I, _I, _I, ctypes.c_double],
+            "oracle_grn_bwd": [_D, _D, _D, _D, _D, _D, _D, _D, _I, _I, _I],
         }
         for name, args in sig.items():
             fn = getattr(_lib, name)
@@ -217,6 +220,32 @@ def gelu_grad(x):
     g = np.empty_like(x)
     lib().oracle_gelu_grad(_p(x), _p(g), x.size)
     return g
+
+
+def grn_fwd(x, gamma, beta, eps=1e-6):
+    """MedNeXt v2 GRN forward (ops/grn.py:16-29) in fp64: (y, norm [N, C], den [N])."""
+    x = _f64(x)
+    n, c = x.shape[:2]
+    vol = int(np.prod(x.shape[2:]))
+    y = np.empty_like(x)
+    norm = np.empty((n, c))
+    den = np.empty((n,))
+    lib().oracle_grn_fwd(_p(x), _p(_f64(gamma).reshape(-1)), _p(_f64(beta).reshape(-1)), _p(y), _p(norm), _p(den),
+                         n, c, vol, float(eps))
+    return y, norm, den
+
+
+def grn_bwd(dy, x, gamma, norm, den):
+    """GRN backward in fp64: (dx, dgamma [C], dbeta [C])."""
+    dy, x = _f64(dy), _f64(x)
+    n, c = x.shape[:2]
+    vol = int(np.prod(x.shape[2:]))
+    dx = np.empty_like(x)
+    dg = np.empty((c,))
+    db = np.empty((c,))
+    lib().oracle_grn_bwd(_p(dy), _p(x), _p(_f64(gamma).reshape(-1)), _p(_f64(norm)), _p(_f64(den)), _p(dx), _p(dg),
+                         _p(db), n, c, vol)
+    return dx, dg, db
 
 
 def pointwise_fwd(x, w, b):

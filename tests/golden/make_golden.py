@@ -21,6 +21,12 @@ inputs with the shapes of the reference's tests:
 * ``small_model.npz`` — seed-0 ``mednext_small(base_channels=4)`` float64
   forward/backward on a 32^3 input: the five deep-supervision heads, the
   mean cross-entropy loss and the stem/head grads.
+* ``grn.npz``        — the v2 Global Response Norm, ``GlobalResponseNorm3d``
+  (ops/grn.py:16-46) with seeded gamma/beta, forward and autograd backward in
+  float64 on [2,6,5,6,7] (one all-zero channel: the zero-norm case) and on
+  [1,3,4,4,4].
+
+``python tests/golden/make_golden.py grn`` writes only the named fixtures.
 """
 
 from __future__ import annotations
@@ -145,16 +151,50 @@ def small_model() -> dict[str, np.ndarray]:
     return out
 
 
+def grn() -> dict[str, np.ndarray]:
+    from mednext_accel.ops.grn import GlobalResponseNorm3d
+
+    out: dict[str, np.ndarray] = {}
+    for case, shape in enumerate(((2, 6, 5, 6, 7), (1, 3, 4, 4, 4))):
+        gen = torch.Generator().manual_seed(100 + case)
+        layer = GlobalResponseNorm3d(shape[1]).double()
+        with torch.no_grad():
+            layer.gamma.copy_(torch.randn(layer.gamma.shape, generator=gen, dtype=torch.float64))
+            layer.beta.copy_(torch.randn(layer.beta.shape, generator=gen, dtype=torch.float64))
+        x = torch.randn(shape, generator=gen, dtype=torch.float64)
+        if case == 0:
+            x[1, 2].zero_()  # a channel with zero norm
+        x.requires_grad_()
+        dy = torch.randn(shape, generator=gen, dtype=torch.float64)
+        y = layer(x)
+        y.backward(dy)
+        for name, value in (("x", x), ("gamma", layer.gamma), ("beta", layer.beta), ("dy", dy), ("y", y),
+                            ("dx", x.grad), ("dgamma", layer.gamma.grad), ("dbeta", layer.beta.grad)):
+            out[f"{case}/{name}"] = _np(value)
+    return out
+
+
 def main() -> int:
     try:
         import mednext_accel  # noqa: F401
     except ImportError:
         print("put the reference src/ directory on PYTHONPATH", file=sys.stderr)
         return 2
-    np.savez_compressed(OUT / "depthwise.npz", **depthwise())
-    np.savez_compressed(OUT / "blocks.npz", **blocks())
-    (OUT / "model_init.json").write_text(json.dumps(model_init()))
-    np.savez_compressed(OUT / "small_model.npz", **small_model())
+    wanted = set(sys.argv[1:])
+
+    def want(name: str) -> bool:
+        return not wanted or name in wanted
+
+    if want("depthwise"):
+        np.savez_compressed(OUT / "depthwise.npz", **depthwise())
+    if want("blocks"):
+        np.savez_compressed(OUT / "blocks.npz", **blocks())
+    if want("model_init"):
+        (OUT / "model_init.json").write_text(json.dumps(model_init()))
+    if want("small_model"):
+        np.savez_compressed(OUT / "small_model.npz", **small_model())
+    if want("grn"):
+        np.savez_compressed(OUT / "grn.npz", **grn())
     print("wrote", sorted(p.name for p in OUT.iterdir()))
     return 0
 

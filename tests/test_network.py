@@ -228,3 +228,23 @@ def test_registry_rejects_duplicates_and_names_unknown_ids():
     approx = ImplementationSpec("gelu_tanh", 1, ("gelu",), ("inference",), "approximate", True)
     assert not approx.is_allowed(allow_approximate=False) and approx.is_allowed(allow_approximate=True)
     assert default_implementation_registry().resolve_metadata("triton_split_dw").identifier == "triton_split_dw"
+
+
+def test_grn_layer_reference_formula_and_argument_contract():
+    """GRN starts as the identity (zero gamma/beta, ops/grn.py:32-46) and the fused
+    entry point rejects what the reference's rejects, with its messages
+    (ops/_triton/grn.py:416-437, tests/ops/test_grn_triton.py:116)."""
+    layer = mx.GlobalResponseNorm3d(6)
+    x = torch.randn(2, 6, 3, 4, 5)
+    assert torch.equal(layer(x), x)
+    assert tuple(layer.gamma.shape) == (1, 6, 1, 1, 1) and tuple(layer.beta.shape) == (1, 6, 1, 1, 1)
+    with pytest.raises(ValueError, match="GRN expects an NCDHW tensor"):
+        mx.global_response_norm3d_reference(torch.randn(2, 6, 3), layer.gamma, layer.beta)
+    with pytest.raises(ValueError, match="channels"):
+        mx.GlobalResponseNorm3d(0)
+    with pytest.raises(ValueError, match="eps"):
+        mx.GlobalResponseNorm3d(4, eps=float("nan"))
+    with pytest.raises(ValueError, match="^fused GRN requires CUDA tensors$"):
+        mx.fused_global_response_norm3d(x, layer.gamma, layer.beta)
+    with pytest.raises(ValueError, match="rank-5"):
+        mx.fused_global_response_norm3d(torch.randn(2, 6, 3), layer.gamma, layer.beta)

@@ -90,3 +90,17 @@ def test_gelu_grad_matches_finite_difference():
     h = 1e-6
     fd = (orc.gelu(x + h) - orc.gelu(x - h)) / (2 * h)
     np.testing.assert_allclose(orc.gelu_grad(x), fd, rtol=1e-6, atol=1e-8)
+
+
+def test_grn_oracle_matches_reference(golden):
+    """The v2 GRN restatement against the reference's GlobalResponseNorm3d forward and
+    autograd backward (tests/golden/grn.npz), zero-norm channel included."""
+    fx = golden("grn.npz")
+    for case in (0, 1):
+        g = lambda k: fx[f"{case}/{k}"]  # noqa: E731
+        y, norm, den = orc.grn_fwd(g("x"), g("gamma"), g("beta"), 1e-6)
+        np.testing.assert_allclose(y, g("y"), rtol=1e-12, atol=1e-12)
+        dx, dgamma, dbeta = orc.grn_bwd(g("dy"), g("x"), g("gamma"), norm, den)
+        np.testing.assert_allclose(dx, g("dx"), rtol=1e-11, atol=1e-12)
+        np.testing.assert_allclose(dgamma, g("dgamma").reshape(-1), rtol=1e-11, atol=1e-12)
+        np.testing.assert_allclose(dbeta, g("dbeta").reshape(-1), rtol=1e-11, atol=1e-12)
