@@ -269,6 +269,54 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
+// 16 lanes x 16 consecutive 32-bit columns in the MMA-fragment layout: thread t
+// gets r[0..1] = (lane base + t/4, columns 2(t%4), 2(t%4)+1), r[2..3] = (lane
+// base + 8 + t/4, the same columns), r[4..7] = the same at columns + 8.  The lane
+// base must lie in the warp's own 32-lane quarter.  Followed by tmem_ld_wait().
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                 "=r"(r[7])
+               : "r"(taddr));
+}
+// Four 8x8 16-bit matrices from shared memory, transposed: lanes 8m..8m+7 give
+// the addresses of matrix m's eight 16-byte rows; thread t receives in q[m]
+// (row 2(t%4), column t/4) in the low half and (row 2(t%4)+1, column t/4) in the high.
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t* q) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3])
+               : "r"(addr));
+}
+// The inverse: thread t's q[m] low/high halves land at (row 2(t%4) / 2(t%4)+1,
+// column t/4) of matrix m, whose row addresses lanes 8m..8m+7 give.
+__device__ __forceinline__ void stsm_x4_trans(uint32_t addr, const uint32_t* q) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(q[0]),
+               "r"(q[1]), "r"(q[2]), "r"(q[3])
+               : "memory");
+}
+// Two 16-bit values (low, high halves) <-> a float pair.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t v);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+  return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&v));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float2 v);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float2 v) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(v.x, v.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float2 v) {
+  const __half2 h = __floats2half2_rn(v.x, v.y);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

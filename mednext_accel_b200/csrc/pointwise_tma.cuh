@@ -198,6 +198,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   static_assert(!(FW_GELU && FW_GN), "one fused weight-grad operand");
   constexpr bool MLP = EPI >= 0 && (EPI & kEpiMlp) != 0;
   static_assert(!(MLP && FW), "one fused second GEMM");
+  // 16-bit outputs take the fragment epilogue (swizzled operand and staging tiles);
+  // float32 outputs the one-voxel-per-lane epilogue (unswizzled tiles)
+  constexpr bool kFrag = sizeof(TY) == 2;
   // fused weight grad: two g tiles (one per epilogue group) after the staging buffers
   uint8_t* gbuf = ringStg + (size_t)FwdEpi<PRO>::warps * 2 * kStgBytes;
   gbuf += ((1024u - (smem_u32(gbuf) & 1023u)) & 1023u);
@@ -547,6 +550,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int epi = EPI >= 0 ? EPI : p.epilogue;
     uint8_t* stg0 = ringStg + (size_t)ew * 2 * kStgBytes;
     uint32_t nstored = 0;
+    // fragment epilogue: lane L gives the row address of 8x8 matrix L / 8 = (x, vh) =
+    // (L / 16, L / 8 % 2), row L % 8; t % 4 selects the thread's channel pair
+    const int f_rr = lane & 7, f_x = (lane >> 4) & 1, f_vh = (lane >> 3) & 1, tq = lane & 3;
     for (int i = tg; i < ntile_local; i += tgs) {
       int s, j0, mt;
       long long v0;
@@ -561,12 +567,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const TA* auxt = reinterpret_cast<const TA*>(ringAux + (size_t)e * cfg.aux_bytes + (vl >> 6) * (cfg.aux_bytes / 2)) + (vl & 63);
       const TY* rest = reinterpret_cast<const TY*>(ringRes + (size_t)e * cfg.res_bytes + (vl >> 6) * (cfg.res_bytes / 2)) + (vl & 63);
       const uint32_t d_tmem = tmem + (uint32_t)acc * ncols + ((uint32_t)(q4 * 32) << 16);
+      const uint32_t aux_u32 = smem_u32(ringAux + (size_t)e * cfg.aux_bytes);
+      const uint32_t res_u32 = smem_u32(ringRes + (size_t)e * cfg.res_bytes);
       // fused weight grad: this group's g tile (voxel vl's column of box vl / 64), free
       // again once the weight-grad MMAs of the group's previous tile have read it
       // g-tile addresses of this lane's voxel in rows 8q + k (k < 8): the K-major
       // 128-byte swizzle XORs the 16-byte chunk index with k
       uint32_t gx[8];
-      if constexpr (FW || MLP) {
+      if constexpr ((FW || MLP) && !kFrag) {
         const uint32_t gcol = smem_u32(gbuf + tg * kFwGBytes + (vl >> 6) * 16384 + (vl & 7) * 2);
         const int gchunk = (vl & 63) >> 3;
 #pragma unroll
@@ -577,103 +585,268 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           break;
       }
       for (int c0 = kPwCW * cg; c0 < BN; c0 += kPwCW * kGroups) {
-        uint32_t r[kPwCW];
-        tmem_ld16(d_tmem + (uint32_t)c0, r);
-        // per-column constants: lane l < 16 holds column c0 + l, broadcast with shuffles
-        const int jc = j0 + c0 + lane;
-        const bool jok = lane < kPwCW && jc < p.cout;
-        const float bias_l = ((epi & MEDNEXT_EPI_BIAS) && jok) ? __ldg(p.bias + jc) : 0.f;
-        float mean_l = 0.f, rstd_l = 0.f;
-        if ((epi & MEDNEXT_EPI_GN_BWD_STATS) && jok) {
-          mean_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc));
-          rstd_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc) + 1);
-        }
-        // fused weight grad after a GroupNorm: g = GroupNorm(aux) = aux * ca + cb, with the
-        // same coefficients (and rounding) as the weight-grad kernel's GroupNorm prologue
-        float ca_l = 0.f, cb_l = 0.f;
-        if constexpr (FW_GN) {
-          if (jok) {
-            ca_l = rstd_l * __ldg(p.pro_gamma + jc);
-            cb_l = __ldg(p.pro_beta + jc) - mean_l * ca_l;
-          }
-        }
-        // staging buffer: wait until the store issued two chunks ago has read it
-        TY* stg = reinterpret_cast<TY*>(stg0 + (nstored & 1) * kStgBytes);
-        if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-        tmem_ld_wait();
-        float s1[kPwCW], s2[kPwCW];
-        float gg[kPwCW];  // GELU'(aux) of the chunk's columns, in pairs
-        // g row c0 + jj of this lane's voxel (rows past cout keep their zeros / ones)
-        const bool gfull = c0 + kPwCW <= p.cout;
-        auto gstore = [&](int jj, float v) {
-          if (gfull || c0 + jj < p.cout) {
-            const TA b = from_acc<TA>(v);
-            st_shared_b16(gx[jj & 7] + (uint32_t)(((c0 >> 3) + (jj >> 3)) * 1024), *reinterpret_cast<const uint16_t*>(&b));
-          }
-        };
-        if constexpr (FW_GELU) {
-          // GELU(aux) as well, from the same Phi: into the g tile (channels past cout keep their zeros / ones)
+        if constexpr (kFrag) {
+          // ---- fragment epilogue (16-bit outputs): thread t holds voxels t/4 (+8, +16,
+          // +24) and channel pairs 8x + 2(t%4) of the chunk; auxiliary tiles come in and
+          // the result goes out through 8x8 transposes (ldmatrix / stmatrix .trans) on
+          // swizzled tiles, so every shared-memory access moves 16 bytes per lane.
+          uint32_t r[16];
+          tmem_ld_16x256b_x2(d_tmem + (uint32_t)c0, r);
+          tmem_ld_16x256b_x2(d_tmem + (16u << 16) + (uint32_t)c0, r + 8);
+          const int jr = c0 + 8 * f_x + f_rr;  // this lane's ldmatrix / stmatrix row (channel)
+          uint32_t ax[8], rs[8];
+          if (has_aux) {
 #pragma unroll
-          for (int jj = 0; jj < kPwCW; jj += 2) {
-            float2 gv;
-            const float2 g = gelu_grad2_and_gelu(
-                make_float2(to_acc<TA>(auxt[(c0 + jj) * 64]), to_acc<TA>(auxt[(c0 + jj + 1) * 64])), gv);
-            gg[jj] = g.x;
-            gg[jj + 1] = g.y;
-            gstore(jj, gv.x);
-            gstore(jj + 1, gv.y);
+            for (int h = 0; h < 2; ++h) {
+              const int vt = q4 * 32 + 16 * h + 8 * f_vh;
+              ldsm_x4_trans(aux_u32 + (uint32_t)((vt >> 6) * (cfg.aux_bytes / 2) + jr * 128 +
+                                                 ((((vt & 63) >> 3) ^ (jr & 7)) << 4)),
+                            ax + 4 * h);
+            }
           }
-        } else if (epi & MEDNEXT_EPI_GELU_GRAD) {
+          if (epi & MEDNEXT_EPI_RESIDUAL) {
 #pragma unroll
-          for (int jj = 0; jj < kPwCW; jj += 2) {
-            const float2 g = gelu_grad2(
-                make_float2(to_acc<TA>(auxt[(c0 + jj) * 64]), to_acc<TA>(auxt[(c0 + jj + 1) * 64])));
-            gg[jj] = g.x;
-            gg[jj + 1] = g.y;
+            for (int h = 0; h < 2; ++h) {
+              const int vt = q4 * 32 + 16 * h + 8 * f_vh;
+              ldsm_x4_trans(res_u32 + (uint32_t)((vt >> 6) * (cfg.res_bytes / 2) + jr * 128 +
+                                                 ((((vt & 63) >> 3) ^ (jr & 7)) << 4)),
+                            rs + 4 * h);
+            }
           }
-        }
+          // per-channel constants of this thread's channels j0 + c0 + 8x + 2(t%4) + {0, 1}
+          float2 bias2[2], mean2[2], rstd2[2], ca2[2], cb2[2];
 #pragma unroll
-        for (int jj = 0; jj < kPwCW; ++jj) {
-          const int jl = c0 + jj;
-          float a = __uint_as_float(r[jj]);
-          if (epi & MEDNEXT_EPI_BIAS) a += __shfl_sync(0xffffffffu, bias_l, jj);
-          if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_RESIDUAL)) a = to_acc<TA>(from_acc<TA>(a));
-          float ax = 0.f;
-          if (epi & MEDNEXT_EPI_GN_BWD_STATS) ax = to_acc<TA>(auxt[jl * 64]);
-          if constexpr (FW_GN)
-            gstore(jj, fmaf(ax, __shfl_sync(0xffffffffu, ca_l, jj), __shfl_sync(0xffffffffu, cb_l, jj)));
-          if (epi & MEDNEXT_EPI_GELU_GRAD) a *= gg[jj];
-          if (epi & MEDNEXT_EPI_RESIDUAL) a += (float)to_acc<TY>(rest[jl * 64]);
-          const TY o = from_acc<TY>((typename Elem<TY>::Acc)a);
-          stg[jj * 32 + lane] = o;
-          if constexpr (MLP) gstore(jj, (float)to_acc<TY>(o));  // u as stored; GELU follows in place
+          for (int x = 0; x < 2; ++x) {
+            const int jc = j0 + c0 + 8 * x + 2 * tq;
+            const bool ok0 = jc < p.cout, ok1 = jc + 1 < p.cout;
+            bias2[x] = make_float2(0.f, 0.f);
+            mean2[x] = rstd2[x] = ca2[x] = cb2[x] = make_float2(0.f, 0.f);
+            if (epi & MEDNEXT_EPI_BIAS)
+              bias2[x] = make_float2(ok0 ? __ldg(p.bias + jc) : 0.f, ok1 ? __ldg(p.bias + jc + 1) : 0.f);
+            if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
+              const float* st = p.epi_stats + 2 * ((size_t)s * p.cout + jc);
+              mean2[x] = make_float2(ok0 ? __ldg(st) : 0.f, ok1 ? __ldg(st + 2) : 0.f);
+              rstd2[x] = make_float2(ok0 ? __ldg(st + 1) : 0.f, ok1 ? __ldg(st + 3) : 0.f);
+            }
+            if constexpr (FW_GN) {
+              // g = GroupNorm(aux) = aux * ca + cb, the weight-grad kernel's prologue coefficients
+              if (ok0) {
+                ca2[x].x = rstd2[x].x * __ldg(p.pro_gamma + jc);
+                cb2[x].x = __ldg(p.pro_beta + jc) - mean2[x].x * ca2[x].x;
+              }
+              if (ok1) {
+                ca2[x].y = rstd2[x].y * __ldg(p.pro_gamma + jc + 1);
+                cb2[x].y = __ldg(p.pro_beta + jc + 1) - mean2[x].y * ca2[x].y;
+              }
+            }
+          }
+          // staging buffer: wait until the store issued two chunks ago has read it
+          const uint32_t stg_u32 = smem_u32(stg0 + (nstored & 1) * kStgBytes);
+          if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          tmem_ld_wait();
+          uint32_t out[8], gpk[8];
+          float2 st1[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+          float2 st2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {  // pair k = (h, x, vh) = (k / 4, k / 2 % 2, k % 2)
+            const int x = (k >> 1) & 1;
+            float2 a = make_float2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+            if (epi & MEDNEXT_EPI_BIAS) a = make_float2(a.x + bias2[x].x, a.y + bias2[x].y);
+            if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_RESIDUAL)) a = unpack2<TA>(pack2<TA>(a));
+            float2 axv = make_float2(0.f, 0.f);
+            if (has_aux) axv = unpack2<TA>(ax[k]);
+            if constexpr (FW_GN)
+              gpk[k] = pack2<TA>(make_float2(fmaf(axv.x, ca2[x].x, cb2[x].x), fmaf(axv.y, ca2[x].y, cb2[x].y)));
+            if constexpr (FW_GELU) {
+              float2 gv;
+              const float2 g = gelu_grad2_and_gelu(axv, gv);
+              gpk[k] = pack2<TA>(gv);
+              a = make_float2(a.x * g.x, a.y * g.y);
+            } else if (epi & MEDNEXT_EPI_GELU_GRAD) {
+              const float2 g = gelu_grad2(axv);
+              a = make_float2(a.x * g.x, a.y * g.y);
+            }
+            if (epi & MEDNEXT_EPI_RESIDUAL) {
+              const float2 rv = unpack2<TY>(rs[k]);
+              a = make_float2(a.x + rv.x, a.y + rv.y);
+            }
+            out[k] = pack2<TY>(a);
+            if constexpr (MLP) gpk[k] = out[k];  // u as stored; GELU follows in place
+            if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
+              // out-of-range voxels / channels hold exact zeros (zero-filled operands)
+              const float2 d = unpack2<TY>(out[k]);
+              st1[x] = make_float2(st1[x].x + d.x, st1[x].y + d.y);
+              st2[x] = make_float2(st2[x].x + d.x * (axv.x - mean2[x].x), st2[x].y + d.y * (axv.y - mean2[x].y));
+            }
+          }
+          {
+            const int R = 8 * f_x + f_rr;  // staging row (channel of the chunk), 64-byte rows, 64-byte swizzle
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              stsm_x4_trans(stg_u32 + (uint32_t)(R * 64 + ((((2 * h + f_vh) ^ (R >> 1)) & 3) << 4)), out + 4 * h);
+          }
+          if constexpr (FW || MLP) {
+            // g tile rows = this GEMM's output channels (rows past cout keep their zeros / ones)
+            const uint32_t gt = smem_u32(gbuf + tg * kFwGBytes);
+            if (c0 + kPwCW <= p.cout) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int vt = q4 * 32 + 16 * h + 8 * f_vh;
+                stsm_x4_trans(gt + (uint32_t)((vt >> 6) * 16384 + sw128_kmajor_off(jr, (vt & 63) >> 3)), gpk + 4 * h);
+              }
+            } else {
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                const int h = k >> 2, x = (k >> 1) & 1, vh = k & 1;
+                const int vt = q4 * 32 + 16 * h + 8 * vh + (lane >> 2);
+#pragma unroll
+                for (int e2 = 0; e2 < 2; ++e2) {
+                  const int row = c0 + 8 * x + 2 * tq + e2;
+                  if (row < p.cout)
+                    st_shared_b16(gt + (uint32_t)((vt >> 6) * 16384 + sw128_kmajor_off(row, (vt & 63) >> 3) +
+                                                  (vt & 7) * 2),
+                                  (uint16_t)(gpk[k] >> (16 * e2)));
+                }
+              }
+            }
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&mY, reinterpret_cast<void*>(stg0 + (nstored & 1) * kStgBytes), (int)v0 + q4 * 32, j0 + c0, s);
+            bulk_commit();
+          }
+          ++nstored;
           if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
-            // out-of-range voxels / channels hold exact zeros (zero-filled operands)
-            const float d = (float)to_acc<TY>(o);
-            s1[jj] = d;
-            s2[jj] = d * (ax - __shfl_sync(0xffffffffu, mean_l, jj));
+            // channel sums over the quarter's 32 voxels: the thread's four, then lanes
+            // with the same t % 4 (xor 4, 8, 16); lanes 0-3 hold channels 8x + 2t + {0, 1}
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+#pragma unroll
+              for (int o = 4; o < 32; o <<= 1) {
+                st1[x].x += __shfl_xor_sync(0xffffffffu, st1[x].x, o);
+                st1[x].y += __shfl_xor_sync(0xffffffffu, st1[x].y, o);
+                st2[x].x += __shfl_xor_sync(0xffffffffu, st2[x].x, o);
+                st2[x].y += __shfl_xor_sync(0xffffffffu, st2[x].y, o);
+              }
+              if (lane < 4) {
+                const int col = j0 + c0 + 8 * x + 2 * lane;
+                const size_t base = (((size_t)s * p.cout + col) * p.mtiles + mt) * 4 + q4;
+                if (col < p.cout) {
+                  GnBwdPartial gp;
+                  gp.s1 = (double)st1[x].x;
+                  gp.s2 = (double)(st2[x].x * rstd2[x].x);
+                  p.gn_part[base] = gp;
+                }
+                if (col + 1 < p.cout) {
+                  GnBwdPartial gp;
+                  gp.s1 = (double)st1[x].y;
+                  gp.s2 = (double)(st2[x].y * rstd2[x].y);
+                  p.gn_part[base + (size_t)p.mtiles * 4] = gp;
+                }
+              }
+            }
           }
-        }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&mY, stg, (int)v0 + q4 * 32, j0 + c0, s);
-          bulk_commit();
-        }
-        ++nstored;
-        if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
-          // column sums over the 32 voxels; lanes 2c and 2c+1 end up with column c
-          const float t1 = warp_transpose_sum16(s1, lane);
-          const float t2 = warp_transpose_sum16(s2, lane);
-          const float rstd_c = __shfl_sync(0xffffffffu, rstd_l, lane >> 1);
-          const int col = j0 + c0 + (lane >> 1);
-          if ((lane & 1) == 0 && col < p.cout) {
-            // one partial per (channel, tile, 32-voxel quarter): no cross-warp sync
-            GnBwdPartial gp;
-            gp.s1 = (double)t1;
-            gp.s2 = (double)(t2 * rstd_c);
-            p.gn_part[(((size_t)s * p.cout + col) * p.mtiles + mt) * 4 + q4] = gp;
+        } else {
+          uint32_t r[kPwCW];
+          tmem_ld16(d_tmem + (uint32_t)c0, r);
+          // per-column constants: lane l < 16 holds column c0 + l, broadcast with shuffles
+          const int jc = j0 + c0 + lane;
+          const bool jok = lane < kPwCW && jc < p.cout;
+          const float bias_l = ((epi & MEDNEXT_EPI_BIAS) && jok) ? __ldg(p.bias + jc) : 0.f;
+          float mean_l = 0.f, rstd_l = 0.f;
+          if ((epi & MEDNEXT_EPI_GN_BWD_STATS) && jok) {
+            mean_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc));
+            rstd_l = __ldg(p.epi_stats + 2 * (s * p.cout + jc) + 1);
+          }
+          // fused weight grad after a GroupNorm: g = GroupNorm(aux) = aux * ca + cb, with the
+          // same coefficients (and rounding) as the weight-grad kernel's GroupNorm prologue
+          float ca_l = 0.f, cb_l = 0.f;
+          if constexpr (FW_GN) {
+            if (jok) {
+              ca_l = rstd_l * __ldg(p.pro_gamma + jc);
+              cb_l = __ldg(p.pro_beta + jc) - mean_l * ca_l;
+            }
+          }
+          // staging buffer: wait until the store issued two chunks ago has read it
+          TY* stg = reinterpret_cast<TY*>(stg0 + (nstored & 1) * kStgBytes);
+          if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          tmem_ld_wait();
+          float s1[kPwCW], s2[kPwCW];
+          float gg[kPwCW];  // GELU'(aux) of the chunk's columns, in pairs
+          // g row c0 + jj of this lane's voxel (rows past cout keep their zeros / ones)
+          const bool gfull = c0 + kPwCW <= p.cout;
+          auto gstore = [&](int jj, float v) {
+            if (gfull || c0 + jj < p.cout) {
+              const TA b = from_acc<TA>(v);
+              st_shared_b16(gx[jj & 7] + (uint32_t)(((c0 >> 3) + (jj >> 3)) * 1024), *reinterpret_cast<const uint16_t*>(&b));
+            }
+          };
+          if constexpr (FW_GELU) {
+            // GELU(aux) as well, from the same Phi: into the g tile (channels past cout keep their zeros / ones)
+  #pragma unroll
+            for (int jj = 0; jj < kPwCW; jj += 2) {
+              float2 gv;
+              const float2 g = gelu_grad2_and_gelu(
+                  make_float2(to_acc<TA>(auxt[(c0 + jj) * 64]), to_acc<TA>(auxt[(c0 + jj + 1) * 64])), gv);
+              gg[jj] = g.x;
+              gg[jj + 1] = g.y;
+              gstore(jj, gv.x);
+              gstore(jj + 1, gv.y);
+            }
+          } else if (epi & MEDNEXT_EPI_GELU_GRAD) {
+  #pragma unroll
+            for (int jj = 0; jj < kPwCW; jj += 2) {
+              const float2 g = gelu_grad2(
+                  make_float2(to_acc<TA>(auxt[(c0 + jj) * 64]), to_acc<TA>(auxt[(c0 + jj + 1) * 64])));
+              gg[jj] = g.x;
+              gg[jj + 1] = g.y;
+            }
+          }
+  #pragma unroll
+          for (int jj = 0; jj < kPwCW; ++jj) {
+            const int jl = c0 + jj;
+            float a = __uint_as_float(r[jj]);
+            if (epi & MEDNEXT_EPI_BIAS) a += __shfl_sync(0xffffffffu, bias_l, jj);
+            if (epi & (MEDNEXT_EPI_GELU_GRAD | MEDNEXT_EPI_RESIDUAL)) a = to_acc<TA>(from_acc<TA>(a));
+            float ax = 0.f;
+            if (epi & MEDNEXT_EPI_GN_BWD_STATS) ax = to_acc<TA>(auxt[jl * 64]);
+            if constexpr (FW_GN)
+              gstore(jj, fmaf(ax, __shfl_sync(0xffffffffu, ca_l, jj), __shfl_sync(0xffffffffu, cb_l, jj)));
+            if (epi & MEDNEXT_EPI_GELU_GRAD) a *= gg[jj];
+            if (epi & MEDNEXT_EPI_RESIDUAL) a += (float)to_acc<TY>(rest[jl * 64]);
+            const TY o = from_acc<TY>((typename Elem<TY>::Acc)a);
+            stg[jj * 32 + lane] = o;
+            if constexpr (MLP) gstore(jj, (float)to_acc<TY>(o));  // u as stored; GELU follows in place
+            if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
+              // out-of-range voxels / channels hold exact zeros (zero-filled operands)
+              const float d = (float)to_acc<TY>(o);
+              s1[jj] = d;
+              s2[jj] = d * (ax - __shfl_sync(0xffffffffu, mean_l, jj));
+            }
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&mY, stg, (int)v0 + q4 * 32, j0 + c0, s);
+            bulk_commit();
+          }
+          ++nstored;
+          if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
+            // column sums over the 32 voxels; lanes 2c and 2c+1 end up with column c
+            const float t1 = warp_transpose_sum16(s1, lane);
+            const float t2 = warp_transpose_sum16(s2, lane);
+            const float rstd_c = __shfl_sync(0xffffffffu, rstd_l, lane >> 1);
+            const int col = j0 + c0 + (lane >> 1);
+            if ((lane & 1) == 0 && col < p.cout) {
+              // one partial per (channel, tile, 32-voxel quarter): no cross-warp sync
+              GnBwdPartial gp;
+              gp.s1 = (double)t1;
+              gp.s2 = (double)(t2 * rstd_c);
+              p.gn_part[(((size_t)s * p.cout + col) * p.mtiles + mt) * 4 + q4] = gp;
+            }
           }
         }
       }
@@ -691,27 +864,78 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tc_fence_after();
         const uint32_t d2_tmem = tmem + (uint32_t)cfg.d2_col + (uint32_t)(tg * cfg.d2_stride) + ((uint32_t)(q4 * 32) << 16);
         for (int c0 = kPwCW * cg; c0 < cfg.bn2; c0 += kPwCW * kGroups) {
-          uint32_t r[kPwCW];
-          tmem_ld16(d2_tmem + (uint32_t)c0, r);
-          const int jc = c0 + lane;
-          const float bias_l = (lane < kPwCW && jc < p.cout2) ? __ldg(p.bias2 + jc) : 0.f;
-          TY* stg = reinterpret_cast<TY*>(stg0 + (nstored & 1) * kStgBytes);
-          if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
-          __syncwarp();
-          tmem_ld_wait();
+          if constexpr (kFrag) {
+            uint32_t r[16];
+            tmem_ld_16x256b_x2(d2_tmem + (uint32_t)c0, r);
+            tmem_ld_16x256b_x2(d2_tmem + (16u << 16) + (uint32_t)c0, r + 8);
+            const int jr = c0 + 8 * f_x + f_rr;
+            uint32_t rs[8];
+            if (has_res) {
 #pragma unroll
-          for (int jj = 0; jj < kPwCW; ++jj) {
-            float a = __uint_as_float(r[jj]) + __shfl_sync(0xffffffffu, bias_l, jj);
-            if (has_res) a = to_acc<TA>(from_acc<TA>(a)) + (float)to_acc<TY>(rest[(c0 + jj) * 64]);
-            stg[jj * 32 + lane] = from_acc<TY>((typename Elem<TY>::Acc)a);
+              for (int h = 0; h < 2; ++h) {
+                const int vt = q4 * 32 + 16 * h + 8 * f_vh;
+                ldsm_x4_trans(res_u32 + (uint32_t)((vt >> 6) * (cfg.res_bytes / 2) + jr * 128 +
+                                                   ((((vt & 63) >> 3) ^ (jr & 7)) << 4)),
+                              rs + 4 * h);
+              }
+            }
+            float2 bias2[2];
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              const int jc = c0 + 8 * x + 2 * tq;
+              bias2[x] = make_float2(jc < p.cout2 ? __ldg(p.bias2 + jc) : 0.f,
+                                     jc + 1 < p.cout2 ? __ldg(p.bias2 + jc + 1) : 0.f);
+            }
+            const uint32_t stg_u32 = smem_u32(stg0 + (nstored & 1) * kStgBytes);
+            if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+            tmem_ld_wait();
+            uint32_t out[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int x = (k >> 1) & 1;
+              float2 a = make_float2(__uint_as_float(r[2 * k]) + bias2[x].x, __uint_as_float(r[2 * k + 1]) + bias2[x].y);
+              if (has_res) {
+                a = unpack2<TA>(pack2<TA>(a));
+                const float2 rv = unpack2<TY>(rs[k]);
+                a = make_float2(a.x + rv.x, a.y + rv.y);
+              }
+              out[k] = pack2<TY>(a);
+            }
+            const int R = 8 * f_x + f_rr;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              stsm_x4_trans(stg_u32 + (uint32_t)(R * 64 + ((((2 * h + f_vh) ^ (R >> 1)) & 3) << 4)), out + 4 * h);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&mY2, reinterpret_cast<void*>(stg0 + (nstored & 1) * kStgBytes), (int)v0 + q4 * 32, c0, s);
+              bulk_commit();
+            }
+            ++nstored;
+          } else {
+            uint32_t r[kPwCW];
+            tmem_ld16(d2_tmem + (uint32_t)c0, r);
+            const int jc = c0 + lane;
+            const float bias_l = (lane < kPwCW && jc < p.cout2) ? __ldg(p.bias2 + jc) : 0.f;
+            TY* stg = reinterpret_cast<TY*>(stg0 + (nstored & 1) * kStgBytes);
+            if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+            tmem_ld_wait();
+  #pragma unroll
+            for (int jj = 0; jj < kPwCW; ++jj) {
+              float a = __uint_as_float(r[jj]) + __shfl_sync(0xffffffffu, bias_l, jj);
+              if (has_res) a = to_acc<TA>(from_acc<TA>(a)) + (float)to_acc<TY>(rest[(c0 + jj) * 64]);
+              stg[jj * 32 + lane] = from_acc<TY>((typename Elem<TY>::Acc)a);
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&mY2, stg, (int)v0 + q4 * 32, c0, s);
+              bulk_commit();
+            }
+            ++nstored;
           }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_3d(&mY2, stg, (int)v0 + q4 * 32, c0, s);
-            bulk_commit();
-          }
-          ++nstored;
         }
       }
       if (has_aux || has_res) mbar_arrive(&sh.eempty[e]);

@@ -68,8 +68,12 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   if (MLP && (a.cin > kPwBK || a.ntiles != 1 || a.cout % 16 != 0 || a.cout > kPwBM || bn2 < 16 || bn2 > 256 ||
               a.w2 == nullptr || a.y2 == nullptr || a.bias2 == nullptr || !a16(a.w2) || !a16(a.y2)))
     return -1;
-  if (!encode3<TY>(&mY, a.y, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 32, kPwCW,
-                    CU_TENSOR_MAP_SWIZZLE_NONE))
+  // 16-bit outputs: the fragment epilogue stages 32-voxel x 16-channel blocks with a
+  // 64-byte swizzle and reads the aux / residual tiles with a 128-byte swizzle
+  constexpr bool kFrag = sizeof(TY) == 2;
+  const CUtensorMapSwizzle sw_out = kFrag ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  const CUtensorMapSwizzle sw_opnd = kFrag ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  if (!encode3<TY>(&mY, a.y, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 32, kPwCW, sw_out))
     return -1;
   const int a_rows = std::min(kPwBK, (a.cin + 15) / 16 * 16);
   if (!encode3<TA>(&mA, a.a, (uint64_t)a.vox, (uint64_t)a.cin, (uint64_t)a.S, 64, (uint32_t)a_rows,
@@ -82,17 +86,16 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   if (!encode2<TA>(&mB, wt, (uint64_t)wk, (uint64_t)a.cout, kPwBK, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return -1;
   if (has_aux && !encode3<TA>(&mAux, a.aux, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 64, (uint32_t)a.BN,
-                              CU_TENSOR_MAP_SWIZZLE_NONE))
+                              sw_opnd))
     return -1;
   const int res_rows = MLP ? a.cout2 : a.cout, res_bn = MLP ? bn2 : a.BN;
   if (has_res && !encode3<TY>(&mRes, a.residual, (uint64_t)a.vox, (uint64_t)res_rows, (uint64_t)a.S, 64,
-                              (uint32_t)res_bn, CU_TENSOR_MAP_SWIZZLE_NONE))
+                              (uint32_t)res_bn, sw_opnd))
     return -1;
   if (MLP) {
     if (!encode2<TA>(&mB2, a.w2, (uint64_t)a.cout, (uint64_t)a.cout2, kPwBK, (uint32_t)bn2, CU_TENSOR_MAP_SWIZZLE_128B))
       return -1;
-    if (!encode3<TY>(&mY2, a.y2, (uint64_t)a.vox, (uint64_t)a.cout2, (uint64_t)a.S, 32, kPwCW,
-                     CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (!encode3<TY>(&mY2, a.y2, (uint64_t)a.vox, (uint64_t)a.cout2, (uint64_t)a.S, 32, kPwCW, sw_out))
       return -1;
   }
   // fused compress weight grad (kEpiFusedWgrad): one K stage and one N tile, H + 1
