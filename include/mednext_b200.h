@@ -300,6 +300,21 @@ int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue,
                            void* pro_out, void* workspace, size_t workspace_bytes, int64_t n,
                            int64_t cin, int64_t cout, int64_t vox, int a_dtype, int y_dtype,
                            mednext_stream_t stream);
+/* The forward GEMM of mednext_pw_fwd (bf16 only; prologue NONE or GROUPNORM; bias
+ * or none) that also writes g = gelu(y) (exact erf form, of y as stored in bf16) to
+ * g, an array of y's shape: the expand GEMM of the MedNeXt block hands the compress
+ * GEMM its activated input this way, so that GEMM runs without a GELU prologue and
+ * the compress weight grad reads g instead of recomputing it (models/blocks.py:75-77,
+ * the expand -> GELU -> project chain).  y and g rows must start 16-byte aligned
+ * (vox a multiple of 8).  Returns MEDNEXT_ERR_UNSUPPORTED for other dtypes, a GELU
+ * prologue or other shapes (the caller then runs mednext_pw_fwd with a GELU
+ * prologue on the next GEMM).  Workspace as mednext_pw_fwd_workspace_size(...,
+ * bias ? MEDNEXT_EPI_BIAS : 0). */
+int mednext_pw_fwd_gelu_out(const void* a, const void* wt, void* y, void* g, int prologue,
+                            const float* pro_stats, const float* pro_gamma, const float* pro_beta,
+                            const float* bias, void* workspace, size_t workspace_bytes, int64_t n,
+                            int64_t cin, int64_t cout, int64_t vox, int dtype,
+                            mednext_stream_t stream);
 /* The block's expansion, fused (models/blocks.py:79-84 with the residual add of
  * 89-90): with z = GroupNorm(t) (stats [n*c][2], gamma, beta FLOAT32 [c]),
  *   u[s, h, v] = sum_k we[h, k] * z[s, k, v] + be[h]               (written: saved for backward)

@@ -100,6 +100,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _INT,
         [_P, _P, _P, _INT, _P, _P, _P, _INT, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _INT, _P],
     ),
+    "mednext_pw_fwd_gelu_out": (
+        _INT, [_P, _P, _P, _P, _INT, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _P],
+    ),
     "mednext_pw_gelu_bwd_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _INT]),
     "mednext_pw_gelu_bwd": (_INT, [_P, _P, _P, _P, _P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _INT, _P]),
     "mednext_ce_workspace_size": (_SZ, [_I64, _I64, _I64]),

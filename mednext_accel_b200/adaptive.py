@@ -329,7 +329,7 @@ class FusedBlockRunner:
         res = getattr(block, "residual", None) if fuse_res else None
         res_w = res.weight if res is not None else None
         res_b = res.bias if res is not None else None
-        y, _, _, _ = mednext_block(
+        y, _, _, _, _ = mednext_block(
             x, addend, block.depthwise.weight, block.depthwise.bias, block.norm.weight, block.norm.bias,
             block.expand.weight, block.expand.bias, block.project.weight, block.project.bias, res_w, res_b,
             self.kind, int(block.depthwise.kernel_size[0]), float(block.norm.eps), bool(residual_is_input), keep,

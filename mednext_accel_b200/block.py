@@ -33,7 +33,8 @@ from torch.nn import functional as F
 
 from . import _native as nat
 from . import depthwise as dwk
-from .pointwise import gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_gn_bwd_fused, pw_wgrad
+from .pointwise import (gelu_bwd_fused_covers, gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm,
+                        pw_gemm_gelu_out, pw_gn_bwd_fused, pw_wgrad)
 
 _NS = "mednext_accel_b200"
 KIND_REGULAR, KIND_DOWN, KIND_UP = 0, 1, 2
@@ -142,14 +143,42 @@ def _depthwise_forward(xb: Tensor, w: Tensor, b: Tensor | None, kind: int, k: in
 
 
 def _expansion(t: Tensor, stats: Tensor, gn_w: Tensor, gn_b: Tensor, prm: _Params, cdt, cout: int,
-               res: Tensor | None) -> tuple[Tensor, Tensor]:
-    """(u, y): u = expand(GroupNorm(t)), y = project(GELU(u)) (+ res), as two GEMMs.
-    (The one-kernel form, ``pointwise.pw_mlp_fwd``, gives the same bits but measured
-    slower at level 0: its two epilogue groups wait on the GELU pass between the GEMMs.)"""
+               res: Tensor | None) -> tuple[Tensor, Tensor, Tensor]:
+    """(u, g, y): u = expand(GroupNorm(t)), y = project(GELU(u)) (+ res), and g =
+    GELU(u) where the backward wants it stored (else an empty tensor).
+
+    Where the backward's fused project kernel (``pw_gelu_bwd``) covers the block it
+    recomputes GELU(u) from u on the fly, so the project GEMM applies GELU as its
+    prologue and nothing more is stored.  Elsewhere the expand GEMM's epilogue
+    writes g beside u: the project GEMM runs without a prologue (and, at the deep
+    levels, on narrower N tiles) and the backward's project weight grad reads g.
+    Both forms give the same bits.  (The one-kernel form, ``pointwise.pw_mlp_fwd``,
+    gives the same bits too but measured slower at level 0: its two epilogue groups
+    wait on the GELU pass between the GEMMs.)"""
+    ydt = res.dtype if res is not None else cdt
+    resc = res.contiguous() if res is not None else None
+    ug = None
+    if _stores_gelu(int(t.shape[0]), int(prm.pw.shape[0]), int(prm.ew.shape[0]), int(t[0, 0].numel()), cdt):
+        ug = _expand_gelu(t, stats, gn_w, gn_b, prm)
+    if ug is not None:
+        u, g = ug
+        y, _ = pw_gemm(g, prm.pw, cout, out_dtype=ydt, bias=prm.pb, residual=resc)
+        return u, g, y
     u = _expand(t, stats, gn_w, gn_b, prm, cdt)
-    y, _ = pw_gemm(u, prm.pw, cout, out_dtype=res.dtype if res is not None else cdt, prologue=nat.PRO_GELU,
-                   bias=prm.pb, residual=res.contiguous() if res is not None else None)
-    return u, y
+    y, _ = pw_gemm(u, prm.pw, cout, out_dtype=ydt, prologue=nat.PRO_GELU, bias=prm.pb, residual=resc)
+    return u, u.new_empty((0,)), y
+
+
+def _stores_gelu(n: int, cout: int, rc: int, vox: int, cdt) -> bool:
+    """Whether a block stores g = GELU(u): where the fused project backward does not
+    cover it and the GELU-output GEMM can produce g (bf16, 16-byte aligned rows)."""
+    return cdt == torch.bfloat16 and vox % 8 == 0 and not gelu_bwd_fused_covers(n, cout, rc, vox, cdt)
+
+
+def _expand_gelu(t: Tensor, stats: Tensor, gn_w: Tensor, gn_b: Tensor, prm: _Params) -> tuple[Tensor, Tensor] | None:
+    rc = int(prm.ew.shape[0])
+    return pw_gemm_gelu_out(t, prm.ew, rc, prologue=nat.PRO_GROUPNORM, pro_stats=stats,
+                            pro_gamma=gn_w.float().contiguous(), pro_beta=gn_b.float().contiguous(), bias=prm.eb)
 
 
 def _expand(t: Tensor, stats: Tensor, gn_w: Tensor, gn_b: Tensor, prm: _Params, cdt) -> Tensor:
@@ -181,9 +210,9 @@ def mednext_block(
     residual_is_input: bool,
     keep_expansion: bool,
     compute_dtype: int,
-) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-    """Returns (y, t, u, stats); t, u (empty when not kept) and stats are saved
-    for backward and carry no gradient.
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (y, t, u, g, stats); t, u and g = GELU(u) (both empty when not kept)
+    and stats are saved for backward and carry no gradient.
 
     For the up block (kind 2) y is the final, left-padded (2S)^3 output of the
     reference's ``F.pad(block(x) + residual(x))`` and t, u are pitched
@@ -214,17 +243,21 @@ def mednext_block(
         if res_w is not None:
             rs, _ = pw_gemm(xb, prm.rw, cout, out_dtype=cdt, bias=prm.rb)
             res_p = dwk.upsample2_fill(rs, prm.rb, pitch)
-        u, y_p = _expansion(t, stats, gn_w, gn_b, prm, cdt, cout, res_p)
+        u, g, y_p = _expansion(t, stats, gn_w, gn_b, prm, cdt, cout, res_p)
         if addend is not None and addend.dtype != cdt:
             y = F.pad(dwk.pitched_view(y_p, big), (1, 0) * 3) + addend
         else:
             y = dwk.pad_front_add(y_p, big, addend)
-        return y, t, (u if keep_expansion else u.new_empty((0,))), stats
+        if not keep_expansion:
+            u, g = u.new_empty((0,)), u.new_empty((0,))
+        return y, t, u, g, stats
     t, stats = _depthwise_forward(xb, wdw, bdw, kind, kernel_size, eps)
     if res_w is not None and kind == KIND_DOWN:
         res, _ = pw_gemm(_even(xb), prm.rw, cout, out_dtype=cdt, bias=prm.rb)
-    u, y = _expansion(t, stats, gn_w, gn_b, prm, cdt, cout, res)
-    return y, t, (u if keep_expansion else u.new_empty((0,))), stats
+    u, g, y = _expansion(t, stats, gn_w, gn_b, prm, cdt, cout, res)
+    if not keep_expansion:
+        u, g = u.new_empty((0,)), u.new_empty((0,))
+    return y, t, u, g, stats
 
 
 @mednext_block.register_fake
@@ -249,7 +282,10 @@ def _(x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, res_w, res_b, kind,
         t = x.new_empty((n, c, *sp), dtype=cdt)
         u = x.new_empty((n, e_w.shape[0], *sp), dtype=cdt) if keep_expansion else x.new_empty((0,), dtype=cdt)
     stats = x.new_empty((n * c, 2), dtype=torch.float32)
-    return y, t, u, stats
+    vox = int(t[0, 0].numel())
+    g = torch.empty_like(u) if keep_expansion and _stores_gelu(n, int(p_w.shape[0]), int(e_w.shape[0]), vox, cdt) \
+        else x.new_empty((0,), dtype=cdt)
+    return y, t, u, g, stats
 
 
 @custom_op(f"{_NS}::mednext_block_backward", mutates_args=())
@@ -258,6 +294,7 @@ def mednext_block_backward(
     x: Tensor,
     t: Tensor,
     u_saved: Tensor,
+    g_saved: Tensor,
     stats: Tensor,
     dw_w: Tensor,
     gn_w: Tensor,
@@ -291,7 +328,13 @@ def mednext_block_backward(
     # input grad of the residual GEMM: the down block needs W^T [cin, cout], the up block W [cin, cout]
     rmode = (res_w, kind == KIND_DOWN) if res_w is not None else None
     prm = _block_params(dw_w, None, e_w, e_b, p_w, None, cdt, transposed=True, res=rmode)
-    u = u_saved if u_saved.numel() > 0 else _expand(t, stats, gn_w, gn_b, prm, cdt)
+    if u_saved.numel() > 0:
+        u, g = u_saved, (g_saved if g_saved.numel() > 0 else None)
+    else:  # the expansion was not kept (activation checkpointing): recompute it
+        ug = None
+        if _stores_gelu(int(t.shape[0]), cout, rc, int(t[0, 0].numel()), cdt):
+            ug = _expand_gelu(t, stats, gn_w, gn_b, prm)
+        u, g = ug if ug is not None else (_expand(t, stats, gn_w, gn_b, prm, cdt), None)
     # project dgrad with the GELU derivative in the epilogue and, where the fused
     # kernel covers the shape, the project weight grad from the same pass
     fused = pw_gelu_bwd(dyb, prm.pwt, u)
@@ -299,7 +342,8 @@ def mednext_block_backward(
         du, dpw, dpb = fused
     else:
         du, _ = pw_gemm(dyb, prm.pwt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
-        dpw, dpb = pw_wgrad(dyb, u, prologue=nat.PRO_GELU)
+        # the project weight grad from the stored GELU(u) (else GELU applied on load)
+        dpw, dpb = pw_wgrad(dyb, g) if g is not None else pw_wgrad(dyb, u, prologue=nat.PRO_GELU)
     # GroupNorm affine parameters in fp32 for the kernels
     g_w = gn_w.float().contiguous()
     g_b = gn_b.float().contiguous()
@@ -363,8 +407,8 @@ def mednext_block_backward(
 
 
 @mednext_block_backward.register_fake
-def _(dy, x, t, u_saved, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w, kind, kernel_size, residual_is_input,
-      compute_dtype):
+def _(dy, x, t, u_saved, g_saved, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w, kind, kernel_size,
+      residual_is_input, compute_dtype):
     nres = 0 if res_w is None else res_w.shape[1] if kind == KIND_UP else res_w.shape[0]
     return (
         torch.empty_like(x),
@@ -384,9 +428,9 @@ def _(dy, x, t, u_saved, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w, kind, ke
 def _setup(ctx, inputs, output):
     (x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, res_w, res_b, kind, k, eps, residual_is_input, keep,
      cdt) = inputs
-    y, t, u, stats = output
-    ctx.save_for_backward(x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w)
-    ctx.mark_non_differentiable(t, u, stats)
+    y, t, u, g, stats = output
+    ctx.save_for_backward(x, t, u, g, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w)
+    ctx.mark_non_differentiable(t, u, g, stats)
     # t, u and stats never receive a gradient: without this, autograd would allocate
     # and zero-fill tensors of their (expanded, full-resolution) shapes every step
     ctx.set_materialize_grads(False)
@@ -398,12 +442,13 @@ def _setup(ctx, inputs, output):
     ctx.addend_dtype = addend.dtype if addend is not None else None
 
 
-def _backward(ctx, dy, _dt, _du, _dstats):
+def _backward(ctx, dy, _dt, _du, _dg, _dstats):
     if dy is None:  # the block output does not reach the loss
         return (None,) * 18
-    x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w = ctx.saved_tensors
+    x, t, u, g, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w = ctx.saved_tensors
     dx, dww, dwb, dgw, dgb, dew, deb, dpw, dpb, drw, drb = mednext_block_backward(
-        dy, x, t, u, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w, ctx.kind, ctx.k, ctx.residual_is_input, ctx.cdt
+        dy, x, t, u, g, stats, dw_w, gn_w, gn_b, e_w, e_b, p_w, res_w, ctx.kind, ctx.k, ctx.residual_is_input,
+        ctx.cdt
     )
     if res_w is None:
         drw = drb = None

@@ -488,11 +488,12 @@ int mednext_pw_fwd(const void* a, const void* wt, void* y, int prologue, const f
                                 stream);
 }
 
-int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue, const float* pro_stats,
-                           const float* pro_gamma, const float* pro_beta, int epilogue, const float* bias,
-                           const void* residual, const void* aux, const float* epi_stats, void* pro_out,
-                           void* workspace, size_t workspace_bytes, int64_t n, int64_t cin, int64_t cout,
-                           int64_t vox, int a_dtype, int y_dtype, mednext_stream_t stream) {
+// Argument checks and the kernel arguments shared by the forward-GEMM entry points.
+static int pw_fwd_setup(const void* a, const void* wt, void* y, int prologue, const float* pro_stats,
+                        const float* pro_gamma, const float* pro_beta, int epilogue, const float* bias,
+                        const void* residual, const void* aux, const float* epi_stats, void* pro_out,
+                        void* workspace, size_t workspace_bytes, int64_t n, int64_t cin, int64_t cout,
+                        int64_t vox, int a_dtype, int y_dtype, PwFwdArgs* out) {
   if (!pw_dtype_ok(a_dtype)) return MEDNEXT_ERR_BAD_DTYPE;
   if (y_dtype != a_dtype && y_dtype != MEDNEXT_FLOAT32) return MEDNEXT_ERR_BAD_DTYPE;
   if (!pw_shape_ok(n, cin, cout, vox)) return MEDNEXT_ERR_BAD_SHAPE;
@@ -514,14 +515,15 @@ int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue,
       (aux && !aligned(aux, asz)) || (pro_out && !aligned(pro_out, asz)))
     return MEDNEXT_ERR_ALIGNMENT;
   if (prologue == MEDNEXT_PRO_NONE) pro_out = nullptr;  // nothing transformed: nothing to write
-  PwFwdArgs args{};
+  PwFwdArgs& args = *out;
+  args = PwFwdArgs{};
   args.a = a; args.wt = wt; args.y = y;
   args.pro_stats = pro_stats; args.pro_gamma = pro_gamma; args.pro_beta = pro_beta;
   args.bias = bias; args.residual = residual; args.aux = aux; args.epi_stats = epi_stats;
   args.pro_out = pro_out;
   args.gn_part = static_cast<GnBwdPartial*>(workspace);
   args.S = (int)n; args.cin = (int)cin; args.cout = (int)cout; args.vox = vox;
-  args.BN = pw_bn(cout);
+  args.BN = pw_fwd_bn(n, cout, vox, prologue);
   args.mtiles = (int)((vox + kPwBM - 1) / kPwBM);
   args.ntiles = (int)((cout + args.BN - 1) / args.BN);
   args.epilogue = epilogue;
@@ -530,7 +532,37 @@ int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue,
   args.wpad = pw_fwd_wpad_bytes(cin, cout) > 0 ? static_cast<char*>(workspace) + pw_fwd_gn_bytes(n, cout, vox, epilogue)
                                               : nullptr;
   if ((long long)args.S * args.ntiles * args.mtiles >= (1LL << 31)) return MEDNEXT_ERR_BAD_SHAPE;
+  return MEDNEXT_OK;
+}
+
+int mednext_pw_fwd_pro_out(const void* a, const void* wt, void* y, int prologue, const float* pro_stats,
+                           const float* pro_gamma, const float* pro_beta, int epilogue, const float* bias,
+                           const void* residual, const void* aux, const float* epi_stats, void* pro_out,
+                           void* workspace, size_t workspace_bytes, int64_t n, int64_t cin, int64_t cout,
+                           int64_t vox, int a_dtype, int y_dtype, mednext_stream_t stream) {
+  PwFwdArgs args;
+  const int st = pw_fwd_setup(a, wt, y, prologue, pro_stats, pro_gamma, pro_beta, epilogue, bias, residual, aux,
+                              epi_stats, pro_out, workspace, workspace_bytes, n, cin, cout, vox, a_dtype, y_dtype,
+                              &args);
+  if (st != MEDNEXT_OK) return st;
   return dispatch_pw_fwd(a_dtype, y_dtype, prologue, args, as_stream(stream));
+}
+
+int mednext_pw_fwd_gelu_out(const void* a, const void* wt, void* y, void* g, int prologue, const float* pro_stats,
+                            const float* pro_gamma, const float* pro_beta, const float* bias, void* workspace,
+                            size_t workspace_bytes, int64_t n, int64_t cin, int64_t cout, int64_t vox, int dtype,
+                            mednext_stream_t stream) {
+  if (g == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if (!aligned(g, elem_size(dtype))) return MEDNEXT_ERR_ALIGNMENT;
+  PwFwdArgs args;
+  const int epilogue = bias != nullptr ? MEDNEXT_EPI_BIAS : 0;
+  const int st = pw_fwd_setup(a, wt, y, prologue, pro_stats, pro_gamma, pro_beta, epilogue, bias, nullptr, nullptr,
+                              nullptr, nullptr, workspace, workspace_bytes, n, cin, cout, vox, dtype, dtype, &args);
+  if (st != MEDNEXT_OK) return st;
+  if (dtype != MEDNEXT_BFLOAT16 || prologue == MEDNEXT_PRO_GELU || vox % 8 != 0) return MEDNEXT_ERR_UNSUPPORTED;
+  args.y2 = g;
+  const int rc = pw_fwd_gelu_out_bf16(prologue, args, as_stream(stream));
+  return rc == -1 ? MEDNEXT_ERR_UNSUPPORTED : rc;
 }
 
 static bool pw_gelu_bwd_covered(int64_t n, int64_t c, int64_t h, int64_t vox, int dtype) {

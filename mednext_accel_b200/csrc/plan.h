@@ -158,6 +158,18 @@ inline int pw_bn(int64_t cout) {
   if (cout >= 256) return 256;
   return (int)(((cout + 15) / 16) * 16);
 }
+// N tile of the forward / input-grad GEMM: up to 256 output channels.  Where the
+// tiles would leave SMs idle (the deep levels: a few thousand voxels), GEMMs whose
+// prologue is cheap take narrower N tiles, down to 32 channels, until about 128
+// tiles exist; each N tile re-reads its A tile, which at these sizes comes from L2.
+// A GELU prologue keeps the widest tile (each N tile would repeat the GELU work).
+inline int pw_fwd_bn(int64_t n, int64_t cout, int64_t vox, int prologue) {
+  int bn = pw_bn(cout);
+  if (prologue == MEDNEXT_PRO_GELU) return bn;
+  const int64_t mt = n * ((vox + 127) / 128);
+  while (bn > 32 && mt * ((cout + bn - 1) / bn) < 128) bn = std::max(32, (bn / 2 + 15) / 16 * 16);
+  return bn;
+}
 inline size_t pw_smem(int BN) { return 32768 + 2 * (size_t)BN * 128 + 1024; }
 struct PwWPlan {
   int BN, mtiles, ntiles, splits;
@@ -213,6 +225,9 @@ int pw_fwd_bf16_bf16(int prologue, const PwFwdArgs& a, cudaStream_t s);
 int pw_gelu_bwd_bf16(const PwFwdArgs& a, cudaStream_t s);
 int pw_gn_bwd_bf16(const PwFwdArgs& a, cudaStream_t s);
 int pw_mlp_fwd_bf16(const PwFwdArgs& a, cudaStream_t s);
+// Forward GEMM that also writes g = GELU(y) to a.y2 (prologue none or GroupNorm, bias or
+// none): MEDNEXT_OK when launched, -1 when the shape does not allow the TMA kernel.
+int pw_fwd_gelu_out_bf16(int prologue, const PwFwdArgs& a, cudaStream_t s);
 int pw_fused_grid(long long total_tiles);  // CTAs (= weight-grad splits) of pw_gelu_bwd_bf16
 int dispatch_pw_wgrad_reduce(const float* part, const float* part_b, float* dw, float* dbias, int splits, int cout,
                              int cin, cudaStream_t s);

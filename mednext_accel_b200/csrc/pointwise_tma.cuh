@@ -57,11 +57,23 @@ constexpr int kFwLag = 2;          // the weight-grad MMAs of tile i run after t
 // the residual and stores y.  u is never read back from HBM.
 constexpr int kEpiMlp = 32;
 constexpr int kFwGBytes = 32768;   // one g tile: two 64-voxel K-major boxes of 128 rows
-template <int PRO>
+// EPI bit (internal, fragment epilogue only): the epilogue also writes GELU of its
+// output, g = GELU(y) with y rounded as stored, through the second output map (mY2):
+// the expand GEMM hands the compress GEMM its activated input, so the compress GEMM
+// needs no prologue and the compress weight grad can read g instead of recomputing it.
+constexpr int kEpiGeluOut = 128;
+// Warp roles after the producer / MMA / aux-producer / prologue-store warps 0-3:
+// prologue warps 4 .. warp0 - 1 (8 of them, or 4 when the epilogue carries the
+// GELU output and the prologue is the cheap GroupNorm apply), epilogue warps up to 19.
+template <int PRO, int EPI>
 struct FwdEpi {
-  static constexpr int warp0 = PRO == MEDNEXT_PRO_NONE ? 4 : 12;
+  static constexpr bool gelu_out = EPI >= 0 && (EPI & kEpiGeluOut) != 0;
+  static constexpr int warp0 = PRO == MEDNEXT_PRO_NONE ? 4 : (gelu_out ? 8 : 12);
   static constexpr int warps = kFwdThreads / 32 - warp0;
   static constexpr int threads = warps * 32;
+  static constexpr int pro_threads = (warp0 - 4) * 32;
+  // staging buffers per epilogue warp: y, and g with the GELU output, double-buffered
+  static constexpr int stg_bufs = gelu_out ? 4 : 2;
 };
 constexpr int kMaxStages = 8;
 // Prologue-output stores kept in flight by warp 3 (< ring stages, checked on the host).
@@ -190,19 +202,22 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint8_t* ringRes = ringAux + (size_t)E * cfg.aux_bytes; // E x res_bytes
   uint8_t* ringStg = ringRes + (size_t)E * cfg.res_bytes;  // epilogue warps x 2 x (16 x 32) TY
   constexpr int kStgBytes = 32 * kPwCW * (int)sizeof(TY);
-  constexpr int kEpiWarp0 = FwdEpi<PRO>::warp0;
-  constexpr int kEpiThreads = FwdEpi<PRO>::threads;
+  constexpr int kEpiWarp0 = FwdEpi<PRO, EPI>::warp0;
+  constexpr int kEpiThreads = FwdEpi<PRO, EPI>::threads;
+  constexpr int kProThreads = FwdEpi<PRO, EPI>::pro_threads > 0 ? FwdEpi<PRO, EPI>::pro_threads : kFwdProThreads;
   constexpr bool FW = EPI >= 0 && (EPI & kEpiFusedWgrad) != 0;
   constexpr bool FW_GELU = FW && (EPI & MEDNEXT_EPI_GELU_GRAD) != 0;      // g = GELU(aux)
   constexpr bool FW_GN = FW && (EPI & MEDNEXT_EPI_GN_BWD_STATS) != 0;     // g = GroupNorm(aux)
   static_assert(!(FW_GELU && FW_GN), "one fused weight-grad operand");
   constexpr bool MLP = EPI >= 0 && (EPI & kEpiMlp) != 0;
   static_assert(!(MLP && FW), "one fused second GEMM");
+  constexpr bool GOUT = FwdEpi<PRO, EPI>::gelu_out;
+  static_assert(!GOUT || (!MLP && !FW && sizeof(TY) == 2), "the GELU output rides on the plain fragment epilogue");
   // 16-bit outputs take the fragment epilogue (swizzled operand and staging tiles);
   // float32 outputs the one-voxel-per-lane epilogue (unswizzled tiles)
   constexpr bool kFrag = sizeof(TY) == 2;
   // fused weight grad: two g tiles (one per epilogue group) after the staging buffers
-  uint8_t* gbuf = ringStg + (size_t)FwdEpi<PRO>::warps * 2 * kStgBytes;
+  uint8_t* gbuf = ringStg + (size_t)FwdEpi<PRO, EPI>::warps * FwdEpi<PRO, EPI>::stg_bufs * kStgBytes;
   gbuf += ((1024u - (smem_u32(gbuf) & 1023u)) & 1023u);
 
   const uint32_t ncols = tmem_cols_for(BN);
@@ -227,7 +242,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
       mbar_init(&sh.full[i], 1);
-      mbar_init(&sh.ready[i], kFwdProThreads);
+      mbar_init(&sh.ready[i], kProThreads);
       // a stage is free again after its MMAs and, with a prologue output, its store
       mbar_init(&sh.empty[i], cfg.pro_store ? 2 : 1);
     }
@@ -243,7 +258,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     mbar_init(&sh.wfull, 1);
     for (int b = 0; b < 2; ++b) {
       // the fused expansion's g tile is finished (GELU applied) by the prologue warps
-      mbar_init(&sh.gready[b], MLP ? kFwdProThreads : kEpiThreads / 2);
+      mbar_init(&sh.gready[b], MLP ? kProThreads : kEpiThreads / 2);
       mbar_init(&sh.gempty[b], 1);
       mbar_init(&sh.uready[b], kEpiThreads / 2);
     }
@@ -263,6 +278,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tma_prefetch_map(&mB2);
       tma_prefetch_map(&mY2);
     }
+    if constexpr (GOUT) tma_prefetch_map(&mY2);
   }
   tc_fence_before();
   __syncthreads();
@@ -468,9 +484,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else if (warp >= kFwdProWarp0 && warp < kEpiWarp0) {
     // ------------------------------------------------ prologue transform (in place)
     if constexpr (PRO != MEDNEXT_PRO_NONE) {
-      const int t = tid - kFwdProWarp0 * 32;  // 0..255
+      const int t = tid - kFwdProWarp0 * 32;  // 0 .. kProThreads - 1
       const int mch = t & 15;                 // 16 chunks of 8 voxels (two 64-voxel boxes)
-      const int kr = t >> 4;                  // rows kr, kr+16, kr+32, kr+48 (same swizzle row)
+      const int kr = t >> 4;                  // rows kr, kr + kRowStep, ... (the same swizzle row)
+      constexpr int kRowStep = kProThreads / 16;
       // MLP: GELU in place over the u that epilogue group w & 1 wrote into its g tile (two
       // 64-voxel boxes of H rows, 16-byte chunks; elementwise, so the swizzle is irrelevant)
       auto gelu_tile = [&](int w) -> bool {
@@ -478,7 +495,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (!wait_or_abort(&sh.uready[gb], (uint32_t)((w >> 1) & 1), abort)) return false;
         uint8_t* gt = gbuf + gb * kFwGBytes;
         const int per_box = p.cout * 8;
-        for (int item = t; item < 2 * per_box; item += kFwdProThreads) {
+        for (int item = t; item < 2 * per_box; item += kProThreads) {
           const int box = item / per_box, rem = item - box * per_box;
           uint4* chunk = reinterpret_cast<uint4*>(gt + box * 16384 + rem * 16);
           float v[8];
@@ -500,8 +517,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (!wait_or_abort(&sh.full[st], r & 1, abort)) break;
           uint8_t* a = ringA + (size_t)st * AS + (mch >> 3) * AH;
 #pragma unroll
-          for (int ii = 0; ii < 4; ++ii) {
-            const int kl = kr + 16 * ii;
+          for (int ii = 0; ii < kPwBK / kRowStep; ++ii) {
+            const int kl = kr + kRowStep * ii;
             if (kl >= cfg.a_rows) break;  // rows the TMA box does not cover are never read
             const int k = kk * kPwBK + kl;
             uint4* chunk = reinterpret_cast<uint4*>(a + kl * 128 + ((((mch & 7) ^ (kl & 7))) << 4));
@@ -542,13 +559,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // block is staged in shared memory and written with one TMA bulk tensor
     // store (out-of-range rows and columns are clipped by the store).
     const int tgs = cfg.tgroups;
-    const int kGroups = FwdEpi<PRO>::warps / 4 / tgs;
+    const int kGroups = FwdEpi<PRO, EPI>::warps / 4 / tgs;
     const int ew = warp - kEpiWarp0;
     const int q4 = warp & 3;
     const int tg = (ew >> 2) % tgs;
     const int cg = (ew >> 2) / tgs;
     const int epi = EPI >= 0 ? EPI : p.epilogue;
-    uint8_t* stg0 = ringStg + (size_t)ew * 2 * kStgBytes;
+    uint8_t* stg0 = ringStg + (size_t)ew * FwdEpi<PRO, EPI>::stg_bufs * kStgBytes;
     uint32_t nstored = 0;
     // fragment epilogue: lane L gives the row address of 8x8 matrix L / 8 = (x, vh) =
     // (L / 16, L / 8 % 2), row L % 8; t % 4 selects the thread's channel pair
@@ -645,7 +662,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (nstored >= 2 && lane == 0) bulk_wait_read<1>();
           __syncwarp();
           tmem_ld_wait();
-          uint32_t out[8], gpk[8];
+          uint32_t out[8], gpk[8], gel[8];
           float2 st1[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
           float2 st2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -673,6 +690,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             }
             out[k] = pack2<TY>(a);
             if constexpr (MLP) gpk[k] = out[k];  // u as stored; GELU follows in place
+            if constexpr (GOUT) gel[k] = pack2<TY>(gelu2(unpack2<TY>(out[k])));  // GELU of y as stored
             if (epi & MEDNEXT_EPI_GN_BWD_STATS) {
               // out-of-range voxels / channels hold exact zeros (zero-filled operands)
               const float2 d = unpack2<TY>(out[k]);
@@ -685,6 +703,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int h = 0; h < 2; ++h)
               stsm_x4_trans(stg_u32 + (uint32_t)(R * 64 + ((((2 * h + f_vh) ^ (R >> 1)) & 3) << 4)), out + 4 * h);
+            if constexpr (GOUT) {
+              const uint32_t stg_g = stg_u32 + 2 * kStgBytes;  // the g buffer of the same parity
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                stsm_x4_trans(stg_g + (uint32_t)(R * 64 + ((((2 * h + f_vh) ^ (R >> 1)) & 3) << 4)), gel + 4 * h);
+            }
           }
           if constexpr (FW || MLP) {
             // g tile rows = this GEMM's output channels (rows past cout keep their zeros / ones)
@@ -715,6 +739,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           __syncwarp();
           if (lane == 0) {
             tma_store_3d(&mY, reinterpret_cast<void*>(stg0 + (nstored & 1) * kStgBytes), (int)v0 + q4 * 32, j0 + c0, s);
+            if constexpr (GOUT)
+              tma_store_3d(&mY2, reinterpret_cast<void*>(stg0 + (2 + (nstored & 1)) * kStgBytes), (int)v0 + q4 * 32,
+                           j0 + c0, s);
             bulk_commit();
           }
           ++nstored;

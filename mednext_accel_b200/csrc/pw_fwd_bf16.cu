@@ -25,6 +25,15 @@ int pw_gn_bwd_bf16(const PwFwdArgs& a, cudaStream_t s) {
 int pw_mlp_fwd_bf16(const PwFwdArgs& a, cudaStream_t s) {
   return try_pw_fwd_tma<__nv_bfloat16, __nv_bfloat16, MEDNEXT_PRO_GROUPNORM, MEDNEXT_EPI_BIAS | kEpiMlp>(a, s);
 }
+int pw_fwd_gelu_out_bf16(int prologue, const PwFwdArgs& a, cudaStream_t s) {
+  using T = __nv_bfloat16;
+  const bool bias = (a.epilogue & MEDNEXT_EPI_BIAS) != 0;
+  if (prologue == MEDNEXT_PRO_GROUPNORM)
+    return bias ? try_pw_fwd_tma<T, T, MEDNEXT_PRO_GROUPNORM, MEDNEXT_EPI_BIAS | kEpiGeluOut>(a, s)
+                : try_pw_fwd_tma<T, T, MEDNEXT_PRO_GROUPNORM, kEpiGeluOut>(a, s);
+  return bias ? try_pw_fwd_tma<T, T, MEDNEXT_PRO_NONE, MEDNEXT_EPI_BIAS | kEpiGeluOut>(a, s)
+              : try_pw_fwd_tma<T, T, MEDNEXT_PRO_NONE, kEpiGeluOut>(a, s);
+}
 int pw_fused_grid(long long total_tiles) { return (int)std::min<long long>(total_tiles, num_sms()); }
 MEDNEXT_DEFINE_ERROR_READER(read_clear_errors_pwf0)
 

@@ -92,6 +92,13 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   if (has_res && !encode3<TY>(&mRes, a.residual, (uint64_t)a.vox, (uint64_t)res_rows, (uint64_t)a.S, 64,
                               (uint32_t)res_bn, sw_opnd))
     return -1;
+  constexpr bool GOUT = FwdEpi<PRO, EPI>::gelu_out;
+  if constexpr (GOUT) {
+    // g = GELU(y): a second output of y's shape through the second output map
+    if (!kFrag || a.y2 == nullptr || !a16(a.y2) ||
+        !encode3<TY>(&mY2, a.y2, (uint64_t)a.vox, (uint64_t)a.cout, (uint64_t)a.S, 32, kPwCW, sw_out))
+      return -1;
+  }
   if (MLP) {
     if (!encode2<TA>(&mB2, a.w2, (uint64_t)a.cout, (uint64_t)a.cout2, kPwBK, (uint32_t)bn2, CU_TENSOR_MAP_SWIZZLE_128B))
       return -1;
@@ -123,7 +130,8 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
   cfg.a_slot = 2 * 128 * a_rows;  // a multiple of 4 KB: the boxes stay 1 KB aligned for the swizzle
   const size_t per_stage = (size_t)cfg.a_slot + (cfg.w_res ? 0 : (size_t)cfg.b_bytes);
   const size_t ebytes = (size_t)cfg.aux_bytes + cfg.res_bytes;
-  const size_t stg = (size_t)FwdEpi<PRO>::warps * 2 * 32 * kPwCW * sizeof(TY);  // epilogue staging, 2 per warp
+  // epilogue staging: 2 buffers per warp (4 with the GELU output)
+  const size_t stg = (size_t)FwdEpi<PRO, EPI>::warps * FwdEpi<PRO, EPI>::stg_bufs * 32 * kPwCW * sizeof(TY);
   const size_t g_bytes = (FW || MLP) ? 1024 + 2 * (size_t)kFwGBytes : 0;       // two g tiles, 1 KB aligned
   const size_t budget = kSmemBudget - stg - w_bytes - g_bytes - w2_bytes;
   // Epilogue-operand ring: 4 or 2 stages while keeping at least 4 A/W stages,
@@ -139,6 +147,8 @@ int try_pw_fwd_tma(const PwFwdArgs& a, cudaStream_t s) {
     else if (2 * ebytes + min_a * per_stage <= budget) cfg.estages = 2;
   }
   cfg.tgroups = (ebytes == 0 || cfg.estages % 2 == 0) ? 2 : 1;
+  // an odd number of 4-warp epilogue groups (the GELU-output variant's 12 warps) stays one group
+  if ((FwdEpi<PRO, EPI>::warps / 4) % 2 != 0) cfg.tgroups = 1;
   // the fused weight grad gives each of the two epilogue groups its own g tile
   if ((FW || MLP) && cfg.tgroups != 2) return -1;
   // extra TMEM: the fused weight grad's accumulator, or the fused expansion's two second-GEMM ones

@@ -21,7 +21,8 @@ import torch
 from . import _native as nat
 from . import depthwise as dwk
 from .pointwise import (
-    gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_gn_bwd_fused, pw_mlp_fwd, pw_wgrad,
+    gn_backward_from_partials, gn_stats, pw_gelu_bwd, pw_gemm, pw_gemm_gelu_out, pw_gn_bwd_fused, pw_mlp_fwd,
+    pw_wgrad,
 )
 
 V = 128**3  # level-0 voxels
@@ -55,6 +56,12 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
         "pw expand fwd (GroupNorm prologue, bias)": (
             lambda: pw_gemm(t, we, RC, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g, pro_beta=bb, bias=b1),
             (C + RC) * 2 * V),
+        "pw expand fwd + GELU output (GroupNorm prologue, bias)": (
+            lambda: pw_gemm_gelu_out(t, we, RC, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g,
+                                     pro_beta=bb, bias=b1),
+            (C + 2 * RC) * 2 * V),
+        "pw project fwd (no prologue: GELU output read, bias, residual)": (
+            lambda: pw_gemm(gout, wp, C, bias=b2, residual=x), (RC + C + C) * 2 * V),
         "pw project fwd (GELU prologue, bias, residual)": (
             lambda: pw_gemm(u, wp, C, prologue=nat.PRO_GELU, bias=b2, residual=x), (RC + C + C) * 2 * V),
         "pw expansion fwd fused (expand + GELU + project)": (

@@ -83,6 +83,40 @@ def pw_gemm(
     return y, ws
 
 
+def pw_gemm_gelu_out(
+    a: Tensor,
+    wt: Tensor,
+    cout: int,
+    *,
+    prologue: int = nat.PRO_NONE,
+    pro_stats: Tensor | None = None,
+    pro_gamma: Tensor | None = None,
+    pro_beta: Tensor | None = None,
+    bias: Tensor | None = None,
+) -> tuple[Tensor, Tensor] | None:
+    """(y, g): y = W @ pro(a) (+ bias) in a's dtype and g = GELU(y) (of y as stored),
+    both written by one kernel.  None when the entry point does not cover the call
+    (dtype, prologue or shape); the caller then applies GELU as the next GEMM's prologue."""
+    nat.require_device(a)
+    lib = nat.load()
+    n, cin = int(a.shape[0]), int(a.shape[1])
+    vox = _vox(a)
+    y = torch.empty((n, cout, *a.shape[2:]), dtype=a.dtype, device=a.device)
+    g = torch.empty_like(y)
+    epi = nat.EPI_BIAS if bias is not None else 0
+    ws_bytes = lib.mednext_pw_fwd_workspace_size(n, cin, cout, vox, epi)
+    ws = nat.workspace(ws_bytes, a.device) if ws_bytes > 0 else None
+    st = lib.mednext_pw_fwd_gelu_out(
+        a.data_ptr(), wt.data_ptr(), y.data_ptr(), g.data_ptr(), prologue, nat.ptr(pro_stats), nat.ptr(pro_gamma),
+        nat.ptr(pro_beta), nat.ptr(bias), nat.ptr(ws), 0 if ws is None else ws.numel(), n, cin, cout, vox,
+        nat.dtype_code(a.dtype), nat.stream(),
+    )
+    if st == nat.ERR_UNSUPPORTED:
+        return None
+    nat.check(st, "mednext_pw_fwd_gelu_out")
+    return y, g
+
+
 def pw_wgrad(
     g: Tensor,
     a: Tensor,
@@ -111,6 +145,12 @@ def pw_wgrad(
         "mednext_pw_wgrad",
     )
     return dw, db
+
+
+def gelu_bwd_fused_covers(n: int, c: int, h: int, vox: int, dtype: torch.dtype) -> bool:
+    """Whether ``pw_gelu_bwd`` (the compress input grad with its weight grad fused in)
+    covers a block whose project GEMM maps h expanded channels to c."""
+    return nat.load().mednext_pw_gelu_bwd_workspace_size(n, c, h, vox, nat.dtype_code(dtype)) > 0
 
 
 def pw_gelu_bwd(dy: Tensor, wpt: Tensor, u: Tensor) -> tuple[Tensor, Tensor, Tensor] | None:

@@ -393,3 +393,106 @@ def test_fused_gelu_backward_declines_uncovered_shapes():
 
 def test_no_device_error_recorded():
     assert nat.device_error() == 0
+
+
+# Deep, narrow levels: few 128-voxel tiles and K up to 2048 (long K loops through the
+# ring, two samples, ragged voxel counts).
+SPLITK_SHAPES = [
+    (1, 1024, 256, (16, 16, 16)),   # level 3 compress: 32 tiles x 16 K stages
+    (1, 2048, 512, (8, 8, 8)),      # level 4 compress: 8 tiles x 32 K stages
+    (2, 1024, 256, (8, 8, 9)),      # two samples, ragged voxel count
+]
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", SPLITK_SHAPES)
+def test_split_k_gelu_prologue_bias_residual(n, cin, cout, spatial):
+    u = rand((n, cin, *spatial), 41)
+    w = rand((cout, cin), 42, scale=1 / np.sqrt(cin))
+    b = rand((cout,), 43, torch.float32)
+    res = rand((n, cout, *spatial), 44)
+    y, _ = pw_gemm(u.cuda(), w.cuda(), cout, prologue=nat.PRO_GELU, bias=b.cuda(), residual=res.cuda())
+    want = orc.pointwise_fwd(orc.round_bf16(orc.gelu(h(u))), h(w), h(b))
+    want = orc.round_bf16(want) + h(res)
+    assert_close_bf16(y, want, "y")
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", SPLITK_SHAPES[:2])
+def test_split_k_dgrad_epilogues(n, cin, cout, spatial):
+    from mednext_accel_b200.pointwise import gn_backward_from_partials
+
+    du = rand((n, cin, *spatial), 45)
+    wt = rand((cout, cin), 46, scale=1 / np.sqrt(cin))
+    t = rand((n, cout, *spatial), 47)
+    stats = gn_stats(t.cuda(), 1e-5)
+    dz, part = pw_gemm(du.cuda(), wt.cuda(), cout, aux=t.cuda(), gn_bwd_stats=stats)
+    gamma = (1 + 0.1 * rand((cout,), 48, torch.float64)).float().cuda()
+    dt, dg, db = gn_backward_from_partials(dz, t.cuda(), stats, gamma, part)
+    assert_close_bf16(dz, orc.round_bf16(orc.pointwise_fwd(h(du), h(wt), None)), "dz")
+    mean, rstd = h(stats)[:, 0], h(stats)[:, 1]
+    want_dt, want_dg, want_db = orc.groupnorm_bwd(h(dz), h(t), mean, rstd, h(gamma))
+    assert_close_bf16(dt, want_dt, "dt")
+    np.testing.assert_allclose(h(dg), want_dg, rtol=2e-4, atol=2e-3)
+    np.testing.assert_allclose(h(db), want_db, rtol=2e-4, atol=2e-3)
+    u = rand((n, cout, *spatial), 49)
+    dv, _ = pw_gemm(du.cuda(), wt.cuda(), cout, aux=u.cuda(), gelu_grad=True)
+    want = orc.round_bf16(orc.pointwise_fwd(h(du), h(wt), None)) * orc.gelu_grad(h(u))
+    assert_close_bf16(dv, want, "dv")
+
+
+def test_split_k_results_are_bitwise_reproducible():
+    """Repeated launches (as in a replayed CUDA graph) give identical bits."""
+    n, cin, cout, spatial = SPLITK_SHAPES[0]
+    u = rand((n, cin, *spatial), 51).cuda()
+    w = rand((cout, cin), 52, scale=1 / np.sqrt(cin)).cuda()
+    b = rand((cout,), 53, torch.float32).cuda()
+    first, _ = pw_gemm(u, w, cout, prologue=nat.PRO_GELU, bias=b)
+    for _ in range(3):
+        again, _ = pw_gemm(u, w, cout, prologue=nat.PRO_GELU, bias=b)
+        assert torch.equal(first, again)
+    assert nat.device_error() == 0
+
+
+GELU_OUT_SHAPES = [
+    (1, 32, 64, (16, 16, 16)),     # level 0: GroupNorm prologue, 12 epilogue warps
+    (2, 64, 192, (8, 8, 8)),       # level 1 widths, two samples
+    (1, 96, 64, (8, 8, 16)),       # K not a multiple of 64
+    (1, 256, 1024, (8, 8, 8)),     # deep level: narrow N tiles
+]
+
+
+@pytest.mark.parametrize("n,cin,cout,spatial", GELU_OUT_SHAPES)
+def test_gelu_output_matches_the_gelu_prologue_path_bit_for_bit(n, cin, cout, spatial):
+    """(u, g) from the expand GEMM's GELU-output epilogue: u equals the plain expand
+    GEMM, g equals GELU(u) as the compress GEMM's prologue computes it (its prologue
+    output), and the compress GEMM on g equals the compress GEMM with the GELU prologue."""
+    from mednext_accel_b200.pointwise import pw_gemm_gelu_out
+
+    t = (rand((n, cin, *spatial), 61).double() * 2 + 0.3).to(torch.bfloat16).cuda()
+    gamma = (1 + 0.2 * rand((cin,), 62, torch.float64)).float().cuda()
+    beta = (0.2 * rand((cin,), 63, torch.float64)).float().cuda()
+    we = rand((cout, cin), 64, scale=1 / np.sqrt(cin)).cuda()
+    be = rand((cout,), 65, torch.float32).cuda()
+    stats = gn_stats(t, 1e-5)
+    gn = dict(prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=gamma, pro_beta=beta, bias=be)
+    out = pw_gemm_gelu_out(t, we, cout, **gn)
+    assert out is not None
+    u, g = out
+    u_ref, _ = pw_gemm(t, we, cout, **gn)
+    assert torch.equal(u, u_ref)
+    wp = rand((cin, cout), 66, scale=1 / np.sqrt(cout)).cuda()
+    bp = rand((cin,), 67, torch.float32).cuda()
+    g_ref = torch.empty_like(u)
+    y_ref, _ = pw_gemm(u, wp, cin, prologue=nat.PRO_GELU, bias=bp, pro_out=g_ref)
+    assert torch.equal(g, g_ref)
+    y, _ = pw_gemm(g, wp, cin, bias=bp)
+    assert torch.equal(y, y_ref)
+    want_g = orc.round_bf16(orc.gelu(h(u)))
+    assert_close_bf16(g, want_g, "g")
+
+
+def test_gelu_output_declines_unaligned_rows():
+    from mednext_accel_b200.pointwise import pw_gemm_gelu_out
+
+    t = rand((1, 32, 5, 5, 5), 68).cuda()  # 125 voxels: rows not 16-byte aligned
+    we = rand((64, 32), 69, scale=0.2).cuda()
+    assert pw_gemm_gelu_out(t, we, 64) is None
