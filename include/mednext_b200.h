@@ -188,32 +188,49 @@ int mednext_dw_s2_wgrad_f32out(const void* x, const void* dy, void* dweight, voi
 
 /* ------- depthwise ConvTranspose3d, stride 2, padding k/2 (up block) ------
  * (d, h, w) are the INPUT sizes; the output is (2d-1, 2h-1, 2w-1).
- * big_pitch: elements between consecutive (n, c) volumes of the (2d-1)^3-sized
- * tensor (y in fwd, dy in dgrad/wgrad); 0 means contiguous.  A larger pitch
- * (e.g. the voxel count rounded up to a multiple of 8) lets the following 1x1
- * GEMMs describe the tensor with TMA; fwd writes zeros into the pitch tail. */
+ * big_pitch: elements between consecutive W-rows of the (2d-1, 2h-1, 2w-1)
+ * tensor (y in fwd, dy in dgrad/wgrad); 0 means 2w-1 (contiguous).  The (n, c)
+ * volumes are then (2d-1)(2h-1)*big_pitch elements apart.  The fused up block
+ * uses big_pitch = 2w (w a multiple of 4): every row starts 16-byte aligned, so
+ * the depthwise kernels and the following 1x1 GEMMs reach the tensor by TMA, and
+ * the GEMMs run over the pad column too.  fwd writes zeros into the pad columns;
+ * dgrad and wgrad never read them. */
 int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y, int64_t n,
                     int64_t c, int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype,
                     mednext_stream_t stream);
+/* mednext_dwT_fwd plus the GroupNorm statistics of y over its grid voxels (pad
+ * columns excluded): gn_stats = float [n*c][2] (mean, rstd with gn_eps), as
+ * mednext_dw_fwd gives them for the regular block.  On the packed-FMA path the
+ * kernel accumulates them while it stores y; elsewhere a second pass reads y.
+ * The fused up block's transposed conv + GroupNorm statistics
+ * (models/blocks.py:165-172 followed by the GroupNorm of blocks.py:74).
+ * workspace: mednext_dwT_fwd_workspace_size bytes. */
+size_t mednext_dwT_fwd_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
+                                      int64_t big_pitch, int k, int dtype);
+int mednext_dwT_fwd_stats(const void* x, const void* weight, const void* bias, void* y,
+                          float* gn_stats, float gn_eps, void* workspace, size_t workspace_bytes,
+                          int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t big_pitch,
+                          int k, int dtype, mednext_stream_t stream);
 /* addend: NULL, or a tensor of dx's shape added to dx: the input grad of the up
  * block's 1x1, stride-2 transposed residual convolution (models/blocks.py:173-182). */
 int mednext_dwT_dgrad(const void* dy, const void* weight, const void* addend, void* dx, int64_t n,
                       int64_t c, int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k,
                       int dtype, mednext_stream_t stream);
-/* Stride-2 expansion onto the up block's (2d-1, 2h-1, 2w-1) grid (pitch as above):
- * big[2m] = small[m] at the all-even positions, bias[c] (fp32, NULL = 0) at all
- * others, zeros in the pitch tail.  With small = W x + bias from the pointwise
+/* Stride-2 expansion onto the up block's (2d-1, 2h-1, 2w-1) grid (row pitch as
+ * above): big[2m] = small[m] at the all-even positions, bias[c] (fp32, NULL = 0)
+ * at all others, zeros in the pad columns.  With small = W x + bias from the pointwise
  * GEMM this is the output of the up block's ConvTranspose3d(1x1x1, stride 2)
  * residual branch (models/blocks.py:173-182). */
 /* out [n, c, d+1, h+1, w+1] = F.pad(v, (1, 0, 1, 0, 1, 0)) + addend, one rounding;
- * v is the pitched [n, c, pitch] grid of (d, h, w) voxels, addend (out's shape,
+ * v is the (d, h, w) grid with W-rows `pitch` elements apart (0 = w), (n, c)
+ * volumes d*h*pitch apart; addend (out's shape,
  * may be NULL) in the same dtype.  Replaces the up block's output pad and the
  * decoder's skip add: models/blocks.py:177-181, models/mednext_v1.py:205. */
 int mednext_pad_front_add(const void* v, const void* addend, void* out, int64_t n, int64_t c,
                           int64_t d, int64_t h, int64_t w, int64_t pitch, int dtype,
                           mednext_stream_t stream);
-/* The inverse: v [n, c, pitch] = the (z, y, x >= 1) interior of padded
- * [n, c, d+1, h+1, w+1], zero tail.  The grad of the up block's padded output,
+/* The inverse: v (the row-pitched (d, h, w) grid, as above) = the (z, y, x >= 1)
+ * interior of padded [n, c, d+1, h+1, w+1], zeros in the pad columns.  The grad of the up block's padded output,
  * repacked for its GEMMs (the backward of models/blocks.py:178). */
 int mednext_unpad_front(const void* padded, void* v, int64_t n, int64_t c, int64_t d, int64_t h,
                         int64_t w, int64_t pitch, int dtype, mednext_stream_t stream);
@@ -239,6 +256,15 @@ size_t mednext_gn_stats_workspace_size(int64_t n, int64_t c, int64_t spatial);
 int mednext_gn_stats(const void* x, float* stats, void* workspace, size_t workspace_bytes,
                      int64_t n, int64_t c, int64_t spatial, int64_t pitch, float eps, int dtype,
                      mednext_stream_t stream);
+/* Statistics of a row-pitched tensor: each (n, c) volume is `rows` rows of
+ * row_pitch elements (0 = row_len), of which the first row_len are statistics;
+ * volumes are rows*row_pitch elements apart.  The up block's transposed-conv
+ * output with its pad column.  workspace: mednext_gn_stats_workspace_size(n, c,
+ * rows * row_pitch) bytes.  No reference counterpart (the reference's tensors
+ * are never pitched). */
+int mednext_gn_stats_rows(const void* x, float* stats, void* workspace, size_t workspace_bytes,
+                          int64_t n, int64_t c, int64_t rows, int64_t row_len, int64_t row_pitch,
+                          float eps, int dtype, mednext_stream_t stream);
 int mednext_gn_fwd(const void* x, const float* stats, const void* gamma, const void* beta,
                    void* y, int64_t n, int64_t c, int64_t spatial, int x_dtype, int y_dtype,
                    int gamma_dtype, mednext_stream_t stream);
@@ -368,8 +394,10 @@ int mednext_pw_wgrad(const void* g, const void* a, float* dw, float* dbias, int 
                      int64_t cout, int64_t vox, int dtype, mednext_stream_t stream);
 /* GroupNorm backward driven by the partial sums that mednext_pw_fwd wrote with
  * MEDNEXT_EPI_GN_BWD_STATS (dz = that GEMM's output = grad of GroupNorm output).
- * vox: valid voxels per (n, c) row; pitch: row length the GEMM ran over (its
- * vox argument; 0 = vox).  The partials in pw_workspace are folded in place. */
+ * vox: valid voxels per (n, c) row (the mean's divisor); pitch: row length the
+ * GEMM ran over (its vox argument; 0 = vox).  dx is written over the whole pitch
+ * (entries that are not valid voxels get values without meaning).  The partials
+ * in pw_workspace are folded in place. */
 int mednext_gn_bwd_from_partials(const void* dz, const void* x, const float* stats,
                                  const void* gamma, void* dx, float* dgamma, float* dbeta,
                                  void* pw_workspace, int64_t n, int64_t c, int64_t vox,

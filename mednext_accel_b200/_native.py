@@ -76,6 +76,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mednext_dw_s2_wgrad": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dw_s2_wgrad_f32out": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_INT, _INT, _P]),
     "mednext_dwT_fwd": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_I64, _INT, _INT, _P]),
+    "mednext_dwT_fwd_workspace_size": (_SZ, _DIMS5 + [_I64, _INT, _INT]),
+    "mednext_dwT_fwd_stats": (_INT, [_P, _P, _P, _P, _P, _F, _P, _SZ] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_dwT_dgrad": (_INT, [_P, _P, _P, _P] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_upsample2_fill": (_INT, [_P, _P, _P] + _DIMS5 + [_I64, _INT, _P]),
     "mednext_pad_front_add": (_INT, [_P, _P, _P] + _DIMS5 + [_I64, _INT, _P]),
@@ -85,6 +87,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mednext_dwT_wgrad_f32out": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_gn_stats_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "mednext_gn_stats": (_INT, [_P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _F, _INT, _P]),
+    "mednext_gn_stats_rows": (_INT, [_P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _I64, _F, _INT, _P]),
     "mednext_gn_fwd": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _INT, _INT, _INT, _P]),
     "mednext_gn_bwd_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "mednext_gn_bwd": (

@@ -127,12 +127,13 @@ def _even(x: Tensor) -> Tensor:
     return x[:, :, ::2, ::2, ::2].contiguous()
 
 
-def _pitch(spatial: tuple[int, ...]) -> tuple[int, int]:
-    """(voxels, row pitch rounded up to 8 elements = 16 bytes of bf16)."""
+def _row_pitch(spatial: tuple[int, ...]) -> tuple[int, int]:
+    """(valid voxels, W-row pitch rounded up to 8 elements = 16 bytes of bf16) of the
+    up block's (2S-1)^3 grid."""
     vox = 1
     for s in spatial:
         vox *= int(s)
-    return vox, (vox + 7) // 8 * 8
+    return vox, (int(spatial[-1]) + 7) // 8 * 8
 
 
 def _depthwise_forward(xb: Tensor, w: Tensor, b: Tensor | None, kind: int, k: int, eps: float) -> tuple[Tensor, Tensor]:
@@ -215,9 +216,10 @@ def mednext_block(
     and stats are saved for backward and carry no gradient.
 
     For the up block (kind 2) y is the final, left-padded (2S)^3 output of the
-    reference's ``F.pad(block(x) + residual(x))`` and t, u are pitched
-    [n, c, pitch] buffers whose rows hold the (2S-1)^3 voxels followed by a zero
-    tail, so that every GEMM operand has 16-byte aligned rows for TMA.  Its
+    reference's ``F.pad(block(x) + residual(x))`` and t, u are row-pitched
+    [n, c, 2S-1, 2S-1, pitch] buffers whose W-rows hold 2S-1 voxels and pad
+    columns up to a multiple of 8, so that every depthwise and GEMM operand has
+    16-byte aligned rows for TMA (the GEMMs run over the pad columns too).  Its
     ``addend`` (the decoder's skip, models/mednext_v1.py:205) has the padded
     shape and is added after the pad, in the same pass.
 
@@ -236,9 +238,8 @@ def mednext_block(
     res = x if residual_is_input else addend
     if kind == KIND_UP:
         big = tuple(2 * int(s) - 1 for s in x.shape[2:])
-        vox, pitch = _pitch(big)
-        t = dwk.t_forward(xb, wdw, bdw, kernel_size, pitch=pitch)
-        stats = gn_stats(t, eps, vox=vox)
+        _, pitch = _row_pitch(big)
+        t, stats = dwk.t_forward_stats(xb, wdw, bdw, kernel_size, eps, row_pitch=pitch)
         res_p = None
         if res_w is not None:
             rs, _ = pw_gemm(xb, prm.rw, cout, out_dtype=cdt, bias=prm.rb)
@@ -271,10 +272,11 @@ def _(x, addend, dw_w, dw_b, gn_w, gn_b, e_w, e_b, p_w, p_b, res_w, res_b, kind,
     if kind == KIND_UP:
         ydt = torch.promote_types(cdt, addend.dtype) if addend is not None else cdt
         big = tuple(2 * s - 1 for s in sp)
-        _, pitch = _pitch(big)
+        _, pitch = _row_pitch(big)
         y = x.new_empty((n, p_w.shape[0], *(2 * s for s in sp)), dtype=ydt)
-        t = x.new_empty((n, c, pitch), dtype=cdt)
-        u = x.new_empty((n, e_w.shape[0], pitch), dtype=cdt) if keep_expansion else x.new_empty((0,), dtype=cdt)
+        t = x.new_empty((n, c, big[0], big[1], pitch), dtype=cdt)
+        u = x.new_empty((n, e_w.shape[0], big[0], big[1], pitch), dtype=cdt) if keep_expansion \
+            else x.new_empty((0,), dtype=cdt)
     else:
         if kind == KIND_DOWN:
             sp = tuple((s + 1) // 2 for s in sp)
@@ -317,9 +319,10 @@ def mednext_block_backward(
     if kind == KIND_UP:
         # dy is the grad of the padded (2S)^3 output; the pad voxels carry no
         # dependence on the block, so only the (2S-1)^3 interior flows back,
-        # repacked into a pitched buffer with a zero tail
+        # repacked into the row-pitched layout with zeros in the pad columns (so
+        # the GEMMs' sums over voxels see nothing there)
         big = tuple(2 * int(s) - 1 for s in x.shape[2:])
-        vox, pitch = _pitch(big)
+        vox, pitch = _row_pitch(big)
         dyb = dwk.unpad_front(dy.to(cdt), pitch)
     else:
         dy = dy.contiguous()

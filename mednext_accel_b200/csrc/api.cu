@@ -87,6 +87,10 @@ bool pw_shape_ok(int64_t n, int64_t cin, int64_t cout, int64_t vox) {
 }
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 bool pitch_ok(int64_t pitch, int64_t vol) { return pitch == 0 || pitch >= vol; }
+// a W-row pitch of rows `width` elements wide: 0 (contiguous) or at least width
+bool row_pitch_ok(int64_t row_pitch, int64_t width) {
+  return row_pitch == 0 || (row_pitch >= width && row_pitch < (1LL << 30));
+}
 
 }  // namespace
 
@@ -289,7 +293,7 @@ int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y
                     int64_t h, int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
-  if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
+  if (!row_pitch_ok(big_pitch, 2 * w - 1)) return MEDNEXT_ERR_BAD_SHAPE;
   if (x == nullptr || weight == nullptr || y == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   if (!aligned(x, esz) || !aligned(y, esz) || !aligned(weight, esz) || (bias && !aligned(bias, esz)))
@@ -298,11 +302,37 @@ int mednext_dwT_fwd(const void* x, const void* weight, const void* bias, void* y
                                 as_stream(stream));
 }
 
+size_t mednext_dwT_fwd_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t big_pitch,
+                                      int k, int dtype) {
+  if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK || !row_pitch_ok(big_pitch, 2 * w - 1)) return 0;
+  const DwS2Geom g = s2_geom_up(n, c, d, h, w, big_pitch);
+  if (!gn_shape_ok(n, c, g.bp)) return 0;
+  return align_up(dwT_fwd_stats_ws(dtype, k, g), 256);
+}
+
+int mednext_dwT_fwd_stats(const void* x, const void* weight, const void* bias, void* y, float* gn_stats, float gn_eps,
+                          void* workspace, size_t workspace_bytes, int64_t n, int64_t c, int64_t d, int64_t h,
+                          int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
+  int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (!row_pitch_ok(big_pitch, 2 * w - 1)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (x == nullptr || weight == nullptr || y == nullptr || gn_stats == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const size_t esz = elem_size(dtype);
+  if (!aligned(x, esz) || !aligned(y, esz) || !aligned(weight, esz) || (bias && !aligned(bias, esz)) ||
+      !aligned(gn_stats, 8))
+    return MEDNEXT_ERR_ALIGNMENT;
+  const size_t need = mednext_dwT_fwd_workspace_size(n, c, d, h, w, big_pitch, k, dtype);
+  if (need == 0) return MEDNEXT_ERR_BAD_SHAPE;
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < need) return MEDNEXT_ERR_WORKSPACE;
+  return dispatch_dwT_fwd_stats(dtype, k, x, weight, bias, y, static_cast<GnPartial*>(workspace), gn_eps, gn_stats,
+                                s2_geom_up(n, c, d, h, w, big_pitch), as_stream(stream));
+}
+
 int mednext_dwT_dgrad(const void* dy, const void* weight, const void* addend, void* dx, int64_t n, int64_t c,
                       int64_t d, int64_t h, int64_t w, int64_t big_pitch, int k, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
-  if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
+  if (!row_pitch_ok(big_pitch, 2 * w - 1)) return MEDNEXT_ERR_BAD_SHAPE;
   if (dy == nullptr || weight == nullptr || dx == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   if (!aligned(dy, esz) || !aligned(dx, esz) || !aligned(weight, esz) || (addend && !aligned(addend, esz)))
@@ -315,18 +345,19 @@ int mednext_upsample2_fill(const void* small, const float* bias, void* big, int6
                            int64_t h, int64_t w, int64_t big_pitch, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d, h, w, 1, dtype);
   if (st != MEDNEXT_OK) return st;
-  if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
+  if (!row_pitch_ok(big_pitch, 2 * w - 1)) return MEDNEXT_ERR_BAD_SHAPE;
   if (small == nullptr || big == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   if (!aligned(small, esz) || !aligned(big, esz) || (bias && !aligned(bias, 4))) return MEDNEXT_ERR_ALIGNMENT;
   return dispatch_upsample2_fill(dtype, small, bias, big, s2_geom_up(n, c, d, h, w, big_pitch), as_stream(stream));
 }
 
-static DwS2Geom pad_geom(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t pitch) {
+static DwS2Geom pad_geom(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t row_pitch) {
   DwS2Geom g{};
   g.N = (int)n; g.C = (int)c;
   g.Db = (int)d; g.Hb = (int)h; g.Wb = (int)w;
-  g.bp = pitch;
+  g.bw = row_pitch > 0 ? (int)row_pitch : (int)w;
+  g.bp = (long long)d * h * g.bw;
   return g;
 }
 
@@ -334,7 +365,7 @@ int mednext_pad_front_add(const void* v, const void* addend, void* out, int64_t 
                           int64_t w, int64_t pitch, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d + 1, h + 1, w + 1, 1, dtype);
   if (st != MEDNEXT_OK) return st;
-  if (d < 1 || h < 1 || w < 1 || !pitch_ok(pitch, d * h * w)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (d < 1 || h < 1 || w < 1 || !row_pitch_ok(pitch, w)) return MEDNEXT_ERR_BAD_SHAPE;
   if (v == nullptr || out == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   if (!aligned(v, esz) || !aligned(out, esz) || (addend && !aligned(addend, esz))) return MEDNEXT_ERR_ALIGNMENT;
@@ -345,7 +376,7 @@ int mednext_unpad_front(const void* padded, void* v, int64_t n, int64_t c, int64
                         int64_t pitch, int dtype, mednext_stream_t stream) {
   int st = check_dw(n, c, d + 1, h + 1, w + 1, 1, dtype);
   if (st != MEDNEXT_OK) return st;
-  if (d < 1 || h < 1 || w < 1 || !pitch_ok(pitch, d * h * w)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (d < 1 || h < 1 || w < 1 || !row_pitch_ok(pitch, w)) return MEDNEXT_ERR_BAD_SHAPE;
   if (padded == nullptr || v == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   if (!aligned(padded, esz) || !aligned(v, esz)) return MEDNEXT_ERR_ALIGNMENT;
@@ -364,7 +395,7 @@ int dwT_wgrad_impl(const void* x, const void* dy, void* dweight, void* dbias, vo
   int st = check_dw(n, c, d, h, w, k, dtype);
   if (st != MEDNEXT_OK) return st;
   if (out_f32 && !f32_out_ok(dtype)) return MEDNEXT_ERR_BAD_DTYPE;
-  if (!pitch_ok(big_pitch, (2 * d - 1) * (2 * h - 1) * (2 * w - 1))) return MEDNEXT_ERR_BAD_SHAPE;
+  if (!row_pitch_ok(big_pitch, 2 * w - 1)) return MEDNEXT_ERR_BAD_SHAPE;
   if (x == nullptr || dy == nullptr || dweight == nullptr) return MEDNEXT_ERR_NULL_POINTER;
   const size_t esz = elem_size(dtype);
   const size_t osz = out_f32 ? 4 : esz;
@@ -409,7 +440,23 @@ int mednext_gn_stats(const void* x, float* stats, void* workspace, size_t worksp
     return MEDNEXT_ERR_WORKSPACE;
   if (!pitch_ok(pitch, spatial)) return MEDNEXT_ERR_BAD_SHAPE;
   return dispatch_gn_stats(dtype, x, static_cast<GnPartial*>(workspace), n * c, spatial, pitch > 0 ? pitch : spatial,
-                           gn_chunks(n * c, spatial), eps, stats, as_stream(stream));
+                           gn_chunks(n * c, spatial), 1, 1, eps, stats, as_stream(stream));
+}
+
+int mednext_gn_stats_rows(const void* x, float* stats, void* workspace, size_t workspace_bytes, int64_t n, int64_t c,
+                          int64_t rows, int64_t row_len, int64_t row_pitch, float eps, int dtype,
+                          mednext_stream_t stream) {
+  if (elem_size(dtype) == 0) return MEDNEXT_ERR_BAD_DTYPE;
+  if (x == nullptr || stats == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  if (rows < 1 || row_len < 1 || !row_pitch_ok(row_pitch, row_len)) return MEDNEXT_ERR_BAD_SHAPE;
+  const int64_t rp = row_pitch > 0 ? row_pitch : row_len;
+  const int64_t vol = rows * rp;
+  if (!gn_shape_ok(n, c, vol)) return MEDNEXT_ERR_BAD_SHAPE;
+  if (!aligned(x, elem_size(dtype)) || !aligned(stats, 8)) return MEDNEXT_ERR_ALIGNMENT;
+  if (workspace == nullptr || !aligned16(workspace) || workspace_bytes < mednext_gn_stats_workspace_size(n, c, vol))
+    return MEDNEXT_ERR_WORKSPACE;
+  return dispatch_gn_stats(dtype, x, static_cast<GnPartial*>(workspace), n * c, vol, vol, gn_chunks(n * c, vol),
+                           (int)rp, (int)row_len, eps, stats, as_stream(stream));
 }
 
 int mednext_gn_fwd(const void* x, const float* stats, const void* gamma, const void* beta, void* y, int64_t n,

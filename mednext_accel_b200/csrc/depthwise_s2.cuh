@@ -17,7 +17,8 @@ struct DwS2Geom {
   int N, C;
   int Db, Hb, Wb;  // big grid
   int Ds, Hs, Ws;  // small grid
-  long long bp;    // elements between consecutive (n, c) volumes of the big grid (>= Db*Hb*Wb)
+  int bw;          // elements between consecutive W-rows of the big grid (>= Wb)
+  long long bp;    // elements between consecutive (n, c) volumes of the big grid (Db*Hb*bw)
 };
 
 // Work decomposition of the three kernels: a CTA owns one (sample, channel) and
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_gather_kernel(const T* __
           const int ih = 2 * mh - P + kh;
           const bool ok = dok && ih >= 0 && ih < g.Hb;
           const int ihc = min(max(ih, 0), g.Hb - 1);
-          const T* row = bsrc + ((size_t)idc * g.Hb + ihc) * g.Wb;
+          const T* row = bsrc + ((size_t)idc * g.Hb + ihc) * g.bw;
 #pragma unroll
           for (int kw = 0; kw < K; ++kw) {
             const Acc v = s2_ld<T>(row, 2 * mw - P + kw, g.Wb);
@@ -174,7 +175,7 @@ __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_scatter_kernel(const T* _
 #pragma unroll
         for (int eh = 0; eh < 2; ++eh) {
           const int ih = 2 * qh + eh;
-          T* row = bvol + ((size_t)id * g.Hb + ih) * g.Wb;
+          T* row = bvol + ((size_t)id * g.Hb + ih) * g.bw;
 #pragma unroll
           for (int ew = 0; ew < 2; ++ew) {
             Acc acc = b0;
@@ -205,16 +206,21 @@ __global__ void __launch_bounds__(kS2Warps * 32) dw_s2_scatter_kernel(const T* _
       }
     }
   }
-  // padding tail of a pitched (n, c) row: keep it finite
-  const size_t bvol_elems = (size_t)g.Db * g.Hb * g.Wb;
-  if (qd == QD - 1) {
-    for (size_t e = bvol_elems + threadIdx.x; e < (size_t)g.bp; e += blockDim.x) bvol[e] = from_acc<T>(Acc(0));
+  // pad columns [Wb, bw) of the CTA's rows: zeros
+  if (g.bw > g.Wb) {
+    const int pad = g.bw - g.Wb;
+    for (int ed = 0; ed < 2; ++ed) {
+      const int id = 2 * qd + ed;
+      if (id >= g.Db) break;
+      for (int e = threadIdx.x; e < g.Hb * pad; e += blockDim.x)
+        bvol[((size_t)id * g.Hb + e / pad) * g.bw + g.Wb + e % pad] = from_acc<T>(Acc(0));
+    }
   }
 }
 
 // Stride-2 expansion of a small grid onto the big grid of the up block:
 // big[2m] = small[m] at the all-even positions, bias[c] (0 without bias) at the
-// others, zeros in the pitch tail.  This is the layout of a ConvTranspose3d with a
+// others, zeros in the pad columns [Wb, bw) of each row.  This is the layout of a ConvTranspose3d with a
 // 1x1x1 kernel and stride 2 once its per-voxel product (small, bias included) is
 // done.  CTA = (n, c, id) big-grid plane; warps take rows, lanes run along W.
 template <typename T>
@@ -225,18 +231,14 @@ __global__ void __launch_bounds__(kS2Warps * 32) upsample2_fill_kernel(const T* 
   const int nc = (int)(blockIdx.x / (unsigned)g.Db);
   const T fill = from_acc<T>(bias != nullptr ? bias[nc % g.C] : 0.0f);
   const T* src = small + ((size_t)nc * g.Ds + (id >> 1)) * ((size_t)g.Hs * g.Ws);
-  T* bvol = big + (size_t)nc * (size_t)g.bp;
-  T* dst = bvol + (size_t)id * g.Hb * g.Wb;
+  T* dst = big + (size_t)nc * (size_t)g.bp + (size_t)id * g.Hb * g.bw;
+  const T zero = from_acc<T>(0.0f);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int ih = warp; ih < g.Hb; ih += kS2Warps) {
     const bool even_row = ((id | ih) & 1) == 0;
     const T* srow = src + (size_t)(ih >> 1) * g.Ws;
-    for (int iw = lane; iw < g.Wb; iw += 32)
-      dst[(size_t)ih * g.Wb + iw] = (even_row && (iw & 1) == 0) ? srow[iw >> 1] : fill;
-  }
-  const size_t bvol_elems = (size_t)g.Db * g.Hb * g.Wb;
-  if (id == g.Db - 1) {
-    for (size_t e = bvol_elems + threadIdx.x; e < (size_t)g.bp; e += blockDim.x) bvol[e] = from_acc<T>(0.0f);
+    for (int iw = lane; iw < g.bw; iw += 32)
+      dst[(size_t)ih * g.bw + iw] = iw >= g.Wb ? zero : (even_row && (iw & 1) == 0) ? srow[iw >> 1] : fill;
   }
 }
 
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__(kS2Warps * 32) pad_front_add_kernel(const T* _
         for (int e = 0; e < E; ++e) a[e] = Acc(0);
       }
       if (z > 0 && y > 0) {
-        const T* srow = v + (size_t)nc * (size_t)g.bp + ((size_t)(z - 1) * g.Hb + (y - 1)) * g.Wb;
+        const T* srow = v + (size_t)nc * (size_t)g.bp + ((size_t)(z - 1) * g.Hb + (y - 1)) * g.bw;
 #pragma unroll
         for (int e = 0; e < E; ++e)
           if (x0 + e > 0) a[e] += to_acc<T>(srow[x0 + e - 1]);
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(kS2Warps * 32) pad_front_add_kernel(const T* _
   }
   for (int y = warp; y < Hp; y += kS2Warps) {
     const bool row_in = z > 0 && y > 0;
-    const T* srow = row_in ? v + (size_t)nc * (size_t)g.bp + ((size_t)(z - 1) * g.Hb + (y - 1)) * g.Wb : nullptr;
+    const T* srow = row_in ? v + (size_t)nc * (size_t)g.bp + ((size_t)(z - 1) * g.Hb + (y - 1)) * g.bw : nullptr;
     for (int x = lane; x < Wp; x += 32) {
       Acc a = (row_in && x > 0) ? to_acc<T>(srow[x - 1]) : Acc(0);
       if (add != nullptr) a += to_acc<T>(add[(size_t)y * Wp + x]);
@@ -298,8 +300,13 @@ __global__ void __launch_bounds__(kS2Warps * 32) pad_front_add_kernel(const T* _
 }
 
 // The inverse: the interior (z, y, x >= 1) of a left-padded (Db+1, Hb+1, Wb+1)
-// volume into the pitched grid, with a zero pitch tail.  The up block's output
-// grad, repacked for its GEMMs.  CTA = (n, c, interior plane).
+// volume into the row-pitched grid, with zeros in the pad columns [Wb, bw).  The
+// up block's output grad, repacked for its GEMMs.  CTA = (n, c, interior plane).
+// When the padded rows are 16-byte chunks and bw = Wb + 1 (the up block's
+// layout: a grid row and a padded row have the same length), output chunk j of a
+// row is padded chunk j shifted left by one element, its last element taken from
+// padded chunk j + 1 (or zero for the row's last chunk, the pad column): 16-byte
+// loads and stores.
 template <typename T>
 __global__ void __launch_bounds__(kS2Warps * 32) unpad_front_kernel(const T* __restrict__ padded,
                                                                     T* __restrict__ v, DwS2Geom g) {
@@ -308,16 +315,32 @@ __global__ void __launch_bounds__(kS2Warps * 32) unpad_front_kernel(const T* __r
   const int nc = (int)(blockIdx.x / (unsigned)g.Db);
   // padded row y+1 of plane z+1; output element x is its element x+1
   const T* src = padded + ((size_t)nc * (g.Db + 1) + (z + 1)) * ((size_t)Hp * Wp) + Wp;
-  T* vol = v + (size_t)nc * (size_t)g.bp;
-  T* dst = vol + (size_t)z * g.Hb * g.Wb;
+  T* dst = v + (size_t)nc * (size_t)g.bp + (size_t)z * g.Hb * g.bw;
+  constexpr int E = 16 / (int)sizeof(T);
+  if constexpr (sizeof(T) == 2) {
+    if (g.bw == Wp && Wp % E == 0 && (reinterpret_cast<uintptr_t>(padded) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
+      const int cpr = Wp / E;
+      for (int q = threadIdx.x; q < g.Hb * cpr; q += blockDim.x) {
+        const int y = q / cpr, j = q - y * cpr;
+        const T* srow = src + (size_t)y * Wp;
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(srow) + j);
+        const uint32_t nx = j + 1 < cpr ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(srow) + (j + 1) * E) : 0u;
+        uint4 o;
+        o.x = __funnelshift_r(a.x, a.y, 16);
+        o.y = __funnelshift_r(a.y, a.z, 16);
+        o.z = __funnelshift_r(a.z, a.w, 16);
+        o.w = __funnelshift_r(a.w, nx, 16);
+        reinterpret_cast<uint4*>(dst + (size_t)y * g.bw)[j] = o;
+      }
+      return;
+    }
+  }
+  const T zero = from_acc<T>(0.0f);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // lanes on consecutive elements: both the (shifted) reads and the writes coalesce
   for (int y = warp; y < g.Hb; y += kS2Warps)
-    for (int x = lane; x < g.Wb; x += 32) dst[(size_t)y * g.Wb + x] = src[(size_t)y * Wp + x + 1];
-  if (z == g.Db - 1) {
-    const size_t vox = (size_t)g.Db * g.Hb * g.Wb;
-    for (size_t e = vox + threadIdx.x; e < (size_t)g.bp; e += blockDim.x) vol[e] = from_acc<T>(0.0f);
-  }
+    for (int x = lane; x < g.bw; x += 32) dst[(size_t)y * g.bw + x] = x < g.Wb ? src[(size_t)y * Wp + x + 1] : zero;
 }
 
 // wgrad: the CTA's threads form K groups (group g owns the K*K taps with kd = g,
@@ -365,7 +388,7 @@ __global__ void __launch_bounds__(448) dw_s2_wgrad_kernel(const T* __restrict__ 
         for (int kh = 0; kh < K; ++kh) {
           const int ih = 2 * mh - P + kh;
           const Acc svh = (ih >= 0 && ih < g.Hb) ? svd : Acc(0);
-          const T* row = bsrc + ((size_t)idc * g.Hb + min(max(ih, 0), g.Hb - 1)) * g.Wb;
+          const T* row = bsrc + ((size_t)idc * g.Hb + min(max(ih, 0), g.Hb - 1)) * g.bw;
 #pragma unroll
           for (int kw = 0; kw < K; ++kw)
             acc[kh * K + kw] = fma(s2_ld<T>(row, 2 * mw - P + kw, g.Wb), svh, acc[kh * K + kw]);
@@ -396,19 +419,21 @@ __global__ void __launch_bounds__(448) dw_s2_wgrad_kernel(const T* __restrict__ 
 }
 
 // Per-(sample, channel, chunk) sums of a tensor into slot K^3 of the wgrad
-// partials (bias grad of the up block, whose dy is the big grid).  Rows start
-// every `pitch` elements; with a 16-byte aligned base and pitch the chunks are
-// read as 16-byte vectors.
+// partials (bias grad of the up block, whose dy is the big grid).  Volumes start
+// every `pitch` elements and hold `vol` elements in rows of `row_pitch`, of which
+// the first `row_len` are summed (row_len = row_pitch: all).  With a 16-byte
+// aligned base, pitch and row pitch the chunks are read as 16-byte vectors.
 template <typename T>
 __global__ void __launch_bounds__(256) chan_sum_into_partials_kernel(
     const T* __restrict__ src, typename Elem<T>::Acc* __restrict__ part, size_t vol, size_t pitch, int chunks,
-    int K3) {
+    int K3, int row_pitch, int row_len) {
   using Acc = typename Elem<T>::Acc;
   constexpr int E = 16 / (int)sizeof(T);
   const int j = (int)(blockIdx.x % (unsigned)chunks);
   const size_t nc = blockIdx.x / (unsigned)chunks;
   const T* p = src + nc * pitch;
-  const bool vec = (reinterpret_cast<uintptr_t>(src) % 16 == 0) && (pitch % E == 0);
+  const bool masked = row_len < row_pitch;
+  const bool vec = (reinterpret_cast<uintptr_t>(src) % 16 == 0) && (pitch % E == 0) && (row_pitch % E == 0);
   // chunk bounds on whole 16-byte vectors
   const size_t per = ((vol + chunks - 1) / chunks + E - 1) / E * E;
   const size_t beg = min((size_t)j * per, vol);
@@ -420,12 +445,15 @@ __global__ void __launch_bounds__(256) chan_sum_into_partials_kernel(
     for (size_t i = threadIdx.x; i < nv; i += blockDim.x) {
       Acc v[E];
       unpack16<T>(__ldg(pv + i), v);
+      const int col = masked ? (int)((beg + i * E) % (size_t)row_pitch) : 0;
 #pragma unroll
-      for (int e = 0; e < E; ++e) s += v[e];
+      for (int e = 0; e < E; ++e) s += (!masked || col + e < row_len) ? v[e] : Acc(0);
     }
-    for (size_t i = beg + nv * E + threadIdx.x; i < end; i += blockDim.x) s += to_acc<T>(__ldg(p + i));
+    for (size_t i = beg + nv * E + threadIdx.x; i < end; i += blockDim.x)
+      if (!masked || (int)(i % (size_t)row_pitch) < row_len) s += to_acc<T>(__ldg(p + i));
   } else {
-    for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) s += to_acc<T>(__ldg(p + i));
+    for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x)
+      if (!masked || (int)(i % (size_t)row_pitch) < row_len) s += to_acc<T>(__ldg(p + i));
   }
   __shared__ Acc red[8];
 #pragma unroll

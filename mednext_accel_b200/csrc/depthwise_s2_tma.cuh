@@ -66,10 +66,13 @@ __device__ __forceinline__ void dw_s2pk_window(const T* __restrict__ rowp, int c
   }
 }
 
-template <typename T>
+// ADD: an addend of the output's shape is added last (the up block's input grad
+// takes its residual branch's grad this way), one rounding per output.
+template <typename T, bool ADD>
 __global__ void __launch_bounds__(kS2PkThreads, 2)
     dw_s2_gather_pk_kernel(const __grid_constant__ CUtensorMap mX, const T* __restrict__ wgt,
-                           const T* __restrict__ bias, T* __restrict__ small, DwS2PkGeom pg) {
+                           const T* __restrict__ bias, const T* __restrict__ addend, T* __restrict__ small,
+                           DwS2PkGeom pg) {
   constexpr int K = 3;
   constexpr int K3 = 27;
   using L = DwS2PkLayout<T>;
@@ -140,6 +143,7 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
   const uint64_t bv2 = pk_pair(bvb, bvb);
   const size_t plane = (size_t)g.Hs * g.Ws;
   T* out0 = small + ((size_t)nc * g.Ds) * plane + (size_t)oh * g.Ws + ow;
+  const T* add0 = ADD ? addend + ((size_t)nc * g.Ds) * plane + (size_t)oh * g.Ws + ow : nullptr;
 
   uint64_t acc[2][4];
 #pragma unroll
@@ -215,6 +219,12 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
       float lo[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) pk_split(acc[prev][i], lo[i], lo[i + 4]);
+      if constexpr (ADD) {
+        float av[8];
+        unpack16<T>(__ldg(reinterpret_cast<const uint4*>(add0 + (size_t)(md0 + u - 1) * plane)), av);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lo[e] += av[e];
+      }
       *reinterpret_cast<uint4*>(out0 + (size_t)(md0 + u - 1) * plane) = pack16<T>(lo);
     }
     return true;
@@ -262,7 +272,12 @@ struct DwS2PkWLayout {
   static __host__ size_t smem(const DwS2PkGeom& p) { return 128 + kDwSlots * slot(p); }
 };
 
-template <typename T>
+// BIG_BIAS: the bias slot sums the big grid instead (the up block, whose dy is
+// the big grid): each thread adds the 2 rows x 16 columns of the big planes that
+// its outputs own (tile rows 1 + 2r, 2 + 2r; every plane but the chunk's first,
+// which belongs to the previous chunk); zero-filled positions past the grid add
+// nothing, so every grid voxel is summed once.
+template <typename T, bool BIG_BIAS>
 __global__ void __launch_bounds__(kS2PkThreads, 2)
     dw_s2_wgrad_pk_kernel(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mDY,
                           float* __restrict__ part, DwS2PkGeom pg) {
@@ -366,14 +381,23 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
 #pragma unroll
         for (int i = 0; i < 4; ++i) dyp[cur][i] = 0ull;
       }
+      if constexpr (!BIG_BIAS) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) accb = pk_add(accb, dyp[cur][i]);
+        for (int i = 0; i < 4; ++i) accb = pk_add(accb, dyp[cur][i]);
+      }
     }
     const T* xp = reinterpret_cast<const T*>(sb) + xbase;
 #pragma unroll
     for (int kh = 0; kh < K; ++kh) {
       uint64_t p[9];
       dw_s2pk_window<T>(xp + kh * rsp, col, left_edge, src_l, p);
+      if constexpr (BIG_BIAS) {
+        // p[1..8] hold the thread's own 16 columns of this row
+        if (kh > 0 && s > 0 && active) {
+#pragma unroll
+          for (int m = 1; m <= 8; ++m) accb = pk_add(accb, p[m]);
+        }
+      }
 #pragma unroll
       for (int kw = 0; kw < K; ++kw) {
         if constexpr (even) {
@@ -506,11 +530,14 @@ __device__ __forceinline__ void dw_s2sc_window(const T* __restrict__ rowp, int c
 // big-grid parity e and small offset a along one axis -> tap, or -1 (k = 3)
 __host__ __device__ constexpr int s2sc_tap(int e, int a) { return e == 0 ? (a == 0 ? 1 : -1) : (a == 0 ? 2 : 0); }
 
-template <typename T, bool ADD>
+// STATS: GroupNorm partial statistics (count, mean, M2) of the stored values of
+// the grid columns, one per (n, c, tile) in `stats` (the up block's forward,
+// whose output is normalised next).
+template <typename T, bool ADD, bool STATS>
 __global__ void __launch_bounds__(kS2PkThreads, 2)
     dw_s2_scatter_pk_kernel(const __grid_constant__ CUtensorMap mS, const T* __restrict__ wgt,
                             const T* __restrict__ bias, const T* __restrict__ add_even, T* __restrict__ big,
-                            DwS2ScGeom pg) {
+                            GnPartial* __restrict__ stats, DwS2ScGeom pg) {
   constexpr int K = 3;
   constexpr int K3 = 27;
   using L = DwS2ScLayout<T>;
@@ -563,7 +590,7 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
   const bool active = r < pg.THs;
   const int qh = qh0 + r;
   const int qw = qw0 + 8 * wt;
-  // Ws is a multiple of 8 and Wb = 2 Ws on this path: a thread's 16 big columns are in or out together
+  // Ws is a multiple of 8 and bw = 2 Ws on this path: a thread's 16 big columns lie in one row
   const bool cols_ok = active && qw < g.Ws;
   const bool row0_ok = cols_ok && 2 * qh < g.Hb, row1_ok = cols_ok && 2 * qh + 1 < g.Hb;
   // a row of lw <= 8 threads lies within one warp: the right neighbour is lane + 1
@@ -580,8 +607,10 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
   }
   const uint32_t bvb = __float_as_uint(bias != nullptr ? to_acc<T>(bias[c]) : 0.f);
   const uint64_t bv2 = pk_pair(bvb, bvb);
-  const size_t bplane = (size_t)g.Hb * g.Wb;
-  T* out0 = big + (size_t)nc * (size_t)g.bp + (size_t)(2 * qh) * g.Wb + 2 * qw;
+  const size_t bplane = (size_t)g.Hb * g.bw;
+  T* out0 = big + (size_t)nc * (size_t)g.bp + (size_t)(2 * qh) * g.bw + 2 * qw;
+  // big columns of this thread past the grid's last (the pad columns of a row-pitched grid): zeros
+  const int wvalid = g.Wb - 2 * qw;
   const T* add0 = ADD ? add_even + (size_t)nc * g.Ds * ((size_t)g.Hs * g.Ws) + (size_t)qh * g.Ws + qw : nullptr;
 
   // the odd big plane 2q + 1 between its two halves: [eh][ew][pair]
@@ -613,6 +642,9 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
       }
     }
   };
+  // shifted sums of the stored values (STATS)
+  float st_n = 0.f, st_shift = 0.f;
+  float2 st_s1 = make_float2(0.f, 0.f), st_s2 = make_float2(0.f, 0.f);
   // 16 big columns of one row: column 2i + ew is pair (i % 4) of acc[ew], low half for i < 4
   auto store_row = [&](T* dst, const uint64_t (&acc)[2][4]) {
     float lo[8], hi[8];
@@ -621,8 +653,31 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
       pk_split(acc[0][i], lo[2 * i], hi[2 * i]);
       pk_split(acc[1][i], lo[2 * i + 1], hi[2 * i + 1]);
     }
-    reinterpret_cast<uint4*>(dst)[0] = pack16<T>(lo);
-    reinterpret_cast<uint4*>(dst)[1] = pack16<T>(hi);
+    if (wvalid < 16) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (e >= wvalid) lo[e] = 0.f;
+        if (e + 8 >= wvalid) hi[e] = 0.f;
+      }
+    }
+    const uint4 qlo = pack16<T>(lo), qhi = pack16<T>(hi);
+    reinterpret_cast<uint4*>(dst)[0] = qlo;
+    reinterpret_cast<uint4*>(dst)[1] = qhi;
+    if constexpr (STATS) {
+      float rl[8], rh[8];
+      unpack16<T>(qlo, rl);
+      unpack16<T>(qhi, rh);
+      if (st_n == 0.f) st_shift = rl[0];
+      const float2 sh = make_float2(-st_shift, -st_shift);
+      // columns past the grid enter as the shift (a zero deviation) and are not counted
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float2 dv = __fadd2_rn(make_float2(e < wvalid ? rl[e] : st_shift, e + 8 < wvalid ? rh[e] : st_shift), sh);
+        st_s1 = __fadd2_rn(st_s1, dv);
+        st_s2 = __ffma2_rn(dv, dv, st_s2);
+      }
+      st_n += (float)min(16, wvalid);
+    }
   };
 
   auto step = [&](const int s) -> bool {
@@ -642,7 +697,7 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
 #pragma unroll
       for (int eh = 0; eh < 2; ++eh) {
         add_taps(0, eh, odd[eh], q0, q1);
-        if (eh == 0 ? row0_ok : row1_ok) store_row(out0 + (size_t)(2 * qd - 1) * bplane + (size_t)eh * g.Wb, odd[eh]);
+        if (eh == 0 ? row0_ok : row1_ok) store_row(out0 + (size_t)(2 * qd - 1) * bplane + (size_t)eh * g.bw, odd[eh]);
       }
     }
     if (s < dcount) {
@@ -664,7 +719,7 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
           }
         }
         if (2 * qd < g.Db && (eh == 0 ? row0_ok : row1_ok))
-          store_row(out0 + (size_t)(2 * qd) * bplane + (size_t)eh * g.Wb, acc);
+          store_row(out0 + (size_t)(2 * qd) * bplane + (size_t)eh * g.bw, acc);
       }
       // big plane 2qd + 1: bias and its first half (a_d = 0, tap 2)
 #pragma unroll
@@ -705,8 +760,29 @@ __global__ void __launch_bounds__(kS2PkThreads, 2)
     const int issued = ring.issued;
     for (int q = issued > kDwSlots ? issued - kDwSlots : 0; q < issued; ++q)
       mbar_wait(&ring.full[q % kDwSlots], (uint32_t)((q / kDwSlots) & 1));
-    raise_device_error(kErrMbarTimeout);
   }
+  if constexpr (STATS) {
+    __shared__ double red[3 * 32];
+    double n = (double)st_n, mean = 0.0, m2 = 0.0;
+    if (st_n > 0.f) {
+      const double s1 = (double)st_s1.x + (double)st_s1.y, s2 = (double)st_s2.x + (double)st_s2.y;
+      mean = (double)st_shift + s1 / n;
+      m2 = fmax(s2 - s1 * s1 / n, 0.0);
+    }
+    __syncthreads();
+    block_merge_stats(n, mean, m2, red);
+    if (threadIdx.x == 0) {
+      const int tiles = pg.tilesW * pg.tilesH * pg.tilesD;
+      const int tile = (td * pg.tilesH + th) * pg.tilesW + tw;
+      GnPartial gp;
+      gp.count = n;
+      gp.mean = mean;
+      gp.m2 = m2;
+      gp.pad = 0.0;
+      stats[(size_t)nc * tiles + tile] = gp;
+    }
+  }
+  if (*abort && threadIdx.x == 0) raise_device_error(kErrMbarTimeout);
 }
 
 }  // namespace mednext

@@ -49,11 +49,15 @@ __device__ __forceinline__ bool vec_ok(const void* p, size_t vol) {
 }
 
 // Standalone statistics: per-thread shifted sums, block Chan merge, one
-// partial per (n, c, chunk).
+// partial per (n, c, chunk).  Each (n, c) volume starts `pitch` elements after
+// the previous one and its first `vol` elements are read, as rows of
+// `row_pitch` elements of which the first `row_len` are statistics (row_len =
+// row_pitch: every element).
 template <typename T>
 __global__ void __launch_bounds__(256) gn_stats_partial_kernel(const T* __restrict__ x,
                                                                GnPartial* __restrict__ part,
-                                                               size_t vol, size_t pitch, int chunks) {
+                                                               size_t vol, size_t pitch, int chunks,
+                                                               int row_pitch, int row_len) {
   using Acc = typename Elem<T>::Acc;
   const int j = blockIdx.x % chunks;
   const size_t nc = blockIdx.x / chunks;
@@ -62,6 +66,7 @@ __global__ void __launch_bounds__(256) gn_stats_partial_kernel(const T* __restri
   const size_t beg = min((size_t)j * per, vol);
   const size_t end = min(beg + per, vol);
   const T* p = x + nc * pitch;
+  const bool masked = row_len < row_pitch;
   Acc cnt = Acc(0), shift = Acc(0), s1 = Acc(0), s2 = Acc(0);
   auto add = [&](Acc v) {
     if (cnt == Acc(0)) shift = v;
@@ -70,19 +75,29 @@ __global__ void __launch_bounds__(256) gn_stats_partial_kernel(const T* __restri
     s2 = fma(d, d, s2);
     cnt += Acc(1);
   };
+  auto in_row = [&](size_t i) { return !masked || (int)(i % (size_t)row_pitch) < row_len; };
   constexpr int E = 16 / (int)sizeof(T);
-  if (vec_ok<T>(x, pitch) && beg % E == 0) {
+  if (vec_ok<T>(x, pitch) && beg % E == 0 && (!masked || row_pitch % E == 0)) {
     // whole 16-byte chunks, then the (at most E-1) trailing elements
     const size_t vend = beg + (end - beg) / E * E;
     for (size_t i = beg + (size_t)threadIdx.x * E; i < vend; i += (size_t)blockDim.x * E) {
       Acc v[E];
       unpack16<T>(__ldg(reinterpret_cast<const uint4*>(p + i)), v);
+      if (masked) {
+        const int col = (int)(i % (size_t)row_pitch);
 #pragma unroll
-      for (int e = 0; e < E; ++e) add(v[e]);
+        for (int e = 0; e < E; ++e)
+          if (col + e < row_len) add(v[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) add(v[e]);
+      }
     }
-    for (size_t i = vend + threadIdx.x; i < end; i += blockDim.x) add(to_acc<T>(__ldg(p + i)));
+    for (size_t i = vend + threadIdx.x; i < end; i += blockDim.x)
+      if (in_row(i)) add(to_acc<T>(__ldg(p + i)));
   } else {
-    for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x) add(to_acc<T>(__ldg(p + i)));
+    for (size_t i = beg + threadIdx.x; i < end; i += blockDim.x)
+      if (in_row(i)) add(to_acc<T>(__ldg(p + i)));
   }
   double n = (double)cnt, mean = 0.0, m2 = 0.0;
   if (cnt > Acc(0)) {
@@ -226,7 +241,9 @@ static __global__ void gn_fold_spans_kernel(GnBwdPartial* __restrict__ part, int
 }
 
 // Backward pass 2: dx = rstd * gamma * (dz - S1/V - xhat * S2/V), with the
-// folded sums of (n, c) at folded[nc * stride].
+// folded sums of (n, c) at folded[nc * stride] and V = vol; all `pitch` elements
+// of each (n, c) row are written (positions past the valid voxels of a pitched
+// row get values without meaning).
 template <typename TD, typename TX, typename TO, typename TG>
 __global__ void __launch_bounds__(256) gn_bwd_apply_kernel(
     const TD* __restrict__ dz, const TX* __restrict__ x, const float* __restrict__ stats,
@@ -241,9 +258,9 @@ __global__ void __launch_bounds__(256) gn_bwd_apply_kernel(
   const float mean = stats[2 * nc], rstd = stats[2 * nc + 1];
   const float gr = rstd * (gamma != nullptr ? param_f(gamma, c) : 1.0f);
   // chunks start on 8-element boundaries (16-byte vectors); trailing chunks may be empty
-  const size_t per = ((vol + chunks - 1) / chunks + 7) / 8 * 8;
-  const size_t beg = min((size_t)j * per, vol);
-  const size_t end = min(beg + per, vol);
+  const size_t per = ((pitch + chunks - 1) / chunks + 7) / 8 * 8;
+  const size_t beg = min((size_t)j * per, pitch);
+  const size_t end = min(beg + per, pitch);
   const TD* g = dz + nc * pitch;
   const TX* xs = x + nc * pitch;
   TO* o = dx + nc * pitch;

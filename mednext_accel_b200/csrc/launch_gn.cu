@@ -31,13 +31,11 @@ int dispatch_gn_finalize(const GnPartial* part, int tiles, int nc, float eps, fl
 }
 
 int dispatch_gn_stats(int dtype, const void* x, GnPartial* part, int64_t nc, int64_t vol, int64_t pitch, int chunks,
-                      float eps,
-                      float* stats, cudaStream_t s) {
+                      int row_pitch, int row_len, float eps, float* stats, cudaStream_t s) {
   int st = MEDNEXT_OK;
   MEDNEXT_T_SWITCH(dtype, T, {
-    gn_stats_partial_kernel<T><<<(unsigned)(nc * chunks), 256, 0, s>>>(static_cast<const T*>(x), part, (size_t)vol,
-                                                                         (size_t)pitch,
-                                                                         chunks);
+    gn_stats_partial_kernel<T><<<(unsigned)(nc * chunks), 256, 0, s>>>(
+        static_cast<const T*>(x), part, (size_t)vol, (size_t)pitch, chunks, row_pitch, row_len);
     st = record_launch();
   });
   if (st != MEDNEXT_OK) return st;

@@ -132,17 +132,19 @@ inline DwS2Geom s2_geom_down(int64_t n, int64_t c, int64_t d, int64_t h, int64_t
   g.N = (int)n; g.C = (int)c;
   g.Db = (int)d; g.Hb = (int)h; g.Wb = (int)w;
   g.Ds = (int)((d + 1) / 2); g.Hs = (int)((h + 1) / 2); g.Ws = (int)((w + 1) / 2);
+  g.bw = (int)w;
   g.bp = (long long)d * h * w;
   return g;
 }
-// pitch: elements between (n, c) volumes of the (2d-1, 2h-1, 2w-1) grid; 0 = contiguous
-inline DwS2Geom s2_geom_up(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t pitch) {
+// row_pitch: elements between consecutive W-rows of the (2d-1, 2h-1, 2w-1) grid
+// (0 = 2w-1, contiguous); the (n, c) volumes are (2d-1)(2h-1) row pitches apart
+inline DwS2Geom s2_geom_up(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int64_t row_pitch) {
   DwS2Geom g{};
   g.N = (int)n; g.C = (int)c;
   g.Ds = (int)d; g.Hs = (int)h; g.Ws = (int)w;
   g.Db = (int)(2 * d - 1); g.Hb = (int)(2 * h - 1); g.Wb = (int)(2 * w - 1);
-  const long long bvol = (long long)g.Db * g.Hb * g.Wb;
-  g.bp = pitch > 0 ? pitch : bvol;
+  g.bw = row_pitch > 0 ? (int)row_pitch : g.Wb;
+  g.bp = (long long)g.Db * g.Hb * g.bw;
   return g;
 }
 
@@ -209,9 +211,13 @@ int dispatch_dw_s2_scatter(int dtype, int k, const void* small, const void* w, c
                            const DwS2Geom& g, cudaStream_t s);
 int dispatch_dw_s2_wgrad(int dtype, int k, const void* big, const void* small, void* dw, void* db, void* ws,
                          const DwS2Geom& g, bool bias_from_big, bool out_f32, cudaStream_t s);
+size_t dwT_fwd_stats_ws(int dtype, int k, const DwS2Geom& g);
+int dispatch_dwT_fwd_stats(int dtype, int k, const void* small, const void* w, const void* b, void* big,
+                           GnPartial* part, float eps, float* stats, const DwS2Geom& g, cudaStream_t s);
 int dispatch_gn_finalize(const GnPartial* part, int tiles, int nc, float eps, float* stats, cudaStream_t s);
+// rows of row_pitch elements of which the first row_len are statistics (equal: all)
 int dispatch_gn_stats(int dtype, const void* x, GnPartial* part, int64_t nc, int64_t vol, int64_t pitch, int chunks,
-                      float eps, float* stats, cudaStream_t s);
+                      int row_pitch, int row_len, float eps, float* stats, cudaStream_t s);
 int dispatch_gn_fwd(int x_dtype, int y_dtype, int g_dtype, const void* x, const float* stats, const void* gamma,
                     const void* beta, void* y, int C, int64_t nc, int64_t vol, cudaStream_t s);
 int dispatch_gn_bwd_partial(int x_dtype, int dz_dtype, const void* dz, const void* x, const float* stats,

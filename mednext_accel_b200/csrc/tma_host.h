@@ -62,14 +62,16 @@ inline bool encode2(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, 
 }
 
 // [d3][d2][d1][d0] tensor, box (b0, b1, 1, 1), no swizzle: one plane tile of a
-// volume per load (the depthwise kernels' halo tiles).
+// volume per load (the depthwise kernels' halo tiles).  row_pitch: elements
+// between consecutive d0-rows (0 = d0); columns past d0 read as zeros.
 template <typename T>
 inline bool encode4(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint32_t b0,
-                    uint32_t b1) {
+                    uint32_t b1, uint64_t row_pitch = 0) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
+  const uint64_t rp = row_pitch > 0 ? row_pitch : d0;
   const cuuint64_t dims[4] = {d0, d1, d2, d3};
-  const cuuint64_t strides[3] = {d0 * sizeof(T), d0 * d1 * sizeof(T), d0 * d1 * d2 * sizeof(T)};
+  const cuuint64_t strides[3] = {rp * sizeof(T), rp * d1 * sizeof(T), rp * d1 * d2 * sizeof(T)};
   const cuuint32_t box[4] = {b0, b1, 1, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return fn(m, tma_dtype<T>(), 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,

@@ -161,18 +161,18 @@ def s2_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True,
     return dw, db
 
 
-def t_forward(x: Tensor, weight: Tensor, bias: Tensor | None, kernel_size: int, pitch: int = 0) -> Tensor:
-    """Transposed stride-2 forward.  With ``pitch`` > 0 the result is returned as an
-    [n, c, pitch] buffer whose rows hold the (2d-1)(2h-1)(2w-1) voxels followed by a
-    zero tail (see :func:`pitched_view`)."""
+def t_forward(x: Tensor, weight: Tensor, bias: Tensor | None, kernel_size: int, row_pitch: int = 0) -> Tensor:
+    """Transposed stride-2 forward: [n, c, 2d-1, 2h-1, 2w-1].  With ``row_pitch`` > 0
+    the result is [n, c, 2d-1, 2h-1, row_pitch]: every W-row is padded to
+    ``row_pitch`` elements with zeros (see :func:`pitched_view`)."""
     nat.require_device(x)
     n, c, d, h, w = _dims(x)
     big = (2 * d - 1, 2 * h - 1, 2 * w - 1)
-    shape = (n, c, pitch) if pitch else (n, c, *big)
+    shape = (n, c, big[0], big[1], int(row_pitch) if row_pitch else big[2])
     y = torch.empty(shape, dtype=x.dtype, device=x.device)
     nat.check(
         nat.load().mednext_dwT_fwd(
-            x.data_ptr(), weight.data_ptr(), nat.ptr(bias), y.data_ptr(), n, c, d, h, w, pitch, kernel_size,
+            x.data_ptr(), weight.data_ptr(), nat.ptr(bias), y.data_ptr(), n, c, d, h, w, int(row_pitch), kernel_size,
             nat.dtype_code(x.dtype), nat.stream(),
         ),
         "mednext_dwT_fwd",
@@ -180,26 +180,56 @@ def t_forward(x: Tensor, weight: Tensor, bias: Tensor | None, kernel_size: int, 
     return y
 
 
+def t_forward_stats(x: Tensor, weight: Tensor, bias: Tensor | None, kernel_size: int, gn_eps: float,
+                    row_pitch: int = 0) -> tuple[Tensor, Tensor]:
+    """:func:`t_forward` plus the GroupNorm statistics of its output over the grid
+    voxels: float32 [n*c, 2] (mean, rstd)."""
+    nat.require_device(x)
+    lib = nat.load()
+    n, c, d, h, w = _dims(x)
+    big = (2 * d - 1, 2 * h - 1, 2 * w - 1)
+    y = torch.empty((n, c, big[0], big[1], int(row_pitch) if row_pitch else big[2]), dtype=x.dtype, device=x.device)
+    stats = torch.empty((n * c, 2), dtype=torch.float32, device=x.device)
+    code = nat.dtype_code(x.dtype)
+    ws = nat.workspace(lib.mednext_dwT_fwd_workspace_size(n, c, d, h, w, int(row_pitch), kernel_size, code), x.device)
+    nat.check(
+        lib.mednext_dwT_fwd_stats(
+            x.data_ptr(), weight.data_ptr(), nat.ptr(bias), y.data_ptr(), stats.data_ptr(), float(gn_eps),
+            ws.data_ptr(), ws.numel(), n, c, d, h, w, int(row_pitch), kernel_size, code, nat.stream(),
+        ),
+        "mednext_dwT_fwd_stats",
+    )
+    return y, stats
+
+
 def pitched_view(buf: Tensor, spatial: tuple[int, int, int]) -> Tensor:
-    """The [n, c, *spatial] view of the valid voxels of an [n, c, pitch] buffer."""
-    vox = spatial[0] * spatial[1] * spatial[2]
-    return buf[:, :, :vox].unflatten(2, spatial)
+    """The [n, c, *spatial] view of the grid voxels of a row-pitched
+    [n, c, d, h, row_pitch] buffer (its first ``spatial[2]`` columns)."""
+    return buf[..., : int(spatial[2])]
+
+
+def _row_pitch(t: Tensor, width: int) -> int:
+    """W-row pitch of a [n, c, d, h, pitch] grid whose rows hold ``width`` voxels
+    (0 when the rows are packed)."""
+    if t.ndim != 5 or int(t.shape[4]) < width:
+        raise ValueError(f"expected a [n, c, d, h, >= {width}] tensor")
+    return 0 if int(t.shape[4]) == width else int(t.shape[4])
 
 
 def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int, small: tuple[int, int, int] | None = None,
             addend: Tensor | None = None) -> Tensor:
-    """Input grad of the transposed conv.  ``grad`` is [n, c, 2d-1, 2h-1, 2w-1], or a
-    pitched [n, c, pitch] buffer when ``small`` = (d, h, w) is given.  ``addend``
-    (the output's shape) is added to the result."""
+    """Input grad of the transposed conv.  ``grad`` is [n, c, 2d-1, 2h-1, 2w-1] or,
+    when ``small`` = (d, h, w) is given, a row-pitched [n, c, 2d-1, 2h-1, pitch]
+    buffer (pad columns ignored).  ``addend`` (the output's shape) is added to the
+    result."""
     nat.require_device(grad)
     n, c = int(grad.shape[0]), int(grad.shape[1])
-    pitch = 0
     if small is not None:
-        d, h, w = small
-        pitch = int(grad.shape[2])
+        d, h, w = (int(v) for v in small)
     else:
         _, _, od, oh, ow = _dims(grad)
         d, h, w = (od + 1) // 2, (oh + 1) // 2, (ow + 1) // 2
+    pitch = _row_pitch(grad, 2 * w - 1)
     out = torch.empty((n, c, d, h, w), dtype=grad.dtype, device=grad.device)
     if addend is not None:
         _check_addend(addend, out.shape, out.dtype, "addend")
@@ -216,12 +246,12 @@ def t_dgrad(grad: Tensor, weight: Tensor, kernel_size: int, small: tuple[int, in
 
 def t_wgrad(x: Tensor, grad: Tensor, kernel_size: int, want_bias: bool = True,
             out_dtype: torch.dtype | None = None) -> tuple[Tensor, Tensor | None]:
-    """Weight (and bias) grad of the transposed conv; ``grad`` may be a pitched
-    [n, c, pitch] buffer (3-D) or [n, c, 2d-1, 2h-1, 2w-1]."""
+    """Weight (and bias) grad of the transposed conv; ``grad`` is
+    [n, c, 2d-1, 2h-1, 2w-1] or row-pitched [n, c, 2d-1, 2h-1, pitch]."""
     nat.require_device(x)
     lib = nat.load()
     n, c, d, h, w = _dims(x)
-    pitch = int(grad.shape[2]) if grad.ndim == 3 else 0
+    pitch = _row_pitch(grad, 2 * w - 1)
     code = nat.dtype_code(x.dtype)
     dw, db, suffix = _wgrad_outputs(x, kernel_size, want_bias, out_dtype)
     ws = nat.workspace(lib.mednext_dwT_wgrad_workspace_size(n, c, d, h, w, kernel_size, code), x.device)
@@ -242,12 +272,13 @@ def _check_addend(t: Tensor, shape, dtype, name: str) -> None:
 
 
 def pad_front_add(v: Tensor, spatial: tuple[int, int, int], addend: Tensor | None = None) -> Tensor:
-    """``F.pad(pitched_view(v, spatial), (1, 0) * 3) + addend`` in one pass: ``v`` is a
-    pitched [n, c, pitch] buffer of the (d, h, w) grid, ``addend`` (optional) has the
-    padded shape [n, c, d+1, h+1, w+1] and v's dtype."""
+    """``F.pad(pitched_view(v, spatial), (1, 0) * 3) + addend`` in one pass: ``v`` is the
+    (d, h, w) grid, packed or row-pitched [n, c, d, h, pitch]; ``addend`` (optional) has
+    the padded shape [n, c, d+1, h+1, w+1] and v's dtype."""
     nat.require_device(v)
     n, c = int(v.shape[0]), int(v.shape[1])
     d, h, w = (int(s) for s in spatial)
+    pitch = _row_pitch(v, w)
     out = torch.empty((n, c, d + 1, h + 1, w + 1), dtype=v.dtype, device=v.device)
     if addend is not None:
         if addend.shape != out.shape or addend.dtype != v.dtype:
@@ -255,43 +286,44 @@ def pad_front_add(v: Tensor, spatial: tuple[int, int, int], addend: Tensor | Non
         addend = addend.contiguous()
     nat.check(
         nat.load().mednext_pad_front_add(
-            v.data_ptr(), nat.ptr(addend), out.data_ptr(), n, c, d, h, w, int(v.shape[2]),
-            nat.dtype_code(v.dtype), nat.stream(),
+            v.data_ptr(), nat.ptr(addend), out.data_ptr(), n, c, d, h, w, pitch, nat.dtype_code(v.dtype), nat.stream(),
         ),
         "mednext_pad_front_add",
     )
     return out
 
 
-def unpad_front(padded: Tensor, pitch: int) -> Tensor:
-    """The pitched [n, c, pitch] buffer of ``padded[:, :, 1:, 1:, 1:]`` with a zero tail."""
+def unpad_front(padded: Tensor, row_pitch: int = 0) -> Tensor:
+    """``padded[:, :, 1:, 1:, 1:]`` as [n, c, d, h, row_pitch] (0: packed rows), zeros in
+    the pad columns."""
     nat.require_device(padded)
     n, c = int(padded.shape[0]), int(padded.shape[1])
     d, h, w = (int(s) - 1 for s in padded.shape[2:])
     padded = padded.contiguous()
-    v = torch.empty((n, c, int(pitch)), dtype=padded.dtype, device=padded.device)
+    v = torch.empty((n, c, d, h, int(row_pitch) if row_pitch else w), dtype=padded.dtype, device=padded.device)
     nat.check(
         nat.load().mednext_unpad_front(
-            padded.data_ptr(), v.data_ptr(), n, c, d, h, w, int(pitch), nat.dtype_code(padded.dtype), nat.stream(),
+            padded.data_ptr(), v.data_ptr(), n, c, d, h, w, int(row_pitch), nat.dtype_code(padded.dtype), nat.stream(),
         ),
         "mednext_unpad_front",
     )
     return v
 
 
-def upsample2_fill(small: Tensor, bias: Tensor | None, pitch: int) -> Tensor:
-    """[n, c, pitch] buffer holding the (2d-1, 2h-1, 2w-1) grid with small[m] at the
-    all-even positions 2m, bias[c] elsewhere and a zero pitch tail: the output of a
+def upsample2_fill(small: Tensor, bias: Tensor | None, row_pitch: int = 0) -> Tensor:
+    """[n, c, 2d-1, 2h-1, row_pitch] (0: 2w-1) buffer holding small[m] at the all-even
+    positions 2m, bias[c] elsewhere and zeros in the pad columns: the output of a
     1x1x1, stride-2 ConvTranspose3d whose per-voxel product (bias included) is
     ``small`` [n, c, d, h, w]."""
     nat.require_device(small)
     n, c, d, h, w = _dims(small)
     small = small.contiguous()
-    big = torch.empty((n, c, int(pitch)), dtype=small.dtype, device=small.device)
+    big = torch.empty((n, c, 2 * d - 1, 2 * h - 1, int(row_pitch) if row_pitch else 2 * w - 1), dtype=small.dtype,
+                      device=small.device)
     b = bias.float().contiguous() if bias is not None else None
     nat.check(
         nat.load().mednext_upsample2_fill(
-            small.data_ptr(), nat.ptr(b), big.data_ptr(), n, c, d, h, w, int(pitch), nat.dtype_code(small.dtype),
+            small.data_ptr(), nat.ptr(b), big.data_ptr(), n, c, d, h, w, int(row_pitch), nat.dtype_code(small.dtype),
             nat.stream(),
         ),
         "mednext_upsample2_fill",

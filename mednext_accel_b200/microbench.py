@@ -51,7 +51,10 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
     w3b = (torch.randn(2 * C, 1, 3, 3, 3, device=dev) * 0.2).to(bf)
     ys2 = r(1, C, 64, 64, 64)
     xs, ybig = r(1, 2 * C, 64, 64, 64), r(1, 2 * C, 127, 127, 127)
+    # the fused up block's layout: W-rows of the 127^3 grid padded to 128 elements
+    ybig_p = r(1, 2 * C, 127, 127, 128)
     up_bytes = 2 * C * 2 * (64**3 + 127**3)
+    dy_pad, t_up, y_up = r(1, C, 128, 128, 128), r(1, 2 * C, 127, 127, 128), r(1, C, 127, 127, 128)
     return {
         "pw expand fwd (GroupNorm prologue, bias)": (
             lambda: pw_gemm(t, we, RC, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g, pro_beta=bb, bias=b1),
@@ -92,6 +95,14 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
         "dwT fwd C64 64^3->127^3 k3": (lambda: dwk.t_forward(xs, w3b, None, 3), up_bytes),
         "dwT dgrad C64 k3": (lambda: dwk.t_dgrad(ybig, w3b, 3), up_bytes),
         "dwT wgrad C64 k3": (lambda: dwk.t_wgrad(xs, ybig, 3), up_bytes),
+        "dwT fwd C64 row-pitched k3": (lambda: dwk.t_forward(xs, w3b, None, 3, row_pitch=128), up_bytes),
+        "dwT dgrad C64 row-pitched + addend k3": (
+            lambda: dwk.t_dgrad(ybig_p, w3b, 3, small=(64, 64, 64), addend=xs), up_bytes + 2 * C * 2 * 64**3),
+        "dwT wgrad C64 row-pitched k3": (lambda: dwk.t_wgrad(xs, ybig_p, 3), up_bytes),
+        "gn stats C64 row-pitched 127^3": (lambda: gn_stats(t_up, 1e-5, row_len=127), 2 * C * 2 * 127**3),
+        "unpad_front C32 128^3 -> row-pitched": (lambda: dwk.unpad_front(dy_pad, 128), 2 * C * 2 * 128**3),
+        "pad_front_add C32 row-pitched -> 128^3": (
+            lambda: dwk.pad_front_add(y_up, (127, 127, 127), dy_pad), 3 * C * 2 * 128**3),
         "gn stats C32": (lambda: gn_stats(t, 1e-5), C * 2 * V),
         "gn bwd C32 (fold + apply)": (lambda: gn_backward_from_partials(dz, t, stats, g, part), 3 * C * 2 * V),
     }

@@ -240,15 +240,28 @@ def pw_gn_bwd_fused(
     return dz, ws, dw, db
 
 
-def gn_stats(x: Tensor, eps: float, vox: int | None = None) -> Tensor:
+def gn_stats(x: Tensor, eps: float, vox: int | None = None, row_len: int | None = None) -> Tensor:
     """Per-(n, c) mean / rstd.  ``vox``: number of valid voxels when ``x`` is a pitched
-    [n, c, pitch] buffer (only the first ``vox`` of each row are statistics)."""
+    [n, c, pitch] buffer (only the first ``vox`` of each row are statistics).
+    ``row_len``: x is row-pitched [n, c, ..., row_pitch] and only the first
+    ``row_len`` elements of each last-axis row are statistics."""
     nat.require_device(x)
     lib = nat.load()
     n, c = int(x.shape[0]), int(x.shape[1])
     rows = _vox(x)
-    vox = rows if vox is None else int(vox)
     stats = torch.empty((n * c, 2), dtype=torch.float32, device=x.device)
+    if row_len is not None:
+        rp = int(x.shape[-1])
+        ws = nat.workspace(lib.mednext_gn_stats_workspace_size(n, c, rows), x.device)
+        nat.check(
+            lib.mednext_gn_stats_rows(
+                x.data_ptr(), stats.data_ptr(), ws.data_ptr(), ws.numel(), n, c, rows // rp, int(row_len), rp,
+                float(eps), nat.dtype_code(x.dtype), nat.stream(),
+            ),
+            "mednext_gn_stats_rows",
+        )
+        return stats
+    vox = rows if vox is None else int(vox)
     ws = nat.workspace(lib.mednext_gn_stats_workspace_size(n, c, vox), x.device)
     nat.check(
         lib.mednext_gn_stats(

@@ -243,16 +243,19 @@ def test_loss_curve_matches_native_path_over_adamw_steps():
         assert abs(losses[0] - losses[1]) <= 1e-2 * abs(losses[1]), losses
 
 
-@pytest.mark.parametrize("spatial", [(7, 9, 11), (15, 15, 15), (127, 127, 127)])
+@pytest.mark.parametrize("spatial,pitch", [((7, 9, 11), 0), ((7, 9, 11), 16), ((15, 15, 15), 16),
+                                           ((127, 127, 127), 128), ((63, 63, 63), 64)])
 @pytest.mark.parametrize("with_addend", [False, True])
-def test_pad_front_and_unpad_match_torch(spatial, with_addend):
+def test_pad_front_and_unpad_match_torch(spatial, pitch, with_addend):
+    """pad_front_add / unpad_front on packed and row-pitched grids (the 16-byte
+    shifted-copy path when the pitch is the padded row length) equal torch's pad,
+    add and slice exactly; unpad writes zeros into the pad columns."""
     from mednext_accel_b200 import depthwise as dwk
 
     n, c = 2, 3
-    vox = spatial[0] * spatial[1] * spatial[2]
-    pitch = (vox + 7) // 8 * 8
-    gen = torch.Generator().manual_seed(_seed("pad", spatial))
-    v = torch.randn((n, c, pitch), generator=gen).to(torch.bfloat16).cuda()
+    rp = pitch or spatial[2]
+    gen = torch.Generator().manual_seed(_seed("pad", spatial, pitch))
+    v = torch.randn((n, c, spatial[0], spatial[1], rp), generator=gen).to(torch.bfloat16).cuda()
     padded_shape = (n, c, *(s + 1 for s in spatial))
     addend = torch.randn(padded_shape, generator=gen).to(torch.bfloat16).cuda() if with_addend else None
     got = dwk.pad_front_add(v, spatial, addend)

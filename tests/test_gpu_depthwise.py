@@ -271,6 +271,85 @@ def test_stride2_input_grad_tma_kernel_is_bit_exact_with_fp32_kernel(dtype, shap
     assert nat.device_error() == 0
 
 
+# Up-block grids: small (d, h, w) inputs of the transposed conv; the fused up
+# block stores its (2d-1, 2h-1, 2w-1) tensors with W-rows padded to a multiple of 8.
+UP_SHAPES = [
+    (1, 64, 64, 64, 64),     # the benchmark's level-0 up block (C64 64^3 -> 127^3)
+    (2, 3, 8, 10, 16),       # ragged row tile, two samples
+    (1, 4, 5, 7, 8),         # odd small depth and height
+    (1, 2, 4, 4, 128),       # two 64-wide tiles along W
+    (1, 3, 6, 6, 12),        # small W not a multiple of 8: packed-FMA path declines
+]
+
+
+def _pitched(t: torch.Tensor, pitch: int, fill: float) -> torch.Tensor:
+    """t [n, c, D, H, W] copied into [n, c, D, H, pitch] with `fill` in the pad columns."""
+    out = torch.full((*t.shape[:4], pitch), fill, dtype=t.dtype, device=t.device)
+    out[..., : t.shape[4]] = t
+    return out
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", UP_SHAPES)
+def test_up_block_row_pitched_kernels_match_the_packed_fp32_kernels(dtype, shape):
+    """The transposed conv on the row-pitched layout of the fused up block: forward
+    and input grad (k = 3, 16-bit, TMA plane ring with packed FMAs where the rows are
+    2w elements apart) give the fp32 kernels' results on packed grids rounded once;
+    the forward writes zeros into the pad columns; input and weight grads ignore
+    whatever the pad columns of dy hold; the weight grad matches the fp32 kernel to
+    the output's rounding and repeats exactly."""
+    seed = seed_of("up-rows", str(dtype), shape)
+    n, c, d, h, w = shape
+    big = (n, c, 2 * d - 1, 2 * h - 1, 2 * w - 1)
+    pitch = (2 * w - 1 + 7) // 8 * 8
+    xs = rand(shape, dtype, seed).cuda()
+    wt = rand((c, 1, 3, 3, 3), dtype, seed + 1, scale=0.2).cuda()
+    b = rand((c,), dtype, seed + 2).cuda()
+    y = dwk.t_forward(xs, wt, b, 3, row_pitch=pitch)
+    assert tuple(y.shape) == (*big[:4], pitch)
+    want = dwk.t_forward(xs.float(), wt.float(), b.float(), 3).to(dtype)
+    assert torch.equal(dwk.pitched_view(y, big[2:]), want)
+    assert torch.all(y[..., big[4]:] == 0)
+    # with the GroupNorm statistics of the output (fused into the packed kernel)
+    from mednext_accel_b200.pointwise import gn_stats
+
+    y2, st = dwk.t_forward_stats(xs, wt, b, 3, 1e-5, row_pitch=pitch)
+    assert torch.equal(y2, y)
+    torch.testing.assert_close(st, gn_stats(y, 1e-5, row_len=big[4]), rtol=1e-5, atol=1e-6)
+    dy = rand(big, dtype, seed + 3).cuda()
+    dyp = _pitched(dy, pitch, 1000.0)
+    add = rand(shape, dtype, seed + 4).cuda()
+    for addend in (None, add):
+        dx = dwk.t_dgrad(dyp, wt, 3, small=(d, h, w), addend=addend)
+        want = dwk.t_dgrad(dy.float(), wt.float(), 3, addend=None if addend is None else addend.float())
+        assert torch.equal(dx, want.to(dtype))
+    dw, db = dwk.t_wgrad(xs, dyp, 3)
+    dw32, db32 = dwk.t_wgrad(xs.float(), dy.float(), 3)
+    for got, want in ((dw, dw32), (db, db32)):
+        scale = want.abs().max().item()
+        torch.testing.assert_close(got.float(), want, rtol=2.0**-7, atol=1e-4 * scale)
+    dw2, db2 = dwk.t_wgrad(xs, dyp, 3)
+    assert torch.equal(dw, dw2) and torch.equal(db, db2)
+    assert nat.device_error() == 0
+
+
+@pytest.mark.parametrize("shape,pitch", [((1, 64, 127, 127, 127), 128), ((2, 3, 15, 19, 31), 32),
+                                         ((1, 5, 7, 9, 11), 16)])
+def test_groupnorm_statistics_of_row_pitched_grid(shape, pitch):
+    """gn_stats over the valid columns of a row-pitched grid whose pad columns hold
+    large values: the statistics of the packed grid (fp64 reference, 1e-5)."""
+    from mednext_accel_b200.pointwise import gn_stats
+
+    seed = seed_of("gn-rows", shape)
+    t = (rand(shape, torch.float32, seed) * 3 + 0.5).to(torch.bfloat16).cuda()
+    st = gn_stats(_pitched(t, pitch, 500.0), 1e-5, row_len=shape[4]).cpu().double()
+    flat = t.double().reshape(shape[0] * shape[1], -1)
+    mean = flat.mean(dim=1).cpu()
+    rstd = (1.0 / torch.sqrt(flat.var(dim=1, unbiased=False) + 1e-5)).cpu()
+    torch.testing.assert_close(st[:, 0], mean, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(st[:, 1], rstd, rtol=1e-5, atol=1e-5)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_weight_grads_with_fp32_output_equal_the_cast_of_the_16bit_ones(dtype):
     """The _f32out weight-grad entry points write what casting the 16-bit result to fp32

@@ -89,3 +89,18 @@ def test_pointwise_workspace_sizes():
     # one 16-byte partial per (channel, 128-voxel tile, 32-voxel quarter)
     assert lib.mednext_pw_fwd_workspace_size(1, 128, 32, 128**3, nat.EPI_GN_BWD_STATS) == 32 * (128**3 // 128) * 4 * 16
     assert lib.mednext_pw_wgrad_workspace_size(1, 32, 64, 128**3) > 0
+
+
+@pytest.mark.parametrize("small", [(1, 1, 1), (2, 3, 4), (4, 4, 4), (5, 7, 8), (8, 8, 8), (64, 64, 64), (3, 9, 24)])
+@pytest.mark.parametrize("dtype", [0, 1, 2])
+def test_transposed_forward_workspace_planning_on_every_grid(small, dtype):
+    """The up block's forward-with-statistics workspace query runs the host-side tile
+    planner for every grid, including those the packed-FMA kernel declines (small
+    W below or not a multiple of 8): it answers a size, never traps."""
+    lib = nat.load()
+    d, h, w = small
+    for pitch in (0, (2 * w - 1 + 7) // 8 * 8):
+        for k in (1, 3, 5):
+            assert lib.mednext_dwT_fwd_workspace_size(2, 6, d, h, w, pitch, k, dtype) > 0
+    if w > 1:  # a pitch below the row length is rejected
+        assert lib.mednext_dwT_fwd_workspace_size(2, 6, d, h, w, 2 * w - 2, 3, dtype) == 0
