@@ -233,6 +233,33 @@ __global__ void __launch_bounds__(kS2Warps * 32) upsample2_fill_kernel(const T* 
   const T* src = small + ((size_t)nc * g.Ds + (id >> 1)) * ((size_t)g.Hs * g.Ws);
   T* dst = big + (size_t)nc * (size_t)g.bp + (size_t)id * g.Hb * g.bw;
   const T zero = from_acc<T>(0.0f);
+  if constexpr (sizeof(T) == 2) {
+    // the up block's row-pitched grid (bw = 2 Ws, Ws a multiple of 4): one 16-byte
+    // chunk of 8 big columns per thread; on an all-even row its even columns are
+    // small[4j .. 4j+3] (one 8-byte load), every other element is the fill, and
+    // the pad column gets zero
+    if (g.bw == 2 * g.Ws && g.Ws % 4 == 0 && (reinterpret_cast<uintptr_t>(big) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(small) & 7) == 0) {
+      const uint32_t f = (uint32_t)reinterpret_cast<const unsigned short&>(fill);
+      const int cpr = g.bw / 8;
+      for (int q = threadIdx.x; q < g.Hb * cpr; q += blockDim.x) {
+        const int ih = q / cpr, j = q - ih * cpr;
+        uint32_t o[4] = {f | (f << 16), f | (f << 16), f | (f << 16), f | (f << 16)};
+        if (((id | ih) & 1) == 0) {
+          const uint2 sv = __ldg(reinterpret_cast<const uint2*>(src + (size_t)(ih >> 1) * g.Ws + 4 * j));
+          o[0] = (sv.x & 0xffffu) | (f << 16);
+          o[1] = (sv.x >> 16) | (f << 16);
+          o[2] = (sv.y & 0xffffu) | (f << 16);
+          o[3] = (sv.y >> 16) | (f << 16);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (8 * j + e >= g.Wb) o[e >> 1] &= (e & 1) ? 0x0000ffffu : 0xffff0000u;
+        reinterpret_cast<uint4*>(dst + (size_t)ih * g.bw)[j] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      return;
+    }
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int ih = warp; ih < g.Hb; ih += kS2Warps) {
     const bool even_row = ((id | ih) & 1) == 0;

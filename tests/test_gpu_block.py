@@ -269,6 +269,27 @@ def test_pad_front_and_unpad_match_torch(spatial, pitch, with_addend):
     assert torch.equal(back, want_back)
 
 
+@pytest.mark.parametrize("small,pitch", [((8, 8, 8), 16), ((64, 64, 64), 128), ((3, 5, 6), 0), ((4, 4, 12), 24)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_upsample2_fill_matches_torch(small, pitch, with_bias):
+    """upsample2_fill: small[m] at the all-even big positions 2m, the bias elsewhere, zeros
+    in the pad columns, on packed and row-pitched big grids (the 16-byte path where the
+    pitch is 2w)."""
+    from mednext_accel_b200 import depthwise as dwk
+
+    n, c = 2, 3
+    gen = torch.Generator().manual_seed(_seed("upsample", small, pitch))
+    s = torch.randn((n, c, *small), generator=gen).to(torch.bfloat16).cuda()
+    b = torch.randn((c,), generator=gen).cuda() if with_bias else None
+    got = dwk.upsample2_fill(s, b, pitch)
+    big = tuple(2 * v - 1 for v in small)
+    fill = b.to(torch.bfloat16) if b is not None else torch.zeros(c, dtype=torch.bfloat16, device="cuda")
+    want = fill.view(1, c, 1, 1, 1).expand(n, c, *big).clone()
+    want[:, :, ::2, ::2, ::2] = s
+    assert torch.equal(dwk.pitched_view(got, big), want)
+    assert torch.all(got[..., big[2]:] == 0)
+
+
 def test_up_block_skip_addend_is_fused_exactly():
     """block(x, addend=skip) == block(x) + skip, and the skip's grad is dy."""
     block = make_block("up", 32, 16, 2, 3, 7)
