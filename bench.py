@@ -27,6 +27,13 @@ package from ``baseline/_ref`` on the GPU: ``mednext_base(...,
 optimization="auto")`` compiled with ``torch.compile(mode="default",
 fullgraph=True)`` and ``cudnn.benchmark``, median of per-step CUDA events, as the
 reference's benchmarks/implementations.py:137-190 does.
+
+``--workload`` (opt-in) times the other shapes of the reference's benchmark
+suite on the same path, without the CPU and roofline legs: ``large-k5``
+(MedNeXt-Large k5, block counts [3,4,8,8,8,8,8,4,3], 2 samples per GPU,
+all-expansion-stage activation checkpointing) and ``block-k5`` (one MedNeXtBlock,
+C = 64, R = 4, k = 5, on a 2x64x64^3 input: forward and backward).  The line
+adds the peak allocated device memory.
 """
 
 from __future__ import annotations
@@ -65,6 +72,9 @@ def parse_args(argv=None):
                    help="reference-gpu: the reference factory's optimization argument (auto or reference)")
     p.add_argument("--ref-eager", action="store_true", help="reference-gpu: skip torch.compile")
     p.add_argument("--bucket-mb", type=float, default=6.0, help="gradient all-reduce bucket size (fp32 MB)")
+    p.add_argument("--workload", choices=tuple(WORKLOADS), default="base-k3",
+                   help="base-k3: the headline step (default); large-k5: MedNeXt-Large k5, 2 samples per GPU, "
+                        "all-expansion-stage checkpointing; block-k5: one C64 R4 k5 block forward + backward")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--spatial", type=int, default=SPATIAL, help=argparse.SUPPRESS)
     p.add_argument("--profile-step", action="store_true",
@@ -91,6 +101,14 @@ def downsampled_targets(target: torch.Tensor) -> dict[tuple[int, ...], torch.Ten
         else:
             out[size] = F.interpolate(target[:, None].float(), size=size, mode="nearest")[:, 0].long()
     return out
+
+
+WORKLOADS = {
+    "base-k3": "MedNeXt-Base k3 {S}^3 B1/GPU train step: 5-head deep-supervision CE + AdamW",
+    "large-k5": ("MedNeXt-Large k5 {S}^3 B2/GPU train step, all-expansion-stage activation checkpointing: "
+                 "5-head deep-supervision CE + AdamW"),
+    "block-k5": "one MedNeXtBlock C64 R4 k5 forward + backward on 2x64x{S}^3 input, bf16 autocast",
+}
 
 
 def five_head_loss(heads, targets):
@@ -475,31 +493,62 @@ def run_ours(args) -> int:
     import mednext_accel_b200 as mx
     from mednext_accel_b200 import _native as nat
     from mednext_accel_b200.data_parallel import GradientBucketReducer, broadcast_parameters
+    from mednext_accel_b200.adaptive import ModelOptimizationContext
 
     torch.backends.cudnn.benchmark = True
     S = args.spatial
+    wl = args.workload
     torch.manual_seed(0)
-    model = mx.mednext_base(in_channels=1, out_channels=3, kernel_size=3, deep_supervision=True).to(device).train()
-    broadcast_parameters(model)
-    reducer = GradientBucketReducer(model, bucket_cap_mb=args.bucket_mb)
-    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True, capturable=True)
-
     gen = torch.Generator().manual_seed(1000 + rank)
-    x_host = torch.randn((1, 1, S, S, S), generator=gen).pin_memory()
-    t_host = torch.randint(0, 3, (1, S, S, S), generator=gen).pin_memory()
-    x = x_host.to(device)
-    target = t_host.to(device)
-    targets = downsampled_targets(target)
+    if wl == "block-k5":
+        # one MedNeXtBlock forward + backward: y = block(x), then y.backward(dy)
+        S = 64 if args.spatial == SPATIAL else S
+        block = mx.MedNeXtBlock(spatial_dims=3, in_channels=64, out_channels=64, expansion_ratio=4, kernel_size=5)
+        mx.install_adaptive_operators(block, resolver=mx.PolicyResolver(),
+                                      model_context=ModelOptimizationContext("mednext_v1", "base", "none"))
+        block = block.to(device).train()
+        x_host = torch.randn((2, 64, S, S, S), generator=gen).pin_memory()
+        t_host = torch.randn((2, 64, S, S, S), generator=gen).to(torch.bfloat16).pin_memory()  # upstream grad
+        x = x_host.to(device).requires_grad_()
+        target = t_host.to(device)
+        reducer = None
 
-    def step():
-        reducer.zero_grad()
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            heads = model(x)
-            loss = five_head_loss(heads, targets)
-        loss.backward()
-        reducer.finish()
-        opt.step()
-        return loss
+        def step():
+            for prm in block.parameters():
+                prm.grad = None
+            x.grad = None
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                y = block(x)
+            y.backward(target)
+            return y[0, 0, 0, 0, :1].float().sum()
+    else:
+        if wl == "large-k5":
+            model = mx.mednext_large(in_channels=1, out_channels=3, kernel_size=5, deep_supervision=True,
+                                     checkpointing=mx.CheckpointConfig("expansion"))
+            batch = 2
+        else:
+            model = mx.mednext_base(in_channels=1, out_channels=3, kernel_size=3, deep_supervision=True)
+            batch = 1
+        model = model.to(device).train()
+        broadcast_parameters(model)
+        reducer = GradientBucketReducer(model, bucket_cap_mb=args.bucket_mb)
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-4, fused=True, capturable=True)
+        x_host = torch.randn((batch, 1, S, S, S), generator=gen).pin_memory()
+        t_host = torch.randint(0, 3, (batch, S, S, S), generator=gen).pin_memory()
+        x = x_host.to(device)
+        target = t_host.to(device)
+    targets = downsampled_targets(target) if wl != "block-k5" else {}
+
+    if wl != "block-k5":
+        def step():
+            reducer.zero_grad()
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                heads = model(x)
+                loss = five_head_loss(heads, targets)
+            loss.backward()
+            reducer.finish()
+            opt.step()
+            return loss
 
     # Warm-up on the stream the graph is captured on (required before capture).
     # Autograd's AccumulateGrad nodes remember the stream of their first use, so
@@ -579,7 +628,8 @@ def run_ours(args) -> int:
         dist.barrier()
     e0.record()
     for _ in range(e2e_steps):
-        x.copy_(x_host, non_blocking=True)
+        with torch.no_grad():
+            x.copy_(x_host, non_blocking=True)
         target.copy_(t_host, non_blocking=True)
         for size, t in targets.items():
             if t is not target:
@@ -593,12 +643,14 @@ def run_ours(args) -> int:
         dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e.item()) / e2e_steps
 
-    roof = depthwise_backward_roofline(device) if rank == 0 else None
-    roof_gemm = compress_forward_roofline(device) if rank == 0 else None
+    headline = wl == "base-k3"
+    roof = depthwise_backward_roofline(device) if rank == 0 and headline else None
+    roof_gemm = compress_forward_roofline(device) if rank == 0 and headline else None
     dev_err = nat.device_error()
+    peak_mib = round(torch.cuda.max_memory_allocated(device) / 2**20)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and headline:
         cpu_ms, info, timed = cpu_reference_step_ms(3, spatial=S, warmup=1)
         cpu = {"value": round(cpu_ms, 1), "unit": "ms", "steps": timed, **info}
 
@@ -623,8 +675,8 @@ def run_ours(args) -> int:
         "dtype": "bf16",
         "data": "synthetic",
         "config": {
-            "workload": f"MedNeXt-Base k3 {S}^3 B1/GPU train step: 5-head deep-supervision CE + AdamW (config 3)",
-            "global_batch": world,
+            "workload": WORKLOADS[wl].format(S=S),
+            "global_batch": world * (2 if wl != "base-k3" else 1),
             "spatial": S,
             "parallelism": f"dp{world}",
             "step_mode": mode,
@@ -637,6 +689,7 @@ def run_ours(args) -> int:
         "gpu_launches": int(per_step_launches * args.steps),
         "clocks": clocks.summary(),
         "final_loss": round(final_loss, 5),
+        "peak_allocated_mib": peak_mib,
         "device_error": dev_err,
     }
     print(json.dumps(line), flush=True)
