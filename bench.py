@@ -662,7 +662,7 @@ def run_ours(args) -> int:
     if rank != 0:
         return 0
     line = {
-        "metric": METRIC,
+        "metric": METRIC if headline else f"{wl} step ms on B200 (bf16; see config.workload)",
         "value": round(ms, 3),
         "unit": "ms",
         "n_gpus": world,

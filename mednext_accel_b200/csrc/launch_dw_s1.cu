@@ -84,9 +84,37 @@ int try_s1_conv_pk(const void* x, const void* wgt, const void* bias, const void*
   }
 }
 
+// k = 5 / 7 on 16-bit types on the tensor cores (the plan decided: its GroupNorm
+// partials follow the tensor-core tiling, so there is no fallback from here).
+template <typename T, int K, bool STATS, bool ADD>
+int launch_s1_conv_tc(const void* x, const void* wgt, const void* bias, const void* addend, void* y, GnPartial* st,
+                      const S1Plan& p, int flip, cudaStream_t s) {
+  const DwTcGeom& t = p.tc;
+  CUtensorMap m;
+  if (!tma::encode_dw_tc<T>(&m, x, (uint64_t)t.W, (uint64_t)t.H, (uint64_t)t.D, (uint64_t)t.N * t.C, (uint32_t)t.Hp,
+                            (uint32_t)t.Dp, (uint32_t)t.chunks))
+    return MEDNEXT_ERR_CUDA;
+  const size_t smem = dw_tc_smem(t);
+  auto kern = dw_s1_conv_tc_kernel<T, K, STATS, ADD>;
+  if (const int rc = ensure_smem(kern, smem)) return rc;
+  const long long ctas = (long long)t.N * t.C * t.tilesW * t.tilesH * t.tilesD;
+  kern<<<(unsigned)ctas, kDwTcThreads, smem, s>>>(m, static_cast<const T*>(wgt), static_cast<const T*>(bias),
+                                                   static_cast<const T*>(addend), static_cast<T*>(y), st, t, flip);
+  return record_launch();
+}
+
 template <typename T, int K>
 int launch_s1_conv(const void* x, const void* wgt, const void* bias, const void* addend, void* y, GnPartial* st,
                    const S1Plan& p, int flip, cudaStream_t s) {
+  if constexpr ((K == 5 || K == 7) && (std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value)) {
+    if (p.use_tc) {
+      if (st != nullptr)
+        return addend != nullptr ? launch_s1_conv_tc<T, K, true, true>(x, wgt, bias, addend, y, st, p, flip, s)
+                                 : launch_s1_conv_tc<T, K, true, false>(x, wgt, bias, addend, y, st, p, flip, s);
+      return addend != nullptr ? launch_s1_conv_tc<T, K, false, true>(x, wgt, bias, addend, y, st, p, flip, s)
+                               : launch_s1_conv_tc<T, K, false, false>(x, wgt, bias, addend, y, st, p, flip, s);
+    }
+  }
   const int pst = try_s1_conv_pk<T, K>(x, wgt, bias, addend, y, st, p, flip, s);
   if (pst != -1) return pst;
   const int tst = try_s1_conv_tma<T, K>(x, wgt, bias, addend, y, st, p, flip, s);

@@ -10,6 +10,7 @@
 
 #include "../../include/mednext_b200.h"
 #include "depthwise_s1.cuh"
+#include "depthwise_s1_tc.cuh"
 #include "depthwise_s2.cuh"
 #include "groupnorm.cuh"
 #include "pointwise.cuh"
@@ -35,7 +36,58 @@ struct S1Plan {
   int threads;
   size_t smem;
   long long grid;
+  bool use_tc;  // forward / input grad on the tensor cores (dw_s1_conv_tc_kernel), tiled by tc
+  DwTcGeom tc;
 };
+
+// Tiles of the tensor-core k = 5 / 7 forward and input grad (16-bit types, W a
+// multiple of 16).  Searched over the tile width (64, 32 or 16 columns, dividing
+// W), 32-row tiles (Ht + K - 1 row slots per plane) and 1..4 blocks of 128 row
+// slots (at most 256 TMEM columns), within 113 KB of shared memory so two CTAs
+// share an SM.  Cost of a candidate: its tiles x (tensor-core operand bytes read
+// from shared memory + 3 x the bytes its TMA copy loads); the smallest wins.
+// tmem_cols = 0: not eligible.
+inline DwTcGeom plan_dw_tc(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k) {
+  DwTcGeom best{};
+  if ((k != 5 && k != 7) || w < 16 || w % 16 != 0 || d < 1 || h < 1) return best;
+  double best_cost = -1.0;
+  for (int tw = 64; tw >= 16; tw /= 2) {
+    if (w % tw != 0) continue;
+    for (int nb = 1; nb <= kDwTcMaxBlk; ++nb) {
+      if (nb * tw > 256) continue;
+      DwTcGeom t{};
+      t.N = (int)n; t.C = (int)c; t.D = (int)d; t.H = (int)h; t.W = (int)w;
+      t.K = k;
+      t.TW = tw;
+      t.chunks = tw / 8 + 2;
+      t.Ht = (int)std::min<int64_t>(32, h);
+      t.Hp = t.Ht + k - 1;
+      const int dt_max = nb * 128 / t.Hp;
+      if (dt_max < 1) continue;
+      t.Dt = (int)std::min<int64_t>(dt_max, d);
+      t.nblk = (t.Dt * t.Hp + 127) / 128;
+      t.Dp = (t.nblk * 128 + (k - 1) * (t.Hp + 1) + t.Hp - 1) / t.Hp;
+      if (t.Dp > 256 || dw_tc_smem(t) > 113 * 1024) continue;
+      t.tilesW = (int)(w / tw);
+      t.tilesH = (int)((h + t.Ht - 1) / t.Ht);
+      t.tilesD = (int)((d + t.Dt - 1) / t.Dt);
+      const double tiles = (double)n * c * t.tilesW * t.tilesH * t.tilesD;
+      if (tiles >= 2147483648.0) continue;
+      const double mma_bytes = (double)t.nblk * (tw / 16) * k * k * 2 * 4096;
+      const double load_bytes = (double)dw_tc_x_bytes(t);
+      const double cost = tiles * (mma_bytes + 3.0 * load_bytes);
+      if (best_cost < 0.0 || cost < best_cost) {
+        best_cost = cost;
+        best = t;
+      }
+    }
+  }
+  if (best_cost < 0.0) return DwTcGeom{};
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(best.nblk * best.TW)) cols *= 2;
+  best.tmem_cols = cols;
+  return best;
+}
 
 inline int nh_for(int k) { return k <= 3 ? 2 : 1; }
 
@@ -107,9 +159,17 @@ inline S1Plan plan_s1(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int
   const size_t acc = esz == 8 ? 8 : 4;
   p.smem = wgrad ? tile : (((size_t)k * k * k * acc + 15) / 16) * 16 + tile;
   p.grid = base * g.tilesD;
+  if (!wgrad && (k == 5 || k == 7) && esz == 2) {
+    p.tc = plan_dw_tc(n, c, d, h, w, k);
+    p.use_tc = p.tc.tmem_cols != 0;
+  }
   return p;
 }
-inline size_t s1_tiles(const S1Plan& p) { return (size_t)p.g.tilesW * p.g.tilesH * p.g.tilesD; }
+// GroupNorm partials per (n, c) that the forward of this plan writes
+inline size_t s1_tiles(const S1Plan& p) {
+  if (p.use_tc) return (size_t)p.tc.tilesW * p.tc.tilesH * p.tc.tilesD;
+  return (size_t)p.g.tilesW * p.g.tilesH * p.g.tilesD;
+}
 
 // ------------------------------ stride-2 depthwise ------------------------------
 constexpr int kS2Group = 64;

@@ -79,5 +79,23 @@ inline bool encode4(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The depthwise tensor-core operand: x [nc][d][h][w] viewed as
+// (8 elements, h, d, w / 8 chunks, nc) with strides (2 B, w, h*w, 16 B, d*h*w), box
+// (8, bh, bd, bc, 1): a copy lands as [chunk][plane][row] x 16 bytes.
+template <typename T>
+inline bool encode_dw_tc(CUtensorMap* m, const void* base, uint64_t w, uint64_t h, uint64_t d, uint64_t nc,
+                         uint32_t bh, uint32_t bd, uint32_t bc) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const uint64_t e = 16 / sizeof(T);
+  const cuuint64_t dims[5] = {e, h, d, w / e, nc};
+  const cuuint64_t strides[4] = {w * sizeof(T), w * h * sizeof(T), 16, w * h * d * sizeof(T)};
+  const cuuint32_t box[5] = {(cuuint32_t)e, bh, bd, bc, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return fn(m, tma_dtype<T>(), 5, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace tma
 }  // namespace mednext

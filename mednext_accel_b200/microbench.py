@@ -47,6 +47,8 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
     vol = (1, C, 128, 128, 128)
     x5, dy5 = x.view(vol), dy.view(vol)
     w3 = (torch.randn(C, 1, 3, 3, 3, device=dev) * 0.2).to(bf)
+    w5 = (torch.randn(C, 1, 5, 5, 5, device=dev) * 0.09).to(bf)
+    w7 = (torch.randn(C, 1, 7, 7, 7, device=dev) * 0.05).to(bf)
     b3 = torch.randn(C, device=dev).to(bf)
     w3b = (torch.randn(2 * C, 1, 3, 3, 3, device=dev) * 0.2).to(bf)
     ys2 = r(1, C, 64, 64, 64)
@@ -89,6 +91,12 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
         "dw dgrad + addend C32 k3": (lambda: dwk.dw_dgrad(dy5, w3, 3, addend=x5), 3 * C * 2 * V),
         "dw dgrad C32 k3": (lambda: dwk.dw_dgrad(dy5, w3, 3), 2 * C * 2 * V),
         "dw wgrad C32 k3": (lambda: dwk.dw_wgrad(x5, dy5, 3), 2 * C * 2 * V),
+        "dw fwd + GN stats C32 k5 (tensor cores)": (lambda: dwk.dw_forward(x5, w5, w5[:, 0, 0, 0, 0], 5, gn_eps=1e-5),
+                                                    2 * C * 2 * V),
+        "dw dgrad + addend C32 k5 (tensor cores)": (lambda: dwk.dw_dgrad(dy5, w5, 5, addend=x5), 3 * C * 2 * V),
+        "dw wgrad C32 k5": (lambda: dwk.dw_wgrad(x5, dy5, 5), 2 * C * 2 * V),
+        "dw fwd C32 k7 (tensor cores)": (lambda: dwk.dw_forward(x5, w7, None, 7), 2 * C * 2 * V),
+        "dw dgrad C32 k7 (tensor cores)": (lambda: dwk.dw_dgrad(dy5, w7, 7), 2 * C * 2 * V),
         "s2 fwd C32 k3": (lambda: dwk.s2_forward(x5, w3, None, 3), C * 2 * V * 9 // 8),
         "s2 dgrad C32 k3": (lambda: dwk.s2_dgrad(ys2, w3, (128, 128, 128), 3), C * 2 * V * 9 // 8),
         "s2 wgrad C32 k3": (lambda: dwk.s2_wgrad(x5, ys2, 3), C * 2 * V * 9 // 8),

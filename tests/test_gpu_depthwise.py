@@ -207,6 +207,59 @@ def test_packed_k3_kernel_is_bit_exact_with_fp32_kernel(dtype, shape):
     torch.testing.assert_close(stats[:, 1].double(), rstd, rtol=1e-5, atol=1e-6)
 
 
+TC_SHAPES = [
+    (1, 32, 64, 128, 128),   # level-0 planes (64-column tiles, 32-row tiles)
+    (1, 64, 64, 64, 64),     # level 1
+    (1, 128, 32, 32, 32),    # level 2 (32-column tiles)
+    (1, 256, 16, 16, 16),    # level 3 (16-column tiles, one 16-row tile)
+    (1, 3, 6, 40, 256),      # four W tiles, a ragged second H tile
+    (2, 2, 5, 9, 64),        # short planes and depth
+    (2, 5, 17, 33, 48),      # 16-column tiles, 33 rows: a one-row last H tile
+]
+
+
+def _assert_one_rounding(got: torch.Tensor, want32: torch.Tensor, what: str) -> None:
+    """got (16-bit) is want32 (fp32) rounded once, up to the few fp32 ulps by which the
+    tensor-core sum may differ from the FMA sum: every element within one 16-bit ulp
+    (plus an fp32-level allowance where the taps cancel), and all but a few (values
+    within a few fp32 ulps of a rounding boundary: at most 1 %, measured about 0.3 %
+    for fp16 at k = 5) exactly the rounded fp32 value."""
+    dt = got.dtype
+    ulp = torch.finfo(dt).eps
+    diff = (got.float() - want32).abs()
+    bound = ulp * want32.abs() + 2.0**-18 * want32.abs().max()
+    assert bool((diff <= bound).all()), f"{what}: {(diff / bound).max().item():.3f} x the bound"
+    mismatch = (got != want32.to(dt)).sum().item()
+    assert mismatch <= max(4, got.numel() // 100), f"{what}: {mismatch} of {got.numel()} not the rounded fp32 value"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("k", [5, 7])
+@pytest.mark.parametrize("shape", TC_SHAPES)
+def test_tensor_core_k5_k7_kernels_match_fp32_kernel(dtype, k, shape):
+    """k = 5 and 7 on 16-bit tensors with W a multiple of 16 run on the tensor cores
+    (band matrices along W, one MMA per (kd, kh) tap pair, fp32 accumulation in TMEM):
+    the forward with bias and GroupNorm statistics and the input grad with the
+    residual addend are the fp32 kernel's results rounded once, to within the tensor
+    core's own fp32 summation order; the statistics are those of the stored output."""
+    seed = seed_of("tc", str(dtype), k, shape)
+    x = rand(shape, dtype, seed).cuda()
+    w = rand((shape[1], 1, k, k, k), dtype, seed + 1, scale=1 / np.sqrt(k**3)).cuda()
+    b = rand((shape[1],), dtype, seed + 2).cuda()
+    a = rand(shape, dtype, seed + 3).cuda()
+    y, stats = dwk.dw_forward(x, w, b, k, gn_eps=1e-5)
+    _assert_one_rounding(y, dwk.dw_forward(x.float(), w.float(), b.float(), k), "y")
+    dx = dwk.dw_dgrad(x, w, k, addend=a)
+    _assert_one_rounding(dx, dwk.dw_dgrad(x.float(), w.float(), k, addend=a.float()), "dx")
+    y0 = dwk.dw_forward(x, w, None, k)
+    _assert_one_rounding(y0, dwk.dw_forward(x.float(), w.float(), None, k), "y without bias")
+    yf = y.double().reshape(shape[0] * shape[1], -1)
+    torch.testing.assert_close(stats[:, 0].double(), yf.mean(1), rtol=1e-5, atol=1e-6)
+    rstd = 1 / torch.sqrt(yf.var(1, unbiased=False) + 1e-5)
+    torch.testing.assert_close(stats[:, 1].double(), rstd, rtol=1e-5, atol=1e-6)
+    assert nat.device_error() == 0
+
+
 DOWN_SHAPES = [
     (1, 32, 128, 128, 128),  # the benchmark's first down block
     (2, 3, 16, 20, 32),      # ragged last row tile of the small grid

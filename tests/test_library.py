@@ -104,3 +104,15 @@ def test_transposed_forward_workspace_planning_on_every_grid(small, dtype):
             assert lib.mednext_dwT_fwd_workspace_size(2, 6, d, h, w, pitch, k, dtype) > 0
     if w > 1:  # a pitch below the row length is rejected
         assert lib.mednext_dwT_fwd_workspace_size(2, 6, d, h, w, 2 * w - 2, 3, dtype) == 0
+
+
+@pytest.mark.parametrize("shape", [(1, 32, 128, 128, 128), (2, 5, 17, 33, 48), (1, 3, 6, 40, 256), (1, 1, 1, 1, 16),
+                                   (1, 2, 3, 4, 8), (1, 256, 16, 16, 16)])
+@pytest.mark.parametrize("k", [1, 3, 5, 7])
+def test_depthwise_forward_workspace_planning(shape, k):
+    """The stride-1 forward's workspace query runs the host-side tile planners (the
+    packed-FMA and, for k = 5 / 7 on 16-bit types, the tensor-core one) on every
+    grid: it answers a size, never traps."""
+    lib = nat.load()
+    for dtype in (0, 1, 2):
+        assert lib.mednext_dw_fwd_workspace_size(*shape, k, dtype) > 0
