@@ -117,6 +117,21 @@ int mednext_dw_dgrad(const void* dy, const void* weight, const void* addend, voi
                      mednext_stream_t stream);
 /* dweight[c,0,kd,kh,kw] = sum over n, positions of x(shifted) * dy; dbias = sum of dy
  * (dbias may be NULL).  Deterministic: fixed-order two-pass reduction. */
+/* The kernel family and tiling that mednext_dw_fwd / mednext_dw_dgrad (wgrad = 0)
+ * or mednext_dw_wgrad (wgrad = 1) choose for this shape (16-byte aligned
+ * operands), with no launch: out[8] = {family, tile W, tile H, tile D, tiles along
+ * W, H, D, CTAs}.  Families are the MEDNEXT_DWPLAN_* values.  No reference
+ * counterpart: it replaces the reference's per-shape auto-tuning record
+ * (optimization/*), which a fixed sm_100a table reports from here. */
+enum {
+  MEDNEXT_DWPLAN_GENERIC = 0,       /* per-output loads (fp64, unaligned rows) */
+  MEDNEXT_DWPLAN_PACKED_FMA = 1,    /* k3, 16-bit: TMA plane ring, packed fp32 FMAs */
+  MEDNEXT_DWPLAN_TENSOR_CORES = 2,  /* k5/k7, 16-bit: banded MMA, TMEM accumulators */
+  MEDNEXT_DWPLAN_TMA_RING = 3,      /* TMA plane ring, scalar FMAs */
+  MEDNEXT_DWPLAN_GROUPED = 4        /* weight grad k >= 5: taps split by kd across thread groups */
+};
+int mednext_dw_plan(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype, int wgrad,
+                    int32_t* out);
 size_t mednext_dw_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w,
                                        int k, int dtype);
 int mednext_dw_wgrad(const void* x, const void* dy, void* dweight, void* dbias, void* workspace,

@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "mednext_dwT_wgrad": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_dwT_wgrad_f32out": (_INT, [_P, _P, _P, _P, _P, _SZ] + _DIMS5 + [_I64, _INT, _INT, _P]),
     "mednext_gn_stats_workspace_size": (_SZ, [_I64, _I64, _I64]),
+    "mednext_dw_plan": (_INT, _DIMS5 + [_INT, _INT, _INT, _P]),
     "mednext_gn_stats": (_INT, [_P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _F, _INT, _P]),
     "mednext_gn_stats_rows": (_INT, [_P, _P, _P, _SZ, _I64, _I64, _I64, _I64, _I64, _F, _INT, _P]),
     "mednext_gn_fwd": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _INT, _INT, _INT, _P]),

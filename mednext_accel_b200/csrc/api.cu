@@ -186,6 +186,15 @@ int mednext_dw_dgrad(const void* dy, const void* weight, const void* addend, voi
   return dispatch_dw_s1_conv(dtype, k, dy, weight, nullptr, addend, dx, nullptr, p, 1, as_stream(stream));
 }
 
+int mednext_dw_plan(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype, int wgrad,
+                    int32_t* out) {
+  const int st = check_dw(n, c, d, h, w, k, dtype);
+  if (st != MEDNEXT_OK) return st;
+  if (out == nullptr) return MEDNEXT_ERR_NULL_POINTER;
+  const S1Plan p = plan_s1(n, c, d, h, w, k, elem_size(dtype), wgrad != 0);
+  return describe_dw_s1(dtype, k, p, wgrad != 0, out);
+}
+
 size_t mednext_dw_wgrad_workspace_size(int64_t n, int64_t c, int64_t d, int64_t h, int64_t w, int k, int dtype) {
   if (check_dw(n, c, d, h, w, k, dtype) != MEDNEXT_OK) return 0;
   return s1_wgrad_ws(n, c, d, h, w, k, dtype);

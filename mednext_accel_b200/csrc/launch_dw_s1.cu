@@ -196,6 +196,22 @@ int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws,
 
 }  // namespace
 
+#define MEDNEXT_K_SWITCH_HOST(k, KC, ...)                      \
+  switch (k) {                                                 \
+    case 1: { constexpr int KC = 1; __VA_ARGS__; } break;      \
+    case 3: { constexpr int KC = 3; __VA_ARGS__; } break;      \
+    case 5: { constexpr int KC = 5; __VA_ARGS__; } break;      \
+    case 7: { constexpr int KC = 7; __VA_ARGS__; } break;      \
+    default: return MEDNEXT_ERR_BAD_KERNEL;                    \
+  }
+#define MEDNEXT_DW_T_SWITCH_HOST(dtype, TC, ...)                              \
+  switch (dtype) {                                                            \
+    case MEDNEXT_FLOAT32: { using TC = float; __VA_ARGS__; } break;           \
+    case MEDNEXT_BFLOAT16: { using TC = __nv_bfloat16; __VA_ARGS__; } break;  \
+    case MEDNEXT_FLOAT16: { using TC = __half; __VA_ARGS__; } break;          \
+    case MEDNEXT_FLOAT64: { using TC = double; __VA_ARGS__; } break;          \
+    default: return MEDNEXT_ERR_BAD_DTYPE;                                    \
+  }
 #define MEDNEXT_K_SWITCH(k, KC, ...)                         \
   switch (k) {                                               \
     case 1: { constexpr int KC = 1; __VA_ARGS__; } break;    \
@@ -212,6 +228,39 @@ int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws,
     case MEDNEXT_FLOAT64: { using TC = double; __VA_ARGS__; } break;         \
     default: return MEDNEXT_ERR_BAD_DTYPE;                                   \
   }
+
+// The kernel family and tiling the launches above choose for a stride-1 plan
+// (operands assumed 16-byte aligned, as the entry points require):
+// out = {family, tile W, tile H, tile D, tiles W, tiles H, tiles D, CTAs}.
+int describe_dw_s1(int dtype, int k, const S1Plan& p, bool wgrad, int32_t* out) {
+  const DwS1Geom& g = p.g;
+  const void* aligned = reinterpret_cast<const void*>(uintptr_t{256});
+  int family = MEDNEXT_DWPLAN_GENERIC;
+  if (!wgrad && p.use_tc) {
+    family = MEDNEXT_DWPLAN_TENSOR_CORES;
+    const DwTcGeom& t = p.tc;
+    const int32_t v[8] = {family, t.TW, t.Ht, t.Dt, t.tilesW, t.tilesH, t.tilesD,
+                          (int32_t)((long long)t.N * t.C * t.tilesW * t.tilesH * t.tilesD)};
+    for (int i = 0; i < 8; ++i) out[i] = v[i];
+    return MEDNEXT_OK;
+  }
+  bool tma = false;
+  MEDNEXT_DW_T_SWITCH_HOST(dtype, T, MEDNEXT_K_SWITCH_HOST(k, KC, tma = s1_tma_ok<T, KC>(aligned, p)));
+  const bool sixteen = dtype == MEDNEXT_BFLOAT16 || dtype == MEDNEXT_FLOAT16;
+  if (!wgrad) {
+    if (k == 3 && sixteen && tma && g.LW >= 2 && p.threads <= kDwPkThreads &&
+        DwPkLayout<__nv_bfloat16>::pitch(g.TW) <= 256)
+      family = MEDNEXT_DWPLAN_PACKED_FMA;
+    else if (tma)
+      family = MEDNEXT_DWPLAN_TMA_RING;
+  } else {
+    if (k <= 3 && tma) family = MEDNEXT_DWPLAN_TMA_RING;
+    else if (k >= 5) family = MEDNEXT_DWPLAN_GROUPED;
+  }
+  const int32_t v[8] = {family, g.TW, g.TH, g.TD, g.tilesW, g.tilesH, g.tilesD, (int32_t)p.grid};
+  for (int i = 0; i < 8; ++i) out[i] = v[i];
+  return MEDNEXT_OK;
+}
 
 int dispatch_dw_s1_conv(int dtype, int k, const void* x, const void* w, const void* b, const void* addend, void* y,
                         GnPartial* stats, const S1Plan& p, int flip, cudaStream_t s) {

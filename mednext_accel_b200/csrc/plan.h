@@ -255,6 +255,7 @@ inline PwWPlan plan_pw_wgrad(int64_t n, int64_t cin, int64_t cout, int64_t vox) 
 
 // ------------------------------ dispatch (defined in launch_*.cu) ----------------
 // Each returns a mednext_status and never allocates.
+int describe_dw_s1(int dtype, int k, const S1Plan& p, bool wgrad, int32_t* out);
 int dispatch_dw_s1_conv(int dtype, int k, const void* x, const void* w, const void* b, const void* addend, void* y,
                         GnPartial* stats, const S1Plan& p, int flip, cudaStream_t s);
 int dispatch_dw_s1_wgrad(int dtype, int k, const void* x, const void* dy, void* dw, void* db, void* ws,

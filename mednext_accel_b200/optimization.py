@@ -414,20 +414,19 @@ class TableRow:
 
 
 def _block_rows() -> tuple[TableRow, ...]:
-    # MedNeXt v1 block shapes at 128^3 input (Base/Large, k 3/5).  The stored
-    # expanded activation of the widest high-resolution blocks is recomputed in
-    # backward instead of kept (a GEMM is cheaper than the HBM round trip).
-    rows = []
-    for spatial, channels in ((128, 32), (64, 64), (32, 128), (16, 256), (8, 512)):
-        for ratio in (2, 3, 4, 8):
-            rows.append(
-                TableRow(
-                    f"block-c{channels}-r{ratio}-s{spatial}", "mednext_block3d", "regular", "sm100_fused_block",
-                    channels=channels, ratio=ratio, spatial=spatial,
-                    parameters={"recompute_expansion": False},
-                )
-            )
-    return tuple(rows)
+    """One row per MedNeXt v1 regular-block shape (channels, ratio, kernel, spatial at a
+    128^3 input), whose parameters are the launch choices the kernels make for it
+    (depthwise kernel family and tiling, fused GEMM backward variants, whether the
+    expand GEMM stores GELU(u)), each citing the profile that justifies it.  The
+    choices are committed as data in :mod:`.sm100_table` and pinned to the
+    library's planners by tests."""
+    from .sm100_table import SM100_BLOCK_TABLE
+
+    return tuple(
+        TableRow(f"block-c{c}-r{r}-k{k}-s{s}", "mednext_block3d", "regular", "sm100_fused_block",
+                 channels=c, ratio=r, kernel=k, spatial=s, parameters=plan)
+        for (c, r, k, s), plan in SM100_BLOCK_TABLE.items()
+    )
 
 
 SM100_TABLE: tuple[TableRow, ...] = (
