@@ -774,4 +774,172 @@ __global__ void __launch_bounds__(kDwMaxComputeWarps * 32 + 32, 2)
   if (*abort && threadIdx.x == 0) raise_device_error(kErrMbarTimeout);
 }
 
+// ----------------------------------------------------------------------------
+// Weight grad for k = 5, 7 on a TMA plane ring.  The compute threads form K
+// groups (group g owns the K*K taps with kd = g); a producer warp streams the x
+// plane tile and the dy plane tile of each step into a ring of kDwGSlots(K)
+// slots.  At step s group g pairs x plane d0 - P + s (slot s) with dy plane
+// d0 + s - g (slot s - g, landed g steps earlier), so a slot is released by
+// each group after its last use: group g's warps arrive on slot s - g's empty
+// barrier at step s, and the producer refills a slot once every compute warp
+// has arrived.  No block barrier inside the loop.
+// ----------------------------------------------------------------------------
+__host__ __device__ constexpr int dw_gslots(int K) { return K + 2; }
+constexpr int kDwGMaxSlots = 9;
+
+struct DwGRing {
+  uint64_t full[kDwGMaxSlots];
+  uint64_t empty[kDwGMaxSlots];
+  int abort;
+};
+
+template <typename T, int K, int NH>
+__global__ void __launch_bounds__(448 + 32, 1)
+    dw_s1_wgrad_grouped_tma_kernel(const __grid_constant__ CUtensorMap mX, const __grid_constant__ CUtensorMap mDY,
+                                   typename Elem<T>::Acc* __restrict__ part, DwS1Geom g) {
+  using Acc = typename Elem<T>::Acc;
+  using L = DwTmaLayout<T>;
+  constexpr int P = K / 2;
+  constexpr int K2 = K * K;
+  constexpr int K3 = K2 * K;
+  constexpr int OFF = DwTile<T>::off(P);
+  constexpr int E = DwTile<T>::E;
+  constexpr int S = dw_gslots(K);
+  static_assert(S <= kDwGMaxSlots, "ring depth");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ DwGRing ring;
+  const size_t slot_bytes = L::slot(g, K, true);
+  const size_t x_bytes = L::x_tile(g, K);
+  const size_t dy_off = L::dy_offset(g, K);
+  unsigned char* slots = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);
+  const int compute_threads = (int)blockDim.x - 32;
+  const bool producer = (int)threadIdx.x >= compute_threads;
+
+  int b = blockIdx.x;
+  const int tw = b % g.tilesW;
+  b /= g.tilesW;
+  const int th = b % g.tilesH;
+  b /= g.tilesH;
+  const int td = b % g.tilesD;
+  const int nc = b / g.tilesD;
+  const int w0 = tw * g.TW, h0 = th * g.TH, d0 = td * g.TD;
+  const int rsw = DwTile<T>::row_elems(g.TW, P);
+  const int dcount = min(g.TD, g.D - d0);
+  const int nsteps = dcount + K - 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&ring.full[i], 1);
+      mbar_init(&ring.empty[i], (uint32_t)(compute_threads / 32));
+    }
+    ring.abort = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  volatile int* abort = &ring.abort;
+  int issued = 0;
+
+  Acc acc[K2 + 1];
+#pragma unroll
+  for (int t = 0; t <= K2; ++t) acc[t] = Acc(0);
+  const int G = compute_threads / K;  // threads per group, whole warps
+  const int grp = producer ? 0 : (int)threadIdx.x / G;
+
+  if (producer) {
+    if ((threadIdx.x & 31) == 0) {
+      tma_prefetch_map(&mX);
+      tma_prefetch_map(&mDY);
+      for (int s = 0; s < nsteps && !*abort; ++s) {
+        const int slot = s % S, r = s / S;
+        if (r > 0 && !mbar_wait(&ring.empty[slot], (uint32_t)((r - 1) & 1))) {
+          *abort = 1;
+          break;
+        }
+        unsigned char* dst = slots + (size_t)slot * slot_bytes;
+        const bool with_dy = s < dcount;
+        mbar_arrive_expect_tx(&ring.full[slot], (uint32_t)(x_bytes + (with_dy ? L::dy_tile(g) : 0)));
+        tma_load_4d(dst, &mX, &ring.full[slot], w0 - OFF, h0 - P, d0 - P + s, nc);
+        if (with_dy) tma_load_4d(dst + dy_off, &mDY, &ring.full[slot], w0, h0, d0 + s, nc);
+        ++issued;
+      }
+    }
+  } else {
+    const int lane = threadIdx.x & 31;
+    const int lt = (int)threadIdx.x - grp * G;
+    const int wt = lt % g.LW;
+    const int tr = lt / g.LW;
+    const int hrow = tr * NH;
+    const bool active = tr < g.TR;
+    for (int s = 0; s < nsteps; ++s) {
+      const int slot = s % S;
+      const bool ok = !*abort && mbar_wait(&ring.full[slot], (uint32_t)((s / S) & 1));
+      if (!__all_sync(0xffffffffu, ok)) {
+        *abort = 1;
+        break;
+      }
+      const int orel = s - grp;  // this group's dy plane (relative), landed in slot orel % S
+      if (orel >= 0) {
+        if (active && orel < dcount) {
+          const T* sp = reinterpret_cast<const T*>(slots + (size_t)slot * slot_bytes);
+          const T* dyt = reinterpret_cast<const T*>(slots + (size_t)(orel % S) * slot_bytes + dy_off);
+          Acc dyp[NH][kDwNW];
+#pragma unroll
+          for (int jh = 0; jh < NH; ++jh) {
+            const uint4* rowp = reinterpret_cast<const uint4*>(dyt + (size_t)(hrow + jh) * g.TW + kDwNW * wt);
+#pragma unroll
+            for (int q = 0; q < kDwNW / E; ++q) unpack16<T>(rowp[q], dyp[jh] + q * E);
+            if (grp == 0) {
+#pragma unroll
+              for (int i = 0; i < kDwNW; ++i) acc[K2] += dyp[jh][i];
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < NH + K - 1; ++r) {
+            Acc win[kDwNW + 2 * P];
+            dw_read_window<T, P>(sp, hrow + r, rsw, wt, win);
+#pragma unroll
+            for (int jh = 0; jh < NH; ++jh) {
+              const int kh = r - jh;
+              if (kh < 0 || kh >= K) continue;
+#pragma unroll
+              for (int kw = 0; kw < K; ++kw) {
+                Acc sacc = acc[kh * K + kw];
+#pragma unroll
+                for (int i = 0; i < kDwNW; ++i) sacc = fma(win[i + kw], dyp[jh][i], sacc);
+                acc[kh * K + kw] = sacc;
+              }
+            }
+          }
+        }
+        // this group is done with slot orel (its x at step orel, its dy now)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ring.empty[orel % S]);
+      }
+    }
+  }
+
+  __shared__ Acc red[15 * (K2 + 1)];
+  __syncthreads();
+  if (*abort && producer && (threadIdx.x & 31) == 0) {
+    for (int q = issued > S ? issued - S : 0; q < issued; ++q)
+      mbar_wait(&ring.full[q % S], (uint32_t)((q / S) & 1));
+  }
+  block_sum_to_smem<Acc, K2 + 1>(acc, red);
+  __syncthreads();
+  const int wpg = G >> 5;  // warps per group
+  const int tiles = g.tilesW * g.tilesH * g.tilesD;
+  const int tile = (td * g.tilesH + th) * g.tilesW + tw;
+  Acc* dst = part + ((size_t)nc * tiles + tile) * (K3 + 1);
+  for (int e = threadIdx.x; e < K * (K2 + 1); e += blockDim.x) {
+    const int gg = e / (K2 + 1);
+    const int t = e - gg * (K2 + 1);
+    if (t == K2 && gg != 0) continue;
+    Acc sum = Acc(0);
+    for (int w = 0; w < wpg; ++w) sum += red[(gg * wpg + w) * (K2 + 1) + t];
+    if (t == K2) dst[K3] = sum;
+    else dst[gg * K2 + t] = sum;
+  }
+  if (*abort && threadIdx.x == 0) raise_device_error(kErrMbarTimeout);
+}
+
 }  // namespace mednext

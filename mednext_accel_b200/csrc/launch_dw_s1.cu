@@ -171,12 +171,54 @@ int try_s1_wgrad_tma(const void* x, const void* dy, typename Elem<T>::Acc* part,
   }
 }
 
+// k >= 5 weight grad on the TMA plane ring (the taps split by kd across thread
+// groups): 16-byte rows, tiles within the TMA box, at most 448 compute threads.
+template <typename T, int K>
+bool s1_wgrad_grouped_tma_ok(const void* x, const void* dy, const S1Plan& p) {
+  if constexpr (std::is_same<T, double>::value || K < 5) {
+    return false;
+  } else {
+    const DwS1Geom& g = p.g;
+    return ((size_t)g.W * sizeof(T)) % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(dy) & 15) == 0 && p.threads <= 448 && p.threads % (32 * K) == 0 &&
+           DwTile<T>::row_elems(g.TW, K / 2) <= 256 && g.TH + 2 * (K / 2) <= 256;
+  }
+}
+
+template <typename T, int K>
+int try_s1_wgrad_grouped_tma(const void* x, const void* dy, typename Elem<T>::Acc* part, const S1Plan& p,
+                             cudaStream_t s) {
+  if constexpr (std::is_same<T, double>::value || K < 5) {
+    return -1;
+  } else {
+    if (!s1_wgrad_grouped_tma_ok<T, K>(x, dy, p)) return -1;
+    constexpr int NH = 1;
+    using L = DwTmaLayout<T>;
+    const DwS1Geom& g = p.g;
+    CUtensorMap mx, mdy;
+    const uint64_t nc = (uint64_t)g.N * g.C;
+    if (!tma::encode4<T>(&mx, x, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.D, nc,
+                         (uint32_t)DwTile<T>::row_elems(g.TW, K / 2), (uint32_t)(g.TH + 2 * (K / 2))))
+      return -1;
+    if (!tma::encode4<T>(&mdy, dy, (uint64_t)g.W, (uint64_t)g.H, (uint64_t)g.D, nc, (uint32_t)g.TW, (uint32_t)g.TH))
+      return -1;
+    const size_t smem = 128 + (size_t)dw_gslots(K) * L::slot(g, K, true);
+    auto kern = dw_s1_wgrad_grouped_tma_kernel<T, K, NH>;
+    if (const int rc = ensure_smem(kern, smem)) return rc;
+    kern<<<(unsigned)p.grid, p.threads + 32, smem, s>>>(mx, mdy, part, p.g);
+    return record_launch();
+  }
+}
+
 template <typename T, int K>
 int launch_s1_wgrad(const void* x, const void* dy, void* dw, void* db, void* ws, const S1Plan& p, bool f32,
                     cudaStream_t s) {
   using Acc = typename Elem<T>::Acc;
   constexpr int NH = K <= 3 ? 2 : 1;
   Acc* part = static_cast<Acc*>(ws);
+  const int gst = try_s1_wgrad_grouped_tma<T, K>(x, dy, part, p, s);
+  if (gst == MEDNEXT_OK) return finish_wgrad<T>(part, dw, db, p.g.N, p.g.C, (int)s1_tiles(p), K * K * K, f32, s);
+  if (gst != -1) return gst;
   const int tst = try_s1_wgrad_tma<T, K>(x, dy, part, p, s);
   if (tst == MEDNEXT_OK) return finish_wgrad<T>(part, dw, db, p.g.N, p.g.C, (int)s1_tiles(p), K * K * K, f32, s);
   if (tst != -1) return tst;
@@ -254,8 +296,10 @@ int describe_dw_s1(int dtype, int k, const S1Plan& p, bool wgrad, int32_t* out) 
     else if (tma)
       family = MEDNEXT_DWPLAN_TMA_RING;
   } else {
+    bool gtma = false;
+    MEDNEXT_DW_T_SWITCH_HOST(dtype, T, MEDNEXT_K_SWITCH_HOST(k, KC, gtma = s1_wgrad_grouped_tma_ok<T, KC>(aligned, aligned, p)));
     if (k <= 3 && tma) family = MEDNEXT_DWPLAN_TMA_RING;
-    else if (k >= 5) family = MEDNEXT_DWPLAN_GROUPED;
+    else if (k >= 5) family = gtma ? MEDNEXT_DWPLAN_GROUPED_TMA_RING : MEDNEXT_DWPLAN_GROUPED;
   }
   const int32_t v[8] = {family, g.TW, g.TH, g.TD, g.tilesW, g.tilesH, g.tilesD, (int32_t)p.grid};
   for (int i = 0; i < 8; ++i) out[i] = v[i];

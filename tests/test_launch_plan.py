@@ -31,7 +31,7 @@ def test_table_covers_every_mednext_v1_block_shape():
     # Base k3 and Large k5 level-0 rows: the measured families of the step profiles
     assert SM100_BLOCK_TABLE[(32, 2, 3, 128)]["depthwise_forward"]["family"] == "packed-fma"
     assert SM100_BLOCK_TABLE[(32, 3, 5, 128)]["depthwise_forward"]["family"] == "tensor-cores"
-    assert SM100_BLOCK_TABLE[(32, 3, 5, 128)]["depthwise_weight_grad"]["family"] == "grouped"
+    assert SM100_BLOCK_TABLE[(32, 3, 5, 128)]["depthwise_weight_grad"]["family"] == "grouped-tma-ring"
 
 
 def test_every_choice_cites_a_committed_profile():
