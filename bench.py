@@ -141,6 +141,14 @@ class ClockSampler:
             self.thread.start()
         except (OSError, ValueError):
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start (longer with several ranks starting it at
+        # once): wait, bounded, for its first sample, then keep only the samples taken
+        # from here on, i.e. during the timed region
+        t0 = time.perf_counter()
+        while not self.lines and time.perf_counter() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.lines.clear()
         return self
 
     def _read(self):
