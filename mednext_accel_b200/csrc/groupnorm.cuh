@@ -244,15 +244,28 @@ static __global__ void gn_fold_spans_kernel(GnBwdPartial* __restrict__ part, int
 // folded sums of (n, c) at folded[nc * stride] and V = vol; all `pitch` elements
 // of each (n, c) row are written (positions past the valid voxels of a pitched
 // row get values without meaning).
+// The sums of (n, c) are folded[nc * stride] plus, with spans > 1, the span sums
+// at every kGnFoldSpan-th slot after it (added in order, as gn_fold_spans_kernel
+// does).  dgamma / dbeta (one sample, N = 1): the chunk-0 CTA of each channel
+// writes them, as gn_param_grad_kernel would.
 template <typename TD, typename TX, typename TO, typename TG>
 __global__ void __launch_bounds__(256) gn_bwd_apply_kernel(
     const TD* __restrict__ dz, const TX* __restrict__ x, const float* __restrict__ stats,
-    const TG* __restrict__ gamma, const GnBwdPartial* __restrict__ folded, int stride,
-    TO* __restrict__ dx, int C, size_t vol, size_t pitch, int chunks) {
+    const TG* __restrict__ gamma, const GnBwdPartial* __restrict__ folded, int stride, int spans,
+    TO* __restrict__ dx, int C, size_t vol, size_t pitch, int chunks, float* __restrict__ dgamma,
+    float* __restrict__ dbeta) {
   const int j = blockIdx.x % chunks;
   const size_t nc = blockIdx.x / chunks;
   const int c = (int)(nc % C);
-  const GnBwdPartial f = folded[nc * stride];
+  GnBwdPartial f = folded[nc * stride];
+  for (int sp = 1; sp < spans; ++sp) {
+    f.s1 += folded[nc * stride + (size_t)sp * kGnFoldSpan].s1;
+    f.s2 += folded[nc * stride + (size_t)sp * kGnFoldSpan].s2;
+  }
+  if (j == 0 && threadIdx.x == 0) {
+    if (dbeta != nullptr) dbeta[c] = (float)(0.0 + f.s1);
+    if (dgamma != nullptr) dgamma[c] = (float)(0.0 + f.s2);
+  }
   const float m1 = (float)(f.s1 / (double)vol);
   const float m2 = (float)(f.s2 / (double)vol);
   const float mean = stats[2 * nc], rstd = stats[2 * nc + 1];

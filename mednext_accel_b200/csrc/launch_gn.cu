@@ -72,27 +72,32 @@ int dispatch_gn_bwd_apply(int x_dtype, int dz_dtype, int g_dtype, const void* dz
   const int64_t nc = (int64_t)N * C;
   const int chunks = gn_chunks(nc, vol);
   int st = MEDNEXT_OK;
+  // one sample: the apply kernel adds the span sums and writes dgamma / dbeta itself
+  const bool one = N == 1;
+  int spans = 1;
   if (part_tiles > 1) {
     // fold in place; the workspace belongs to this call sequence
-    const int spans = (part_tiles + kGnFoldSpan - 1) / kGnFoldSpan;
+    spans = (part_tiles + kGnFoldSpan - 1) / kGnFoldSpan;
     gn_fold_partials_kernel<<<(unsigned)(nc * spans), 256, 0, s>>>(const_cast<GnBwdPartial*>(part), part_tiles);
     st = record_launch();
     if (st != MEDNEXT_OK) return st;
-    if (spans > 1) {
+    if (spans > 1 && !one) {
       gn_fold_spans_kernel<<<(unsigned)((nc + 127) / 128), 128, 0, s>>>(const_cast<GnBwdPartial*>(part), part_tiles,
                                                                          (int)nc);
       st = record_launch();
       if (st != MEDNEXT_OK) return st;
+      spans = 1;
     }
   }
   MEDNEXT_GN_DISPATCH(x_dtype, dz_dtype, g_dtype, TX, TD, TG, {
     gn_bwd_apply_kernel<TD, TX, TX, TG><<<(unsigned)(nc * chunks), 256, 0, s>>>(
         static_cast<const TD*>(dz), static_cast<const TX*>(x), stats, static_cast<const TG*>(gamma), part, part_tiles,
-        static_cast<TX*>(dx), C, (size_t)vol, (size_t)pitch, chunks);
+        spans, static_cast<TX*>(dx), C, (size_t)vol, (size_t)pitch, chunks, one ? dgamma : nullptr,
+        one ? dbeta : nullptr);
     st = record_launch();
   });
   if (st != MEDNEXT_OK) return st;
-  if (dgamma != nullptr || dbeta != nullptr) {
+  if (!one && (dgamma != nullptr || dbeta != nullptr)) {
     gn_param_grad_kernel<<<(C + 127) / 128, 128, 0, s>>>(part, part_tiles, N, C, dgamma, dbeta);
     st = record_launch();
   }
