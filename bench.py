@@ -250,7 +250,26 @@ def depthwise_backward_roofline(device: torch.device, reps: int = 10) -> dict:
         "algorithmic_bytes": algo_bytes,
         "dgrad_ms": round(statistics.median(tg), 4),
         "wgrad_ms": round(statistics.median(tw), 4),
+        **fma_floor(2 * 2 * 27 * x.numel(), algo_bytes, peak, t_ms, device),
     }
+
+
+def fma_floor(flops: int, algo_bytes: int, hbm_gbs: float, t_ms: float, device: torch.device) -> dict:
+    """The depthwise convolution does 27 FMAs per 4 bytes at k = 3, past the FP32
+    ridge point, so its floor is the larger of bytes / HBM bandwidth and FLOPs /
+    FP32 FMA peak.  The FMA peak is nominal: SMs x 128 FP32 lanes x 2 FLOP x the
+    maximum SM clock (nvidia-smi clocks.max.sm)."""
+    props = torch.cuda.get_device_properties(device)
+    try:
+        mhz = float(subprocess.run(["nvidia-smi", f"--id={device.index or 0}", "--query-gpu=clocks.max.sm",
+                                    "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                   timeout=10).stdout.strip().splitlines()[0])
+    except (OSError, ValueError, IndexError, subprocess.TimeoutExpired):
+        mhz = 1965.0
+    fp32_tflops = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+    floor_us = max(algo_bytes / (hbm_gbs * 1e9), flops / (fp32_tflops * 1e12)) * 1e6
+    return {"flops": flops, "fp32_fma_peak_tflops": round(fp32_tflops, 1),
+            "floor_us": round(floor_us, 1), "frac_of_floor": round(floor_us / (t_ms * 1e3), 4)}
 
 
 def compress_forward_roofline(device: torch.device, reps: int = 10) -> dict:
