@@ -439,15 +439,27 @@ def run_reference_gpu(args) -> int:
     torch.cuda.set_device(local)
     torch.backends.cudnn.benchmark = True
     torch.manual_seed(0)
-    model = ref.mednext_base(in_channels=1, out_channels=3, kernel_size=3, deep_supervision=True,
-                             optimization=args.ref_optimization).cuda().train()
+    if args.workload == "block-k5":
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "the block workload has no reference factory"}),
+              flush=True)
+        return 0
+    batch = 1
+    if args.workload == "large-k5":
+        batch = 2
+        model = ref.mednext_large(in_channels=1, out_channels=3, kernel_size=5, deep_supervision=True,
+                                  optimization=args.ref_optimization,
+                                  checkpointing=ref.CheckpointConfig(style="expansion"))
+    else:
+        model = ref.mednext_base(in_channels=1, out_channels=3, kernel_size=3, deep_supervision=True,
+                                 optimization=args.ref_optimization)
+    model = model.cuda().train()
     compiled = not args.ref_eager
     if compiled:
         model = torch.compile(model, mode="default", fullgraph=True)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4)
     gen = torch.Generator().manual_seed(1000)
-    x = torch.randn((1, 1, SPATIAL, SPATIAL, SPATIAL), generator=gen).cuda()
-    target = torch.randint(0, 3, (1, SPATIAL, SPATIAL, SPATIAL), generator=gen).cuda()
+    x = torch.randn((batch, 1, SPATIAL, SPATIAL, SPATIAL), generator=gen).cuda()
+    target = torch.randint(0, 3, (batch, SPATIAL, SPATIAL, SPATIAL), generator=gen).cuda()
     targets = downsampled_targets(target)
 
     def step():
@@ -480,7 +492,7 @@ def run_reference_gpu(args) -> int:
     ms = statistics.median(times)
     line = {
         "impl": "reference-gpu",
-        "metric": METRIC,
+        "metric": METRIC if args.workload == "base-k3" else f"{args.workload} step ms on B200 (bf16; see config.workload)",
         "value": round(ms, 3),
         "unit": "ms",
         "n_gpus": 1,
@@ -491,7 +503,7 @@ def run_reference_gpu(args) -> int:
         "higher_is_better": False,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": "MedNeXt-Base k3 128^3 B1 train step (5-head CE, AdamW), reference package on GPU",
+        "config": {"workload": WORKLOADS[args.workload].format(S=SPATIAL) + ", reference package on GPU",
                    "optimization": args.ref_optimization, "compiled": compiled,
                    "compile": "torch.compile(mode='default', fullgraph=True)" if compiled else None,
                    "cudnn_benchmark": True, "timing": "median of per-step CUDA events"},
