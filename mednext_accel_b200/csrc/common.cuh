@@ -404,6 +404,42 @@ __device__ __forceinline__ float rcp_approx(float x) {
   return y;
 }
 
+// Mixed-precision FMA (sm_100): a * b + c with 16-bit a, b and an fp32 c, d.  The
+// product of two 16-bit floats is exact in fp32, so the result is fmaf of the
+// widened operands, with no widening instructions: the operands are halves of
+// 32-bit registers.
+template <typename T>
+__device__ __forceinline__ float mix_fma(uint16_t a, uint16_t b, float c);
+template <>
+__device__ __forceinline__ float mix_fma<__nv_bfloat16>(uint16_t a, uint16_t b, float c) {
+  float d;
+  asm("fma.rn.f32.bf16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+template <>
+__device__ __forceinline__ float mix_fma<__half>(uint16_t a, uint16_t b, float c) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+// the 16-bit bit pattern of 1.0
+template <typename T>
+__device__ __forceinline__ uint16_t one16();
+template <>
+__device__ __forceinline__ uint16_t one16<__nv_bfloat16>() {
+  return 0x3f80u;
+}
+template <>
+__device__ __forceinline__ uint16_t one16<__half>() {
+  return 0x3c00u;
+}
+// element i of an array of 32-bit words read as 16-bit elements (little endian:
+// element 2q is the low half of word q)
+template <int N>
+__device__ __forceinline__ uint16_t half16(const uint32_t (&w)[N], int i) {
+  return (i & 1) ? (uint16_t)(w[i >> 1] >> 16) : (uint16_t)(w[i >> 1] & 0xffffu);
+}
+
 // Exact (erf-form) GELU of F.gelu(approximate="none"): x * Phi(x), with
 // Phi(x) = erfc(-x / sqrt 2) / 2.  erfc(z), z >= 0, by the Chebyshev fit of
 // Numerical Recipes (Press et al., 2nd ed., sec. 6.2, "erfcc"):

@@ -627,6 +627,9 @@ __global__ void __launch_bounds__(kDwMaxComputeWarps * 32 + 32, 2)
   constexpr int K3 = K * K * K;
   constexpr int OFF = DwTile<T>::off(P);
   constexpr int E = DwTile<T>::E;
+  // k = 3 on 16-bit types: mixed-precision FMAs straight from the packed elements
+  constexpr bool kMixed =
+      K == 3 && kDwNW == 8 && (std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value);
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ DwRing ring;
   const size_t slot_bytes = L::slot(g, K, true);
@@ -680,6 +683,89 @@ __global__ void __launch_bounds__(kDwMaxComputeWarps * 32 + 32, 2)
         tma_load_4d(dst, &mX, &ring.full[slot], w0 - OFF, h0 - P, d0 - P + s, nc);
         if (with_dy) tma_load_4d(dst + dy_off, &mDY, &ring.full[slot], w0, h0, d0 + s, nc);
         ++issued;
+      }
+    }
+  } else if constexpr (kMixed) {
+    // 16-bit x and dy stay packed as loaded; every product is one mixed-precision
+    // FMA (16-bit operands, fp32 accumulator), in the order of the branch below,
+    // so the tap sums are bit-identical to it on the widened inputs.
+    const int lane = threadIdx.x & 31;
+    const int wt = threadIdx.x % g.LW;
+    const int tr = threadIdx.x / g.LW;
+    const int hrow = tr * NH;
+    const bool active = tr < g.TR;
+    uint32_t dyw[K][NH][kDwNW / 2];  // dy rows of the last K planes, two elements per word
+#pragma unroll
+    for (int a = 0; a < K; ++a)
+#pragma unroll
+      for (int jh = 0; jh < NH; ++jh)
+#pragma unroll
+        for (int i = 0; i < kDwNW / 2; ++i) dyw[a][jh][i] = 0u;
+
+    bool stop = false;  // warp-uniform: every lane leaves the loop at the same step
+    for (int sb = 0; sb < nsteps && !stop; sb += K) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        const int s = sb + j;
+        if (s < nsteps) {
+          const int slot = s % kDwSlots;
+          const bool ok = !*abort && mbar_wait(&ring.full[slot], (uint32_t)((s / kDwSlots) & 1));
+          if (!__all_sync(0xffffffffu, ok)) {
+            *abort = 1;
+            stop = true;
+            break;
+          }
+          const unsigned char* base = slots + (size_t)slot * slot_bytes;
+          const T* sp = reinterpret_cast<const T*>(base);
+          if (active && s < dcount) {
+            const T* dyt = reinterpret_cast<const T*>(base + dy_off);
+#pragma unroll
+            for (int jh = 0; jh < NH; ++jh) {
+              const uint4 q = *reinterpret_cast<const uint4*>(dyt + (size_t)(hrow + jh) * g.TW + kDwNW * wt);
+              dyw[j][jh][0] = q.x;
+              dyw[j][jh][1] = q.y;
+              dyw[j][jh][2] = q.z;
+              dyw[j][jh][3] = q.w;
+#pragma unroll
+              for (int i = 0; i < kDwNW; ++i) acc[K3] = mix_fma<T>(half16(dyw[j][jh], i), one16<T>(), acc[K3]);
+            }
+          } else {
+#pragma unroll
+            for (int jh = 0; jh < NH; ++jh)
+#pragma unroll
+              for (int i = 0; i < kDwNW / 2; ++i) dyw[j][jh][i] = 0u;
+          }
+          if (active) {
+#pragma unroll
+            for (int r = 0; r < NH + K - 1; ++r) {
+              // window element m (input column w0 + 8 wt - 1 + m) is 16-bit element
+              // m + 1 of xw: the high half of word 0, then words 1-4, then the low
+              // half of word 5
+              const uint32_t* rowp = reinterpret_cast<const uint32_t*>(sp + (size_t)(hrow + r) * rsw) + 4 * wt;
+              const uint4 mid = *reinterpret_cast<const uint4*>(rowp + 4);
+              const uint32_t xw[6] = {rowp[3], mid.x, mid.y, mid.z, mid.w, rowp[8]};
+#pragma unroll
+              for (int jh = 0; jh < NH; ++jh) {
+                const int kh = r - jh;
+                if (kh < 0 || kh >= K) continue;
+#pragma unroll
+                for (int kd = 0; kd < K; ++kd) {
+                  const int dslot = (j - kd + K) % K;
+#pragma unroll
+                  for (int kw = 0; kw < K; ++kw) {
+                    float sacc = acc[(kd * K + kh) * K + kw];
+#pragma unroll
+                    for (int i = 0; i < kDwNW; ++i)
+                      sacc = mix_fma<T>(half16(xw, i + kw + 1), half16(dyw[dslot][jh], i), sacc);
+                    acc[(kd * K + kh) * K + kw] = sacc;
+                  }
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ring.empty[slot]);
+        }
       }
     }
   } else {

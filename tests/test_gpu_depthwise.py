@@ -207,6 +207,33 @@ def test_packed_k3_kernel_is_bit_exact_with_fp32_kernel(dtype, shape):
     torch.testing.assert_close(stats[:, 1].double(), rstd, rtol=1e-5, atol=1e-6)
 
 
+WGRAD_SHAPES = [
+    (1, 3, 6, 40, 256),      # two W tiles, ragged H tile
+    (2, 2, 5, 9, 64),
+    (1, 2, 11, 70, 128),     # three H tiles, the last one ragged
+    (1, 2, 7, 8, 16),
+    (2, 8, 32, 32, 32),
+    (1, 32, 128, 128, 128),  # the benchmark's level-0 shape
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", WGRAD_SHAPES)
+def test_k3_weight_grad_16bit_is_bit_exact_with_fp32_kernel(dtype, shape):
+    """The stride-1 k = 3 weight grad on 16-bit tensors multiplies the packed
+    elements with mixed-precision FMAs (16-bit operands, fp32 sums) in the fp32
+    kernel's order on the same tiling; a product of two 16-bit floats is exact in
+    fp32, so its weight and bias grads are the fp32 kernel's on the widened inputs,
+    rounded once."""
+    seed = seed_of("wgrad16", str(dtype), shape)
+    x = rand(shape, dtype, seed).cuda()
+    dy = rand(shape, dtype, seed + 1).cuda()
+    dw, db = dwk.dw_wgrad(x, dy, 3)
+    dw32, db32 = dwk.dw_wgrad(x.float(), dy.float(), 3)
+    assert torch.equal(dw, dw32.to(dtype)) and torch.equal(db, db32.to(dtype))
+    assert nat.device_error() == 0
+
+
 TC_SHAPES = [
     (1, 32, 64, 128, 128),   # level-0 planes (64-column tiles, 32-row tiles)
     (1, 64, 64, 64, 64),     # level 1
