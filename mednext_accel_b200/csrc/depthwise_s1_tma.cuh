@@ -613,6 +613,30 @@ __global__ void __launch_bounds__(kDwPkThreads, 2)
   if (*abort && threadIdx.x == 0) raise_device_error(kErrMbarTimeout);
 }
 
+// Raw 16-bit window of thread column wt for the mixed-precision weight grads:
+// window element m (input column w0 + 8 wt - P + m, m < 8 + 2P) is 16-bit
+// element m + kMixH0<P> of xw.  rowb is the shared-memory row, whose element 0
+// is input column w0 - 8 (16-bit types, P <= 3: the left halo is one chunk).
+template <int P>
+constexpr int kMixWL = (P + 1) / 2;  // words left (and right) of the thread's 4 words
+template <int P>
+constexpr int kMixH0 = 2 * kMixWL<P> - P;
+template <int P>
+__device__ __forceinline__ void dw_read_window_raw(const void* rowb, int wt, uint32_t (&xw)[4 + 2 * kMixWL<P>]) {
+  constexpr int WL = kMixWL<P>;
+  const uint32_t* rowp = reinterpret_cast<const uint32_t*>(rowb) + 4 * wt;
+  const uint4 mid = *reinterpret_cast<const uint4*>(rowp + 4);
+#pragma unroll
+  for (int q = 0; q < WL; ++q) {
+    xw[q] = rowp[4 - WL + q];
+    xw[WL + 4 + q] = rowp[8 + q];
+  }
+  xw[WL] = mid.x;
+  xw[WL + 1] = mid.y;
+  xw[WL + 2] = mid.z;
+  xw[WL + 3] = mid.w;
+}
+
 // ----------------------------------------------------------------------------
 // Weight grad, every tap in one thread (k = 1, 3).  The ring slot carries the
 // x plane tile and, after it, the dy plane tile of the same step.
@@ -738,12 +762,8 @@ __global__ void __launch_bounds__(kDwMaxComputeWarps * 32 + 32, 2)
           if (active) {
 #pragma unroll
             for (int r = 0; r < NH + K - 1; ++r) {
-              // window element m (input column w0 + 8 wt - 1 + m) is 16-bit element
-              // m + 1 of xw: the high half of word 0, then words 1-4, then the low
-              // half of word 5
-              const uint32_t* rowp = reinterpret_cast<const uint32_t*>(sp + (size_t)(hrow + r) * rsw) + 4 * wt;
-              const uint4 mid = *reinterpret_cast<const uint4*>(rowp + 4);
-              const uint32_t xw[6] = {rowp[3], mid.x, mid.y, mid.z, mid.w, rowp[8]};
+              uint32_t xw[4 + 2 * kMixWL<P>];
+              dw_read_window_raw<P>(sp + (size_t)(hrow + r) * rsw, wt, xw);
 #pragma unroll
               for (int jh = 0; jh < NH; ++jh) {
                 const int kh = r - jh;
@@ -756,7 +776,7 @@ __global__ void __launch_bounds__(kDwMaxComputeWarps * 32 + 32, 2)
                     float sacc = acc[(kd * K + kh) * K + kw];
 #pragma unroll
                     for (int i = 0; i < kDwNW; ++i)
-                      sacc = mix_fma<T>(half16(xw, i + kw + 1), half16(dyw[dslot][jh], i), sacc);
+                      sacc = mix_fma<T>(half16(xw, i + kw + kMixH0<P>), half16(dyw[dslot][jh], i), sacc);
                     acc[(kd * K + kh) * K + kw] = sacc;
                   }
                 }
@@ -892,6 +912,9 @@ __global__ void __launch_bounds__(448 + 32, 1)
   constexpr int E = DwTile<T>::E;
   constexpr int S = dw_gslots(K);
   static_assert(S <= kDwGMaxSlots, "ring depth");
+  // 16-bit types: mixed-precision FMAs straight from the packed elements
+  constexpr bool kMixed = P <= 3 && kDwNW == 8 && DwTile<T>::off(P) == 8 &&
+                          (std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value);
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ DwGRing ring;
   const size_t slot_bytes = L::slot(g, K, true);
@@ -968,31 +991,67 @@ __global__ void __launch_bounds__(448 + 32, 1)
         if (active && orel < dcount) {
           const T* sp = reinterpret_cast<const T*>(slots + (size_t)slot * slot_bytes);
           const T* dyt = reinterpret_cast<const T*>(slots + (size_t)(orel % S) * slot_bytes + dy_off);
-          Acc dyp[NH][kDwNW];
-#pragma unroll
-          for (int jh = 0; jh < NH; ++jh) {
-            const uint4* rowp = reinterpret_cast<const uint4*>(dyt + (size_t)(hrow + jh) * g.TW + kDwNW * wt);
-#pragma unroll
-            for (int q = 0; q < kDwNW / E; ++q) unpack16<T>(rowp[q], dyp[jh] + q * E);
-            if (grp == 0) {
-#pragma unroll
-              for (int i = 0; i < kDwNW; ++i) acc[K2] += dyp[jh][i];
-            }
-          }
-#pragma unroll
-          for (int r = 0; r < NH + K - 1; ++r) {
-            Acc win[kDwNW + 2 * P];
-            dw_read_window<T, P>(sp, hrow + r, rsw, wt, win);
+          if constexpr (kMixed) {
+            // 16-bit operands straight from the packed elements (mixed-precision
+            // FMAs; the products and their order as in the branch below)
+            uint32_t dyw[NH][kDwNW / 2];
 #pragma unroll
             for (int jh = 0; jh < NH; ++jh) {
-              const int kh = r - jh;
-              if (kh < 0 || kh >= K) continue;
+              const uint4 q = *reinterpret_cast<const uint4*>(dyt + (size_t)(hrow + jh) * g.TW + kDwNW * wt);
+              dyw[jh][0] = q.x;
+              dyw[jh][1] = q.y;
+              dyw[jh][2] = q.z;
+              dyw[jh][3] = q.w;
+              if (grp == 0) {
 #pragma unroll
-              for (int kw = 0; kw < K; ++kw) {
-                Acc sacc = acc[kh * K + kw];
+                for (int i = 0; i < kDwNW; ++i) acc[K2] = mix_fma<T>(half16(dyw[jh], i), one16<T>(), acc[K2]);
+              }
+            }
 #pragma unroll
-                for (int i = 0; i < kDwNW; ++i) sacc = fma(win[i + kw], dyp[jh][i], sacc);
-                acc[kh * K + kw] = sacc;
+            for (int r = 0; r < NH + K - 1; ++r) {
+              uint32_t xw[4 + 2 * kMixWL<P>];
+              dw_read_window_raw<P>(sp + (size_t)(hrow + r) * rsw, wt, xw);
+#pragma unroll
+              for (int jh = 0; jh < NH; ++jh) {
+                const int kh = r - jh;
+                if (kh < 0 || kh >= K) continue;
+#pragma unroll
+                for (int kw = 0; kw < K; ++kw) {
+                  float sacc = acc[kh * K + kw];
+#pragma unroll
+                  for (int i = 0; i < kDwNW; ++i)
+                    sacc = mix_fma<T>(half16(xw, i + kw + kMixH0<P>), half16(dyw[jh], i), sacc);
+                  acc[kh * K + kw] = sacc;
+                }
+              }
+            }
+          } else {
+            Acc dyp[NH][kDwNW];
+#pragma unroll
+            for (int jh = 0; jh < NH; ++jh) {
+              const uint4* rowp = reinterpret_cast<const uint4*>(dyt + (size_t)(hrow + jh) * g.TW + kDwNW * wt);
+#pragma unroll
+              for (int q = 0; q < kDwNW / E; ++q) unpack16<T>(rowp[q], dyp[jh] + q * E);
+              if (grp == 0) {
+#pragma unroll
+                for (int i = 0; i < kDwNW; ++i) acc[K2] += dyp[jh][i];
+              }
+            }
+#pragma unroll
+            for (int r = 0; r < NH + K - 1; ++r) {
+              Acc win[kDwNW + 2 * P];
+              dw_read_window<T, P>(sp, hrow + r, rsw, wt, win);
+#pragma unroll
+              for (int jh = 0; jh < NH; ++jh) {
+                const int kh = r - jh;
+                if (kh < 0 || kh >= K) continue;
+#pragma unroll
+                for (int kw = 0; kw < K; ++kw) {
+                  Acc sacc = acc[kh * K + kw];
+#pragma unroll
+                  for (int i = 0; i < kDwNW; ++i) sacc = fma(win[i + kw], dyp[jh][i], sacc);
+                  acc[kh * K + kw] = sacc;
+                }
               }
             }
           }

@@ -218,18 +218,19 @@ WGRAD_SHAPES = [
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("k", [3, 5, 7])
 @pytest.mark.parametrize("shape", WGRAD_SHAPES)
-def test_k3_weight_grad_16bit_is_bit_exact_with_fp32_kernel(dtype, shape):
-    """The stride-1 k = 3 weight grad on 16-bit tensors multiplies the packed
-    elements with mixed-precision FMAs (16-bit operands, fp32 sums) in the fp32
-    kernel's order on the same tiling; a product of two 16-bit floats is exact in
-    fp32, so its weight and bias grads are the fp32 kernel's on the widened inputs,
-    rounded once."""
-    seed = seed_of("wgrad16", str(dtype), shape)
+def test_weight_grad_16bit_is_bit_exact_with_fp32_kernel(dtype, k, shape):
+    """The stride-1 weight grads on 16-bit tensors (k = 3, and the grouped k = 5 / 7
+    kernel) multiply the packed elements with mixed-precision FMAs (16-bit operands,
+    fp32 sums) in the fp32 kernel's order on the same tiling; a product of two
+    16-bit floats is exact in fp32, so the weight and bias grads are the fp32
+    kernel's on the widened inputs, rounded once."""
+    seed = seed_of("wgrad16", str(dtype), k, shape)
     x = rand(shape, dtype, seed).cuda()
     dy = rand(shape, dtype, seed + 1).cuda()
-    dw, db = dwk.dw_wgrad(x, dy, 3)
-    dw32, db32 = dwk.dw_wgrad(x.float(), dy.float(), 3)
+    dw, db = dwk.dw_wgrad(x, dy, k)
+    dw32, db32 = dwk.dw_wgrad(x.float(), dy.float(), k)
     assert torch.equal(dw, dw32.to(dtype)) and torch.equal(db, db32.to(dtype))
     assert nat.device_error() == 0
 
