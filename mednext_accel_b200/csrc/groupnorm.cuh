@@ -282,7 +282,28 @@ __global__ void __launch_bounds__(256) gn_bwd_apply_kernel(
     constexpr int E = 8;
     if (vec_ok<TX>(dz, pitch) && vec_ok<TX>(x, pitch) && vec_ok<TX>(dx, pitch) && beg % E == 0) {
       const size_t vend = beg + (end - beg) / E * E;
-      for (size_t i = beg + (size_t)threadIdx.x * E; i < vend; i += (size_t)blockDim.x * E) {
+      // four 16-byte vectors of each input in flight per thread: all loads first
+      constexpr int U = 4;
+      const size_t step = (size_t)blockDim.x * E;
+      size_t i = beg + (size_t)threadIdx.x * E;
+      for (; i + (U - 1) * step < vend; i += U * step) {
+        uint4 qd[U], qx[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          qd[u] = __ldg(reinterpret_cast<const uint4*>(g + i + u * step));
+          qx[u] = __ldg(reinterpret_cast<const uint4*>(xs + i + u * step));
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          float d[E], xv[E], r[E];
+          unpack16<TD>(qd[u], d);
+          unpack16<TX>(qx[u], xv);
+#pragma unroll
+          for (int e = 0; e < E; ++e) r[e] = gr * (d[e] - m1 - (xv[e] - mean) * rstd * m2);
+          *reinterpret_cast<uint4*>(o + i + u * step) = pack16<TO>(r);
+        }
+      }
+      for (; i < vend; i += step) {
         float d[E], xv[E], r[E];
         unpack16<TD>(__ldg(reinterpret_cast<const uint4*>(g + i)), d);
         unpack16<TX>(__ldg(reinterpret_cast<const uint4*>(xs + i)), xv);
