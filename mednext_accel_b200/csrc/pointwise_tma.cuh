@@ -1017,6 +1017,11 @@ constexpr int kWgThreads = 512;
 constexpr int kWgProWarp0 = 4;
 constexpr int kWgProThreads = 256;
 constexpr int kWgEpiWarp0 = 12;
+// epilogue staging after the ring: one 32 x 32 fp32 tile per epilogue warp (column
+// c of row r at r * 32 + (c ^ r): conflict-free by rows and by columns), so that a
+// warp turns its 32 rows x 32 columns of accumulator into 32 coalesced row stores
+constexpr int kWgStgFloats = 32 * 32;
+constexpr size_t kWgStgBytes = 4 * kWgStgFloats * sizeof(float);
 
 struct PwTmaWgradCfg {
   int stages;
@@ -1026,6 +1031,7 @@ struct PwTmaWgradCfg {
   int g_rows;    // rows of g per TMA box (min(128, cout))
   int a_rows;    // rows of a per TMA box
   int ones_row;  // B-tile row held at 1.0 for the bias grad, or -1
+  int stage_epi; // the epilogue stores rows through the staging tiles after the ring
 };
 
 template <typename TA, int PRO>
@@ -1239,8 +1245,40 @@ __global__ void __launch_bounds__(kWgThreads, 1)
       // the MMA warp commits tfull once per unit, with or without MMAs
       if (!__all_sync(0xffffffffu, wait_or_abort(&sh.tfull[0], (uint32_t)(i & 1), abort))) break;  // warp-uniform
       tc_fence_after();
-      const int j = mt * kPwBM + q4 * 32 + lane;
-      float bval = 0.f;
+      // lane = accumulator row j0 + lane.  With few chunks per unit (the deep
+      // levels) the partial stores weigh: the staging tile turns each 32 x 32 block
+      // into row stores, lane e writing column c0 + e of row j0 + jj, 32 lanes to one
+      // 128-byte segment.  Otherwise each lane stores its own row (32 segments per
+      // store, but once per several hundred chunks) and the ring keeps the space.
+      const int j0 = mt * kPwBM + q4 * 32;
+      if (!cfg.stage_epi) {
+        const int j = j0 + lane;
+        float bval = 0.f;
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          if (any) {
+            tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, r);
+            tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = 0u;
+          }
+          if (j < p.cout) {
+            float* dst = p.part + ((size_t)sp * p.cout + j) * p.cin;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int k = nt * BN + c0 + e;
+              if (c0 + e < BN && k < p.cin) dst[k] = __uint_as_float(r[e]);
+              if (c0 + e == cfg.ones_row) bval = __uint_as_float(r[e]);
+            }
+          }
+        }
+        if (ones && j < p.cout) p.part_b[(size_t)sp * p.cout + j] = bval;
+        tc_fence_before();
+        mbar_arrive(&sh.tempty[0]);
+        continue;
+      }
+      float* stg = reinterpret_cast<float*>(ringB + (size_t)SL * cfg.b_bytes) + q4 * kWgStgFloats;
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         if (any) {
@@ -1250,17 +1288,21 @@ __global__ void __launch_bounds__(kWgThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) r[e] = 0u;
         }
-        if (j < p.cout) {
-          float* dst = p.part + ((size_t)sp * p.cout + j) * p.cin;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int k = nt * BN + c0 + e;
-            if (c0 + e < BN && k < p.cin) dst[k] = __uint_as_float(r[e]);
-            if (c0 + e == cfg.ones_row) bval = __uint_as_float(r[e]);
-          }
+        for (int e = 0; e < 32; ++e) stg[lane * 32 + (e ^ lane)] = __uint_as_float(r[e]);
+        __syncwarp();
+        const int k = nt * BN + c0 + lane;
+        const bool col_ok = c0 + lane < BN && k < p.cin;
+        const bool bias_col = c0 + lane == cfg.ones_row;
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = j0 + jj;
+          if (j >= p.cout) break;  // warp-uniform
+          const float v = stg[jj * 32 + (lane ^ jj)];
+          if (col_ok) p.part[((size_t)sp * p.cout + j) * p.cin + k] = v;
+          if (bias_col) p.part_b[(size_t)sp * p.cout + j] = v;
         }
+        __syncwarp();
       }
-      if (ones && j < p.cout) p.part_b[(size_t)sp * p.cout + j] = bval;
       tc_fence_before();
       mbar_arrive(&sh.tempty[0]);
     }

@@ -53,6 +53,7 @@ def test_cross_entropy_under_autocast_and_graph_capture():
         loss.backward()
         want_grad = logits.grad.clone()
         logits.grad = None
+        del loss  # free the eager graph: no AccumulateGrad node of it outlives the capture
         with torch.cuda.graph(g):
             out = cross_entropy(logits, target)
             out.backward()
