@@ -122,6 +122,47 @@ def _block_params(dw_w: Tensor, dw_b: Tensor | None, e_w: Tensor, e_b: Tensor, p
     return out
 
 
+# Below this many voxels per (sample, channel) a block's kernels leave most SMs idle
+# (32^3 and smaller: MedNeXt levels 2-4), so its backward runs the weight grads on a
+# side stream beside the input-grad chain; both orders give the same bits.
+_BRANCH_MAX_VOX = 32 * 32 * 32
+_SIDE_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+class _Branch:
+    """Launches on a side stream forked from the current one (when ``on``): each
+    ``run`` waits for everything queued so far on the current stream, ``join``
+    makes the current stream wait for the side stream and marks the side stream's
+    outputs as used by the current stream (for the caching allocator).  The side
+    stream is per device and lives as long as the process; CUDA-graph capture
+    records the fork and the join."""
+
+    def __init__(self, device: torch.device, on: bool) -> None:
+        self.on = on
+        if on:
+            idx = device.index if device.index is not None else torch.cuda.current_device()
+            self.main = torch.cuda.current_stream(device)
+            side = _SIDE_STREAMS.get(idx)
+            if side is None:
+                side = _SIDE_STREAMS[idx] = torch.cuda.Stream(device=device)
+            self.side = side
+
+    def run(self, fn):
+        if not self.on:
+            return fn()
+        self.side.wait_stream(self.main)
+        with torch.cuda.stream(self.side):
+            return fn()
+
+    def join(self, *outs: Tensor | None) -> None:
+        if not self.on:
+            return
+        self.main.wait_stream(self.side)
+        for t in outs:
+            if t is not None:
+                t.record_stream(self.main)
+
+
 def _even(x: Tensor) -> Tensor:
     """x at the all-even positions, contiguous: the input of a 1x1x1 stride-2 conv."""
     return x[:, :, ::2, ::2, ::2].contiguous()
@@ -340,13 +381,15 @@ def mednext_block_backward(
         u, g = ug if ug is not None else (_expand(t, stats, gn_w, gn_b, prm, cdt), None)
     # project dgrad with the GELU derivative in the epilogue and, where the fused
     # kernel covers the shape, the project weight grad from the same pass
+    # deep levels: the weight grads run on a side stream beside the input-grad chain
+    br = _Branch(x.device, int(t[0, 0].numel()) <= _BRANCH_MAX_VOX)
     fused = pw_gelu_bwd(dyb, prm.pwt, u)
     if fused is not None:
         du, dpw, dpb = fused
     else:
-        du, _ = pw_gemm(dyb, prm.pwt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
         # the project weight grad from the stored GELU(u) (else GELU applied on load)
-        dpw, dpb = pw_wgrad(dyb, g) if g is not None else pw_wgrad(dyb, u, prologue=nat.PRO_GELU)
+        dpw, dpb = br.run(lambda: pw_wgrad(dyb, g) if g is not None else pw_wgrad(dyb, u, prologue=nat.PRO_GELU))
+        du, _ = pw_gemm(dyb, prm.pwt, rc, out_dtype=cdt, aux=u, gelu_grad=True)
     # GroupNorm affine parameters in fp32 for the kernels
     g_w = gn_w.float().contiguous()
     g_b = gn_b.float().contiguous()
@@ -355,7 +398,8 @@ def mednext_block_backward(
     if fused is not None:
         dz, part, dew, deb = fused
     else:
-        dew, deb = pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g_w, pro_beta=g_b)
+        dew, deb = br.run(lambda: pw_wgrad(du, t, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g_w,
+                                           pro_beta=g_b))
         dz, part = pw_gemm(du, prm.ewt, c, out_dtype=cdt, aux=t, gn_bwd_stats=stats)
     dt, dgamma, dbeta = gn_backward_from_partials(dz, t, stats, g_w, part, vox=vox)
     wdw = prm.wdw
@@ -364,29 +408,32 @@ def mednext_block_backward(
         cin = int(x.shape[1])
         if kind == KIND_DOWN:
             # residual out[m] = W x[2m] + b: its grad is dy on the small grid
-            drw, drb = pw_wgrad(dyb, _even(xb))
+            drw, drb = br.run(lambda: pw_wgrad(dyb, _even(xb)))
             dxr, _ = pw_gemm(dyb, prm.rw, cin, out_dtype=cdt)  # added at the even positions of dx
         else:
             # residual out[2m] = W^T x[m] + b, out[odd] = b: the weight and input grads see dy at
             # the even interior positions (odd in the left-padded output); the bias grad is the
             # sum of dy over the whole interior, which the project GEMM's bias grad already is
             dye = dy[:, :, 1::2, 1::2, 1::2].to(cdt).contiguous()
-            drw_t, _ = pw_wgrad(dye, xb, want_bias=False)  # [cout, cin]
+            drw_t, _ = br.run(lambda: pw_wgrad(dye, xb, want_bias=False))  # [cout, cin]
             drw = drw_t.t()
-            drb = dpb.clone()
+            drb = None  # dpb, once the side stream has joined
             dxr, _ = pw_gemm(dye, prm.rw, cin, out_dtype=cdt)
     # the depthwise weight grad straight in the parameter's dtype where the kernels offer it
     # (fp32 parameters, 16-bit compute: the same values as a cast of the compute-dtype grad)
     wdt = dw_w.dtype if dw_w.dtype in (xb.dtype, torch.float32) else None
     if kind == KIND_REGULAR:
+        dwdw, dbdw = br.run(lambda: dwk.dw_wgrad(xb, dt, kernel_size, out_dtype=wdt))
         dx = dwk.dw_dgrad(dt, wdw, kernel_size, addend=dyb if residual_is_input and dy.dtype == cdt else None)
-        dwdw, dbdw = dwk.dw_wgrad(xb, dt, kernel_size, out_dtype=wdt)
     elif kind == KIND_DOWN:
+        dwdw, dbdw = br.run(lambda: dwk.s2_wgrad(xb, dt, kernel_size, out_dtype=wdt))
         dx = dwk.s2_dgrad(dt, wdw, tuple(int(s) for s in x.shape[2:]), kernel_size, addend_even=dxr)
-        dwdw, dbdw = dwk.s2_wgrad(xb, dt, kernel_size, out_dtype=wdt)
     else:
+        dwdw, dbdw = br.run(lambda: dwk.t_wgrad(xb, dt, kernel_size, out_dtype=wdt))
         dx = dwk.t_dgrad(dt, wdw, kernel_size, small=tuple(int(s) for s in x.shape[2:]), addend=dxr)
-        dwdw, dbdw = dwk.t_wgrad(xb, dt, kernel_size, out_dtype=wdt)
+    br.join(dpw, dpb, dew, deb, drw, drb, dwdw, dbdw)
+    if res_w is not None and kind == KIND_UP:
+        drb = dpb.clone()
     if dx.dtype != x.dtype:
         dx = dx.to(x.dtype)
         if residual_is_input:
