@@ -57,7 +57,16 @@ def _cases(dev: torch.device) -> dict[str, tuple]:
     ybig_p = r(1, 2 * C, 127, 127, 128)
     up_bytes = 2 * C * 2 * (64**3 + 127**3)
     dy_pad, t_up, y_up = r(1, C, 128, 128, 128), r(1, 2 * C, 127, 127, 128), r(1, C, 127, 127, 128)
+    # a deep level of MedNeXt-Base: C256, ratio 4, 16^3 voxels
+    vd = 16**3
+    t_d, u_d, dy_d = r(1, 256, vd), r(1, 1024, vd), r(1, 256, vd)
+    g_d, bb_d = torch.ones(256, device=dev), torch.zeros(256, device=dev)
+    stats_d = gn_stats(t_d, 1e-5)
     return {
+        "pw compress wgrad C256 16^3 (saved GELU output)": (lambda: pw_wgrad(dy_d, u_d), (256 + 1024) * 2 * vd),
+        "pw expand wgrad C256 16^3 (GroupNorm prologue)": (
+            lambda: pw_wgrad(u_d, t_d, prologue=nat.PRO_GROUPNORM, pro_stats=stats_d, pro_gamma=g_d, pro_beta=bb_d),
+            (256 + 1024) * 2 * vd),
         "pw expand fwd (GroupNorm prologue, bias)": (
             lambda: pw_gemm(t, we, RC, prologue=nat.PRO_GROUPNORM, pro_stats=stats, pro_gamma=g, pro_beta=bb, bias=b1),
             (C + RC) * 2 * V),
