@@ -127,7 +127,7 @@ enum {
   MEDNEXT_DWPLAN_GENERIC = 0,       /* per-output loads (fp64, unaligned rows) */
   MEDNEXT_DWPLAN_PACKED_FMA = 1,    /* k3, 16-bit: TMA plane ring, packed fp32 FMAs */
   MEDNEXT_DWPLAN_TENSOR_CORES = 2,  /* k5/k7, 16-bit: banded MMA, TMEM accumulators */
-  MEDNEXT_DWPLAN_TMA_RING = 3,      /* TMA plane ring, scalar FMAs */
+  MEDNEXT_DWPLAN_TMA_RING = 3,      /* TMA plane ring, scalar FMAs (16-bit weight grads: fp32 sums of 16-bit operands) */
   MEDNEXT_DWPLAN_GROUPED = 4,       /* weight grad k >= 5: taps split by kd across thread groups */
   MEDNEXT_DWPLAN_GROUPED_TMA_RING = 5  /* the same on a TMA plane ring with a producer warp */
 };
